@@ -1,0 +1,621 @@
+/* CPU restatement of the reference's hot-path kernels (see oracle.h).
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline.
+ *
+ * Floating-point conventions shared with oracle/ocl_shim.hpp (which compiles
+ * the reference kernels themselves): OpenCL mad() = fmaf; dot(float4) =
+ * fmaf(w, fmaf(z, fmaf(y, x*x')))); built with -ffp-contract=off so that no
+ * other multiply-add is fused. */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* gelu_erf / apply_act: sam3_kernels.cl:43-55. */
+static inline float gelu_erf(float x)
+{
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+static inline float apply_act(float v, int act)
+{
+    if (act == OR_ACT_GELU)
+        return gelu_erf(v);
+    if (act == OR_ACT_RELU)
+        return fmaxf(v, 0.0f);
+    return v;
+}
+
+/* store_one: sam3_kernels.cl:307-319. */
+static inline void store_one(float *C, const float *R, const float *bias,
+                             int m, int n, int ldc, float alpha, int act,
+                             float v)
+{
+    float x = alpha * v;
+
+    if (bias)
+        x += bias[n];
+    x = apply_act(x, act);
+    if (R)
+        x += R[(long)m * ldc + n];
+    C[(long)m * ldc + n] = x;
+}
+
+/* gemm_cpu_t (sam3_kernels.cl:334-391) for one 2 x 4 output block
+ * (m0, n0): eight-lane partial sums along K in steps of 8 when the whole
+ * block is inside C, hsum8 (lo + hi, then x + y + z + w), then the K tail. */
+static void gemm_t_block(int M, int N, int K, const float *A, int lda,
+                         const float *B, int ldb, float *C, int ldc,
+                         const float *bias, const float *R, float alpha,
+                         int act, int m0, int n0)
+{
+    float s[2][4][8];
+    int i, j, k, l;
+
+    memset(s, 0, sizeof(s));
+    if (m0 + 1 < M && n0 + 3 < N) {
+        const float *a0 = A + (long)m0 * lda, *a1 = A + (long)(m0 + 1) * lda;
+
+        for (k = 0; k + 8 <= K; k += 8)
+            for (j = 0; j < 4; j++) {
+                const float *bv = B + (long)(n0 + j) * ldb + k;
+
+                for (l = 0; l < 8; l++) {
+                    s[0][j][l] = fmaf(a0[k + l], bv[l], s[0][j][l]);
+                    s[1][j][l] = fmaf(a1[k + l], bv[l], s[1][j][l]);
+                }
+            }
+    }
+    else
+        k = 0;
+    for (i = 0; i < 2; i++)
+        for (j = 0; j < 4; j++) {
+            const int m = m0 + i, n = n0 + j;
+            const float *t = s[i][j];
+            float h0, h1, h2, h3, v;
+            int kk;
+
+            if (m >= M || n >= N)
+                continue;
+            h0 = t[0] + t[4];
+            h1 = t[1] + t[5];
+            h2 = t[2] + t[6];
+            h3 = t[3] + t[7];
+            v = h0 + h1 + h2 + h3;
+            for (kk = k; kk < K; kk++)
+                v = fmaf(A[(long)m * lda + kk], B[(long)n * ldb + kk], v);
+            store_one(C, R, bias, m, n, ldc, alpha, act, v);
+        }
+}
+
+/* gemm_cpu_n (sam3_kernels.cl:395-448): every output is one fmaf chain
+ * along K starting from zero, in both the float8 and the scalar branch. */
+static void gemm_n_row(int N, int K, const float *A, int lda, const float *B,
+                       int ldb, float *C, int ldc, const float *bias,
+                       const float *R, float alpha, int act, int m, float *acc)
+{
+    int n, k;
+
+    for (n = 0; n < N; n++)
+        acc[n] = 0.0f;
+    for (k = 0; k < K; k++) {
+        const float a = A[(long)m * lda + k];
+        const float *b = B + (long)k * ldb;
+
+        for (n = 0; n < N; n++)
+            acc[n] = fmaf(a, b[n], acc[n]);
+    }
+    for (n = 0; n < N; n++)
+        store_one(C, R, bias, m, n, ldc, alpha, act, acc[n]);
+}
+
+/* Batched GEMM with the reference's operand contract (sam3_kernels.cl:57-69,
+ * host geometry sam3_model.c:289-296). */
+void or_gemm(const struct or_gemm_args *a, int nb)
+{
+    int b;
+
+    for (b = 0; b < nb; b++) {
+        const long b0 = b / a->nb1, b1 = b % a->nb1;
+        const float *A = a->A + a->aoff + b0 * a->sa0 + b1 * a->sa1;
+        const float *B = a->B + a->boff + b0 * a->sb0 + b1 * a->sb1;
+        float *C = a->C + a->coff + b0 * a->sc0 + b1 * a->sc1;
+        const float *R = a->R ? a->R + a->roff + b0 * a->sc0 + b1 * a->sc1
+                              : NULL;
+
+        if (a->transb) {
+            const int mb = (a->M + 1) / 2, nbk = (a->N + 3) / 4;
+            long t;
+
+#pragma omp parallel for schedule(dynamic, 8)
+            for (t = 0; t < (long)mb * nbk; t++)
+                gemm_t_block(a->M, a->N, a->K, A, a->lda, B, a->ldb, C,
+                             a->ldc, a->bias, R, a->alpha, a->act,
+                             (int)(t / nbk) * 2, (int)(t % nbk) * 4);
+        }
+        else {
+#pragma omp parallel
+            {
+                float *acc = malloc(sizeof(float) * (size_t)a->N);
+                int m;
+
+#pragma omp for schedule(dynamic, 4)
+                for (m = 0; m < a->M; m++)
+                    gemm_n_row(a->N, a->K, A, a->lda, B, a->ldb, C, a->ldc,
+                               a->bias, R, a->alpha, a->act, m, acc);
+                free(acc);
+            }
+        }
+    }
+}
+
+/* layernorm: sam3_kernels.cl:489-514 with one work-item per row. */
+void or_layernorm(const float *X, float *Y, const float *g, const float *b,
+                  long rows, int C, float eps, int act)
+{
+    long r;
+
+#pragma omp parallel for schedule(static)
+    for (r = 0; r < rows; r++) {
+        const float *x = X + r * C;
+        float *y = Y + r * C;
+        float s = 0.0f, mean, var;
+        int c;
+
+        for (c = 0; c < C; c++)
+            s += x[c];
+        mean = s / C;
+        s = 0.0f;
+        for (c = 0; c < C; c++) {
+            const float d = x[c] - mean;
+
+            s += d * d;
+        }
+        var = s / C;
+        s = 1.0f / sqrtf(var + eps);
+        for (c = 0; c < C; c++)
+            y[c] = apply_act((x[c] - mean) * s * g[c] + b[c], act);
+    }
+}
+
+/* softmax_rows: sam3_kernels.cl:637-656 with one work-item per row. */
+static void softmax_row(float *s, int L)
+{
+    float m = -INFINITY, sum = 0.0f, v;
+    int j;
+
+    for (j = 0; j < L; j++)
+        m = fmaxf(m, s[j]);
+    for (j = 0; j < L; j++) {
+        v = expf(s[j] - m);
+        s[j] = v;
+        sum += v;
+    }
+    v = 1.0f / sum;
+    for (j = 0; j < L; j++)
+        s[j] *= v;
+}
+
+void or_softmax_rows(float *S, long rows, int L)
+{
+    long r;
+
+#pragma omp parallel for schedule(static)
+    for (r = 0; r < rows; r++)
+        softmax_row(S + r * L, L);
+}
+
+/* rope_apply: sam3_kernels.cl:679-698 (row r uses table row r % npos). */
+void or_rope_apply(float *qkv, long rows, int E, int hd, int npos,
+                   const float *cs)
+{
+    const int nf = hd / 2;
+    long r;
+
+#pragma omp parallel for schedule(static)
+    for (r = 0; r < rows; r++) {
+        int qk, pr;
+
+        for (qk = 0; qk < 2; qk++)
+            for (pr = 0; pr < E / 2; pr++) {
+                const int h = pr / nf, j = pr % nf;
+                float *x = qkv + r * 3 * E + qk * E + h * hd + 2 * j;
+                const float *rot = cs + ((r % npos) * nf + j) * 2;
+                const float a = x[0], b = x[1];
+
+                x[0] = a * rot[0] - b * rot[1];
+                x[1] = a * rot[1] + b * rot[0];
+            }
+    }
+}
+
+/* add_bcast: sam3_kernels.cl:701-708. */
+void or_add_bcast(float *out, const float *a, const float *b, long n,
+                  long bmod)
+{
+    long i;
+
+#pragma omp parallel for schedule(static)
+    for (i = 0; i < n; i++)
+        out[i] = a[i] + b[i % bmod];
+}
+
+/* window_partition: sam3_kernels.cl:712-724. */
+void or_window_partition(const float *X, float *out, int H, int C, int ws,
+                         int nwx)
+{
+    const long rows = (long)nwx * nwx * ws * ws;
+    long r;
+
+#pragma omp parallel for schedule(static)
+    for (r = 0; r < rows; r++) {
+        const int w = (int)(r / (ws * ws)), i = (int)(r % (ws * ws));
+        const int y = (w / nwx) * ws + i / ws, x = (w % nwx) * ws + i % ws;
+        int c;
+
+        for (c = 0; c < C; c++)
+            out[r * C + c] =
+                (y < H && x < H) ? X[((long)y * H + x) * C + c] : 0.0f;
+    }
+}
+
+/* window_unpartition_add: sam3_kernels.cl:728-741. */
+void or_window_unpartition_add(float *X, const float *Wd, int H, int C,
+                               int ws, int nwx)
+{
+    long t;
+
+#pragma omp parallel for schedule(static)
+    for (t = 0; t < (long)H * H; t++) {
+        const int y = (int)(t / H), x = (int)(t % H);
+        const int w = (y / ws) * nwx + x / ws, i = (y % ws) * ws + x % ws;
+        int c;
+
+        for (c = 0; c < C; c++)
+            X[t * C + c] += Wd[((long)w * ws * ws + i) * C + c];
+    }
+}
+
+/* patch_im2col: sam3_kernels.cl:661-672. */
+void or_patch_im2col(const float *img, float *out, int side, int grid, int ps)
+{
+    const int k = 3 * ps * ps;
+    long t;
+
+#pragma omp parallel for schedule(static)
+    for (t = 0; t < (long)grid * grid; t++) {
+        const int ty = (int)(t / grid), tx = (int)(t % grid);
+        int col;
+
+        for (col = 0; col < k; col++) {
+            const int c = col / (ps * ps), ky = (col % (ps * ps)) / ps,
+                      kx = col % ps;
+
+            out[t * k + col] =
+                img[((long)c * side + ty * ps + ky) * side + tx * ps + kx];
+        }
+    }
+}
+
+/* image_encoder_input without resampling (image.c:346-369): uint8 HWC to
+ * CHW floats (u / 255 - 0.5) / 0.5 (pixel_mean = pixel_std = 0.5,
+ * image.c:28-29). */
+void or_image_input(const uint8_t *rgb, int side, float *out)
+{
+    long i;
+
+#pragma omp parallel for schedule(static)
+    for (i = 0; i < (long)side * side; i++) {
+        int c;
+
+        for (c = 0; c < 3; c++)
+            out[(long)c * side * side + i] = (rgb[i * 3 + c] / 255.0f - 0.5f) / 0.5f;
+    }
+}
+
+/* float16 dot product of the decoder kernels (dot16,
+ * sam3_kernels.cl:516-520): four float4 dots added left to right. */
+static inline float dot4(const float *a, const float *b)
+{
+    return fmaf(a[3], b[3], fmaf(a[2], b[2], fmaf(a[1], b[1], a[0] * b[0])));
+}
+
+static inline float dot16(const float *a, const float *b)
+{
+    return dot4(a, b) + dot4(a + 4, b + 4) + dot4(a + 8, b + 8) +
+           dot4(a + 12, b + 12);
+}
+
+/* attn_fewkeys: sam3_kernels.cl:527-569, one (prompt, head, query) item. */
+static void attn_fewkeys_item(const float *Q, int sq, const float *K, int sk,
+                              const float *V, int sv, float *O, int Nq, int Nk,
+                              int dint, int c, float scale, int gid)
+{
+    const int heads = 8;
+    const int i = gid % Nq, ph = gid / Nq;
+    const int h = ph % heads, p = ph / heads;
+    const float *q = Q + (long)p * sq + (long)i * dint + h * c;
+    const float *kb = K + (long)p * sk + h * c;
+    const float *vb = V + (long)p * sv + h * c;
+    float o[32] = {0}, m = -INFINITY, sum = 0.0f;
+    int j, l;
+
+    for (j = 0; j < Nk; j++) {
+        const float *kj = kb + (long)j * dint, *vj = vb + (long)j * dint;
+        float s = dot16(q, kj), mn, corr, e;
+
+        if (c > 16)
+            s += dot16(q + 16, kj + 16);
+        s *= scale;
+        mn = fmaxf(m, s);
+        corr = expf(m - mn);
+        e = expf(s - mn);
+        sum = sum * corr + e;
+        for (l = 0; l < (c > 16 ? 32 : 16); l++)
+            o[l] = o[l] * corr + e * vj[l];
+        m = mn;
+    }
+    O += ((long)p * Nq + i) * dint + h * c;
+    for (l = 0; l < (c > 16 ? 32 : 16); l++)
+        O[l] = o[l] / sum;
+}
+
+/* attn_manykeys: sam3_kernels.cl:577-633 for one (prompt, head, query)
+ * row: 256 item-partial online softmaxes, then the work-group tree
+ * reductions (wg_max, wg_sum, and the 16 weighted-value sums). */
+static void attn_manykeys_row(const float *Q, int sq, const float *K, int sk,
+                              const float *V, int sv, float *O, int Nq, int Nk,
+                              int dint, int c, float scale, int row,
+                              float (*part)[257], float *mm, float *ss)
+{
+    const int heads = 8;
+    const int i = row % Nq, ph = row / Nq;
+    const int h = ph % heads, p = ph / heads;
+    const float *kb = K + (long)p * sk + h * c;
+    const float *vb = V + (long)p * sv + h * c;
+    const float *q = Q + (long)p * sq + (long)i * dint + h * c;
+    float scratch[256], mall, inv;
+    int lid, j, s;
+
+    for (lid = 0; lid < 256; lid++) {
+        float o[16] = {0}, m = -INFINITY, sum = 0.0f;
+
+        for (j = lid; j < Nk; j += 256) {
+            const float sc = dot16(q, kb + (long)j * dint) * scale;
+            const float mn = fmaxf(m, sc), corr = expf(m - mn),
+                        e = expf(sc - mn);
+            int l;
+
+            sum = sum * corr + e;
+            for (l = 0; l < 16; l++)
+                o[l] = o[l] * corr + e * vb[(long)j * dint + l];
+            m = mn;
+        }
+        mm[lid] = m;
+        ss[lid] = sum;
+        for (j = 0; j < 16; j++)
+            part[j][lid] = o[j];
+    }
+    for (lid = 0; lid < 256; lid++)
+        scratch[lid] = mm[lid];
+    for (s = 128; s > 0; s >>= 1)
+        for (lid = 0; lid < s; lid++)
+            scratch[lid] = fmaxf(scratch[lid], scratch[lid + s]);
+    mall = scratch[0];
+    for (lid = 0; lid < 256; lid++) {
+        const float f = mm[lid] == -INFINITY ? 0.0f : expf(mm[lid] - mall);
+
+        for (j = 0; j < 16; j++)
+            part[j][lid] *= f;
+        scratch[lid] = ss[lid] * f;
+    }
+    for (s = 128; s > 0; s >>= 1)
+        for (lid = 0; lid < s; lid++)
+            scratch[lid] += scratch[lid + s];
+    inv = 1.0f / scratch[0];
+    for (s = 128; s > 0; s >>= 1)
+        for (lid = 0; lid < s; lid++)
+            for (j = 0; j < 16; j++)
+                part[j][lid] += part[j][lid + s];
+    for (j = 0; j < 16; j++)
+        O[((long)p * Nq + i) * dint + h * c + j] = part[j][0] * inv;
+}
+
+/* mha: sam3_model.c:419-451 (8 heads, scale 1/sqrt(c), fewkeys for
+ * Nk <= 64, manykeys otherwise, which needs c == 16). */
+int or_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
+           const float *kp, long sk, const float *vp, long sv, float *o)
+{
+    const int heads = 8, c = dint / heads, total = P * heads * Nq;
+    const float scale = 1.0f / sqrtf((float)c);
+    int g;
+
+    if (Nk > 64 && c != 16)
+        return -1;
+    if (Nk <= 64) {
+#pragma omp parallel for schedule(static)
+        for (g = 0; g < total; g++)
+            attn_fewkeys_item(qp, (int)sq, kp, (int)sk, vp, (int)sv, o, Nq, Nk,
+                              dint, c, scale, g);
+        return 0;
+    }
+#pragma omp parallel
+    {
+        float(*part)[257] = malloc(sizeof(float) * 16 * 257);
+        float *mm = malloc(sizeof(float) * 256), *ss = malloc(sizeof(float) * 256);
+
+#pragma omp for schedule(dynamic, 4)
+        for (g = 0; g < total; g++)
+            attn_manykeys_row(qp, (int)sq, kp, (int)sk, vp, (int)sv, o, Nq, Nk,
+                              dint, c, scale, g, part, mm, ss);
+        free(part);
+        free(mm);
+        free(ss);
+    }
+    return 0;
+}
+
+/* Attention of vit_block, sam3_model.c:1000-1013, one query row at a time:
+ * scores by the gemm_cpu_t arithmetic (2 x 4 blocks, eight lanes along the
+ * head dimension, alpha applied in store_one), softmax_rows, then P.V by
+ * the gemm_cpu_n arithmetic (one fmaf chain along the keys). Rows of the
+ * score matrix are independent, so this gives the same bits as the
+ * reference's batched, head-chunked launches. */
+void or_attention(const float *qkv, int nseq, int N, int E, int heads, int hd,
+                  float alpha, float *out)
+{
+    const long ld = 3L * E;
+    const long total = (long)nseq * heads * N;
+    long t;
+
+#pragma omp parallel
+    {
+        float *s = malloc(sizeof(float) * (size_t)N);
+        float *acc = malloc(sizeof(float) * (size_t)hd);
+
+#pragma omp for schedule(dynamic, 16)
+        for (t = 0; t < total; t++) {
+            const int m = (int)(t % N), h = (int)((t / N) % heads);
+            const long w = t / ((long)N * heads);
+            const float *Q = qkv + w * N * ld + (long)h * hd;
+            const float *K = qkv + w * N * ld + E + (long)h * hd;
+            const float *V = qkv + w * N * ld + 2L * E + (long)h * hd;
+            const float *q = Q + (long)m * ld;
+            const int m0 = m & ~1;
+            int n, k, l, d;
+
+            for (n = 0; n < N; n++) {
+                const int n0 = n & ~3;
+                const float *kv = K + (long)n * ld;
+                float v;
+
+                k = 0;
+                if (m0 + 1 < N && n0 + 3 < N) {
+                    float lane[8] = {0};
+
+                    for (k = 0; k + 8 <= hd; k += 8)
+                        for (l = 0; l < 8; l++)
+                            lane[l] = fmaf(q[k + l], kv[k + l], lane[l]);
+                    v = (lane[0] + lane[4]) + (lane[1] + lane[5]) +
+                        (lane[2] + lane[6]) + (lane[3] + lane[7]);
+                }
+                else
+                    v = 0.0f;
+                for (; k < hd; k++)
+                    v = fmaf(q[k], kv[k], v);
+                s[n] = alpha * v;
+            }
+            softmax_row(s, N);
+            for (d = 0; d < hd; d++)
+                acc[d] = 0.0f;
+            for (k = 0; k < N; k++) {
+                const float p = s[k];
+                const float *vv = V + (long)k * ld;
+
+                for (d = 0; d < hd; d++)
+                    acc[d] = fmaf(p, vv[d], acc[d]);
+            }
+            for (d = 0; d < hd; d++)
+                out[(w * N + m) * E + (long)h * hd + d] = 1.0f * acc[d];
+        }
+        free(s);
+        free(acc);
+    }
+}
+
+static void linear(int rows, int in, int out, const float *X, const float *W,
+                   const float *b, float *Y, int act, int residual)
+{
+    struct or_gemm_args a;
+
+    memset(&a, 0, sizeof(a));
+    a.M = rows;
+    a.N = out;
+    a.K = in;
+    a.A = X;
+    a.lda = in;
+    a.B = W;
+    a.ldb = in;
+    a.transb = 1;
+    a.C = Y;
+    a.ldc = out;
+    a.nb1 = 1;
+    a.bias = b;
+    a.R = residual ? Y : NULL;
+    a.alpha = 1.0f;
+    a.act = act;
+    or_gemm(&a, 1);
+}
+
+void or_vit_block(const struct or_trunk *t, const struct or_block *b, float *x)
+{
+    const int G = t->grid, T = G * G, E = t->E, hd = t->hd;
+    const int s = b->window ? b->window : G;
+    const int nwx = (G + s - 1) / s, nwin = nwx * nwx, N = s * s;
+    const long rows = (long)nwin * N;
+    const float eps = 1e-5f, scale = 1.0f / sqrtf((float)hd);
+    float *xn = malloc(sizeof(float) * (size_t)T * E);
+    float *xw = b->window ? malloc(sizeof(float) * (size_t)rows * E) : NULL;
+    float *qkv = malloc(sizeof(float) * (size_t)rows * 3 * E);
+    float *attn = malloc(sizeof(float) * (size_t)rows * E);
+    float *mlp = malloc(sizeof(float) * (size_t)T * t->mlp);
+    const float *A = xn;
+
+    or_layernorm(x, xn, b->n1w, b->n1b, T, E, eps, OR_ACT_NONE);
+    if (b->window) {
+        or_window_partition(xn, xw, G, E, s, nwx);
+        A = xw;
+    }
+    linear((int)rows, E, 3 * E, A, b->qkvw, b->qkvb, qkv, OR_ACT_NONE, 0);
+    or_rope_apply(qkv, rows, E, hd, N, b->window ? t->rope_win : t->rope_glob);
+    or_attention(qkv, nwin, N, E, E / hd, hd, scale, attn);
+    if (b->window) {
+        float *tmp = xw; /* free again: reuse as the projection output */
+
+        linear((int)rows, E, E, attn, b->projw, b->projb, tmp, OR_ACT_NONE, 0);
+        or_window_unpartition_add(x, tmp, G, E, s, nwx);
+    }
+    else
+        linear(T, E, E, attn, b->projw, b->projb, x, OR_ACT_NONE, 1);
+    or_layernorm(x, xn, b->n2w, b->n2b, T, E, eps, OR_ACT_NONE);
+    linear(T, E, t->mlp, xn, b->l1w, b->l1b, mlp, OR_ACT_GELU, 0);
+    linear(T, t->mlp, E, mlp, b->l2w, b->l2b, x, OR_ACT_NONE, 1);
+    free(xn);
+    free(xw);
+    free(qkv);
+    free(attn);
+    free(mlp);
+}
+
+void or_encode_trunk(const struct or_trunk *t, const float *img, float *x,
+                     int first, int last)
+{
+    const int G = t->grid, T = G * G, E = t->E;
+    const int K = 3 * t->patch * t->patch;
+    int i;
+
+    if (first == 0) {
+        float *col = malloc(sizeof(float) * (size_t)T * K);
+
+        or_patch_im2col(img, col, t->img, G, t->patch);
+        linear(T, K, E, col, t->pe_w, NULL, x, OR_ACT_NONE, 0);
+        or_add_bcast(x, x, t->pos, (long)T * E, (long)T * E);
+        or_layernorm(x, x, t->lnpw, t->lnpb, T, E, 1e-5f, OR_ACT_NONE);
+        free(col);
+    }
+    for (i = first; i < last; i++)
+        or_vit_block(t, &t->blocks[i], x);
+}
+
+int or_num_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
