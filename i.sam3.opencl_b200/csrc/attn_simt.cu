@@ -1,0 +1,393 @@
+// SPDX-License-Identifier: Unlicense
+// fp32 CUDA-core kernels: the backbone attention in reference precision
+// (the "fp32-reference mode" of the global-attention config), the mask
+// decoder's fused attention (attn_fewkeys / attn_manykeys,
+// sam3_kernels.cl:527-633) and the reference-contract batched GEMM used for
+// operands the tensor-core path does not take (sam3_kernels.cl:57-156).
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace sam3 {
+namespace {
+
+inline int grid_for(long n, int block)
+{
+    long g = (n + block - 1) / block;
+    return (int)(g < 1 ? 1 : (g > 0x7fffffffL ? 0x7fffffffL : g));
+}
+
+// ------------------------------------------------------ fp32 attention
+// One thread per query row (128 per CTA), K/V tiles of 32 keys staged in
+// shared memory, online softmax per tile with expf. hd = 64.
+constexpr int F_HD = 64;
+constexpr int F_BQ = 128;
+constexpr int F_BK = 32;
+
+__global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict__ qkv, int nseq,
+                                                       int N, int E, int heads, float scale,
+                                                       float *__restrict__ out)
+{
+    __shared__ float ks[F_BK][F_HD];
+    __shared__ float vs[F_BK][F_HD];
+    const int nqt = (N + F_BQ - 1) / F_BQ;
+    const int qt = blockIdx.x % nqt;
+    const int h = (blockIdx.x / nqt) % heads;
+    const int seq = blockIdx.x / (nqt * heads);
+    const long ld = 3L * E;
+    const long base = (long)seq * N * ld;
+    const int qi = qt * F_BQ + threadIdx.x;
+    const bool valid = qi < N;
+    float q[F_HD], o[F_HD];
+    const float *qp = qkv + base + (long)(valid ? qi : 0) * ld + h * F_HD;
+#pragma unroll
+    for (int d = 0; d < F_HD; d += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(qp + d);
+        q[d] = v.x * scale;
+        q[d + 1] = v.y * scale;
+        q[d + 2] = v.z * scale;
+        q[d + 3] = v.w * scale;
+        o[d] = o[d + 1] = o[d + 2] = o[d + 3] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;
+    for (int k0 = 0; k0 < N; k0 += F_BK) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < F_BK * F_HD / 4; i += F_BQ) {
+            const int kr = i / (F_HD / 4), c = (i % (F_HD / 4)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + kr < N) {
+                const float *row = qkv + base + (long)(k0 + kr) * ld + h * F_HD + c;
+                kv = *reinterpret_cast<const float4 *>(row + E);
+                vv = *reinterpret_cast<const float4 *>(row + 2 * E);
+            }
+            *reinterpret_cast<float4 *>(&ks[kr][c]) = kv;
+            *reinterpret_cast<float4 *>(&vs[kr][c]) = vv;
+        }
+        __syncthreads();
+        const int nk = min(F_BK, N - k0);
+        float s[F_BK];
+        float mx = m;
+#pragma unroll
+        for (int j = 0; j < F_BK; j++) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < F_HD; d++)
+                acc = fmaf(q[d], ks[j][d], acc);
+            s[j] = j < nk ? acc : -INFINITY;
+            mx = fmaxf(mx, s[j]);
+        }
+        const float corr = expf(m - mx);
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < F_HD; d++)
+            o[d] *= corr;
+#pragma unroll
+        for (int j = 0; j < F_BK; j++) {
+            const float p = expf(s[j] - mx);
+            l += p;
+#pragma unroll
+            for (int d = 0; d < F_HD; d++)
+                o[d] = fmaf(p, vs[j][d], o[d]);
+        }
+        m = mx;
+    }
+    if (valid) {
+        const float inv = 1.0f / l;
+        float *op = out + ((long)seq * N + qi) * E + h * F_HD;
+#pragma unroll
+        for (int d = 0; d < F_HD; d += 4)
+            *reinterpret_cast<float4 *>(op + d) =
+                make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+    }
+}
+
+// ------------------------------------------------------ decoder attention
+// attn_fewkeys (sam3_kernels.cl:527-569): one thread per (prompt, query,
+// head) with the head index fastest so a warp reads whole query rows;
+// online softmax over Nk <= 64 keys, c = 16 or 32 channels per head.
+template <int CW>
+__global__ void mha_fewkeys_kernel(const float *__restrict__ Q, long sq,
+                                   const float *__restrict__ K, long sk,
+                                   const float *__restrict__ V, long sv, float *__restrict__ O,
+                                   int Nq, int Nk, int dint, float scale, long total)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= total)
+        return;
+    const int h = (int)(gid % 8);
+    const long pi = gid / 8;
+    const int i = (int)(pi % Nq);
+    const long p = pi / Nq;
+    const float *q = Q + p * sq + (long)i * dint + h * CW;
+    const float *kb = K + p * sk + h * CW;
+    const float *vb = V + p * sv + h * CW;
+    float qr[CW], o[CW];
+#pragma unroll
+    for (int c = 0; c < CW; c += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(q + c);
+        qr[c] = v.x;
+        qr[c + 1] = v.y;
+        qr[c + 2] = v.z;
+        qr[c + 3] = v.w;
+        o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.0f;
+    }
+    float m = -INFINITY, sum = 0.0f;
+    for (int j = 0; j < Nk; j++) {
+        const float *kj = kb + (long)j * dint;
+        const float *vj = vb + (long)j * dint;
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CW; c += 4) {
+            const float4 k4 = __ldg(reinterpret_cast<const float4 *>(kj + c));
+            s = fmaf(qr[c], k4.x, s);
+            s = fmaf(qr[c + 1], k4.y, s);
+            s = fmaf(qr[c + 2], k4.z, s);
+            s = fmaf(qr[c + 3], k4.w, s);
+        }
+        s *= scale;
+        const float mn = fmaxf(m, s), corr = expf(m - mn), e = expf(s - mn);
+        sum = sum * corr + e;
+#pragma unroll
+        for (int c = 0; c < CW; c += 4) {
+            const float4 v4 = __ldg(reinterpret_cast<const float4 *>(vj + c));
+            o[c] = o[c] * corr + e * v4.x;
+            o[c + 1] = o[c + 1] * corr + e * v4.y;
+            o[c + 2] = o[c + 2] * corr + e * v4.z;
+            o[c + 3] = o[c + 3] * corr + e * v4.w;
+        }
+        m = mn;
+    }
+    float *op = O + (p * Nq + i) * dint + h * CW;
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int c = 0; c < CW; c += 4)
+        *reinterpret_cast<float4 *>(op + c) =
+            make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+}
+
+// attn_manykeys (sam3_kernels.cl:577-633) for c = 16: one CTA per
+// (prompt, head) and all Nq (<= 8) queries of it, one warp per query;
+// lanes take every 32nd key with a private online softmax, then merge
+// across the warp. K/V of the (prompt, head) stream from HBM once and are
+// shared through L1 by the CTA's warps.
+__global__ void __launch_bounds__(256) mha_manykeys_kernel(
+    const float *__restrict__ Q, long sq, const float *__restrict__ K, long sk,
+    const float *__restrict__ V, long sv, float *__restrict__ O, int Nq, int Nk, int dint,
+    float scale)
+{
+    const int h = blockIdx.x % 8;
+    const long p = blockIdx.x / 8;
+    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *kb = K + p * sk + h * 16;
+    const float *vb = V + p * sv + h * 16;
+    for (int i = wq; i < Nq; i += 8) {
+        const float *q = Q + p * sq + (long)i * dint + h * 16;
+        float qr[16], o[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+            qr[c] = __ldg(q + c) * scale;
+            o[c] = 0.0f;
+        }
+        float m = -INFINITY, sum = 0.0f;
+        for (int j = lane; j < Nk; j += 32) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(kb + (long)j * dint);
+            const float4 *v4 = reinterpret_cast<const float4 *>(vb + (long)j * dint);
+            float s = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float4 kk = __ldg(k4 + c);
+                s = fmaf(qr[4 * c], kk.x, s);
+                s = fmaf(qr[4 * c + 1], kk.y, s);
+                s = fmaf(qr[4 * c + 2], kk.z, s);
+                s = fmaf(qr[4 * c + 3], kk.w, s);
+            }
+            const float mn = fmaxf(m, s), corr = expf(m - mn), e = expf(s - mn);
+            sum = sum * corr + e;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float4 vv = __ldg(v4 + c);
+                o[4 * c] = o[4 * c] * corr + e * vv.x;
+                o[4 * c + 1] = o[4 * c + 1] * corr + e * vv.y;
+                o[4 * c + 2] = o[4 * c + 2] * corr + e * vv.z;
+                o[4 * c + 3] = o[4 * c + 3] * corr + e * vv.w;
+            }
+            m = mn;
+        }
+        float mall = m;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            mall = fmaxf(mall, __shfl_xor_sync(0xffffffffu, mall, off));
+        const float f = (m == -INFINITY) ? 0.0f : expf(m - mall);
+        sum *= f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+            float v = o[c] * f;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                v += __shfl_xor_sync(0xffffffffu, v, off);
+            o[c] = v;
+        }
+        if (lane < 16) {
+            float v = o[0];
+#pragma unroll
+            for (int c = 1; c < 16; c++)
+                if (lane == c)
+                    v = o[c];
+            O[(p * Nq + i) * dint + h * 16 + lane] = v / sum;
+        }
+    }
+}
+
+// ------------------------------------------------------ SIMT GEMM
+// The reference GEMM contract (sam3_kernels.cl:57-69) on CUDA cores, any
+// strides, operands fp32 / bf16 / fp16: 64 x 64 tile per 256 threads, 4 x 4
+// outputs per thread, K steps of 16 through shared memory.
+__device__ __forceinline__ float ld_any(const void *p, int dt, long i)
+{
+    if (dt == 1)
+        return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+    if (dt == 2)
+        return __half2float(reinterpret_cast<const __half *>(p)[i]);
+    return reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ float act_fn(float v, int act)
+{
+    if (act == K_ACT_GELU)
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    if (act == K_ACT_RELU)
+        return fmaxf(v, 0.0f);
+    return v;
+}
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(
+    int M, int N, int K, const void *A, int adt, long aoff, int lda, long sa0, long sa1,
+    const void *B, int bdt, long boff, int ldb, long sb0, long sb1, int transb, float *C,
+    long coff, int ldc, long sc0, long sc1, int nb1, const float *bias, const float *R, long roff,
+    float alpha, int act)
+{
+    __shared__ float As[16][65];
+    __shared__ float Bs[16][65];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int n0 = blockIdx.x * 64, m0 = blockIdx.y * 64;
+    const long b = blockIdx.z, b0 = b / nb1, b1 = b % nb1;
+    const long ao = aoff + b0 * sa0 + b1 * sa1;
+    const long bo = boff + b0 * sb0 + b1 * sb1;
+    const long co = coff + b0 * sc0 + b1 * sc1;
+    const long ro = roff + b0 * sc0 + b1 * sc1;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int l = threadIdx.x; l < 1024; l += 256) {
+            const int r = l >> 4, c = l & 15;
+            const int gm = m0 + r, gk = k0 + c;
+            As[c][r] = (gm < M && gk < K) ? ld_any(A, adt, ao + (long)gm * lda + gk) : 0.0f;
+            if (transb) {
+                const int gn = n0 + r;
+                Bs[c][r] = (gn < N && gk < K) ? ld_any(B, bdt, bo + (long)gn * ldb + gk) : 0.0f;
+            }
+            else {
+                const int kk = l >> 6, nn = l & 63;
+                const int gk2 = k0 + kk, gn = n0 + nn;
+                Bs[kk][nn] = (gn < N && gk2 < K) ? ld_any(B, bdt, bo + (long)gk2 * ldb + gn) : 0.0f;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            float a[4], bb[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                a[i] = As[k][ty + 16 * i];
+                bb[i] = Bs[k][tx + 16 * i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty + 16 * i;
+        if (m >= M)
+            continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx + 16 * j;
+            if (n >= N)
+                continue;
+            float v = alpha * acc[i][j];
+            if (bias)
+                v += bias[n];
+            v = act_fn(v, act);
+            if (R)
+                v += R[ro + (long)m * ldc + n];
+            C[co + (long)m * ldc + n] = v;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace sam3
+
+using namespace sam3;
+#define STREAM(s) reinterpret_cast<cudaStream_t>(s)
+
+extern "C" int k_attn_f32(const float *qkv, int nseq, int N, int E, int heads, int hd,
+                          float scale, float *out, k_stream s)
+{
+    if (hd != F_HD || E != heads * hd || nseq <= 0 || N <= 0 || ((uintptr_t)qkv & 15) ||
+        ((uintptr_t)out & 15))
+        return K_EARG;
+    const long grid = (long)nseq * heads * ((N + F_BQ - 1) / F_BQ);
+    attn_f32_kernel<<<(int)grid, F_BQ, 0, STREAM(s)>>>(qkv, nseq, N, E, heads, scale, out);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,
+                     long sk, const float *vp, long sv, float *o, k_stream s)
+{
+    const int c = dint / 8;
+    const float scale = 1.0f / sqrtf((float)c);
+    if (P <= 0 || Nq <= 0 || Nk <= 0 || dint % 8 || ((uintptr_t)qp & 15) || ((uintptr_t)kp & 15) ||
+        ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) || (sk & 3) || (sv & 3))
+        return K_EARG;
+    if (Nk > 64) {
+        if (c != 16)  // the reference rejects the same shape (sam3_model.c:429-430)
+            return K_EARG;
+        mha_manykeys_kernel<<<P * 8, 256, 0, STREAM(s)>>>(qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint,
+                                                          scale);
+        return (int)cudaGetLastError();
+    }
+    const long total = (long)P * Nq * 8;
+    if (c == 16)
+        mha_fewkeys_kernel<16><<<grid_for(total, 128), 128, 0, STREAM(s)>>>(
+            qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint, scale, total);
+    else if (c == 32)
+        mha_fewkeys_kernel<32><<<grid_for(total, 128), 128, 0, STREAM(s)>>>(
+            qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint, scale, total);
+    else
+        return K_EARG;
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_gemm_simt(int M, int N, int K, const void *A, int adt, long aoff, int lda,
+                           long sa0, long sa1, const void *B, int bdt, long boff, int ldb,
+                           long sb0, long sb1, int transb, float *C, long coff, int ldc, long sc0,
+                           long sc1, int nb, int nb1, const float *bias, const float *R, long roff,
+                           float alpha, int act, k_stream s)
+{
+    if (M <= 0 || N <= 0 || K <= 0 || nb <= 0 || nb1 <= 0 || nb > 65535)
+        return K_EARG;
+    dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
+    gemm_simt_kernel<<<grid, 256, 0, STREAM(s)>>>(M, N, K, A, adt, aoff, lda, sa0, sa1, B, bdt,
+                                                  boff, ldb, sb0, sb1, transb, C, coff, ldc, sc0,
+                                                  sc1, nb1, bias, R, roff, alpha, act);
+    return (int)cudaGetLastError();
+}

@@ -1,0 +1,518 @@
+// SPDX-License-Identifier: Unlicense
+// Memory-bound kernels of the PE backbone path and the reference-contract
+// helpers: LayerNorm (one warp per row, 128-bit loads, row kept in
+// registers), RoPE, window (un)partition, add_bcast, patch extraction with
+// the uint8 -> [-1, 1] input normalisation, casts, row permutations and the
+// seeded generator. Each kernel cites the reference kernel it replaces.
+#include "kernels.h"
+#include "sam3_synth.h"
+#include "tc_ptx.cuh"
+
+#include <cuda_bf16.h>
+
+namespace sam3 {
+namespace {
+
+inline int grid_for(long n, int block)
+{
+    long g = (n + block - 1) / block;
+    return (int)(g < 1 ? 1 : (g > 0x7fffffffL ? 0x7fffffffL : g));
+}
+
+__device__ __forceinline__ float gelu_erf(float x)
+{
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float act_fn(float v, int act)
+{
+    if (act == K_ACT_GELU)
+        return gelu_erf(v);
+    if (act == K_ACT_RELU)
+        return fmaxf(v, 0.0f);
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// layernorm (sam3_kernels.cl:489-514): two-pass mean / variance, eps inside
+// the square root, optional activation. One warp per row; the row stays in
+// registers (NV float4 per lane), so X is read once and Y written once.
+template <int NV, bool OUT_BF16>
+__global__ void __launch_bounds__(256) ln_reg_kernel(const float *__restrict__ X, void *Y,
+                                                     const float *__restrict__ g,
+                                                     const float *__restrict__ b, long rows, int C,
+                                                     float eps, int act)
+{
+    const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows)
+        return;
+    const float4 *x = reinterpret_cast<const float4 *>(X + row * C);
+    float4 v[NV];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        v[i] = x[i * 32 + lane];
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    const float mean = warp_sum(s) / C;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + bb * bb) + (c * c + d * d);
+    }
+    const float inv = rsqrtf(warp_sum(q) / C + eps);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    const float4 *b4 = reinterpret_cast<const float4 *>(b);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const int c4 = i * 32 + lane;
+        const float4 gg = __ldg(g4 + c4), bt = __ldg(b4 + c4);
+        float4 y;
+        y.x = act_fn((v[i].x - mean) * inv * gg.x + bt.x, act);
+        y.y = act_fn((v[i].y - mean) * inv * gg.y + bt.y, act);
+        y.z = act_fn((v[i].z - mean) * inv * gg.z + bt.z, act);
+        y.w = act_fn((v[i].w - mean) * inv * gg.w + bt.w, act);
+        if (OUT_BF16) {
+            uint2 p;
+            p.x = pack_bf16x2(y.x, y.y);
+            p.y = pack_bf16x2(y.z, y.w);
+            reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(Y) + row * C)[c4] = p;
+        }
+        else
+            reinterpret_cast<float4 *>(reinterpret_cast<float *>(Y) + row * C)[c4] = y;
+    }
+}
+
+// Any C: one warp per row, three passes over global memory.
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(256) ln_any_kernel(const float *__restrict__ X, void *Y,
+                                                     const float *__restrict__ g,
+                                                     const float *__restrict__ b, long rows, int C,
+                                                     float eps, int act)
+{
+    const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows)
+        return;
+    const float *x = X + row * C;
+    float s = 0.0f;
+    for (int c = lane; c < C; c += 32)
+        s += x[c];
+    const float mean = warp_sum(s) / C;
+    float q = 0.0f;
+    for (int c = lane; c < C; c += 32) {
+        const float d = x[c] - mean;
+        q += d * d;
+    }
+    const float inv = rsqrtf(warp_sum(q) / C + eps);
+    // Read every input before the first write: Y may alias X.
+    __syncwarp();
+    for (int c = lane; c < C; c += 32) {
+        const float y = act_fn((x[c] - mean) * inv * g[c] + b[c], act);
+        if (OUT_BF16)
+            reinterpret_cast<__nv_bfloat16 *>(Y)[row * C + c] = __float2bfloat16_rn(y);
+        else
+            reinterpret_cast<float *>(Y)[row * C + c] = y;
+    }
+}
+
+// ---------------------------------------------------------------- softmax
+// softmax_rows (sam3_kernels.cl:637-656): in place, one warp per row.
+__global__ void __launch_bounds__(256) softmax_rows_kernel(float *S, long rows, int L)
+{
+    const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows)
+        return;
+    float *s = S + row * L;
+    float m = -INFINITY;
+    for (int j = lane; j < L; j += 32)
+        m = fmaxf(m, s[j]);
+    m = warp_max(m);
+    float sum = 0.0f;
+    for (int j = lane; j < L; j += 32) {
+        const float v = expf(s[j] - m);
+        s[j] = v;
+        sum += v;
+    }
+    const float inv = 1.0f / warp_sum(sum);
+    for (int j = lane; j < L; j += 32)
+        s[j] *= inv;
+}
+
+// ---------------------------------------------------------------- RoPE
+// rope_apply (sam3_kernels.cl:679-698): pair (2j, 2j+1) of q and k of row r
+// rotated by cs[(r % npos) * hd/2 + j]. One thread per pair.
+__global__ void rope_apply_kernel(float *qkv, long rows, int E, int hd, int npos,
+                                  const float2 *__restrict__ cs)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int half = E / 2;
+    if (gid >= rows * 2 * half)
+        return;
+    const int pr = (int)(gid % half);
+    const long rest = gid / half;
+    const int qk = (int)(rest % 2);
+    const long r = rest / 2;
+    const int nf = hd / 2, h = pr / nf, j = pr % nf;
+    float2 *x = reinterpret_cast<float2 *>(qkv + r * 3 * E + qk * E + h * hd + 2 * j);
+    const float2 rot = __ldg(cs + (r % npos) * nf + j);
+    const float2 v = *x;
+    *x = make_float2(v.x * rot.x - v.y * rot.y, v.x * rot.y + v.y * rot.x);
+}
+
+// fp32 qkv -> bf16 qkv, RoPE on q and k, plain cast of v. One thread per
+// 4 columns (two pairs).
+__global__ void rope_cast_kernel(const float *__restrict__ qkv, long rows, int E, int hd,
+                                 int npos, const float2 *__restrict__ cs, __nv_bfloat16 *out)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int per_row = 3 * E / 4;
+    if (gid >= rows * per_row)
+        return;
+    const long r = gid / per_row;
+    const int c = (int)(gid % per_row) * 4;
+    float4 v = *reinterpret_cast<const float4 *>(qkv + r * 3 * E + c);
+    if (c < 2 * E) {
+        const int j = (c % hd) / 2, nf = hd / 2;
+        const float2 *t = cs + (r % npos) * nf + j;
+        const float2 r0 = __ldg(t), r1 = __ldg(t + 1);
+        v = make_float4(v.x * r0.x - v.y * r0.y, v.x * r0.y + v.y * r0.x,
+                        v.z * r1.x - v.w * r1.y, v.z * r1.y + v.w * r1.x);
+    }
+    uint2 p;
+    p.x = pack_bf16x2(v.x, v.y);
+    p.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2 *>(out + r * 3 * E + c) = p;
+}
+
+// ---------------------------------------------------------------- misc
+// add_bcast (sam3_kernels.cl:701-708).
+__global__ void add_bcast_kernel(float *out, const float *a, const float *b, long n, long bmod)
+{
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+        out[i] = a[i] + b[i % bmod];
+}
+
+// window_partition (sam3_kernels.cl:712-724).
+__global__ void window_partition_kernel(const float *X, float *out, int H, int C, int ws, int nwx,
+                                        long total)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= total)
+        return;
+    const long r = gid / C;
+    const int c = (int)(gid % C);
+    const int w = (int)(r / (ws * ws)), i = (int)(r % (ws * ws));
+    const int y = (w / nwx) * ws + i / ws, x = (w % nwx) * ws + i % ws;
+    out[gid] = (y < H && x < H) ? X[((long)y * H + x) * C + c] : 0.0f;
+}
+
+// window_unpartition_add (sam3_kernels.cl:728-741).
+__global__ void window_unpartition_add_kernel(float *X, const float *Wd, int H, int C, int ws,
+                                              int nwx)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long t = gid / C;
+    if (t >= (long)H * H)
+        return;
+    const int c = (int)(gid % C);
+    const int y = (int)(t / H), x = (int)(t % H);
+    const int w = (y / ws) * nwx + x / ws, i = (y % ws) * ws + x % ws;
+    X[gid] += Wd[((long)w * ws * ws + i) * C + c];
+}
+
+// patch_im2col (sam3_kernels.cl:661-672).
+__global__ void patch_im2col_kernel(const float *img, float *out, int side, int grid, int ps)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int k = 3 * ps * ps;
+    const long t = gid / k;
+    if (t >= (long)grid * grid)
+        return;
+    const int col = (int)(gid % k);
+    const int c = col / (ps * ps), ky = (col % (ps * ps)) / ps, kx = col % ps;
+    const int ty = (int)(t / grid), tx = (int)(t % grid);
+    out[gid] = img[((long)c * side + ty * ps + ky) * side + tx * ps + kx];
+}
+
+// Patch rows straight from uint8 HWC tiles, normalised as
+// image_encoder_input does (image.c:360-366), in window-major token order,
+// bf16, K padded with zeros to kpad. One thread per 8 output columns.
+__global__ void patch_embed_in_kernel(const uint8_t *__restrict__ rgb, int ntile, int side,
+                                      int grid, int ps, int ws, int kpad, __nv_bfloat16 *out)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int groups = kpad / 8;
+    const long T = (long)grid * grid;
+    if (gid >= ntile * T * groups)
+        return;
+    const long row = gid / groups;
+    const int g0 = (int)(gid % groups) * 8;
+    const int tile = (int)(row / T), r = (int)(row % T);
+    const int nwx = grid / ws, w2 = ws * ws;
+    const int w = r / w2, i = r % w2;
+    const int ty = (w / nwx) * ws + i / ws, tx = (w % nwx) * ws + i % ws;
+    const int K = 3 * ps * ps;
+    const uint8_t *src = rgb + (long)tile * side * side * 3;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const int col = g0 + e;
+        float f = 0.0f;
+        if (col < K) {
+            const int c = col / (ps * ps), ky = (col % (ps * ps)) / ps, kx = col % ps;
+            const uint8_t u = src[((long)(ty * ps + ky) * side + tx * ps + kx) * 3 + c];
+            f = ((float)u / 255.0f - 0.5f) / 0.5f;
+        }
+        v[e] = f;
+    }
+    uint4 p;
+    p.x = pack_bf16x2(v[0], v[1]);
+    p.y = pack_bf16x2(v[2], v[3]);
+    p.z = pack_bf16x2(v[4], v[5]);
+    p.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4 *>(out + row * kpad + g0) = p;
+}
+
+__global__ void cast_f32_bf16_kernel(const float *x, __nv_bfloat16 *y, long n)
+{
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+__global__ void cast_bf16_f32_kernel(const __nv_bfloat16 *x, float *y, long n)
+{
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+        y[i] = __bfloat162float(x[i]);
+}
+
+// Row r of the window-major layout <-> raster row of the same token.
+__device__ __forceinline__ long raster_of(long r, int grid, int ws)
+{
+    const long T = (long)grid * grid;
+    const long tile = r / T;
+    const int t = (int)(r % T), w2 = ws * ws, nwx = grid / ws;
+    const int w = t / w2, i = t % w2;
+    const int y = (w / nwx) * ws + i / ws, x = (w % nwx) * ws + i % ws;
+    return tile * T + (long)y * grid + x;
+}
+
+// dir 0: y[raster] = x[window-major]; dir 1: y[window-major] = x[raster].
+__global__ void permute_rows_kernel(const float *__restrict__ x, float *__restrict__ y, long rows,
+                                    int grid, int ws, int C, int dir)
+{
+    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int c4 = C / 4;
+    if (gid >= rows * c4)
+        return;
+    const long r = gid / c4;
+    const int c = (int)(gid % c4);
+    const long p = raster_of(r, grid, ws);
+    const float4 *src = reinterpret_cast<const float4 *>(x + (dir == 0 ? r : p) * C);
+    float4 *dst = reinterpret_cast<float4 *>(y + (dir == 0 ? p : r) * C);
+    dst[c] = src[c];
+}
+
+// Device copy of sam3_synth_normal: same hash, same Irwin-Hall sum, one
+// correctly rounded multiply and add.
+__global__ void synth_normal_kernel(uint64_t base, long n, float mean, float std, float *out32,
+                                    __nv_bfloat16 *out16)
+{
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n)
+        return;
+    const float z = sam3_normal_at(base, (uint64_t)i);
+    const float v = __fadd_rn(mean, __fmul_rn(std, z));
+    if (out16)
+        out16[i] = __float2bfloat16_rn(v);
+    else
+        out32[i] = v;
+}
+
+}  // namespace
+}  // namespace sam3
+
+using namespace sam3;
+
+#define STREAM(s) reinterpret_cast<cudaStream_t>(s)
+#define LAUNCH_RET() return (int)cudaGetLastError()
+
+extern "C" int k_layernorm(const float *X, void *Y, int y_bf16, const float *g, const float *b,
+                           long rows, int C, float eps, int act, k_stream s)
+{
+    if (rows <= 0 || C <= 0)
+        return rows == 0 ? 0 : K_EARG;
+    const int grid = grid_for(rows, 8);
+    const bool vec = (C % 128 == 0) && !((uintptr_t)X & 15) && !((uintptr_t)Y & 15) &&
+                     !((uintptr_t)g & 15) && !((uintptr_t)b & 15);
+#define LN_REG(NV)                                                                          \
+    if (vec && C == NV * 128) {                                                             \
+        if (y_bf16)                                                                         \
+            ln_reg_kernel<NV, true><<<grid, 256, 0, STREAM(s)>>>(X, Y, g, b, rows, C, eps, act); \
+        else                                                                                \
+            ln_reg_kernel<NV, false><<<grid, 256, 0, STREAM(s)>>>(X, Y, g, b, rows, C, eps, act); \
+        LAUNCH_RET();                                                                       \
+    }
+    LN_REG(2)
+    LN_REG(4)
+    LN_REG(8)
+    LN_REG(16)
+#undef LN_REG
+    if (y_bf16)
+        ln_any_kernel<true><<<grid, 256, 0, STREAM(s)>>>(X, Y, g, b, rows, C, eps, act);
+    else
+        ln_any_kernel<false><<<grid, 256, 0, STREAM(s)>>>(X, Y, g, b, rows, C, eps, act);
+    LAUNCH_RET();
+}
+
+extern "C" int k_softmax_rows(float *S, long rows, int L, k_stream s)
+{
+    if (rows <= 0)
+        return 0;
+    softmax_rows_kernel<<<grid_for(rows, 8), 256, 0, STREAM(s)>>>(S, rows, L);
+    LAUNCH_RET();
+}
+
+extern "C" int k_rope_apply(float *qkv, long rows, int E, int hd, int npos, const float *cs,
+                            k_stream s)
+{
+    if (hd % 2 || E % hd || npos <= 0)
+        return K_EARG;
+    const long n = rows * E;
+    rope_apply_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        qkv, rows, E, hd, npos, reinterpret_cast<const float2 *>(cs));
+    LAUNCH_RET();
+}
+
+extern "C" int k_rope_cast_bf16(const float *qkv, long rows, int E, int hd, int npos,
+                                const float *cs, void *out, k_stream s)
+{
+    if (hd % 4 || E % hd || npos <= 0 || ((uintptr_t)qkv & 15) || ((uintptr_t)out & 7))
+        return K_EARG;
+    const long n = rows * (3L * E / 4);
+    rope_cast_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        qkv, rows, E, hd, npos, reinterpret_cast<const float2 *>(cs),
+        reinterpret_cast<__nv_bfloat16 *>(out));
+    LAUNCH_RET();
+}
+
+extern "C" int k_add_bcast(float *out, const float *a, const float *b, long n, long bmod,
+                           k_stream s)
+{
+    if (n <= 0)
+        return 0;
+    if (bmod <= 0)
+        return K_EARG;
+    add_bcast_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(out, a, b, n, bmod);
+    LAUNCH_RET();
+}
+
+extern "C" int k_window_partition(const float *X, float *out, int H, int C, int ws, int nwx,
+                                  k_stream s)
+{
+    const long total = (long)nwx * nwx * ws * ws * C;
+    window_partition_kernel<<<grid_for(total, 256), 256, 0, STREAM(s)>>>(X, out, H, C, ws, nwx,
+                                                                          total);
+    LAUNCH_RET();
+}
+
+extern "C" int k_window_unpartition_add(float *X, const float *Wd, int H, int C, int ws, int nwx,
+                                        k_stream s)
+{
+    const long n = (long)H * H * C;
+    window_unpartition_add_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(X, Wd, H, C, ws, nwx);
+    LAUNCH_RET();
+}
+
+extern "C" int k_patch_im2col(const float *img, float *out, int side, int grid, int ps,
+                              k_stream s)
+{
+    const long n = (long)grid * grid * 3 * ps * ps;
+    patch_im2col_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(img, out, side, grid, ps);
+    LAUNCH_RET();
+}
+
+extern "C" int k_patch_embed_in(const uint8_t *rgb, int ntile, int side, int grid, int ps, int ws,
+                                int kpad, void *out, k_stream s)
+{
+    if (kpad % 8 || kpad < 3 * ps * ps || grid % ws || ((uintptr_t)out & 15))
+        return K_EARG;
+    const long n = (long)ntile * grid * grid * (kpad / 8);
+    patch_embed_in_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        rgb, ntile, side, grid, ps, ws, kpad, reinterpret_cast<__nv_bfloat16 *>(out));
+    LAUNCH_RET();
+}
+
+extern "C" int k_cast_f32_bf16(const float *x, void *y, long n, k_stream s)
+{
+    if (n <= 0)
+        return 0;
+    cast_f32_bf16_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        x, reinterpret_cast<__nv_bfloat16 *>(y), n);
+    LAUNCH_RET();
+}
+
+extern "C" int k_cast_bf16_f32(const void *x, float *y, long n, k_stream s)
+{
+    if (n <= 0)
+        return 0;
+    cast_bf16_f32_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(x), y, n);
+    LAUNCH_RET();
+}
+
+extern "C" int k_unpermute_rows(const float *x, float *y, int ntile, int grid, int ws, int C,
+                                k_stream s)
+{
+    if (C % 4 || grid % ws)
+        return K_EARG;
+    const long rows = (long)ntile * grid * grid;
+    permute_rows_kernel<<<grid_for(rows * (C / 4), 256), 256, 0, STREAM(s)>>>(x, y, rows, grid, ws,
+                                                                               C, 0);
+    LAUNCH_RET();
+}
+
+extern "C" int k_permute_rows(const float *x, float *y, int ntile, int grid, int ws, int C,
+                              k_stream s)
+{
+    if (C % 4 || grid % ws)
+        return K_EARG;
+    const long rows = (long)ntile * grid * grid;
+    permute_rows_kernel<<<grid_for(rows * (C / 4), 256), 256, 0, STREAM(s)>>>(x, y, rows, grid, ws,
+                                                                               C, 1);
+    LAUNCH_RET();
+}
+
+extern "C" int k_synth_normal(uint64_t seed, uint64_t stream, long n, float mean, float std,
+                              void *out, int out_bf16, k_stream s)
+{
+    if (n <= 0)
+        return 0;
+    const uint64_t base = sam3_stream_base(seed, stream);
+    synth_normal_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        base, n, mean, std, out_bf16 ? nullptr : reinterpret_cast<float *>(out),
+        out_bf16 ? reinterpret_cast<__nv_bfloat16 *>(out) : nullptr);
+    LAUNCH_RET();
+}

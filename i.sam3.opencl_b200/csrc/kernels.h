@@ -1,0 +1,121 @@
+/* SPDX-License-Identifier: Unlicense */
+/* Internal launch entry points of the CUDA kernels (C linkage), called by
+ * the C host layer (cuda_backend.c, sam3_ops.c, sam3_backbone.c). Every
+ * launcher enqueues on the given stream and returns a cudaError_t value
+ * (0 on success) or one of the SAM3_E* argument errors below. Device-side
+ * failures (bounded waits that ran out) are written to *err. */
+#ifndef SAM3_CUDA_KERNELS_H
+#define SAM3_CUDA_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *k_stream;
+
+#define K_ACT_NONE 0
+#define K_ACT_GELU 1
+#define K_ACT_RELU 2
+
+/* Argument errors (distinct from cudaError_t values, which are < 1000). */
+#define K_EARG 1001   /* shape, stride or alignment not supported */
+#define K_ETMAP 1002  /* cuTensorMapEncodeTiled failed */
+
+/* RoPE epilogue of the QKV projection: rotate the (2j, 2j+1) column pairs
+ * of the q and k blocks (columns [0, 2E)) by the (cos, sin) table row of
+ * each output row (sam3_kernels.cl:679-698). mode 0: off; 1: table row =
+ * row % npos (the reference's indexing, rows in window order); 2: rows in
+ * window-major order over a grid x grid image of ws-wide windows, table row
+ * = raster position of the token (global attention on window-major rows). */
+struct k_rope {
+    const float *cs;
+    int mode, E, hd, npos, ws, nwx, grid;
+};
+
+/* C[M,N] = epi(alpha * A[M,K] . B[N,K]^T); A, B bf16 row-major (lda, ldb in
+ * elements, multiples of 8); epilogue: + bias[n], act, + R[m', n] with
+ * m' = m % rmod (rmod 0: m' = m; fp32, ldr; may alias C), RoPE; C fp32 or
+ * bf16 (c_bf16), ldc in elements. */
+int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const void *B,
+                   int ldb, void *C, int ldc, int c_bf16, const float *bias,
+                   const float *R, int ldr, int rmod, float alpha, int act,
+                   const struct k_rope *rope, int *err, int num_sms,
+                   k_stream s);
+
+/* Reference-contract GEMM on CUDA cores (any strides/offsets, fp32 math):
+ * C = act(alpha * A op(B) + bias) + R, batched with the two-level strides of
+ * sam3_kernels.cl:57-69. Operand dtypes: 0 fp32, 1 bf16, 2 fp16. */
+int k_gemm_simt(int M, int N, int K, const void *A, int adt, long aoff, int lda,
+                long sa0, long sa1, const void *B, int bdt, long boff, int ldb,
+                long sb0, long sb1, int transb, float *C, long coff, int ldc,
+                long sc0, long sc1, int nb, int nb1, const float *bias,
+                const float *R, long roff, float alpha, int act, k_stream s);
+
+/* Fused windowed/global self-attention on tensor cores. qkv: bf16
+ * [nseq * N, 3E] rows (q | k | v, head h at column h * hd, RoPE already
+ * applied), out: [nseq * N, E] fp32 or bf16. scale multiplies the scores
+ * (1/sqrt(hd)). hd must be 64; E % 64 == 0. */
+int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
+              void *out, int out_bf16, int *err, k_stream s);
+
+/* The same attention in fp32 on CUDA cores (reference mode): qkv fp32. */
+int k_attn_f32(const float *qkv, int nseq, int N, int E, int heads, int hd,
+               float scale, float *out, k_stream s);
+
+/* fp32 qkv -> bf16 qkv with RoPE on q and k (table row = row % npos). */
+int k_rope_cast_bf16(const float *qkv, long rows, int E, int hd, int npos,
+                     const float *cs, void *out, k_stream s);
+
+/* In-place RoPE on fp32 qkv rows (rope_apply, sam3_kernels.cl:679-698). */
+int k_rope_apply(float *qkv, long rows, int E, int hd, int npos,
+                 const float *cs, k_stream s);
+
+/* Row LayerNorm (sam3_kernels.cl:489-514): fp32 X [rows, C] -> Y (fp32 or
+ * bf16); Y may alias X when fp32. */
+int k_layernorm(const float *X, void *Y, int y_bf16, const float *g,
+                const float *b, long rows, int C, float eps, int act,
+                k_stream s);
+
+int k_softmax_rows(float *S, long rows, int L, k_stream s);
+int k_add_bcast(float *out, const float *a, const float *b, long n, long bmod,
+                k_stream s);
+int k_window_partition(const float *X, float *out, int H, int C, int ws,
+                       int nwx, k_stream s);
+int k_window_unpartition_add(float *X, const float *Wd, int H, int C, int ws,
+                             int nwx, k_stream s);
+int k_patch_im2col(const float *img, float *out, int side, int grid, int ps,
+                   k_stream s);
+int k_cast_f32_bf16(const float *x, void *y, long n, k_stream s);
+int k_cast_bf16_f32(const void *x, float *y, long n, k_stream s);
+
+/* Decoder attention (sam3_kernels.cl:527-633): 8 heads, scale 1/sqrt(c). */
+int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
+          const float *kp, long sk, const float *vp, long sv, float *o,
+          k_stream s);
+
+/* uint8 HWC tiles -> bf16 patch rows in window-major token order:
+ * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight
+ * order), value (u/255 - 0.5)/0.5 (image.c:360-366), zero for columns >= 3
+ * ps^2. Row order: token r of a tile is window w = r / ws^2, in-window
+ * index i = r % ws^2 (ws = grid gives raster order). */
+int k_patch_embed_in(const uint8_t *rgb, int ntile, int side, int grid, int ps,
+                     int ws, int kpad, void *out, k_stream s);
+
+/* Seeded generator on the device (bit-identical to include/sam3_synth.h). */
+int k_synth_normal(uint64_t seed, uint64_t stream, long n, float mean,
+                   float std, void *out, int out_bf16, k_stream s);
+
+/* x (window-major rows) -> y (raster rows) for ntile tiles. */
+int k_unpermute_rows(const float *x, float *y, int ntile, int grid, int ws,
+                     int C, k_stream s);
+/* pos [T, C] raster -> window-major rows. */
+int k_permute_rows(const float *x, float *y, int ntile, int grid, int ws,
+                   int C, k_stream s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,280 @@
+/* SPDX-License-Identifier: Unlicense */
+/* C-ABI of the B200 backend for the SAM 3 Perception Encoder hot path.
+ *
+ * Drop-in for the reference's OpenCL backend and operator layer
+ * (i.sam3.opencl: ocl_backend.h, sam3_ops.h). Plain C types only: opaque
+ * handles, pointers, sizes and int status codes (0 = success, see
+ * cb_errstr). Every call that enqueues device work runs on the backend's
+ * stream; results are visible after cb_sync() or a blocking cb_read().
+ *
+ * Per-device state lives in the cb_backend handle (no globals), so one
+ * process may drive several GPUs from several host threads, one backend
+ * per thread. */
+#ifndef SAM3_CUDA_H
+#define SAM3_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status */
+#define CB_OK 0
+#define CB_ENODEV 1   /* no CUDA device / bad ordinal / not sm_100 */
+#define CB_EALLOC 2   /* device or host allocation failed */
+#define CB_EARG 3     /* invalid argument, shape, stride or alignment */
+#define CB_ECUDA 4    /* CUDA runtime error (cb_last_error has the text) */
+#define CB_ETIMEOUT 5 /* a kernel's bounded wait ran out (device error word) */
+#define CB_EDTYPE 6   /* operand dtype not supported by this op */
+
+/* Buffer element types. */
+#define CB_F32 0
+#define CB_BF16 1
+#define CB_F16 2
+#define CB_U8 3
+
+/* Activations, as sam3_ops.h:11-13. */
+#define CB_ACT_NONE 0
+#define CB_ACT_GELU 1
+#define CB_ACT_RELU 2
+
+typedef struct cb_backend cb_backend;
+typedef struct cb_mem_s *cb_mem;
+
+/* ------------------------------------------------------------ backend
+ * Replaces ocl_backend.h:57-104. */
+
+/* ocl_init (ocl_backend.h:57-59): select CUDA device `device` (ordinal),
+ * create a stream and the device error word. Fails with CB_ENODEV when the
+ * device is absent or is not compute capability 10.x. */
+int cb_init(cb_backend **out, int device);
+/* ocl_free (ocl_backend.h:79). */
+void cb_free(cb_backend *b);
+/* ocl_errstr (ocl_backend.h:82): text of a status code. */
+const char *cb_errstr(int status);
+/* Detail of the last failure on this backend (CUDA error text etc.). */
+const char *cb_last_error(const cb_backend *b);
+int cb_device(const cb_backend *b);
+int cb_num_sms(const cb_backend *b);
+
+/* ocl_alloc (ocl_backend.h:88): device buffer of `bytes`, tagged dtype. */
+int cb_alloc(cb_backend *b, size_t bytes, int dtype, cb_mem *out);
+/* Borrow an existing device pointer (not freed by cb_release). */
+int cb_wrap(cb_backend *b, void *dptr, size_t bytes, int dtype, cb_mem *out);
+/* ocl_upload (ocl_backend.h:91): allocate and fill from host memory. */
+int cb_upload(cb_backend *b, const void *src, size_t bytes, int dtype,
+              cb_mem *out);
+/* ocl_upload_weight (ocl_backend.h:65): count fp32 values stored as dtype
+ * (CB_BF16 for tensor-core GEMM operands, CB_F16 or CB_F32), rounded to
+ * nearest even. */
+int cb_upload_weight(cb_backend *b, const float *src, size_t count, int dtype,
+                     cb_mem *out);
+/* ocl_write / ocl_read (ocl_backend.h:94-97): blocking copies, byte
+ * offsets. */
+int cb_write(cb_backend *b, cb_mem dst, size_t off, const void *src, size_t n);
+int cb_read(cb_backend *b, cb_mem src, size_t off, void *dst, size_t n);
+/* ocl_release (ocl_backend.h:104): free and set *m to NULL. */
+int cb_release(cb_mem *m);
+void *cb_ptr(cb_mem m);
+size_t cb_bytes(cb_mem m);
+int cb_dtype(cb_mem m);
+/* clFinish (sam3_model.c:1140 etc.): wait for the stream, then report a
+ * device-side failure (CB_ETIMEOUT) if a kernel recorded one. */
+int cb_sync(cb_backend *b);
+/* Use an external CUDA stream (cudaStream_t as void*); NULL = own stream. */
+int cb_set_stream(cb_backend *b, void *stream);
+void *cb_stream(const cb_backend *b);
+/* Device error word: 0 when no kernel has failed. cb_clear_error resets it. */
+int cb_device_error(cb_backend *b);
+int cb_clear_error(cb_backend *b);
+
+/* Per-kernel profile, the counterpart of the reference's
+ * I_SAM3_OPENCL_PROFILE table (sam3_model.c:149-207, printed in sam_free):
+ * with profiling on, every kernel the backend launches is bracketed by CUDA
+ * events on its stream (no host synchronisation is added) and accounted
+ * under a name with its algorithmic FLOPs and bytes. cb_profile(b, 1)
+ * clears the table and starts; cb_profile(b, 0) stops. cb_profile_entry
+ * synchronises the stream, folds pending events in, and returns entry i
+ * (CB_EARG past the end). */
+int cb_profile(cb_backend *b, int on);
+int cb_profile_entry(cb_backend *b, int i, const char **name, long *calls,
+                     double *ms, double *flops, double *bytes);
+
+/* ------------------------------------------------------------ operators
+ * Replaces sam3_ops.h:17-65. Offsets, leading dimensions and batch strides
+ * are in elements, as in the reference. */
+
+/* struct opnd (sam3_ops.h:19-24). */
+struct cb_opnd {
+    cb_mem buf;
+    int64_t off;
+    int32_t ld;
+    int64_t s0, s1;
+};
+
+/* mat / bmat (sam3_ops.h:48-49). */
+struct cb_opnd cb_mat(cb_mem buf, int64_t off, int32_t ld);
+struct cb_opnd cb_bmat(cb_mem buf, int64_t off, int32_t ld, int64_t s0,
+                       int64_t s1);
+
+/* gemm (sam3_ops.h:51-54, kernel contract sam3_kernels.cl:57-69): batched
+ * C = act(alpha * A op(B) + bias) + R. transb != 0: B is N x K (Linear
+ * weight layout). Batch b = (b / nb1, b % nb1) with per-operand strides s0,
+ * s1; R has C's layout (offset roff) and may alias C. A, B: F32, BF16 or
+ * F16; C, bias, R: F32, except that C may be BF16 on the tensor-core path.
+ * nb == 1, transb, bf16 A and B with 16-byte aligned rows run on tcgen05
+ * tensor cores (fp32 accumulation); other operands on CUDA cores (fp32). */
+int cb_gemm(cb_backend *b, int M, int N, int K, struct cb_opnd A,
+            struct cb_opnd B, int transb, struct cb_opnd C, int nb, int nb1,
+            cb_mem bias, cb_mem R, int64_t roff, float alpha, int act);
+
+/* linear (sam3_ops.h:56-58): Y[rows, out] = act(X[rows, in] W^T + b)
+ * (+ Y when residual). An F32 X with a BF16 W is converted to bf16 in the
+ * backend's scratch buffer first. */
+int cb_linear(cb_backend *b, int rows, int in, int out, cb_mem X, int64_t xoff,
+              cb_mem W, cb_mem bias, cb_mem Y, int64_t yoff, int act,
+              int residual);
+
+/* layernorm (sam3_ops.h:60-61): X F32 [rows, C] -> Y F32 or BF16; Y may
+ * alias X (F32). */
+int cb_layernorm(cb_backend *b, int64_t rows, int C, cb_mem X, cb_mem Y,
+                 cb_mem g, cb_mem bias, float eps, int act);
+
+/* add_bcast (sam3_ops.h:63-65): out[i] = a[i] + b[i % bmod]. */
+int cb_add_bcast(cb_backend *b, cb_mem out, cb_mem a, cb_mem bb, int64_t n,
+                 int64_t bmod);
+
+/* The static helpers of sam3_model.c that vit_block calls, exported so a
+ * caller can keep the reference's unfused sequence:
+ * softmax_rows (sam3_model.c:332-341), rope_apply (:965-978, table row =
+ * row % npos, on F32 qkv), window_partition / window_unpartition_add
+ * (:360-392), patch_im2col (sam3_model.c:1120-1130). */
+int cb_softmax_rows(cb_backend *b, cb_mem S, int64_t rows, int L);
+int cb_rope_apply(cb_backend *b, cb_mem qkv, int64_t rows, int E, int hd,
+                  int npos, cb_mem cs);
+int cb_window_partition(cb_backend *b, cb_mem X, cb_mem out, int H, int C,
+                        int ws, int nwx);
+int cb_window_unpartition_add(cb_backend *b, cb_mem X, cb_mem Wd, int H, int C,
+                              int ws, int nwx);
+int cb_patch_im2col(cb_backend *b, cb_mem img, cb_mem out, int side, int grid,
+                    int ps);
+
+/* Attention core of vit_block: the one additive operator. It replaces the
+ * inline sequence rope_apply -> QK^T gemm -> softmax_rows -> P.V gemm of
+ * sam3_model.c:998-1013 (the reference has no attention op in sam3_ops.h).
+ *
+ * qkv: [nseq * N, 3E] rows (q | k | v, head h at column h * hd), as the
+ * QKV linear leaves them. cs: RoPE table [npos, hd/2] (cos, sin) applied to
+ * q and k with table row = row % npos (cs == NULL: RoPE already applied).
+ * out: [nseq * N, E]. scale: 1/sqrt(hd) in vit_block.
+ *   mode CB_ATTN_TC:  bf16 operands, fp32 accumulation, tcgen05 tensor
+ *                     cores; qkv F32 (roped + cast into scratch) or BF16
+ *                     (already roped, cs must be NULL); out F32 or BF16.
+ *   mode CB_ATTN_F32: fp32 on CUDA cores (reference precision); qkv F32,
+ *                     out F32. With cs != NULL, qkv is roped IN PLACE, as
+ *                     the reference's rope_apply does.
+ * hd must be 64 (as load_encoder requires, sam3_model.c:511-513). */
+#define CB_ATTN_TC 0
+#define CB_ATTN_F32 1
+int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
+                 int hd, cb_mem cs, int npos, float scale, int mode,
+                 cb_mem out);
+
+/* mha (sam3_model.c:413-451): mask-decoder attention, 8 heads, scale
+ * 1/sqrt(dint/8); qp/kp/vp hold P prompts of Nq/Nk rows of dint channels
+ * with per-prompt strides sq/sk/sv in elements (0 = shared); o receives
+ * P * Nq rows. Nk > 64 requires dint == 128 (CB_EARG otherwise, as the
+ * reference's "mha: unsupported shape"). All F32. */
+int cb_mha(cb_backend *b, int P, int Nq, int Nk, int dint, cb_mem qp,
+           int64_t sq, cb_mem kp, int64_t sk, cb_mem vp, int64_t sv, cb_mem o);
+
+/* ------------------------------------------------------------ encoder
+ * The PE ViT trunk of sam3_model.c (load_encoder :473-581, alloc_buffers
+ * :815-916, vit_block :981-1028, sam_encode_trunk :1112-1144) on the
+ * tensor-core path, batched over image tiles. */
+typedef struct cb_encoder cb_encoder;
+
+struct cb_encoder_config {
+    int embed;         /* E, 1024 */
+    int depth;         /* blocks, 32 */
+    int heads;         /* 16 (head width E / heads must be 64) */
+    int mlp;           /* 4096 */
+    int grid;          /* tokens per side, 72 */
+    int patch;         /* 14 */
+    int window;        /* window side of windowed blocks, 24 */
+    int max_tiles;     /* work buffers sized for this many tiles at once */
+    uint64_t global_mask; /* bit i set: block i uses global attention */
+};
+
+/* Default SAM 3 geometry: 1024 wide, 32 blocks, global blocks 7/15/23/31. */
+void cb_encoder_default_config(struct cb_encoder_config *cfg);
+
+/* Allocate weights (bf16 matrices, fp32 vectors) and work buffers. */
+int cb_encoder_create(cb_backend *b, const struct cb_encoder_config *cfg,
+                      cb_encoder **out);
+void cb_encoder_free(cb_encoder *e);
+
+/* Random-init weights drawn on the device from include/sam3_synth.h
+ * streams: matrices N(0, std), biases 0, LayerNorm gamma 1 / beta 0,
+ * pos_embed N(0, std) on the 72 x 72 grid, 2D axial RoPE tables with
+ * `theta`. */
+int cb_encoder_init_random(cb_encoder *e, uint64_t seed, float std,
+                           double theta);
+
+/* Set one tensor from host fp32 data (a checkpoint loader's entry point).
+ * which: see CB_W_* below; block is ignored for trunk-level tensors.
+ * Shapes follow the PyTorch checkpoint (load_encoder, sam3_model.c:519-577):
+ * PATCH_W [E, 3, p, p], POS [grid^2, E] (already tiled to the grid, as
+ * sam3_model.c:492-498 does), LN_PRE_W/B [E], ROPE_WIN [window^2, hd/2, 2],
+ * ROPE_GLOB [grid^2, hd/2, 2], and per block N1_W/B, N2_W/B [E], QKV_W
+ * [3E, E], QKV_B [3E], PROJ_W [E, E], PROJ_B [E], FC1_W [mlp, E], FC1_B
+ * [mlp], FC2_W [E, mlp], FC2_B [E]. */
+#define CB_W_PATCH_W 0
+#define CB_W_POS 1
+#define CB_W_LN_PRE_W 2
+#define CB_W_LN_PRE_B 3
+#define CB_W_ROPE_WIN 4
+#define CB_W_ROPE_GLOB 5
+#define CB_W_N1_W 10
+#define CB_W_N1_B 11
+#define CB_W_QKV_W 12
+#define CB_W_QKV_B 13
+#define CB_W_PROJ_W 14
+#define CB_W_PROJ_B 15
+#define CB_W_N2_W 16
+#define CB_W_N2_B 17
+#define CB_W_FC1_W 18
+#define CB_W_FC1_B 19
+#define CB_W_FC2_W 20
+#define CB_W_FC2_B 21
+int cb_encoder_set_weight(cb_encoder *e, int which, int block,
+                          const float *src, size_t count);
+
+/* sam_encode_trunk on ntile uint8 HWC tiles (grid*patch square, RGB) in a
+ * device buffer `tiles` (CB_U8): patch embedding with the image
+ * normalisation of image.c:360-366, + pos_embed, ln_pre, all blocks.
+ * out: F32 [ntile, grid^2, E], tokens in raster order (the reference's
+ * m->x). ntile <= max_tiles. Asynchronous on the backend stream. */
+int cb_encode_tiles(cb_encoder *e, cb_mem tiles, int ntile, cb_mem out);
+
+/* Run blocks [first, last) on a raster-order F32 token buffer x [ntile,
+ * grid^2, E] in place (the prologue is skipped). For block-level tests. */
+int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last);
+
+/* Host-to-host convenience: copies tiles from host memory, encodes in
+ * chunks of at most max_tiles with the copies overlapped, and copies the
+ * tokens back to host memory out [ntile, grid^2, E]. Blocking. */
+int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
+                         float *out);
+
+/* Generator: fill a device buffer with normal(seed, stream, i) values
+ * (include/sam3_synth.h) as F32 or BF16 (the buffer's dtype). */
+int cb_synth_normal(cb_backend *b, uint64_t seed, uint64_t stream, float mean,
+                    float std, cb_mem out, size_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -26,8 +26,14 @@
 extern "C" {
 #endif
 
+#ifdef __CUDACC__
+#define SAM3_HD __host__ __device__
+#else
+#define SAM3_HD
+#endif
+
 /* splitmix64 finalizer. */
-static inline uint64_t sam3_mix64(uint64_t x)
+static inline SAM3_HD uint64_t sam3_mix64(uint64_t x)
 {
     x += 0x9E3779B97F4A7C15ULL;
     x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
@@ -35,13 +41,13 @@ static inline uint64_t sam3_mix64(uint64_t x)
     return x ^ (x >> 31);
 }
 
-static inline uint64_t sam3_stream_base(uint64_t seed, uint64_t stream)
+static inline SAM3_HD uint64_t sam3_stream_base(uint64_t seed, uint64_t stream)
 {
     return sam3_mix64(seed * 0xD1B54A32D192ED03ULL ^ sam3_mix64(stream));
 }
 
 /* Irwin-Hall(12) draw number i of a stream; see the file comment. */
-static inline float sam3_normal_at(uint64_t base, uint64_t i)
+static inline SAM3_HD float sam3_normal_at(uint64_t base, uint64_t i)
 {
     int64_t s = 0;
     for (int k = 0; k < 3; k++) {
@@ -52,7 +58,7 @@ static inline float sam3_normal_at(uint64_t base, uint64_t i)
     return (float)(s - 393210) * (1.0f / 65536.0f);
 }
 
-static inline uint8_t sam3_u8_at(uint64_t base, uint64_t i)
+static inline SAM3_HD uint8_t sam3_u8_at(uint64_t base, uint64_t i)
 {
     return (uint8_t)(sam3_mix64(base + (i >> 3)) >> (8 * (i & 7)));
 }

@@ -71,8 +71,8 @@ def lib():
         L.or_mha.argtypes = [C.c_int] * 4 + [f32p, C.c_long, f32p, C.c_long,
                                              f32p, C.c_long, f32p]
         L.or_attention.argtypes = [f32p] + [C.c_int] * 5 + [C.c_float, f32p]
-        L.or_encode_trunk.argtypes = [C.POINTER(Trunk), f32p, f32p, C.c_int,
-                                      C.c_int]
+        L.or_encode_trunk.argtypes = [C.POINTER(Trunk), C.c_void_p, f32p,
+                                      C.c_int, C.c_int]
         L.or_num_threads.restype = C.c_int
         L.sam3_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t,
                                         C.c_float, C.c_float, f32p]
@@ -202,10 +202,12 @@ def attention(qkv, nseq, N, E, heads, hd, alpha):
     return out
 
 
-def ref_attention(qkv, nseq, N, E, heads, hd, alpha, head_chunk=None):
+def ref_attention(qkv, nseq, N, E, heads, hd, alpha, head_chunk=None,
+                  softmax_local=None):
     """The reference's attention launches (sam3_model.c:1000-1013): QK^T
-    gemm_cpu_t, softmax_rows (work-group 256), P.V gemm_cpu_n, heads chunked
-    like head_chunk() (sam3_model.c:793-798)."""
+    gemm_cpu_t, softmax_rows (work-group 256 as sam3_model.c:336 picks, or
+    softmax_local items), P.V gemm_cpu_n, heads chunked like head_chunk()
+    (sam3_model.c:793-798)."""
     qkv = np.ascontiguousarray(qkv, np.float32)
     out = np.zeros((nseq * N, E), np.float32)
     hc = heads if head_chunk is None else head_chunk
@@ -218,7 +220,8 @@ def ref_attention(qkv, nseq, N, E, heads, hd, alpha, head_chunk=None):
                  lda=3 * E, sa=(tstride, hd), boff=E + h0 * hd, ldb=3 * E,
                  sb=(tstride, hd), ldc=N, sc=(hcc * plane, plane), nb1=hcc,
                  alpha=alpha)
-        ref().ref_softmax_rows(S, nseq * hcc * N, N, 256 if N >= 256 else 64)
+        ref().ref_softmax_rows(S, nseq * hcc * N, N, softmax_local or
+                               (256 if N >= 256 else 64))
         ref_gemm(N, hd, N, S, qkv, 0, out, nb=nseq * hcc, lda=N,
                  sa=(hcc * plane, plane), boff=2 * E + h0 * hd, ldb=3 * E,
                  sb=(tstride, hd), coff=h0 * hd, ldc=E, sc=(N * E, hd),
@@ -301,10 +304,12 @@ class TrunkWeights:
 
 
 def encode_trunk(w, img_chw, first=0, last=None, x=None):
-    """sam_encode_trunk (sam3_model.c:1112-1144); returns x [T, E]."""
+    """sam_encode_trunk (sam3_model.c:1112-1144); returns x [T, E]. With
+    img_chw None the prologue is skipped and x is block `first`'s input."""
     T = w.grid * w.grid
     x = np.zeros((T, w.E), np.float32) if x is None else x
     t = w.ctypes()
-    lib().or_encode_trunk(C.byref(t), np.ascontiguousarray(img_chw, np.float32),
-                          x, first, w.depth if last is None else last)
+    img = None if img_chw is None else np.ascontiguousarray(img_chw, np.float32)
+    lib().or_encode_trunk(C.byref(t), None if img is None else img.ctypes.data, x, first,
+                          w.depth if last is None else last)
     return x

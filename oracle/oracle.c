@@ -598,7 +598,7 @@ void or_encode_trunk(const struct or_trunk *t, const float *img, float *x,
     const int K = 3 * t->patch * t->patch;
     int i;
 
-    if (first == 0) {
+    if (img) {
         float *col = malloc(sizeof(float) * (size_t)T * K);
 
         or_patch_im2col(img, col, t->img, G, t->patch);

@@ -88,8 +88,9 @@ void or_vit_block(const struct or_trunk *t, const struct or_block *b, float *x);
 
 /* sam_encode_trunk (sam3_model.c:1112-1144) on a normalised CHW image;
  * x [grid^2, E] receives the output tokens. first/last select blocks
- * [first, last) (0, depth for the whole trunk); with first > 0 the prologue
- * is skipped and x is the input. */
+ * [first, last) (0, depth for the whole trunk). With img == NULL the
+ * prologue (patch embedding, pos_embed, ln_pre) is skipped and x is the
+ * input of block `first`. */
 void or_encode_trunk(const struct or_trunk *t, const float *img, float *x,
                      int first, int last);
 

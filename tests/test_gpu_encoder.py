@@ -1,0 +1,105 @@
+"""GPU parity of the PE backbone (the encoder of the C-ABI) against the
+oracle's restatement of sam_encode_trunk / vit_block, same seeded weights
+and tiles. embeddings cosine >= 0.999 vs fp32."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "backbone_c4.npz")
+
+
+def cos_sim(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def image_stream(tile):
+    return 3 * 1000003 + tile
+
+
+def test_encoder_two_blocks_vs_oracle(cb, sb, ob):
+    """Prologue + one windowed and one global block, full 72 x 72 grid."""
+    seed = 5
+    enc = sb.Encoder(cb, max_tiles=1, depth=2, global_blocks=(1,))
+    enc.init_random(seed)
+    img = ob.u8(seed, image_stream(0), (1008, 1008, 3))
+    tiles = cb.upload(img, sb.U8)
+    out = cb.alloc(5184 * 1024 * 4, sb.F32)
+    enc.encode_tiles(tiles, 1, out)
+    got = np.empty((5184, 1024), np.float32)
+    cb.read(out, got)
+    cb.sync()
+    w = ob.TrunkWeights(seed, depth=2, global_blocks=(1,))
+    want = ob.encode_trunk(w, ob.image_input(img))
+    c = cos_sim(got, want)
+    assert c >= 0.999, c
+    assert np.abs(got - want).max() < 0.1 * np.abs(want).max()
+    enc.close()
+
+
+def test_encoder_batch_equals_single_tiles(cb, sb, ob):
+    """Batching tiles into one GEMM M dimension does not change results."""
+    seed = 6
+    enc = sb.Encoder(cb, max_tiles=2, depth=2, global_blocks=(0,))
+    enc.init_random(seed)
+    imgs = np.stack([ob.u8(seed, image_stream(t), (1008, 1008, 3)) for t in range(2)])
+    tiles = cb.upload(imgs, sb.U8)
+    out2 = cb.alloc(2 * 5184 * 1024 * 4, sb.F32)
+    enc.encode_tiles(tiles, 2, out2)
+    both = np.empty((2, 5184, 1024), np.float32)
+    cb.read(out2, both)
+    for t in range(2):
+        one = cb.upload(imgs[t], sb.U8)
+        out1 = cb.alloc(5184 * 1024 * 4, sb.F32)
+        enc.encode_tiles(one, 1, out1)
+        single = np.empty((5184, 1024), np.float32)
+        cb.read(out1, single)
+        assert np.array_equal(single, both[t])
+    enc.close()
+
+
+def test_encode_blocks_matches_oracle_vit_block(cb, sb, ob):
+    """cb_encode_blocks on raster tokens == oracle vit_block, per block kind."""
+    seed = 7
+    enc = sb.Encoder(cb, max_tiles=1, depth=2, global_blocks=(1,))
+    enc.init_random(seed)
+    w = ob.TrunkWeights(seed, depth=2, global_blocks=(1,))
+    x0 = ob.normal(seed, 99, (5184, 1024))
+    for blk in (0, 1):
+        mx = cb.upload(x0, sb.F32)
+        enc.encode_blocks(mx, 1, blk, blk + 1)
+        got = np.empty_like(x0)
+        cb.read(mx, got)
+        want = x0.copy()
+        ob.encode_trunk(w, None, blk, blk + 1, x=want)
+        assert cos_sim(got - x0, want - x0) >= 0.999
+    enc.close()
+
+
+def test_encoder_full_backbone_vs_golden(cb, sb):
+    """Config 4: the whole 32-block trunk on one tile vs the oracle's output
+    (tests/golden/make_backbone_golden.py)."""
+    if not os.path.exists(GOLDEN):
+        pytest.skip("backbone golden fixture missing")
+    g = np.load(GOLDEN)
+    seed = int(g["seed"])
+    enc = sb.Encoder(cb, max_tiles=1)
+    enc.init_random(seed)
+    from oracle import binding as ob
+    img = ob.u8(seed, image_stream(0), (1008, 1008, 3))
+    tiles = cb.upload(img, sb.U8)
+    out = cb.alloc(5184 * 1024 * 4, sb.F32)
+    enc.encode_tiles(tiles, 1, out)
+    got = np.empty((5184, 1024), np.float32)
+    cb.read(out, got)
+    cb.sync()
+    rows = g["rows"]
+    c = cos_sim(got[rows], g["x"])
+    assert c >= 0.999, c
+    assert abs(float(got.std()) - float(g["std"])) < 0.01 * float(g["std"])
+    enc.close()

@@ -1,0 +1,306 @@
+"""GPU parity of the CUDA operators, called through the C-ABI.
+
+Floating-point kernels are compared with the oracle (the C restatement of
+the reference kernels, itself pinned to the reference's own kernel source)
+on the same seeded inputs. Tolerances:
+  * bf16 tensor-core paths: max-abs <= 1e-2 and cosine >= 0.9999 against
+    the fp32 oracle for attention; GEMMs against the
+    fp32 product of the same bf16-rounded operands, rel. error <= 1e-3;
+  * fp32 CUDA-core paths: max-abs <= 1e-4 (accumulation order only);
+  * index / copy kernels (window partition, im2col, add_bcast, RoPE):
+    bit-exact where the arithmetic is the same single rounding.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+SEED = 424242
+
+
+def cos_sim(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def bf16_round(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).float().numpy()
+
+
+def dev(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dtype).cuda()
+
+
+# ------------------------------------------------------------------ basics
+def test_device_generator_matches_host(cb, sb, ob):
+    for dt, tdt in ((sb.F32, torch.float32), (sb.BF16, torch.bfloat16)):
+        t = torch.empty(100003, dtype=tdt, device="cuda")
+        m = cb.wrap(t)
+        cb.synth_normal(11, 77, 0.5, 0.02, m, t.numel())
+        cb.sync()
+        host = ob.normal(11, 77, (100003,), 0.5, 0.02)
+        if dt == sb.F32:
+            assert np.array_equal(t.cpu().numpy(), host)
+        else:
+            assert torch.equal(t.cpu(), torch.from_numpy(host).to(torch.bfloat16))
+
+
+def test_read_write_roundtrip(cb, sb):
+    a = np.arange(1000, dtype=np.float32)
+    m = cb.upload(a, sb.F32)
+    out = np.empty_like(a)
+    cb.read(m, out)
+    assert np.array_equal(a, out)
+    with pytest.raises(sb.CBError):
+        cb.read(m, np.empty(2000, np.float32))  # beyond the buffer
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (5184, 1024, 1024),
+                                   (129, 3072, 1024), (77, 64, 40)])
+@pytest.mark.parametrize("out_bf16", [False, True])
+def test_gemm_tc_vs_fp32_product(cb, sb, M, N, K, out_bf16):
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    B = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+    bias = torch.randn(N, generator=g).cuda()
+    R = torch.randn(M, N, generator=g).cuda()
+    C = torch.empty(M, N, dtype=torch.bfloat16 if out_bf16 else torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    mA, mB, mC, mb = cb.wrap(A), cb.wrap(B), cb.wrap(C), cb.wrap(bias)
+    mR = None if out_bf16 else cb.wrap(R)
+    act = sb.ACT_GELU if out_bf16 else sb.ACT_NONE
+    cb.gemm(M, N, K, (mA, 0, K), (mB, 0, K), 1, (mC, 0, N), bias=mb, R=mR,
+            alpha=0.75, act=act)
+    cb.sync()
+    ref = 0.75 * (A.float() @ B.float().T) + bias
+    if act == sb.ACT_GELU:
+        ref = torch.nn.functional.gelu(ref)
+    if mR is not None:
+        ref = ref + R
+    err = (C.float() - ref).abs().max().item()
+    tol = (2e-2 if out_bf16 else 1e-3) * max(1.0, ref.abs().max().item())
+    assert err <= tol, (err, tol)
+
+
+def test_linear_fp32_activations_bf16_weights_vs_oracle(cb, sb, ob):
+    """linear() with the reference's fp32 activations and bf16-stored weights
+    (the analogue of precision=fp16 weights) against the oracle's
+    gemm_cpu_t arithmetic on the same inputs."""
+    rows, n_in, n_out = 333, 256, 192
+    X = ob.normal(SEED, 1, (rows, n_in))
+    W = ob.normal(SEED, 2, (n_out, n_in), 0.0, 0.05)
+    b = ob.normal(SEED, 3, (n_out,))
+    Y0 = ob.normal(SEED, 4, (rows, n_out))
+    mX = cb.upload(X, sb.F32)
+    mW = cb.upload_weight(W, sb.BF16)
+    mb = cb.upload(b, sb.F32)
+    mY = cb.upload(Y0, sb.F32)
+    cb.linear(rows, n_in, n_out, mX, 0, mW, mb, mY, 0, sb.ACT_GELU, 1)
+    got = np.empty_like(Y0)
+    cb.read(mY, got)
+    want = Y0.copy()
+    ob.gemm(rows, n_out, n_in, X, W, 1, want, bias=b, R=want, act=1)
+    assert np.abs(got - want).max() < 2e-2
+    assert cos_sim(got, want) > 0.9999
+
+
+def test_gemm_simt_reference_contract_batched(cb, sb, ob):
+    """The batched, strided QK^T / P.V launches of vit_block
+    (sam3_model.c:1004-1012) through the generic path, fp32."""
+    N, E, hd, heads, nseq = 40, 128, 64, 2, 3
+    qkv = ob.normal(SEED, 10, (nseq * N, 3 * E))
+    tstride, plane = N * 3 * E, N * N
+    S = np.zeros(nseq * heads * plane, np.float32)
+    mq = cb.upload(qkv, sb.F32)
+    mS = cb.upload(S, sb.F32)
+    cb.gemm(N, N, hd, (mq, 0, 3 * E, tstride, hd), (mq, E, 3 * E, tstride, hd), 1,
+            (mS, 0, N, heads * plane, plane), nb=nseq * heads, nb1=heads, alpha=0.125)
+    got = np.empty_like(S)
+    cb.read(mS, got)
+    want = S.copy()
+    ob.gemm(N, N, hd, qkv, qkv, 1, want, nb=nseq * heads, aoff=0, lda=3 * E,
+            sa=(tstride, hd), boff=E, ldb=3 * E, sb=(tstride, hd), ldc=N,
+            sc=(heads * plane, plane), nb1=heads, alpha=0.125)
+    assert np.abs(got - want).max() < 1e-4
+
+
+# ------------------------------------------------------------------ attention
+def _attn_case(ob, side, nseq, E=1024, stream=20):
+    N = side * side
+    qkv = ob.normal(SEED, stream, (nseq * N, 3 * E))
+    cs = ob.rope_axial(side, 64)
+    roped = ob.rope_apply(qkv, E, 64, N, cs)
+    return N, qkv, cs, roped
+
+
+@pytest.mark.parametrize("side,nseq", [(6, 2), (24, 9), (13, 3)])
+def test_attention_tc_vs_oracle(cb, sb, ob, side, nseq):
+    """Config 1 (9 windows of 24x24, 16 heads) and odd sizes: bf16 tensor
+    cores, RoPE + bf16 cast fused ahead of the kernel, fp32 output."""
+    E = 1024
+    N, qkv, cs, roped = _attn_case(ob, side, nseq, E)
+    want = ob.attention(roped, nseq, N, E, 16, 64, 0.125)
+    mq = cb.upload(qkv, sb.F32)
+    mcs = cb.upload(cs, sb.F32)
+    mo = cb.alloc(nseq * N * E * 4, sb.F32)
+    cb.attention(mq, nseq, N, E, 16, 64, mcs, N, 0.125, sb.ATTN_TC, mo)
+    got = np.empty((nseq * N, E), np.float32)
+    cb.read(mo, got)
+    cb.sync()
+    assert np.abs(got - want).max() <= 1e-2
+    assert cos_sim(got, want) >= 0.9999
+
+
+def test_attention_tc_global_vs_oracle(cb, sb, ob):
+    """Config 2: global attention over the 72 x 72 grid, 16 heads."""
+    E = 1024
+    N, qkv, cs, roped = _attn_case(ob, 72, 1, E, stream=21)
+    want = ob.attention(roped, 1, N, E, 16, 64, 0.125)
+    mq = cb.upload(qkv, sb.F32)
+    mcs = cb.upload(cs, sb.F32)
+    for mode in (sb.ATTN_TC, sb.ATTN_F32):
+        mo = cb.alloc(N * E * 4, sb.F32)
+        mq2 = cb.upload(qkv, sb.F32)  # fp32 mode ropes in place
+        cb.attention(mq2, 1, N, E, 16, 64, mcs, N, 0.125, mode, mo)
+        got = np.empty((N, E), np.float32)
+        cb.read(mo, got)
+        cb.sync()
+        if mode == sb.ATTN_TC:
+            assert np.abs(got - want).max() <= 1e-2
+            assert cos_sim(got, want) >= 0.9999
+        else:
+            assert np.abs(got - want).max() <= 1e-4
+
+
+def test_attention_f32_windowed_vs_oracle(cb, sb, ob):
+    E = 1024
+    N, qkv, cs, roped = _attn_case(ob, 24, 9, E, stream=22)
+    want = ob.attention(roped, 9, N, E, 16, 64, 0.125)
+    mq = cb.upload(qkv, sb.F32)
+    mcs = cb.upload(cs, sb.F32)
+    mo = cb.alloc(9 * N * E * 4, sb.F32)
+    cb.attention(mq, 9, N, E, 16, 64, mcs, N, 0.125, sb.ATTN_F32, mo)
+    got = np.empty((9 * N, E), np.float32)
+    cb.read(mo, got)
+    assert np.abs(got - want).max() <= 1e-4
+    # the fp32 mode ropes qkv in place, as rope_apply does
+    roped_dev = np.empty_like(qkv)
+    cb.read(mq, roped_dev)
+    assert np.abs(roped_dev - roped).max() <= 1e-6
+
+
+# ------------------------------------------------------------------ elementwise
+def test_layernorm_vs_oracle(cb, sb, ob):
+    for rows, Cn in ((1000, 1024), (77, 256), (33, 100)):
+        X = ob.normal(SEED, 30, (rows, Cn), 0.3, 2.0)
+        g = ob.normal(SEED, 31, (Cn,), 1.0, 0.1)
+        b = ob.normal(SEED, 32, (Cn,), 0.0, 0.1)
+        want = ob.layernorm(X, g, b, 1e-5, 0)
+        mX, mg, mb = cb.upload(X, sb.F32), cb.upload(g, sb.F32), cb.upload(b, sb.F32)
+        for ydt in (sb.F32, sb.BF16):
+            mY = cb.alloc(rows * Cn * (4 if ydt == sb.F32 else 2), ydt)
+            cb.layernorm(rows, Cn, mX, mY, mg, mb, 1e-5, 0)
+            if ydt == sb.F32:
+                got = np.empty_like(X)
+                cb.read(mY, got)
+                assert np.abs(got - want).max() < 1e-4
+            else:
+                raw = np.empty(rows * Cn, np.uint16)
+                cb.read(mY, raw)
+                got = (raw.astype(np.uint32) << 16).view(np.float32).reshape(rows, Cn)
+                assert np.abs(got - want).max() < 3e-2
+        # in place (Y aliases X), as ln_pre runs
+        cb.layernorm(rows, Cn, mX, mX, mg, mb, 1e-5, 0)
+        got = np.empty_like(X)
+        cb.read(mX, got)
+        assert np.abs(got - want).max() < 1e-4
+
+
+def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
+    S = ob.normal(SEED, 40, (50, 576), 0.0, 3.0)
+    mS = cb.upload(S, sb.F32)
+    cb.softmax_rows(mS, 50, 576)
+    got = np.empty_like(S)
+    cb.read(mS, got)
+    assert np.abs(got - ob.softmax_rows(S)).max() < 1e-6
+
+    E, side = 128, 6
+    qkv = ob.normal(SEED, 41, (2 * side * side, 3 * E))
+    cs = ob.rope_axial(side, 64)
+    mq, mcs = cb.upload(qkv, sb.F32), cb.upload(cs, sb.F32)
+    cb.rope_apply(mq, 2 * side * side, E, 64, side * side, mcs)
+    got = np.empty_like(qkv)
+    cb.read(mq, got)
+    assert np.abs(got - ob.rope_apply(qkv, E, 64, side * side, cs)).max() < 1e-6
+
+    H, Cn, ws = 10, 8, 4
+    nwx = 3
+    X = ob.normal(SEED, 42, (H * H, Cn))
+    Wd = ob.normal(SEED, 43, (nwx * nwx * ws * ws, Cn))
+    mX, mW = cb.upload(X, sb.F32), cb.upload(Wd, sb.F32)
+    mP = cb.alloc(nwx * nwx * ws * ws * Cn * 4, sb.F32)
+    cb.window_partition(mX, mP, H, Cn, ws, nwx)
+    cb.window_unpartition_add(mX, mW, H, Cn, ws, nwx)
+    part = np.empty((nwx * nwx * ws * ws, Cn), np.float32)
+    cb.read(mP, part)
+    want_p = np.empty_like(part)
+    ob.lib().or_window_partition(X, want_p, H, Cn, ws, nwx)
+    assert np.array_equal(part, want_p)
+    got = np.empty_like(X)
+    cb.read(mX, got)
+    want_u = X.copy()
+    ob.lib().or_window_unpartition_add(want_u, Wd, H, Cn, ws, nwx)
+    assert np.array_equal(got, want_u)
+
+    grid, ps = 4, 5
+    img_side = grid * ps + 3
+    img = ob.normal(SEED, 44, (3, img_side, img_side))
+    mI = cb.upload(img, sb.F32)
+    mC = cb.alloc(grid * grid * 3 * ps * ps * 4, sb.F32)
+    cb.patch_im2col(mI, mC, img_side, grid, ps)
+    col = np.empty((grid * grid, 3 * ps * ps), np.float32)
+    cb.read(mC, col)
+    want_c = np.empty_like(col)
+    ob.lib().or_patch_im2col(img, want_c, img_side, grid, ps)
+    assert np.array_equal(col, want_c)
+
+    a = ob.normal(SEED, 45, (1000,))
+    bb = ob.normal(SEED, 46, (48,))
+    ma, mb2 = cb.upload(a, sb.F32), cb.upload(bb, sb.F32)
+    cb.add_bcast(ma, ma, mb2, 1000, 48)
+    got = np.empty_like(a)
+    cb.read(ma, got)
+    assert np.array_equal(got, a + np.tile(bb, 1000 // 48 + 1)[:1000])
+
+
+# ------------------------------------------------------------------ decoder attention
+@pytest.mark.parametrize("name,P,Nq,Nk,dint,shared", [
+    ("self", 64, 8, 8, 256, False),
+    ("t2i", 64, 8, 5184, 128, False),
+    ("t2i_shared", 64, 7, 5184, 128, True),
+    ("i2t", 16, 5184, 8, 128, False),
+    ("self7", 64, 7, 7, 256, False),
+])
+def test_mha_vs_oracle(cb, sb, ob, name, P, Nq, Nk, dint, shared):
+    q = ob.normal(SEED, 50, (P * Nq, dint))
+    kvp = 1 if shared else P
+    k = ob.normal(SEED, 51, (kvp * Nk, dint))
+    v = ob.normal(SEED, 52, (kvp * Nk, dint))
+    sk = 0 if shared else Nk * dint
+    want = ob.mha(P, Nq, Nk, dint, q, Nq * dint, k, sk, v, sk)
+    mq, mk, mv = cb.upload(q, sb.F32), cb.upload(k, sb.F32), cb.upload(v, sb.F32)
+    mo = cb.alloc(P * Nq * dint * 4, sb.F32)
+    cb.mha(P, Nq, Nk, dint, mq, Nq * dint, mk, sk, mv, sk, mo)
+    got = np.empty((P * Nq, dint), np.float32)
+    cb.read(mo, got)
+    assert np.abs(got - want).max() < 1e-4
+
+
+def test_mha_rejects_unsupported_shape(cb, sb):
+    m = cb.alloc(8 * 100 * 256 * 4, sb.F32)
+    with pytest.raises(sb.CBError) as e:
+        cb.mha(1, 8, 100, 256, m, 0, m, 0, m, 0, m)
+    assert e.value.status == 3
