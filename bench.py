@@ -361,6 +361,33 @@ def our_arm(args, world, rank, local, pg):
     return line
 
 
+def profile_case(ntile):
+    """Small case for ncu captures: a 2-block trunk (one windowed, one global
+    block) on `ntile` tiles, encoded twice. Per encode the launches are
+    patch_in, gemm (patch), layernorm, then per block layernorm, gemm (qkv),
+    attention, gemm (proj), layernorm, gemm (fc1), gemm (fc2), and the final
+    unpermute; so with -k regex:gemm_bf16 the 13th GEMM launch is the second
+    encode's fc1, and with -k regex:attn_tc launches 3-4 are the second
+    encode's windowed and global attention."""
+    import torch
+    sb = load_product()
+    cb = sb.Backend(0)
+    enc = sb.Encoder(cb, max_tiles=ntile, depth=2, global_blocks=(1,))
+    enc.init_random(SEED)
+    tiles = torch.empty(ntile, SIDE, SIDE, 3, dtype=torch.uint8)
+    for i in range(ntile):
+        sb.lib().sam3_synth_u8(SEED, image_stream(i), SIDE * SIDE * 3, tiles[i].data_ptr())
+    dev = tiles.cuda()
+    out = torch.empty(ntile, 5184, 1024, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(2):
+        enc.encode_tiles(cb.wrap(dev), ntile, cb.wrap(out))
+    cb.sync()
+    enc.close()
+    cb.close()
+    print(f"profile case done: {ntile} tiles, 2 blocks, 2 encodes")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -368,7 +395,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="TILES",
+                    help="run the small ncu case on TILES tiles and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     world, rank, local, pg = dist_setup(args)
     if args.impl == "reference":
         line = reference_arm(args, world, rank)
