@@ -30,7 +30,8 @@ EXPORTS = [
     "cb_profile_entry", "cb_mat", "cb_bmat",
     "cb_gemm", "cb_linear", "cb_layernorm", "cb_add_bcast", "cb_softmax_rows",
     "cb_rope_apply", "cb_window_partition", "cb_window_unpartition_add",
-    "cb_patch_im2col", "cb_attention", "cb_mha", "cb_encoder_default_config",
+    "cb_patch_im2col", "cb_attention", "cb_attention_noalloc", "cb_mha",
+    "cb_encoder_default_config",
     "cb_encoder_create", "cb_encoder_free", "cb_encoder_init_random",
     "cb_encoder_set_weight", "cb_encode_tiles", "cb_encode_blocks",
     "cb_encode_tiles_host", "cb_synth_normal",
@@ -112,6 +113,7 @@ def lib():
         "cb_window_unpartition_add": (i32, [vp, vp, vp, i32, i32, i32, i32]),
         "cb_patch_im2col": (i32, [vp, vp, vp, i32, i32, i32]),
         "cb_attention": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, i32, f32, i32, vp]),
+        "cb_attention_noalloc": (i32, [vp, i32, i32, i32, i32, vp, i32, f32, vp, vp, vp]),
         "cb_mha": (i32, [vp, i32, i32, i32, i32, vp, i64, vp, i64, vp, i64, vp]),
         "cb_encoder_default_config": (None, [C.POINTER(EncoderConfig)]),
         "cb_encoder_create": (i32, [vp, C.POINTER(EncoderConfig), C.POINTER(vp)]),

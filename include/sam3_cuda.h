@@ -182,6 +182,38 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
                  int hd, cb_mem cs, int npos, float scale, int mode,
                  cb_mem out);
 
+/* Allocation-free variant of cb_attention (mode CB_ATTN_TC, fp32 qkv in,
+ * fp32 out). No counterpart in the reference: it exists for callers that
+ * cannot let a library call cudaMalloc -- code that hands all device memory
+ * to its own pool or arena (an inference server's allocator, PyTorch's
+ * caching allocator) and must not see allocations behind its back, and code
+ * on a latency path where cudaMalloc/cudaFree and the synchronisation they
+ * imply are not acceptable. cb_attention stages the bf16 copy of qkv in the
+ * backend's scratch buffer, which it grows with cudaMalloc; this entry point
+ * stages it in a fixed 32 MiB array compiled into the library instead, and
+ * calls no cudaMalloc, cudaFree or allocating routine.
+ *
+ * Plain device pointers, no backend: qkv [nseq * N, 3E] fp32, cs (cos, sin)
+ * table [npos, 32] fp32 or NULL (no RoPE), out [nseq * N, E] fp32, stream a
+ * cudaStream_t (NULL = default stream); runs on the current device and is
+ * asynchronous on `stream`. err: a caller-owned device int, zeroed by the
+ * caller, that receives CB_ETIMEOUT-style device codes (nonzero = a kernel
+ * wait ran out); NULL uses a word inside the library, cleared on each call.
+ *
+ * Limits: hd 64 (E = 64 * heads); nseq * N * 3E * 2 bytes must fit the
+ * 32 MiB array (at E = 1024: at most 5461 rows, which covers the 9 x 576
+ * windows and the 5184-token global grid of one tile); larger inputs return
+ * CB_EARG before any work is queued.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture. Every call shares the one array, which keeps
+ * the previous call's contents: calls that overlap on the GPU (different
+ * streams, or different host threads on one device) race on it. Each GPU
+ * that loads the library holds the 32 MiB until the process exits. */
+int cb_attention_noalloc(const float *qkv, int nseq, int N, int E, int heads,
+                         const float *cs, int npos, float scale, float *out,
+                         int *err, void *stream);
+
 /* mha (sam3_model.c:413-451): mask-decoder attention, 8 heads, scale
  * 1/sqrt(dint/8); qp/kp/vp hold P prompts of Nq/Nk rows of dint channels
  * with per-prompt strides sq/sk/sv in elements (0 = shared); o receives
