@@ -213,18 +213,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc_fence_after();
                 const int valid = a.N - j * BKV;
-                // Pass 1: row maximum of the scaled scores.
-                float mx = -INFINITY;
+                // Only a sequence's last KV tile can hold keys beyond N.
+                const bool masked = valid < BKV;
+                // Pass 1: row maximum of the scaled scores (64 columns per
+                // TMEM round trip, four independent max chains).
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll 1
-                for (int c = 0; c < BKV / 32; c++) {
-                    uint32_t s[32];
-                    tmem_ld32(tS + c * 32, s);
+                for (int c = 0; c < BKV / 32; c += 2) {
+                    uint32_t s[64];
+                    tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(s));
+                    tmem_ld32(tS + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
                     tmem_wait_ld();
+                    if (masked) {
 #pragma unroll
-                    for (int e = 0; e < 32; e++)
-                        if (c * 32 + e < valid)
-                            mx = fmaxf(mx, __uint_as_float(s[e]));
+                        for (int e = 0; e < 64; e++)
+                            if (c * 32 + e >= valid)
+                                s[e] = __float_as_uint(-INFINITY);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 64; e += 4) {
+                        mx0 = fmaxf(mx0, __uint_as_float(s[e]));
+                        mx1 = fmaxf(mx1, __uint_as_float(s[e + 1]));
+                        mx2 = fmaxf(mx2, __uint_as_float(s[e + 2]));
+                        mx3 = fmaxf(mx3, __uint_as_float(s[e + 3]));
+                    }
                 }
+                const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
                 const float m_new = fmaxf(m_run, mx * sl2);
                 // Fold the previous tile's P.V (relative to m_run) into O.
                 if (j > 0) {
@@ -243,38 +257,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                             o[c * 32 + e] += __uint_as_float(pv[e]);
                     }
                 }
-                const float alpha = ex2_approx(m_run - m_new);
+                if (m_new != m_run) {  // rescale only when the maximum moved
+                    const float alpha = ex2_approx(m_run - m_new);
 #pragma unroll
-                for (int d = 0; d < HD; d++)
-                    o[d] *= alpha;
-                l_run *= alpha;
+                    for (int d = 0; d < HD; d++)
+                        o[d] *= alpha;
+                    l_run *= alpha;
+                }
                 // Pass 2: P = 2^(s * scale_log2 - m_new) as bf16 into smem
                 // (K-major, 128B swizzle: 16-byte chunk q of row r at
-                // chunk q ^ (r & 7)).
+                // chunk q ^ (r & 7)); four independent row-sum chains.
+                float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
 #pragma unroll 1
-                for (int c = 0; c < BKV / 32; c++) {
-                    uint32_t s[32];
-                    tmem_ld32(tS + c * 32, s);
+                for (int c = 0; c < BKV / 32; c += 2) {
+                    uint32_t s[64];
+                    tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(s));
+                    tmem_ld32(tS + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
                     tmem_wait_ld();
-                    float p[32];
+                    float p[64];
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        p[e] = (c * 32 + e < valid)
-                                   ? ex2_approx(fmaf(__uint_as_float(s[e]), sl2, -m_new))
-                                   : 0.0f;
-                        l_run += p[e];
+                    for (int e = 0; e < 64; e++)
+                        p[e] = ex2_approx(fmaf(__uint_as_float(s[e]), sl2, -m_new));
+                    if (masked) {
+#pragma unroll
+                        for (int e = 0; e < 64; e++)
+                            if (c * 32 + e >= valid)
+                                p[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 64; e += 4) {
+                        l0 += p[e];
+                        l1 += p[e + 1];
+                        l2 += p[e + 2];
+                        l3 += p[e + 3];
                     }
                     const uint32_t sub = pbase + (c >> 1) * P_SUB;
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int chunk = (c & 1) * 4 + q;
-                        st_shared_v4(sub + ((chunk ^ (r & 7)) << 4),
+                    for (int q = 0; q < 8; q++)
+                        st_shared_v4(sub + ((q ^ (r & 7)) << 4),
                                      pack_bf16x2(p[q * 8 + 0], p[q * 8 + 1]),
                                      pack_bf16x2(p[q * 8 + 2], p[q * 8 + 3]),
                                      pack_bf16x2(p[q * 8 + 4], p[q * 8 + 5]),
                                      pack_bf16x2(p[q * 8 + 6], p[q * 8 + 7]));
-                    }
                 }
+                l_run += (l0 + l1) + (l2 + l3);
                 m_run = m_new;
                 fence_proxy_async_smem();
                 tc_fence_before();

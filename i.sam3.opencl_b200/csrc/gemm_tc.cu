@@ -6,13 +6,19 @@
 // optional RoPE rotation of the q/k columns (rope_apply,
 // sam3_kernels.cl:679-698) so the QKV output feeds attention directly.
 //
-// One CTA per SM, 6 warps:
-//   warp 0  TMA producer: A/B k-blocks of 64 into a 4-stage smem ring;
-//   warp 1  tensor-memory owner and MMA issuer (one elected thread):
-//           128 x BN x 16 tcgen05.mma into one of two TMEM accumulators;
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//           lanes 32*(w%4)...), epilogue math, global stores, then release
-//           the accumulator so the MMA of the next tile overlaps.
+// One CTA per SM, 10 warps:
+//   warp 0    TMA producer: A/B k-blocks of 64 into a shared-memory ring;
+//   warp 1    tensor-memory owner and MMA issuer (one elected thread):
+//             128 x BN x 16 tcgen05.mma into one of two TMEM accumulators;
+//   warps 2-9 epilogue, two warps per TMEM lane quarter (warp w reads lanes
+//             32*(w%4)...), splitting the tile's 128-byte column chunks:
+//             tcgen05.ld, epilogue math, the chunk written 128B-swizzled
+//             into a per-warp staging tile and stored by TMA (coalesced,
+//             asynchronous, rows/columns beyond C clipped by the tensor
+//             map). Double-buffered staging lets the next chunk's math
+//             overlap the previous chunk's store; the accumulator is
+//             released as soon as it is read, so the MMAs of the next tile
+//             overlap the epilogue of this one.
 // Tiles are visited m-major (all n-tiles of a row block back to back) so a
 // row block of A is read from HBM once and re-read from L2.
 #include "kernels.h"
@@ -26,8 +32,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageTile = 32 * 128;  // one warp's 32 rows x 128 bytes
 
 struct GemmEpi {
     int M, N, K;
@@ -45,10 +52,12 @@ struct GemmEpi {
 
 template <int BN>
 struct GemmSmem {
+    static constexpr int STAGES = BN == 256 ? 3 : 4;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 2 * kStageTile;
     // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort
     static constexpr int BYTES = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
 };
@@ -78,33 +87,44 @@ __device__ __forceinline__ int rope_row(const k_rope &r, int m)
     return y * r.grid + x;
 }
 
-// Applies the epilogue to 32 consecutive accumulator columns of row m,
-// starting at column n, and stores them.
-template <bool OUT_BF16>
-__device__ __forceinline__ void epilogue_chunk(const GemmEpi &p, int m, int n, uint32_t (&r)[32],
-                                               int rrow)
+// Epilogue math on CW consecutive columns of row m starting at column n:
+// alpha, bias, activation, residual, RoPE (the reference's order).
+template <int CW>
+__device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, float (&v)[CW],
+                                              int rrow)
 {
-    float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; j++)
-        v[j] = p.alpha * __uint_as_float(r[j]);
-    const int nvalid = min(32, p.N - n);
+    for (int j = 0; j < CW; j++)
+        v[j] *= p.alpha;
+    const bool full = n + CW <= p.N;
     if (p.bias) {
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (j < nvalid)
-                v[j] += __ldg(p.bias + n + j);
+            for (int j = 0; j < CW; j += 4) {
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + n + j));
+                v[j] += b.x;
+                v[j + 1] += b.y;
+                v[j + 2] += b.z;
+                v[j + 3] += b.w;
+            }
+        }
+        else {
+#pragma unroll
+            for (int j = 0; j < CW; j++)
+                if (n + j < p.N)
+                    v[j] += __ldg(p.bias + n + j);
+        }
     }
     if (p.act != K_ACT_NONE) {
 #pragma unroll
-        for (int j = 0; j < 32; j++)
+        for (int j = 0; j < CW; j++)
             v[j] = act_fn(v[j], p.act);
     }
-    if (p.R) {
+    if (p.R && m < p.M) {
         const float *rp = p.R + (long)(p.rmod ? m % p.rmod : m) * p.ldr + n;
-        if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+        if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
+            for (int j = 0; j < CW; j += 4) {
                 const float4 q = *reinterpret_cast<const float4 *>(rp + j);
                 v[j] += q.x;
                 v[j + 1] += q.y;
@@ -113,61 +133,79 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi &p, int m, int n, u
             }
         }
         else {
-            for (int j = 0; j < nvalid; j++)
-                v[j] += rp[j];
+#pragma unroll
+            for (int j = 0; j < CW; j++)
+                if (n + j < p.N)
+                    v[j] += rp[j];
         }
     }
     if (p.rope.mode && n < 2 * p.rope.E) {
-        // 32-column chunks never straddle the q/k boundary (E % 64 == 0).
+        // Chunks of 32 or 64 columns never straddle the q/k/v boundaries
+        // (E % 64 == 0); each (2j, 2j+1) pair sits in one chunk.
         const float2 *cs = reinterpret_cast<const float2 *>(p.rope.cs) +
                            (long)rrow * (p.rope.hd / 2) + ((n % p.rope.hd) >> 1);
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < CW; j += 2) {
             const float2 rot = __ldg(cs + (j >> 1));
             const float a = v[j], b = v[j + 1];
             v[j] = a * rot.x - b * rot.y;
             v[j + 1] = a * rot.y + b * rot.x;
         }
     }
+}
+
+// Direct (non-TMA) store of one chunk of row m; used when C's base or
+// leading dimension is not 16-byte aligned.
+template <int CW, bool OUT_BF16>
+__device__ __forceinline__ void store_direct(const GemmEpi &p, int m, int n, const float (&v)[CW])
+{
+    if (m >= p.M)
+        return;
     if (OUT_BF16) {
         __nv_bfloat16 *cp = reinterpret_cast<__nv_bfloat16 *>(p.C) + (long)m * p.ldc + n;
-        if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                uint4 q;
-                q.x = pack_bf16x2(v[j], v[j + 1]);
-                q.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                q.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                q.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4 *>(cp + j) = q;
-            }
-        }
-        else {
-            for (int j = 0; j < nvalid; j++)
+        for (int j = 0; j < CW; j++)
+            if (n + j < p.N)
                 cp[j] = __float2bfloat16_rn(v[j]);
-        }
     }
     else {
         float *cp = reinterpret_cast<float *>(p.C) + (long)m * p.ldc + n;
-        if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(cp + j) =
-                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        }
-        else {
-            for (int j = 0; j < nvalid; j++)
+        for (int j = 0; j < CW; j++)
+            if (n + j < p.N)
                 cp[j] = v[j];
-        }
     }
 }
 
-template <int BN, bool OUT_BF16>
+// Writes one row's 128 bytes (CW values) into a 128B-swizzled staging tile:
+// 16-byte chunk q of row r goes to chunk position q ^ (r & 7), the layout a
+// SWIZZLE_128B tensor map expects; eight consecutive rows cover all 32 banks.
+template <int CW, bool OUT_BF16>
+__device__ __forceinline__ void stage_row(uint32_t tile, int r, const float (&v)[CW])
+{
+    const uint32_t row = tile + r * 128;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const uint32_t dst = row + ((q ^ (r & 7)) << 4);
+        if (OUT_BF16)
+            st_shared_v4(dst, pack_bf16x2(v[8 * q], v[8 * q + 1]),
+                         pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                         pack_bf16x2(v[8 * q + 4], v[8 * q + 5]),
+                         pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        else
+            st_shared_v4(dst, __float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                         __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+    }
+}
+
+template <int BN, bool OUT_BF16, bool TMA_STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmEpi p)
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const GemmEpi p)
 {
     using L = GemmSmem<BN>;
+    constexpr int STAGES = L::STAGES;
+    constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
+    constexpr int NCHUNK = BN / CW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -189,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4);
+            mbar_init(&tempty[i], kEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -290,28 +328,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     else {
-        const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        const int ew = warp - 2;          // 0..7
+        const int quarter = warp & 3;     // TMEM lane quarter this warp may read
+        const int half = ew >> 2;         // which chunks of the tile (c % 2)
+        const uint32_t stage0 = smem_addr(smem + L::EPI_OFF + ew * 2 * kStageTile);
+        int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
+        if (TMA_STORE && lane == 0)
+            prefetch_tmap(&tmC);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             const bool ok = mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
             if (!__all_sync(0xffffffffu, ok))
                 break;
             tc_fence_after();
             const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
-            const int m = m0 + row_in_tile;
-            const int rrow = (p.rope.mode && m < p.M) ? rope_row(p.rope, m) : 0;
+            const int r0 = m0 + quarter * 32;
+            const int m = r0 + lane;
+            const int rrow = p.rope.mode ? rope_row(p.rope, m < p.M ? m : 0) : 0;
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
-                uint32_t r[32];
-                tmem_ld32(tbase + c * 32, r);
-                tmem_wait_ld();
-                const int n = n0 + c * 32;
-                if (m < p.M && n < p.N)
-                    epilogue_chunk<OUT_BF16>(p, m, n, r, rrow);
+            for (int c = half; c < NCHUNK; c += 2) {
+                const int n = n0 + c * CW;
+                float v[CW];
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * CW, r);
+                    if constexpr (CW == 64) {
+                        uint32_t r2[32];
+                        tmem_ld32(tbase + c * CW + 32, r2);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            v[32 + j] = __uint_as_float(r2[j]);
+                    }
+                    else
+                        tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        v[j] = __uint_as_float(r[j]);
+                }
+                if (n >= p.N)
+                    continue;  // warp-uniform: a chunk entirely beyond C
+                epilogue_math<CW>(p, m, n, v, rrow);
+                if (TMA_STORE) {
+                    // The store issued two chunks ago used this buffer.
+                    if (lane == 0)
+                        bulk_wait_read<1>();
+                    __syncwarp();
+                    const uint32_t tile = stage0 + buf * kStageTile;
+                    stage_row<CW, OUT_BF16>(tile, lane, v);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && r0 < p.M) {
+                        tma_store_2d(&tmC, smem + L::EPI_OFF + ew * 2 * kStageTile +
+                                               buf * kStageTile,
+                                     n, r0);
+                        bulk_commit();
+                    }
+                    buf ^= 1;
+                }
+                else
+                    store_direct<CW, OUT_BF16>(p, m, n, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -321,6 +400,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (acc == 0)
                 acc_phase ^= 1;
         }
+        if (TMA_STORE && lane == 0)
+            bulk_wait_all();
     }
 
     tc_fence_before();
@@ -331,20 +412,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool OUT_BF16>
-int launch(const CUtensorMap &ta, const CUtensorMap &tb, const GemmEpi &p, int num_sms,
-           cudaStream_t s)
+template <int BN, bool OUT_BF16, bool TMA_STORE>
+int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
+           const GemmEpi &p, int num_sms, cudaStream_t s)
 {
     using L = GemmSmem<BN>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, p);
+    kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, tc, p);
     return (int)cudaGetLastError();
+}
+
+template <int BN>
+int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc, bool tma,
+              bool bf16, const GemmEpi &p, int num_sms, cudaStream_t s)
+{
+    if (bf16)
+        return tma ? launch<BN, true, true>(ta, tb, tc, p, num_sms, s)
+                   : launch<BN, true, false>(ta, tb, tc, p, num_sms, s);
+    return tma ? launch<BN, false, true>(ta, tb, tc, p, num_sms, s)
+               : launch<BN, false, false>(ta, tb, tc, p, num_sms, s);
 }
 
 }  // namespace
@@ -360,11 +452,20 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
         return K_EARG;
     if (rope && rope->mode && (rope->hd != 64 || (rope->E & 63) || 2 * rope->E > N))
         return K_EARG;
+    if (bias && (reinterpret_cast<uintptr_t>(bias) & 15))
+        return K_EARG;
     const int BN = N <= 128 ? 128 : 256;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc;
     if (!make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM) ||
         !make_tmap_bf16(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)BN))
         return K_ETMAP;
+    // TMA stores need a 16-byte aligned base and row pitch; else direct stores.
+    const bool tma = c_bf16 ? make_tmap_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C,
+                                           (uint64_t)M, (uint64_t)N, (uint64_t)ldc, 64, 32)
+                            : make_tmap_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C,
+                                           (uint64_t)M, (uint64_t)N, (uint64_t)ldc, 32, 32);
+    if (!tma)
+        tc = ta;  // unused by the direct-store kernels
     GemmEpi p;
     p.M = M;
     p.N = N;
@@ -384,8 +485,6 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     p.err = err;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
     if (BN == 128)
-        return c_bf16 ? launch<128, true>(ta, tb, p, num_sms, st)
-                      : launch<128, false>(ta, tb, p, num_sms, st);
-    return c_bf16 ? launch<256, true>(ta, tb, p, num_sms, st)
-                  : launch<256, false>(ta, tb, p, num_sms, st);
+        return launch_bn<128>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
+    return launch_bn<256>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
 }

@@ -50,4 +50,25 @@ inline bool make_tmap_bf16(CUtensorMap *map, const void *base, uint64_t rows, ui
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// General 2D tile map: rows x cols elements of `esize` bytes (dtype), leading
+// dimension ld elements, box box_rows x box_cols, 128-byte swizzle (box_cols
+// * esize must be 128 or less).
+inline bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t esize,
+                         const void *base, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint32_t box_cols, uint32_t box_rows)
+{
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esize) & 15) ||
+        box_rows > 256 || box_cols * esize > 128 || rows == 0 || cols == 0)
+        return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * esize};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 }  // namespace sam3
