@@ -516,3 +516,27 @@ extern "C" int k_synth_normal(uint64_t seed, uint64_t stream, long n, float mean
         out_bf16 ? reinterpret_cast<__nv_bfloat16 *>(out) : nullptr);
     LAUNCH_RET();
 }
+
+// ---------------------------------------------------------------- diagnostics
+namespace sam3 {
+namespace {
+__global__ void diag_exp2_kernel(const float *x, float *y_poly, float *y_mufu, int n)
+{
+    const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i + 1 < n) {
+        exp2_poly2(x[i], x[i + 1], y_poly[i], y_poly[i + 1]);
+        y_mufu[i] = ex2_approx(x[i]);
+        y_mufu[i + 1] = ex2_approx(x[i + 1]);
+    }
+}
+}  // namespace
+}  // namespace sam3
+
+extern "C" int cb_diag_exp2(const float *x, float *y_poly, float *y_mufu, int n, void *stream)
+{
+    if (!x || !y_poly || !y_mufu || n <= 0 || (n & 1))
+        return 3;  // CB_EARG
+    diag_exp2_kernel<<<grid_for(n / 2, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        x, y_poly, y_mufu, n);
+    return cudaGetLastError() == cudaSuccess ? 0 : 4;  // CB_OK / CB_ECUDA
+}

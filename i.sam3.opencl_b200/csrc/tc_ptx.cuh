@@ -237,9 +237,43 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
         : "r"(taddr));
 }
 
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld()
 {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers into TMEM (the
+// inverse of tmem_ld32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st()
+{
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile
@@ -286,6 +320,78 @@ __device__ __forceinline__ float ex2_approx(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ---------------------------------------------------------------- packed fp32
+// Pairs of fp32 in one 64-bit register for the sm_100 .f32x2 arithmetic
+// (one instruction for two lanes of add / mul / fma).
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for two values x <= 0 on the FMA pipe, leaving the MUFU unit to the
+// other exponentials of the softmax. Method: Cody-Waite style range
+// reduction x = n + f with n = round(x) (add and subtract 1.5 * 2^23, exact
+// for |x| < 2^22) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose
+// coefficients minimise the maximum relative error on [-0.5, 0.5] (fitted
+// for this kernel by linear programming: 7.5e-5 max relative error in fp32
+// Horner form); 2^n applied by adding n to the exponent field. x is clamped
+// to -125 so the result stays a normal number (2^-125 ~ 2.4e-38, i.e. 0 for
+// a softmax weight). Accuracy is far below the bf16 rounding of P (2^-9).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1)
+{
+    const float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const uint64_t x = f2_make(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+    const uint64_t j = add2(x, f2_make(kMagic, kMagic));
+    const uint64_t n = add2(j, f2_make(-kMagic, -kMagic));
+    const uint64_t f = fma2(n, f2_make(-1.0f, -1.0f), x);
+    uint64_t p = fma2(f2_make(0.05517221987247467f, 0.05517221987247467f), f,
+                      f2_make(0.24261115491390228f, 0.24261115491390228f));
+    p = fma2(p, f, f2_make(0.6932608485221863f, 0.6932608485221863f));
+    p = fma2(p, f, f2_make(0.9999280571937561f, 0.9999280571937561f));
+    float p0, p1, j0, j1;
+    f2_split(p, p0, p1);
+    f2_split(j, j0, j1);
+    // bits(j) = bits(1.5 * 2^23) + n; shifted left by 23 the constant part
+    // leaves 32 bits and n lands in the exponent field.
+    y0 = __uint_as_float(__float_as_uint(j0) * 8388608u + __float_as_uint(p0));
+    y1 = __uint_as_float(__float_as_uint(j1) * 8388608u + __float_as_uint(p1));
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,

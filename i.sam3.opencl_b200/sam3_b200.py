@@ -34,7 +34,7 @@ EXPORTS = [
     "cb_encoder_default_config",
     "cb_encoder_create", "cb_encoder_free", "cb_encoder_init_random",
     "cb_encoder_set_weight", "cb_encode_tiles", "cb_encode_blocks",
-    "cb_encode_tiles_host", "cb_synth_normal",
+    "cb_encode_tiles_host", "cb_synth_normal", "cb_diag_exp2",
     "sam3_synth_normal", "sam3_synth_u8", "sam3_synth_rope_axial",
 ]
 
@@ -124,6 +124,7 @@ def lib():
         "cb_encode_blocks": (i32, [vp, vp, i32, i32, i32]),
         "cb_encode_tiles_host": (i32, [vp, vp, i32, vp]),
         "cb_synth_normal": (i32, [vp, C.c_uint64, C.c_uint64, f32, f32, vp, sz]),
+        "cb_diag_exp2": (i32, [vp, vp, vp, i32, vp]),
         "sam3_synth_normal": (None, [C.c_uint64, C.c_uint64, sz, f32, f32, vp]),
         "sam3_synth_u8": (None, [C.c_uint64, C.c_uint64, sz, vp]),
         "sam3_synth_rope_axial": (None, [i32, i32, C.c_double, vp]),

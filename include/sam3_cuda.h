@@ -301,6 +301,12 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last);
 int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
                          float *out);
 
+/* Diagnostics: the two exponential paths of the attention softmax on n
+ * (even) device values x <= 0: y_poly = the FMA-pipe polynomial 2^x,
+ * y_mufu = ex2.approx, for accuracy tests against the CUDA math library. */
+int cb_diag_exp2(const float *x, float *y_poly, float *y_mufu, int n,
+                 void *stream);
+
 /* Generator: fill a device buffer with normal(seed, stream, i) values
  * (include/sam3_synth.h) as F32 or BF16 (the buffer's dtype). */
 int cb_synth_normal(cb_backend *b, uint64_t seed, uint64_t stream, float mean,

@@ -299,6 +299,31 @@ def test_mha_vs_oracle(cb, sb, ob, name, P, Nq, Nk, dint, shared):
     assert np.abs(got - want).max() < 1e-4
 
 
+def test_softmax_exp2_paths_vs_cuda_exp2(cb, sb):
+    """The attention softmax computes 2^x on the MUFU unit (ex2.approx) and,
+    for a quarter of the columns, with a Cody-Waite / minimax polynomial on
+    the FMA pipe. Both against CUDA's exp2f (torch.exp2) over x in [-130, 0]:
+    relative error <= 1e-4 where the result is a normal float, and results
+    below 2^-125 flushed to (near) zero."""
+    import ctypes as C
+    x = torch.cat([torch.linspace(-130.0, 0.0, 1 << 20, device="cuda"),
+                   -torch.rand(1 << 20, device="cuda") * 20.0])
+    yp = torch.empty_like(x)
+    ym = torch.empty_like(x)
+    torch.cuda.synchronize()
+    rc = sb.lib().cb_diag_exp2(C.c_void_p(x.data_ptr()), C.c_void_p(yp.data_ptr()),
+                               C.c_void_p(ym.data_ptr()), x.numel(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = torch.exp2(x.double())
+    normal = x >= -125.0
+    rel_p = ((yp.double() - ref).abs() / ref)[normal].max().item()
+    rel_m = ((ym.double() - ref).abs() / ref)[x >= -126.0].max().item()
+    assert rel_p <= 1e-4, rel_p
+    assert rel_m <= 1e-5, rel_m
+    assert (yp[~normal].abs() <= 2.0 ** -124).all()
+
+
 def test_mha_rejects_unsupported_shape(cb, sb):
     m = cb.alloc(8 * 100 * 256 * 4, sb.F32)
     with pytest.raises(sb.CBError) as e:
