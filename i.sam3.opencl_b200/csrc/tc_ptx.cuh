@@ -210,6 +210,20 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
+// D (+)= A * B with A read from tensor memory (M rows in TMEM lanes, each
+// 32-bit column holding two consecutive K elements, K = 16 per instruction
+// in 8 columns from a_tmem) and B from a shared-memory descriptor.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // The mbarrier receives one arrival when all tcgen05 operations issued so
 // far by this thread have completed.
 __device__ __forceinline__ void tc_commit(uint64_t *bar)
@@ -271,6 +285,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st()
 {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -291,6 +316,20 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
     d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
     d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// The same for a 64-byte-swizzled K-major tile (rows of 64 bytes = 32 bf16;
+// 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3)): SBO = 512
+// (8 rows x 64 B), layout type SWIZZLE_64B.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;          // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32; // SBO
+    d |= (uint64_t)1 << 46;          // descriptor version (Blackwell)
+    d |= (uint64_t)4 << 61;          // SWIZZLE_64B
     return d;
 }
 
