@@ -20,27 +20,30 @@
 //   warps 0-3  softmax of query tile 0, warps 4-7 of tile 1 (one thread per
 //              query row; warp w reads TMEM lanes 32*(w%4)...);
 //   warp 8     TMA producers: lane 0 loads Q (two buffers) and the K ring,
-//              lane 1 the V ring (two stages each);
+//              lane 1 the V ring (three stages each);
 //   warp 9     TMEM owner and MMA issuer.
 //
-// Tensor memory per query tile t (512 columns in all): two S buffers of 96
-// fp32 columns at t*256 and t*256+96, and the output accumulator O (64
-// columns) at t*256+192, reset by the first P.V of each item. The softmax
-// writes P(g) as bf16 pairs into the first 48 columns of the S buffer it
-// read S(g) from, and P.V(g) takes its A operand from there; S(g+2) is
-// issued into the same buffer right after P.V(g) (tensor-core operations of
-// one thread run in issue order). With g counting this CTA's KV tiles
-// across items, the MMA order per tile is S(0) S(1) | PV(0) S(2) | PV(1)
-// S(3) | ...: the softmax of tile g finds S(g+1) already computed.
+// Score tiles are numbered n = 2g + t (g: this CTA's KV tiles across items,
+// t: query tile), and S(n) goes to TMEM score buffer n % 3 (96 fp32 columns
+// each, at 0, 96, 192). The softmax writes P(n) into the first 48 columns
+// of that buffer (pairs of 16-bit values, the TMEM A-operand layout), P.V(n)
+// reads it from there, and S(n + 3) is issued into the same buffer right
+// after P.V(n) (tensor-core operations of one thread run in issue order), so
+// two score tiles are always computed ahead of the softmax. The output
+// accumulator of tile t (80 columns at 288 + 80t) holds O in columns 0-63
+// and, because every V tile is followed in shared memory by a tile of ones
+// read as output columns 64-79, the row sum of P in column 64: the tensor
+// core sums exactly the 16-bit P values it multiplies.
 //
 // Softmax per KV tile, one pass: the row's 96 scores in one TMEM round trip;
-// row maximum with three-input max; P = 2^(s * scale * log2 e - m) with 5/8
-// of the exponentials on the MUFU unit and 3/8 on the FMA pipe
-// (exp2_poly2); row sums in packed fp32; P back into tensor memory. The
-// running maximum is only raised (and O rescaled in TMEM by
-// 2^(m_old - m_new)) when the tile maximum exceeds it by more than 8 in log2
-// units, so P stays <= 2^8 and most tiles skip the rescale; the final
-// division by the row sum makes the result independent of the offset used.
+// row maximum with three-input max; x = s * scale * log2 e - m in packed
+// fp32; 2^x either two values per MUFU instruction in f16 (when V is f16,
+// P is f16) or per value in fp32 with 3/8 of the values on the FMA pipe
+// (exp2_poly2) and a bf16 pack (when V is bf16). The running maximum is only
+// raised (and O with its row sum rescaled in TMEM by 2^(m_old - m_new)) when
+// the tile maximum exceeds it by more than 8 in log2 units, so P stays
+// <= 2^8 and most tiles skip the rescale; the final division by the row sum
+// makes the result independent of the offset used.
 #include "kernels.h"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -53,32 +56,36 @@ namespace {
 constexpr int HD = 64;
 constexpr int BQ = 128;
 constexpr int BKV = 96;
-constexpr int kSoftmaxWarps = 8;  // 2 tiles x 4 lane quarters
+constexpr int NO = HD + 16;               // O columns: 64 outputs + row-sum block
+constexpr int NSB = 3;                    // TMEM score buffers
+constexpr int KST = 3;                    // K and V ring stages
+constexpr int kSoftmaxWarps = 8;          // 2 tiles x 4 lane quarters
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 32 * 10;
-// Of every 8 pairs of scores, this many take the FMA-pipe exponential
-// (exp2_poly2) instead of the MUFU unit: MUFU ex2 runs at 16 lanes per clock
-// per SM, against 256 MMA flops per score, so about a third of the
-// exponentials must move to the FMA pipe for the MUFU not to bound the loop.
-constexpr int kPolyPairsPer16 = 3;
+// bf16 path: of every 8 pairs of scores, this many take the FMA-pipe
+// exponential (exp2_poly2) instead of two MUFU instructions.
+constexpr int kPolyPairsPer16 = 2;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int Q_BYTES = BQ * HD * 2;     // 16 KB per query tile
 constexpr int KV_BYTES = BKV * HD * 2;   // 12 KB per K or V tile
+constexpr int V_STAGE = 2 * KV_BYTES;    // V tile, then a tile of ones
 constexpr int OFF_Q = 0;                         // [buffer][tile]
-constexpr int OFF_K = OFF_Q + 4 * Q_BYTES;       // K ring, 2 stages
-constexpr int OFF_V = OFF_K + 2 * KV_BYTES;      // V ring, 2 stages
-constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
-// q_full[2], q_empty[2], k_full[2], k_empty[2], v_full[2], v_empty[2],
-// s_full[2][2], p_ready[2][2], pv_full[2][2], drain. Every barrier whose
-// waiter could see it advance by two phases before it looks (the softmax
-// may finish KV tiles g and g+1 before the MMA warp consumes P(g)) is split
-// per buffer, so consecutive uses alternate between two barriers and a
-// parity wait never aliases.
-constexpr int NBAR = 12 + 12 + 1;
+constexpr int OFF_K = OFF_Q + 4 * Q_BYTES;       // K ring
+constexpr int OFF_V = OFF_K + KST * KV_BYTES;    // V ring (+ ones)
+constexpr int OFF_BAR = OFF_V + KST * V_STAGE;
+constexpr uint32_t TM_O = NSB * BKV;             // first O column
+// q_full[2], q_empty[2], k_full[3], k_empty[3], v_full[3], v_empty[3],
+// s_full[3], p_ready[3], pv_full[2 tiles][2], drain. A waiter never finds
+// one of them two phases ahead of the phase it waits for: score buffer i is
+// only refilled after P.V of its previous tile, which needs that tile's
+// p_ready; pv_full is split by KV-tile parity so that the phase before the
+// awaited one (P.V two KV tiles back) is always complete.
+constexpr int NBAR = 4 + 4 * KST + 3 * NSB + 4 + 1;
 constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;
 static_assert(SMEM_BYTES <= 232448, "attention smem");
 static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "alignment");
+static_assert(TM_O + 2 * NO <= 512, "tensor memory");
 
 struct AttnArgs {
     int nseq, N, E, heads;
@@ -96,7 +103,7 @@ __device__ __forceinline__ void item_coords(const AttnArgs &a, int npairs, int i
     seq = item / (npairs * a.heads);
 }
 
-template <bool OUT_BF16>
+template <bool OUT_BF16, bool V_F16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmKV, const AttnArgs a)
@@ -108,12 +115,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *q_full = bars;
     uint64_t *q_empty = q_full + 2;
     uint64_t *k_full = q_empty + 2;
-    uint64_t *k_empty = k_full + 2;
-    uint64_t *v_full = k_empty + 2;
-    uint64_t *v_empty = v_full + 2;
-    uint64_t *s_full = v_empty + 2;   // [tile * 2 + buffer]
-    uint64_t *p_ready = s_full + 4;   // [tile * 2 + buffer]
-    uint64_t *pv_full = p_ready + 4;  // [tile * 2 + buffer]
+    uint64_t *k_empty = k_full + KST;
+    uint64_t *v_full = k_empty + KST;
+    uint64_t *v_empty = v_full + KST;
+    uint64_t *s_full = v_empty + KST;   // [score buffer]
+    uint64_t *p_ready = s_full + NSB;   // [score buffer]
+    uint64_t *pv_full = p_ready + NSB;  // [tile * 2 + KV-tile parity]
     uint64_t *drain = pv_full + 4;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -134,19 +141,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; i++) {
             mbar_init(&q_full[i], 1);
             mbar_init(&q_empty[i], 1);
+        }
+        for (int i = 0; i < KST; i++) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < NSB; i++) {
             mbar_init(&s_full[i], 1);
             mbar_init(&p_ready[i], 4);
-            mbar_init(&pv_full[i], 1);
         }
+        for (int i = 0; i < 4; i++)
+            mbar_init(&pv_full[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
+    }
+    // The ones tiles behind the V stages (16-bit 1.0 in both halves of every
+    // word; the swizzle of a constant tile is immaterial).
+    {
+        const uint32_t one2 = V_F16 ? 0x3C003C00u : 0x3F803F80u;
+        for (int i = threadIdx.x; i < KST * (KV_BYTES / 16); i += kThreads) {
+            const int st = i / (KV_BYTES / 16), c = i - st * (KV_BYTES / 16);
+            st_shared_v4(smem_addr(smem + OFF_V + st * V_STAGE + KV_BYTES + c * 16), one2, one2,
+                         one2, one2);
+        }
+        fence_proxy_async_smem();
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, 512);
@@ -168,8 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint64_t *full = is_k ? k_full : v_full;
             uint64_t *empty = is_k ? k_empty : v_empty;
             uint8_t *ring = smem + (is_k ? OFF_K : OFF_V);
+            const int stride = is_k ? KV_BYTES : V_STAGE;
             int lastq = -1, lastg = -1;
             bool ok = true;
+            int st = 0, use = 0;  // ring stage and use count of KV tile g
             for (int k = 0; k < nmine && ok; k++) {
                 int pair, head, seq;
                 item_coords(a, npairs, (int)blockIdx.x + k * (int)gridDim.x, pair, head, seq);
@@ -186,15 +209,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int col = (is_k ? a.E : 2 * a.E) + head * HD;
                 for (int j = 0; j < nkv; j++) {
-                    const int g = k * nkv + j;
-                    const int st = g & 1;
-                    if (!mbar_wait(&empty[st], ((g >> 1) & 1) ^ 1, a.err, abort_flag)) {
+                    if (!mbar_wait(&empty[st], (use & 1) ^ 1, a.err, abort_flag)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(&full[st], KV_BYTES);
-                    tma_load_2d(ring + st * KV_BYTES, &tmKV, &full[st], col, row0 + j * BKV);
-                    lastg = g;
+                    tma_load_2d(ring + st * stride, &tmKV, &full[st], col, row0 + j * BKV);
+                    lastg = k * nkv + j;
+                    if (++st == KST) {
+                        st = 0;
+                        use++;
+                    }
                 }
             }
             // Let every issued copy land before the CTA can exit.
@@ -202,80 +227,87 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = lastq - 1; k <= lastq; k++)
                 if (k >= 0)
                     mbar_wait(&q_full[k & 1], (k >> 1) & 1, a.err, &no_abort);
-            for (int g = lastg - 1; g <= lastg; g++)
+            for (int g = lastg - (KST - 1); g <= lastg; g++)
                 if (g >= 0)
-                    mbar_wait(&full[g & 1], (g >> 1) & 1, a.err, &no_abort);
+                    mbar_wait(&full[g % KST], (g / KST) & 1, a.err, &no_abort);
         }
     }
     else if (warp == kMmaWarp) {
         if (elect_one() && total > 0) {
             constexpr uint32_t idS = idesc_bf16_f32(BQ, BKV, 0, 0);
-            constexpr uint32_t idPV = idesc_bf16_f32(BQ, HD, 0, 1);
+            constexpr uint32_t idPV = V_F16 ? idesc_f16_f32(BQ, NO, 0, 1)
+                                            : idesc_bf16_f32(BQ, NO, 0, 1);
             const uint32_t sQ = smem_addr(smem + OFF_Q);
             const uint32_t sK = smem_addr(smem + OFF_K);
             const uint32_t sV = smem_addr(smem + OFF_V);
+            const int nscore = 2 * total;
             bool ok = true;
-            // S_t(g2) = Q_t(item k2) K(g2)^T into S buffer g2 % 2, where g2 is
-            // KV tile j2 of item k2. The first S of an item waits for its Q;
-            // the last one releases the Q buffer.
-            auto issue_s = [&](int t, int g2, int k2, int j2) -> bool {
+            // S(n) = Q_t(item k) K(g)^T into score buffer n % 3, n = 2g + t,
+            // g being KV tile j of item k. The first S of an item waits for
+            // its Q; the last one releases the Q buffer.
+            auto issue_s = [&](int n, int k, int j) -> bool {
+                const int t = n & 1, g = n >> 1;
+                const int kst = g % KST;
                 if (t == 0) {
-                    if (!mbar_wait(&k_full[g2 & 1], (g2 >> 1) & 1, a.err, abort_flag))
+                    if (!mbar_wait(&k_full[kst], (g / KST) & 1, a.err, abort_flag))
                         return false;
-                    if (j2 == 0 && !mbar_wait(&q_full[k2 & 1], (k2 >> 1) & 1, a.err, abort_flag))
+                    if (j == 0 && !mbar_wait(&q_full[k & 1], (k >> 1) & 1, a.err, abort_flag))
                         return false;
                     tc_fence_after();
                 }
-                const uint32_t qt = sQ + ((k2 & 1) * 2 + t) * Q_BYTES;
-                const uint32_t kg = sK + (g2 & 1) * KV_BYTES;
+                const uint32_t qt = sQ + ((k & 1) * 2 + t) * Q_BYTES;
+                const uint32_t kg = sK + kst * KV_BYTES;
+                const int buf = n % NSB;
                 for (int kq = 0; kq < HD / 16; kq++)
-                    tc_mma(tmem_base + t * 256 + (g2 & 1) * BKV,
-                           sw128_desc(qt + kq * 32, 16, 1024), sw128_desc(kg + kq * 32, 16, 1024),
-                           idS, kq != 0);
-                tc_commit(&s_full[t * 2 + (g2 & 1)]);
+                    tc_mma(tmem_base + buf * BKV, sw128_desc(qt + kq * 32, 16, 1024),
+                           sw128_desc(kg + kq * 32, 16, 1024), idS, kq != 0);
+                tc_commit(&s_full[buf]);
                 if (t == 1) {
-                    tc_commit(&k_empty[g2 & 1]);
-                    if (j2 == nkv - 1)
-                        tc_commit(&q_empty[k2 & 1]);
+                    tc_commit(&k_empty[kst]);
+                    if (j == nkv - 1)
+                        tc_commit(&q_empty[k & 1]);
                 }
                 return true;
             };
-            for (int g0 = 0; ok && g0 < 2 && g0 < total; g0++)
-                for (int t = 0; ok && t < 2; t++)
-                    ok = issue_s(t, g0, g0 / nkv, g0 % nkv);
-            int j = 0;                                 // KV tile of g within its item
-            int k2 = 2 / nkv, j2 = 2 - (2 / nkv) * nkv;  // item and KV tile of g + 2
-            for (int g = 0; ok && g < total; g++) {
-                if (!mbar_wait(&v_full[g & 1], (g >> 1) & 1, a.err, abort_flag)) {
+            // Prologue: S(0), S(1), S(2).
+            for (int n0 = 0; ok && n0 < NSB && n0 < nscore; n0++) {
+                const int g0 = n0 >> 1;
+                ok = issue_s(n0, g0 / nkv, g0 % nkv);
+            }
+            int jg = 0;                          // KV tile (within its item) of g
+            int k3 = 1 / nkv, j3 = 1 % nkv;      // item and KV tile of (n + 3) >> 1
+            for (int n = 0; ok && n < nscore; n++) {
+                const int t = n & 1, g = n >> 1;
+                const int kst = g % KST;
+                if (t == 0 && !mbar_wait(&v_full[kst], (g / KST) & 1, a.err, abort_flag)) {
                     ok = false;
                     break;
                 }
-                const uint32_t vg = sV + (g & 1) * KV_BYTES;
-                for (int t = 0; t < 2 && ok; t++) {
-                    if (!mbar_wait(&p_ready[t * 2 + (g & 1)], (g >> 1) & 1, a.err, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    // O_t (+)= P_t(g) V(g), P from the S buffer of g; the first
-                    // KV tile of an item resets O.
-                    const uint32_t pt = tmem_base + t * 256 + (g & 1) * BKV;
-                    for (int kk = 0; kk < BKV / 16; kk++)
-                        tc_mma_ts(tmem_base + t * 256 + 2 * BKV, pt + kk * 8,
-                                  sw128_desc(vg + kk * 2048, BKV * 128, 1024), idPV,
-                                  (j | kk) != 0);
-                    tc_commit(&pv_full[t * 2 + (g & 1)]);
-                    if (g + 2 < total)
-                        ok = issue_s(t, g + 2, k2, j2);
-                }
-                if (!ok)
+                const int buf = n % NSB;
+                if (!mbar_wait(&p_ready[buf], (n / NSB) & 1, a.err, abort_flag)) {
+                    ok = false;
                     break;
-                tc_commit(&v_empty[g & 1]);
-                if (++j == nkv)
-                    j = 0;
-                if (++j2 == nkv) {
-                    j2 = 0;
-                    k2++;
+                }
+                tc_fence_after();
+                // O_t (+)= P(n) [V(g) | 1]; the first KV tile of an item resets
+                // O_t and its row sum.
+                const uint32_t vg = sV + kst * V_STAGE;
+                for (int kk = 0; kk < BKV / 16; kk++)
+                    tc_mma_ts(tmem_base + TM_O + t * NO, tmem_base + buf * BKV + kk * 8,
+                              sw128_desc(vg + kk * 2048, KV_BYTES, 1024), idPV,
+                              (jg | kk) != 0);
+                tc_commit(&pv_full[t * 2 + (g & 1)]);
+                if (t == 1) {
+                    tc_commit(&v_empty[kst]);
+                    if (++jg == nkv)
+                        jg = 0;
+                }
+                if (n + NSB < nscore) {
+                    if (((n + NSB) & 1) == 0 && ++j3 == nkv) {  // (n + 3) >> 1 advanced
+                        j3 = 0;
+                        k3++;
+                    }
+                    ok = issue_s(n + NSB, k3, j3);
                 }
             }
             tc_commit(drain);
@@ -287,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = warp >> 2;            // query tile of the item
         const int quarter = warp & 3;       // TMEM lane quarter = rows 32q..32q+31
         const int r = quarter * 32 + lane;  // query row within the tile
-        const uint32_t tT = tmem_base + ((uint32_t)(quarter * 32) << 16) + t * 256;
-        const uint32_t tO = tT + 2 * BKV;
+        const uint32_t tL = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        const uint32_t tO = tL + TM_O + t * NO;
         const float sl2 = a.scale_log2;
         const uint64_t sl2x2 = f2_make(sl2, sl2);
         bool ok = true;
@@ -300,28 +332,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 (2 * (((int)blockIdx.x + k * (int)gridDim.x) % npairs) + t) * BQ + quarter * 32 <
                 a.N;
             float m_used = -INFINITY;
-            uint64_t lsum0 = 0, lsum1 = 0;  // packed partial row sums
             for (int j = 0; j < nkv; j++) {
                 const int g = k * nkv + j;
-                const int b = g & 1;
+                const int n = 2 * g + t;
+                const int buf = n % NSB;
                 ok = __all_sync(0xffffffffu,
-                                mbar_wait(&s_full[t * 2 + b], (g >> 1) & 1, a.err, abort_flag));
+                                mbar_wait(&s_full[buf], (n / NSB) & 1, a.err, abort_flag));
                 if (!ok)
                     break;
                 tc_fence_after();
+                const uint32_t tS = tL + buf * BKV;
                 // The whole 96-score row in one TMEM round trip.
                 uint32_t s[BKV];
-                tmem_ld32(tT + b * BKV, *reinterpret_cast<uint32_t(*)[32]>(s));
-                tmem_ld32(tT + b * BKV + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
-                tmem_ld32(tT + b * BKV + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(s));
+                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
                 tmem_wait_ld();
 
-                const int valid = a.N - j * BKV;
-                const bool masked = valid < BKV;  // only a sequence's last tile
                 bool resc = false;
                 float factor = 1.0f;
                 if (rows_live) {
-                    if (masked) {
+                    const int valid = a.N - j * BKV;
+                    if (valid < BKV) {  // only a sequence's last tile
 #pragma unroll
                         for (int e = 0; e < BKV; e++)
                             if (e >= valid)
@@ -341,65 +373,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                         resc = true;
                         factor = ex2_approx(m_used - m_tile);
                         m_used = m_tile;
-                        const uint64_t f2v = f2_make(factor, factor);
-                        lsum0 = mul2(lsum0, f2v);
-                        lsum1 = mul2(lsum1, f2v);
                     }
-                }
-                if (rows_live) {
-                    // P = 2^(s * scale_log2 - m_used), in place.
+                    // P = 2^(s * scale_log2 - m_used) as 16-bit pairs, in place
+                    // (s[i] holds keys 2i, 2i+1 for i < 48). Keys past N have
+                    // s = -inf and get P = 0.
                     const uint64_t negm = f2_make(-m_used, -m_used);
 #pragma unroll
                     for (int e = 0; e < BKV; e += 2) {
                         const uint64_t x2 = fma2(f2_make(__uint_as_float(s[e]),
                                                          __uint_as_float(s[e + 1])),
                                                  sl2x2, negm);
-                        float x0, x1, p0, p1;
+                        float x0, x1;
                         f2_split(x2, x0, x1);
-                        if (((e >> 1) & 7) >= 8 - kPolyPairsPer16)
-                            exp2_poly2(x0, x1, p0, p1);
-                        else {
-                            p0 = ex2_approx(x0);
-                            p1 = ex2_approx(x1);
+                        uint32_t pp;
+                        if (V_F16) {
+                            pp = ex2_f16x2(pack_f16x2(x0, x1));
                         }
-                        s[e] = __float_as_uint(p0);
-                        s[e + 1] = __float_as_uint(p1);
+                        else if (((e >> 1) & 7) >= 8 - kPolyPairsPer16) {
+                            float p0, p1;
+                            exp2_poly2(x0, x1, p0, p1);
+                            pp = pack_bf16x2(p0, p1);
+                        }
+                        else {
+                            pp = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
+                        }
+                        s[e >> 1] = pp;
                     }
-                    if (masked) {
-#pragma unroll
-                        for (int e = 0; e < BKV; e++)
-                            if (e >= valid)
-                                s[e] = 0;
-                    }
-#pragma unroll
-                    for (int e = 0; e < BKV; e += 4) {
-                        lsum0 = add2(lsum0,
-                                     f2_make(__uint_as_float(s[e]), __uint_as_float(s[e + 1])));
-                        lsum1 = add2(lsum1,
-                                     f2_make(__uint_as_float(s[e + 2]), __uint_as_float(s[e + 3])));
-                    }
-                    // P row as bf16 pairs over the first 48 columns of the S
-                    // buffer, the A operand layout of P.V.
-                    {
-                        uint32_t pk[32];
-#pragma unroll
-                        for (int e = 0; e < 32; e++)
-                            pk[e] = pack_bf16x2(__uint_as_float(s[2 * e]),
-                                                __uint_as_float(s[2 * e + 1]));
-                        tmem_st32(tT + b * BKV, pk);
-                    }
-                    {
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++)
-                            pk[e] = pack_bf16x2(__uint_as_float(s[64 + 2 * e]),
-                                                __uint_as_float(s[64 + 2 * e + 1]));
-                        tmem_st16(tT + b * BKV + 32, pk);
-                    }
+                    tmem_st32(tS, *reinterpret_cast<const uint32_t(*)[32]>(s));
+                    tmem_st16(tS + 32, *reinterpret_cast<const uint32_t(*)[16]>(s + 32));
                 }
-                // A raised maximum rescales O (after P is out of the
-                // registers), which needs P.V(g-1) done; P.V(g) is only issued
-                // after p_ready below.
+                // A raised maximum rescales O and its row sum, which needs
+                // P.V of the previous KV tile done; P.V(n) is only issued after
+                // p_ready below.
                 if (__any_sync(0xffffffffu, resc)) {
                     const int gp = g - 1;
                     ok = __all_sync(0xffffffffu, mbar_wait(&pv_full[t * 2 + (gp & 1)],
@@ -409,33 +414,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint64_t f2v = f2_make(factor, factor);
 #pragma unroll
-                    for (int c = 0; c < 2; c++) {
+                    for (int c = 0; c < 3; c++) {
                         uint32_t o[32];
-                        tmem_ld32(tO + c * 32, o);
+                        const int w = c < 2 ? 32 : 16;
+                        if (c < 2)
+                            tmem_ld32(tO + c * 32, o);
+                        else
+                            tmem_ld16(tO + 64, *reinterpret_cast<uint32_t(*)[16]>(o));
                         tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
-                            float o0, o1;
-                            f2_split(mul2(f2_make(__uint_as_float(o[e]),
-                                                  __uint_as_float(o[e + 1])),
-                                          f2v),
-                                     o0, o1);
-                            o[e] = __float_as_uint(o0);
-                            o[e + 1] = __float_as_uint(o1);
+                            if (e < w) {
+                                float o0, o1;
+                                f2_split(mul2(f2_make(__uint_as_float(o[e]),
+                                                      __uint_as_float(o[e + 1])),
+                                              f2v),
+                                         o0, o1);
+                                o[e] = __float_as_uint(o0);
+                                o[e + 1] = __float_as_uint(o1);
+                            }
                         }
-                        tmem_st32(tO + c * 32, o);
+                        if (c < 2)
+                            tmem_st32(tO + c * 32, o);
+                        else
+                            tmem_st16(tO + 64, *reinterpret_cast<const uint32_t(*)[16]>(o));
                     }
                 }
-                // P(g) (and a rescaled O) is in TMEM: ready for the MMA.
+                // P(n) (and a rescaled O) is in TMEM: ready for the MMA.
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
-                    mbar_arrive(&p_ready[t * 2 + b]);
+                    mbar_arrive(&p_ready[buf]);
             }
             if (!ok)
                 break;
-            // End of the item: O after P.V of its last KV tile, normalised.
+            // End of the item: O after P.V of its last KV tile, normalised by
+            // the row sum in column 64.
             {
                 const int gl = k * nkv + nkv - 1;
                 ok = __all_sync(0xffffffffu, mbar_wait(&pv_full[t * 2 + (gl & 1)],
@@ -448,13 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 item_coords(a, npairs, (int)blockIdx.x + k * (int)gridDim.x, pair, head, seq);
                 tc_fence_after();
                 uint32_t ov[64];
+                uint32_t lsum[16];
                 tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(ov));
                 tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(ov + 32));
+                tmem_ld16(tO + 64, lsum);
                 tmem_wait_ld();
-                float la, lb, lc, ld;
-                f2_split(lsum0, la, lb);
-                f2_split(lsum1, lc, ld);
-                const float inv = 1.0f / ((la + lb) + (lc + ld));
+                const float inv = 1.0f / __uint_as_float(lsum[0]);
                 const int q = (2 * pair + t) * BQ + r;
                 if (q < a.N) {
                     const long orow = (long)(seq * a.N + q) * a.E + head * HD;
@@ -501,11 +515,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <bool OUT_BF16>
+template <bool OUT_BF16, bool V_F16>
 int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int grid,
            cudaStream_t s)
 {
-    auto kern = attn_tc_kernel<OUT_BF16>;
+    auto kern = attn_tc_kernel<OUT_BF16, V_F16>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess)
@@ -518,7 +532,7 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int
 }  // namespace sam3
 
 extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
-                         void *out, int out_bf16, int *err, k_stream s)
+                         void *out, int out_bf16, int v_f16, int *err, k_stream s)
 {
     using namespace sam3;
     if (nseq <= 0 || N <= 0 || heads <= 0 || E != heads * HD ||
@@ -547,5 +561,9 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     a.nitems = (int)nitems;
     const int grid = nitems < sms ? (int)nitems : sms;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
-    return out_bf16 ? launch<true>(tq, tkv, a, grid, st) : launch<false>(tq, tkv, a, grid, st);
+    if (v_f16)
+        return out_bf16 ? launch<true, true>(tq, tkv, a, grid, st)
+                        : launch<false, true>(tq, tkv, a, grid, st);
+    return out_bf16 ? launch<true, false>(tq, tkv, a, grid, st)
+                    : launch<false, false>(tq, tkv, a, grid, st);
 }
