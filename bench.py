@@ -209,9 +209,9 @@ def attention_bench(sb, cb, torch, pk, iters=10):
         mq, mq16, mcs = cb.wrap(qkv), cb.wrap(q16), cb.wrap(cs)
         mo16, mo32 = cb.wrap(out16), cb.wrap(out32)
         flops = 4.0 * nseq * 16 * N * N * 64
-        runs = [("bf16_tc_kernel", lambda: cb.attention(mq16, nseq, N, E, 16, 64, None, N,
-                                                         0.125, sb.ATTN_TC, mo16)),
-                ("bf16_tc_from_f32_qkv", lambda: cb.attention(mq, nseq, N, E, 16, 64, mcs, N,
+        runs = [("tc_kernel", lambda: cb.attention(mq16, nseq, N, E, 16, 64, None, N, 0.125,
+                                                    sb.ATTN_TC, mo16)),
+                ("tc_from_f32_qkv", lambda: cb.attention(mq, nseq, N, E, 16, 64, mcs, N,
                                                                0.125, sb.ATTN_TC, mo32))]
         if nseq == 1:
             runs.append(("f32_reference_mode",

@@ -37,9 +37,8 @@
 //
 // Softmax per KV tile, one pass: the row's 96 scores in one TMEM round trip;
 // row maximum with three-input max; x = s * scale * log2 e - m in packed
-// fp32; 2^x either two values per MUFU instruction in f16 (when V is f16,
-// P is f16) or per value in fp32 with 3/8 of the values on the FMA pipe
-// (exp2_poly2) and a bf16 pack (when V is bf16). The running maximum is only
+// fp32; 2^x on the MUFU unit, with 1/8 of the values on the FMA pipe
+// (exp2_poly2); P packed to bf16 pairs. The running maximum is only
 // raised (and O with its row sum rescaled in TMEM by 2^(m_old - m_new)) when
 // the tile maximum exceeds it by more than 8 in log2 units, so P stays
 // <= 2^8 and most tiles skip the rescale; the final division by the row sum
@@ -63,9 +62,10 @@ constexpr int kSoftmaxWarps = 8;          // 2 tiles x 4 lane quarters
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 32 * 10;
-// bf16 path: of every 8 pairs of scores, this many take the FMA-pipe
-// exponential (exp2_poly2) instead of two MUFU instructions.
-constexpr int kPolyPairsPer16 = 2;
+// Of every 8 pairs of scores, this many take the FMA-pipe exponential
+// (exp2_poly2) instead of two MUFU instructions: the MUFU unit runs 16
+// exponentials per clock per SM against 256 MMA flops per score.
+constexpr int kPolyPairsPer16 = 1;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int Q_BYTES = BQ * HD * 2;     // 16 KB per query tile
 constexpr int KV_BYTES = BKV * HD * 2;   // 12 KB per K or V tile
@@ -103,7 +103,7 @@ __device__ __forceinline__ void item_coords(const AttnArgs &a, int npairs, int i
     seq = item / (npairs * a.heads);
 }
 
-template <bool OUT_BF16, bool V_F16>
+template <bool OUT_BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmKV, const AttnArgs a)
@@ -158,10 +158,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         fence_mbar_init();
     }
-    // The ones tiles behind the V stages (16-bit 1.0 in both halves of every
+    // The ones tiles behind the V stages (bf16 1.0 in both halves of every
     // word; the swizzle of a constant tile is immaterial).
     {
-        const uint32_t one2 = V_F16 ? 0x3C003C00u : 0x3F803F80u;
+        const uint32_t one2 = 0x3F803F80u;
         for (int i = threadIdx.x; i < KST * (KV_BYTES / 16); i += kThreads) {
             const int st = i / (KV_BYTES / 16), c = i - st * (KV_BYTES / 16);
             st_shared_v4(smem_addr(smem + OFF_V + st * V_STAGE + KV_BYTES + c * 16), one2, one2,
@@ -235,80 +235,114 @@ __global__ void __launch_bounds__(kThreads, 1)
     else if (warp == kMmaWarp) {
         if (elect_one() && total > 0) {
             constexpr uint32_t idS = idesc_bf16_f32(BQ, BKV, 0, 0);
-            constexpr uint32_t idPV = V_F16 ? idesc_f16_f32(BQ, NO, 0, 1)
-                                            : idesc_bf16_f32(BQ, NO, 0, 1);
-            const uint32_t sQ = smem_addr(smem + OFF_Q);
-            const uint32_t sK = smem_addr(smem + OFF_K);
-            const uint32_t sV = smem_addr(smem + OFF_V);
+            constexpr uint32_t idPV = idesc_bf16_f32(BQ, NO, 0, 1);
+            // Descriptors of the first 16-element K slice of the operand
+            // regions. A tile or slice offset of d bytes adds d / 16 to the
+            // start-address field (shared addresses stay below 2^18, so the
+            // 14-bit field never carries): K-major slices are 32 bytes apart,
+            // V slices (MN-major, 16 keys) 2048 bytes.
+            const uint64_t dQ = sw128_desc(smem_addr(smem + OFF_Q), 16, 1024);
+            const uint64_t dK = sw128_desc(smem_addr(smem + OFF_K), 16, 1024);
+            const uint64_t dV = sw128_desc(smem_addr(smem + OFF_V), KV_BYTES, 1024);
             const int nscore = 2 * total;
-            bool ok = true;
-            // S(n) = Q_t(item k) K(g)^T into score buffer n % 3, n = 2g + t,
-            // g being KV tile j of item k. The first S of an item waits for
-            // its Q; the last one releases the Q buffer.
-            auto issue_s = [&](int n, int k, int j) -> bool {
-                const int t = n & 1, g = n >> 1;
-                const int kst = g % KST;
-                if (t == 0) {
-                    if (!mbar_wait(&k_full[kst], (g / KST) & 1, a.err, abort_flag))
+            // The last item of a sequence with an odd tile count has its
+            // second tile beyond N: that tile gets no MMAs (its barriers are
+            // still committed).
+            auto pair_dead = [&](int k) -> bool {
+                return (nqt & 1) && ((int)blockIdx.x + k * (int)gridDim.x) % npairs == npairs - 1;
+            };
+            // Cursor over score tiles n = 2g + t, kept by increments (this one
+            // thread issues every MMA; its instruction count is on the
+            // critical path).
+            struct Cursor {
+                int n, t;      // score tile, query tile
+                int kst, kph;  // K/V ring stage of g and its use parity
+                int gpar, j, k;
+                int buf, bph;  // score buffer n % 3 and its use parity
+                bool pdead, dead;
+            };
+            auto advance = [&](Cursor &c) {
+                c.n++;
+                c.t ^= 1;
+                if (++c.buf == NSB) {
+                    c.buf = 0;
+                    c.bph ^= 1;
+                }
+                if (c.t == 0) {
+                    c.gpar ^= 1;
+                    if (++c.kst == KST) {
+                        c.kst = 0;
+                        c.kph ^= 1;
+                    }
+                    if (++c.j == nkv) {
+                        c.j = 0;
+                        c.k++;
+                        c.pdead = pair_dead(c.k);
+                    }
+                }
+                c.dead = c.t == 1 && c.pdead;
+            };
+            const Cursor c0 = {0, 0, 0, 0, 0, 0, 0, 0, 0, pair_dead(0), false};
+            Cursor ahead = c0, cur = c0;
+            // S(n) = Q_t(item k) K(g)^T into score buffer n % 3. The first S of
+            // an item waits for its Q; the last one releases the Q buffer.
+            auto issue_s = [&](const Cursor &c) -> bool {
+                if (c.t == 0) {
+                    if (!mbar_wait(&k_full[c.kst], c.kph, a.err, abort_flag))
                         return false;
-                    if (j == 0 && !mbar_wait(&q_full[k & 1], (k >> 1) & 1, a.err, abort_flag))
+                    if (c.j == 0 && !mbar_wait(&q_full[c.k & 1], (c.k >> 1) & 1, a.err, abort_flag))
                         return false;
                     tc_fence_after();
                 }
-                const uint32_t qt = sQ + ((k & 1) * 2 + t) * Q_BYTES;
-                const uint32_t kg = sK + kst * KV_BYTES;
-                const int buf = n % NSB;
-                for (int kq = 0; kq < HD / 16; kq++)
-                    tc_mma(tmem_base + buf * BKV, sw128_desc(qt + kq * 32, 16, 1024),
-                           sw128_desc(kg + kq * 32, 16, 1024), idS, kq != 0);
-                tc_commit(&s_full[buf]);
-                if (t == 1) {
-                    tc_commit(&k_empty[kst]);
-                    if (j == nkv - 1)
-                        tc_commit(&q_empty[k & 1]);
+                if (!c.dead) {
+                    const uint64_t qd = dQ + (uint64_t)((((c.k & 1) * 2 + c.t) * Q_BYTES) >> 4);
+                    const uint64_t kd = dK + (uint64_t)((c.kst * KV_BYTES) >> 4);
+                    const uint32_t dS = tmem_base + c.buf * BKV;
+#pragma unroll
+                    for (int kq = 0; kq < HD / 16; kq++)
+                        tc_mma(dS, qd + 2 * kq, kd + 2 * kq, idS, kq != 0);
+                }
+                tc_commit(&s_full[c.buf]);
+                if (c.t == 1) {
+                    tc_commit(&k_empty[c.kst]);
+                    if (c.j == nkv - 1)
+                        tc_commit(&q_empty[c.k & 1]);
                 }
                 return true;
             };
-            // Prologue: S(0), S(1), S(2).
-            for (int n0 = 0; ok && n0 < NSB && n0 < nscore; n0++) {
-                const int g0 = n0 >> 1;
-                ok = issue_s(n0, g0 / nkv, g0 % nkv);
-            }
-            int jg = 0;                          // KV tile (within its item) of g
-            int k3 = 1 / nkv, j3 = 1 % nkv;      // item and KV tile of (n + 3) >> 1
-            for (int n = 0; ok && n < nscore; n++) {
-                const int t = n & 1, g = n >> 1;
-                const int kst = g % KST;
-                if (t == 0 && !mbar_wait(&v_full[kst], (g / KST) & 1, a.err, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                const int buf = n % NSB;
-                if (!mbar_wait(&p_ready[buf], (n / NSB) & 1, a.err, abort_flag)) {
-                    ok = false;
-                    break;
-                }
+            // O_t (+)= P(n) [V(g) | 1], P read from score buffer n % 3; the
+            // first KV tile of an item resets O_t and its row sum.
+            auto issue_pv = [&](const Cursor &c) -> bool {
+                if (c.t == 0 && !mbar_wait(&v_full[c.kst], c.kph, a.err, abort_flag))
+                    return false;
+                if (!mbar_wait(&p_ready[c.buf], c.bph, a.err, abort_flag))
+                    return false;
                 tc_fence_after();
-                // O_t (+)= P(n) [V(g) | 1]; the first KV tile of an item resets
-                // O_t and its row sum.
-                const uint32_t vg = sV + kst * V_STAGE;
-                for (int kk = 0; kk < BKV / 16; kk++)
-                    tc_mma_ts(tmem_base + TM_O + t * NO, tmem_base + buf * BKV + kk * 8,
-                              sw128_desc(vg + kk * 2048, KV_BYTES, 1024), idPV,
-                              (jg | kk) != 0);
-                tc_commit(&pv_full[t * 2 + (g & 1)]);
-                if (t == 1) {
-                    tc_commit(&v_empty[kst]);
-                    if (++jg == nkv)
-                        jg = 0;
+                if (!c.dead) {
+                    const uint64_t vd = dV + (uint64_t)((c.kst * V_STAGE) >> 4);
+                    const uint32_t dO = tmem_base + TM_O + c.t * NO;
+                    const uint32_t aP = tmem_base + c.buf * BKV;
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 16; kk++)
+                        tc_mma_ts(dO, aP + kk * 8, vd + 128 * kk, idPV, (c.j | kk) != 0);
                 }
-                if (n + NSB < nscore) {
-                    if (((n + NSB) & 1) == 0 && ++j3 == nkv) {  // (n + 3) >> 1 advanced
-                        j3 = 0;
-                        k3++;
-                    }
-                    ok = issue_s(n + NSB, k3, j3);
+                tc_commit(&pv_full[c.t * 2 + c.gpar]);
+                if (c.t == 1)
+                    tc_commit(&v_empty[c.kst]);
+                return true;
+            };
+            bool ok = true;
+            for (int i = 0; ok && i < NSB && ahead.n < nscore; i++) {
+                ok = issue_s(ahead);
+                advance(ahead);
+            }
+            while (ok && cur.n < nscore) {
+                ok = issue_pv(cur);
+                if (ok && ahead.n < nscore) {
+                    ok = issue_s(ahead);
+                    advance(ahead);
                 }
+                advance(cur);
             }
             tc_commit(drain);
             volatile int no_abort = 0;
@@ -324,6 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = a.scale_log2;
         const uint64_t sl2x2 = f2_make(sl2, sl2);
         bool ok = true;
+        // Score tile n = 2g + t: buffer n % 3 and its use parity, advanced
+        // by increments (n grows by 2 per KV tile).
+        int buf = t, bph = 0;
         for (int k = 0; k < nmine && ok; k++) {
             // Warps whose 32 query rows lie beyond N (the padding tile of an odd
             // tile count, or the second half of a last 128-row tile) keep the
@@ -333,25 +370,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 a.N;
             float m_used = -INFINITY;
             for (int j = 0; j < nkv; j++) {
-                const int g = k * nkv + j;
-                const int n = 2 * g + t;
-                const int buf = n % NSB;
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&s_full[buf], (n / NSB) & 1, a.err, abort_flag));
+                ok = __all_sync(0xffffffffu, mbar_wait(&s_full[buf], bph, a.err, abort_flag));
                 if (!ok)
                     break;
                 tc_fence_after();
                 const uint32_t tS = tL + buf * BKV;
-                // The whole 96-score row in one TMEM round trip.
-                uint32_t s[BKV];
-                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(s));
-                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
-                tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
-                tmem_wait_ld();
-
                 bool resc = false;
                 float factor = 1.0f;
                 if (rows_live) {
+                    // The whole 96-score row in one TMEM round trip.
+                    uint32_t s[BKV];
+                    tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(s));
+                    tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                    tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+                    tmem_wait_ld();
                     const int valid = a.N - j * BKV;
                     if (valid < BKV) {  // only a sequence's last tile
 #pragma unroll
@@ -374,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         factor = ex2_approx(m_used - m_tile);
                         m_used = m_tile;
                     }
-                    // P = 2^(s * scale_log2 - m_used) as 16-bit pairs, in place
+                    // P = 2^(s * scale_log2 - m_used) as bf16 pairs, in place
                     // (s[i] holds keys 2i, 2i+1 for i < 48). Keys past N have
                     // s = -inf and get P = 0.
                     const uint64_t negm = f2_make(-m_used, -m_used);
@@ -386,10 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float x0, x1;
                         f2_split(x2, x0, x1);
                         uint32_t pp;
-                        if (V_F16) {
-                            pp = ex2_f16x2(pack_f16x2(x0, x1));
-                        }
-                        else if (((e >> 1) & 7) >= 8 - kPolyPairsPer16) {
+                        if (((e >> 1) & 7) >= 8 - kPolyPairsPer16) {
                             float p0, p1;
                             exp2_poly2(x0, x1, p0, p1);
                             pp = pack_bf16x2(p0, p1);
@@ -406,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // P.V of the previous KV tile done; P.V(n) is only issued after
                 // p_ready below.
                 if (__any_sync(0xffffffffu, resc)) {
-                    const int gp = g - 1;
+                    const int gp = k * nkv + j - 1;
                     ok = __all_sync(0xffffffffu, mbar_wait(&pv_full[t * 2 + (gp & 1)],
                                                            (gp >> 1) & 1, a.err, abort_flag));
                     if (!ok)
@@ -446,6 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive(&p_ready[buf]);
+                if ((buf += 2) >= NSB) {
+                    buf -= NSB;
+                    bph ^= 1;
+                }
             }
             if (!ok)
                 break;
@@ -515,11 +548,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <bool OUT_BF16, bool V_F16>
+template <bool OUT_BF16>
 int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int grid,
            cudaStream_t s)
 {
-    auto kern = attn_tc_kernel<OUT_BF16, V_F16>;
+    auto kern = attn_tc_kernel<OUT_BF16>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess)
@@ -532,7 +565,7 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int
 }  // namespace sam3
 
 extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
-                         void *out, int out_bf16, int v_f16, int *err, k_stream s)
+                         void *out, int out_bf16, int *err, k_stream s)
 {
     using namespace sam3;
     if (nseq <= 0 || N <= 0 || heads <= 0 || E != heads * HD ||
@@ -561,9 +594,5 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     a.nitems = (int)nitems;
     const int grid = nitems < sms ? (int)nitems : sms;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
-    if (v_f16)
-        return out_bf16 ? launch<true, true>(tq, tkv, a, grid, st)
-                        : launch<false, true>(tq, tkv, a, grid, st);
-    return out_bf16 ? launch<true, false>(tq, tkv, a, grid, st)
-                    : launch<false, false>(tq, tkv, a, grid, st);
+    return out_bf16 ? launch<true>(tq, tkv, a, grid, st) : launch<false>(tq, tkv, a, grid, st);
 }

@@ -54,13 +54,12 @@ int k_gemm_simt(int M, int N, int K, const void *A, int adt, long aoff, int lda,
                 long sc0, long sc1, int nb, int nb1, const float *bias,
                 const float *R, long roff, float alpha, int act, k_stream s);
 
-/* Fused windowed/global self-attention on tensor cores. qkv: 16-bit
+/* Fused windowed/global self-attention on tensor cores. qkv: bf16
  * [nseq * N, 3E] rows (q | k | v, head h at column h * hd, RoPE already
- * applied); q and k bf16, v bf16 or (v_f16) f16. out: [nseq * N, E] fp32 or
- * bf16. scale multiplies the scores (1/sqrt(hd)). hd must be 64;
- * E % 64 == 0. */
+ * applied), out: [nseq * N, E] fp32 or bf16. scale multiplies the scores
+ * (1/sqrt(hd)). hd must be 64; E % 64 == 0. */
 int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
-              void *out, int out_bf16, int v_f16, int *err, k_stream s);
+              void *out, int out_bf16, int *err, k_stream s);
 
 /* The same attention in fp32 on CUDA cores (reference mode): qkv fp32. */
 int k_attn_f32(const float *qkv, int nseq, int N, int E, int heads, int hd,

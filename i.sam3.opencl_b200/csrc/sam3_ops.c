@@ -291,7 +291,7 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
                               "attention: cast"));
         return cbi_kstatus(b,
                           k_attn_tc(s, nseq, N, E, heads, scale, out->ptr,
-                                    out->dtype == CB_BF16, 0, b->d_err,
+                                    out->dtype == CB_BF16, b->d_err,
                                     (k_stream)b->stream),
                           "attention (tcgen05)");
     }
@@ -299,7 +299,7 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
         return cbi_fail(b, CB_EDTYPE, "attention: bf16 qkv must be pre-roped");
     return cbi_kstatus(b,
                       k_attn_tc(qkv->ptr, nseq, N, E, heads, scale, out->ptr,
-                                out->dtype == CB_BF16, 0, b->d_err,
+                                out->dtype == CB_BF16, b->d_err,
                                 (k_stream)b->stream),
                       "attention (tcgen05)");
 }

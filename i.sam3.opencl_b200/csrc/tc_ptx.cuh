@@ -333,19 +333,8 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr)
     return d;
 }
 
-// Instruction descriptors of tcgen05.mma kind::f16 with fp32 D: f16 A and B
-// (idesc_f16_f32) or bf16 A and B (idesc_bf16_f32), M x N tile, A/B K-major
-// (0) or MN-major (1).
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn_major,
-                                                     int b_mn_major)
-{
-    return (1u << 4)                          // D format: F32
-           | ((uint32_t)a_mn_major << 15)     // A format F16 (0), A major
-           | ((uint32_t)b_mn_major << 16)     // B format F16 (0), B major
-           | ((uint32_t)(N >> 3) << 17)       // N / 8
-           | ((uint32_t)(M >> 4) << 24);      // M / 16
-}
-
+// Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B, fp32 D,
+// M x N tile, A/B K-major (0) or MN-major (1).
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn_major,
                                                       int b_mn_major)
 {
@@ -363,21 +352,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
-}
-
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi)
-{
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-
-// 2^x for a pair of f16 values in one MUFU instruction.
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x)
-{
-    uint32_t y;
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-    return y;
 }
 
 __device__ __forceinline__ float ex2_approx(float x)

@@ -154,6 +154,28 @@ def test_attention_tc_vs_oracle(cb, sb, ob, side, nseq):
     assert cos_sim(got, want) >= 0.9999
 
 
+def _bf16_bits(x):
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("side,nseq", [(24, 3), (13, 2)])
+def test_attention_tc_bf16_qkv_vs_oracle(cb, sb, ob, side, nseq):
+    """Pre-roped bf16 qkv in (the QKV projection's output layout), no RoPE
+    table: the kernel alone."""
+    E = 1024
+    N, qkv, cs, roped = _attn_case(ob, side, nseq, E, stream=23)
+    want = ob.attention(roped, nseq, N, E, 16, 64, 0.125)
+    mq = cb.upload(_bf16_bits(roped), sb.BF16)
+    mo = cb.alloc(nseq * N * E * 4, sb.F32)
+    cb.attention(mq, nseq, N, E, 16, 64, None, N, 0.125, sb.ATTN_TC, mo)
+    got = np.empty((nseq * N, E), np.float32)
+    cb.read(mo, got)
+    cb.sync()
+    assert np.abs(got - want).max() <= 1e-2
+    assert cos_sim(got, want) >= 0.9999
+
+
 def test_attention_tc_global_vs_oracle(cb, sb, ob):
     """Config 2: global attention over the 72 x 72 grid, 16 heads."""
     E = 1024
