@@ -88,10 +88,12 @@ __device__ __forceinline__ int rope_row(const k_rope &r, int m)
 }
 
 // Epilogue math on CW consecutive columns of row m starting at column n:
-// alpha, bias, activation, residual, RoPE (the reference's order).
+// alpha, bias, activation, residual, RoPE (the reference's order). rv / rot,
+// when given, hold the chunk's residual values / (cos, sin) pairs already
+// loaded into registers; otherwise they are read here.
 template <int CW>
 __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, float (&v)[CW],
-                                              int rrow)
+                                              int rrow, const float4 *rv, const float2 *rot)
 {
 #pragma unroll
     for (int j = 0; j < CW; j++)
@@ -122,7 +124,16 @@ __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, fl
     }
     if (p.R && m < p.M) {
         const float *rp = p.R + (long)(p.rmod ? m % p.rmod : m) * p.ldr + n;
-        if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+        if (rv) {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+                v[j] += rv[j / 4].x;
+                v[j + 1] += rv[j / 4].y;
+                v[j + 2] += rv[j / 4].z;
+                v[j + 3] += rv[j / 4].w;
+            }
+        }
+        else if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
                 const float4 q = *reinterpret_cast<const float4 *>(rp + j);
@@ -146,57 +157,53 @@ __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, fl
                            (long)rrow * (p.rope.hd / 2) + ((n % p.rope.hd) >> 1);
 #pragma unroll
         for (int j = 0; j < CW; j += 2) {
-            const float2 rot = __ldg(cs + (j >> 1));
+            const float2 r = rot ? rot[j >> 1] : __ldg(cs + (j >> 1));
             const float a = v[j], b = v[j + 1];
-            v[j] = a * rot.x - b * rot.y;
-            v[j + 1] = a * rot.y + b * rot.x;
+            v[j] = a * r.x - b * r.y;
+            v[j + 1] = a * r.y + b * r.x;
         }
     }
 }
 
-// Direct (non-TMA) store of one chunk of row m; used when C's base or
-// leading dimension is not 16-byte aligned.
+// Direct (non-TMA) store of one chunk of row m (its 128 bytes packed in
+// pk: bf16 pairs or fp32 words); used when C's base or leading dimension is
+// not 16-byte aligned.
 template <int CW, bool OUT_BF16>
-__device__ __forceinline__ void store_direct(const GemmEpi &p, int m, int n, const float (&v)[CW])
+__device__ __forceinline__ void store_direct(const GemmEpi &p, int m, int n,
+                                             const uint32_t (&pk)[32])
 {
     if (m >= p.M)
         return;
     if (OUT_BF16) {
-        __nv_bfloat16 *cp = reinterpret_cast<__nv_bfloat16 *>(p.C) + (long)m * p.ldc + n;
+        uint16_t *cp = reinterpret_cast<uint16_t *>(p.C) + (long)m * p.ldc + n;
         for (int j = 0; j < CW; j++)
             if (n + j < p.N)
-                cp[j] = __float2bfloat16_rn(v[j]);
+                cp[j] = (uint16_t)(pk[j >> 1] >> ((j & 1) * 16));
     }
     else {
         float *cp = reinterpret_cast<float *>(p.C) + (long)m * p.ldc + n;
         for (int j = 0; j < CW; j++)
             if (n + j < p.N)
-                cp[j] = v[j];
+                cp[j] = __uint_as_float(pk[j]);
     }
 }
 
-// Writes one row's 128 bytes (CW values) into a 128B-swizzled staging tile:
-// 16-byte chunk q of row r goes to chunk position q ^ (r & 7), the layout a
+// Writes one row's 128 bytes into a 128B-swizzled staging tile: 16-byte
+// chunk q of row r goes to chunk position q ^ (r & 7), the layout a
 // SWIZZLE_128B tensor map expects; eight consecutive rows cover all 32 banks.
-template <int CW, bool OUT_BF16>
-__device__ __forceinline__ void stage_row(uint32_t tile, int r, const float (&v)[CW])
+__device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (&pk)[32])
 {
     const uint32_t row = tile + r * 128;
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-        const uint32_t dst = row + ((q ^ (r & 7)) << 4);
-        if (OUT_BF16)
-            st_shared_v4(dst, pack_bf16x2(v[8 * q], v[8 * q + 1]),
-                         pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                         pack_bf16x2(v[8 * q + 4], v[8 * q + 5]),
-                         pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
-        else
-            st_shared_v4(dst, __float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
-                         __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
-    }
+    for (int q = 0; q < 8; q++)
+        st_shared_v4(row + ((q ^ (r & 7)) << 4), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                     pk[4 * q + 3]);
 }
 
-template <int BN, bool OUT_BF16, bool TMA_STORE>
+// ROPE_PF: bf16 output whose tiles may need RoPE, with the row's (cos, sin)
+// pairs held in registers (a separate instantiation: the register budget of
+// the other epilogues does not carry them).
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -338,47 +345,121 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (TMA_STORE && lane == 0)
             prefetch_tmap(&tmC);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const bool ok = mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
-            if (!__all_sync(0xffffffffu, ok))
-                break;
-            tc_fence_after();
             const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
             const int r0 = m0 + quarter * 32;
             const int m = r0 + lane;
             const int rrow = p.rope.mode ? rope_row(p.rope, m < p.M ? m : 0) : 0;
+            // Global reads issued before the accumulator wait, so that their
+            // latency hides behind the tile's main loop: with bf16 output the
+            // row's 32 RoPE (cos, sin) pairs (every 64-column chunk is one
+            // head and uses all of them); with fp32 output the residual of
+            // this warp's first chunk (later chunks are fetched one ahead).
+            float2 rc[ROPE_PF ? 32 : 1];
+            const bool rope_tile = ROPE_PF && p.rope.mode && p.rope.hd == 64 && n0 < 2 * p.rope.E;
+            if (ROPE_PF && rope_tile) {
+                const float4 *cs = reinterpret_cast<const float4 *>(p.rope.cs) + (long)rrow * 16;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float4 q = __ldg(cs + j);
+                    rc[2 * j] = make_float2(q.x, q.y);
+                    rc[2 * j + 1] = make_float2(q.z, q.w);
+                }
+            }
+            const bool rfast = !OUT_BF16 && p.R && m < p.M && n0 + BN <= p.N &&
+                               (p.ldr & 3) == 0 &&
+                               (reinterpret_cast<uintptr_t>(p.R) & 15) == 0;
+            const float *rrowp =
+                rfast ? p.R + (long)(p.rmod ? m % p.rmod : m) * p.ldr + n0 : nullptr;
+            float4 rnext[OUT_BF16 ? 1 : CW / 4];
+            if (!OUT_BF16 && rfast) {
+#pragma unroll
+                for (int j = 0; j < CW / 4; j++)
+                    rnext[j] = *reinterpret_cast<const float4 *>(rrowp + half * CW + 4 * j);
+            }
+            const bool ok = mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
+            if (!__all_sync(0xffffffffu, ok))
+                break;
+            tc_fence_after();
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
             for (int c = half; c < NCHUNK; c += 2) {
                 const int n = n0 + c * CW;
-                float v[CW];
-                {
-                    uint32_t r[32];
-                    tmem_ld32(tbase + c * CW, r);
-                    if constexpr (CW == 64) {
-                        uint32_t r2[32];
+                if (n >= p.N)
+                    continue;  // warp-uniform: a chunk entirely beyond C
+                uint32_t pk[32];  // the chunk's 128-byte output row
+                float v32[OUT_BF16 ? 1 : 32];
+                if constexpr (OUT_BF16 && !ROPE_PF) {
+                    // 64 columns in one TMEM round trip.
+                    float v[64];
+                    {
+                        uint32_t r[32], r2[32];
+                        tmem_ld32(tbase + c * CW, r);
                         tmem_ld32(tbase + c * CW + 32, r2);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int j = 0; j < 32; j++)
+                        for (int j = 0; j < 32; j++) {
+                            v[j] = __uint_as_float(r[j]);
                             v[32 + j] = __uint_as_float(r2[j]);
+                        }
                     }
-                    else
-                        tmem_wait_ld();
+                    epilogue_math<64>(p, m, n, v, rrow, nullptr, nullptr);
 #pragma unroll
                     for (int j = 0; j < 32; j++)
-                        v[j] = __uint_as_float(r[j]);
+                        pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
                 }
-                if (n >= p.N)
-                    continue;  // warp-uniform: a chunk entirely beyond C
-                epilogue_math<CW>(p, m, n, v, rrow);
+                else if constexpr (OUT_BF16) {
+                    // With the row's RoPE pairs held in registers: 64 columns
+                    // in two halves of 32 (fewer live registers).
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        float v[32];
+                        {
+                            uint32_t r[32];
+                            tmem_ld32(tbase + c * CW + h * 32, r);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                v[j] = __uint_as_float(r[j]);
+                        }
+                        epilogue_math<32>(p, m, n + h * 32, v, rrow, nullptr,
+                                          rope_tile && n < 2 * p.rope.E ? rc + h * 16 : nullptr);
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            pk[h * 16 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                    }
+                }
+                else {
+                    float4 rcur[CW / 4];
+#pragma unroll
+                    for (int j = 0; j < CW / 4; j++)
+                        rcur[j] = rnext[j];
+                    if (rfast && c + 2 < NCHUNK) {
+#pragma unroll
+                        for (int j = 0; j < CW / 4; j++)
+                            rnext[j] = *reinterpret_cast<const float4 *>(rrowp + (c + 2) * CW +
+                                                                         4 * j);
+                    }
+                    {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * CW, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            v32[j] = __uint_as_float(r[j]);
+                    }
+                    epilogue_math<32>(p, m, n, v32, rrow, rfast ? rcur : nullptr, nullptr);
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        pk[j] = __float_as_uint(v32[j]);
+                }
                 if (TMA_STORE) {
                     // The store issued two chunks ago used this buffer.
                     if (lane == 0)
                         bulk_wait_read<1>();
                     __syncwarp();
                     const uint32_t tile = stage0 + buf * kStageTile;
-                    stage_row<CW, OUT_BF16>(tile, lane, v);
+                    stage_row(tile, lane, pk);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0 && r0 < p.M) {
@@ -390,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     buf ^= 1;
                 }
                 else
-                    store_direct<CW, OUT_BF16>(p, m, n, v);
+                    store_direct<CW, OUT_BF16>(p, m, n, pk);
             }
             tc_fence_before();
             __syncwarp();
@@ -412,12 +493,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool OUT_BF16, bool TMA_STORE>
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false>
 int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
            const GemmEpi &p, int num_sms, cudaStream_t s)
 {
     using L = GemmSmem<BN>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess)
@@ -433,7 +514,9 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &t
               bool bf16, const GemmEpi &p, int num_sms, cudaStream_t s)
 {
     if (bf16)
-        return tma ? launch<BN, true, true>(ta, tb, tc, p, num_sms, s)
+        return tma ? (p.rope.mode && p.rope.hd == 64
+                          ? launch<BN, true, true, true>(ta, tb, tc, p, num_sms, s)
+                          : launch<BN, true, true>(ta, tb, tc, p, num_sms, s))
                    : launch<BN, true, false>(ta, tb, tc, p, num_sms, s);
     return tma ? launch<BN, false, true>(ta, tb, tc, p, num_sms, s)
                : launch<BN, false, false>(ta, tb, tc, p, num_sms, s);
