@@ -62,18 +62,32 @@ struct GemmSmem {
     static constexpr int BYTES = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
 };
 
-__device__ __forceinline__ float gelu_erf(float x)
+// GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) (sam3_kernels.cl:43-46) on a pair of
+// values, with erf from Abramowitz & Stegun 7.1.26 (Hastings):
+//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
+// so GELU(x) = x (1 - h) for x >= 0 and x h for x < 0, with
+// h = erfc(|x| / sqrt 2) / 2 = t (...) 2^(-x^2 log2(e) / 2 - 1). Two MUFU
+// operations per value (reciprocal, 2^x) and the polynomial in packed fp32;
+// the result differs from the erf form by at most 4.2e-7 |x|-relative, far
+// below the bf16 rounding of the output it feeds.
+__device__ __forceinline__ void gelu_pair(float &x0, float &x1)
 {
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
-
-__device__ __forceinline__ float act_fn(float v, int act)
-{
-    if (act == K_ACT_GELU)
-        return gelu_erf(v);
-    if (act == K_ACT_RELU)
-        return fmaxf(v, 0.0f);
-    return v;
+    const float kP = 0.3275911f;
+    const float t0 = rcp_approx(fmaf(kP * 0.70710678118654752f, fabsf(x0), 1.0f));
+    const float t1 = rcp_approx(fmaf(kP * 0.70710678118654752f, fabsf(x1), 1.0f));
+    const uint64_t t = f2_make(t0, t1);
+    uint64_t q = fma2(f2_make(1.061405429f, 1.061405429f), t, f2_make(-1.453152027f, -1.453152027f));
+    q = fma2(q, t, f2_make(1.421413741f, 1.421413741f));
+    q = fma2(q, t, f2_make(-0.284496736f, -0.284496736f));
+    q = fma2(q, t, f2_make(0.254829592f, 0.254829592f));
+    const float e0 = ex2_approx(fmaf(x0 * x0, -0.72134752044448170f, -1.0f));
+    const float e1 = ex2_approx(fmaf(x1 * x1, -0.72134752044448170f, -1.0f));
+    q = mul2(mul2(q, t), f2_make(e0, e1));
+    float h0, h1;
+    f2_split(q, h0, h1);
+    x0 *= x0 >= 0.0f ? 1.0f - h0 : h0;
+    x1 *= x1 >= 0.0f ? 1.0f - h1 : h1;
 }
 
 // Table row of the RoPE rotation for output row m.
@@ -117,10 +131,15 @@ __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, fl
                     v[j] += __ldg(p.bias + n + j);
         }
     }
-    if (p.act != K_ACT_NONE) {
+    if (p.act == K_ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < CW; j += 2)
+            gelu_pair(v[j], v[j + 1]);
+    }
+    else if (p.act == K_ACT_RELU) {
 #pragma unroll
         for (int j = 0; j < CW; j++)
-            v[j] = act_fn(v[j], p.act);
+            v[j] = fmaxf(v[j], 0.0f);
     }
     if (p.R && m < p.M) {
         const float *rp = p.R + (long)(p.rmod ? m % p.rmod : m) * p.ldr + n;

@@ -10,6 +10,8 @@ on the same seeded inputs. Tolerances:
   * index / copy kernels (window partition, im2col, add_bcast, RoPE):
     bit-exact where the arithmetic is the same single rounding.
 """
+import math
+
 import numpy as np
 import pytest
 
@@ -83,6 +85,25 @@ def test_gemm_tc_vs_fp32_product(cb, sb, M, N, K, out_bf16):
     err = (C.float() - ref).abs().max().item()
     tol = (2e-2 if out_bf16 else 1e-3) * max(1.0, ref.abs().max().item())
     assert err <= tol, (err, tol)
+
+
+def test_gemm_tc_gelu_epilogue_accuracy(cb, sb):
+    """The tensor-core epilogue's GELU (erf from Abramowitz & Stegun 7.1.26)
+    against the exact erf form: C = GELU(A I) with an identity B, so the
+    product is exact and only the activation is measured."""
+    M, N = 384, 64
+    x = torch.linspace(-10.0, 10.0, M * N, dtype=torch.float64)
+    A = x.reshape(M, N).to(torch.bfloat16).cuda()
+    B = torch.eye(N, dtype=torch.bfloat16).cuda()
+    C = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    cb.gemm(M, N, N, (cb.wrap(A), 0, N), (cb.wrap(B), 0, N), 1, (cb.wrap(C), 0, N),
+            act=sb.ACT_GELU)
+    cb.sync()
+    a = A.double().cpu()
+    ref = 0.5 * a * (1.0 + torch.erf(a / math.sqrt(2.0)))
+    err = ((C.double().cpu() - ref).abs() / a.abs().clamp(min=1.0)).max().item()
+    assert err <= 1e-6, err
 
 
 def test_linear_fp32_activations_bf16_weights_vs_oracle(cb, sb, ob):
