@@ -35,6 +35,10 @@ constexpr int BK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStageTile = 32 * 128;  // one warp's 32 rows x 128 bytes
+// Staging tiles per epilogue warp. One: the shared memory goes to a fourth
+// A/B stage instead, which the main loop gains more from than the epilogue
+// loses by waiting for its previous TMA store to be read.
+constexpr int kEpiBufs = 1;
 
 struct GemmEpi {
     int M, N, K;
@@ -52,14 +56,15 @@ struct GemmEpi {
 
 template <int BN>
 struct GemmSmem {
-    static constexpr int STAGES = BN == 256 ? 3 : 4;
+    static constexpr int STAGES = 4;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 2 * kStageTile;
+    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kEpiBufs * kStageTile;
     // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort
     static constexpr int BYTES = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
+    static_assert(BYTES <= 232448, "GEMM shared memory");
 };
 
 // GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) (sam3_kernels.cl:43-46) on a pair of
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ew = warp - 2;          // 0..7
         const int quarter = warp & 3;     // TMEM lane quarter this warp may read
         const int half = ew >> 2;         // which chunks of the tile (c % 2)
-        const uint32_t stage0 = smem_addr(smem + L::EPI_OFF + ew * 2 * kStageTile);
+        const uint32_t stage0 = smem_addr(smem + L::EPI_OFF + ew * kEpiBufs * kStageTile);
         int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -473,21 +478,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         pk[j] = __float_as_uint(v32[j]);
                 }
                 if (TMA_STORE) {
-                    // The store issued two chunks ago used this buffer.
+                    // The store issued kEpiBufs chunks ago used this buffer.
                     if (lane == 0)
-                        bulk_wait_read<1>();
+                        bulk_wait_read<kEpiBufs - 1>();
                     __syncwarp();
                     const uint32_t tile = stage0 + buf * kStageTile;
                     stage_row(tile, lane, pk);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0 && r0 < p.M) {
-                        tma_store_2d(&tmC, smem + L::EPI_OFF + ew * 2 * kStageTile +
+                        tma_store_2d(&tmC, smem + L::EPI_OFF + ew * kEpiBufs * kStageTile +
                                                buf * kStageTile,
                                      n, r0);
                         bulk_commit();
                     }
-                    buf ^= 1;
+                    buf = (buf + 1) % kEpiBufs;
                 }
                 else
                     store_direct<CW, OUT_BF16>(p, m, n, pk);
