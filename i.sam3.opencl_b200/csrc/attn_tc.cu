@@ -54,7 +54,7 @@ namespace {
 
 constexpr int HD = 64;
 constexpr int BQ = 128;
-constexpr int BKV = 96;
+constexpr int BKV = 96;  // keys per KV tile (a multiple of 32)
 constexpr int NO = HD + 16;               // O columns: 64 outputs + row-sum block
 constexpr int NSB = 3;                    // TMEM score buffers
 constexpr int KST = 3;                    // K and V ring stages
@@ -86,6 +86,7 @@ constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;
 static_assert(SMEM_BYTES <= 232448, "attention smem");
 static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "alignment");
 static_assert(TM_O + 2 * NO <= 512, "tensor memory");
+static_assert(BKV % 32 == 0 && BKV <= 256, "KV tile");
 
 struct AttnArgs {
     int nseq, N, E, heads;
@@ -378,11 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool resc = false;
                 float factor = 1.0f;
                 if (rows_live) {
-                    // The whole 96-score row in one TMEM round trip.
+                    // The whole score row in one TMEM round trip.
                     uint32_t s[BKV];
-                    tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(s));
-                    tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
-                    tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+#pragma unroll
+                    for (int c = 0; c < BKV / 32; c++)
+                        tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
                     tmem_wait_ld();
                     const int valid = a.N - j * BKV;
                     if (valid < BKV) {  // only a sequence's last tile
@@ -428,8 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         s[e >> 1] = pp;
                     }
-                    tmem_st32(tS, *reinterpret_cast<const uint32_t(*)[32]>(s));
-                    tmem_st16(tS + 32, *reinterpret_cast<const uint32_t(*)[16]>(s + 32));
+#pragma unroll
+                    for (int c = 0; c < BKV / 64; c++)
+                        tmem_st32(tS + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(s + 32 * c));
+                    if constexpr (BKV % 64 != 0)
+                        tmem_st16(tS + BKV / 64 * 32,
+                                  *reinterpret_cast<const uint32_t(*)[16]>(s + BKV / 64 * 32));
                 }
                 // A raised maximum rescales O and its row sum, which needs
                 // P.V of the previous KV tile done; P.V(n) is only issued after
