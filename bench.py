@@ -126,7 +126,7 @@ def dist_setup(args):
         import datetime
         import torch.distributed as dist
         backend = "nccl" if args.impl == "ours" else "gloo"
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
         pg = dist
     return world, rank, local, pg
 
@@ -259,13 +259,13 @@ def our_arm(args, world, rank, local, pg):
     torch.cuda.set_device(local)
     pk = peaks()
     cb = sb.Backend(local)
-    n = TOTAL_TILES // world
+    first, n = sb.tile_shard(TOTAL_TILES, world, rank)
     enc = sb.Encoder(cb, max_tiles=n)
     enc.init_random(SEED)
     # this rank's shard of the 64 tiles, pinned host memory and device copy
     host = torch.empty(n, SIDE, SIDE, 3, dtype=torch.uint8).pin_memory()
     for i in range(n):  # the product's seeded generator (include/sam3_synth.h)
-        sb.lib().sam3_synth_u8(SEED, image_stream(rank * n + i), SIDE * SIDE * 3,
+        sb.lib().sam3_synth_u8(SEED, image_stream(first + i), SIDE * SIDE * 3,
                                host[i].data_ptr())
     dev_tiles = host.cuda()
     out = torch.empty(n, 5184, 1024, dtype=torch.float32, device="cuda")
@@ -281,11 +281,7 @@ def our_arm(args, world, rank, local, pg):
             pg.barrier()
 
     def max_over_ranks(v):
-        if not pg:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+        return sb.max_over_ranks(v, pg, "cuda")
 
     for _ in range(args.warmup):
         enc.encode_tiles(m_tiles, n, m_out)
@@ -302,7 +298,7 @@ def our_arm(args, world, rank, local, pg):
     cb.profile(False)
     ms = max_over_ranks(e0.elapsed_time(e1))
     prof = cb.profile_table()
-    value = world * n * args.steps / (ms * 1e-3)
+    value = TOTAL_TILES * args.steps / (ms * 1e-3)
 
     # end to end through the public host API: pinned host tiles in, tokens out
     enc.encode_tiles_host(host.numpy(), host_out.numpy())
@@ -317,7 +313,7 @@ def our_arm(args, world, rank, local, pg):
         barrier()
         e2e_ms.append(t0.elapsed_time(t1))
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms))
-    e2e_value = world * n / (e2e_step * 1e-3)
+    e2e_value = TOTAL_TILES / (e2e_step * 1e-3)
 
     line = None
     if rank == 0:
@@ -351,8 +347,8 @@ def our_arm(args, world, rank, local, pg):
             "kernels": kernels,
             "attention": attn,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
-                    "h2d_bytes_per_step": world * n * SIDE * SIDE * 3,
-                    "d2h_bytes_per_step": world * n * 5184 * 1024 * 4},
+                    "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
+                    "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},
             "gpu_launches": int(sum(v["calls"] for v in prof.values())),
             "clocks": clk.summary(),
         }

@@ -43,6 +43,33 @@ W = dict(PATCH_W=0, POS=1, LN_PRE_W=2, LN_PRE_B=3, ROPE_WIN=4, ROPE_GLOB=5,
          N2_B=17, FC1_W=18, FC1_B=19, FC2_W=20, FC2_B=21)
 
 
+# ---------------------------------------------------------------- tile sharding
+def tile_shard(total, world, rank):
+    """This rank's contiguous block of the crop loop, as (start, count).
+
+    The reference encodes its crops one after another (amg.c:702-709); crops
+    are independent through the backbone, so with one process per GPU each
+    rank takes a contiguous block and no collective is needed in the data
+    path. Counts differ by at most one (lower ranks take the extra crops)."""
+    if world <= 0 or not 0 <= rank < world or total < 0:
+        raise ValueError(f"tile_shard: total={total} world={world} rank={rank}")
+    base, extra = divmod(total, world)
+    return rank * base + min(rank, extra), base + (1 if rank < extra else 0)
+
+
+def max_over_ranks(value, pg=None, device=None):
+    """The largest of a per-rank float over the process group (a step takes
+    as long as its slowest rank). pg: torch.distributed or None (one rank);
+    device: where the reduction tensor lives ("cuda" for NCCL, None for
+    gloo)."""
+    if pg is None:
+        return float(value)
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
 class Opnd(C.Structure):
     """struct cb_opnd (sam3_ops.h:19-24 with cl_mem -> cb_mem)."""
     _fields_ = [("buf", C.c_void_p), ("off", C.c_int64), ("ld", C.c_int32),
