@@ -46,8 +46,13 @@ struct cb_encoder {
     void *qkv;       /* bf16 [rows, 3E] */
     void *attn;      /* bf16 [rows, E] */
     void *h;         /* bf16 [rows, max(mlp, kpad)] */
-    uint8_t *tiles;  /* staging for cb_encode_tiles_host */
-    float *out_dev;  /* staging for cb_encode_tiles_host */
+    /* cb_encode_tiles_host pipeline: two staging buffers per direction,
+     * chunk tiles each, a stream per copy direction and their events */
+    int chunk;
+    uint8_t *tiles[2];
+    float *out_dev[2];
+    cudaStream_t h2d, d2h;
+    cudaEvent_t ev_in[2], ev_done[2], ev_out[2];
 };
 
 void cb_encoder_default_config(struct cb_encoder_config *c)
@@ -80,6 +85,10 @@ void cb_encoder_free(cb_encoder *e)
         return;
     cbi_enter(e->b);
     cudaStreamSynchronize(e->b->stream);
+    if (e->h2d)
+        cudaStreamSynchronize(e->h2d);
+    if (e->d2h)
+        cudaStreamSynchronize(e->d2h);
     if (e->blk)
         for (i = 0; i < e->cfg.depth; i++) {
             struct enc_block *k = &e->blk[i];
@@ -109,8 +118,20 @@ void cb_encoder_free(cb_encoder *e)
     cudaFree(e->qkv);
     cudaFree(e->attn);
     cudaFree(e->h);
-    cudaFree(e->tiles);
-    cudaFree(e->out_dev);
+    for (i = 0; i < 2; i++) {
+        cudaFree(e->tiles[i]);
+        cudaFree(e->out_dev[i]);
+        if (e->ev_in[i])
+            cudaEventDestroy(e->ev_in[i]);
+        if (e->ev_done[i])
+            cudaEventDestroy(e->ev_done[i]);
+        if (e->ev_out[i])
+            cudaEventDestroy(e->ev_out[i]);
+    }
+    if (e->h2d)
+        cudaStreamDestroy(e->h2d);
+    if (e->d2h)
+        cudaStreamDestroy(e->d2h);
     free(e);
 }
 
@@ -553,34 +574,98 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last)
                       "encode_blocks");
 }
 
-int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
-                         float *out)
+/* Chunk of the host-buffer pipeline: about a quarter of a large batch (so
+ * that the copies of neighbouring chunks hide behind the compute), at least
+ * 8 tiles (GEMM tails stay small), at most max_tiles. */
+static int host_chunk(const cb_encoder *e, int ntile)
+{
+    int c = (ntile + 3) / 4;
+
+    if (c < 8)
+        c = ntile < 8 ? ntile : 8;
+    return c > e->cfg.max_tiles ? e->cfg.max_tiles : c;
+}
+
+static int host_pipeline_setup(cb_encoder *e, int chunk)
 {
     const size_t side = (size_t)e->cfg.grid * e->cfg.patch;
     const size_t tile_in = side * side * 3;
     const size_t tile_out = (size_t)e->T * e->cfg.embed * 4;
+    int i;
+
+    if (e->chunk >= chunk)
+        return CB_OK;
+    for (i = 0; i < 2; i++) {
+        cudaFree(e->tiles[i]);
+        cudaFree(e->out_dev[i]);
+        e->tiles[i] = NULL;
+        e->out_dev[i] = NULL;
+    }
+    e->chunk = 0;
+    for (i = 0; i < 2; i++) {
+        CB_TRY(dev_alloc(e, (void **)&e->tiles[i], tile_in * chunk));
+        CB_TRY(dev_alloc(e, (void **)&e->out_dev[i], tile_out * chunk));
+        if (!e->ev_in[i] &&
+            (cudaEventCreateWithFlags(&e->ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+             cudaEventCreateWithFlags(&e->ev_done[i], cudaEventDisableTiming) != cudaSuccess ||
+             cudaEventCreateWithFlags(&e->ev_out[i], cudaEventDisableTiming) != cudaSuccess))
+            return cbi_fail(e->b, CB_ECUDA, "encode_tiles_host: events");
+    }
+    if (!e->h2d && (cudaStreamCreateWithFlags(&e->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+                    cudaStreamCreateWithFlags(&e->d2h, cudaStreamNonBlocking) != cudaSuccess))
+        return cbi_fail(e->b, CB_ECUDA, "encode_tiles_host: streams");
+    e->chunk = chunk;
+    return CB_OK;
+}
+
+/* Host-to-host encode as a three-stage pipeline over chunks: chunk c's
+ * host-to-device copy (h2d stream) and chunk c-1's device-to-host copy (d2h
+ * stream) run while chunk c-1 / c computes on the backend stream. Buffer
+ * c % 2 is reused by chunk c + 2 only after its copy out (outputs) and its
+ * encode (inputs) are done, which the events order. */
+int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
+                         float *out)
+{
+    size_t side, tile_in, tile_out;
     cb_backend *b;
-    int t0;
+    int chunk, t0, c;
 
     if (!e || !tiles || !out || ntile <= 0)
         return cbi_fail(e ? e->b : NULL, CB_EARG, "encode_tiles_host");
     b = e->b;
+    side = (size_t)e->cfg.grid * e->cfg.patch;
+    tile_in = side * side * 3;
+    tile_out = (size_t)e->T * e->cfg.embed * 4;
     CB_TRY(cbi_enter(b));
-    if (!e->tiles) {
-        CB_TRY(dev_alloc(e, (void **)&e->tiles, tile_in * e->cfg.max_tiles));
-        CB_TRY(dev_alloc(e, (void **)&e->out_dev, tile_out * e->cfg.max_tiles));
-    }
-    for (t0 = 0; t0 < ntile; t0 += e->cfg.max_tiles) {
-        const int n = ntile - t0 < e->cfg.max_tiles ? ntile - t0 : e->cfg.max_tiles;
+    chunk = host_chunk(e, ntile);
+    CB_TRY(host_pipeline_setup(e, chunk));
+    for (t0 = 0, c = 0; t0 < ntile; t0 += chunk, c++) {
+        const int n = ntile - t0 < chunk ? ntile - t0 : chunk;
+        const int i = c & 1;
 
-        CB_TRY(cbi_kstatus(b, (int)cudaMemcpyAsync(e->tiles, tiles + t0 * tile_in,
+        if (c >= 2)  /* chunk c - 2's encode has read tiles[i] */
+            CB_TRY(cbi_kstatus(b, (int)cudaStreamWaitEvent(e->h2d, e->ev_done[i], 0),
+                              "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaMemcpyAsync(e->tiles[i], tiles + t0 * tile_in,
                                                   n * tile_in, cudaMemcpyHostToDevice,
-                                                  b->stream), "encode_tiles_host"));
-        CB_TRY(encode_dev(e, e->tiles, n, e->out_dev));
-        CB_TRY(cbi_kstatus(b, (int)cudaMemcpyAsync((char *)out + t0 * tile_out,
-                                                  e->out_dev, n * tile_out,
-                                                  cudaMemcpyDeviceToHost, b->stream),
+                                                  e->h2d), "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaEventRecord(e->ev_in[i], e->h2d), "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaStreamWaitEvent(b->stream, e->ev_in[i], 0),
                           "encode_tiles_host"));
+        if (c >= 2)  /* chunk c - 2's outputs have left out_dev[i] */
+            CB_TRY(cbi_kstatus(b, (int)cudaStreamWaitEvent(b->stream, e->ev_out[i], 0),
+                              "encode_tiles_host"));
+        CB_TRY(encode_dev(e, e->tiles[i], n, e->out_dev[i]));
+        CB_TRY(cbi_kstatus(b, (int)cudaEventRecord(e->ev_done[i], b->stream),
+                          "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaStreamWaitEvent(e->d2h, e->ev_done[i], 0),
+                          "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaMemcpyAsync((char *)out + t0 * tile_out,
+                                                  e->out_dev[i], n * tile_out,
+                                                  cudaMemcpyDeviceToHost, e->d2h),
+                          "encode_tiles_host"));
+        CB_TRY(cbi_kstatus(b, (int)cudaEventRecord(e->ev_out[i], e->d2h), "encode_tiles_host"));
     }
+    CB_TRY(cbi_kstatus(b, (int)cudaStreamSynchronize(e->d2h), "encode_tiles_host"));
     return cb_sync(b);
 }

@@ -295,9 +295,11 @@ int cb_encode_tiles(cb_encoder *e, cb_mem tiles, int ntile, cb_mem out);
  * grid^2, E] in place (the prologue is skipped). For block-level tests. */
 int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last);
 
-/* Host-to-host convenience: copies tiles from host memory, encodes in
- * chunks of at most max_tiles with the copies overlapped, and copies the
- * tokens back to host memory out [ntile, grid^2, E]. Blocking. */
+/* Host-to-host convenience: tiles from host memory, tokens back to host
+ * memory out [ntile, grid^2, E]. Blocking. Runs as a pipeline over chunks
+ * (about ntile / 4 tiles, at least 8, at most max_tiles): the copy of the
+ * next chunk in and of the previous chunk out overlap the encode of the
+ * current one (page-locked host buffers let the copies run asynchronously). */
 int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
                          float *out);
 

@@ -63,6 +63,31 @@ def test_encoder_batch_equals_single_tiles(cb, sb, ob):
     enc.close()
 
 
+@pytest.mark.parametrize("ntile", [3, 11])
+def test_encode_tiles_host_pipeline_equals_device_path(cb, sb, ob, ntile):
+    """The host-buffer entry point (chunks of at least 8 tiles with copies in
+    and out overlapping the encode; 11 tiles = chunks of 8 and 3) returns,
+    bit for bit, what the device-buffer path returns for the same tiles, and
+    a second call reuses its staging buffers."""
+    seed = 8
+    enc = sb.Encoder(cb, max_tiles=ntile, depth=1, global_blocks=(0,))
+    enc.init_random(seed)
+    imgs = np.stack([ob.u8(seed, image_stream(t), (1008, 1008, 3)) for t in range(ntile)])
+    tiles = cb.upload(imgs, sb.U8)
+    out = cb.alloc(ntile * 5184 * 1024 * 4, sb.F32)
+    enc.encode_tiles(tiles, ntile, out)
+    want = np.empty((ntile, 5184, 1024), np.float32)
+    cb.read(out, want)
+    cb.sync()
+    host_in = torch.from_numpy(imgs).pin_memory()
+    host_out = torch.empty(ntile, 5184, 1024, dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        host_out.zero_()
+        enc.encode_tiles_host(host_in, host_out)
+        assert np.array_equal(host_out.numpy(), want)
+    enc.close()
+
+
 def test_encode_blocks_matches_oracle_vit_block(cb, sb, ob):
     """cb_encode_blocks on raster tokens == oracle vit_block, per block kind."""
     seed = 7
