@@ -7,8 +7,10 @@ backbone (width 1024, 16 heads, MLP 4096, 24 x 24 windows, global blocks
 sharded evenly across the GPUs (one process per GPU, no collective in the
 data path). The total is fixed at 64 tiles, so "scaling" is "strong". A step
 = one pass of every rank's tile shard through the backbone. The line also
-carries the attention configs 1 and 2 measured on rank 0 (the metric's "PE
-attention TFLOP/s" part).
+carries, measured on rank 0, the attention configs 1 and 2 (the metric's "PE
+attention TFLOP/s" part) and the decoder attention of config 3 (GB/s against
+the HBM peak); at N = 1 it adds the reference kernels' CPU times of configs
+1-3 (`cpu_configs`) beside the tiles/s `cpu_baseline`.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -240,6 +242,106 @@ def attention_bench(sb, cb, torch, pk, iters=10):
     return res
 
 
+# Config 3: the mask decoder's fused attention for one batch of 64 prompts
+# (sam3_model.c:419-451; dint 128, 8 heads of 16, 5184 image tokens), with the
+# reference's 8 tokens per prompt (sam3_model.c:34-35) and the 7 BASELINE
+# names. t2i: prompt tokens over the image (per-prompt K/V, as the decoder's
+# two-way layers feed it, or one shared K/V); i2t: image tokens over the
+# prompt tokens. HBM-bound: GB/s = algorithmic bytes / kernel time.
+DEC_P, DEC_NK, DEC_D = 64, 5184, 128
+
+
+def decoder_cases(ntok):
+    P, N, D = DEC_P, DEC_NK, DEC_D
+    return [  # name, Nq, Nk, q rows, kv rows, shared kv, algorithmic bytes
+        (f"t2i_per_prompt_kv_{ntok}tok", ntok, N, P * ntok, P * N, False,
+         4 * (P * ntok * D * 2 + 2 * P * N * D)),
+        (f"t2i_shared_kv_{ntok}tok", ntok, N, P * ntok, N, True,
+         4 * (P * ntok * D * 2 + 2 * N * D)),
+        (f"i2t_{ntok}tok", N, ntok, P * N, P * ntok, False,
+         4 * (P * N * D * 2 + 2 * P * ntok * D)),
+    ]
+
+
+def decoder_bench(cb, torch, pk, iters=10):
+    stream = torch.cuda.ExternalStream(cb.stream)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+    res = {}
+    for ntok in (8, 7):
+        for name, nq, nk, qrows, kvrows, shared, nbytes in decoder_cases(ntok):
+            q = torch.randn(qrows, DEC_D, device="cuda", generator=g)
+            k = torch.randn(kvrows, DEC_D, device="cuda", generator=g)
+            v = torch.randn(kvrows, DEC_D, device="cuda", generator=g)
+            o = torch.empty(qrows, DEC_D, device="cuda")
+            torch.cuda.synchronize()
+            mq, mk, mv, mo = cb.wrap(q), cb.wrap(k), cb.wrap(v), cb.wrap(o)
+            skv = 0 if shared else nk * DEC_D
+            times = []
+            for it in range(iters + 3):
+                with torch.cuda.stream(stream):
+                    flush_l2(flush)
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    cb.mha(DEC_P, nq, nk, DEC_D, mq, nq * DEC_D, mk, skv, mv, skv, mo)
+                    e1.record(stream)
+                stream.synchronize()
+                if it >= 3:
+                    times.append(e0.elapsed_time(e1))
+            t = statistics.median(times)
+            gbs = nbytes / (t * 1e-3) / 1e9
+            res[name] = {"ms": t, "gbs": gbs, "frac_hbm": gbs / pk["hbm"],
+                         "bytes": nbytes}
+        cb.sync()
+    res["peak_hbm_gbs"] = pk["hbm"]
+    res["batch"] = f"{DEC_P} prompts, dint {DEC_D}, 8 heads, {DEC_NK} image tokens"
+    return res
+
+
+def cpu_configs_sample():
+    """Configs 1-3 on the reference's kernels (oracle/_ref) on all host
+    cores, rank 0 at N=1: C1 and C2 RoPE + QK^T gemm_cpu_t + softmax_rows +
+    P.V gemm_cpu_n as vit_block launches them (C2 heads chunked by
+    head_chunk), C3 the attn_fewkeys / attn_manykeys kernels for one batch.
+    softmax_rows runs with one work-item per group (the host executor turns
+    work-group barriers into fiber switches; a one-item group needs none),
+    as the tiles/s baseline does. For C3 the faster of the reference kernel
+    and the oracle's restatement is reported, with its kind: attn_manykeys
+    needs its 256-item work-group barriers, which the host executor runs as
+    fibers, far slower than a CPU OpenCL compiler's work-item loops."""
+    from oracle import binding as ob
+    if not ob.have_ref():
+        return None
+    out = {"cores": ob.num_threads(), "kind": "reference"}
+    E = 1024
+    for name, side, nseq, hc in (("config1_window_9x576", 24, 9, 16),
+                                 ("config2_global_5184", 72, 1, 4)):
+        N = side * side
+        qkv = ob.normal(SEED, 70, (nseq * N, 3 * E))
+        cs = ob.rope_axial(side, 64)
+        t0 = time.perf_counter()
+        ob.rope_apply(qkv, E, 64, N, cs, use_ref=True)
+        ob.ref_attention(qkv, nseq, N, E, 16, 64, 0.125, head_chunk=hc, softmax_local=1)
+        t = time.perf_counter() - t0
+        out[name] = {"s": t, "tflops": 4.0 * nseq * 16 * N * N * 64 / t / 1e12}
+    for cname, nq, nk, qrows, kvrows, shared, nbytes in decoder_cases(8):
+        q = ob.normal(SEED, 71, (qrows, DEC_D))
+        k = ob.normal(SEED, 72, (kvrows, DEC_D))
+        v = ob.normal(SEED, 73, (kvrows, DEC_D))
+        skv = 0 if shared else nk * DEC_D
+        best = None
+        for kind, use_ref in (("reference", True), ("port", False)):
+            t0 = time.perf_counter()
+            ob.mha(DEC_P, nq, nk, DEC_D, q, nq * DEC_D, k, skv, v, skv, use_ref=use_ref)
+            t = time.perf_counter() - t0
+            if best is None or t < best[0]:
+                best = (t, kind)
+        out["config3_" + cname] = {"s": best[0], "gbs": nbytes / best[0] / 1e9,
+                                   "kind": best[1]}
+    return out
+
+
 def cpu_baseline_sample():
     """Rank 0, N=1: the reference's CPU kernels on a bounded sample."""
     try:
@@ -329,6 +431,7 @@ def our_arm(args, world, rank, local, pg):
                        "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9,
                        "launches": v["calls"]} for k, v in prof.items()}
         attn = attention_bench(sb, cb, torch, pk)
+        dec = decoder_bench(cb, torch, pk)
         line = {
             "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -346,6 +449,7 @@ def our_arm(args, world, rank, local, pg):
                          "traffic": traffic},
             "kernels": kernels,
             "attention": attn,
+            "decoder_attention": dec,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
                     "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
                     "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},
@@ -404,6 +508,10 @@ def main():
         line = our_arm(args, world, rank, local, pg)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
+            try:
+                line["cpu_configs"] = cpu_configs_sample()
+            except Exception as e:  # reported, never required
+                line["cpu_configs"] = {"failed": str(e)}
     if pg:
         pg.barrier()
         pg.destroy_process_group()

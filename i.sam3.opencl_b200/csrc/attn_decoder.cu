@@ -1,0 +1,437 @@
+// SPDX-License-Identifier: Unlicense
+// The mask decoder's fused attention (mha, sam3_model.c:419-451): 8 heads
+// of c = dint / 8 channels, scale 1/sqrt(c), per-prompt strides sq / sk / sv
+// (elements; 0 shares one K/V among all prompts), output [P * Nq, dint].
+// It is bound by HBM, so both kernels are shaped around moving the bytes once
+// with enough of them in flight:
+//
+//   few keys (Nk <= 64: image-to-token, token self-attention;
+//   attn_fewkeys, sam3_kernels.cl:527-569): one CTA per 256 queries of a
+//   prompt, that prompt's K and V (a few KB) staged once in shared memory,
+//   then 8 blocks of 32 queries, one thread per (query, head), the next
+//   block's query loaded while the current one computes; the 8 heads of a
+//   query sit in 8 adjacent threads (whole 512-byte rows per 8 threads);
+//   online softmax over the keys from shared memory;
+//
+//   many keys (Nk > 64, c = 16: token-to-image; attn_manykeys,
+//   sam3_kernels.cl:577-633): the keys are split over `nsplit` CTAs per
+//   prompt so that every SM streams K/V (a prompt's K/V is 2.6 MB); a CTA
+//   (one split of one prompt, for 8 of its queries) pulls 32-key chunks of K
+//   and V with cp.async into a double buffer while its 256 threads (64
+//   (query, head) pairs x 4 key lanes) run the online softmax over the
+//   previous chunk, merges its 4 key lanes and writes one (m, l, o) partial
+//   per pair; a second kernel combines the splits.
+//
+// The 8 different heads a warp reads at once fall on distinct shared-memory
+// bank groups: rows padded to c + 4 floats per head (few keys) or 16-byte
+// chunks rotated per head (many keys, rows stay 512 bytes for cp.async).
+#include "kernels.h"
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#define STREAM(s) reinterpret_cast<cudaStream_t>(s)
+
+namespace sam3 {
+namespace {
+
+constexpr int kHeads = 8;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
+{
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ------------------------------------------------------------ few keys
+constexpr int kFewBlocks = 8;             // blocks of 32 queries per CTA
+constexpr int kFewQ = 32 * kFewBlocks;    // queries per CTA (256 threads)
+
+template <int C>
+__device__ __forceinline__ void load_q(const float *qp, float (&q)[C], float scale)
+{
+    const float4 *q4 = reinterpret_cast<const float4 *>(qp);
+#pragma unroll
+    for (int c = 0; c < C / 4; c++) {
+        const float4 v = __ldg(q4 + c);
+        q[4 * c] = v.x * scale;
+        q[4 * c + 1] = v.y * scale;
+        q[4 * c + 2] = v.z * scale;
+        q[4 * c + 3] = v.w * scale;
+    }
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) mha_few_kernel(const float *__restrict__ Q, long sq,
+                                                      const float *__restrict__ K, long sk,
+                                                      const float *__restrict__ V, long sv,
+                                                      float *__restrict__ O, int Nq, int Nk,
+                                                      float scale)
+{
+    constexpr int D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
+    extern __shared__ float kv[];  // K rows then V rows, [Nk][8][CP] each
+    float *ks = kv;
+    float *vs = kv + Nk * ROW;
+    const long p = blockIdx.y;
+    const int h = threadIdx.x & 7;
+    const int q0 = blockIdx.x * kFewQ + (threadIdx.x >> 3);  // block b: q0 + 32 b
+    const float *qbase = Q + p * sq + h * C;
+
+    // The first block's query, then the prompt's K and V staged once for
+    // all blocks (float4 pieces into padded rows).
+    float q[C];
+    if (q0 < Nq)
+        load_q<C>(qbase + (long)q0 * D, q, scale);
+    const float *kb = K + p * sk, *vb = V + p * sv;
+    for (int i = threadIdx.x; i < Nk * (D / 4); i += blockDim.x) {
+        const int j = i / (D / 4), col = (i - j * (D / 4)) * 4;
+        const int dst = j * ROW + (col / C) * CP + col % C;
+        *reinterpret_cast<float4 *>(ks + dst) =
+            __ldg(reinterpret_cast<const float4 *>(kb + (long)j * D + col));
+        *reinterpret_cast<float4 *>(vs + dst) =
+            __ldg(reinterpret_cast<const float4 *>(vb + (long)j * D + col));
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int b = 0; b < kFewBlocks; b++) {
+        const int qi = q0 + 32 * b;
+        if (qi >= Nq)
+            break;
+        // Next block's query in flight while this one computes.
+        float qn[C];
+        const bool more = b + 1 < kFewBlocks && qi + 32 < Nq;
+        if (more)
+            load_q<C>(qbase + (long)(qi + 32) * D, qn, scale);
+        float m = -INFINITY, l = 0.0f, o[C];
+#pragma unroll
+        for (int c = 0; c < C; c++)
+            o[c] = 0.0f;
+        for (int j = 0; j < Nk; j++) {
+            const float4 *kr = reinterpret_cast<const float4 *>(ks + j * ROW + h * CP);
+            float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;  // four short chains
+#pragma unroll
+            for (int c = 0; c < C / 4; c++) {
+                const float4 k4 = kr[c];
+                d0 = fmaf(q[4 * c], k4.x, d0);
+                d1 = fmaf(q[4 * c + 1], k4.y, d1);
+                d2 = fmaf(q[4 * c + 2], k4.z, d2);
+                d3 = fmaf(q[4 * c + 3], k4.w, d3);
+            }
+            const float s = (d0 + d1) + (d2 + d3);
+            const float mn = fmaxf(m, s), corr = __expf(m - mn), e = __expf(s - mn);
+            l = l * corr + e;
+            const float4 *vr = reinterpret_cast<const float4 *>(vs + j * ROW + h * CP);
+#pragma unroll
+            for (int c = 0; c < C / 4; c++) {
+                const float4 v4 = vr[c];
+                o[4 * c] = fmaf(e, v4.x, o[4 * c] * corr);
+                o[4 * c + 1] = fmaf(e, v4.y, o[4 * c + 1] * corr);
+                o[4 * c + 2] = fmaf(e, v4.z, o[4 * c + 2] * corr);
+                o[4 * c + 3] = fmaf(e, v4.w, o[4 * c + 3] * corr);
+            }
+            m = mn;
+        }
+        const float inv = 1.0f / l;
+        float4 *op = reinterpret_cast<float4 *>(O + (p * Nq + qi) * D + h * C);
+#pragma unroll
+        for (int c = 0; c < C / 4; c++)
+            op[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
+                                o[4 * c + 3] * inv);
+        if (more) {
+#pragma unroll
+            for (int c = 0; c < C; c++)
+                q[c] = qn[c];
+        }
+    }
+}
+
+// ------------------------------------------------------------ many keys
+constexpr int kManyC = 16;                 // channels per head
+constexpr int kManyD = kManyC * kHeads;    // 128
+constexpr int kManyRow = kManyD;           // 128 floats per staged key
+constexpr int kChunk = 32;                 // keys per staged chunk
+constexpr int kStages = 3;                 // staged chunks in flight
+constexpr int kLanes = 4;                  // key lanes per (query, head)
+constexpr int kPart = 2 + kManyC;          // m, l, o[16]
+constexpr int kManySmem = kStages * 2 * kChunk * kManyRow * 4;  // K and V rings
+
+// Position (in floats) of channels 4c..4c+3 of head h within a staged key
+// row: the 16-byte chunks of a head are rotated by h / 2, so the 8 heads a
+// warp reads at one c fall on 8 different 16-byte bank groups.
+__device__ __forceinline__ int many_pos(int h, int c4)
+{
+    return h * kManyC + (((c4 + (h >> 1)) & 3) << 2);
+}
+
+__global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
+    const float *__restrict__ Q, long sq, const float *__restrict__ K, long sk,
+    const float *__restrict__ V, long sv, float *__restrict__ part, int Nq, int Nk,
+    int keys_per_split, float scale)
+{
+    extern __shared__ float sm[];
+    float *ks = sm;                                     // [kStages][kChunk][kManyRow]
+    float *vs = sm + kStages * kChunk * kManyRow;       // [kStages][kChunk][kManyRow]
+    const int split = blockIdx.x, nsplit = gridDim.x;
+    const long p = blockIdx.y;
+    const int pair = threadIdx.x & 63, lane4 = threadIdx.x >> 6;
+    const int qi = blockIdx.z * 8 + (pair >> 3), h = pair & 7;
+    const bool live = qi < Nq;
+    const int k0 = split * keys_per_split;
+    const int k1 = min(Nk, k0 + keys_per_split);
+    const int nchunk = k1 > k0 ? (k1 - k0 + kChunk - 1) / kChunk : 0;
+    const float *kb = K + p * sk, *vb = V + p * sv;
+
+    // Chunk c of this split into buffer b: 16-byte pieces into padded rows.
+    auto stage = [&](int c, int b) {
+        const int j0 = k0 + c * kChunk, n = min(kChunk, k1 - j0);
+        for (int i = threadIdx.x; i < n * (kManyD / 4); i += blockDim.x) {
+            const int j = i / (kManyD / 4), col = (i - j * (kManyD / 4)) * 4;
+            const int dst = (b * kChunk + j) * kManyRow + many_pos(col / kManyC, (col % kManyC) / 4);
+            cp_async16(ks + dst, kb + (long)(j0 + j) * kManyD + col);
+            cp_async16(vs + dst, vb + (long)(j0 + j) * kManyD + col);
+        }
+        cp_async_commit();
+    };
+
+    float q[kManyC];
+    {
+        const int qq = live ? qi : 0;
+        const float4 *qp =
+            reinterpret_cast<const float4 *>(Q + p * sq + (long)qq * kManyD + h * kManyC);
+#pragma unroll
+        for (int c = 0; c < kManyC / 4; c++) {
+            const float4 v = __ldg(qp + c);
+            q[4 * c] = v.x * scale;
+            q[4 * c + 1] = v.y * scale;
+            q[4 * c + 2] = v.z * scale;
+            q[4 * c + 3] = v.w * scale;
+        }
+    }
+    float m = -INFINITY, l = 0.0f, o[kManyC];
+#pragma unroll
+    for (int c = 0; c < kManyC; c++)
+        o[c] = 0.0f;
+    // Ring of kStages chunks: chunks c+1 and c+2 load while c computes (an
+    // empty commit group keeps the wait count uniform at the tail).
+    for (int c = 0; c < kStages - 1; c++) {
+        if (c < nchunk)
+            stage(c, c);
+        else
+            cp_async_commit();
+    }
+    for (int c = 0; c < nchunk; c++) {
+        const int b = c % kStages;
+        if (c + kStages - 1 < nchunk)  // its buffer was released by the barrier below
+            stage(c + kStages - 1, (c + kStages - 1) % kStages);
+        else
+            cp_async_commit();
+        cp_async_wait<kStages - 1>();
+        __syncthreads();
+        const int n = min(kChunk, k1 - (k0 + c * kChunk));
+        // This lane's keys of the chunk, as one block: scores, block max,
+        // one correction, then P.V.
+        float s[kChunk / kLanes];
+        float bm = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < kChunk / kLanes; t++) {
+            const int j = t * kLanes + lane4;
+            float acc = -INFINITY;
+            if (j < n) {
+                const float *kr = ks + (b * kChunk + j) * kManyRow;
+                float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+                for (int cc = 0; cc < kManyC / 4; cc++) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + many_pos(h, cc));
+                    d0 = fmaf(q[4 * cc], k4.x, d0);
+                    d1 = fmaf(q[4 * cc + 1], k4.y, d1);
+                    d2 = fmaf(q[4 * cc + 2], k4.z, d2);
+                    d3 = fmaf(q[4 * cc + 3], k4.w, d3);
+                }
+                acc = (d0 + d1) + (d2 + d3);
+            }
+            s[t] = acc;
+            bm = fmaxf(bm, acc);
+        }
+        if (bm > -INFINITY) {
+            const float mn = fmaxf(m, bm), corr = __expf(m - mn);
+            l *= corr;
+#pragma unroll
+            for (int cc = 0; cc < kManyC; cc++)
+                o[cc] *= corr;
+#pragma unroll
+            for (int t = 0; t < kChunk / kLanes; t++) {
+                const int j = t * kLanes + lane4;
+                if (j < n) {
+                    const float e = __expf(s[t] - mn);
+                    l += e;
+                    const float *vr = vs + (b * kChunk + j) * kManyRow;
+#pragma unroll
+                    for (int cc = 0; cc < kManyC / 4; cc++) {
+                        const float4 v4 = *reinterpret_cast<const float4 *>(vr + many_pos(h, cc));
+                        o[4 * cc] = fmaf(e, v4.x, o[4 * cc]);
+                        o[4 * cc + 1] = fmaf(e, v4.y, o[4 * cc + 1]);
+                        o[4 * cc + 2] = fmaf(e, v4.z, o[4 * cc + 2]);
+                        o[4 * cc + 3] = fmaf(e, v4.w, o[4 * cc + 3]);
+                    }
+                }
+            }
+            m = mn;
+        }
+        __syncthreads();  // buffer b may be refilled from the next iteration on
+    }
+    // Merge the 4 key lanes of each pair (shared memory reused), then one
+    // partial per (query, head) of this split.
+    float *mer = sm;  // [kLanes][64][kPart]
+    float *mine = mer + (lane4 * 64 + pair) * kPart;
+    mine[0] = m;
+    mine[1] = l;
+#pragma unroll
+    for (int cc = 0; cc < kManyC; cc++)
+        mine[2 + cc] = o[cc];
+    __syncthreads();
+    if (lane4 == 0 && live) {
+        float M = -INFINITY;
+        for (int t = 0; t < kLanes; t++)
+            M = fmaxf(M, mer[(t * 64 + pair) * kPart]);
+        float L = 0.0f, acc[kManyC];
+#pragma unroll
+        for (int cc = 0; cc < kManyC; cc++)
+            acc[cc] = 0.0f;
+        for (int t = 0; t < kLanes; t++) {
+            const float *pt = mer + (t * 64 + pair) * kPart;
+            const float f = pt[0] == -INFINITY ? 0.0f : expf(pt[0] - M);
+            L += pt[1] * f;
+#pragma unroll
+            for (int cc = 0; cc < kManyC; cc++)
+                acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
+        }
+        float *dst = part + (((p * nsplit + split) * Nq + qi) * kHeads + h) * kPart;
+        dst[0] = M;
+        dst[1] = L;
+#pragma unroll
+        for (int cc = 0; cc < kManyC; cc++)
+            dst[2 + cc] = acc[cc];
+    }
+}
+
+// Combines the nsplit partials of each (prompt, query, head) into O.
+__global__ void mha_many_combine_kernel(const float *__restrict__ part, float *__restrict__ O,
+                                        int P, int Nq, int nsplit)
+{
+    const long g = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (p, qi, h)
+    if (g >= (long)P * Nq * kHeads)
+        return;
+    const int h = (int)(g % kHeads);
+    const int qi = (int)((g / kHeads) % Nq);
+    const long p = g / ((long)kHeads * Nq);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; s++)
+        M = fmaxf(M, part[(((p * nsplit + s) * Nq + qi) * kHeads + h) * kPart]);
+    float L = 0.0f, acc[kManyC];
+#pragma unroll
+    for (int cc = 0; cc < kManyC; cc++)
+        acc[cc] = 0.0f;
+    for (int s = 0; s < nsplit; s++) {
+        const float *pt = part + (((p * nsplit + s) * Nq + qi) * kHeads + h) * kPart;
+        const float f = pt[0] == -INFINITY ? 0.0f : expf(pt[0] - M);
+        L += pt[1] * f;
+#pragma unroll
+        for (int cc = 0; cc < kManyC; cc++)
+            acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
+    }
+    const float inv = 1.0f / L;
+    float4 *op = reinterpret_cast<float4 *>(O + (p * Nq + qi) * kManyD + h * kManyC);
+#pragma unroll
+    for (int cc = 0; cc < kManyC / 4; cc++)
+        op[cc] = make_float4(acc[4 * cc] * inv, acc[4 * cc + 1] * inv, acc[4 * cc + 2] * inv,
+                             acc[4 * cc + 3] * inv);
+}
+
+// Splits per prompt: as many CTAs as fit two per SM in one wave (rounding
+// up would start a second, mostly empty wave), at most one per 32 keys.
+int many_splits(int P, int Nk, int num_sms)
+{
+    const int want = 2 * num_sms / P;
+    const int cap = (Nk + kChunk - 1) / kChunk;
+    return want < 1 ? 1 : (want > cap ? cap : want);
+}
+
+template <int C>
+int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
+               const float *vp, long sv, float *o, float scale, cudaStream_t st)
+{
+    const int smem = 2 * Nk * kHeads * (C + 4) * 4;
+    auto kern = mha_few_kernel<C>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+        return (int)e;
+    dim3 grid((Nq + kFewQ - 1) / kFewQ, P);
+    kern<<<grid, 256, smem, st>>>(qp, sq, kp, sk, vp, sv, o, Nq, Nk, scale);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace sam3
+
+extern "C" size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms)
+{
+    if (Nk <= 64 || dint != sam3::kManyD || P <= 0 || Nq <= 0)
+        return 0;
+    return (size_t)P * sam3::many_splits(P, Nk, num_sms) * Nq * sam3::kHeads * sam3::kPart *
+           sizeof(float);
+}
+
+extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,
+                     long sk, const float *vp, long sv, float *o, void *ws, size_t ws_bytes,
+                     int num_sms, k_stream s)
+{
+    using namespace sam3;
+    const int c = dint / kHeads;
+    const float scale = 1.0f / sqrtf((float)c);
+    if (P <= 0 || Nq <= 0 || Nk <= 0 || dint % kHeads || ((uintptr_t)qp & 15) ||
+        ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
+        (sk & 3) || (sv & 3) || P > 65535)
+        return K_EARG;
+    cudaStream_t st = STREAM(s);
+    if (Nk > 64) {
+        // The reference rejects the same shape (sam3_model.c:429-430).
+        if (c != kManyC)
+            return K_EARG;
+        const int nsplit = many_splits(P, Nk, num_sms);
+        if (!ws || ws_bytes < k_mha_workspace(P, Nq, Nk, dint, num_sms))
+            return K_EARG;
+        cudaError_t e = cudaFuncSetAttribute(mha_many_split_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kManySmem);
+        if (e != cudaSuccess)
+            return (int)e;
+        const int per = ((Nk + nsplit - 1) / nsplit + kChunk - 1) / kChunk * kChunk;
+        dim3 grid(nsplit, P, (Nq + 7) / 8);
+        mha_many_split_kernel<<<grid, 256, kManySmem, st>>>(
+            qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), Nq, Nk, per, scale);
+        e = cudaGetLastError();
+        if (e != cudaSuccess)
+            return (int)e;
+        const long total = (long)P * Nq * kHeads;
+        mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
+            static_cast<const float *>(ws), o, P, Nq, nsplit);
+        return (int)cudaGetLastError();
+    }
+    if (c == 16)
+        return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, st);
+    if (c == 32)
+        return launch_few<32>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, st);
+    return K_EARG;
+}

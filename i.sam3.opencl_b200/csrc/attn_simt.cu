@@ -1,9 +1,9 @@
 // SPDX-License-Identifier: Unlicense
 // fp32 CUDA-core kernels: the backbone attention in reference precision
-// (the "fp32-reference mode" of the global-attention config), the mask
-// decoder's fused attention (attn_fewkeys / attn_manykeys,
-// sam3_kernels.cl:527-633) and the reference-contract batched GEMM used for
-// operands the tensor-core path does not take (sam3_kernels.cl:57-156).
+// (the "fp32-reference mode" of the global-attention config) and the
+// reference-contract batched GEMM used for operands the tensor-core path
+// does not take (sam3_kernels.cl:57-156). The mask decoder's attention is in
+// attn_decoder.cu.
 #include "kernels.h"
 
 #include <cuda_bf16.h>
@@ -11,12 +11,6 @@
 
 namespace sam3 {
 namespace {
-
-inline int grid_for(long n, int block)
-{
-    long g = (n + block - 1) / block;
-    return (int)(g < 1 ? 1 : (g > 0x7fffffffL ? 0x7fffffffL : g));
-}
 
 // ------------------------------------------------------ fp32 attention
 // One thread per query row (128 per CTA), K/V tiles of 32 keys staged in
@@ -99,146 +93,6 @@ __global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict_
         for (int d = 0; d < F_HD; d += 4)
             *reinterpret_cast<float4 *>(op + d) =
                 make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-    }
-}
-
-// ------------------------------------------------------ decoder attention
-// attn_fewkeys (sam3_kernels.cl:527-569): one thread per (prompt, query,
-// head) with the head index fastest so a warp reads whole query rows;
-// online softmax over Nk <= 64 keys, c = 16 or 32 channels per head.
-template <int CW>
-__global__ void mha_fewkeys_kernel(const float *__restrict__ Q, long sq,
-                                   const float *__restrict__ K, long sk,
-                                   const float *__restrict__ V, long sv, float *__restrict__ O,
-                                   int Nq, int Nk, int dint, float scale, long total)
-{
-    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= total)
-        return;
-    const int h = (int)(gid % 8);
-    const long pi = gid / 8;
-    const int i = (int)(pi % Nq);
-    const long p = pi / Nq;
-    const float *q = Q + p * sq + (long)i * dint + h * CW;
-    const float *kb = K + p * sk + h * CW;
-    const float *vb = V + p * sv + h * CW;
-    float qr[CW], o[CW];
-#pragma unroll
-    for (int c = 0; c < CW; c += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(q + c);
-        qr[c] = v.x;
-        qr[c + 1] = v.y;
-        qr[c + 2] = v.z;
-        qr[c + 3] = v.w;
-        o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.0f;
-    }
-    float m = -INFINITY, sum = 0.0f;
-    for (int j = 0; j < Nk; j++) {
-        const float *kj = kb + (long)j * dint;
-        const float *vj = vb + (long)j * dint;
-        float s = 0.0f;
-#pragma unroll
-        for (int c = 0; c < CW; c += 4) {
-            const float4 k4 = __ldg(reinterpret_cast<const float4 *>(kj + c));
-            s = fmaf(qr[c], k4.x, s);
-            s = fmaf(qr[c + 1], k4.y, s);
-            s = fmaf(qr[c + 2], k4.z, s);
-            s = fmaf(qr[c + 3], k4.w, s);
-        }
-        s *= scale;
-        const float mn = fmaxf(m, s), corr = expf(m - mn), e = expf(s - mn);
-        sum = sum * corr + e;
-#pragma unroll
-        for (int c = 0; c < CW; c += 4) {
-            const float4 v4 = __ldg(reinterpret_cast<const float4 *>(vj + c));
-            o[c] = o[c] * corr + e * v4.x;
-            o[c + 1] = o[c + 1] * corr + e * v4.y;
-            o[c + 2] = o[c + 2] * corr + e * v4.z;
-            o[c + 3] = o[c + 3] * corr + e * v4.w;
-        }
-        m = mn;
-    }
-    float *op = O + (p * Nq + i) * dint + h * CW;
-    const float inv = 1.0f / sum;
-#pragma unroll
-    for (int c = 0; c < CW; c += 4)
-        *reinterpret_cast<float4 *>(op + c) =
-            make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
-}
-
-// attn_manykeys (sam3_kernels.cl:577-633) for c = 16: one CTA per
-// (prompt, head) and all Nq (<= 8) queries of it, one warp per query;
-// lanes take every 32nd key with a private online softmax, then merge
-// across the warp. K/V of the (prompt, head) stream from HBM once and are
-// shared through L1 by the CTA's warps.
-__global__ void __launch_bounds__(256) mha_manykeys_kernel(
-    const float *__restrict__ Q, long sq, const float *__restrict__ K, long sk,
-    const float *__restrict__ V, long sv, float *__restrict__ O, int Nq, int Nk, int dint,
-    float scale)
-{
-    const int h = blockIdx.x % 8;
-    const long p = blockIdx.x / 8;
-    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float *kb = K + p * sk + h * 16;
-    const float *vb = V + p * sv + h * 16;
-    for (int i = wq; i < Nq; i += 8) {
-        const float *q = Q + p * sq + (long)i * dint + h * 16;
-        float qr[16], o[16];
-#pragma unroll
-        for (int c = 0; c < 16; c++) {
-            qr[c] = __ldg(q + c) * scale;
-            o[c] = 0.0f;
-        }
-        float m = -INFINITY, sum = 0.0f;
-        for (int j = lane; j < Nk; j += 32) {
-            const float4 *k4 = reinterpret_cast<const float4 *>(kb + (long)j * dint);
-            const float4 *v4 = reinterpret_cast<const float4 *>(vb + (long)j * dint);
-            float s = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float4 kk = __ldg(k4 + c);
-                s = fmaf(qr[4 * c], kk.x, s);
-                s = fmaf(qr[4 * c + 1], kk.y, s);
-                s = fmaf(qr[4 * c + 2], kk.z, s);
-                s = fmaf(qr[4 * c + 3], kk.w, s);
-            }
-            const float mn = fmaxf(m, s), corr = expf(m - mn), e = expf(s - mn);
-            sum = sum * corr + e;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float4 vv = __ldg(v4 + c);
-                o[4 * c] = o[4 * c] * corr + e * vv.x;
-                o[4 * c + 1] = o[4 * c + 1] * corr + e * vv.y;
-                o[4 * c + 2] = o[4 * c + 2] * corr + e * vv.z;
-                o[4 * c + 3] = o[4 * c + 3] * corr + e * vv.w;
-            }
-            m = mn;
-        }
-        float mall = m;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-            mall = fmaxf(mall, __shfl_xor_sync(0xffffffffu, mall, off));
-        const float f = (m == -INFINITY) ? 0.0f : expf(m - mall);
-        sum *= f;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-            sum += __shfl_xor_sync(0xffffffffu, sum, off);
-#pragma unroll
-        for (int c = 0; c < 16; c++) {
-            float v = o[c] * f;
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1)
-                v += __shfl_xor_sync(0xffffffffu, v, off);
-            o[c] = v;
-        }
-        if (lane < 16) {
-            float v = o[0];
-#pragma unroll
-            for (int c = 1; c < 16; c++)
-                if (lane == c)
-                    v = o[c];
-            O[(p * Nq + i) * dint + h * 16 + lane] = v / sum;
-        }
     }
 }
 
@@ -347,33 +201,6 @@ extern "C" int k_attn_f32(const float *qkv, int nseq, int N, int E, int heads, i
         return K_EARG;
     const long grid = (long)nseq * heads * ((N + F_BQ - 1) / F_BQ);
     attn_f32_kernel<<<(int)grid, F_BQ, 0, STREAM(s)>>>(qkv, nseq, N, E, heads, scale, out);
-    return (int)cudaGetLastError();
-}
-
-extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,
-                     long sk, const float *vp, long sv, float *o, k_stream s)
-{
-    const int c = dint / 8;
-    const float scale = 1.0f / sqrtf((float)c);
-    if (P <= 0 || Nq <= 0 || Nk <= 0 || dint % 8 || ((uintptr_t)qp & 15) || ((uintptr_t)kp & 15) ||
-        ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) || (sk & 3) || (sv & 3))
-        return K_EARG;
-    if (Nk > 64) {
-        if (c != 16)  // the reference rejects the same shape (sam3_model.c:429-430)
-            return K_EARG;
-        mha_manykeys_kernel<<<P * 8, 256, 0, STREAM(s)>>>(qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint,
-                                                          scale);
-        return (int)cudaGetLastError();
-    }
-    const long total = (long)P * Nq * 8;
-    if (c == 16)
-        mha_fewkeys_kernel<16><<<grid_for(total, 128), 128, 0, STREAM(s)>>>(
-            qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint, scale, total);
-    else if (c == 32)
-        mha_fewkeys_kernel<32><<<grid_for(total, 128), 128, 0, STREAM(s)>>>(
-            qp, sq, kp, sk, vp, sv, o, Nq, Nk, dint, scale, total);
-    else
-        return K_EARG;
     return (int)cudaGetLastError();
 }
 

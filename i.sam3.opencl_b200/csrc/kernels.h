@@ -91,10 +91,13 @@ int k_patch_im2col(const float *img, float *out, int side, int grid, int ps,
 int k_cast_f32_bf16(const float *x, void *y, long n, k_stream s);
 int k_cast_bf16_f32(const void *x, float *y, long n, k_stream s);
 
-/* Decoder attention (sam3_kernels.cl:527-633): 8 heads, scale 1/sqrt(c). */
+/* Decoder attention (sam3_kernels.cl:527-633): 8 heads, scale 1/sqrt(c).
+ * Nk > 64 (c = 16 only) splits the keys over CTAs and needs a device
+ * workspace of k_mha_workspace(...) bytes (0 otherwise). */
+size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms);
 int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
           const float *kp, long sk, const float *vp, long sv, float *o,
-          k_stream s);
+          void *ws, size_t ws_bytes, int num_sms, k_stream s);
 
 /* uint8 HWC tiles -> bf16 patch rows in window-major token order:
  * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight

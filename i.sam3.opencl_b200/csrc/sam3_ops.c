@@ -318,10 +318,17 @@ int cb_mha(cb_backend *b, int P, int Nq, int Nk, int dint, cb_mem qp,
     if (Nk > 64 && dint != 128)
         return cbi_fail(b, CB_EARG, "mha: unsupported shape");
     CB_TRY(cbi_enter(b));
-    return cbi_kstatus(b,
-                      k_mha(P, Nq, Nk, dint, (const float *)qp->ptr, (long)sq,
-                            (const float *)kp->ptr, (long)sk,
-                            (const float *)vp->ptr, (long)sv, (float *)o->ptr,
-                            (k_stream)b->stream),
-                      "mha");
+    {
+        const size_t wsb = k_mha_workspace(P, Nq, Nk, dint, b->num_sms);
+        void *ws = NULL;
+
+        if (wsb)
+            CB_TRY(cbi_scratch(b, wsb, &ws));
+        return cbi_kstatus(b,
+                          k_mha(P, Nq, Nk, dint, (const float *)qp->ptr, (long)sq,
+                                (const float *)kp->ptr, (long)sk,
+                                (const float *)vp->ptr, (long)sv, (float *)o->ptr, ws,
+                                wsb, b->num_sms, (k_stream)b->stream),
+                          "mha");
+    }
 }

@@ -326,6 +326,8 @@ def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
     ("t2i_shared", 64, 7, 5184, 128, True),
     ("i2t", 16, 5184, 8, 128, False),
     ("self7", 64, 7, 7, 256, False),
+    ("t2i_odd", 3, 11, 1000, 128, False),   # 2 query groups, ragged key splits
+    ("i2t_64keys", 2, 300, 64, 128, False),  # the few-keys limit, ragged query blocks
 ])
 def test_mha_vs_oracle(cb, sb, ob, name, P, Nq, Nk, dint, shared):
     q = ob.normal(SEED, 50, (P * Nq, dint))
