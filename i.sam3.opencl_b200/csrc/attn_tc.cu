@@ -8,19 +8,22 @@
 // Input: bf16 qkv rows [nseq * N, 3E] (RoPE already applied to q and k by
 // the QKV GEMM epilogue or by k_rope_cast_bf16), head h at column h*64.
 //
-// Work items are (sequence, head, pair of 128-query tiles); the two tiles
-// of an item share its K/V stream (KV tiles of 96 keys: 576 = 6 x 96,
-// 5184 = 54 x 96). When N / 128 rounds up to an odd count, the last item's
-// second tile lies beyond N: it runs through the tensor core but its softmax
-// work is skipped and nothing is stored. The kernel is persistent: CTA c
-// takes items c, c + grid, ... and streams their KV tiles back to back, so
-// the pipeline is filled once per CTA and the next item's Q and first
-// scores are loaded and computed while the current item finishes.
+// Work items are pairs of 128-query tiles ("slots"). Per sequence and head
+// the full tiles pair up (one K/V stream for both slots: 576 = 4.5 x 128 and
+// 5184 = 40.5 x 128 give 2 and 20 such pairs); the leftover tile of each
+// head (the 64-row tail here) pairs with the leftover of the next head, the
+// two slots then streaming their own K and V. KV tiles hold 96 keys (576 =
+// 6 x 96, 5184 = 54 x 96). Rows of a tail tile beyond N run through the
+// tensor core but their softmax work is skipped and nothing is stored. The
+// kernel is persistent: CTA c takes items c, c + grid, ... and streams their
+// KV tiles back to back, so the pipeline is filled once per CTA and the next
+// item's Q and first scores are loaded and computed while the current item
+// finishes.
 //
 //   warps 0-3  softmax of query tile 0, warps 4-7 of tile 1 (one thread per
 //              query row; warp w reads TMEM lanes 32*(w%4)...);
 //   warp 8     TMA producers: lane 0 loads Q (two buffers) and the K ring,
-//              lane 1 the V ring (three stages each);
+//              lane 1 the V ring (three stages of one or two tiles each);
 //   warp 9     TMEM owner and MMA issuer.
 //
 // Score tiles are numbered n = 2g + t (g: this CTA's KV tiles across items,
@@ -69,14 +72,16 @@ constexpr int kPolyPairsPer16 = 1;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int Q_BYTES = BQ * HD * 2;     // 16 KB per query tile
 constexpr int KV_BYTES = BKV * HD * 2;   // 12 KB per K or V tile
-constexpr int V_STAGE = 2 * KV_BYTES;    // V tile, then a tile of ones
-constexpr int OFF_Q = 0;                         // [buffer][tile]
+constexpr int K_STAGE = 2 * KV_BYTES;    // K of slot 0, K of slot 1
+constexpr int V_STAGE = 2 * KV_BYTES;    // V of slot 0, V of slot 1
+constexpr int OFF_Q = 0;                         // [buffer][slot]
 constexpr int OFF_K = OFF_Q + 4 * Q_BYTES;       // K ring
-constexpr int OFF_V = OFF_K + KST * KV_BYTES;    // V ring (+ ones)
-constexpr int OFF_BAR = OFF_V + KST * V_STAGE;
+constexpr int OFF_V = OFF_K + KST * K_STAGE;     // V ring
+constexpr int OFF_ONES = OFF_V + KST * V_STAGE;  // one tile of ones behind every V
+constexpr int OFF_BAR = OFF_ONES + KV_BYTES;
 constexpr uint32_t TM_O = NSB * BKV;             // first O column
-// q_full[2], q_empty[2], k_full[3], k_empty[3], v_full[3], v_empty[3],
-// s_full[3], p_ready[3], pv_full[2 tiles][2], drain. A waiter never finds
+// q_full[2], q_empty[2], k_full[KST], k_empty[KST], v_full[KST],
+// v_empty[KST], s_full[3], p_ready[3], pv_full[2 tiles][2], drain. A waiter never finds
 // one of them two phases ahead of the phase it waits for: score buffer i is
 // only refilled after P.V of its previous tile, which needs that tile's
 // p_ready; pv_full is split by KV-tile parity so that the phase before the
@@ -84,24 +89,65 @@ constexpr uint32_t TM_O = NSB * BKV;             // first O column
 constexpr int NBAR = 4 + 4 * KST + 3 * NSB + 4 + 1;
 constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;
 static_assert(SMEM_BYTES <= 232448, "attention smem");
-static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "alignment");
+static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_ONES % 1024 == 0 &&
+                  KV_BYTES % 1024 == 0 && OFF_ONES - OFF_V < (1 << 18),
+              "alignment, LBO range");
 static_assert(TM_O + 2 * NO <= 512, "tensor memory");
 static_assert(BKV % 32 == 0 && BKV <= 256, "KV tile");
 
 struct AttnArgs {
     int nseq, N, E, heads;
     int nitems;
+    // Work items per sequence: first the leftover tiles, with nleft == 2 per
+    // head (an odd full tile and the partial tail) one item per head, with
+    // nleft == 1 (only one of them) the leftover tiles of heads 2i and 2i+1,
+    // one item per pair of heads (the second slot empty for an odd head
+    // count); then heads * npf pairs of full 128-row tiles of one head.
+    int npf, nleft, left_tile, per_seq;
+    // Whether leftover tiles of different heads are paired (above), or each
+    // head's tiles pair as (2i, 2i+1) with an odd last tile alone: the first
+    // needs fewer, fuller items, which a long launch prefers; a launch of a
+    // few waves is balanced better by the second's lighter last items.
+    int pair_tails, nqt;
     float scale_log2;
     void *out;
     int *err;
 };
 
-__device__ __forceinline__ void item_coords(const AttnArgs &a, int npairs, int item, int &pair,
-                                            int &head, int &seq)
+// One query tile of an item: head, tile index within the sequence, and
+// whether the slot is empty.
+struct Slot {
+    int head, qt;
+    bool dead;
+};
+
+__device__ __forceinline__ void item_slots(const AttnArgs &a, int item, int &seq, Slot &s0,
+                                           Slot &s1)
 {
-    pair = item % npairs;
-    head = (item / npairs) % a.heads;
-    seq = item / (npairs * a.heads);
+    seq = item / a.per_seq;
+    int r = item - seq * a.per_seq;
+    if (!a.pair_tails) {  // tiles (2i, 2i+1) of one head; an odd last tile alone
+        const int npairs = a.per_seq / a.heads, h = r / npairs, pr = r - h * npairs;
+        s0 = Slot{h, 2 * pr, false};
+        s1 = Slot{h, 2 * pr + 1, 2 * pr + 1 >= a.nqt};
+        return;
+    }
+    const int left_items = a.per_seq - a.heads * a.npf;
+    if (r >= left_items) {  // leftover items first: a short launch ends on full pairs
+        r -= left_items;
+        const int h = r / a.npf, pr = r - h * a.npf;
+        s0 = Slot{h, 2 * pr, false};
+        s1 = Slot{h, 2 * pr + 1, false};
+    }
+    else if (a.nleft == 2) {
+        s0 = Slot{r, a.left_tile, false};
+        s1 = Slot{r, a.left_tile + 1, false};
+    }
+    else {
+        const int h1 = 2 * r + 1;
+        s0 = Slot{2 * r, a.left_tile, false};
+        s1 = h1 < a.heads ? Slot{h1, a.left_tile, false} : Slot{2 * r, a.left_tile, true};
+    }
 }
 
 template <bool OUT_BF16>
@@ -129,8 +175,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const int nqt = (a.N + BQ - 1) / BQ;
-    const int npairs = (nqt + 1) / 2;
     const int nkv = (a.N + BKV - 1) / BKV;
     // Items of this CTA and its total number of KV tiles.
     const int nmine = (int)blockIdx.x < a.nitems
@@ -159,15 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         fence_mbar_init();
     }
-    // The ones tiles behind the V stages (bf16 1.0 in both halves of every
-    // word; the swizzle of a constant tile is immaterial).
+    // The ones tile read as P.V's output columns 64-79 (bf16 1.0 in both
+    // halves of every word; the swizzle of a constant tile is immaterial).
     {
         const uint32_t one2 = 0x3F803F80u;
-        for (int i = threadIdx.x; i < KST * (KV_BYTES / 16); i += kThreads) {
-            const int st = i / (KV_BYTES / 16), c = i - st * (KV_BYTES / 16);
-            st_shared_v4(smem_addr(smem + OFF_V + st * V_STAGE + KV_BYTES + c * 16), one2, one2,
-                         one2, one2);
-        }
+        for (int i = threadIdx.x; i < KV_BYTES / 16; i += kThreads)
+            st_shared_v4(smem_addr(smem + OFF_ONES + i * 16), one2, one2, one2, one2);
         fence_proxy_async_smem();
     }
     if (warp == kMmaWarp) {
@@ -190,32 +231,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint64_t *full = is_k ? k_full : v_full;
             uint64_t *empty = is_k ? k_empty : v_empty;
             uint8_t *ring = smem + (is_k ? OFF_K : OFF_V);
-            const int stride = is_k ? KV_BYTES : V_STAGE;
+            const int stride = is_k ? K_STAGE : V_STAGE;
             int lastq = -1, lastg = -1;
             bool ok = true;
             int st = 0, use = 0;  // ring stage and use count of KV tile g
             for (int k = 0; k < nmine && ok; k++) {
-                int pair, head, seq;
-                item_coords(a, npairs, (int)blockIdx.x + k * (int)gridDim.x, pair, head, seq);
+                int seq;
+                Slot s0, s1;
+                item_slots(a, (int)blockIdx.x + k * (int)gridDim.x, seq, s0, s1);
                 const int row0 = seq * a.N;
+                // The two slots share one K/V stream when they are the same
+                // head (or the second is empty); else each has its own.
+                const bool shared = s0.head == s1.head;
                 if (is_k) {
                     // Q buffer k % 2 was last read by the S MMAs of item k-2.
                     if (!mbar_wait(&q_empty[k & 1], ((k >> 1) & 1) ^ 1, a.err, abort_flag))
                         break;
                     mbar_arrive_expect_tx(&q_full[k & 1], 2 * Q_BYTES);
-                    for (int t = 0; t < 2; t++)
-                        tma_load_2d(smem + OFF_Q + ((k & 1) * 2 + t) * Q_BYTES, &tmQ,
-                                    &q_full[k & 1], head * HD, row0 + (2 * pair + t) * BQ);
+                    tma_load_2d(smem + OFF_Q + ((k & 1) * 2) * Q_BYTES, &tmQ, &q_full[k & 1],
+                                s0.head * HD, row0 + s0.qt * BQ);
+                    tma_load_2d(smem + OFF_Q + ((k & 1) * 2 + 1) * Q_BYTES, &tmQ, &q_full[k & 1],
+                                s1.head * HD, row0 + s1.qt * BQ);
                     lastq = k;
                 }
-                const int col = (is_k ? a.E : 2 * a.E) + head * HD;
+                const int col0 = is_k ? a.E : 2 * a.E;
                 for (int j = 0; j < nkv; j++) {
                     if (!mbar_wait(&empty[st], (use & 1) ^ 1, a.err, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[st], KV_BYTES);
-                    tma_load_2d(ring + st * stride, &tmKV, &full[st], col, row0 + j * BKV);
+                    mbar_arrive_expect_tx(&full[st], shared ? KV_BYTES : 2 * KV_BYTES);
+                    tma_load_2d(ring + st * stride, &tmKV, &full[st], col0 + s0.head * HD,
+                                row0 + j * BKV);
+                    if (!shared)
+                        tma_load_2d(ring + st * stride + KV_BYTES, &tmKV, &full[st],
+                                    col0 + s1.head * HD, row0 + j * BKV);
                     lastg = k * nkv + j;
                     if (++st == KST) {
                         st = 0;
@@ -242,15 +292,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             // start-address field (shared addresses stay below 2^18, so the
             // 14-bit field never carries): K-major slices are 32 bytes apart,
             // V slices (MN-major, 16 keys) 2048 bytes.
+            // P.V's B operand is [V | ones]: the ones tile is the second
+            // N-group, LBO bytes from the V tile. A V tile d bytes into the
+            // ring moves the start-address field up and the LBO field down by
+            // d / 16 (both 14-bit fields stay in range: no carry, no borrow).
             const uint64_t dQ = sw128_desc(smem_addr(smem + OFF_Q), 16, 1024);
             const uint64_t dK = sw128_desc(smem_addr(smem + OFF_K), 16, 1024);
-            const uint64_t dV = sw128_desc(smem_addr(smem + OFF_V), KV_BYTES, 1024);
+            const uint64_t dV = sw128_desc(smem_addr(smem + OFF_V), OFF_ONES - OFF_V, 1024);
+            auto v_desc = [&](int d) -> uint64_t {
+                const uint64_t u = (uint64_t)(d >> 4);
+                return dV + u - (u << 16);
+            };
             const int nscore = 2 * total;
-            // The last item of a sequence with an odd tile count has its
-            // second tile beyond N: that tile gets no MMAs (its barriers are
-            // still committed).
-            auto pair_dead = [&](int k) -> bool {
-                return (nqt & 1) && ((int)blockIdx.x + k * (int)gridDim.x) % npairs == npairs - 1;
+            // Per item: whether the slots share one K/V stream, and whether
+            // the second slot is empty (no MMAs; its barriers are still
+            // committed).
+            auto item_kind = [&](int k, bool &shared, bool &dead1) {
+                int seq;
+                Slot s0, s1;
+                item_slots(a, (int)blockIdx.x + k * (int)gridDim.x, seq, s0, s1);
+                shared = s0.head == s1.head;
+                dead1 = s1.dead;
             };
             // Cursor over score tiles n = 2g + t, kept by increments (this one
             // thread issues every MMA; its instruction count is on the
@@ -260,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int kst, kph;  // K/V ring stage of g and its use parity
                 int gpar, j, k;
                 int buf, bph;  // score buffer n % 3 and its use parity
-                bool pdead, dead;
+                bool shared, dead1, dead;
             };
             auto advance = [&](Cursor &c) {
                 c.n++;
@@ -278,12 +340,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (++c.j == nkv) {
                         c.j = 0;
                         c.k++;
-                        c.pdead = pair_dead(c.k);
+                        if (c.k < nmine)
+                            item_kind(c.k, c.shared, c.dead1);
                     }
                 }
-                c.dead = c.t == 1 && c.pdead;
+                c.dead = c.t == 1 && c.dead1;
             };
-            const Cursor c0 = {0, 0, 0, 0, 0, 0, 0, 0, 0, pair_dead(0), false};
+            Cursor c0 = {0, 0, 0, 0, 0, 0, 0, 0, 0, true, false, false};
+            item_kind(0, c0.shared, c0.dead1);
             Cursor ahead = c0, cur = c0;
             // S(n) = Q_t(item k) K(g)^T into score buffer n % 3. The first S of
             // an item waits for its Q; the last one releases the Q buffer.
@@ -297,7 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!c.dead) {
                     const uint64_t qd = dQ + (uint64_t)((((c.k & 1) * 2 + c.t) * Q_BYTES) >> 4);
-                    const uint64_t kd = dK + (uint64_t)((c.kst * KV_BYTES) >> 4);
+                    const uint64_t kd =
+                        dK + (uint64_t)((c.kst * K_STAGE + (c.shared ? 0 : c.t) * KV_BYTES) >> 4);
                     const uint32_t dS = tmem_base + c.buf * BKV;
 #pragma unroll
                     for (int kq = 0; kq < HD / 16; kq++)
@@ -320,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return false;
                 tc_fence_after();
                 if (!c.dead) {
-                    const uint64_t vd = dV + (uint64_t)((c.kst * V_STAGE) >> 4);
+                    const uint64_t vd = v_desc(c.kst * V_STAGE + (c.shared ? 0 : c.t) * KV_BYTES);
                     const uint32_t dO = tmem_base + TM_O + c.t * NO;
                     const uint32_t aP = tmem_base + c.buf * BKV;
 #pragma unroll
@@ -363,12 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // by increments (n grows by 2 per KV tile).
         int buf = t, bph = 0;
         for (int k = 0; k < nmine && ok; k++) {
-            // Warps whose 32 query rows lie beyond N (the padding tile of an odd
-            // tile count, or the second half of a last 128-row tile) keep the
-            // barrier protocol but skip the softmax work; they store nothing.
-            const bool rows_live =
-                (2 * (((int)blockIdx.x + k * (int)gridDim.x) % npairs) + t) * BQ + quarter * 32 <
-                a.N;
+            // Warps whose 32 query rows lie beyond N (the second half of a
+            // partial tail tile) or in an empty slot keep the barrier protocol
+            // but skip the softmax work; they store nothing.
+            int seq;
+            Slot s0, s1;
+            item_slots(a, (int)blockIdx.x + k * (int)gridDim.x, seq, s0, s1);
+            const Slot me = t ? s1 : s0;
+            const bool rows_live = !me.dead && me.qt * BQ + quarter * 32 < a.N;
             float m_used = -INFINITY;
             for (int j = 0; j < nkv; j++) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&s_full[buf], bph, a.err, abort_flag));
@@ -497,8 +564,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
             }
             if (rows_live) {
-                int pair, head, seq;
-                item_coords(a, npairs, (int)blockIdx.x + k * (int)gridDim.x, pair, head, seq);
                 tc_fence_after();
                 uint32_t ov[64];
                 uint32_t lsum[16];
@@ -507,9 +572,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld16(tO + 64, lsum);
                 tmem_wait_ld();
                 const float inv = 1.0f / __uint_as_float(lsum[0]);
-                const int q = (2 * pair + t) * BQ + r;
+                const int q = me.qt * BQ + r;
                 if (q < a.N) {
-                    const long orow = (long)(seq * a.N + q) * a.E + head * HD;
+                    const long orow = (long)(seq * a.N + q) * a.E + me.head * HD;
                     if (OUT_BF16) {
                         uint4 *dst = reinterpret_cast<uint4 *>(
                             reinterpret_cast<__nv_bfloat16 *>(a.out) + orow);
@@ -592,8 +657,16 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = out;
     a.err = err;
-    const int nqt = (N + BQ - 1) / BQ;
-    const long nitems = (long)nseq * heads * ((nqt + 1) / 2);
+    const int full = N / BQ, tail = N % BQ != 0;
+    a.nqt = full + tail;
+    a.npf = full / 2;
+    a.nleft = (full & 1) + tail;
+    a.left_tile = 2 * a.npf;  // the first leftover tile (odd full tile, or the tail)
+    a.per_seq = heads * a.npf + (a.nleft == 2 ? heads : (a.nleft == 1 ? (heads + 1) / 2 : 0));
+    a.pair_tails = (long)nseq * a.per_seq >= 8L * sms;
+    if (!a.pair_tails)
+        a.per_seq = heads * ((a.nqt + 1) / 2);
+    const long nitems = (long)nseq * a.per_seq;
     if (nitems > 0x7fffffffL)
         return K_EARG;
     a.nitems = (int)nitems;
