@@ -17,9 +17,9 @@
 //   sam3_kernels.cl:577-633): the keys are split over `nsplit` CTAs per
 //   prompt so that every SM streams K/V (a prompt's K/V is 2.6 MB); a CTA
 //   (one split of one prompt, for 8 of its queries) pulls 32-key chunks of K
-//   and V with cp.async into a double buffer while its 256 threads (64
-//   (query, head) pairs x 4 key lanes) run the online softmax over the
-//   previous chunk, merges its 4 key lanes and writes one (m, l, o) partial
+//   and V with cp.async through a 3-stage ring while its 256 threads (64
+//   (query, head) pairs x 4 key lanes) run a blocked online softmax over the
+//   oldest chunk, merges its 4 key lanes and writes one (m, l, o) partial
 //   per pair; a second kernel combines the splits.
 //
 // The 8 different heads a warp reads at once fall on distinct shared-memory

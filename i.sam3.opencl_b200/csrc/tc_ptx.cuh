@@ -319,20 +319,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
     return d;
 }
 
-// The same for a 64-byte-swizzled K-major tile (rows of 64 bytes = 32 bf16;
-// 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3)): SBO = 512
-// (8 rows x 64 B), layout type SWIZZLE_64B.
-__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr)
-{
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;          // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(512 >> 4) << 32; // SBO
-    d |= (uint64_t)1 << 46;          // descriptor version (Blackwell)
-    d |= (uint64_t)4 << 61;          // SWIZZLE_64B
-    return d;
-}
-
 // Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B, fp32 D,
 // M x N tile, A/B K-major (0) or MN-major (1).
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn_major,
