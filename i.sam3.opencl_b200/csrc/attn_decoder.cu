@@ -6,21 +6,23 @@
 // with enough of them in flight:
 //
 //   few keys (Nk <= 64: image-to-token, token self-attention;
-//   attn_fewkeys, sam3_kernels.cl:527-569): one CTA per 256 queries of a
-//   prompt, that prompt's K and V (a few KB) staged once in shared memory,
-//   then 8 blocks of 32 queries, one thread per (query, head), the next
-//   block's query loaded while the current one computes; the 8 heads of a
-//   query sit in 8 adjacent threads (whole 512-byte rows per 8 threads);
-//   online softmax over the keys from shared memory;
+//   attn_fewkeys, sam3_kernels.cl:527-569): persistent CTAs, each taking a
+//   contiguous range of 32-query units (so a prompt's K and V, a few KB, are
+//   staged in shared memory once per CTA and prompt), one thread per
+//   (query, head), the next unit's query loaded while the current one
+//   computes; the 8 heads of a query sit in 8 adjacent threads (whole
+//   512-byte rows per 8 threads); softmax over the keys from shared memory
+//   (two passes for up to 8 keys, online beyond);
 //
 //   many keys (Nk > 64, c = 16: token-to-image; attn_manykeys,
 //   sam3_kernels.cl:577-633): the keys are split over `nsplit` CTAs per
 //   prompt so that every SM streams K/V (a prompt's K/V is 2.6 MB); a CTA
 //   (one split of one prompt, for 8 of its queries) pulls 32-key chunks of K
-//   and V with cp.async through a 3-stage ring while its 256 threads (64
-//   (query, head) pairs x 4 key lanes) run a blocked online softmax over the
-//   oldest chunk, merges its 4 key lanes and writes one (m, l, o) partial
-//   per pair; a second kernel combines the splits.
+//   and V with cp.async through a 3-stage ring while its 256 threads (32
+//   (query pair, head) items x 8 key lanes, each K/V read serving two
+//   queries) run a blocked online softmax over the oldest chunk, merges its
+//   key lanes and writes one (m, l, o) partial per (query, head); a second
+//   kernel combines the splits.
 //
 // The 8 different heads a warp reads at once fall on distinct shared-memory
 // bank groups: rows padded to c + 4 floats per head (few keys) or 16-byte
@@ -56,8 +58,7 @@ __device__ __forceinline__ void cp_async_wait()
 }
 
 // ------------------------------------------------------------ few keys
-constexpr int kFewBlocks = 8;             // blocks of 32 queries per CTA
-constexpr int kFewQ = 32 * kFewBlocks;    // queries per CTA (256 threads)
+constexpr int kFewSmall = 8;              // key counts up to this take two passes
 
 template <int C>
 __device__ __forceinline__ void load_q(const float *qp, float (&q)[C], float scale)
@@ -74,50 +75,110 @@ __device__ __forceinline__ void load_q(const float *qp, float (&q)[C], float sca
 }
 
 template <int C>
-__global__ void __launch_bounds__(256) mha_few_kernel(const float *__restrict__ Q, long sq,
+__global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const float *__restrict__ Q, long sq,
                                                       const float *__restrict__ K, long sk,
                                                       const float *__restrict__ V, long sv,
-                                                      float *__restrict__ O, int Nq, int Nk,
-                                                      float scale)
+                                                      float *__restrict__ O, int P, int Nq,
+                                                      int Nk, float scale)
 {
     constexpr int D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
     extern __shared__ float kv[];  // K rows then V rows, [Nk][8][CP] each
     float *ks = kv;
     float *vs = kv + Nk * ROW;
-    const long p = blockIdx.y;
-    const int h = threadIdx.x & 7;
-    const int q0 = blockIdx.x * kFewQ + (threadIdx.x >> 3);  // block b: q0 + 32 b
-    const float *qbase = Q + p * sq + h * C;
-
-    // The first block's query, then the prompt's K and V staged once for
-    // all blocks (float4 pieces into padded rows).
+    const int h = threadIdx.x & 7, qt = threadIdx.x >> 3;
+    // Units of 32 queries of one prompt; this CTA takes a contiguous range
+    // (mostly one prompt, so its K/V are staged once), sized so that all
+    // CTAs finish together.
+    const int nqb = (Nq + 31) / 32;
+    const long U = (long)P * nqb;
+    const long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
     float q[C];
-    if (q0 < Nq)
-        load_q<C>(qbase + (long)q0 * D, q, scale);
-    const float *kb = K + p * sk, *vb = V + p * sv;
-    for (int i = threadIdx.x; i < Nk * (D / 4); i += blockDim.x) {
-        const int j = i / (D / 4), col = (i - j * (D / 4)) * 4;
-        const int dst = j * ROW + (col / C) * CP + col % C;
-        *reinterpret_cast<float4 *>(ks + dst) =
-            __ldg(reinterpret_cast<const float4 *>(kb + (long)j * D + col));
-        *reinterpret_cast<float4 *>(vs + dst) =
-            __ldg(reinterpret_cast<const float4 *>(vb + (long)j * D + col));
+    if (u0 < u1) {
+        const long p = u0 / nqb;
+        const int qi = (int)(u0 - p * nqb) * 32 + qt;
+        if (qi < Nq)
+            load_q<C>(Q + p * sq + (long)qi * D + h * C, q, scale);
     }
-    __syncthreads();
+    long staged = -1;
 #pragma unroll 1
-    for (int b = 0; b < kFewBlocks; b++) {
-        const int qi = q0 + 32 * b;
-        if (qi >= Nq)
-            break;
-        // Next block's query in flight while this one computes.
+    for (long u = u0; u < u1; u++) {
+        const long p = u / nqb;
+        const int qi = (int)(u - p * nqb) * 32 + qt;
+        if (p != staged) {  // CTA-uniform: stage this prompt's K and V
+            __syncthreads();
+            const float *kb = K + p * sk, *vb = V + p * sv;
+            for (int i = threadIdx.x; i < Nk * (D / 4); i += blockDim.x) {
+                const int j = i / (D / 4), col = (i - j * (D / 4)) * 4;
+                const int dst = j * ROW + (col / C) * CP + col % C;
+                *reinterpret_cast<float4 *>(ks + dst) =
+                    __ldg(reinterpret_cast<const float4 *>(kb + (long)j * D + col));
+                *reinterpret_cast<float4 *>(vs + dst) =
+                    __ldg(reinterpret_cast<const float4 *>(vb + (long)j * D + col));
+            }
+            __syncthreads();
+            staged = p;
+        }
+        // The next unit's query in flight while this one computes.
         float qn[C];
-        const bool more = b + 1 < kFewBlocks && qi + 32 < Nq;
-        if (more)
-            load_q<C>(qbase + (long)(qi + 32) * D, qn, scale);
+        bool more = false;
+        if (u + 1 < u1) {
+            const long pn = (u + 1) / nqb;
+            const int qin = (int)(u + 1 - pn * nqb) * 32 + qt;
+            more = qin < Nq;
+            if (more)
+                load_q<C>(Q + pn * sq + (long)qin * D + h * C, qn, scale);
+        }
+        if (qi >= Nq) {
+            if (more)
+#pragma unroll
+                for (int c = 0; c < C; c++)
+                    q[c] = qn[c];
+            continue;
+        }
         float m = -INFINITY, l = 0.0f, o[C];
 #pragma unroll
         for (int c = 0; c < C; c++)
             o[c] = 0.0f;
+        if (Nk <= kFewSmall) {
+            // Two passes over at most 8 keys: independent scores, one
+            // maximum, then the exponentials and P.V without rescaling.
+            float sc[kFewSmall];
+#pragma unroll
+            for (int j = 0; j < kFewSmall; j++) {
+                sc[j] = -INFINITY;
+                if (j < Nk) {
+                    const float4 *kr = reinterpret_cast<const float4 *>(ks + j * ROW + h * CP);
+                    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < C / 4; c++) {
+                        const float4 k4 = kr[c];
+                        d0 = fmaf(q[4 * c], k4.x, d0);
+                        d1 = fmaf(q[4 * c + 1], k4.y, d1);
+                        d2 = fmaf(q[4 * c + 2], k4.z, d2);
+                        d3 = fmaf(q[4 * c + 3], k4.w, d3);
+                    }
+                    sc[j] = (d0 + d1) + (d2 + d3);
+                    m = fmaxf(m, sc[j]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kFewSmall; j++) {
+                if (j < Nk) {
+                    const float e = __expf(sc[j] - m);
+                    l += e;
+                    const float4 *vr = reinterpret_cast<const float4 *>(vs + j * ROW + h * CP);
+#pragma unroll
+                    for (int c = 0; c < C / 4; c++) {
+                        const float4 v4 = vr[c];
+                        o[4 * c] = fmaf(e, v4.x, o[4 * c]);
+                        o[4 * c + 1] = fmaf(e, v4.y, o[4 * c + 1]);
+                        o[4 * c + 2] = fmaf(e, v4.z, o[4 * c + 2]);
+                        o[4 * c + 3] = fmaf(e, v4.w, o[4 * c + 3]);
+                    }
+                }
+            }
+        }
+        else
         for (int j = 0; j < Nk; j++) {
             const float4 *kr = reinterpret_cast<const float4 *>(ks + j * ROW + h * CP);
             float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;  // four short chains
@@ -163,7 +224,7 @@ constexpr int kManyD = kManyC * kHeads;    // 128
 constexpr int kManyRow = kManyD;           // 128 floats per staged key
 constexpr int kChunk = 32;                 // keys per staged chunk
 constexpr int kStages = 3;                 // staged chunks in flight
-constexpr int kLanes = 4;                  // key lanes per (query, head)
+constexpr int kLanes = 8;                  // key lanes per (query, head)
 constexpr int kPart = 2 + kManyC;          // m, l, o[16]
 constexpr int kManySmem = kStages * 2 * kChunk * kManyRow * 4;  // K and V rings
 
@@ -185,15 +246,16 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
     float *vs = sm + kStages * kChunk * kManyRow;       // [kStages][kChunk][kManyRow]
     const int split = blockIdx.x, nsplit = gridDim.x;
     const long p = blockIdx.y;
-    const int pair = threadIdx.x & 63, lane4 = threadIdx.x >> 6;
-    const int qi = blockIdx.z * 8 + (pair >> 3), h = pair & 7;
-    const bool live = qi < Nq;
+    // Thread = (query pair, head, key lane): queries qg and qg + 4 of the
+    // CTA's 8 share every K/V read from shared memory; a warp is one key lane.
+    const int h = threadIdx.x & 7, qg = (threadIdx.x >> 3) & 3, lane = threadIdx.x >> 5;
+    const int qa = blockIdx.z * 8 + qg, qb = qa + 4;
     const int k0 = split * keys_per_split;
     const int k1 = min(Nk, k0 + keys_per_split);
     const int nchunk = k1 > k0 ? (k1 - k0 + kChunk - 1) / kChunk : 0;
     const float *kb = K + p * sk, *vb = V + p * sv;
 
-    // Chunk c of this split into buffer b: 16-byte pieces into padded rows.
+    // Chunk c of this split into buffer b: 16-byte pieces into rotated rows.
     auto stage = [&](int c, int b) {
         const int j0 = k0 + c * kChunk, n = min(kChunk, k1 - j0);
         for (int i = threadIdx.x; i < n * (kManyD / 4); i += blockDim.x) {
@@ -205,24 +267,25 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
         cp_async_commit();
     };
 
-    float q[kManyC];
-    {
-        const int qq = live ? qi : 0;
+    float q[2][kManyC];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int qq = (u ? qb : qa) < Nq ? (u ? qb : qa) : 0;
         const float4 *qp =
             reinterpret_cast<const float4 *>(Q + p * sq + (long)qq * kManyD + h * kManyC);
 #pragma unroll
         for (int c = 0; c < kManyC / 4; c++) {
             const float4 v = __ldg(qp + c);
-            q[4 * c] = v.x * scale;
-            q[4 * c + 1] = v.y * scale;
-            q[4 * c + 2] = v.z * scale;
-            q[4 * c + 3] = v.w * scale;
+            q[u][4 * c] = v.x * scale;
+            q[u][4 * c + 1] = v.y * scale;
+            q[u][4 * c + 2] = v.z * scale;
+            q[u][4 * c + 3] = v.w * scale;
         }
     }
-    float m = -INFINITY, l = 0.0f, o[kManyC];
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, o[2][kManyC];
 #pragma unroll
     for (int c = 0; c < kManyC; c++)
-        o[c] = 0.0f;
+        o[0][c] = o[1][c] = 0.0f;
     // Ring of kStages chunks: chunks c+1 and c+2 load while c computes (an
     // empty commit group keeps the wait count uniform at the tail).
     for (int c = 0; c < kStages - 1; c++) {
@@ -240,89 +303,115 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
         cp_async_wait<kStages - 1>();
         __syncthreads();
         const int n = min(kChunk, k1 - (k0 + c * kChunk));
-        // This lane's keys of the chunk, as one block: scores, block max,
-        // one correction, then P.V.
-        float s[kChunk / kLanes];
-        float bm = -INFINITY;
+        // This lane's keys of the chunk as one block per query: scores, block
+        // maximum, one correction, then P.V.
+        constexpr int KT = kChunk / kLanes;
+        float s[2][KT];
+        float bm[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int t = 0; t < kChunk / kLanes; t++) {
-            const int j = t * kLanes + lane4;
-            float acc = -INFINITY;
+        for (int t = 0; t < KT; t++) {
+            const int j = t * kLanes + lane;
+            s[0][t] = s[1][t] = -INFINITY;
             if (j < n) {
                 const float *kr = ks + (b * kChunk + j) * kManyRow;
-                float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+                float d[2][4] = {};
 #pragma unroll
                 for (int cc = 0; cc < kManyC / 4; cc++) {
                     const float4 k4 = *reinterpret_cast<const float4 *>(kr + many_pos(h, cc));
-                    d0 = fmaf(q[4 * cc], k4.x, d0);
-                    d1 = fmaf(q[4 * cc + 1], k4.y, d1);
-                    d2 = fmaf(q[4 * cc + 2], k4.z, d2);
-                    d3 = fmaf(q[4 * cc + 3], k4.w, d3);
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        d[u][0] = fmaf(q[u][4 * cc], k4.x, d[u][0]);
+                        d[u][1] = fmaf(q[u][4 * cc + 1], k4.y, d[u][1]);
+                        d[u][2] = fmaf(q[u][4 * cc + 2], k4.z, d[u][2]);
+                        d[u][3] = fmaf(q[u][4 * cc + 3], k4.w, d[u][3]);
+                    }
                 }
-                acc = (d0 + d1) + (d2 + d3);
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    s[u][t] = (d[u][0] + d[u][1]) + (d[u][2] + d[u][3]);
+                    bm[u] = fmaxf(bm[u], s[u][t]);
+                }
             }
-            s[t] = acc;
-            bm = fmaxf(bm, acc);
         }
-        if (bm > -INFINITY) {
-            const float mn = fmaxf(m, bm), corr = __expf(m - mn);
-            l *= corr;
+        if (bm[0] > -INFINITY) {  // the key count is the same for both queries
+            float e[2][KT];
 #pragma unroll
-            for (int cc = 0; cc < kManyC; cc++)
-                o[cc] *= corr;
+            for (int u = 0; u < 2; u++) {
+                const float mn = fmaxf(m[u], bm[u]), corr = __expf(m[u] - mn);
+                l[u] *= corr;
 #pragma unroll
-            for (int t = 0; t < kChunk / kLanes; t++) {
-                const int j = t * kLanes + lane4;
+                for (int cc = 0; cc < kManyC; cc++)
+                    o[u][cc] *= corr;
+#pragma unroll
+                for (int t = 0; t < KT; t++) {
+                    e[u][t] = __expf(s[u][t] - mn);  // 0 for keys past the chunk
+                    l[u] += e[u][t];
+                }
+                m[u] = mn;
+            }
+#pragma unroll
+            for (int t = 0; t < KT; t++) {
+                const int j = t * kLanes + lane;
                 if (j < n) {
-                    const float e = __expf(s[t] - mn);
-                    l += e;
                     const float *vr = vs + (b * kChunk + j) * kManyRow;
 #pragma unroll
                     for (int cc = 0; cc < kManyC / 4; cc++) {
                         const float4 v4 = *reinterpret_cast<const float4 *>(vr + many_pos(h, cc));
-                        o[4 * cc] = fmaf(e, v4.x, o[4 * cc]);
-                        o[4 * cc + 1] = fmaf(e, v4.y, o[4 * cc + 1]);
-                        o[4 * cc + 2] = fmaf(e, v4.z, o[4 * cc + 2]);
-                        o[4 * cc + 3] = fmaf(e, v4.w, o[4 * cc + 3]);
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            o[u][4 * cc] = fmaf(e[u][t], v4.x, o[u][4 * cc]);
+                            o[u][4 * cc + 1] = fmaf(e[u][t], v4.y, o[u][4 * cc + 1]);
+                            o[u][4 * cc + 2] = fmaf(e[u][t], v4.z, o[u][4 * cc + 2]);
+                            o[u][4 * cc + 3] = fmaf(e[u][t], v4.w, o[u][4 * cc + 3]);
+                        }
                     }
                 }
             }
-            m = mn;
         }
         __syncthreads();  // buffer b may be refilled from the next iteration on
     }
-    // Merge the 4 key lanes of each pair (shared memory reused), then one
-    // partial per (query, head) of this split.
-    float *mer = sm;  // [kLanes][64][kPart]
-    float *mine = mer + (lane4 * 64 + pair) * kPart;
-    mine[0] = m;
-    mine[1] = l;
+    // Merge the key lanes of each (query, head) (shared memory reused), then
+    // one partial per (query, head) of this split.
+    float *mer = sm;  // [kLanes][8 queries][8 heads][kPart]
 #pragma unroll
-    for (int cc = 0; cc < kManyC; cc++)
-        mine[2 + cc] = o[cc];
-    __syncthreads();
-    if (lane4 == 0 && live) {
-        float M = -INFINITY;
-        for (int t = 0; t < kLanes; t++)
-            M = fmaxf(M, mer[(t * 64 + pair) * kPart]);
-        float L = 0.0f, acc[kManyC];
+    for (int u = 0; u < 2; u++) {
+        float *mine = mer + ((lane * 8 + qg + 4 * u) * kHeads + h) * kPart;
+        mine[0] = m[u];
+        mine[1] = l[u];
 #pragma unroll
         for (int cc = 0; cc < kManyC; cc++)
-            acc[cc] = 0.0f;
-        for (int t = 0; t < kLanes; t++) {
-            const float *pt = mer + (t * 64 + pair) * kPart;
-            const float f = pt[0] == -INFINITY ? 0.0f : expf(pt[0] - M);
-            L += pt[1] * f;
+            mine[2 + cc] = o[u][cc];
+    }
+    __syncthreads();
+    if (lane == 0) {
+#pragma unroll 1
+        for (int u = 0; u < 2; u++) {
+            const int qi = u ? qb : qa;
+            if (qi >= Nq)
+                continue;
+            const int slot = (qg + 4 * u) * kHeads + h;
+            float M = -INFINITY;
+            for (int t = 0; t < kLanes; t++)
+                M = fmaxf(M, mer[(t * 64 + slot) * kPart]);
+            float L = 0.0f, acc[kManyC];
 #pragma unroll
             for (int cc = 0; cc < kManyC; cc++)
-                acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
-        }
-        float *dst = part + (((p * nsplit + split) * Nq + qi) * kHeads + h) * kPart;
-        dst[0] = M;
-        dst[1] = L;
+                acc[cc] = 0.0f;
+            for (int t = 0; t < kLanes; t++) {
+                const float *pt = mer + (t * 64 + slot) * kPart;
+                const float f = pt[0] == -INFINITY ? 0.0f : __expf(pt[0] - M);
+                L += pt[1] * f;
 #pragma unroll
-        for (int cc = 0; cc < kManyC; cc++)
-            dst[2 + cc] = acc[cc];
+                for (int cc = 0; cc < kManyC; cc++)
+                    acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
+            }
+            float *dst = part + (((p * nsplit + split) * Nq + qi) * kHeads + h) * kPart;
+            dst[0] = M;
+            dst[1] = L;
+#pragma unroll
+            for (int cc = 0; cc < kManyC; cc++)
+                dst[2 + cc] = acc[cc];
+        }
     }
 }
 
@@ -370,15 +459,21 @@ int many_splits(int P, int Nk, int num_sms)
 
 template <int C>
 int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
-               const float *vp, long sv, float *o, float scale, cudaStream_t st)
+               const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
 {
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess)
         return (int)e;
-    dim3 grid((Nq + kFewQ - 1) / kFewQ, P);
-    kern<<<grid, 256, smem, st>>>(qp, sq, kp, sk, vp, sv, o, Nq, Nk, scale);
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem);
+    if (e != cudaSuccess)
+        return (int)e;
+    const long units = (long)P * ((Nq + 31) / 32);
+    const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
+    kern<<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(qp, sq, kp, sk, vp, sv, o, P,
+                                                                    Nq, Nk, scale);
     return (int)cudaGetLastError();
 }
 
@@ -430,8 +525,8 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         return (int)cudaGetLastError();
     }
     if (c == 16)
-        return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, st);
+        return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     if (c == 32)
-        return launch_few<32>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, st);
+        return launch_few<32>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     return K_EARG;
 }
