@@ -299,6 +299,56 @@ def decoder_bench(cb, torch, pk, iters=10):
     return res
 
 
+MASK_P = 64  # prompts per decode (config 3: batches of 64)
+
+
+def mask_decoder_bench(sb, cb, torch, iters=5):
+    """The whole point-prompt decoder (cb_decode: prompt tokens from host
+    points, two-way transformer, output upscaling, heads, low-res logits,
+    IoU back to the host) on MASK_P prompts per call, synthetic image
+    features and random-init weights; device-timed with CUDA events on the
+    backend stream around each blocking call, plus one profiled call for the
+    per-kernel shares."""
+    stream = torch.cuda.ExternalStream(cb.stream)
+    dec = sb.Decoder(cb, MASK_P)
+    dec.init_random(SEED, 0.02)
+    T = 5184
+    feats = []
+    for k, n in enumerate((T * 256, 16 * T * 32, 4 * T * 64)):
+        m = cb.alloc(n * 4, sb.F32)
+        cb.synth_normal(SEED, 9216 + k, 0.0, 1.0, m, n)
+        feats.append(m)
+    dec.set_image(*feats)
+    rng = np.random.default_rng(SEED)
+    pts = rng.uniform(0, 1008, size=(MASK_P, 2)).astype(np.float32)
+    low = cb.alloc(MASK_P * 3 * 288 * 288 * 4, sb.F32)
+    times = []
+    for it in range(iters + 2):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.decode(pts, low)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 2:
+            times.append(e0.elapsed_time(e1))
+    cb.profile(True)
+    dec.decode(pts, low)
+    cb.profile(False)
+    prof = cb.profile_table()
+    dec.close()
+    t = statistics.median(times)
+    total = sum(v["ms"] for v in prof.values())
+    kernels = {k: {"share": v["ms"] / total, "launches": v["calls"],
+                   "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9,
+                   "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12 if v["flops"] else None}
+               for k, v in prof.items()}
+    return {"prompts": MASK_P, "ms_per_decode": t, "prompts_per_s": MASK_P / (t * 1e-3),
+            "kernels": kernels,
+            "work": "cb_decode: 64 one-point prompts on one 72 x 72 image embedding, "
+                    "lowres [64, 3, 288, 288] on the device, IoU to the host"}
+
+
 def cpu_configs_sample():
     """Configs 1-3 on the reference's kernels (oracle/_ref) on all host
     cores, rank 0 at N=1: C1 and C2 RoPE + QK^T gemm_cpu_t + softmax_rows +
@@ -339,6 +389,15 @@ def cpu_configs_sample():
                 best = (t, kind)
         out["config3_" + cname] = {"s": best[0], "gbs": nbytes / best[0] / 1e9,
                                    "kind": best[1]}
+    # the whole mask decoder, oracle restatement of sam_decode (its kernels are
+    # the reference's, pinned bit-exact), 2 prompts
+    w = ob.DecoderWeights(SEED, 0.02)
+    img = ob.decoder_image(SEED)
+    pts = np.array([[100.0, 200.0], [700.0, 800.0]], np.float32)
+    t0 = time.perf_counter()
+    ob.sam_decode(w, *img, pts)
+    t = time.perf_counter() - t0
+    out["mask_decoder_2_prompts"] = {"s": t, "prompts_per_s": 2 / t, "kind": "port"}
     return out
 
 
@@ -432,6 +491,7 @@ def our_arm(args, world, rank, local, pg):
                        "launches": v["calls"]} for k, v in prof.items()}
         attn = attention_bench(sb, cb, torch, pk)
         dec = decoder_bench(cb, torch, pk)
+        mdec = mask_decoder_bench(sb, cb, torch)
         line = {
             "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -450,6 +510,7 @@ def our_arm(args, world, rank, local, pg):
             "kernels": kernels,
             "attention": attn,
             "decoder_attention": dec,
+            "mask_decoder": mdec,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
                     "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
                     "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},

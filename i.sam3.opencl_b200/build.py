@@ -20,8 +20,9 @@ LIB = os.path.join(HERE, "libsam3cuda.so")
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA, "bin", "nvcc")
 
-CU = ["gemm_tc.cu", "attn_tc.cu", "attn_simt.cu", "attn_decoder.cu", "elementwise.cu", "attn_noalloc.cu"]
-C = ["cuda_backend.c", "sam3_ops.c", "sam3_encoder.c", "synth.c"]
+CU = ["gemm_tc.cu", "attn_tc.cu", "attn_simt.cu", "attn_decoder.cu", "elementwise.cu", "attn_noalloc.cu",
+      "decoder.cu"]
+C = ["cuda_backend.c", "sam3_ops.c", "sam3_encoder.c", "sam3_decoder.c", "synth.c"]
 HEADERS = ["tc_ptx.cuh", "tmap.cuh", "kernels.h", "backend_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

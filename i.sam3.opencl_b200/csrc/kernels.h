@@ -99,6 +99,28 @@ int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
           const float *kp, long sk, const float *vp, long sv, float *o,
           void *ws, size_t ws_bytes, int num_sms, k_stream s);
 
+/* Mask decoder (decoder.cu). convt_scatter: G [P*H*W, Co*4] (16-byte
+ * aligned) -> out [P, 2H, 2W, Co], + bias, + add (shared, may be NULL),
+ * act. mask_logits: U [P, npix, 32], hyper [P, 96] -> out [P, 3, npix].
+ * dec_heads: hypernetwork MLPs w/b[0..2] on token rows 3..5 and the IoU
+ * head w/b[3] on row 1 of tok [P, 8, 256] -> hyper [P, 96], iou [P, 3]
+ * (sigmoid). transpose_cast: fp32 [rows, cols] -> bf16 [cols, rows]. */
+int k_convt_scatter(const float *G, float *out, const float *bias,
+                    const float *add, int P, int H, int W, int Co, int act,
+                    k_stream s);
+int k_mask_logits(const float *U, const float *hyper, float *out, int P,
+                  int npix, k_stream s);
+struct k_dec_heads_w {
+    const float *w[4][3], *b[4][3];
+};
+int k_dec_heads(const float *tok, int P, const struct k_dec_heads_w *hw,
+                float *hyper, float *iou, k_stream s);
+/* out = bf16(x[i] + a[i % amod]), i < n. */
+int k_add_cast_bf16(const float *x, const float *a, long n, long amod,
+                    void *out, k_stream s);
+int k_transpose_cast_bf16(const float *src, int rows, int cols, void *dst,
+                          k_stream s);
+
 /* uint8 HWC tiles -> bf16 patch rows in window-major token order:
  * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight
  * order), value (u/255 - 0.5)/0.5 (image.c:360-366), zero for columns >= 3

@@ -1,0 +1,660 @@
+/* SPDX-License-Identifier: Unlicense */
+/* The point-prompt mask decoder (sam3_model.c: load_decoder :656-755,
+ * decoder caches :877-902 and :1153-1170, pe_encode :760-773, sam_decode
+ * :1239-1399) on the B200 kernels of this library.
+ *
+ * Data flow and precision. The token stream (P * 8 rows of 256) and the
+ * per-prompt image stream ("keys", P * 5184 rows of 256) stay fp32, as in
+ * the reference; every Linear runs on the tcgen05 GEMM with bf16 operands
+ * and fp32 accumulation, its fp32 input rounded to bf16 once (fused with
+ * the positional-encoding add where the reference adds one first). The
+ * decoder attention (k_mha) reads fp32 Q/K/V. Fusions against the
+ * reference's op sequence:
+ *   - keys = Linear(bo) + src: the add_bcast of src (shared by all
+ *     prompts) is the GEMM epilogue's residual with row m % 5184;
+ *   - the LayerNorm2d + GELU of the output upscaling writes bf16, the
+ *     operand of the next ConvTranspose GEMM;
+ *   - the ConvTranspose weights are stored as [cout * 4, cin] bf16, so both
+ *     upscaling GEMMs are plain tcgen05 GEMMs followed by the scatter;
+ *   - the hypernetwork and IoU MLPs run on the device (dec_heads), so the
+ *     decode does not stop for a host round trip before mask_logits.
+ * Everything runs on the backend stream; cb_decode blocks only to return
+ * the IoU predictions. */
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "backend_internal.h"
+#include "sam3_synth.h"
+
+#define DEC_GRID 72
+#define DEC_T (DEC_GRID * DEC_GRID)
+#define DEC_DIM 256
+#define DEC_NTOK 8
+#define DEC_IMG 1008
+#define DEC_LOWRES 288
+#define DEC_EPS 1e-5f
+#define LN2D_EPS 1e-6f
+
+/* Tensors that are GEMM weights (stored bf16 on the device). */
+static int is_gemm_weight(int i)
+{
+    int r, c, k;
+
+    if (i == SAM3_DT_UP0_W || i == SAM3_DT_UP3_W)
+        return 1;
+    if (i >= SAM3_DT_NF_W)
+        return 0;
+    sam3_dec_tensor(i, &r, &c, &k);
+    return k == SAM3_INIT_W;
+}
+
+/* Tensors the host needs (prompt encoding, token setup). */
+static int is_host_tensor(int i)
+{
+    return i >= SAM3_DT_GAUSS;
+}
+
+struct cb_decoder {
+    cb_backend *b;
+    int batch;
+    void *w[SAM3_DT_COUNT];     /* device: bf16 [out, in] GEMM weights, else fp32 */
+    float *hw[SAM3_DT_COUNT];   /* host copies of the prompt-side tensors */
+    int have_image;
+    /* image-side state (sam_encode's decoder caches) */
+    float *src, *srcpe, *pe_img, *kp0, *vp0, *qp0, *feat_s0, *feat_s1;
+    /* token stream [batch * 8, 256] and its scratch */
+    float *qpe, *qry, *qin, *sq, *sk, *sv, *so, *sh;
+    void *tok_bf16;             /* bf16 [batch * 8, 2048] GEMM operand */
+    /* per-prompt image stream */
+    float *keys;                /* [batch * T, 256] */
+    void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
+    float *bq, *bk, *bv, *bo;   /* [batch * T, 128] */
+    void *bo_bf16;              /* bf16 [batch * T, 128] */
+    float *G;                   /* [batch * T, 256], first ConvT GEMM */
+    float *u1;                  /* [batch * 4T, 64] */
+    void *u1_bf16;
+    float *g2;                  /* [batch * 4T, 128] */
+    float *u2;                  /* [batch * 16T, 32] */
+    float *hyper, *iou;         /* [batch, 96], [batch, 3] */
+    void *mha_ws;
+    size_t mha_ws_bytes;
+    float *h_tok;               /* host [batch * 8, 256] */
+};
+
+static int dalloc(cb_decoder *d, void **p, size_t bytes)
+{
+    if (cudaMalloc(p, bytes ? bytes : 16) != cudaSuccess) {
+        *p = NULL;
+        return cbi_fail(d->b, CB_EALLOC, "decoder buffers");
+    }
+    return CB_OK;
+}
+
+void cb_decoder_free(cb_decoder *d)
+{
+    int i;
+
+    if (!d)
+        return;
+    cbi_enter(d->b);
+    cudaStreamSynchronize(d->b->stream);
+    for (i = 0; i < SAM3_DT_COUNT; i++) {
+        cudaFree(d->w[i]);
+        free(d->hw[i]);
+    }
+    {
+        void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
+                       d->feat_s1, d->qpe, d->qry, d->qin, d->sq, d->sk, d->sv, d->so,
+                       d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
+                       d->bv, d->bo, d->bo_bf16, d->G, d->u1, d->u1_bf16, d->g2, d->u2,
+                       d->hyper, d->iou, d->mha_ws};
+
+        for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
+            cudaFree(dev[i]);
+    }
+    free(d->h_tok);
+    free(d);
+}
+
+int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
+{
+    cb_decoder *d;
+    const size_t T = DEC_T, B = (size_t)batch, nt = B * DEC_NTOK;
+    size_t ws_t2i, ws_i2t;
+    int i, rc = CB_OK;
+
+    if (!b || !out)
+        return CB_EARG;
+    *out = NULL;
+    if (batch <= 0 || batch > 1024)
+        return cbi_fail(b, CB_EARG, "decoder batch");
+    CB_TRY(cbi_enter(b));
+    d = calloc(1, sizeof(*d));
+    if (!d)
+        return CB_EALLOC;
+    d->b = b;
+    d->batch = batch;
+#define A(p, n) \
+    if (rc == CB_OK) rc = dalloc(d, (void **)&(p), (n))
+    for (i = 0; i < SAM3_DT_COUNT; i++) {
+        int r, c, k;
+
+        sam3_dec_tensor(i, &r, &c, &k);
+        A(d->w[i], (size_t)r * c * (is_gemm_weight(i) ? 2 : 4));
+        if (rc == CB_OK && is_host_tensor(i)) {
+            d->hw[i] = calloc((size_t)r * c, sizeof(float));
+            if (!d->hw[i])
+                rc = CB_EALLOC;
+        }
+    }
+    A(d->src, T * DEC_DIM * 4);
+    A(d->srcpe, T * DEC_DIM * 4);
+    A(d->pe_img, T * DEC_DIM * 4);
+    A(d->kp0, T * 128 * 4);
+    A(d->vp0, T * 128 * 4);
+    A(d->qp0, T * 128 * 4);
+    A(d->feat_s0, 16 * T * 32 * 4);
+    A(d->feat_s1, 4 * T * 64 * 4);
+    A(d->qpe, nt * DEC_DIM * 4);
+    A(d->qry, nt * DEC_DIM * 4);
+    A(d->qin, nt * DEC_DIM * 4);
+    A(d->sq, nt * DEC_DIM * 4);
+    A(d->sk, nt * DEC_DIM * 4);
+    A(d->sv, nt * DEC_DIM * 4);
+    A(d->so, nt * DEC_DIM * 4);
+    A(d->sh, nt * 2048 * 4);
+    A(d->tok_bf16, nt * 2048 * 2);
+    A(d->keys, B * T * DEC_DIM * 4);
+    A(d->keys_bf16, B * T * DEC_DIM * 2);
+    A(d->kin_bf16, B * T * DEC_DIM * 2);
+    A(d->bq, B * T * 128 * 4);
+    A(d->bk, B * T * 128 * 4);
+    A(d->bv, B * T * 128 * 4);
+    A(d->bo, B * T * 128 * 4);
+    A(d->bo_bf16, B * T * 128 * 2);
+    A(d->G, B * T * 256 * 4);
+    A(d->u1, B * 4 * T * 64 * 4);
+    A(d->u1_bf16, B * 4 * T * 64 * 2);
+    A(d->g2, B * 4 * T * 128 * 4);
+    A(d->u2, B * 16 * T * 32 * 4);
+    A(d->hyper, B * 96 * 4);
+    A(d->iou, B * 3 * 4);
+    ws_t2i = k_mha_workspace(batch, DEC_NTOK, DEC_T, 128, b->num_sms);
+    ws_i2t = k_mha_workspace(batch, DEC_T, DEC_NTOK, 128, b->num_sms);
+    d->mha_ws_bytes = ws_t2i > ws_i2t ? ws_t2i : ws_i2t;
+    A(d->mha_ws, d->mha_ws_bytes);
+#undef A
+    if (rc == CB_OK) {
+        d->h_tok = malloc(nt * DEC_DIM * sizeof(float));
+        if (!d->h_tok)
+            rc = CB_EALLOC;
+    }
+    if (rc != CB_OK) {
+        cb_decoder_free(d);
+        return rc;
+    }
+    *out = d;
+    return CB_OK;
+}
+
+/* ---------------------------------------------------------------- weights */
+
+/* One launch bracketed by the profiler, its result mapped to a status. */
+#define LAUNCH(name, flops, bytes, call)                                       \
+    do {                                                                       \
+        int lrc_;                                                              \
+        cbi_prof_begin(b, name, (double)(flops), (double)(bytes));             \
+        lrc_ = (call);                                                         \
+        cbi_prof_end(b);                                                       \
+        CB_TRY(cbi_kstatus(b, lrc_, name));                                    \
+    } while (0)
+
+/* PositionEmbeddingRandom of normalised (x, y) (pe_encode,
+ * sam3_model.c:760-773): 128 sines then 128 cosines of
+ * 2 pi (x' g[i] + y' g[128 + i]), x' = 2x - 1, y' = 2y - 1. */
+static void pe_encode(const float *gauss, float x, float y, float *out)
+{
+    int i;
+
+    x = 2.0f * x - 1.0f;
+    y = 2.0f * y - 1.0f;
+    for (i = 0; i < DEC_DIM / 2; i++) {
+        float v = x * gauss[i] + y * gauss[DEC_DIM / 2 + i];
+
+        v *= 2.0f * (float)M_PI;
+        out[i] = sinf(v);
+        out[DEC_DIM / 2 + i] = cosf(v);
+    }
+}
+
+/* Dense positional encoding of the 72 x 72 grid (sam3_model.c:886-892). */
+static int compute_pe_img(cb_decoder *d)
+{
+    cb_backend *b = d->b;
+    float *pe = malloc((size_t)DEC_T * DEC_DIM * sizeof(float));
+    int x, y, rc;
+
+    if (!pe)
+        return CB_EALLOC;
+    for (y = 0; y < DEC_GRID; y++)
+        for (x = 0; x < DEC_GRID; x++)
+            pe_encode(d->hw[SAM3_DT_GAUSS], (x + 0.5f) / DEC_GRID, (y + 0.5f) / DEC_GRID,
+                      pe + ((size_t)y * DEC_GRID + x) * DEC_DIM);
+    rc = cbi_kstatus(b,
+                     (int)cudaMemcpyAsync(d->pe_img, pe, (size_t)DEC_T * DEC_DIM * 4,
+                                          cudaMemcpyHostToDevice, b->stream),
+                     "decoder pe");
+    if (rc == CB_OK)
+        rc = cbi_kstatus(b, (int)cudaStreamSynchronize(b->stream), "decoder pe");
+    free(pe);
+    return rc;
+}
+
+/* Device copy of tensor i from fp32 values already on the device (rows x
+ * cols in the checkpoint layout): bf16 for GEMM weights (the ConvTranspose
+ * ones transposed to [cout * 4, cin]), fp32 otherwise. */
+static int store_tensor(cb_decoder *d, int i, const float *f32)
+{
+    cb_backend *b = d->b;
+    const k_stream st = (k_stream)b->stream;
+    int r, c, k;
+
+    sam3_dec_tensor(i, &r, &c, &k);
+    if (i == SAM3_DT_UP0_W || i == SAM3_DT_UP3_W)
+        return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, d->w[i], st), "decoder weights");
+    if (is_gemm_weight(i))
+        return cbi_kstatus(b, k_cast_f32_bf16(f32, d->w[i], (long)r * c, st), "decoder weights");
+    return cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(d->w[i], f32, (size_t)r * c * 4,
+                                            cudaMemcpyDeviceToDevice, b->stream),
+                       "decoder weights");
+}
+
+static void init_params(int kind, float std, float *mean, float *sd)
+{
+    *mean = kind == SAM3_INIT_LNW ? 1.0f : 0.0f;
+    *sd = kind == SAM3_INIT_EMB ? 1.0f
+          : (kind == SAM3_INIT_LNW || kind == SAM3_INIT_LNB) ? 0.1f : std;
+}
+
+int cb_decoder_init_random(cb_decoder *d, uint64_t seed, float std)
+{
+    cb_backend *b;
+    void *s = NULL;
+    int i;
+
+    if (!d)
+        return CB_EARG;
+    b = d->b;
+    CB_TRY(cbi_enter(b));
+    CB_TRY(cbi_scratch(b, (size_t)2048 * 256 * 4, &s));
+    for (i = 0; i < SAM3_DT_COUNT; i++) {
+        int r, c, k;
+        float mean, sd;
+
+        sam3_dec_tensor(i, &r, &c, &k);
+        init_params(k, std, &mean, &sd);
+        CB_TRY(cbi_kstatus(b,
+                           k_synth_normal(seed, SAM3_STREAM_DECW + (uint64_t)i, (long)r * c,
+                                          mean, sd, s, 0, (k_stream)b->stream),
+                           "decoder init"));
+        CB_TRY(store_tensor(d, i, (const float *)s));
+        if (d->hw[i])
+            sam3_synth_normal(seed, SAM3_STREAM_DECW + (uint64_t)i, (size_t)r * c, mean, sd,
+                              d->hw[i]);
+        /* the scratch buffer is reused by the next tensor */
+        CB_TRY(cbi_kstatus(b, (int)cudaStreamSynchronize(b->stream), "decoder init"));
+    }
+    d->have_image = 0;
+    return compute_pe_img(d);
+}
+
+int cb_decoder_set_weight(cb_decoder *d, int which, const float *src, size_t count)
+{
+    cb_backend *b;
+    void *s = NULL;
+    int r, c, k;
+
+    if (!d || !src)
+        return CB_EARG;
+    b = d->b;
+    if (which < 0 || which >= SAM3_DT_COUNT)
+        return cbi_fail(b, CB_EARG, "decoder set_weight: tensor");
+    sam3_dec_tensor(which, &r, &c, &k);
+    if (count != (size_t)r * c)
+        return cbi_fail(b, CB_EARG, "decoder set_weight: shape");
+    CB_TRY(cbi_enter(b));
+    CB_TRY(cbi_scratch(b, count * 4, &s));
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(s, src, count * 4, cudaMemcpyHostToDevice,
+                                            b->stream),
+                       "decoder set_weight"));
+    CB_TRY(store_tensor(d, which, (const float *)s));
+    CB_TRY(cbi_kstatus(b, (int)cudaStreamSynchronize(b->stream), "decoder set_weight"));
+    if (d->hw[which])
+        memcpy(d->hw[which], src, count * 4);
+    d->have_image = 0;
+    if (which == SAM3_DT_GAUSS)
+        return compute_pe_img(d);
+    return CB_OK;
+}
+
+/* ---------------------------------------------------------------- layers */
+
+/* Y[rows, out] = act(Xb W^T + bias) (+ R[m % rmod] when R): Xb bf16
+ * [rows, in], W bf16 [out, in], Y fp32. */
+static int lin16(cb_decoder *d, const char *name, const void *Xb, long rows, int in, int out,
+                 int wi, int bi, float *Y, const float *R, int rmod, int act)
+{
+    cb_backend *b = d->b;
+    const double dr = (double)rows;
+
+    LAUNCH(name, 2.0 * dr * in * out,
+           dr * in * 2 + (double)in * out * 2 + dr * out * 4 * (R ? 2 : 1),
+           k_gemm_bf16_tc((int)rows, out, in, Xb, in, d->w[wi], in, Y, out, 0,
+                          bi >= 0 ? (const float *)d->w[bi] : NULL, R, out, rmod, 1.0f, act,
+                          NULL, b->d_err, b->num_sms, (k_stream)b->stream));
+    return CB_OK;
+}
+
+/* The same on an fp32 X, rounded to bf16 into xs first. */
+static int lin32(cb_decoder *d, const char *name, const float *X, void *xs, long rows, int in,
+                 int out, int wi, int bi, float *Y, const float *R, int rmod, int act)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_cast", 0, (double)rows * in * 6,
+           k_cast_f32_bf16(X, xs, rows * in, (k_stream)b->stream));
+    return lin16(d, name, xs, rows, in, out, wi, bi, Y, R, rmod, act);
+}
+
+/* xs = bf16(X + A[i % amod]): the positional-encoding add fused with the
+ * cast of a GEMM operand. */
+static int add_cast(cb_decoder *d, const float *X, const float *A, long n, long amod, void *xs)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_add_cast", (double)n, (double)n * 10,
+           k_add_cast_bf16(X, A, n, amod, xs, (k_stream)b->stream));
+    return CB_OK;
+}
+
+static int ln(cb_decoder *d, float *X, void *Y, int y_bf16, long rows, int C, int wi, int bi,
+              float eps, int act)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_layernorm", 8.0 * rows * C, (double)rows * C * (y_bf16 ? 6 : 8),
+           k_layernorm(X, Y, y_bf16, (const float *)d->w[wi], (const float *)d->w[bi], rows, C,
+                       eps, act, (k_stream)b->stream));
+    return CB_OK;
+}
+
+static int add(cb_decoder *d, float *out, const float *a, const float *bb, long n, long bmod)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_add", (double)n, (double)n * 12,
+           k_add_bcast(out, a, bb, n, bmod, (k_stream)b->stream));
+    return CB_OK;
+}
+
+static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, long sq,
+               const float *k, long sk, const float *v, long sv, float *o)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH(Nk > 64 ? "dec_mha_t2i" : (Nq > 64 ? "dec_mha_i2t" : "dec_mha_self"),
+           4.0 * P * Nq * (double)Nk * dint,
+           4.0 * ((double)P * Nq * dint * 2 + (sk ? (double)P : 1.0) * Nk * dint * 2),
+           k_mha(P, Nq, Nk, dint, q, sq, k, sk, v, sv, o, d->mha_ws, d->mha_ws_bytes,
+                 b->num_sms, (k_stream)b->stream));
+    return CB_OK;
+}
+
+#define ATT(blk, t) (SAM3_DT_ATTN + 8 * (blk) + (t))
+#define LAY(l, t) (SAM3_DT_LAYER + 12 * (l) + (t))
+enum { QW = 0, QB, KW, KB, VW, VB, OW, OB };
+enum { N1W = 0, N1B, N2W, N2B, N3W, N3B, N4W, N4B, M1W, M1B, M2W, M2B };
+
+int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_s1)
+{
+    cb_backend *b;
+    const size_t T = DEC_T;
+
+    if (!d || !emb || !feat_s0 || !feat_s1)
+        return CB_EARG;
+    b = d->b;
+    if (emb->dtype != CB_F32 || feat_s0->dtype != CB_F32 || feat_s1->dtype != CB_F32 ||
+        emb->bytes < T * DEC_DIM * 4 || feat_s0->bytes < 16 * T * 32 * 4 ||
+        feat_s1->bytes < 4 * T * 64 * 4)
+        return cbi_fail(b, CB_EARG, "decoder set_image");
+    CB_TRY(cbi_enter(b));
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(d->feat_s0, feat_s0->ptr, 16 * T * 32 * 4,
+                                            cudaMemcpyDeviceToDevice, b->stream),
+                       "decoder set_image"));
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(d->feat_s1, feat_s1->ptr, 4 * T * 64 * 4,
+                                            cudaMemcpyDeviceToDevice, b->stream),
+                       "decoder set_image"));
+    /* src = emb + no_mask_embed, srcpe = src + dense PE; the layer-0
+     * projections every prompt shares (sam3_model.c:1160-1168) */
+    CB_TRY(add(d, d->src, (const float *)emb->ptr, (const float *)d->w[SAM3_DT_NO_MASK],
+               (long)T * DEC_DIM, DEC_DIM));
+    CB_TRY(add(d, d->srcpe, d->src, d->pe_img, (long)T * DEC_DIM, (long)T * DEC_DIM));
+    CB_TRY(lin32(d, "dec_gemm_img", d->srcpe, d->kin_bf16, (long)T, DEC_DIM, 128,
+                 ATT(SAM3_DA_L0_T2I, KW), ATT(SAM3_DA_L0_T2I, KB), d->kp0, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_img", d->src, d->kin_bf16, (long)T, DEC_DIM, 128,
+                 ATT(SAM3_DA_L0_T2I, VW), ATT(SAM3_DA_L0_T2I, VB), d->vp0, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_img", d->srcpe, d->kin_bf16, (long)T, DEC_DIM, 128,
+                 ATT(SAM3_DA_L0_I2T, QW), ATT(SAM3_DA_L0_I2T, QB), d->qp0, NULL, 0, K_ACT_NONE));
+    d->have_image = 1;
+    return CB_OK;
+}
+
+/* ---------------------------------------------------------------- decode */
+
+/* Token -> image attention on per-prompt keys, residual into the queries
+ * (t2i_attention, sam3_model.c:1212-1229). kin = keys + dense PE is kept in
+ * bf16: layer 1's image -> token queries read it again. */
+static int t2i_attention(cb_decoder *d, int P, int blk)
+{
+    const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
+
+    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
+    CB_TRY(add_cast(d, d->keys, d->pe_img, rows * DEC_DIM, (long)DEC_T * DEC_DIM, d->kin_bf16));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, QW),
+                 ATT(blk, QB), d->sq, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
+                 d->bk, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_img", d->keys, d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
+                 ATT(blk, VB), d->bv, NULL, 0, K_ACT_NONE));
+    CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->bk, (long)DEC_T * 128, d->bv,
+               (long)DEC_T * 128, d->so));
+    return lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, 128, DEC_DIM, ATT(blk, OW),
+                 ATT(blk, OB), d->qry, d->qry, 0, K_ACT_NONE);
+}
+
+/* token_mlp (sam3_model.c:1231-1237): 256 -> 2048 (ReLU) -> 256, residual. */
+static int token_mlp(cb_decoder *d, int P, int l)
+{
+    const long nt = (long)P * DEC_NTOK;
+
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, 2048, LAY(l, M1W),
+                 LAY(l, M1B), d->sh, NULL, 0, K_ACT_RELU));
+    return lin32(d, "dec_gemm_tok", d->sh, d->tok_bf16, nt, 2048, DEC_DIM, LAY(l, M2W),
+                 LAY(l, M2B), d->qry, d->qry, 0, K_ACT_NONE);
+}
+
+/* Self attention of the tokens; layer 0 without positional encoding and
+ * without residual (skip_first_layer_pe), layer 1 with both
+ * (sam3_model.c:1269-1282, 1311-1324). */
+static int self_attention(cb_decoder *d, int P, int l)
+{
+    const long nt = (long)P * DEC_NTOK;
+    const int blk = l ? SAM3_DA_L1_SELF : SAM3_DA_L0_SELF;
+    const float *qk = d->qry;
+
+    if (l) {
+        CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
+        qk = d->qin;
+    }
+    CB_TRY(lin32(d, "dec_gemm_tok", qk, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, QW),
+                 ATT(blk, QB), d->sq, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_tok", qk, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, KW),
+                 ATT(blk, KB), d->sk, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, VW),
+                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    CB_TRY(mha(d, P, DEC_NTOK, DEC_NTOK, DEC_DIM, d->sq, DEC_NTOK * DEC_DIM, d->sk,
+               DEC_NTOK * DEC_DIM, d->sv, DEC_NTOK * DEC_DIM, d->so));
+    return lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, OW),
+                 ATT(blk, OB), d->qry, l ? d->qry : NULL, 0, K_ACT_NONE);
+}
+
+/* Image -> token attention of layer l (sam3_model.c:1297-1309, 1334-1348):
+ * queries from the image stream (the shared layer-0 projection, or kin of
+ * layer 1), keys and values from the tokens; the output projection lands
+ * in keys, + src (layer 0: the add_bcast of sam3_model.c:1307 as the GEMM
+ * residual with row m % T) or + keys (layer 1), then norm4. */
+static int i2t_attention(cb_decoder *d, int P, int l)
+{
+    const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
+    const int blk = l ? SAM3_DA_L1_I2T : SAM3_DA_L0_I2T;
+
+    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
+    if (l)
+        CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, QW),
+                     ATT(blk, QB), d->bq, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, KW),
+                 ATT(blk, KB), d->sk, NULL, 0, K_ACT_NONE));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, VW),
+                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    CB_TRY(mha(d, P, DEC_T, DEC_NTOK, 128, l ? d->bq : d->qp0, l ? (long)DEC_T * 128 : 0, d->sk,
+               DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo));
+    CB_TRY(lin32(d, "dec_gemm_img", d->bo, d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW),
+                 ATT(blk, OB), d->keys, l ? d->keys : d->src, l ? 0 : DEC_T, K_ACT_NONE));
+    return ln(d, d->keys, d->keys, 0, rows, DEC_DIM, LAY(l, N4W), LAY(l, N4B), DEC_EPS,
+              K_ACT_NONE);
+}
+
+/* Prompt tokens (sam3_model.c:1249-1263): object score token, IoU token,
+ * 4 mask tokens, the point's encoding + point_embeddings[1], and
+ * not_a_point (the padding point SAM appends without a box). */
+static void prompt_tokens(const cb_decoder *d, int P, const float *points, float *tok)
+{
+    int p, i;
+
+    for (p = 0; p < P; p++) {
+        float *t = tok + (size_t)p * DEC_NTOK * DEC_DIM;
+
+        memcpy(t, d->hw[SAM3_DT_OBJ_TOKEN], DEC_DIM * sizeof(float));
+        memcpy(t + DEC_DIM, d->hw[SAM3_DT_IOU_TOKEN], DEC_DIM * sizeof(float));
+        memcpy(t + 2 * DEC_DIM, d->hw[SAM3_DT_MASK_TOKENS], 4 * DEC_DIM * sizeof(float));
+        pe_encode(d->hw[SAM3_DT_GAUSS], (points[2 * p] + 0.5f) / DEC_IMG,
+                  (points[2 * p + 1] + 0.5f) / DEC_IMG, t + 6 * DEC_DIM);
+        for (i = 0; i < DEC_DIM; i++) {
+            t[6 * DEC_DIM + i] += d->hw[SAM3_DT_POINT_EMB + 1][i];
+            t[7 * DEC_DIM + i] = d->hw[SAM3_DT_NOT_A_POINT][i];
+        }
+    }
+}
+
+int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowres)
+{
+    cb_backend *b;
+    struct k_dec_heads_w heads;
+    long nt, rows;
+    int l, m;
+
+    if (!d || !points || !iou || !lowres)
+        return CB_EARG;
+    b = d->b;
+    if (P <= 0 || P > d->batch || lowres->dtype != CB_F32 ||
+        lowres->bytes < (size_t)P * 3 * DEC_LOWRES * DEC_LOWRES * 4)
+        return cbi_fail(b, CB_EARG, "decode: batch or lowres buffer");
+    if (!d->have_image)
+        return cbi_fail(b, CB_EARG, "decode: no image (cb_decoder_set_image)");
+    CB_TRY(cbi_enter(b));
+    nt = (long)P * DEC_NTOK;
+    rows = (long)P * DEC_T;
+
+    prompt_tokens(d, P, points, d->h_tok);
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(d->qpe, d->h_tok, (size_t)nt * DEC_DIM * 4,
+                                            cudaMemcpyHostToDevice, b->stream),
+                       "decode: tokens"));
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(d->qry, d->qpe, (size_t)nt * DEC_DIM * 4,
+                                            cudaMemcpyDeviceToDevice, b->stream),
+                       "decode: tokens"));
+
+    /* Layer 0: self attention (no PE, no residual), token -> image on the
+     * shared layer-0 projections, MLP, image -> token. */
+    CB_TRY(self_attention(d, P, 0));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N1W), LAY(0, N1B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128,
+                 ATT(SAM3_DA_L0_T2I, QW), ATT(SAM3_DA_L0_T2I, QB), d->sq, NULL, 0, K_ACT_NONE));
+    CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->kp0, 0, d->vp0, 0, d->so));
+    CB_TRY(lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, 128, DEC_DIM,
+                 ATT(SAM3_DA_L0_T2I, OW), ATT(SAM3_DA_L0_T2I, OB), d->qry, d->qry, 0,
+                 K_ACT_NONE));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N2W), LAY(0, N2B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(token_mlp(d, P, 0));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N3W), LAY(0, N3B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(i2t_attention(d, P, 0));
+
+    /* Layer 1. */
+    CB_TRY(self_attention(d, P, 1));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N1W), LAY(1, N1B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(t2i_attention(d, P, SAM3_DA_L1_T2I));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N2W), LAY(1, N2B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(token_mlp(d, P, 1));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N3W), LAY(1, N3B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(i2t_attention(d, P, 1));
+
+    /* Final token -> image attention. */
+    CB_TRY(t2i_attention(d, P, SAM3_DA_FINAL_T2I));
+    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, SAM3_DT_NF_W, SAM3_DT_NF_B, DEC_EPS,
+              K_ACT_NONE));
+
+    /* Output upscaling (sam3_model.c:1353-1366): ConvT 256 -> 64 (+ feat_s1),
+     * LayerNorm2d + GELU, ConvT 64 -> 32 (+ feat_s0), GELU. */
+    LAUNCH("dec_cast", 0, (double)rows * DEC_DIM * 6,
+           k_cast_f32_bf16(d->keys, d->keys_bf16, rows * DEC_DIM, (k_stream)b->stream));
+    CB_TRY(lin16(d, "dec_gemm_up", d->keys_bf16, rows, DEC_DIM, 256, SAM3_DT_UP0_W, -1, d->G,
+                 NULL, 0, K_ACT_NONE));
+    LAUNCH("dec_convt", 0, (double)rows * 256 * 8,
+           k_convt_scatter(d->G, d->u1, (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1, P,
+                           DEC_GRID, DEC_GRID, 64, K_ACT_NONE, (k_stream)b->stream));
+    CB_TRY(ln(d, d->u1, d->u1_bf16, 1, 4 * rows, 64, SAM3_DT_UP1_W, SAM3_DT_UP1_B, LN2D_EPS,
+              K_ACT_GELU));
+    CB_TRY(lin16(d, "dec_gemm_up", d->u1_bf16, 4 * rows, 64, 128, SAM3_DT_UP3_W, -1, d->g2,
+                 NULL, 0, K_ACT_NONE));
+    LAUNCH("dec_convt", 0, (double)4 * rows * 128 * 8,
+           k_convt_scatter(d->g2, d->u2, (const float *)d->w[SAM3_DT_UP3_B], d->feat_s0, P,
+                           2 * DEC_GRID, 2 * DEC_GRID, 32, K_ACT_GELU, (k_stream)b->stream));
+
+    /* Hypernetwork MLPs 1..3 and the IoU head on the final tokens, then the
+     * low-resolution logits of the three multimask outputs. */
+    for (m = 0; m < 4; m++)
+        for (l = 0; l < 3; l++) {
+            const int base = m < 3 ? SAM3_DT_HYPER + 6 * (m + 1) : SAM3_DT_IOU;
+
+            heads.w[m][l] = (const float *)d->w[base + 2 * l];
+            heads.b[m][l] = (const float *)d->w[base + 2 * l + 1];
+        }
+    LAUNCH("dec_heads", 2.0 * P * 4 * (2 * 65536.0 + 32 * 256), (double)P * 4 * 2 * 65536 * 4,
+           k_dec_heads(d->qry, P, &heads, d->hyper, d->iou, (k_stream)b->stream));
+    LAUNCH("dec_mask_logits", 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
+           (double)P * DEC_LOWRES * DEC_LOWRES * (32 + 3) * 4,
+           k_mask_logits(d->u2, d->hyper, (float *)lowres->ptr, P, DEC_LOWRES * DEC_LOWRES,
+                         (k_stream)b->stream));
+    CB_TRY(cbi_kstatus(b,
+                       (int)cudaMemcpyAsync(iou, d->iou, (size_t)P * 3 * 4,
+                                            cudaMemcpyDeviceToHost, b->stream),
+                       "decode: iou"));
+    return cb_sync(b);
+}

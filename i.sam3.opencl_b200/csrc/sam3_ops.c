@@ -332,3 +332,39 @@ int cb_mha(cb_backend *b, int P, int Nq, int Nk, int dint, cb_mem qp,
                           "mha");
     }
 }
+
+int cb_convt_scatter(cb_backend *b, cb_mem G, cb_mem out, cb_mem bias,
+                     cb_mem add, int P, int H, int W, int Co, int act)
+{
+    const int64_t n = (int64_t)P * H * W * Co;
+
+    if (!b || !G || !out || !bias || P <= 0 || H <= 0 || W <= 0 || Co <= 0 ||
+        G->dtype != CB_F32 || out->dtype != CB_F32 || bias->dtype != CB_F32 ||
+        (add && add->dtype != CB_F32) || !fits(G, 4 * n) || !fits(out, 4 * n) ||
+        !fits(bias, Co) || (add && !fits(add, 4 * (int64_t)H * W * Co)) ||
+        !aligned16(G->ptr))
+        return cbi_fail(b, CB_EARG, "convt_scatter");
+    CB_TRY(cbi_enter(b));
+    return cbi_kstatus(b,
+                      k_convt_scatter((const float *)G->ptr, (float *)out->ptr,
+                                      (const float *)bias->ptr,
+                                      add ? (const float *)add->ptr : NULL, P, H, W,
+                                      Co, act, (k_stream)b->stream),
+                      "convt_scatter");
+}
+
+int cb_mask_logits(cb_backend *b, cb_mem U, cb_mem hyper, cb_mem out, int P,
+                   int npix)
+{
+    if (!b || !U || !hyper || !out || P <= 0 || npix <= 0 ||
+        U->dtype != CB_F32 || hyper->dtype != CB_F32 || out->dtype != CB_F32 ||
+        !fits(U, (int64_t)P * npix * 32) || !fits(hyper, (int64_t)P * 96) ||
+        !fits(out, (int64_t)P * 3 * npix) || !aligned16(U->ptr) ||
+        !aligned16(hyper->ptr))
+        return cbi_fail(b, CB_EARG, "mask_logits");
+    CB_TRY(cbi_enter(b));
+    return cbi_kstatus(b,
+                      k_mask_logits((const float *)U->ptr, (const float *)hyper->ptr,
+                                    (float *)out->ptr, P, npix, (k_stream)b->stream),
+                      "mask_logits");
+}

@@ -35,6 +35,9 @@ EXPORTS = [
     "cb_encoder_create", "cb_encoder_free", "cb_encoder_init_random",
     "cb_encoder_set_weight", "cb_encode_tiles", "cb_encode_blocks",
     "cb_encode_tiles_host", "cb_synth_normal", "cb_diag_exp2",
+    "cb_convt_scatter", "cb_mask_logits", "cb_decoder_create", "cb_decoder_free",
+    "cb_decoder_init_random", "cb_decoder_set_weight", "cb_decoder_set_image",
+    "cb_decode",
     "sam3_synth_normal", "sam3_synth_u8", "sam3_synth_rope_axial",
 ]
 
@@ -152,6 +155,14 @@ def lib():
         "cb_encode_tiles_host": (i32, [vp, vp, i32, vp]),
         "cb_synth_normal": (i32, [vp, C.c_uint64, C.c_uint64, f32, f32, vp, sz]),
         "cb_diag_exp2": (i32, [vp, vp, vp, i32, vp]),
+        "cb_convt_scatter": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32]),
+        "cb_mask_logits": (i32, [vp, vp, vp, vp, i32, i32]),
+        "cb_decoder_create": (i32, [vp, i32, C.POINTER(vp)]),
+        "cb_decoder_free": (None, [vp]),
+        "cb_decoder_init_random": (i32, [vp, C.c_uint64, f32]),
+        "cb_decoder_set_weight": (i32, [vp, i32, vp, sz]),
+        "cb_decoder_set_image": (i32, [vp, vp, vp, vp]),
+        "cb_decode": (i32, [vp, i32, vp, vp, vp]),
         "sam3_synth_normal": (None, [C.c_uint64, C.c_uint64, sz, f32, f32, vp]),
         "sam3_synth_u8": (None, [C.c_uint64, C.c_uint64, sz, vp]),
         "sam3_synth_rope_axial": (None, [i32, i32, C.c_double, vp]),
@@ -343,6 +354,13 @@ class Backend:
     def synth_normal(self, seed, stream, mean, std, out, count):
         self.check(lib().cb_synth_normal(self.h, seed, stream, mean, std, out.h, count))
 
+    def convt_scatter(self, G, out, bias, add, P, H, W, Co, act=ACT_NONE):
+        self.check(lib().cb_convt_scatter(self.h, G.h, out.h, bias.h,
+                                          add.h if add else None, P, H, W, Co, act))
+
+    def mask_logits(self, U, hyper, out, P, npix):
+        self.check(lib().cb_mask_logits(self.h, U.h, hyper.h, out.h, P, npix))
+
 
 class Encoder:
     """cb_encoder: the PE trunk (sam_encode_trunk) over batches of tiles."""
@@ -394,4 +412,50 @@ class Encoder:
     def close(self):
         if self.h:
             lib().cb_encoder_free(self.h)
+            self.h = C.c_void_p(None)
+
+
+# Decoder tensor indices (include/sam3_synth.h, SAM3_DT_*).
+DEC_TENSORS = 128
+DT = dict(ATTN=0, LAYER=56, NF_W=80, NF_B=81, UP0_W=82, UP0_B=83, UP1_W=84, UP1_B=85,
+          UP3_W=86, UP3_B=87, HYPER=88, IOU=112, GAUSS=118, POINT_EMB=119,
+          NOT_A_POINT=123, NO_MASK=124, OBJ_TOKEN=125, IOU_TOKEN=126, MASK_TOKENS=127)
+LOWRES = 288
+
+
+class Decoder:
+    """cb_decoder: the point-prompt mask decoder (sam_decode) for batches of
+    up to `batch` prompts on one image."""
+
+    def __init__(self, backend, batch):
+        self.backend = backend
+        self.batch = batch
+        h = C.c_void_p()
+        backend.check(lib().cb_decoder_create(backend.h, batch, C.byref(h)))
+        self.h = h
+
+    def init_random(self, seed, std=0.02):
+        self.backend.check(lib().cb_decoder_init_random(self.h, seed, std))
+
+    def set_weight(self, which, array):
+        import numpy as np
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        self.backend.check(lib().cb_decoder_set_weight(self.h, which, a.ctypes.data, a.size))
+
+    def set_image(self, emb, feat_s0, feat_s1):
+        self.backend.check(lib().cb_decoder_set_image(self.h, emb.h, feat_s0.h, feat_s1.h))
+
+    def decode(self, points, lowres):
+        """points: float32 [P, 2] (x, y) in input pixels; lowres: F32 Mem of
+        at least P * 3 * 288 * 288 values. Returns the IoU predictions [P, 3]."""
+        import numpy as np
+        pts = np.ascontiguousarray(points, dtype=np.float32).reshape(-1, 2)
+        iou = np.empty((pts.shape[0], 3), np.float32)
+        self.backend.check(lib().cb_decode(self.h, pts.shape[0], pts.ctypes.data,
+                                           iou.ctypes.data, lowres.h))
+        return iou
+
+    def close(self):
+        if self.h:
+            lib().cb_decoder_free(self.h)
             self.h = C.c_void_p(None)

@@ -303,6 +303,62 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last);
 int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
                          float *out);
 
+/* ------------------------------------------------------------ decoder ops
+ * Kernels of the mask decoder's output upscaling (sam3_kernels.cl:762-807).
+ *
+ * convt_scatter (sam3_model.c:394-410, sam3_kernels.cl:762-781): the GEMM
+ * form G [P * H * W, Co * 4] (column co * 4 + dy * 2 + dx) of a 2x2 /
+ * stride-2 ConvTranspose2d scattered into out [P, 2H, 2W, Co], + bias[co],
+ * + add[(2H * 2W * Co) index] when add != NULL (shared by all P), then act.
+ * All F32. */
+int cb_convt_scatter(cb_backend *b, cb_mem G, cb_mem out, cb_mem bias,
+                     cb_mem add, int P, int H, int W, int Co, int act);
+
+/* mask_logits (sam3_model.c:1387-1399, sam3_kernels.cl:787-807):
+ * out[p, m, pix] = hyper[p, m, :] . U[p, pix, :] for m < 3 over 32
+ * channels; U [P, npix, 32], hyper [P, 96], out [P, 3, npix]. All F32. */
+int cb_mask_logits(cb_backend *b, cb_mem U, cb_mem hyper, cb_mem out, int P,
+                   int npix);
+
+/* ------------------------------------------------------------ decoder
+ * The point-prompt mask decoder of sam3_model.c: prompt encoding
+ * (pe_encode :760-773), the image-side caches of sam_encode (:1153-1170),
+ * sam_decode (:1239-1399: two-way transformer, final token-to-image
+ * attention, output upscaling, hypernetwork and IoU heads, mask_logits).
+ * Tensors and their order: include/sam3_synth.h (SAM3_DT_*). */
+typedef struct cb_decoder cb_decoder;
+
+/* Weights and work buffers for up to `batch` prompts per decode. */
+int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out);
+void cb_decoder_free(cb_decoder *d);
+
+/* Random init of every decoder tensor from the sam3_synth.h streams
+ * (SAM3_STREAM_DECW + index; init kinds SAM3_INIT_*, std for the W and B
+ * kinds). */
+int cb_decoder_init_random(cb_decoder *d, uint64_t seed, float std);
+
+/* Set decoder tensor `which` (SAM3_DT_*) from host fp32 data in the
+ * checkpoint's layout and shape (sam3_dec_tensor gives rows x cols). */
+int cb_decoder_set_weight(cb_decoder *d, int which, const float *src,
+                          size_t count);
+
+/* Image-side inputs of the decodes that follow (the outputs of the neck,
+ * sam3_model.c:1098-1110): emb [72 * 72, 256] (with no_mem_embed added),
+ * feat_s0 [288 * 288, 32], feat_s1 [144 * 144, 64], all F32 device
+ * buffers, copied. Computes src = emb + no_mask_embed, the dense
+ * positional encoding and the layer-0 projections that every prompt
+ * shares (sam3_model.c:1153-1170). */
+int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0,
+                         cb_mem feat_s1);
+
+/* sam_decode for P <= batch prompts, one positive point each: points [2P]
+ * host (x, y) in input-image pixels; iou [3P] host receives the IoU
+ * predictions of the three multimask outputs; lowres F32 device [P, 3,
+ * 288, 288] receives their low-resolution mask logits. Blocking (iou is
+ * read back at the end). */
+int cb_decode(cb_decoder *d, int P, const float *points, float *iou,
+              cb_mem lowres);
+
 /* Diagnostics: the two exponential paths of the attention softmax on n
  * (even) device values x <= 0: y_poly = the FMA-pipe polynomial 2^x,
  * y_mufu = ex2.approx, for accuracy tests against the CUDA math library. */

@@ -97,6 +97,133 @@ enum {
 };
 #define SAM3_IMAGE_STREAM_TILE(t) ((uint64_t)SAM3_STREAM_IMAGE * 1000003ULL + (uint64_t)(t))
 
+/* ------------------------------------------------ point-prompt mask decoder
+ * The tensors of the decoder (sam3_model.c load_decoder :656-755 and the
+ * decoder's share of load_point_neck :642-654) in one fixed order, with the
+ * reference's shapes ([rows, cols], cols 1 for vectors; 4-D ConvTranspose
+ * weights [cin, cout, 2, 2] as [cin, cout * 4]). Random init of tensor i
+ * draws stream SAM3_STREAM_DECW + i:
+ *   SAM3_INIT_W     N(0, std)      Linear / ConvTranspose weights
+ *   SAM3_INIT_B     N(0, std)      their biases
+ *   SAM3_INIT_LNW   N(1, 0.1)      LayerNorm weights
+ *   SAM3_INIT_LNB   N(0, 0.1)      LayerNorm biases
+ *   SAM3_INIT_EMB   N(0, 1)        tokens, prompt embeddings, the gaussian
+ *                                  matrix of the positional encoding
+ * The image-side inputs of a decode (image embedding [T, 256], feat_s0
+ * [16T, 32], feat_s1 [4T, 64]) draw N(0, 1) from SAM3_STREAM_DECIMG + 0, 1,
+ * 2 when a test or benchmark synthesises them. */
+enum {
+    SAM3_INIT_W = 0,
+    SAM3_INIT_B = 1,
+    SAM3_INIT_LNW = 2,
+    SAM3_INIT_LNB = 3,
+    SAM3_INIT_EMB = 4
+};
+#define SAM3_STREAM_DECW 8192ULL
+#define SAM3_STREAM_DECIMG 9216ULL
+
+/* Attention blocks of the decoder, 8 tensors each (q, k, v, out projection
+ * weight and bias: q_w [d, 256], q_b [d], k_w, k_b, v_w, v_b, o_w [256, d],
+ * o_b [256]) with inner width d = 256 (self) or 128 (cross). */
+enum {
+    SAM3_DA_L0_SELF = 0,
+    SAM3_DA_L0_T2I = 1,
+    SAM3_DA_L0_I2T = 2,
+    SAM3_DA_L1_SELF = 3,
+    SAM3_DA_L1_T2I = 4,
+    SAM3_DA_L1_I2T = 5,
+    SAM3_DA_FINAL_T2I = 6,
+    SAM3_DA_COUNT = 7
+};
+/* Tensor indices. */
+enum {
+    SAM3_DT_ATTN = 0,                       /* + 8 * block + {q_w, q_b, k_w, k_b, v_w, v_b, o_w, o_b} */
+    SAM3_DT_LAYER = 8 * SAM3_DA_COUNT,      /* + 12 * layer + {n1w, n1b, n2w, n2b, n3w, n3b, n4w, n4b, m1w, m1b, m2w, m2b} */
+    SAM3_DT_NF_W = SAM3_DT_LAYER + 24,      /* norm_final_attn */
+    SAM3_DT_NF_B,
+    SAM3_DT_UP0_W,                          /* output_upscaling.0: [256, 64 * 4] */
+    SAM3_DT_UP0_B,                          /* [64] */
+    SAM3_DT_UP1_W,                          /* output_upscaling.1 (LayerNorm2d) [64] */
+    SAM3_DT_UP1_B,
+    SAM3_DT_UP3_W,                          /* output_upscaling.3: [64, 32 * 4] */
+    SAM3_DT_UP3_B,                          /* [32] */
+    SAM3_DT_HYPER,                          /* + 6 * mlp + {w0, b0, w1, b1, w2, b2}, 4 MLPs */
+    SAM3_DT_IOU = SAM3_DT_HYPER + 24,       /* + {w0, b0, w1, b1, w2, b2} */
+    SAM3_DT_GAUSS = SAM3_DT_IOU + 6,        /* [2, 128] */
+    SAM3_DT_POINT_EMB,                      /* + 4: point_embeddings.0..3 [256] */
+    SAM3_DT_NOT_A_POINT = SAM3_DT_POINT_EMB + 4,
+    SAM3_DT_NO_MASK,
+    SAM3_DT_OBJ_TOKEN,
+    SAM3_DT_IOU_TOKEN,
+    SAM3_DT_MASK_TOKENS,                    /* [4, 256] */
+    SAM3_DT_COUNT
+};
+
+/* Shape and init kind of decoder tensor i (0 <= i < SAM3_DT_COUNT). */
+static inline void sam3_dec_tensor(int i, int *rows, int *cols, int *init)
+{
+    int r = 256, c = 1, k = SAM3_INIT_EMB;
+
+    if (i < SAM3_DT_LAYER) {
+        const int blk = i / 8, t = i % 8;
+        const int d = (blk == SAM3_DA_L0_SELF || blk == SAM3_DA_L1_SELF) ? 256 : 128;
+
+        r = t < 6 ? d : 256;
+        c = (t & 1) ? 1 : (t < 6 ? 256 : d);
+        k = (t & 1) ? SAM3_INIT_B : SAM3_INIT_W;
+    }
+    else if (i < SAM3_DT_NF_W) {
+        const int t = (i - SAM3_DT_LAYER) % 12;
+
+        if (t < 8) {
+            k = (t & 1) ? SAM3_INIT_LNB : SAM3_INIT_LNW;
+        }
+        else if (t == 8 || t == 9) {
+            r = 2048;
+            c = t == 8 ? 256 : 1;
+            k = t == 8 ? SAM3_INIT_W : SAM3_INIT_B;
+        }
+        else {
+            c = t == 10 ? 2048 : 1;
+            k = t == 10 ? SAM3_INIT_W : SAM3_INIT_B;
+        }
+    }
+    else if (i == SAM3_DT_NF_W || i == SAM3_DT_NF_B) {
+        k = i == SAM3_DT_NF_W ? SAM3_INIT_LNW : SAM3_INIT_LNB;
+    }
+    else if (i == SAM3_DT_UP0_W) {
+        c = 256, k = SAM3_INIT_W;
+    }
+    else if (i == SAM3_DT_UP0_B || i == SAM3_DT_UP1_W || i == SAM3_DT_UP1_B) {
+        r = 64;
+        k = i == SAM3_DT_UP0_B ? SAM3_INIT_B : (i == SAM3_DT_UP1_W ? SAM3_INIT_LNW : SAM3_INIT_LNB);
+    }
+    else if (i == SAM3_DT_UP3_W) {
+        r = 64, c = 128, k = SAM3_INIT_W;
+    }
+    else if (i == SAM3_DT_UP3_B) {
+        r = 32, k = SAM3_INIT_B;
+    }
+    else if (i < SAM3_DT_GAUSS) {
+        /* hypernetwork MLPs (output 32) and the IoU head (output 4) */
+        const int t = (i - SAM3_DT_HYPER) % 6, last = t >= 4;
+        const int nout = i >= SAM3_DT_IOU ? 4 : 32;
+
+        r = last ? nout : 256;
+        c = (t & 1) ? 1 : 256;
+        k = (t & 1) ? SAM3_INIT_B : SAM3_INIT_W;
+    }
+    else if (i == SAM3_DT_GAUSS) {
+        r = 2, c = 128;
+    }
+    else if (i == SAM3_DT_MASK_TOKENS) {
+        r = 4, c = 256;
+    }
+    *rows = r;
+    *cols = c;
+    *init = k;
+}
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,12 @@ def lib():
         L.or_encode_trunk.argtypes = [C.POINTER(Trunk), C.c_void_p, f32p,
                                       C.c_int, C.c_int]
         L.or_num_threads.restype = C.c_int
+        L.or_convt_scatter.argtypes = [f32p, f32p, f32p, C.c_void_p] + [C.c_int] * 5
+        L.or_mask_logits.argtypes = [f32p, f32p, f32p, C.c_int, C.c_long]
+        L.or_pe_encode.argtypes = [f32p, C.c_float, C.c_float, f32p]
+        L.or_dec_tensor.argtypes = [C.c_int] + [C.POINTER(C.c_int)] * 3
+        L.or_sam_decode.argtypes = [C.POINTER(C.c_void_p), f32p, f32p, f32p, C.c_int,
+                                    f32p, f32p, f32p]
         L.sam3_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t,
                                         C.c_float, C.c_float, f32p]
         L.sam3_synth_u8.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t, u8p]
@@ -105,6 +111,8 @@ def ref():
                                               f32p, C.c_long, f32p]
         R.ref_mha.restype = C.c_int
         R.ref_num_threads.restype = C.c_int
+        R.ref_convt_scatter.argtypes = [f32p, f32p, f32p, C.c_void_p] + [C.c_int] * 5
+        R.ref_mask_logits.argtypes = [f32p, f32p, f32p, C.c_int, C.c_long]
     return _ref
 
 
@@ -313,3 +321,83 @@ def encode_trunk(w, img_chw, first=0, last=None, x=None):
     lib().or_encode_trunk(C.byref(t), None if img is None else img.ctypes.data, x, first,
                           w.depth if last is None else last)
     return x
+
+
+# ---------------------------------------------------------------- mask decoder
+def convt_scatter(G, bias, add, P, H, W, Co, act=0, use_ref=False):
+    """convt_scatter (sam3_kernels.cl:766-781): G [P*H*W, Co*4] -> [P, 2H, 2W, Co]."""
+    G = np.ascontiguousarray(G, np.float32)
+    out = np.empty((P, 2 * H, 2 * W, Co), np.float32)
+    addp = None
+    if add is not None:
+        add = np.ascontiguousarray(add, np.float32)
+        addp = add.ctypes.data
+    fn = ref().ref_convt_scatter if use_ref else lib().or_convt_scatter
+    fn(G, out, np.ascontiguousarray(bias, np.float32), addp, P, H, W, Co, act)
+    return out
+
+
+def mask_logits(U, hyper, P, npix, use_ref=False):
+    """mask_logits (sam3_kernels.cl:789-807): U [P, npix, 32], hyper [P, 96]."""
+    out = np.empty((P, 3, npix), np.float32)
+    fn = ref().ref_mask_logits if use_ref else lib().or_mask_logits
+    fn(np.ascontiguousarray(U, np.float32), np.ascontiguousarray(hyper, np.float32), out,
+       npix, P * npix)
+    return out
+
+
+def pe_encode(gauss, x, y):
+    out = np.empty(256, np.float32)
+    lib().or_pe_encode(np.ascontiguousarray(gauss, np.float32), x, y, out)
+    return out
+
+
+DEC_TENSORS = 128
+DEC_STREAM = 8192
+DEC_IMG_STREAM = 9216
+
+
+def dec_tensor_info(i):
+    r, c, k = C.c_int(), C.c_int(), C.c_int()
+    lib().or_dec_tensor(i, C.byref(r), C.byref(c), C.byref(k))
+    return r.value, c.value, k.value
+
+
+class DecoderWeights:
+    """The decoder's random-init tensors (include/sam3_synth.h: tensor i
+    draws stream 8192 + i; W and B kinds N(0, std), LayerNorm weights
+    N(1, 0.1), LayerNorm biases N(0, 0.1), embeddings N(0, 1)), fp32 in the
+    checkpoint layout."""
+
+    def __init__(self, seed, std=0.02):
+        self.t = []
+        for i in range(DEC_TENSORS):
+            r, c, k = dec_tensor_info(i)
+            mean = 1.0 if k == 2 else 0.0
+            sd = 1.0 if k == 4 else (0.1 if k in (2, 3) else std)
+            self.t.append(normal(seed, DEC_STREAM + i, (r, c), mean, sd))
+
+    def ctypes(self):
+        arr = (C.c_void_p * DEC_TENSORS)(*[a.ctypes.data for a in self.t])
+        return arr
+
+
+def decoder_image(seed):
+    """Synthetic image-side decoder inputs: emb [5184, 256], feat_s0
+    [82944, 32], feat_s1 [20736, 64], N(0, 1)."""
+    return (normal(seed, DEC_IMG_STREAM + 0, (5184, 256)),
+            normal(seed, DEC_IMG_STREAM + 1, (16 * 5184, 32)),
+            normal(seed, DEC_IMG_STREAM + 2, (4 * 5184, 64)))
+
+
+def sam_decode(w, emb, s0, s1, points):
+    """Decoder caches + sam_decode (sam3_model.c:1153-1170, 1239-1399) for the
+    prompts points [P, 2]; returns (iou [P, 3], lowres [P, 3, 288, 288])."""
+    pts = np.ascontiguousarray(points, np.float32).reshape(-1, 2)
+    P = pts.shape[0]
+    iou = np.empty((P, 3), np.float32)
+    low = np.empty((P, 3, 288, 288), np.float32)
+    lib().or_sam_decode(w.ctypes(), np.ascontiguousarray(emb, np.float32),
+                        np.ascontiguousarray(s0, np.float32),
+                        np.ascontiguousarray(s1, np.float32), P, pts, iou, low)
+    return iou, low

@@ -7,6 +7,7 @@
  * fmaf(w, fmaf(z, fmaf(y, x*x')))); built with -ffp-contract=off so that no
  * other multiply-add is fused. */
 #include "oracle.h"
+#include "sam3_synth.h"
 
 #include <math.h>
 #include <stdlib.h>
@@ -618,4 +619,259 @@ int or_num_threads(void)
 #else
     return 1;
 #endif
+}
+
+/* ------------------------------------------------------------ mask decoder */
+
+/* Shape and init kind of decoder tensor i (include/sam3_synth.h). */
+void or_dec_tensor(int i, int *rows, int *cols, int *init)
+{
+    sam3_dec_tensor(i, rows, cols, init);
+}
+
+/* convt_scatter: sam3_kernels.cl:766-781, one work-item per output value. */
+void or_convt_scatter(const float *G, float *out, const float *bias,
+                      const float *add, int P, int H, int W, int Co, int act)
+{
+    const long total = (long)P * 4 * H * W * Co;
+    long gid;
+
+#pragma omp parallel for schedule(static)
+    for (gid = 0; gid < total; gid++) {
+        const int co = (int)(gid % Co);
+        const long pix = gid / Co;
+        const int ox = (int)(pix % (2 * W));
+        const long rest = pix / (2 * W);
+        const int oy = (int)(rest % (2 * H));
+        const long p = rest / (2 * H);
+        const int y = oy >> 1, x = ox >> 1, dy = oy & 1, dx = ox & 1;
+        float v = G[((p * H + y) * W + x) * (Co * 4) + co * 4 + dy * 2 + dx] + bias[co];
+
+        if (add)
+            v += add[gid % (4L * H * W * Co)];
+        out[gid] = apply_act(v, act);
+    }
+}
+
+/* mask_logits: sam3_kernels.cl:789-807. */
+void or_mask_logits(const float *U, const float *hyper, float *out, int npix,
+                    long total)
+{
+    long gid;
+
+#pragma omp parallel for schedule(static)
+    for (gid = 0; gid < total; gid++) {
+        const long p = gid / npix;
+        const int pix = (int)(gid % npix);
+        const float *h = hyper + p * 96, *u = U + gid * 32;
+        int m;
+
+        for (m = 0; m < 3; m++)
+            out[(p * 3 + m) * npix + pix] =
+                dot16(u, h + 32 * m) + dot16(u + 16, h + 32 * m + 16);
+    }
+}
+
+/* pe_encode: sam3_model.c:760-773. */
+void or_pe_encode(const float *gauss, float x, float y, float *out)
+{
+    int i;
+
+    x = 2.0f * x - 1.0f;
+    y = 2.0f * y - 1.0f;
+    for (i = 0; i < 128; i++) {
+        float v = x * gauss[i] + y * gauss[128 + i];
+
+        v *= 2.0f * (float)M_PI;
+        out[i] = sinf(v);
+        out[128 + i] = cosf(v);
+    }
+}
+
+/* host_linear / host_mlp3: sam3_model.c:1188-1210. */
+static void host_linear(const float *W, const float *b, const float *x, int nin,
+                        int nout, int relu, float *y)
+{
+    int o, i;
+
+    for (o = 0; o < nout; o++) {
+        const float *w = W + (long)o * nin;
+        double acc = b[o];
+
+        for (i = 0; i < nin; i++)
+            acc += (double)w[i] * x[i];
+        y[o] = relu && acc < 0.0 ? 0.0f : (float)acc;
+    }
+}
+
+static void host_mlp3(const float *const *wb, const float *x, int nout, float *y)
+{
+    float h1[256], h2[256];
+
+    host_linear(wb[0], wb[1], x, 256, 256, 1, h1);
+    host_linear(wb[2], wb[3], h1, 256, 256, 1, h2);
+    host_linear(wb[4], wb[5], h2, 256, nout, 0, y);
+}
+
+#define DT(i) (w[(i)])
+#define DATT(blk, t) (w[SAM3_DT_ATTN + 8 * (blk) + (t)])
+#define DLAY(l, t) (w[SAM3_DT_LAYER + 12 * (l) + (t)])
+
+/* t2i_attention: sam3_model.c:1212-1229. */
+static void dec_t2i(const float *const *w, int blk, int P, float *qry,
+                    const float *qpe, float *qin, float *keys, float *kin,
+                    const float *pe_img, float *sq, float *bk, float *bv,
+                    float *so)
+{
+    const long T = 5184, n = (long)P * 8 * 256;
+
+    or_add_bcast(qin, qry, qpe, n, n);
+    or_add_bcast(kin, keys, pe_img, P * T * 256, T * 256);
+    linear(P * 8, 256, 128, qin, DATT(blk, 0), DATT(blk, 1), sq, OR_ACT_NONE, 0);
+    linear((int)(P * T), 256, 128, kin, DATT(blk, 2), DATT(blk, 3), bk, OR_ACT_NONE, 0);
+    linear((int)(P * T), 256, 128, keys, DATT(blk, 4), DATT(blk, 5), bv, OR_ACT_NONE, 0);
+    or_mha(P, 8, (int)T, 128, sq, 8 * 128, bk, T * 128, bv, T * 128, so);
+    linear(P * 8, 128, 256, so, DATT(blk, 6), DATT(blk, 7), qry, OR_ACT_NONE, 1);
+}
+
+/* token_mlp: sam3_model.c:1231-1237. */
+static void dec_mlp(const float *const *w, int l, int P, float *qry, float *sh)
+{
+    linear(P * 8, 256, 2048, qry, DLAY(l, 8), DLAY(l, 9), sh, OR_ACT_RELU, 0);
+    linear(P * 8, 2048, 256, sh, DLAY(l, 10), DLAY(l, 11), qry, OR_ACT_NONE, 1);
+}
+
+void or_sam_decode(const float *const *w, const float *emb, const float *s0,
+                   const float *s1, int P, const float *points, float *iou,
+                   float *lowres)
+{
+    const long T = 5184, n = (long)P * 8 * 256, L = 288;
+    const float eps = 1e-5f;
+    float *src = malloc(sizeof(float) * T * 256), *srcpe = malloc(sizeof(float) * T * 256);
+    float *pe_img = malloc(sizeof(float) * T * 256);
+    float *kp0 = malloc(sizeof(float) * T * 128), *vp0 = malloc(sizeof(float) * T * 128);
+    float *qp0 = malloc(sizeof(float) * T * 128);
+    float *tok = malloc(sizeof(float) * n), *qpe = malloc(sizeof(float) * n);
+    float *qry = malloc(sizeof(float) * n), *qin = malloc(sizeof(float) * n);
+    float *sq = malloc(sizeof(float) * n), *sk = malloc(sizeof(float) * n);
+    float *sv = malloc(sizeof(float) * n), *so = malloc(sizeof(float) * n);
+    float *sh = malloc(sizeof(float) * P * 8 * 2048);
+    float *keys = malloc(sizeof(float) * P * T * 256), *kin = malloc(sizeof(float) * P * T * 256);
+    float *bq = malloc(sizeof(float) * P * T * 128), *bk = malloc(sizeof(float) * P * T * 128);
+    float *bv = malloc(sizeof(float) * P * T * 128), *bo = malloc(sizeof(float) * P * T * 128);
+    float *u1 = malloc(sizeof(float) * P * 4 * T * 64);
+    float *g2 = malloc(sizeof(float) * P * 4 * T * 128);
+    float *u2 = malloc(sizeof(float) * P * 16 * T * 32);
+    float *hyper = malloc(sizeof(float) * P * 96);
+    struct or_gemm_args a;
+    int p, i, x, y;
+
+    /* decoder caches of sam_encode (sam3_model.c:1153-1170, 886-892) */
+    or_add_bcast(src, emb, DT(SAM3_DT_NO_MASK), T * 256, 256);
+    for (y = 0; y < 72; y++)
+        for (x = 0; x < 72; x++)
+            or_pe_encode(DT(SAM3_DT_GAUSS), (x + 0.5f) / 72, (y + 0.5f) / 72,
+                         pe_img + ((long)y * 72 + x) * 256);
+    or_add_bcast(srcpe, src, pe_img, T * 256, T * 256);
+    linear((int)T, 256, 128, srcpe, DATT(1, 2), DATT(1, 3), kp0, OR_ACT_NONE, 0);
+    linear((int)T, 256, 128, src, DATT(1, 4), DATT(1, 5), vp0, OR_ACT_NONE, 0);
+    linear((int)T, 256, 128, srcpe, DATT(2, 0), DATT(2, 1), qp0, OR_ACT_NONE, 0);
+
+    /* prompt tokens (sam3_model.c:1249-1263) */
+    for (p = 0; p < P; p++) {
+        float *t = tok + (long)p * 8 * 256;
+
+        memcpy(t, DT(SAM3_DT_OBJ_TOKEN), 256 * sizeof(float));
+        memcpy(t + 256, DT(SAM3_DT_IOU_TOKEN), 256 * sizeof(float));
+        memcpy(t + 512, DT(SAM3_DT_MASK_TOKENS), 4 * 256 * sizeof(float));
+        or_pe_encode(DT(SAM3_DT_GAUSS), (points[2 * p] + 0.5f) / 1008,
+                     (points[2 * p + 1] + 0.5f) / 1008, t + 6 * 256);
+        for (i = 0; i < 256; i++) {
+            t[6 * 256 + i] += DT(SAM3_DT_POINT_EMB + 1)[i];
+            t[7 * 256 + i] = DT(SAM3_DT_NOT_A_POINT)[i];
+        }
+    }
+    memcpy(qpe, tok, sizeof(float) * n);
+    memcpy(qry, tok, sizeof(float) * n);
+
+    /* layer 0 (sam3_model.c:1269-1309) */
+    linear(P * 8, 256, 256, qry, DATT(0, 0), DATT(0, 1), sq, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 256, qry, DATT(0, 2), DATT(0, 3), sk, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 256, qry, DATT(0, 4), DATT(0, 5), sv, OR_ACT_NONE, 0);
+    or_mha(P, 8, 8, 256, sq, 8 * 256, sk, 8 * 256, sv, 8 * 256, so);
+    linear(P * 8, 256, 256, so, DATT(0, 6), DATT(0, 7), qry, OR_ACT_NONE, 0);
+    or_layernorm(qry, qry, DLAY(0, 0), DLAY(0, 1), P * 8, 256, eps, OR_ACT_NONE);
+    or_add_bcast(qin, qry, qpe, n, n);
+    linear(P * 8, 256, 128, qin, DATT(1, 0), DATT(1, 1), sq, OR_ACT_NONE, 0);
+    or_mha(P, 8, (int)T, 128, sq, 8 * 128, kp0, 0, vp0, 0, so);
+    linear(P * 8, 128, 256, so, DATT(1, 6), DATT(1, 7), qry, OR_ACT_NONE, 1);
+    or_layernorm(qry, qry, DLAY(0, 2), DLAY(0, 3), P * 8, 256, eps, OR_ACT_NONE);
+    dec_mlp(w, 0, P, qry, sh);
+    or_layernorm(qry, qry, DLAY(0, 4), DLAY(0, 5), P * 8, 256, eps, OR_ACT_NONE);
+    or_add_bcast(qin, qry, qpe, n, n);
+    linear(P * 8, 256, 128, qin, DATT(2, 2), DATT(2, 3), sk, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 128, qry, DATT(2, 4), DATT(2, 5), sv, OR_ACT_NONE, 0);
+    or_mha(P, (int)T, 8, 128, qp0, 0, sk, 8 * 128, sv, 8 * 128, bo);
+    linear((int)(P * T), 128, 256, bo, DATT(2, 6), DATT(2, 7), keys, OR_ACT_NONE, 0);
+    or_add_bcast(keys, keys, src, P * T * 256, T * 256);
+    or_layernorm(keys, keys, DLAY(0, 6), DLAY(0, 7), P * T, 256, eps, OR_ACT_NONE);
+
+    /* layer 1 (sam3_model.c:1311-1348) */
+    or_add_bcast(qin, qry, qpe, n, n);
+    linear(P * 8, 256, 256, qin, DATT(3, 0), DATT(3, 1), sq, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 256, qin, DATT(3, 2), DATT(3, 3), sk, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 256, qry, DATT(3, 4), DATT(3, 5), sv, OR_ACT_NONE, 0);
+    or_mha(P, 8, 8, 256, sq, 8 * 256, sk, 8 * 256, sv, 8 * 256, so);
+    linear(P * 8, 256, 256, so, DATT(3, 6), DATT(3, 7), qry, OR_ACT_NONE, 1);
+    or_layernorm(qry, qry, DLAY(1, 0), DLAY(1, 1), P * 8, 256, eps, OR_ACT_NONE);
+    dec_t2i(w, 4, P, qry, qpe, qin, keys, kin, pe_img, sq, bk, bv, so);
+    or_layernorm(qry, qry, DLAY(1, 2), DLAY(1, 3), P * 8, 256, eps, OR_ACT_NONE);
+    dec_mlp(w, 1, P, qry, sh);
+    or_layernorm(qry, qry, DLAY(1, 4), DLAY(1, 5), P * 8, 256, eps, OR_ACT_NONE);
+    or_add_bcast(qin, qry, qpe, n, n);
+    linear((int)(P * T), 256, 128, kin, DATT(5, 0), DATT(5, 1), bq, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 128, qin, DATT(5, 2), DATT(5, 3), sk, OR_ACT_NONE, 0);
+    linear(P * 8, 256, 128, qry, DATT(5, 4), DATT(5, 5), sv, OR_ACT_NONE, 0);
+    or_mha(P, (int)T, 8, 128, bq, T * 128, sk, 8 * 128, sv, 8 * 128, bo);
+    linear((int)(P * T), 128, 256, bo, DATT(5, 6), DATT(5, 7), keys, OR_ACT_NONE, 1);
+    or_layernorm(keys, keys, DLAY(1, 6), DLAY(1, 7), P * T, 256, eps, OR_ACT_NONE);
+
+    /* final token -> image attention (sam3_model.c:1350-1352) */
+    dec_t2i(w, 6, P, qry, qpe, qin, keys, kin, pe_img, sq, bk, bv, so);
+    or_layernorm(qry, qry, DT(SAM3_DT_NF_W), DT(SAM3_DT_NF_B), P * 8, 256, eps, OR_ACT_NONE);
+
+    /* output upscaling (sam3_model.c:1353-1366) */
+    memset(&a, 0, sizeof(a));
+    a.M = (int)(P * T), a.N = 256, a.K = 256, a.A = keys, a.lda = 256;
+    a.B = DT(SAM3_DT_UP0_W), a.ldb = 256, a.C = kin, a.ldc = 256, a.nb1 = 1;
+    a.alpha = 1.0f;
+    or_gemm(&a, 1);
+    or_convt_scatter(kin, u1, DT(SAM3_DT_UP0_B), s1, P, 72, 72, 64, OR_ACT_NONE);
+    or_layernorm(u1, u1, DT(SAM3_DT_UP1_W), DT(SAM3_DT_UP1_B), P * 4 * T, 64, 1e-6f,
+                 OR_ACT_GELU);
+    memset(&a, 0, sizeof(a));
+    a.M = (int)(P * 4 * T), a.N = 128, a.K = 64, a.A = u1, a.lda = 64;
+    a.B = DT(SAM3_DT_UP3_W), a.ldb = 128, a.C = g2, a.ldc = 128, a.nb1 = 1;
+    a.alpha = 1.0f;
+    or_gemm(&a, 1);
+    or_convt_scatter(g2, u2, DT(SAM3_DT_UP3_B), s0, P, 144, 144, 32, OR_ACT_GELU);
+
+    /* hypernetwork MLPs 1..3 and the IoU head (sam3_model.c:1368-1386) */
+    for (p = 0; p < P; p++) {
+        const float *t = qry + (long)p * 8 * 256;
+        float out[4];
+
+        for (i = 1; i <= 3; i++)
+            host_mlp3(w + SAM3_DT_HYPER + 6 * i, t + (2 + i) * 256, 32,
+                      hyper + (long)p * 96 + (i - 1) * 32);
+        host_mlp3(w + SAM3_DT_IOU, t + 256, 4, out);
+        for (i = 0; i < 3; i++)
+            iou[p * 3 + i] = 1.0f / (1.0f + expf(-out[1 + i]));
+    }
+    or_mask_logits(u2, hyper, lowres, (int)(L * L), P * L * L);
+
+    free(src), free(srcpe), free(pe_img), free(kp0), free(vp0), free(qp0);
+    free(tok), free(qpe), free(qry), free(qin), free(sq), free(sk), free(sv), free(so);
+    free(sh), free(keys), free(kin), free(bq), free(bk), free(bv), free(bo);
+    free(u1), free(g2), free(u2), free(hyper);
 }

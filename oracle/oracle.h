@@ -96,6 +96,26 @@ void or_encode_trunk(const struct or_trunk *t, const float *img, float *x,
 
 int or_num_threads(void);
 
+/* Mask decoder kernels: convt_scatter (sam3_kernels.cl:766-781),
+ * mask_logits (sam3_kernels.cl:789-807; total = P * npix), pe_encode
+ * (sam3_model.c:760-773). */
+void or_convt_scatter(const float *G, float *out, const float *bias,
+                      const float *add, int P, int H, int W, int Co, int act);
+void or_mask_logits(const float *U, const float *hyper, float *out, int npix,
+                    long total);
+void or_pe_encode(const float *gauss, float x, float y, float *out);
+void or_dec_tensor(int i, int *rows, int *cols, int *init);
+
+/* The decoder caches of sam_encode (sam3_model.c:1153-1170) and sam_decode
+ * (sam3_model.c:1239-1399) for P prompts: w holds the decoder tensors in
+ * include/sam3_synth.h order (SAM3_DT_*) and checkpoint layout; emb
+ * [5184, 256], s0 [288 * 288, 32], s1 [144 * 144, 64]; points [2P] (x, y)
+ * in input pixels; iou [3P] and lowres [P, 3, 288, 288] receive the
+ * outputs. Work buffers are allocated inside. */
+void or_sam_decode(const float *const *w, const float *emb, const float *s0,
+                   const float *s1, int P, const float *points, float *iou,
+                   float *lowres);
+
 #ifdef __cplusplus
 }
 #endif

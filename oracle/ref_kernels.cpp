@@ -416,6 +416,37 @@ int ref_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
     return 0;
 }
 
+/* ---- convt_scatter: sam3_kernels.cl:766-781, host sam3_model.c:394-410 */
+struct ct_args {
+    const float *G;
+    float *out;
+    const float *bias, *add;
+    int H, W, Co, total, act;
+};
+static void k_ct(void *p) { ct_args *a = (ct_args *)p; ocl::convt_scatter(a->G, a->out, a->bias, a->add, a->H, a->W, a->Co, a->total, a->act); }
+
+void ref_convt_scatter(const float *G, float *out, const float *bias,
+                       const float *add, int P, int H, int W, int Co, int act)
+{
+    ct_args a = {G, out, bias, add, H, W, Co, P * 4 * H * W * Co, act};
+    run1d(k_ct, &a, (size_t)a.total);
+}
+
+/* ---- mask_logits: sam3_kernels.cl:789-807, host sam3_model.c:1387-1399 */
+struct ml_args {
+    const float *U, *hyper;
+    float *out;
+    int npix, total;
+};
+static void k_ml(void *p) { ml_args *a = (ml_args *)p; ocl::mask_logits(a->U, a->hyper, a->out, a->npix, a->total); }
+
+void ref_mask_logits(const float *U, const float *hyper, float *out, int npix,
+                     long total)
+{
+    ml_args a = {U, hyper, out, npix, (int)total};
+    run1d(k_ml, &a, (size_t)total);
+}
+
 int ref_num_threads(void) { return omp_get_max_threads(); }
 
 } // extern "C"

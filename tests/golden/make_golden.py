@@ -7,7 +7,7 @@ unmodified as host C++ by oracle/Makefile (oracle/_ref/libsam3ref.so), on
 inputs drawn from the seeded generator (include/sam3_synth.h). Only the
 outputs are stored; tests regenerate the inputs from the seeds.
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle && python tests/golden/make_golden.py [case names]
 
 Launch geometry is the reference host code's: layernorm with 256-item
 work-groups for rows of >= 1024 channels (sam3_model.c:320), softmax_rows
@@ -152,18 +152,42 @@ def cases():
     mha_case("mha_t2i_many", 2, 8, 300, 128, False, 910)
     mha_case("mha_t2i_shared", 2, 7, 1000, 128, True, 920)
     mha_case("mha_i2t_few", 2, 40, 7, 128, False, 930)
+
+    def convt_case(name, P, H, W, Co, act, with_add, stream):
+        def run(use_ref):
+            G = ob.normal(SEED, stream, (P * H * W, Co * 4))
+            bias = ob.normal(SEED, stream + 1, (Co,))
+            add = ob.normal(SEED, stream + 2, (4 * H * W * Co,)) if with_add else None
+            return {"out": ob.convt_scatter(G, bias, add, P, H, W, Co, act, use_ref=use_ref)}
+        out.append((name, run))
+
+    convt_case("convt_scatter_add", 2, 5, 3, 8, 0, True, 1000)
+    convt_case("convt_scatter_gelu", 3, 4, 4, 4, 1, True, 1010)
+    convt_case("convt_scatter_relu_noadd", 1, 3, 6, 12, 2, False, 1020)
+
+    def logits_case(name, P, npix, stream):
+        def run(use_ref):
+            U = ob.normal(SEED, stream, (P, npix, 32))
+            hyper = ob.normal(SEED, stream + 1, (P, 96))
+            return {"out": ob.mask_logits(U, hyper, P, npix, use_ref=use_ref)}
+        out.append((name, run))
+
+    logits_case("mask_logits", 3, 77, 1100)
     return out
 
 
-def main():
+def main(only=None):
+    """Write every case's fixture (or only the named ones)."""
     if not ob.have_ref():
         sys.exit("oracle/_ref/libsam3ref.so missing: run make -C oracle "
                  "where the reference tree is present")
     for name, run in cases():
+        if only and name not in only:
+            continue
         res = run(True)
         np.savez_compressed(os.path.join(HERE, name + ".npz"), **res)
         print(name, {k: v.shape for k, v in res.items()})
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or None)
