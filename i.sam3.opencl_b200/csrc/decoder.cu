@@ -2,10 +2,11 @@
 // Kernels of the point-prompt mask decoder around its attention
 // (sam3_model.c sam_decode :1239-1399): the ConvTranspose scatter of the
 // output upscaling, the mask logits, the hypernetwork / IoU heads that the
-// reference runs on the host, the positional-encoding add fused with the
-// cast of a GEMM operand, and the weight layout change of the ConvTranspose
+// reference runs on the host, the fused LayerNorm / upscaling passes of the
+// decoder's image stream, and the weight layout change of the ConvTranspose
 // GEMM operands.
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -141,29 +142,166 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
         iou[p * 3 + threadIdx.x] = 1.0f / (1.0f + expf(-hs[1 + threadIdx.x]));
 }
 
-// out = bf16(x[i] + a[i % amod]): the positional-encoding add of a decoder
-// Linear's input fused with its cast to the GEMM operand type; four values
-// per thread (n and amod multiples of 4, 16-byte aligned inputs).
-__global__ void __launch_bounds__(256) add_cast_kernel(const float4 *__restrict__ x,
-                                                       const float4 *__restrict__ a, long n4,
-                                                       long amod4, uint2 *__restrict__ out)
+__device__ __forceinline__ float warp_sum(float v)
 {
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi)
+{
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// LayerNorm of the decoder's image stream (256 channels, norm4 of the
+// image -> token attention, sam3_model.c:1309/1348) with the outputs its
+// consumers need written in the same pass: Y (fp32, may alias X; NULL =
+// not written), Yb = bf16(Y) (operand of the value projection and of the
+// first upscaling GEMM) and Yk = bf16(Y + pe[row % T]) (keys + dense
+// positional encoding, operand of the key / query projections). One warp
+// per row, 8 values per lane; two-pass mean / variance as the reference.
+__global__ void __launch_bounds__(256) ln_keys_kernel(const float *X, float *Y,
+                                                      const float *__restrict__ g,
+                                                      const float *__restrict__ b, long rows,
+                                                      float eps, const float *__restrict__ pe,
+                                                      int T, uint2 *__restrict__ Yb,
+                                                      uint2 *__restrict__ Yk)
+{
+    const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows)
+        return;
+    const float4 *x = reinterpret_cast<const float4 *>(X + row * 256);
+    float4 v[2] = {x[lane], x[32 + lane]};
+    const float mean =
+        warp_sum((v[0].x + v[0].y) + (v[0].z + v[0].w) + (v[1].x + v[1].y) + (v[1].z + v[1].w)) /
+        256.0f;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float a = v[i].x - mean, c = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
+        q += (a * a + c * c) + (d * d + e * e);
+    }
+    const float inv = rsqrtf(warp_sum(q) / 256.0f + eps);
+    const float4 *pr = reinterpret_cast<const float4 *>(pe + (row % T) * 256);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int c4 = i * 32 + lane;
+        const float4 gg = __ldg(reinterpret_cast<const float4 *>(g) + c4);
+        const float4 bt = __ldg(reinterpret_cast<const float4 *>(b) + c4);
+        float4 y;
+        y.x = (v[i].x - mean) * inv * gg.x + bt.x;
+        y.y = (v[i].y - mean) * inv * gg.y + bt.y;
+        y.z = (v[i].z - mean) * inv * gg.z + bt.z;
+        y.w = (v[i].w - mean) * inv * gg.w + bt.w;
+        if (Y)
+            reinterpret_cast<float4 *>(Y + row * 256)[c4] = y;
+        Yb[row * 64 + c4] = make_uint2(pack2(y.x, y.y), pack2(y.z, y.w));
+        const float4 p4 = __ldg(pr + c4);
+        Yk[row * 64 + c4] =
+            make_uint2(pack2(y.x + p4.x, y.y + p4.y), pack2(y.z + p4.z, y.w + p4.w));
+    }
+}
+
+// First output-upscaling stage in one pass (sam3_model.c:1355-1360): the
+// ConvTranspose 256 -> 64 scatter of G [P*72*72, 256] (column co*4 + dy*2 +
+// dx) + bias + feat_s1, LayerNorm2d over the 64 channels of each output
+// pixel (eps 1e-6), GELU, written as bf16 [P, 144, 144, 64] for the next
+// GEMM. One warp per input pixel: lane l holds G columns 8l..8l+7 (channels
+// 2l, 2l+1 of the four sub-pixels), so each output pixel's LayerNorm is a
+// warp reduction. The reference writes the fp32 map and normalises it in a
+// second kernel; the values are the same up to the order of the sums.
+__global__ void __launch_bounds__(256) up1_kernel(const float4 *__restrict__ G,
+                                                  const float *__restrict__ bias,
+                                                  const float *__restrict__ feat,
+                                                  const float *__restrict__ g,
+                                                  const float *__restrict__ b, float eps, int H,
+                                                  int W, long npix, uint32_t *__restrict__ out)
+{
+    const long ip = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (ip >= npix)
+        return;
+    const int x = (int)(ip % W);
+    const long py = ip / W;
+    const int y = (int)(py % H);
+    const long p = py / H;
+    const float4 a0 = G[ip * 64 + 2 * lane], a1 = G[ip * 64 + 2 * lane + 1];
+    const float ga[4] = {a0.x, a0.y, a0.z, a0.w}, gb[4] = {a1.x, a1.y, a1.z, a1.w};
+    const int c0 = 2 * lane;
+    const float b0 = __ldg(bias + c0), b1 = __ldg(bias + c0 + 1);
+    const float g0 = __ldg(g + c0), g1 = __ldg(g + c0 + 1);
+    const float t0 = __ldg(b + c0), t1 = __ldg(b + c0 + 1);
+#pragma unroll
+    for (int d = 0; d < 4; d++) {
+        const int oy = 2 * y + (d >> 1), ox = 2 * x + (d & 1);
+        const long opix = (long)oy * 2 * W + ox;
+        const float2 f = __ldg(reinterpret_cast<const float2 *>(feat + opix * 64) + lane);
+        const float v0 = (ga[d] + b0) + f.x, v1 = (gb[d] + b1) + f.y;
+        const float mean = warp_sum(v0 + v1) / 64.0f;
+        const float e0 = v0 - mean, e1 = v1 - mean;
+        const float inv = rsqrtf(warp_sum(e0 * e0 + e1 * e1) / 64.0f + eps);
+        const float y0 = act_fn(e0 * inv * g0 + t0, K_ACT_GELU);
+        const float y1 = act_fn(e1 * inv * g1 + t1, K_ACT_GELU);
+        out[(p * 4L * H * W + opix) * 32 + lane] = pack2(y0, y1);
+    }
+}
+
+// Second output-upscaling stage fused with the mask logits
+// (sam3_model.c:1361-1366, 1387-1399). g2 [P*H*W, 128] holds the
+// ConvTranspose 64 -> 32 GEMM in sub-pixel-major columns d * 32 + co (the
+// weight rows are stored in that order), so the 32 channels of output
+// pixel (2y + dy, 2x + dx), d = 2 dy + dx, are one 128-byte run. One thread
+// per output pixel: GELU((g2 + bias) + feat_s0) of its 32 channels, dotted
+// with the prompt's three hypernetwork vectors; the [P, 288, 288, 32] map
+// of the reference is never stored. GELU uses the Abramowitz-Stegun erf
+// (gelu_as); four consecutive threads share one input pixel.
+__global__ void __launch_bounds__(256) up2_logits_kernel(const float4 *__restrict__ G,
+                                                         const float *__restrict__ bias,
+                                                         const float *__restrict__ feat,
+                                                         const float *__restrict__ hyper, int H,
+                                                         int W, long nsub,
+                                                         float *__restrict__ out)
+{
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nsub;
          i += (long)gridDim.x * blockDim.x) {
-        const float4 v = x[i], w = __ldg(a + i % amod4);
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x + w.x, v.y + w.y);
-        __nv_bfloat162 hi = __floats2bfloat162_rn(v.z + w.z, v.w + w.w);
-        uint2 o;
-        o.x = *reinterpret_cast<uint32_t *>(&lo);
-        o.y = *reinterpret_cast<uint32_t *>(&hi);
-        out[i] = o;
+        const long ip = i >> 2;
+        const int d = (int)(i & 3);
+        const int x = (int)(ip % W);
+        const long py = ip / W;
+        const int y = (int)(py % H);
+        const long p = py / H;
+        const long opix = (long)(2 * y + (d >> 1)) * 2 * W + 2 * x + (d & 1);
+        const float4 *g = G + ip * 32 + d * 8;
+        const float4 *f = reinterpret_cast<const float4 *>(feat + opix * 32);
+        const float4 *bq = reinterpret_cast<const float4 *>(bias);
+        const float4 *h = reinterpret_cast<const float4 *>(hyper + p * 96);
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float4 gv = g[j], fv = __ldg(f + j), bv = __ldg(bq + j);
+            const float4 h0 = __ldg(h + j), h1 = __ldg(h + 8 + j), h2 = __ldg(h + 16 + j);
+            const float u0 = gelu_as((gv.x + bv.x) + fv.x), u1 = gelu_as((gv.y + bv.y) + fv.y);
+            const float u2 = gelu_as((gv.z + bv.z) + fv.z), u3 = gelu_as((gv.w + bv.w) + fv.w);
+            a0 = fmaf(u3, h0.w, fmaf(u2, h0.z, fmaf(u1, h0.y, fmaf(u0, h0.x, a0))));
+            a1 = fmaf(u3, h1.w, fmaf(u2, h1.z, fmaf(u1, h1.y, fmaf(u0, h1.x, a1))));
+            a2 = fmaf(u3, h2.w, fmaf(u2, h2.z, fmaf(u1, h2.y, fmaf(u0, h2.x, a2))));
+        }
+        const long onpix = 4L * H * W;
+        out[(p * 3 + 0) * onpix + opix] = a0;
+        out[(p * 3 + 1) * onpix + opix] = a1;
+        out[(p * 3 + 2) * onpix + opix] = a2;
     }
 }
 
 // src [rows, cols] fp32 -> dst [cols, rows] bf16 (round to nearest even),
-// through 32 x 32 shared-memory tiles.
+// through 32 x 32 shared-memory tiles. With dmajor, source column
+// c = co * 4 + d becomes destination row d * (cols / 4) + co.
 __global__ void transpose_cast_kernel(const float *__restrict__ src, int rows, int cols,
-                                      __nv_bfloat16 *__restrict__ dst)
+                                      int dmajor, __nv_bfloat16 *__restrict__ dst)
 {
     __shared__ float tile[32][33];
     const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
@@ -175,8 +313,9 @@ __global__ void transpose_cast_kernel(const float *__restrict__ src, int rows, i
     __syncthreads();
     for (int j = threadIdx.y; j < 32; j += 8) {
         const int c = c0 + j, r = r0 + threadIdx.x;
+        const int oc = dmajor ? (c & 3) * (cols >> 2) + (c >> 2) : c;
         if (r < rows && c < cols)
-            dst[(long)c * rows + r] = __float2bfloat16_rn(tile[threadIdx.x][j]);
+            dst[(long)oc * rows + r] = __float2bfloat16_rn(tile[threadIdx.x][j]);
     }
 }
 
@@ -221,26 +360,51 @@ extern "C" int k_dec_heads(const float *tok, int P, const k_dec_heads_w *hw, flo
     return (int)cudaGetLastError();
 }
 
-extern "C" int k_add_cast_bf16(const float *x, const float *a, long n, long amod, void *out,
-                               k_stream s)
+extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor, void *dst,
+                                     k_stream s)
 {
-    if (n < 0 || amod <= 0 || (n & 3) || (amod & 3) || (reinterpret_cast<uintptr_t>(x) & 15) ||
-        (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
+    if (rows <= 0 || cols <= 0 || (dmajor && (cols & 3)))
         return K_EARG;
-    if (n == 0)
-        return 0;
-    const int grid = grid_for(n / 4, 256);
-    add_cast_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(
-        reinterpret_cast<const float4 *>(x), reinterpret_cast<const float4 *>(a), n / 4, amod / 4,
-        reinterpret_cast<uint2 *>(out));
+    transpose_cast_kernel<<<dim3((cols + 31) / 32, (rows + 31) / 32), dim3(32, 8), 0, STREAM(s)>>>(
+        src, rows, cols, dmajor, reinterpret_cast<__nv_bfloat16 *>(dst));
     return (int)cudaGetLastError();
 }
 
-extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, void *dst, k_stream s)
+extern "C" int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b, long rows,
+                             float eps, const float *pe, int T, void *Yb, void *Yk, k_stream s)
 {
-    if (rows <= 0 || cols <= 0)
+    if (rows <= 0 || T <= 0 || !Yb || !Yk || (reinterpret_cast<uintptr_t>(X) & 15) ||
+        (reinterpret_cast<uintptr_t>(Y) & 15) || (reinterpret_cast<uintptr_t>(pe) & 15) ||
+        (reinterpret_cast<uintptr_t>(Yb) & 7) || (reinterpret_cast<uintptr_t>(Yk) & 7))
         return K_EARG;
-    transpose_cast_kernel<<<dim3((cols + 31) / 32, (rows + 31) / 32), dim3(32, 8), 0, STREAM(s)>>>(
-        src, rows, cols, reinterpret_cast<__nv_bfloat16 *>(dst));
+    ln_keys_kernel<<<grid_for(rows, 8), 256, 0, STREAM(s)>>>(
+        X, Y, g, b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb), reinterpret_cast<uint2 *>(Yk));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_dec_up1(const float *G, const float *bias, const float *feat, const float *g,
+                         const float *b, float eps, int P, int H, int W, void *out, k_stream s)
+{
+    if (P <= 0 || H <= 0 || W <= 0 || (reinterpret_cast<uintptr_t>(G) & 15) ||
+        (reinterpret_cast<uintptr_t>(feat) & 7) || (reinterpret_cast<uintptr_t>(out) & 3))
+        return K_EARG;
+    const long npix = (long)P * H * W;
+    up1_kernel<<<grid_for(npix, 8), 256, 0, STREAM(s)>>>(reinterpret_cast<const float4 *>(G), bias,
+                                                         feat, g, b, eps, H, W, npix,
+                                                         reinterpret_cast<uint32_t *>(out));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_dec_up2_logits(const float *G, const float *bias, const float *feat,
+                                const float *hyper, int P, int H, int W, float *out, k_stream s)
+{
+    if (P <= 0 || H <= 0 || W <= 0 || (reinterpret_cast<uintptr_t>(G) & 15) ||
+        (reinterpret_cast<uintptr_t>(feat) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15) ||
+        (reinterpret_cast<uintptr_t>(hyper) & 15))
+        return K_EARG;
+    const long nsub = 4L * P * H * W;
+    const int grid = grid_for(nsub, 256);
+    up2_logits_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(
+        reinterpret_cast<const float4 *>(G), bias, feat, hyper, H, W, nsub, out);
     return (int)cudaGetLastError();
 }

@@ -294,6 +294,18 @@ __global__ void patch_embed_in_kernel(const uint8_t *__restrict__ rgb, int ntile
     *reinterpret_cast<uint4 *>(out + row * kpad + g0) = p;
 }
 
+// Eight values per thread: two 16-byte loads, one 16-byte store.
+__global__ void cast_f32_bf16_v8_kernel(const float4 *__restrict__ x, uint4 *__restrict__ y,
+                                        long n8)
+{
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (long)gridDim.x * blockDim.x) {
+        const float4 a = x[2 * i], b = x[2 * i + 1];
+        y[i] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                          pack_bf16x2(b.z, b.w));
+    }
+}
+
 __global__ void cast_f32_bf16_kernel(const float *x, __nv_bfloat16 *y, long n)
 {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -469,6 +481,12 @@ extern "C" int k_cast_f32_bf16(const float *x, void *y, long n, k_stream s)
 {
     if (n <= 0)
         return 0;
+    if (n % 8 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 15)) {
+        const int g = grid_for(n / 8, 256);
+        cast_f32_bf16_v8_kernel<<<g < 148 * 16 ? g : 148 * 16, 256, 0, STREAM(s)>>>(
+            reinterpret_cast<const float4 *>(x), reinterpret_cast<uint4 *>(y), n / 8);
+        LAUNCH_RET();
+    }
     cast_f32_bf16_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
         x, reinterpret_cast<__nv_bfloat16 *>(y), n);
     LAUNCH_RET();

@@ -115,11 +115,25 @@ struct k_dec_heads_w {
 };
 int k_dec_heads(const float *tok, int P, const struct k_dec_heads_w *hw,
                 float *hyper, float *iou, k_stream s);
-/* out = bf16(x[i] + a[i % amod]), i < n. */
-int k_add_cast_bf16(const float *x, const float *a, long n, long amod,
-                    void *out, k_stream s);
-int k_transpose_cast_bf16(const float *src, int rows, int cols, void *dst,
-                          k_stream s);
+int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor,
+                          void *dst, k_stream s);
+/* Decoder fusions. ln_keys: LayerNorm of 256-wide rows, Y fp32 (may alias
+ * X, NULL = skipped), Yb = bf16(Y), Yk = bf16(Y + pe[row % T]). up1:
+ * ConvT 256 -> 64 scatter of G [P*H*W, 256] + bias + feat [4HW, 64],
+ * LayerNorm2d (g, b, eps), GELU -> bf16 [P, 2H, 2W, 64]. up2_logits: ConvT
+ * 64 -> 32 scatter of G [P*H*W, 128] (sub-pixel-major columns d*32 + co)
+ * + bias + feat [4HW, 32], GELU, dotted with hyper [P, 96] -> out
+ * [P, 3, 2H * 2W]. transpose_cast with dmajor: source column co*4 + d
+ * becomes row d * cols/4 + co. */
+int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b,
+                  long rows, float eps, const float *pe, int T, void *Yb,
+                  void *Yk, k_stream s);
+int k_dec_up1(const float *G, const float *bias, const float *feat,
+              const float *g, const float *b, float eps, int P, int H, int W,
+              void *out, k_stream s);
+int k_dec_up2_logits(const float *G, const float *bias, const float *feat,
+                     const float *hyper, int P, int H, int W, float *out,
+                     k_stream s);
 
 /* uint8 HWC tiles -> bf16 patch rows in window-major token order:
  * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight

@@ -6,18 +6,23 @@
  * Data flow and precision. The token stream (P * 8 rows of 256) and the
  * per-prompt image stream ("keys", P * 5184 rows of 256) stay fp32, as in
  * the reference; every Linear runs on the tcgen05 GEMM with bf16 operands
- * and fp32 accumulation, its fp32 input rounded to bf16 once (fused with
- * the positional-encoding add where the reference adds one first). The
- * decoder attention (k_mha) reads fp32 Q/K/V. Fusions against the
- * reference's op sequence:
+ * and fp32 accumulation, its fp32 input rounded to bf16 once. The decoder
+ * attention (k_mha) reads fp32 Q/K/V. Fusions against the reference's op
+ * sequence:
  *   - keys = Linear(bo) + src: the add_bcast of src (shared by all
  *     prompts) is the GEMM epilogue's residual with row m % 5184;
- *   - the LayerNorm2d + GELU of the output upscaling writes bf16, the
- *     operand of the next ConvTranspose GEMM;
+ *   - the LayerNorm of keys (norm4) also writes bf16(keys) and
+ *     bf16(keys + dense PE), the operands of the next token -> image
+ *     attention's projections, of layer 1's image queries and of the first
+ *     upscaling GEMM: no separate add_bcast or cast passes over keys;
  *   - the ConvTranspose weights are stored as [cout * 4, cin] bf16, so both
- *     upscaling GEMMs are plain tcgen05 GEMMs followed by the scatter;
+ *     upscaling convolutions are plain tcgen05 GEMMs; the first one's
+ *     scatter + feat_s1 + LayerNorm2d + GELU is one pass writing bf16, the
+ *     second one's scatter + feat_s0 + GELU is dotted with the
+ *     hypernetwork outputs in the same pass, so the [P, 288, 288, 32] map
+ *     is never stored;
  *   - the hypernetwork and IoU MLPs run on the device (dec_heads), so the
- *     decode does not stop for a host round trip before mask_logits.
+ *     decode does not stop for a host round trip before the logits.
  * Everything runs on the backend stream; cb_decode blocks only to return
  * the IoU predictions. */
 #include <math.h>
@@ -72,10 +77,8 @@ struct cb_decoder {
     float *bq, *bk, *bv, *bo;   /* [batch * T, 128] */
     void *bo_bf16;              /* bf16 [batch * T, 128] */
     float *G;                   /* [batch * T, 256], first ConvT GEMM */
-    float *u1;                  /* [batch * 4T, 64] */
-    void *u1_bf16;
+    void *u1_bf16;              /* bf16 [batch * 4T, 64] */
     float *g2;                  /* [batch * 4T, 128] */
-    float *u2;                  /* [batch * 16T, 32] */
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
     void *mha_ws;
     size_t mha_ws_bytes;
@@ -107,7 +110,7 @@ void cb_decoder_free(cb_decoder *d)
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->qin, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
-                       d->bv, d->bo, d->bo_bf16, d->G, d->u1, d->u1_bf16, d->g2, d->u2,
+                       d->bv, d->bo, d->bo_bf16, d->G, d->u1_bf16, d->g2,
                        d->hyper, d->iou, d->mha_ws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
@@ -174,10 +177,8 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->bo, B * T * 128 * 4);
     A(d->bo_bf16, B * T * 128 * 2);
     A(d->G, B * T * 256 * 4);
-    A(d->u1, B * 4 * T * 64 * 4);
     A(d->u1_bf16, B * 4 * T * 64 * 2);
     A(d->g2, B * 4 * T * 128 * 4);
-    A(d->u2, B * 16 * T * 32 * 4);
     A(d->hyper, B * 96 * 4);
     A(d->iou, B * 3 * 4);
     ws_t2i = k_mha_workspace(batch, DEC_NTOK, DEC_T, 128, b->num_sms);
@@ -261,8 +262,12 @@ static int store_tensor(cb_decoder *d, int i, const float *f32)
     int r, c, k;
 
     sam3_dec_tensor(i, &r, &c, &k);
+    /* ConvTranspose weights [cin, cout * 4] -> GEMM operands [cout * 4, cin];
+     * the second one's rows in sub-pixel-major order d * 32 + co, the
+     * column order its fused scatter + logits pass reads. */
     if (i == SAM3_DT_UP0_W || i == SAM3_DT_UP3_W)
-        return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, d->w[i], st), "decoder weights");
+        return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, i == SAM3_DT_UP3_W, d->w[i], st),
+                           "decoder weights");
     if (is_gemm_weight(i))
         return cbi_kstatus(b, k_cast_f32_bf16(f32, d->w[i], (long)r * c, st), "decoder weights");
     return cbi_kstatus(b,
@@ -369,17 +374,6 @@ static int lin32(cb_decoder *d, const char *name, const float *X, void *xs, long
     return lin16(d, name, xs, rows, in, out, wi, bi, Y, R, rmod, act);
 }
 
-/* xs = bf16(X + A[i % amod]): the positional-encoding add fused with the
- * cast of a GEMM operand. */
-static int add_cast(cb_decoder *d, const float *X, const float *A, long n, long amod, void *xs)
-{
-    cb_backend *b = d->b;
-
-    LAUNCH("dec_add_cast", (double)n, (double)n * 10,
-           k_add_cast_bf16(X, A, n, amod, xs, (k_stream)b->stream));
-    return CB_OK;
-}
-
 static int ln(cb_decoder *d, float *X, void *Y, int y_bf16, long rows, int C, int wi, int bi,
               float eps, int act)
 {
@@ -457,19 +451,20 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_
 /* ---------------------------------------------------------------- decode */
 
 /* Token -> image attention on per-prompt keys, residual into the queries
- * (t2i_attention, sam3_model.c:1212-1229). kin = keys + dense PE is kept in
- * bf16: layer 1's image -> token queries read it again. */
+ * (t2i_attention, sam3_model.c:1212-1229). Its image-side operands, keys and
+ * kin = keys + dense PE in bf16, were written by the LayerNorm that ended
+ * the previous image -> token attention (ln_keys); kin serves layer 1's
+ * image -> token queries as well. */
 static int t2i_attention(cb_decoder *d, int P, int blk)
 {
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
 
     CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-    CB_TRY(add_cast(d, d->keys, d->pe_img, rows * DEC_DIM, (long)DEC_T * DEC_DIM, d->kin_bf16));
     CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, QW),
                  ATT(blk, QB), d->sq, NULL, 0, K_ACT_NONE));
     CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
                  d->bk, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_img", d->keys, d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
+    CB_TRY(lin16(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
                  ATT(blk, VB), d->bv, NULL, 0, K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->bk, (long)DEC_T * 128, d->bv,
                (long)DEC_T * 128, d->so));
@@ -517,7 +512,10 @@ static int self_attention(cb_decoder *d, int P, int l)
  * queries from the image stream (the shared layer-0 projection, or kin of
  * layer 1), keys and values from the tokens; the output projection lands
  * in keys, + src (layer 0: the add_bcast of sam3_model.c:1307 as the GEMM
- * residual with row m % T) or + keys (layer 1), then norm4. */
+ * residual with row m % T) or + keys (layer 1), then norm4, which also
+ * writes the bf16 operands keys and keys + PE of the next token -> image
+ * attention (and of the upscaling). After layer 1 nothing reads the fp32
+ * keys again, so that LayerNorm writes only the bf16 copies. */
 static int i2t_attention(cb_decoder *d, int P, int l)
 {
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
@@ -535,8 +533,15 @@ static int i2t_attention(cb_decoder *d, int P, int l)
                DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo));
     CB_TRY(lin32(d, "dec_gemm_img", d->bo, d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW),
                  ATT(blk, OB), d->keys, l ? d->keys : d->src, l ? 0 : DEC_T, K_ACT_NONE));
-    return ln(d, d->keys, d->keys, 0, rows, DEC_DIM, LAY(l, N4W), LAY(l, N4B), DEC_EPS,
-              K_ACT_NONE);
+    {
+        cb_backend *b = d->b;
+
+        LAUNCH("dec_ln_keys", 8.0 * rows * DEC_DIM, (double)rows * DEC_DIM * (l ? 8 : 12),
+               k_dec_ln_keys(d->keys, l ? NULL : d->keys, (const float *)d->w[LAY(l, N4W)],
+                             (const float *)d->w[LAY(l, N4B)], rows, DEC_EPS, d->pe_img, DEC_T,
+                             d->keys_bf16, d->kin_bf16, (k_stream)b->stream));
+    }
+    return CB_OK;
 }
 
 /* Prompt tokens (sam3_model.c:1249-1263): object score token, IoU token,
@@ -620,25 +625,9 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, SAM3_DT_NF_W, SAM3_DT_NF_B, DEC_EPS,
               K_ACT_NONE));
 
-    /* Output upscaling (sam3_model.c:1353-1366): ConvT 256 -> 64 (+ feat_s1),
-     * LayerNorm2d + GELU, ConvT 64 -> 32 (+ feat_s0), GELU. */
-    LAUNCH("dec_cast", 0, (double)rows * DEC_DIM * 6,
-           k_cast_f32_bf16(d->keys, d->keys_bf16, rows * DEC_DIM, (k_stream)b->stream));
-    CB_TRY(lin16(d, "dec_gemm_up", d->keys_bf16, rows, DEC_DIM, 256, SAM3_DT_UP0_W, -1, d->G,
-                 NULL, 0, K_ACT_NONE));
-    LAUNCH("dec_convt", 0, (double)rows * 256 * 8,
-           k_convt_scatter(d->G, d->u1, (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1, P,
-                           DEC_GRID, DEC_GRID, 64, K_ACT_NONE, (k_stream)b->stream));
-    CB_TRY(ln(d, d->u1, d->u1_bf16, 1, 4 * rows, 64, SAM3_DT_UP1_W, SAM3_DT_UP1_B, LN2D_EPS,
-              K_ACT_GELU));
-    CB_TRY(lin16(d, "dec_gemm_up", d->u1_bf16, 4 * rows, 64, 128, SAM3_DT_UP3_W, -1, d->g2,
-                 NULL, 0, K_ACT_NONE));
-    LAUNCH("dec_convt", 0, (double)4 * rows * 128 * 8,
-           k_convt_scatter(d->g2, d->u2, (const float *)d->w[SAM3_DT_UP3_B], d->feat_s0, P,
-                           2 * DEC_GRID, 2 * DEC_GRID, 32, K_ACT_GELU, (k_stream)b->stream));
-
-    /* Hypernetwork MLPs 1..3 and the IoU head on the final tokens, then the
-     * low-resolution logits of the three multimask outputs. */
+    /* Hypernetwork MLPs 1..3 and the IoU head on the final tokens
+     * (sam3_model.c:1368-1386), first: the last upscaling stage takes their
+     * outputs. */
     for (m = 0; m < 4; m++)
         for (l = 0; l < 3; l++) {
             const int base = m < 3 ? SAM3_DT_HYPER + 6 * (m + 1) : SAM3_DT_IOU;
@@ -648,10 +637,25 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
         }
     LAUNCH("dec_heads", 2.0 * P * 4 * (2 * 65536.0 + 32 * 256), (double)P * 4 * 2 * 65536 * 4,
            k_dec_heads(d->qry, P, &heads, d->hyper, d->iou, (k_stream)b->stream));
-    LAUNCH("dec_mask_logits", 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
-           (double)P * DEC_LOWRES * DEC_LOWRES * (32 + 3) * 4,
-           k_mask_logits(d->u2, d->hyper, (float *)lowres->ptr, P, DEC_LOWRES * DEC_LOWRES,
-                         (k_stream)b->stream));
+
+    /* Output upscaling (sam3_model.c:1353-1366) and mask_logits
+     * (:1387-1399): ConvT 256 -> 64 as a GEMM on the bf16 keys, then its
+     * scatter + feat_s1 + LayerNorm2d + GELU in one pass to bf16; ConvT
+     * 64 -> 32 as a GEMM, then its scatter + feat_s0 + GELU dotted with the
+     * hypernetwork outputs in one pass, straight to the logits. */
+    CB_TRY(lin16(d, "dec_gemm_up", d->keys_bf16, rows, DEC_DIM, 256, SAM3_DT_UP0_W, -1, d->G,
+                 NULL, 0, K_ACT_NONE));
+    LAUNCH("dec_up1", 0, (double)rows * 256 * 4 + (double)rows * 4 * 64 * 2,
+           k_dec_up1(d->G, (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1,
+                     (const float *)d->w[SAM3_DT_UP1_W], (const float *)d->w[SAM3_DT_UP1_B],
+                     LN2D_EPS, P, DEC_GRID, DEC_GRID, d->u1_bf16, (k_stream)b->stream));
+    CB_TRY(lin16(d, "dec_gemm_up", d->u1_bf16, 4 * rows, 64, 128, SAM3_DT_UP3_W, -1, d->g2,
+                 NULL, 0, K_ACT_NONE));
+    LAUNCH("dec_up2_logits", 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
+           (double)4 * rows * 128 * 4 + (double)P * 3 * DEC_LOWRES * DEC_LOWRES * 4,
+           k_dec_up2_logits(d->g2, (const float *)d->w[SAM3_DT_UP3_B], d->feat_s0, d->hyper, P,
+                            2 * DEC_GRID, 2 * DEC_GRID, (float *)lowres->ptr,
+                            (k_stream)b->stream));
     CB_TRY(cbi_kstatus(b,
                        (int)cudaMemcpyAsync(iou, d->iou, (size_t)P * 3 * 4,
                                             cudaMemcpyDeviceToHost, b->stream),
