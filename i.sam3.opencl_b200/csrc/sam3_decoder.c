@@ -363,7 +363,8 @@ static int lin16(cb_decoder *d, const char *name, const void *Xb, long rows, int
     return CB_OK;
 }
 
-/* The same on an fp32 X, rounded to bf16 into xs first. */
+/* The same on an fp32 X of the image stream, rounded to bf16 into xs
+ * first. */
 static int lin32(cb_decoder *d, const char *name, const float *X, void *xs, long rows, int in,
                  int out, int wi, int bi, float *Y, const float *R, int rmod, int act)
 {
@@ -372,6 +373,15 @@ static int lin32(cb_decoder *d, const char *name, const float *X, void *xs, long
     LAUNCH("dec_cast", 0, (double)rows * in * 6,
            k_cast_f32_bf16(X, xs, rows * in, (k_stream)b->stream));
     return lin16(d, name, xs, rows, in, out, wi, bi, Y, R, rmod, act);
+}
+
+/* A Linear of the token stream (8 rows per prompt): Y = act(X W^T + bias)
+ * (+ Y when residual), X rounded to bf16 into the token operand buffer. */
+static int lintok(cb_decoder *d, const float *X, long rows, int in, int out, int wi, int bi,
+                  float *Y, int residual, int act)
+{
+    return lin32(d, "dec_gemm_tok", X, d->tok_bf16, rows, in, out, wi, bi, Y,
+                 residual ? Y : NULL, 0, act);
 }
 
 static int ln(cb_decoder *d, float *X, void *Y, int y_bf16, long rows, int C, int wi, int bi,
@@ -460,16 +470,15 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
 
     CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, QW),
-                 ATT(blk, QB), d->sq, NULL, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
+                  K_ACT_NONE));
     CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
                  d->bk, NULL, 0, K_ACT_NONE));
     CB_TRY(lin16(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
                  ATT(blk, VB), d->bv, NULL, 0, K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->bk, (long)DEC_T * 128, d->bv,
                (long)DEC_T * 128, d->so));
-    return lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, 128, DEC_DIM, ATT(blk, OW),
-                 ATT(blk, OB), d->qry, d->qry, 0, K_ACT_NONE);
+    return lintok(d, d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, 1, K_ACT_NONE);
 }
 
 /* token_mlp (sam3_model.c:1231-1237): 256 -> 2048 (ReLU) -> 256, residual. */
@@ -477,10 +486,8 @@ static int token_mlp(cb_decoder *d, int P, int l)
 {
     const long nt = (long)P * DEC_NTOK;
 
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, 2048, LAY(l, M1W),
-                 LAY(l, M1B), d->sh, NULL, 0, K_ACT_RELU));
-    return lin32(d, "dec_gemm_tok", d->sh, d->tok_bf16, nt, 2048, DEC_DIM, LAY(l, M2W),
-                 LAY(l, M2B), d->qry, d->qry, 0, K_ACT_NONE);
+    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 2048, LAY(l, M1W), LAY(l, M1B), d->sh, 0, K_ACT_RELU));
+    return lintok(d, d->sh, nt, 2048, DEC_DIM, LAY(l, M2W), LAY(l, M2B), d->qry, 1, K_ACT_NONE);
 }
 
 /* Self attention of the tokens; layer 0 without positional encoding and
@@ -496,16 +503,14 @@ static int self_attention(cb_decoder *d, int P, int l)
         CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
         qk = d->qin;
     }
-    CB_TRY(lin32(d, "dec_gemm_tok", qk, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, QW),
-                 ATT(blk, QB), d->sq, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_tok", qk, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, KW),
-                 ATT(blk, KB), d->sk, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, VW),
-                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, qk, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, qk, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
+                  K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_NTOK, DEC_DIM, d->sq, DEC_NTOK * DEC_DIM, d->sk,
                DEC_NTOK * DEC_DIM, d->sv, DEC_NTOK * DEC_DIM, d->so));
-    return lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, OW),
-                 ATT(blk, OB), d->qry, l ? d->qry : NULL, 0, K_ACT_NONE);
+    return lintok(d, d->so, nt, DEC_DIM, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, l,
+                  K_ACT_NONE);
 }
 
 /* Image -> token attention of layer l (sam3_model.c:1297-1309, 1334-1348):
@@ -525,10 +530,10 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     if (l)
         CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, QW),
                      ATT(blk, QB), d->bq, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, KW),
-                 ATT(blk, KB), d->sk, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->tok_bf16, nt, DEC_DIM, 128, ATT(blk, VW),
-                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
+                  K_ACT_NONE));
+    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
+                  K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_T, DEC_NTOK, 128, l ? d->bq : d->qp0, l ? (long)DEC_T * 128 : 0, d->sk,
                DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo));
     CB_TRY(lin32(d, "dec_gemm_img", d->bo, d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW),
@@ -600,12 +605,11 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     CB_TRY(self_attention(d, P, 0));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N1W), LAY(0, N1B), DEC_EPS, K_ACT_NONE));
     CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qin, d->tok_bf16, nt, DEC_DIM, 128,
-                 ATT(SAM3_DA_L0_T2I, QW), ATT(SAM3_DA_L0_T2I, QB), d->sq, NULL, 0, K_ACT_NONE));
+    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
+                  ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->kp0, 0, d->vp0, 0, d->so));
-    CB_TRY(lin32(d, "dec_gemm_tok", d->so, d->tok_bf16, nt, 128, DEC_DIM,
-                 ATT(SAM3_DA_L0_T2I, OW), ATT(SAM3_DA_L0_T2I, OB), d->qry, d->qry, 0,
-                 K_ACT_NONE));
+    CB_TRY(lintok(d, d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
+                  ATT(SAM3_DA_L0_T2I, OB), d->qry, 1, K_ACT_NONE));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N2W), LAY(0, N2B), DEC_EPS, K_ACT_NONE));
     CB_TRY(token_mlp(d, P, 0));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N3W), LAY(0, N3B), DEC_EPS, K_ACT_NONE));
