@@ -299,6 +299,57 @@ def decoder_bench(cb, torch, pk, iters=10):
     return res
 
 
+NECK_TILES = 8
+# multiply-adds per token of point_neck (E = 1024): ConvT 1024->512 (x2
+# levels), ConvT 512->256 (4 sub-pixels), 1x1 and 3x3 convolutions and the
+# conv_s0 / conv_s1 projections at 16x, 4x and 1x the token count
+NECK_MAC_PER_TOKEN = (2 * 1024 * 2048 + 4 * 512 * 1024 + 16 * 256 * 256 + 16 * 2304 * 256
+                      + 16 * 256 * 32 + 4 * 512 * 256 + 4 * 2304 * 256 + 4 * 256 * 64
+                      + 1024 * 256 + 2304 * 256)
+
+
+def neck_bench(sb, cb, torch, iters=5):
+    """The SimpleFPN neck (cb_neck_run) on NECK_TILES trunk outputs per call,
+    random-init weights, synthetic fp32 tokens; device-timed, plus one
+    profiled call for the per-kernel shares."""
+    stream = torch.cuda.ExternalStream(cb.stream)
+    T = 5184
+    neck = sb.Neck(cb, grid=72, embed=1024, max_tiles=NECK_TILES)
+    neck.init_random(SEED, 0.02)
+    x = cb.alloc(NECK_TILES * T * 1024 * 4, sb.F32)
+    cb.synth_normal(SEED, 9400, 0.0, 1.0, x, NECK_TILES * T * 1024)
+    outs = [cb.alloc(NECK_TILES * T * 256 * 4, sb.F32),
+            cb.alloc(NECK_TILES * 16 * T * 32 * 4, sb.F32),
+            cb.alloc(NECK_TILES * 4 * T * 64 * 4, sb.F32)]
+    times = []
+    for it in range(iters + 2):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        neck.run(x, NECK_TILES, *outs)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 2:
+            times.append(e0.elapsed_time(e1))
+    cb.profile(True)
+    neck.run(x, NECK_TILES, *outs)
+    cb.profile(False)
+    prof = cb.profile_table()
+    neck.close()
+    t = statistics.median(times)
+    flop = 2.0 * NECK_MAC_PER_TOKEN * T * NECK_TILES
+    total = sum(v["ms"] for v in prof.values())
+    kernels = {k: {"share": v["ms"] / total, "launches": v["calls"],
+                   "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9,
+                   "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12 if v["flops"] else None}
+               for k, v in prof.items()}
+    return {"tiles": NECK_TILES, "ms_per_call": t, "ms_per_tile": t / NECK_TILES,
+            "tflops": flop / (t * 1e-3) / 1e12, "gflop_per_tile": flop / NECK_TILES / 1e9,
+            "kernels": kernels,
+            "work": "cb_neck_run: point_neck of 8 tiles (72 x 72 x 1024 fp32 tokens) "
+                    "-> emb, feat_s0, feat_s1"}
+
+
 MASK_P = 64  # prompts per decode (config 3: batches of 64)
 
 
@@ -398,6 +449,14 @@ def cpu_configs_sample():
     ob.sam_decode(w, *img, pts)
     t = time.perf_counter() - t0
     out["mask_decoder_2_prompts"] = {"s": t, "prompts_per_s": 2 / t, "kind": "port"}
+    # the neck on one tile, oracle restatement (im2col pinned to the reference)
+    x = ob.normal(SEED, 9400, (5184, 1024))
+    nw = ob.NeckWeights(SEED, 0.02)
+    t0 = time.perf_counter()
+    ob.point_neck(nw, x, 72)
+    t = time.perf_counter() - t0
+    out["neck_1_tile"] = {"s": t, "tflops": 2.0 * NECK_MAC_PER_TOKEN * 5184 / t / 1e12,
+                          "kind": "port"}
     return out
 
 
@@ -492,6 +551,7 @@ def our_arm(args, world, rank, local, pg):
         attn = attention_bench(sb, cb, torch, pk)
         dec = decoder_bench(cb, torch, pk)
         mdec = mask_decoder_bench(sb, cb, torch)
+        nk = neck_bench(sb, cb, torch)
         line = {
             "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -511,6 +571,7 @@ def our_arm(args, world, rank, local, pg):
             "attention": attn,
             "decoder_attention": dec,
             "mask_decoder": mdec,
+            "neck": nk,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
                     "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
                     "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},

@@ -37,7 +37,8 @@ EXPORTS = [
     "cb_encode_tiles_host", "cb_synth_normal", "cb_diag_exp2",
     "cb_convt_scatter", "cb_mask_logits", "cb_decoder_create", "cb_decoder_free",
     "cb_decoder_init_random", "cb_decoder_set_weight", "cb_decoder_set_image",
-    "cb_decode",
+    "cb_decode", "cb_neck_create", "cb_neck_free", "cb_neck_init_random",
+    "cb_neck_set_weight", "cb_neck_run",
     "sam3_synth_normal", "sam3_synth_u8", "sam3_synth_rope_axial",
 ]
 
@@ -163,6 +164,11 @@ def lib():
         "cb_decoder_set_weight": (i32, [vp, i32, vp, sz]),
         "cb_decoder_set_image": (i32, [vp, vp, vp, vp]),
         "cb_decode": (i32, [vp, i32, vp, vp, vp]),
+        "cb_neck_create": (i32, [vp, i32, i32, i32, C.POINTER(vp)]),
+        "cb_neck_free": (None, [vp]),
+        "cb_neck_init_random": (i32, [vp, C.c_uint64, f32]),
+        "cb_neck_set_weight": (i32, [vp, i32, vp, sz]),
+        "cb_neck_run": (i32, [vp, vp, i32, vp, vp, vp]),
         "sam3_synth_normal": (None, [C.c_uint64, C.c_uint64, sz, f32, f32, vp]),
         "sam3_synth_u8": (None, [C.c_uint64, C.c_uint64, sz, vp]),
         "sam3_synth_rope_axial": (None, [i32, i32, C.c_double, vp]),
@@ -458,4 +464,34 @@ class Decoder:
     def close(self):
         if self.h:
             lib().cb_decoder_free(self.h)
+            self.h = C.c_void_p(None)
+
+
+NECK_TENSORS = 29
+
+
+class Neck:
+    """cb_neck: the SimpleFPN neck (point_neck) over batches of tiles."""
+
+    def __init__(self, backend, grid=72, embed=1024, max_tiles=1):
+        self.backend = backend
+        self.grid, self.embed = grid, embed
+        h = C.c_void_p()
+        backend.check(lib().cb_neck_create(backend.h, grid, embed, max_tiles, C.byref(h)))
+        self.h = h
+
+    def init_random(self, seed, std=0.02):
+        self.backend.check(lib().cb_neck_init_random(self.h, seed, std))
+
+    def set_weight(self, which, array):
+        import numpy as np
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        self.backend.check(lib().cb_neck_set_weight(self.h, which, a.ctypes.data, a.size))
+
+    def run(self, x, ntile, emb, feat_s0, feat_s1):
+        self.backend.check(lib().cb_neck_run(self.h, x.h, ntile, emb.h, feat_s0.h, feat_s1.h))
+
+    def close(self):
+        if self.h:
+            lib().cb_neck_free(self.h)
             self.h = C.c_void_p(None)

@@ -359,6 +359,37 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0,
 int cb_decode(cb_decoder *d, int P, const float *points, float *iou,
               cb_mem lowres);
 
+/* ------------------------------------------------------------ neck
+ * The SimpleFPN neck of the point-prompt head and the decoder's
+ * high-resolution projections (sam3_model.c: load_neck :585-622,
+ * load_point_neck :642-654, conv3x3 :1032-1054, convt2x2 :1058-1065,
+ * neck_level :1071-1095, point_neck :1098-1110), batched over tiles.
+ * Tensors and their order: include/sam3_synth.h (SAM3_NT_*). */
+typedef struct cb_neck cb_neck;
+
+/* Weights and work buffers for maps of grid x grid tokens of width embed
+ * (72 and 1024 for SAM 3; embed % 64 == 0), up to max_tiles per call. */
+int cb_neck_create(cb_backend *b, int grid, int embed, int max_tiles,
+                   cb_neck **out);
+void cb_neck_free(cb_neck *n);
+
+/* Random init from the sam3_synth.h streams (SAM3_STREAM_NECKW + index),
+ * weights and biases N(0, std). */
+int cb_neck_init_random(cb_neck *n, uint64_t seed, float std);
+
+/* Set neck tensor `which` (SAM3_NT_*) from host fp32 data in the
+ * checkpoint's layout (sam3_neck_tensor gives rows x cols; tensors a level
+ * does not have are rejected). */
+int cb_neck_set_weight(cb_neck *n, int which, const float *src, size_t count);
+
+/* point_neck on ntile trunk outputs x F32 [ntile, grid^2, embed] (raster
+ * tokens, as cb_encode_tiles writes them): emb F32 [ntile, grid^2, 256]
+ * (no_mem_embed added), feat_s0 F32 [ntile, (4 grid)^2, 32], feat_s1 F32
+ * [ntile, (2 grid)^2, 64] -- the inputs of cb_decoder_set_image.
+ * Asynchronous on the backend stream. */
+int cb_neck_run(cb_neck *n, cb_mem x, int ntile, cb_mem emb, cb_mem feat_s0,
+                cb_mem feat_s1);
+
 /* Diagnostics: the two exponential paths of the attention softmax on n
  * (even) device values x <= 0: y_poly = the FMA-pipe polynomial 2^x,
  * y_mufu = ex2.approx, for accuracy tests against the CUDA math library. */

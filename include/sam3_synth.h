@@ -224,6 +224,78 @@ static inline void sam3_dec_tensor(int i, int *rows, int *cols, int *init)
     *init = k;
 }
 
+/* ------------------------------------------------ SimpleFPN neck
+ * The neck of the point-prompt head (sam3_model.c load_neck :585-622 with
+ * E = 1024, SAM_DIM = 256) and the decoder's high-resolution projections
+ * and no-memory embedding (load_point_neck :642-654). Level l = 0, 1, 2
+ * (scale 4, 2, 1) has 8 tensors {d0_w, d0_b, d1_w, d1_b, c1_w, c1_b, c3_w,
+ * c3_b}; the ones a level does not have are empty (0 rows). Shapes in the
+ * checkpoint layout, ConvTranspose weights [cin, cout, 2, 2] as
+ * [cin, cout * 4], convolution weights [cout, cin, kh, kw] as
+ * [cout, cin * kh * kw]. Random init of tensor i draws stream
+ * SAM3_STREAM_NECKW + i: weights and biases N(0, std) (SAM3_INIT_W / _B). */
+#define SAM3_STREAM_NECKW 10240ULL
+enum {
+    SAM3_NT_LEVEL = 0,           /* + 8 * level + {d0w, d0b, d1w, d1b, c1w, c1b, c3w, c3b} */
+    SAM3_NT_S0_W = 24,           /* conv_s0 [32, 256] */
+    SAM3_NT_S0_B,                /* [32] */
+    SAM3_NT_S1_W,                /* conv_s1 [64, 256] */
+    SAM3_NT_S1_B,                /* [64] */
+    SAM3_NT_NO_MEM,              /* no_mem_embed [256] */
+    SAM3_NT_COUNT
+};
+
+/* Shape and init kind of neck tensor i for backbone width E. */
+static inline void sam3_neck_tensor(int i, int E, int *rows, int *cols, int *init)
+{
+    int r = 0, c = 1, k = SAM3_INIT_B;
+
+    if (i < SAM3_NT_S0_W) {
+        const int l = i / 8, t = i % 8;
+        const int cin = l == 0 ? E / 4 : (l == 1 ? E / 2 : E);
+
+        switch (t) {
+        case 0: /* ConvTranspose 0: E -> E / 2 (levels 0 and 1) */
+            if (l < 2)
+                r = E, c = (E / 2) * 4;
+            break;
+        case 1:
+            if (l < 2)
+                r = E / 2;
+            break;
+        case 2: /* ConvTranspose 1: E / 2 -> E / 4 (level 0) */
+            if (l == 0)
+                r = E / 2, c = (E / 4) * 4;
+            break;
+        case 3:
+            if (l == 0)
+                r = E / 4;
+            break;
+        case 4:
+            r = 256, c = cin;
+            break;
+        case 6:
+            r = 256, c = 256 * 9;
+            break;
+        default: /* c1_b, c3_b */
+            r = 256;
+        }
+        k = (t & 1) ? SAM3_INIT_B : SAM3_INIT_W;
+    }
+    else if (i == SAM3_NT_S0_W || i == SAM3_NT_S1_W) {
+        r = i == SAM3_NT_S0_W ? 32 : 64, c = 256, k = SAM3_INIT_W;
+    }
+    else if (i == SAM3_NT_S0_B || i == SAM3_NT_S1_B) {
+        r = i == SAM3_NT_S0_B ? 32 : 64;
+    }
+    else if (i == SAM3_NT_NO_MEM) {
+        r = 256;
+    }
+    *rows = r;
+    *cols = r ? c : 0;
+    *init = k;
+}
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,10 @@ def lib():
         L.or_dec_tensor.argtypes = [C.c_int] + [C.POINTER(C.c_int)] * 3
         L.or_sam_decode.argtypes = [C.POINTER(C.c_void_p), f32p, f32p, f32p, C.c_int,
                                     f32p, f32p, f32p]
+        L.or_im2col3x3.argtypes = [f32p, f32p] + [C.c_int] * 4 + [C.c_long]
+        L.or_neck_tensor.argtypes = [C.c_int, C.c_int] + [C.POINTER(C.c_int)] * 3
+        L.or_point_neck.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, f32p, f32p,
+                                    f32p, f32p]
         L.sam3_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t,
                                         C.c_float, C.c_float, f32p]
         L.sam3_synth_u8.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t, u8p]
@@ -113,6 +117,7 @@ def ref():
         R.ref_num_threads.restype = C.c_int
         R.ref_convt_scatter.argtypes = [f32p, f32p, f32p, C.c_void_p] + [C.c_int] * 5
         R.ref_mask_logits.argtypes = [f32p, f32p, f32p, C.c_int, C.c_long]
+        R.ref_im2col3x3.argtypes = [f32p, f32p] + [C.c_int] * 4 + [C.c_long]
     return _ref
 
 
@@ -401,3 +406,49 @@ def sam_decode(w, emb, s0, s1, points):
                         np.ascontiguousarray(s0, np.float32),
                         np.ascontiguousarray(s1, np.float32), P, pts, iou, low)
     return iou, low
+
+
+# ---------------------------------------------------------------- neck
+NECK_TENSORS = 29
+NECK_STREAM = 10240
+
+
+def im2col3x3(X, H, W, Cn, t0, n, use_ref=False):
+    """im2col3x3 (sam3_kernels.cl:746-760): tokens t0 .. t0 + n of X [H*W, C]."""
+    out = np.empty((n, 9 * Cn), np.float32)
+    fn = ref().ref_im2col3x3 if use_ref else lib().or_im2col3x3
+    fn(np.ascontiguousarray(X, np.float32), out, H, W, Cn, t0, n * 9 * Cn)
+    return out
+
+
+def neck_tensor_info(i, E=1024):
+    r, c, k = C.c_int(), C.c_int(), C.c_int()
+    lib().or_neck_tensor(i, E, C.byref(r), C.byref(c), C.byref(k))
+    return r.value, c.value, k.value
+
+
+class NeckWeights:
+    """The neck's random-init tensors (include/sam3_synth.h: tensor i draws
+    stream 10240 + i, N(0, std)); empty arrays for tensors a level lacks."""
+
+    def __init__(self, seed, std=0.02, E=1024):
+        self.E = E
+        self.t = []
+        for i in range(NECK_TENSORS):
+            r, c, _ = neck_tensor_info(i, E)
+            self.t.append(normal(seed, NECK_STREAM + i, (r, c), 0.0, std) if r
+                          else np.zeros((1,), np.float32))
+
+    def ctypes(self):
+        return (C.c_void_p * NECK_TENSORS)(*[a.ctypes.data for a in self.t])
+
+
+def point_neck(w, x, grid):
+    """point_neck (sam3_model.c:1098-1110) on x [grid^2, E]; returns
+    (emb [grid^2, 256], feat_s0 [16 grid^2, 32], feat_s1 [4 grid^2, 64])."""
+    T = grid * grid
+    emb = np.empty((T, 256), np.float32)
+    s0 = np.empty((16 * T, 32), np.float32)
+    s1 = np.empty((4 * T, 64), np.float32)
+    lib().or_point_neck(w.ctypes(), grid, w.E, np.ascontiguousarray(x, np.float32), emb, s0, s1)
+    return emb, s0, s1

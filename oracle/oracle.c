@@ -875,3 +875,97 @@ void or_sam_decode(const float *const *w, const float *emb, const float *s0,
     free(sh), free(keys), free(kin), free(bq), free(bk), free(bv), free(bo);
     free(u1), free(g2), free(u2), free(hyper);
 }
+
+/* ------------------------------------------------------------ neck */
+
+/* im2col3x3: sam3_kernels.cl:746-760 (tokens t0 .. of an H x W x C map,
+ * column c * 9 + ky * 3 + kx). */
+void or_im2col3x3(const float *X, float *out, int H, int W, int C, int t0,
+                  long total)
+{
+    long gid;
+
+#pragma omp parallel for schedule(static)
+    for (gid = 0; gid < total; gid++) {
+        const int t = t0 + (int)(gid / (C * 9)), col = (int)(gid % (C * 9));
+        const int c = col / 9, ky = (col % 9) / 3, kx = col % 3;
+        const int y = t / W + ky - 1, x = t % W + kx - 1;
+
+        out[gid] = (y >= 0 && y < H && x >= 0 && x < W) ? X[((long)y * W + x) * C + c] : 0.0f;
+    }
+}
+
+void or_neck_tensor(int i, int E, int *rows, int *cols, int *init)
+{
+    sam3_neck_tensor(i, E, rows, cols, init);
+}
+
+/* conv3x3: sam3_model.c:1032-1054, im2col in bands of col_rows tokens
+ * (128 MB of fp32 columns, sam3_model.c:849). */
+static void neck_conv3x3(const float *X, int side, const float *w, const float *b, float *Y)
+{
+    const long T = (long)side * side, col_rows = (128L << 20) / (9 * 256 * 4);
+    float *col = malloc(sizeof(float) * (size_t)(col_rows < T ? col_rows : T) * 9 * 256);
+    long t0;
+
+    for (t0 = 0; t0 < T; t0 += col_rows) {
+        const long n = T - t0 < col_rows ? T - t0 : col_rows;
+
+        or_im2col3x3(X, col, side, side, 256, (int)t0, n * 9 * 256);
+        linear((int)n, 9 * 256, 256, col, w, b, Y + t0 * 256, OR_ACT_NONE, 0);
+    }
+    free(col);
+}
+
+/* convt2x2: sam3_model.c:1058-1065. */
+static void neck_convt2x2(const float *X, int side, int cin, int cout, const float *w,
+                          const float *b, float *G, float *Y, int act)
+{
+    struct or_gemm_args a;
+
+    memset(&a, 0, sizeof(a));
+    a.M = side * side, a.N = cout * 4, a.K = cin, a.A = X, a.lda = cin;
+    a.B = w, a.ldb = cout * 4, a.C = G, a.ldc = cout * 4, a.nb1 = 1, a.alpha = 1.0f;
+    or_gemm(&a, 1);
+    or_convt_scatter(G, Y, b, NULL, 1, side, side, cout, act);
+}
+
+/* neck_level: sam3_model.c:1071-1095 (level l, scale 4 >> l). */
+static void neck_level(const float *const *w, int l, int Gd, int E, const float *x, float *nka,
+                       float *nkb, float *g, float *out)
+{
+    const float *const *t = w + 8 * l;
+    const int scale = 4 >> l;
+
+    if (scale == 4) {
+        neck_convt2x2(x, Gd, E, E / 2, t[0], t[1], g, nkb, OR_ACT_GELU);
+        neck_convt2x2(nkb, 2 * Gd, E / 2, E / 4, t[2], t[3], g, nka, OR_ACT_NONE);
+        linear(16 * Gd * Gd, E / 4, 256, nka, t[4], t[5], nkb, OR_ACT_NONE, 0);
+    }
+    else if (scale == 2) {
+        neck_convt2x2(x, Gd, E, E / 2, t[0], t[1], g, nka, OR_ACT_NONE);
+        linear(4 * Gd * Gd, E / 2, 256, nka, t[4], t[5], nkb, OR_ACT_NONE, 0);
+    }
+    else
+        linear(Gd * Gd, E, 256, x, t[4], t[5], nkb, OR_ACT_NONE, 0);
+    neck_conv3x3(nkb, scale * Gd, t[6], t[7], out);
+}
+
+void or_point_neck(const float *const *w, int Gd, int E, const float *x, float *emb,
+                   float *s0, float *s1)
+{
+    const long T = (long)Gd * Gd;
+    float *nka = malloc(sizeof(float) * 16 * T * (E / 4 > 256 ? E / 4 : 256));
+    float *nkb = malloc(sizeof(float) * 16 * T * (E / 4 > 256 ? E / 4 : 256));
+    float *g = malloc(sizeof(float) * 4 * T * E);
+    float *out = malloc(sizeof(float) * 16 * T * 256);
+
+    /* point_neck: sam3_model.c:1098-1110 */
+    neck_level(w, 0, Gd, E, x, nka, nkb, g, out);
+    linear((int)(16 * T), 256, 32, out, w[SAM3_NT_S0_W], w[SAM3_NT_S0_B], s0, OR_ACT_NONE, 0);
+    neck_level(w, 1, Gd, E, x, nka, nkb, g, out);
+    linear((int)(4 * T), 256, 64, out, w[SAM3_NT_S1_W], w[SAM3_NT_S1_B], s1, OR_ACT_NONE, 0);
+    neck_level(w, 2, Gd, E, x, nka, nkb, g, emb);
+    or_add_bcast(emb, emb, w[SAM3_NT_NO_MEM], T * 256, 256);
+    free(nka), free(nkb), free(g), free(out);
+}

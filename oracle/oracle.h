@@ -116,6 +116,17 @@ void or_sam_decode(const float *const *w, const float *emb, const float *s0,
                    const float *s1, int P, const float *points, float *iou,
                    float *lowres);
 
+/* Neck: im2col3x3 (sam3_kernels.cl:746-760, total = n * 9 * C values from
+ * token t0), and point_neck (sam3_model.c:1098-1110 with neck_level,
+ * conv3x3, convt2x2) on the trunk output x [Gd^2, E]: w holds the neck
+ * tensors in include/sam3_synth.h order (SAM3_NT_*); emb [Gd^2, 256],
+ * s0 [16 Gd^2, 32], s1 [4 Gd^2, 64]. */
+void or_im2col3x3(const float *X, float *out, int H, int W, int C, int t0,
+                  long total);
+void or_neck_tensor(int i, int E, int *rows, int *cols, int *init);
+void or_point_neck(const float *const *w, int Gd, int E, const float *x,
+                   float *emb, float *s0, float *s1);
+
 #ifdef __cplusplus
 }
 #endif

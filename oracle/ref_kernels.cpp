@@ -447,6 +447,20 @@ void ref_mask_logits(const float *U, const float *hyper, float *out, int npix,
     run1d(k_ml, &a, (size_t)total);
 }
 
+/* ---- im2col3x3: sam3_kernels.cl:746-760, host sam3_model.c:1032-1054 */
+struct ic_args {
+    const float *X;
+    float *out;
+    int H, W, C, t0, total;
+};
+static void k_ic(void *p) { ic_args *a = (ic_args *)p; ocl::im2col3x3(a->X, a->out, a->H, a->W, a->C, a->t0, a->total); }
+
+void ref_im2col3x3(const float *X, float *out, int H, int W, int C, int t0, long total)
+{
+    ic_args a = {X, out, H, W, C, t0, (int)total};
+    run1d(k_ic, &a, (size_t)total);
+}
+
 int ref_num_threads(void) { return omp_get_max_threads(); }
 
 } // extern "C"

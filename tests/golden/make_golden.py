@@ -173,6 +173,14 @@ def cases():
         out.append((name, run))
 
     logits_case("mask_logits", 3, 77, 1100)
+
+    def im2col_case(name, H, W, Cn, t0, n, stream):
+        def run(use_ref):
+            X = ob.normal(SEED, stream, (H * W, Cn))
+            return {"col": ob.im2col3x3(X, H, W, Cn, t0, n, use_ref=use_ref)}
+        out.append((name, run))
+
+    im2col_case("im2col3x3_band", 7, 5, 6, 9, 20, 1200)
     return out
 
 
