@@ -148,6 +148,22 @@ int k_im2col3x3_bf16(const void *X, int H, int W, int C, long t0, long rows,
 int k_permute_conv3x3_bf16(const float *src, int cout, int cin, void *dst,
                            k_stream s);
 
+/* Input path (input.cu). resize_pass_u8: one axis of the uint8 antialiased
+ * resize over `lines` lines of interleaved RGB, source / destination
+ * strides in bytes between lines (s_line, d_line) and between pixels along
+ * the axis (s_step, d_step); bounds [2 nout] (first, count), kk [nout,
+ * ksize] fixed-point weights with `prec` fraction bits; line_fastest:
+ * consecutive threads take consecutive lines. crop_copy_u8: w x h
+ * RGB crop (row pitch in bytes) -> packed. normalize_chw: uint8 HWC side^2
+ * tile -> fp32 CHW (u / 255 - 0.5) / 0.5. */
+int k_resize_pass_u8(const uint8_t *src, long s_line, long s_step,
+                     uint8_t *dst, long d_line, long d_step, int lines,
+                     int nout, int line_fastest, const int *bounds,
+                     const int *kk, int ksize, int prec, k_stream s);
+int k_crop_copy_u8(const uint8_t *src, long pitch, int w, int h, uint8_t *dst,
+                   k_stream s);
+int k_normalize_chw(const uint8_t *tile, int side, float *out, k_stream s);
+
 /* uint8 HWC tiles -> bf16 patch rows in window-major token order:
  * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight
  * order), value (u/255 - 0.5)/0.5 (image.c:360-366), zero for columns >= 3

@@ -38,7 +38,7 @@ EXPORTS = [
     "cb_convt_scatter", "cb_mask_logits", "cb_decoder_create", "cb_decoder_free",
     "cb_decoder_init_random", "cb_decoder_set_weight", "cb_decoder_set_image",
     "cb_decode", "cb_neck_create", "cb_neck_free", "cb_neck_init_random",
-    "cb_neck_set_weight", "cb_neck_run",
+    "cb_neck_set_weight", "cb_neck_run", "cb_image_encoder_input",
     "sam3_synth_normal", "sam3_synth_u8", "sam3_synth_rope_axial",
 ]
 
@@ -169,6 +169,8 @@ def lib():
         "cb_neck_init_random": (i32, [vp, C.c_uint64, f32]),
         "cb_neck_set_weight": (i32, [vp, i32, vp, sz]),
         "cb_neck_run": (i32, [vp, vp, i32, vp, vp, vp]),
+        "cb_image_encoder_input": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, i32,
+                                         vp]),
         "sam3_synth_normal": (None, [C.c_uint64, C.c_uint64, sz, f32, f32, vp]),
         "sam3_synth_u8": (None, [C.c_uint64, C.c_uint64, sz, vp]),
         "sam3_synth_rope_axial": (None, [i32, i32, C.c_double, vp]),
@@ -363,6 +365,12 @@ class Backend:
     def convt_scatter(self, G, out, bias, add, P, H, W, Co, act=ACT_NONE):
         self.check(lib().cb_convt_scatter(self.h, G.h, out.h, bias.h,
                                           add.h if add else None, P, H, W, Co, act))
+
+    def image_encoder_input(self, img, cols, rows, x0, y0, w, h, side=1008, tiles=None,
+                            tile=0, chw=None):
+        self.check(lib().cb_image_encoder_input(self.h, img.h, cols, rows, x0, y0, w, h, side,
+                                                tiles.h if tiles else None, tile,
+                                                chw.h if chw else None))
 
     def mask_logits(self, U, hyper, out, P, npix):
         self.check(lib().cb_mask_logits(self.h, U.h, hyper.h, out.h, P, npix))

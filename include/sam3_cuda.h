@@ -390,6 +390,22 @@ int cb_neck_set_weight(cb_neck *n, int which, const float *src, size_t count);
 int cb_neck_run(cb_neck *n, cb_mem x, int ntile, cb_mem emb, cb_mem feat_s0,
                 cb_mem feat_s1);
 
+/* ------------------------------------------------------------ input path
+ * image_encoder_input (image.c:346-371) on the device: the crop (x0, y0, w,
+ * h) of an interleaved 8-bit RGB image cols x rows in device buffer img
+ * (CB_U8), resized to side x side with torchvision's uint8 antialiased
+ * bilinear (aa_resize, image.c:209-339; bit-exact: integer arithmetic,
+ * weights computed as the reference computes them) unless it has that size
+ * already. Outputs (either may be NULL, not both): tiles (CB_U8) receives
+ * the uint8 tile at byte offset tile * side * side * 3 -- the input of
+ * cb_encode_tiles, which fuses the normalisation; chw (CB_F32 [3, side,
+ * side]) receives the reference's float output (u / 255 - 0.5) / 0.5.
+ * Asynchronous on the backend stream (the resize tables are computed on the
+ * host and copied in the call). */
+int cb_image_encoder_input(cb_backend *b, cb_mem img, int cols, int rows,
+                           int x0, int y0, int w, int h, int side,
+                           cb_mem tiles, int tile, cb_mem chw);
+
 /* Diagnostics: the two exponential paths of the attention softmax on n
  * (even) device values x <= 0: y_poly = the FMA-pipe polynomial 2^x,
  * y_mufu = ex2.approx, for accuracy tests against the CUDA math library. */

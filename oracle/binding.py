@@ -81,6 +81,8 @@ def lib():
         L.or_sam_decode.argtypes = [C.POINTER(C.c_void_p), f32p, f32p, f32p, C.c_int,
                                     f32p, f32p, f32p]
         L.or_im2col3x3.argtypes = [f32p, f32p] + [C.c_int] * 4 + [C.c_long]
+        L.or_aa_resize.argtypes = [u8p] + [C.c_int] * 5 + [u8p]
+        L.or_image_encoder_input.argtypes = [u8p] + [C.c_int] * 6 + [f32p]
         L.or_neck_tensor.argtypes = [C.c_int, C.c_int] + [C.POINTER(C.c_int)] * 3
         L.or_point_neck.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, f32p, f32p,
                                     f32p, f32p]
@@ -452,3 +454,21 @@ def point_neck(w, x, grid):
     s1 = np.empty((4 * T, 64), np.float32)
     lib().or_point_neck(w.ctypes(), grid, w.E, np.ascontiguousarray(x, np.float32), emb, s0, s1)
     return emb, s0, s1
+
+
+# ---------------------------------------------------------------- input path
+def aa_resize(rgb, nw, nh):
+    """aa_resize (image.c:284-339) of an HWC uint8 image to nh x nw."""
+    rgb = np.ascontiguousarray(rgb, np.uint8)
+    h, w = rgb.shape[:2]
+    out = np.empty((nh, nw, 3), np.uint8)
+    lib().or_aa_resize(rgb, w, h, w, nw, nh, out)
+    return out
+
+
+def image_encoder_input(rgb, x0, y0, w, h, side=1008):
+    """image_encoder_input (image.c:346-371): float CHW [3, side, side]."""
+    rgb = np.ascontiguousarray(rgb, np.uint8)
+    out = np.empty((3, side, side), np.float32)
+    lib().or_image_encoder_input(rgb, rgb.shape[1], x0, y0, w, h, side, out)
+    return out

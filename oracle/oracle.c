@@ -969,3 +969,142 @@ void or_point_neck(const float *const *w, int Gd, int E, const float *x, float *
     or_add_bcast(emb, emb, w[SAM3_NT_NO_MEM], T * 256, 256);
     free(nka), free(nkb), free(g), free(out);
 }
+
+/* ------------------------------------------------------------ input path */
+
+/* precompute_coeffs (image.c:219-276): per output pixel of one axis, the
+ * window [xmin, xmin + cnt) and its fixed-point triangle weights, with the
+ * axis' precision (the largest at which the biggest weight fits int16). */
+struct or_coeffs {
+    int ksize, prec;
+    int *bounds, *kk;
+};
+
+static void or_precompute_coeffs(int in, int out, struct or_coeffs *c)
+{
+    const double scale = (double)in / out;
+    const double filterscale = scale < 1.0 ? 1.0 : scale;
+    const double support = 1.0 * filterscale, ss = 1.0 / filterscale;
+    double *w, wt_max = 0.0;
+    int xx, x;
+
+    c->ksize = (int)ceil(support) * 2 + 1;
+    c->bounds = malloc(2 * (size_t)out * sizeof(int));
+    c->kk = calloc((size_t)out * c->ksize, sizeof(int));
+    w = calloc((size_t)out * c->ksize, sizeof(double));
+    for (xx = 0; xx < out; xx++) {
+        const double center = (xx + 0.5) * scale;
+        double ww = 0.0, *k = w + (size_t)xx * c->ksize;
+        int xmin = (int)(center - support + 0.5), xmax = (int)(center + support + 0.5);
+
+        if (xmin < 0)
+            xmin = 0;
+        if (xmax > in)
+            xmax = in;
+        xmax -= xmin;
+        if (xmax > c->ksize)
+            xmax = c->ksize;
+        if (xmax < 0)
+            xmax = 0;
+        for (x = 0; x < xmax; x++) {
+            const double t = fabs((x + xmin - center + 0.5) * ss);
+
+            k[x] = t < 1.0 ? 1.0 - t : 0.0;
+            ww += k[x];
+        }
+        if (ww != 0.0)
+            for (x = 0; x < xmax; x++) {
+                k[x] /= ww;
+                if (k[x] > wt_max)
+                    wt_max = k[x];
+            }
+        c->bounds[2 * xx] = xmin;
+        c->bounds[2 * xx + 1] = xmax;
+    }
+    for (c->prec = 0; c->prec < 22; c->prec++)
+        if ((int)(0.5 + wt_max * (1 << (c->prec + 1))) >= (1 << 15))
+            break;
+    for (xx = 0; xx < out * c->ksize; xx++) {
+        const double v = w[xx] * (1 << c->prec);
+
+        c->kk[xx] = v < 0 ? (int)(-0.5 + v) : (int)(0.5 + v);
+    }
+    free(w);
+}
+
+static unsigned char or_clip8(int64_t v, int prec)
+{
+    v >>= prec;
+    return v < 0 ? 0 : v > 255 ? 255 : (unsigned char)v;
+}
+
+/* aa_resize (image.c:284-339): interleaved RGB w x h (row stride `stride`
+ * pixels) -> nw x nh, horizontal pass first, each pass rounded and clipped
+ * to 8 bits. */
+void or_aa_resize(const uint8_t *src, int w, int h, int stride, int nw, int nh, uint8_t *dst)
+{
+    struct or_coeffs cx, cy;
+    uint8_t *tmp = malloc((size_t)nw * h * 3);
+    int y;
+
+    or_precompute_coeffs(w, nw, &cx);
+    or_precompute_coeffs(h, nh, &cy);
+#pragma omp parallel for schedule(static)
+    for (y = 0; y < h; y++) {
+        int x, c, i;
+
+        for (x = 0; x < nw; x++) {
+            const int *k = cx.kk + (size_t)x * cx.ksize;
+            const int xmin = cx.bounds[2 * x], cnt = cx.bounds[2 * x + 1];
+
+            for (c = 0; c < 3; c++) {
+                int64_t ss = (int64_t)1 << (cx.prec - 1);
+
+                for (i = 0; i < cnt; i++)
+                    ss += (int64_t)src[((size_t)y * stride + xmin + i) * 3 + c] * k[i];
+                tmp[((size_t)y * nw + x) * 3 + c] = or_clip8(ss, cx.prec);
+            }
+        }
+    }
+#pragma omp parallel for schedule(static)
+    for (y = 0; y < nh; y++) {
+        const int *k = cy.kk + (size_t)y * cy.ksize;
+        const int ymin = cy.bounds[2 * y], cnt = cy.bounds[2 * y + 1];
+        int x, c, i;
+
+        for (x = 0; x < nw; x++)
+            for (c = 0; c < 3; c++) {
+                int64_t ss = (int64_t)1 << (cy.prec - 1);
+
+                for (i = 0; i < cnt; i++)
+                    ss += (int64_t)tmp[((size_t)(ymin + i) * nw + x) * 3 + c] * k[i];
+                dst[((size_t)y * nw + x) * 3 + c] = or_clip8(ss, cy.prec);
+            }
+    }
+    free(tmp);
+    free(cx.bounds), free(cx.kk), free(cy.bounds), free(cy.kk);
+}
+
+/* image_encoder_input (image.c:346-371): the crop (x0, y0, w, h) of an
+ * interleaved RGB image `cols` pixels wide, resized to side x side unless it
+ * has that size already, then out[c][y][x] = (u / 255 - 0.5) / 0.5. */
+void or_image_encoder_input(const uint8_t *rgb, int cols, int x0, int y0, int w, int h, int side,
+                            float *out)
+{
+    const uint8_t *src = rgb + ((size_t)y0 * cols + x0) * 3;
+    uint8_t *rs = NULL;
+    int stride = cols, c, y, x;
+
+    if (w != side || h != side) {
+        rs = malloc((size_t)side * side * 3);
+        or_aa_resize(src, w, h, cols, side, side, rs);
+        src = rs;
+        stride = side;
+    }
+    for (c = 0; c < 3; c++)
+        for (y = 0; y < side; y++)
+            for (x = 0; x < side; x++)
+                out[((size_t)c * side + y) * side + x] =
+                    (src[((size_t)y * stride + x) * 3 + c] / 255.0f - 0.5f) / 0.5f;
+    free(rs);
+}

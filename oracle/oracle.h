@@ -127,6 +127,13 @@ void or_neck_tensor(int i, int E, int *rows, int *cols, int *init);
 void or_point_neck(const float *const *w, int Gd, int E, const float *x,
                    float *emb, float *s0, float *s1);
 
+/* Input path: aa_resize (image.c:284-339, torchvision's uint8 antialiased
+ * bilinear) and image_encoder_input (image.c:346-371). */
+void or_aa_resize(const uint8_t *src, int w, int h, int stride, int nw, int nh,
+                  uint8_t *dst);
+void or_image_encoder_input(const uint8_t *rgb, int cols, int x0, int y0,
+                            int w, int h, int side, float *out);
+
 #ifdef __cplusplus
 }
 #endif
