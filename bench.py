@@ -350,6 +350,32 @@ def neck_bench(sb, cb, torch, iters=5):
                     "-> emb, feat_s0, feat_s1"}
 
 
+def input_bench(sb, cb, torch, iters=10):
+    """The input path (cb_image_encoder_input) on a 2100 x 1500 crop of a
+    seeded uint8 image resized to one 1008 x 1008 tile, uint8 tile output
+    (what cb_encode_tiles reads); device-timed."""
+    stream = torch.cuda.ExternalStream(cb.stream)
+    rows, cols = 1600, 2200
+    img = cb.alloc(rows * cols * 3, sb.U8)
+    h = np.random.default_rng(SEED).integers(0, 256, size=(rows, cols, 3), dtype=np.uint8)
+    cb.write(img, h)
+    tiles = cb.alloc(1008 * 1008 * 3, sb.U8)
+    times = []
+    for it in range(iters + 3):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        cb.image_encoder_input(img, cols, rows, 40, 60, 2100, 1500, 1008, tiles=tiles)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 3:
+            times.append(e0.elapsed_time(e1))
+    t = statistics.median(times)
+    nbytes = 2100 * 1500 * 3 + 2 * 1500 * 1008 * 3 + 1008 * 1008 * 3
+    return {"ms_per_crop": t, "crops_per_s": 1e3 / t, "gbs": nbytes / (t * 1e-3) / 1e9,
+            "work": "2100 x 1500 RGB crop -> 1008 x 1008 uint8 tile (antialiased bilinear)"}
+
+
 MASK_P = 64  # prompts per decode (config 3: batches of 64)
 
 
@@ -457,6 +483,10 @@ def cpu_configs_sample():
     t = time.perf_counter() - t0
     out["neck_1_tile"] = {"s": t, "tflops": 2.0 * NECK_MAC_PER_TOKEN * 5184 / t / 1e12,
                           "kind": "port"}
+    img = ob.u8(SEED, 9600, (1500, 2100, 3))
+    t0 = time.perf_counter()
+    ob.aa_resize(img, 1008, 1008)
+    out["input_resize_1_crop"] = {"s": time.perf_counter() - t0, "kind": "port"}
     return out
 
 
@@ -552,6 +582,7 @@ def our_arm(args, world, rank, local, pg):
         dec = decoder_bench(cb, torch, pk)
         mdec = mask_decoder_bench(sb, cb, torch)
         nk = neck_bench(sb, cb, torch)
+        inp = input_bench(sb, cb, torch)
         line = {
             "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -572,6 +603,7 @@ def our_arm(args, world, rank, local, pg):
             "decoder_attention": dec,
             "mask_decoder": mdec,
             "neck": nk,
+            "input_path": inp,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
                     "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
                     "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},
