@@ -21,7 +21,8 @@ CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA, "bin", "nvcc")
 
 CU = ["gemm_tc.cu", "attn_tc.cu", "attn_simt.cu", "attn_decoder.cu", "elementwise.cu", "attn_noalloc.cu",
-      "decoder.cu", "neck.cu", "input.cu"]
+      "decoder.cu", "neck.cu", "input.cu",
+      "detector.cu"]
 C = ["cuda_backend.c", "sam3_ops.c", "sam3_encoder.c", "sam3_decoder.c", "sam3_neck.c", "sam3_input.c",
      "synth.c"]
 HEADERS = ["tc_ptx.cuh", "tmap.cuh", "kernels.h", "backend_internal.h"]

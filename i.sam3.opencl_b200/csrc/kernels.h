@@ -164,6 +164,25 @@ int k_crop_copy_u8(const uint8_t *src, long pitch, int w, int h, uint8_t *dst,
                    k_stream s);
 int k_normalize_chw(const uint8_t *tile, int side, float *out, k_stream s);
 
+/* Detector attention (detector.cu). pack_qkv_pad64: fp32 q, k, v [N, ld]
+ * (head h at column h * hd) -> bf16 [N, 3 * heads * 64] with heads
+ * zero-padded to 64 columns (the tcgen05 attention's layout);
+ * unpack_heads64: fp32 [N, heads * 64] -> O [N, ldo], first hd columns of
+ * each head. attend_simt: fp32 flash attention (hd 32 or 64) with an
+ * optional causal mask or box relative position bias dy / dx (key grid W
+ * wide), keys split over CTAs; workspace k_attend_workspace bytes. */
+int k_pack_qkv_pad64(const float *q, int ldq, const float *k, int ldk,
+                     const float *v, int ldv, long N, int heads, int hd,
+                     void *out, k_stream s);
+int k_unpack_heads64(const float *in, long N, int heads, int hd, float *O,
+                     int ldo, k_stream s);
+int k_attend_splits(int Nq, int Nk, int heads, int num_sms);
+size_t k_attend_workspace(int Nq, int Nk, int heads, int hd, int num_sms);
+int k_attend_simt(int Nq, int Nk, int heads, int hd, const float *Q, int ldq,
+                  const float *K, int ldk, const float *V, int ldv, float *O,
+                  int ldo, int causal, const float *dy, const float *dx,
+                  int W, void *ws, size_t ws_bytes, int num_sms, k_stream s);
+
 /* uint8 HWC tiles -> bf16 patch rows in window-major token order:
  * out[ntile * grid^2, kpad], column c*ps*ps + ky*ps + kx (the Conv2d weight
  * order), value (u/255 - 0.5)/0.5 (image.c:360-366), zero for columns >= 3

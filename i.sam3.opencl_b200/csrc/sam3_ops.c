@@ -4,6 +4,7 @@
  * calls (sam3_model.c:147-451, 965-1013). Every operator validates shapes,
  * dtypes and buffer extents, then enqueues one or two kernels on the
  * backend stream. */
+#include <math.h>
 #include <string.h>
 
 #include "backend_internal.h"
@@ -367,4 +368,60 @@ int cb_mask_logits(cb_backend *b, cb_mem U, cb_mem hyper, cb_mem out, int P,
                       k_mask_logits((const float *)U->ptr, (const float *)hyper->ptr,
                                     (float *)out->ptr, P, npix, (k_stream)b->stream),
                       "mask_logits");
+}
+
+int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ldq,
+              cb_mem K, int ldk, cb_mem V, int ldv, cb_mem O, int ldo, int causal,
+              cb_mem dy, cb_mem dx, int W, int mode)
+{
+    const int E = heads * hd;
+    const k_stream st = (k_stream)(b ? b->stream : NULL);
+
+    if (!b || !Q || !K || !V || !O || Nq <= 0 || Nk <= 0 || heads <= 0 ||
+        (hd != 32 && hd != 64) || ldq < E || ldk < E || ldv < E || ldo < E ||
+        Q->dtype != CB_F32 || K->dtype != CB_F32 || V->dtype != CB_F32 ||
+        O->dtype != CB_F32 || !fits(Q, (int64_t)(Nq - 1) * ldq + E) ||
+        !fits(K, (int64_t)(Nk - 1) * ldk + E) || !fits(V, (int64_t)(Nk - 1) * ldv + E) ||
+        !fits(O, (int64_t)(Nq - 1) * ldo + E) || (!dy) != (!dx) ||
+        (dy && (W <= 0 || Nk % W || dy->dtype != CB_F32 || dx->dtype != CB_F32 ||
+                !fits(dy, (int64_t)Nq * (Nk / W) * heads) ||
+                !fits(dx, (int64_t)Nq * W * heads))))
+        return cbi_fail(b, CB_EARG, "attend");
+    CB_TRY(cbi_enter(b));
+    if (mode == CB_ATTN_TC && !causal && !dy && Nq == Nk && Nq >= 1024 &&
+        ldq % 4 == 0 && ldk % 4 == 0 && ldv % 4 == 0 && ldo % 4 == 0 &&
+        aligned16(Q->ptr) && aligned16(K->ptr) && aligned16(V->ptr) && aligned16(O->ptr)) {
+        /* tensor cores: heads zero-padded to 64 columns in bf16 */
+        const size_t packed = (size_t)Nq * 3 * heads * 64 * 2, out = (size_t)Nq * heads * 64 * 4;
+        char *s = NULL;
+
+        CB_TRY(cbi_scratch(b, packed + out, (void **)&s));
+        CB_TRY(cbi_kstatus(b,
+                           k_pack_qkv_pad64((const float *)Q->ptr, ldq, (const float *)K->ptr,
+                                            ldk, (const float *)V->ptr, ldv, Nq, heads, hd, s,
+                                            st),
+                           "attend: pack"));
+        CB_TRY(cbi_kstatus(b,
+                           k_attn_tc(s, 1, Nq, heads * 64, heads, 1.0f / sqrtf((float)hd),
+                                     s + packed, 0, b->d_err, st),
+                           "attend"));
+        return cbi_kstatus(b,
+                           k_unpack_heads64((const float *)(s + packed), Nq, heads, hd,
+                                            (float *)O->ptr, ldo, st),
+                           "attend: unpack");
+    }
+    {
+        const size_t wsb = k_attend_workspace(Nq, Nk, heads, hd, b->num_sms);
+        void *ws = NULL;
+
+        CB_TRY(cbi_scratch(b, wsb, &ws));
+        return cbi_kstatus(b,
+                           k_attend_simt(Nq, Nk, heads, hd, (const float *)Q->ptr, ldq,
+                                         (const float *)K->ptr, ldk, (const float *)V->ptr, ldv,
+                                         (float *)O->ptr, ldo, causal,
+                                         dy ? (const float *)dy->ptr : NULL,
+                                         dx ? (const float *)dx->ptr : NULL, W, ws, wsb,
+                                         b->num_sms, st),
+                           "attend");
+    }
 }

@@ -39,6 +39,7 @@ EXPORTS = [
     "cb_decoder_init_random", "cb_decoder_set_weight", "cb_decoder_set_image",
     "cb_decode", "cb_neck_create", "cb_neck_free", "cb_neck_init_random",
     "cb_neck_set_weight", "cb_neck_run", "cb_image_encoder_input",
+    "cb_attend",
     "sam3_synth_normal", "sam3_synth_u8", "sam3_synth_rope_axial",
 ]
 
@@ -171,6 +172,8 @@ def lib():
         "cb_neck_run": (i32, [vp, vp, i32, vp, vp, vp]),
         "cb_image_encoder_input": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, i32,
                                          vp]),
+        "cb_attend": (i32, [vp, i32, i32, i32, i32, vp, i32, vp, i32, vp, i32, vp, i32, i32,
+                            vp, vp, i32, i32]),
         "sam3_synth_normal": (None, [C.c_uint64, C.c_uint64, sz, f32, f32, vp]),
         "sam3_synth_u8": (None, [C.c_uint64, C.c_uint64, sz, vp]),
         "sam3_synth_rope_axial": (None, [i32, i32, C.c_double, vp]),
@@ -371,6 +374,12 @@ class Backend:
         self.check(lib().cb_image_encoder_input(self.h, img.h, cols, rows, x0, y0, w, h, side,
                                                 tiles.h if tiles else None, tile,
                                                 chw.h if chw else None))
+
+    def attend(self, Nq, Nk, heads, hd, Q, ldq, K, ldk, V, ldv, O, ldo, causal=0, dy=None,
+               dx=None, W=0, mode=0):
+        self.check(lib().cb_attend(self.h, Nq, Nk, heads, hd, Q.h, ldq, K.h, ldk, V.h, ldv,
+                                   O.h, ldo, causal, dy.h if dy else None,
+                                   dx.h if dx else None, W, mode))
 
     def mask_logits(self, U, hyper, out, P, npix):
         self.check(lib().cb_mask_logits(self.h, U.h, hyper.h, out.h, P, npix))

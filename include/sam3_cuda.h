@@ -390,6 +390,23 @@ int cb_neck_set_weight(cb_neck *n, int which, const float *src, size_t count);
 int cb_neck_run(cb_neck *n, cb_mem x, int ntile, cb_mem emb, cb_mem feat_s0,
                 cb_mem feat_s1);
 
+/* ------------------------------------------------------------ detector attention
+ * attend (sam3_text.c:305-343): O = softmax(Q K^T / sqrt(hd) [+ mask or
+ * bias]) V per head, Nq queries over Nk keys, heads of hd columns (32 or
+ * 64), Q/K/V/O F32 rows with their own leading dimensions (elements), head h
+ * at column h * hd. causal != 0 excludes keys j > query i; dy / dx (F32,
+ * both or neither) add SAM 3's box relative position bias dy[(i * (Nk / W)
+ * + y) * heads + h] + dx[(i * W + x) * heads + h] for key j = y * W + x
+ * (softmax_ext, sam3_kernels.cl:889-921). mode CB_ATTN_TC runs unmasked,
+ * unbiased self-attention of at least 1024 tokens (Nq == Nk; the fusion
+ * encoder's 5184-token layers) on the tcgen05 flash kernel with bf16
+ * operands (heads zero-padded to 64 columns), everything else on the CUDA
+ * cores in fp32 (a flash kernel with the keys split over CTAs);
+ * CB_ATTN_F32 always uses the fp32 kernel. */
+int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q,
+              int ldq, cb_mem K, int ldk, cb_mem V, int ldv, cb_mem O, int ldo,
+              int causal, cb_mem dy, cb_mem dx, int W, int mode);
+
 /* ------------------------------------------------------------ input path
  * image_encoder_input (image.c:346-371) on the device: the crop (x0, y0, w,
  * h) of an interleaved 8-bit RGB image cols x rows in device buffer img

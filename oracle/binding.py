@@ -82,6 +82,12 @@ def lib():
                                     f32p, f32p, f32p]
         L.or_im2col3x3.argtypes = [f32p, f32p] + [C.c_int] * 4 + [C.c_long]
         L.or_aa_resize.argtypes = [u8p] + [C.c_int] * 5 + [u8p]
+        L.or_softmax_ext.argtypes = [f32p, C.c_long] + [C.c_int] * 4 + [C.c_void_p,
+                                                                       C.c_void_p,
+                                                                       C.c_int, C.c_int]
+        L.or_attend.argtypes = [C.c_int] * 4 + [f32p, C.c_int, f32p, C.c_int, f32p, C.c_int,
+                                                f32p, C.c_int, C.c_int, C.c_void_p,
+                                                C.c_void_p, C.c_int]
         L.or_image_encoder_input.argtypes = [u8p] + [C.c_int] * 6 + [f32p]
         L.or_neck_tensor.argtypes = [C.c_int, C.c_int] + [C.POINTER(C.c_int)] * 3
         L.or_point_neck.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, f32p, f32p,
@@ -120,6 +126,10 @@ def ref():
         R.ref_convt_scatter.argtypes = [f32p, f32p, f32p, C.c_void_p] + [C.c_int] * 5
         R.ref_mask_logits.argtypes = [f32p, f32p, f32p, C.c_int, C.c_long]
         R.ref_im2col3x3.argtypes = [f32p, f32p] + [C.c_int] * 4 + [C.c_long]
+        R.ref_softmax_ext.argtypes = [f32p, C.c_long] + [C.c_int] * 4 + [C.c_void_p,
+                                                                        C.c_void_p,
+                                                                        C.c_int, C.c_int,
+                                                                        C.c_int]
     return _ref
 
 
@@ -472,3 +482,34 @@ def image_encoder_input(rgb, x0, y0, w, h, side=1008):
     out = np.empty((3, side, side), np.float32)
     lib().or_image_encoder_input(rgb, rgb.shape[1], x0, y0, w, h, side, out)
     return out
+
+
+# ---------------------------------------------------------------- detector attention
+def _ptr(a):
+    return None if a is None else np.ascontiguousarray(a, np.float32).ctypes.data
+
+
+def softmax_ext(S, Nq, h0=0, causal=0, dy=None, dx=None, W=0, nh=8, use_ref=False, local=64):
+    """softmax_ext (sam3_kernels.cl:889-921) on S [rows, L] in place (a copy)."""
+    S = np.array(S, np.float32, copy=True, order="C")
+    dy = None if dy is None else np.ascontiguousarray(dy, np.float32)
+    dx = None if dx is None else np.ascontiguousarray(dx, np.float32)
+    args = (S, S.shape[0], S.shape[1], Nq, h0, causal, _ptr(dy), _ptr(dx), W, nh)
+    if use_ref:
+        ref().ref_softmax_ext(*args, local)
+    else:
+        lib().or_softmax_ext(*args)
+    return S
+
+
+def attend(Q, K, V, heads, hd, causal=0, dy=None, dx=None, W=0):
+    """attend (sam3_text.c:305-343): Q [Nq, heads*hd], K, V [Nk, heads*hd]."""
+    Q = np.ascontiguousarray(Q, np.float32)
+    K = np.ascontiguousarray(K, np.float32)
+    V = np.ascontiguousarray(V, np.float32)
+    dy = None if dy is None else np.ascontiguousarray(dy, np.float32)
+    dx = None if dx is None else np.ascontiguousarray(dx, np.float32)
+    O = np.zeros((Q.shape[0], heads * hd), np.float32)
+    lib().or_attend(Q.shape[0], K.shape[0], heads, hd, Q, Q.shape[1], K, K.shape[1], V,
+                    V.shape[1], O, heads * hd, causal, _ptr(dy), _ptr(dx), W)
+    return O

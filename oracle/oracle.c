@@ -1108,3 +1108,70 @@ void or_image_encoder_input(const uint8_t *rgb, int cols, int x0, int y0, int w,
                     (src[((size_t)y * stride + x) * 3 + c] / 255.0f - 0.5f) / 0.5f;
     free(rs);
 }
+
+/* ------------------------------------------------------------ detector attention */
+
+/* softmax_ext: sam3_kernels.cl:889-921 (serial sums, i.e. one work-item
+ * per group). Rows r < rows, row = (head - h0) * Nq + query. */
+void or_softmax_ext(float *S, long rows, int L, int Nq, int h0, int causal, const float *dy,
+                    const float *dx, int W, int nh)
+{
+    long row;
+
+#pragma omp parallel for schedule(static)
+    for (row = 0; row < rows; row++) {
+        const int i = (int)(row % Nq), h = h0 + (int)(row / Nq);
+        const int H = W > 0 ? L / W : 0;
+        float *s = S + row * L;
+        float m = -INFINITY, sum = 0.0f, v;
+        int j;
+
+        for (j = 0; j < L; j++) {
+            v = s[j];
+            if (causal && j > i)
+                v = -INFINITY;
+            else if (dy)
+                v += dy[((long)i * H + j / W) * nh + h] + dx[((long)i * W + j % W) * nh + h];
+            s[j] = v;
+            m = fmaxf(m, v);
+        }
+        for (j = 0; j < L; j++) {
+            v = expf(s[j] - m);
+            s[j] = v;
+            sum += v;
+        }
+        v = 1.0f / sum;
+        for (j = 0; j < L; j++)
+            s[j] *= v;
+    }
+}
+
+/* attend: sam3_text.c:305-343 (the GEMM-based detector attention), one head
+ * at a time (the reference's head chunking does not change the result). */
+void or_attend(int Nq, int Nk, int heads, int hd, const float *Q, int ldq, const float *K,
+               int ldk, const float *V, int ldv, float *O, int ldo, int causal,
+               const float *dy, const float *dx, int W)
+{
+    float *S = malloc(sizeof(float) * (size_t)Nq * Nk);
+    struct or_gemm_args a;
+    int h;
+
+    for (h = 0; h < heads; h++) {
+        memset(&a, 0, sizeof(a));
+        a.M = Nq, a.N = Nk, a.K = hd;
+        a.A = Q, a.aoff = (long)h * hd, a.lda = ldq;
+        a.B = K, a.boff = (long)h * hd, a.ldb = ldk, a.transb = 1;
+        a.C = S, a.ldc = Nk, a.nb1 = 1;
+        a.alpha = 1.0f / sqrtf((float)hd);
+        or_gemm(&a, 1);
+        or_softmax_ext(S, Nq, Nk, Nq, h, causal, dy, dx, W, heads);
+        memset(&a, 0, sizeof(a));
+        a.M = Nq, a.N = hd, a.K = Nk;
+        a.A = S, a.lda = Nk;
+        a.B = V, a.boff = (long)h * hd, a.ldb = ldv;
+        a.C = O, a.coff = (long)h * hd, a.ldc = ldo, a.nb1 = 1;
+        a.alpha = 1.0f;
+        or_gemm(&a, 1);
+    }
+    free(S);
+}

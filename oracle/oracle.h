@@ -134,6 +134,16 @@ void or_aa_resize(const uint8_t *src, int w, int h, int stride, int nw, int nh,
 void or_image_encoder_input(const uint8_t *rgb, int cols, int x0, int y0,
                             int w, int h, int side, float *out);
 
+/* Detector attention: softmax_ext (sam3_kernels.cl:889-921; rows =
+ * heads * Nq score rows of L keys, optional causal mask or box relative
+ * position bias dy / dx over a key grid W wide) and attend
+ * (sam3_text.c:305-343: Q.K^T / sqrt(hd), softmax_ext, P.V per head). */
+void or_softmax_ext(float *S, long rows, int L, int Nq, int h0, int causal,
+                    const float *dy, const float *dx, int W, int nh);
+void or_attend(int Nq, int Nk, int heads, int hd, const float *Q, int ldq,
+               const float *K, int ldk, const float *V, int ldv, float *O,
+               int ldo, int causal, const float *dy, const float *dx, int W);
+
 #ifdef __cplusplus
 }
 #endif

@@ -461,6 +461,23 @@ void ref_im2col3x3(const float *X, float *out, int H, int W, int C, int t0, long
     run1d(k_ic, &a, (size_t)total);
 }
 
+/* ---- softmax_ext: sam3_kernels.cl:889-921, host sam3_text.c:319-337 */
+struct sx_args {
+    float *S;
+    int L, Nq, h0, causal;
+    const float *dy, *dx;
+    int W, nh;
+};
+static void k_sx(void *p) { sx_args *a = (sx_args *)p; ocl::softmax_ext(a->S, a->L, a->Nq, a->h0, a->causal, a->dy, a->dx, a->W, a->nh); }
+
+void ref_softmax_ext(float *S, long rows, int L, int Nq, int h0, int causal, const float *dy,
+                     const float *dx, int W, int nh, int local)
+{
+    sx_args a = {S, L, Nq, h0, causal, dy, dx, W, nh};
+    size_t ls = local, gs = rows * ls;
+    run_ndrange(1, &gs, &ls, 1, k_sx, &a);
+}
+
 int ref_num_threads(void) { return omp_get_max_threads(); }
 
 } // extern "C"

@@ -181,6 +181,19 @@ def cases():
         out.append((name, run))
 
     im2col_case("im2col3x3_band", 7, 5, 6, 9, 20, 1200)
+
+    def softmax_ext_case(name, Nq, L, heads, h0, causal, W, stream):
+        def run(use_ref):
+            S = ob.normal(SEED, stream, (heads * Nq, L), 0.0, 3.0)
+            dy = dx = None
+            if W:
+                dy = ob.normal(SEED, stream + 1, (Nq * (L // W) * 8,), 0.0, 2.0)
+                dx = ob.normal(SEED, stream + 2, (Nq * W * 8,), 0.0, 2.0)
+            return {"P": ob.softmax_ext(S, Nq, h0, causal, dy, dx, W, 8, use_ref=use_ref)}
+        out.append((name, run))
+
+    softmax_ext_case("softmax_ext_rpb", 5, 48, 2, 3, 0, 8, 1300)
+    softmax_ext_case("softmax_ext_causal", 12, 12, 3, 0, 1, 0, 1310)
     return out
 
 

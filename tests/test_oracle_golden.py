@@ -13,7 +13,8 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 # exactly. The others differ only in the order of a work-group reduction
 # (256-way tree in the reference, serial in the oracle).
 REDUCTION_ORDER = {"layernorm_1024", "layernorm_256_gelu", "softmax_576",
-                   "softmax_100", "attention_win6", "attention_win5_odd"}
+                   "softmax_100", "attention_win6", "attention_win5_odd",
+                   "softmax_ext_rpb", "softmax_ext_causal"}
 
 
 @pytest.mark.parametrize("name,run", cases(), ids=[c[0] for c in cases()])
