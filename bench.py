@@ -376,6 +376,43 @@ def input_bench(sb, cb, torch, iters=10):
             "work": "2100 x 1500 RGB crop -> 1008 x 1008 uint8 tile (antialiased bilinear)"}
 
 
+def detector_attention_bench(sb, cb, torch, pk, iters=10):
+    """cb_attend on the detector's two image-sized shapes: the fusion
+    encoder's self-attention (5184 tokens, 8 heads of 32; tensor cores) and
+    the decoder's 201 queries over the image with the box relative position
+    bias (fp32 CUDA cores); synthetic N(0, 1) inputs, device-timed."""
+    stream = torch.cuda.ExternalStream(cb.stream)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
+    heads, hd, T = 8, 32, 5184
+    res = {}
+    for name, nq, rpb in (("fusion_self_5184", T, False), ("decoder_image_rpb_201", 201, True)):
+        q = torch.randn(nq, heads * hd, device="cuda", generator=g)
+        k = torch.randn(T, heads * hd, device="cuda", generator=g)
+        v = torch.randn(T, heads * hd, device="cuda", generator=g)
+        o = torch.empty(nq, heads * hd, device="cuda")
+        dy = torch.randn(nq * 72 * heads, device="cuda", generator=g) if rpb else None
+        dx = torch.randn(nq * 72 * heads, device="cuda", generator=g) if rpb else None
+        torch.cuda.synchronize()
+        w = [cb.wrap(t) for t in (q, k, v, o)]
+        wb = [cb.wrap(t) for t in (dy, dx)] if rpb else [None, None]
+        times = []
+        for it in range(iters + 3):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            cb.attend(nq, T, heads, hd, w[0], heads * hd, w[1], heads * hd, w[2], heads * hd,
+                      w[3], heads * hd, 0, wb[0], wb[1], 72 if rpb else 0, 0)
+            e1.record(stream)
+            e1.synchronize()
+            if it >= 3:
+                times.append(e0.elapsed_time(e1))
+        t = statistics.median(times)
+        flop = 4.0 * nq * T * hd * heads
+        res[name] = {"ms": t, "tflops": flop / (t * 1e-3) / 1e12,
+                     "path": "tcgen05 (bf16)" if not rpb else "CUDA cores (fp32)"}
+    return res
+
+
 MASK_P = 64  # prompts per decode (config 3: batches of 64)
 
 
@@ -487,6 +524,19 @@ def cpu_configs_sample():
     t0 = time.perf_counter()
     ob.aa_resize(img, 1008, 1008)
     out["input_resize_1_crop"] = {"s": time.perf_counter() - t0, "kind": "port"}
+    # detector attention: the decoder's 201 queries with the box bias in full,
+    # the fusion encoder's self-attention for one of its 8 heads (x 8)
+    qd = ob.normal(SEED, 9700, (201, 256))
+    kd = ob.normal(SEED, 9701, (5184, 256))
+    dyb = ob.normal(SEED, 9702, (201 * 72 * 8,))
+    t0 = time.perf_counter()
+    ob.attend(qd, kd, kd, 8, 32, 0, dyb, dyb, 72)
+    out["detector_rpb_201x5184"] = {"s": time.perf_counter() - t0, "kind": "port"}
+    qf = ob.normal(SEED, 9703, (5184, 32))
+    t0 = time.perf_counter()
+    ob.attend(qf, qf, qf, 1, 32)
+    out["detector_fusion_self_5184"] = {"s": 8 * (time.perf_counter() - t0), "kind": "port",
+                                        "sample": "one head of 8, x 8"}
     return out
 
 
@@ -583,6 +633,7 @@ def our_arm(args, world, rank, local, pg):
         mdec = mask_decoder_bench(sb, cb, torch)
         nk = neck_bench(sb, cb, torch)
         inp = input_bench(sb, cb, torch)
+        det = detector_attention_bench(sb, cb, torch, pk)
         line = {
             "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -604,6 +655,7 @@ def our_arm(args, world, rank, local, pg):
             "mask_decoder": mdec,
             "neck": nk,
             "input_path": inp,
+            "detector_attention": det,
             "e2e": {"value": e2e_value, "unit": "tiles/s",
                     "h2d_bytes_per_step": TOTAL_TILES * SIDE * SIDE * 3,
                     "d2h_bytes_per_step": TOTAL_TILES * 5184 * 1024 * 4},
