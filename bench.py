@@ -694,6 +694,50 @@ def profile_case(ntile):
     print(f"profile case done: {ntile} tiles, 2 blocks, 2 encodes")
 
 
+def profile_part(part):
+    """Small cases of the parts beyond the backbone for ncu captures, each
+    run twice (the second run is the one to capture): `decoder` = cb_decode
+    of 16 prompts, `neck` = cb_neck_run on 2 tiles, `detector` = the two
+    cb_attend shapes of the bench, `input` = one 2100 x 1500 crop."""
+    import torch
+    sb = load_product()
+    cb = sb.Backend(0)
+    T = 5184
+    if part == "decoder":
+        dec = sb.Decoder(cb, 16)
+        dec.init_random(SEED, 0.02)
+        feats = []
+        for k, n in enumerate((T * 256, 16 * T * 32, 4 * T * 64)):
+            m = cb.alloc(n * 4, sb.F32)
+            cb.synth_normal(SEED, 9216 + k, 0.0, 1.0, m, n)
+            feats.append(m)
+        dec.set_image(*feats)
+        pts = np.random.default_rng(SEED).uniform(0, 1008, size=(16, 2)).astype(np.float32)
+        low = cb.alloc(16 * 3 * 288 * 288 * 4, sb.F32)
+        for _ in range(2):
+            dec.decode(pts, low)
+        dec.close()
+    elif part == "neck":
+        neck = sb.Neck(cb, grid=72, embed=1024, max_tiles=2)
+        neck.init_random(SEED, 0.02)
+        x = cb.alloc(2 * T * 1024 * 4, sb.F32)
+        cb.synth_normal(SEED, 9400, 0.0, 1.0, x, 2 * T * 1024)
+        outs = [cb.alloc(2 * T * 256 * 4, sb.F32), cb.alloc(2 * 16 * T * 32 * 4, sb.F32),
+                cb.alloc(2 * 4 * T * 64 * 4, sb.F32)]
+        for _ in range(2):
+            neck.run(x, 2, *outs)
+        neck.close()
+    elif part == "detector":
+        for _ in range(2):
+            detector_attention_bench(sb, cb, torch, None, iters=1)
+    elif part == "input":
+        for _ in range(2):
+            input_bench(sb, cb, torch, iters=1)
+    cb.sync()
+    cb.close()
+    print(f"profile part done: {part}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -703,7 +747,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="TILES",
                     help="run the small ncu case on TILES tiles and exit")
+    ap.add_argument("--profile-part", choices=["decoder", "neck", "detector", "input"],
+                    help="run a small case of one part beyond the backbone and exit")
     args = ap.parse_args()
+    if args.profile_part:
+        profile_part(args.profile_part)
+        return
     if args.profile_case:
         profile_case(args.profile_case)
         return
