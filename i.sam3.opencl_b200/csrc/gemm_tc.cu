@@ -54,6 +54,12 @@ struct GemmEpi {
     int *err;
 };
 
+// CONV3 geometry: 3x3 / pad-1 convolution of cimg maps cH x cW x (K / 9)
+// channels (implicit GEMM); M tiles are 8 x 16 pixel blocks, cyb x cxb per map.
+struct ConvGeom {
+    int cH, cW, cimg, cyb, cxb;
+};
+
 template <int BN>
 struct GemmSmem {
     static constexpr int STAGES = 4;
@@ -227,11 +233,19 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 // ROPE_PF: bf16 output whose tiles may need RoPE, with the row's (cos, sin)
 // pairs held in registers (a separate instantiation: the register budget of
 // the other epilogues does not carry them).
-template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF>
+// CONV3: the A operand is a 3x3 / pad-1 convolution's implicit im2col: K =
+// 9 taps x C channels in tap-major order (ky * 3 + kx, then c), each K block
+// of 64 one 4-D TMA load of the input map (C, W, H, image) at the tap's
+// shifted pixel block -- rows and columns outside the map read as zero, so
+// the padding costs nothing and no im2col is ever written. An M tile is an
+// 8 x 16 pixel block (row r = y * 16 + x), and each epilogue warp's 32 rows
+// (two pixel rows) leave as one 4-D TMA store into the NHWC output.
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, const GemmEpi p)
+                        const __grid_constant__ CUtensorMap tmC, const GemmEpi p,
+                        const ConvGeom cg)
 {
     using L = GemmSmem<BN>;
     constexpr int STAGES = L::STAGES;
@@ -273,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_m = (p.M + BM - 1) / BM;
+    const int num_m = CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM;
     const int num_n = (p.N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int kblocks = (p.K + BK - 1) / BK;
@@ -288,6 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+                int img = 0, py0 = 0, px0 = 0;
+                if constexpr (CONV3) {
+                    const int mt = t / num_n;
+                    img = mt / (cg.cyb * cg.cxb);
+                    py0 = ((mt / cg.cxb) % cg.cyb) * 8;
+                    px0 = (mt % cg.cxb) * 16;
+                }
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, p.err, abort_flag)) {
                         ok = false;
@@ -295,7 +316,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t *sa = smem + stage * L::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+                    if constexpr (CONV3) {
+                        const int cblocks = p.K / (9 * BK), tap = kb / cblocks;
+                        tma_load_4d(sa, &tmA, &full[stage], (kb % cblocks) * BK,
+                                    px0 + tap % 3 - 1, py0 + tap / 3 - 1, img);
+                    }
+                    else
+                        tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
                     tma_load_2d(sa + L::A_BYTES, &tmB, &full[stage], kb * BK, n0);
                     issued_mask |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -370,8 +397,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tmap(&tmC);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
-            const int r0 = m0 + quarter * 32;
-            const int m = r0 + lane;
+            int r0 = m0 + quarter * 32;
+            int m = r0 + lane;
+            int cimg = 0, cy = 0, cx0 = 0;
+            if constexpr (CONV3) {
+                // this warp's rows: pixel rows cy, cy + 1 of the block, x
+                // cx0 .. cx0 + 15; m = the pixel's index in the NHWC output
+                // (p.M when outside the map)
+                const int mt = t / num_n;
+                cimg = mt / (cg.cyb * cg.cxb);
+                cy = ((mt / cg.cxb) % cg.cyb) * 8 + 2 * quarter;
+                cx0 = (mt % cg.cxb) * 16;
+                const int py = cy + lane / 16, px = cx0 + lane % 16;
+                m = (py < cg.cH && px < cg.cW) ? (cimg * cg.cH + py) * cg.cW + px : p.M;
+                r0 = cy < cg.cH ? 0 : p.M;  // the chunk's store is issued when r0 < p.M
+            }
             const int rrow = p.rope.mode ? rope_row(p.rope, m < p.M ? m : 0) : 0;
             // Global reads issued before the accumulator wait, so that their
             // latency hides behind the tile's main loop: with bf16 output the
@@ -487,9 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0 && r0 < p.M) {
-                        tma_store_2d(&tmC, smem + L::EPI_OFF + ew * kEpiBufs * kStageTile +
-                                               buf * kStageTile,
-                                     n, r0);
+                        const void *src = smem + L::EPI_OFF + ew * kEpiBufs * kStageTile +
+                                          buf * kStageTile;
+                        if constexpr (CONV3)
+                            tma_store_4d(&tmC, src, n, cx0, cy, cimg);
+                        else
+                            tma_store_2d(&tmC, src, n, r0);
                         bulk_commit();
                     }
                     buf = (buf + 1) % kEpiBufs;
@@ -517,19 +560,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false>
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false, bool CONV3 = false>
 int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
-           const GemmEpi &p, int num_sms, cudaStream_t s)
+           const GemmEpi &p, int num_sms, cudaStream_t s,
+           const ConvGeom &cg = ConvGeom{0, 0, 0, 0, 0})
 {
     using L = GemmSmem<BN>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
-    const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM) *
+                      ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, tc, p);
+    kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, tc, p, cg);
     return (int)cudaGetLastError();
 }
 
@@ -594,4 +639,52 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     if (BN == 128)
         return launch_bn<128>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
     return launch_bn<256>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
+}
+
+extern "C" int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C, const void *Wt,
+                                 int N, const float *bias, const float *R, void *out,
+                                 int out_bf16, int *err, int num_sms, k_stream s)
+{
+    using namespace sam3;
+    if (nimg <= 0 || H <= 0 || W <= 0 || C <= 0 || C % BK || N <= 0 || N % 64 ||
+        (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) ||
+        (R && (reinterpret_cast<uintptr_t>(R) & 15)))
+        return K_EARG;
+    const int BN = N <= 128 ? 128 : 256;
+    const int K = 9 * C;
+    CUtensorMap ta, tb, tc;
+    if (!make_tmap_nhwc(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, X, (uint64_t)nimg,
+                        (uint64_t)H, (uint64_t)W, (uint64_t)C, BK, 16, 8) ||
+        !make_tmap_bf16(&tb, Wt, (uint64_t)N, (uint64_t)K, (uint64_t)K, (uint32_t)BN) ||
+        !(out_bf16 ? make_tmap_nhwc(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, (uint64_t)nimg,
+                                    (uint64_t)H, (uint64_t)W, (uint64_t)N, 64, 16, 2)
+                   : make_tmap_nhwc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, (uint64_t)nimg,
+                                    (uint64_t)H, (uint64_t)W, (uint64_t)N, 32, 16, 2)))
+        return K_ETMAP;
+    GemmEpi p;
+    p.M = nimg * H * W;
+    p.N = N;
+    p.K = K;
+    p.C = out;
+    p.ldc = N;
+    p.bias = bias;
+    p.R = R;
+    p.ldr = N;
+    p.rmod = 1;  // R: one row added to every pixel
+    p.alpha = 1.0f;
+    p.act = K_ACT_NONE;
+    p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
+    p.err = err;
+    ConvGeom cg;
+    cg.cH = H;
+    cg.cW = W;
+    cg.cimg = nimg;
+    cg.cyb = (H + 7) / 8;
+    cg.cxb = (W + 15) / 16;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
+    if (BN == 128)
+        return out_bf16 ? launch<128, true, true, false, true>(ta, tb, tc, p, num_sms, st, cg)
+                        : launch<128, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
+    return out_bf16 ? launch<256, true, true, false, true>(ta, tb, tc, p, num_sms, st, cg)
+                    : launch<256, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
 }

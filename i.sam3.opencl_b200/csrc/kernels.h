@@ -45,6 +45,16 @@ int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const void *B,
                    const struct k_rope *rope, int *err, int num_sms,
                    k_stream s);
 
+/* 3x3 / pad-1 convolution as an implicit tcgen05 GEMM: X bf16 [nimg, H, W, C]
+ * (C % 64 == 0), Wt bf16 [N, 9C] in tap-major column order ((ky*3 + kx)*C +
+ * c), out [nimg, H, W, N] fp32 or bf16 (out_bf16) = conv + bias[n]
+ * (+ R[n], one fp32 row added to every pixel, when R != NULL). N % 64 == 0,
+ * 16-byte aligned buffers. */
+int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C,
+                      const void *Wt, int N, const float *bias, const float *R,
+                      void *out, int out_bf16, int *err, int num_sms,
+                      k_stream s);
+
 /* Reference-contract GEMM on CUDA cores (any strides/offsets, fp32 math):
  * C = act(alpha * A op(B) + bias) + R, batched with the two-level strides of
  * sam3_kernels.cl:57-69. Operand dtypes: 0 fp32, 1 bf16, 2 fp16. */

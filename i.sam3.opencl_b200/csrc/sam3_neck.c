@@ -12,11 +12,12 @@
  *     scatter pass adds the bias, applies the activation and writes the
  *     upsampled map in bf16 (the next GEMM's operand);
  *   - 1x1: a GEMM with the bias in its epilogue, bf16 out;
- *   - 3x3 / pad 1: a bf16 im2col with tap-major columns ((ky * 3 + kx) *
- *     256 + c; each tap one contiguous 512-byte copy) and a GEMM with K =
- *     2304 against the weight permuted to the same order, one tile at a time
- *     (the reference bands the im2col by 128 MB); the image embedding's
- *     no_mem_embed add (sam3_model.c:1109) is that GEMM's residual.
+ *   - 3x3 / pad 1: an implicit GEMM (k_conv3x3_bf16_tc) against the weight
+ *     permuted to tap-major columns ((ky * 3 + kx) * 256 + c): each K block
+ *     is a TMA load of the input map at the tap's shifted 8 x 16 pixel
+ *     block, zero outside the map, so no im2col is written (the reference
+ *     materialises one in 128 MB bands); the image embedding's no_mem_embed
+ *     add (sam3_model.c:1109) is the GEMM's broadcast residual.
  * The conv_s0 / conv_s1 projections read the level outputs in bf16 and
  * write the decoder's fp32 feat_s0 / feat_s1. */
 #include <stdlib.h>
@@ -36,7 +37,6 @@ struct cb_neck {
     void *a0;               /* bf16 [4R, E / 2] */
     void *a1;               /* bf16 [16R, E / 4] */
     void *c1;               /* bf16 [16R, 256] */
-    void *col;              /* bf16 [16T, 2304], one tile */
     void *c3;               /* bf16 [16R, 256] */
 };
 
@@ -72,7 +72,6 @@ void cb_neck_free(cb_neck *n)
     cudaFree(n->a0);
     cudaFree(n->a1);
     cudaFree(n->c1);
-    cudaFree(n->col);
     cudaFree(n->c3);
     free(n);
 }
@@ -112,7 +111,6 @@ int cb_neck_create(cb_backend *b, int grid, int embed, int max_tiles, cb_neck **
     A(n->a0, 4 * R * (embed / 2) * 2);
     A(n->a1, 16 * R * (embed / 4) * 2);
     A(n->c1, 16 * R * NECK_DIM * 2);
-    A(n->col, 16 * T * 9 * NECK_DIM * 2);
     A(n->c3, 16 * R * NECK_DIM * 2);
 #undef A
     if (rc != CB_OK) {
@@ -240,23 +238,19 @@ static int convt(cb_neck *n, const void *A, int nt, int H, int W, int cin, int c
     return CB_OK;
 }
 
-/* conv3x3 (sam3_model.c:1032-1054) of nt maps side x side x 256 (bf16 X),
- * one tile at a time: im2col, GEMM + bias (+ R broadcast row) into out. */
+/* conv3x3 (sam3_model.c:1032-1054) of nt maps side x side x 256 (bf16 X)
+ * as one implicit tcgen05 GEMM (no im2col), + bias (+ R broadcast row). */
 static int conv3(cb_neck *n, const void *X, int nt, int side, int wi, int bi, void *out,
                  int out_bf16, const float *R)
 {
     cb_backend *b = n->b;
-    const long T = (long)side * side;
-    int t;
+    const double rows = (double)nt * side * side;
 
-    for (t = 0; t < nt; t++) {
-        LAUNCH("neck_im2col", 0, (double)T * 9 * NECK_DIM * 2 * 2,
-               k_im2col3x3_bf16((const char *)X + (size_t)t * T * NECK_DIM * 2, side, side,
-                                NECK_DIM, 0, T, n->col, (k_stream)b->stream));
-        CB_TRY(ngemm(n, "neck_gemm_conv3x3", n->col, T, 9 * NECK_DIM, NECK_DIM, wi, bi,
-                     (char *)out + (size_t)t * T * NECK_DIM * (out_bf16 ? 2 : 4), out_bf16, R,
-                     R ? 1 : 0));
-    }
+    LAUNCH("neck_conv3x3", 2.0 * rows * 9 * NECK_DIM * NECK_DIM,
+           rows * NECK_DIM * 2 + 9.0 * NECK_DIM * NECK_DIM * 2 + rows * NECK_DIM * (out_bf16 ? 2 : 4),
+           k_conv3x3_bf16_tc(X, nt, side, side, NECK_DIM, n->w[wi], NECK_DIM,
+                             (const float *)n->w[bi], R, out, out_bf16, b->d_err, b->num_sms,
+                             (k_stream)b->stream));
     return CB_OK;
 }
 

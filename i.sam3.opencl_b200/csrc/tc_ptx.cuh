@@ -125,6 +125,30 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 4-D tile load (innermost coordinate first); coordinates outside the
+// tensor read as zero.
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+        "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 4-D tile store (elements outside the tensor are not written).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *smem_src,
+                                             int32_t c0, int32_t c1, int32_t c2, int32_t c3)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(smem_src))
+        : "memory");
+}
+
 // Tile store shared -> global through a tensor map (out-of-range rows and
 // columns of the box are not written), tracked by the bulk-group mechanism.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src,

@@ -71,4 +71,25 @@ inline bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t e
            CUDA_SUCCESS;
 }
 
+// 4-D map over n images of h x w pixels of c channels (channels innermost,
+// packed), box box_c x box_w x box_h x 1 with 128-byte swizzle (box_c *
+// esize = 128 or less). Out-of-range elements read as zero; stores clip.
+inline bool make_tmap_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t esize,
+                           const void *base, uint64_t n, uint64_t h, uint64_t w, uint64_t c,
+                           uint32_t box_c, uint32_t box_w, uint32_t box_h)
+{
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || ((c * esize) & 15) ||
+        box_c * esize > 128 || box_w > 256 || box_h > 256 || !n || !h || !w || !c)
+        return false;
+    cuuint64_t dims[4] = {c, w, h, n};
+    cuuint64_t strides[3] = {c * esize, w * c * esize, h * w * c * esize};
+    cuuint32_t box[4] = {box_c, box_w, box_h, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(map, dtype, 4, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 }  // namespace sam3

@@ -38,7 +38,7 @@ def _run(cb, sb, neck, x, ntile, grid):
     return res
 
 
-@pytest.mark.parametrize("grid", [24, 72])
+@pytest.mark.parametrize("grid", [13, 24, 72])
 def test_neck_vs_oracle(cb, sb, ob, grid):
     seed = 51
     neck = sb.Neck(cb, grid=grid, embed=1024, max_tiles=1)
