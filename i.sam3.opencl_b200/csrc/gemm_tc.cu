@@ -60,11 +60,13 @@ struct ConvGeom {
     int cH, cW, cimg, cyb, cxb;
 };
 
-template <int BN>
+// PAIR: each CTA of a pair holds half of the B tile (BN / 2 rows), so a
+// stage is 32 KB and six fit.
+template <int BN, bool PAIR = false>
 struct GemmSmem {
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = PAIR ? 6 : 4;
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kEpiBufs * kStageTile;
@@ -240,14 +242,24 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 // the padding costs nothing and no im2col is ever written. An M tile is an
 // 8 x 16 pixel block (row r = y * 16 + x), and each epilogue warp's 32 rows
 // (two pixel rows) leave as one 4-D TMA store into the NHWC output.
-template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false>
+// PAIR: a cluster of two CTAs (the two SMs of a TPC) computes 256 x BN
+// tiles with cta_group::2 MMAs: each CTA loads its 128 rows of A and half of
+// the B tile into its own shared memory, both signalling rank 0's full
+// barrier; rank 0 issues 256 x BN x 16 MMAs whose accumulator rows 0-127
+// land in its tensor memory and 128-255 in rank 1's, and its commits arrive
+// on both CTAs' barriers; each CTA's epilogue stores its own 128 rows and
+// releases the accumulator on rank 0's barrier. Per SM this halves the B
+// tile traffic from L2 into shared memory.
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false,
+          bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmEpi p,
                         const ConvGeom cg)
 {
-    using L = GemmSmem<BN>;
+    static_assert(!(PAIR && CONV3), "pair tiles are row blocks");
+    using L = GemmSmem<BN, PAIR>;
     constexpr int STAGES = L::STAGES;
     constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
     constexpr int NCHUNK = BN / CW;
@@ -264,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
@@ -272,22 +285,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], kEpiWarps);
+            mbar_init(&tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 2 * BN);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, 2 * BN);
+            tmem_relinquish_pair();
+        }
+        else {
+            tmem_alloc(tmem_slot, 2 * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync_all();  // both CTAs' barriers exist before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_m = CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM;
+    constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile
+    const int first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int num_m = CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + TM - 1) / TM;
     const int num_n = (p.N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int kblocks = (p.K + BK - 1) / BK;
@@ -300,8 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, last_parity = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+            for (int t = first; t < num_tiles && ok; t += step) {
+                const int m0 = (t / num_n) * TM + (int)rank * BM, n0 = (t % num_n) * BN;
                 int img = 0, py0 = 0, px0 = 0;
                 if constexpr (CONV3) {
                     const int mt = t / num_n;
@@ -310,11 +334,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     px0 = (mt % cg.cxb) * 16;
                 }
                 for (int kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, p.err, abort_flag)) {
+                    if (!(PAIR ? mbar_wait_cluster(&empty[stage], phase ^ 1, p.err, abort_flag)
+                               : mbar_wait(&empty[stage], phase ^ 1, p.err, abort_flag))) {
                         ok = false;
                         break;
                     }
                     uint8_t *sa = smem + stage * L::STAGE_BYTES;
+                    if constexpr (PAIR) {
+                        if (rank == 0)
+                            mbar_arrive_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+                        const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
+                        tma_load_2d_pair(sa, &tmA, fb, kb * BK, m0);
+                        tma_load_2d_pair(sa + L::A_BYTES, &tmB, fb, kb * BK,
+                                         n0 + (int)rank * (BN / 2));
+                        issued_mask |= 1u << stage;
+                        last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
                     if constexpr (CONV3) {
                         const int cblocks = p.K / (9 * BK), tap = kb / cblocks;
@@ -332,9 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // Let every copy this thread issued land before the CTA exits.
+            // Let every copy this thread issued land before the CTA exits
+            // (in a pair, rank 0's barriers count both CTAs' copies; rank 1
+            // is held by the closing cluster barrier).
             for (int s = 0; s < STAGES; s++)
-                if (issued_mask & (1u << s)) {
+                if (rank == 0 && (issued_mask & (1u << s))) {
                     volatile int no_abort = 0;
                     mbar_wait(&full[s], (last_parity >> s) & 1, p.err, &no_abort);
                 }
@@ -342,47 +384,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     else if (warp == 1) {
         if (elect_one()) {
-            constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, 0, 0);
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, abort_flag))
-                    break;
-                tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(&full[stage], phase, p.err, abort_flag)) {
-                        ok = false;
+            if (rank == 0) {
+                constexpr uint32_t idesc = idesc_bf16_f32(TM, BN, 0, 0);
+                int stage = 0;
+                uint32_t phase = 0;
+                int acc = 0;
+                uint32_t acc_phase = 0;
+                bool ok = true;
+                for (int t = first; t < num_tiles && ok; t += step) {
+                    if (!(PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.err, abort_flag)
+                               : mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, abort_flag)))
                         break;
-                    }
                     tc_fence_after();
-                    const uint32_t sa = smem_addr(smem + stage * L::STAGE_BYTES);
-                    const uint32_t sb = sa + L::A_BYTES;
+                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                    for (int kb = 0; kb < kblocks; kb++) {
+                        if (!mbar_wait(&full[stage], phase, p.err, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = smem_addr(smem + stage * L::STAGE_BYTES);
+                        const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / 16; k++)
-                        tc_mma(d, sw128_desc(sa + k * 32, 16, 1024),
-                               sw128_desc(sb + k * 32, 16, 1024), idesc, (kb | k) != 0);
-                    tc_commit(&empty[stage]);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
+                        for (int k = 0; k < BK / 16; k++) {
+                            if constexpr (PAIR)
+                                tc_mma_pair(d, sw128_desc(sa + k * 32, 16, 1024),
+                                            sw128_desc(sb + k * 32, 16, 1024), idesc,
+                                            (kb | k) != 0);
+                            else
+                                tc_mma(d, sw128_desc(sa + k * 32, 16, 1024),
+                                       sw128_desc(sb + k * 32, 16, 1024), idesc, (kb | k) != 0);
+                        }
+                        if constexpr (PAIR)
+                            tc_commit_pair(&empty[stage], 3);
+                        else
+                            tc_commit(&empty[stage]);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
                     }
+                    if (!ok)
+                        break;
+                    if constexpr (PAIR)
+                        tc_commit_pair(&tfull[acc], 3);
+                    else
+                        tc_commit(&tfull[acc]);
+                    acc ^= 1;
+                    if (acc == 0)
+                        acc_phase ^= 1;
                 }
-                if (!ok)
-                    break;
-                tc_commit(&tfull[acc]);
-                acc ^= 1;
-                if (acc == 0)
-                    acc_phase ^= 1;
+                // Drain: one arrival (on both CTAs' barriers in a pair) once
+                // every MMA issued above has completed.
+                if constexpr (PAIR)
+                    tc_commit_pair(drain, 3);
+                else
+                    tc_commit(drain);
             }
-            // Drain: wait until every MMA issued above has completed, so
-            // tensor memory is idle before it is freed.
-            tc_commit(drain);
+            // Tensor memory is idle before it is freed.
             volatile int no_abort = 0;
-            mbar_wait(drain, 0, p.err, &no_abort);
+            if constexpr (PAIR)
+                mbar_wait_cluster(drain, 0, p.err, &no_abort);
+            else
+                mbar_wait(drain, 0, p.err, &no_abort);
         }
     }
     else {
@@ -395,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         if (TMA_STORE && lane == 0)
             prefetch_tmap(&tmC);
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+        for (int t = first; t < num_tiles; t += step) {
+            const int m0 = (t / num_n) * TM + (int)rank * BM, n0 = (t % num_n) * BN;
             int r0 = m0 + quarter * 32;
             int m = r0 + lane;
             int cimg = 0, cy = 0, cx0 = 0;
@@ -440,7 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < CW / 4; j++)
                     rnext[j] = *reinterpret_cast<const float4 *>(rrowp + half * CW + 4 * j);
             }
-            const bool ok = mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
+            const bool ok = PAIR ? mbar_wait_cluster(&tfull[acc], acc_phase, p.err, abort_flag)
+                                 : mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
             if (!__all_sync(0xffffffffu, ok))
                 break;
             tc_fence_after();
@@ -542,8 +607,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&tempty[acc]);
+            if (lane == 0) {
+                if constexpr (PAIR)
+                    mbar_arrive_cluster(mapa_shared(smem_addr(&tempty[acc]), 0));
+                else
+                    mbar_arrive(&tempty[acc]);
+            }
             acc ^= 1;
             if (acc == 0)
                 acc_phase ^= 1;
@@ -554,9 +623,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    // In a pair, neither CTA leaves (nor frees tensor memory) while the
+    // other's MMAs, copies or arrivals may still touch its shared memory.
+    if constexpr (PAIR)
+        cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 2 * BN);
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem_base, 2 * BN);
+        else
+            tmem_dealloc(tmem_base, 2 * BN);
     }
 }
 
@@ -576,6 +652,56 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
     const int grid = tiles < num_sms ? tiles : num_sms;
     kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, tc, p, cg);
     return (int)cudaGetLastError();
+}
+
+// Co-resident clusters of two CTAs of the pair kernel, per device (0: not
+// known yet; -1: none).
+static int g_pair_clusters[64];
+
+// The pair kernel over 256 x 256 tiles: a persistent grid of as many CTA
+// pairs as can be resident at once (each cluster on the two SMs of a TPC).
+// Returns 1 when pairs cannot be launched here (the caller uses single CTAs).
+template <bool OUT_BF16, bool ROPE_PF>
+int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
+                const GemmEpi &p, int num_sms, cudaStream_t s)
+{
+    constexpr int BN = 256;
+    using L = GemmSmem<BN, true>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, false, true>;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return 1;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    if (e != cudaSuccess)
+        return (int)e;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms / 2 > 0 ? num_sms / 2 : 1));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (g_pair_clusters[dev] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = -1;
+        }
+        g_pair_clusters[dev] = n;
+    }
+    if (g_pair_clusters[dev] < 0)
+        return 1;
+    const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
+    const int pairs = tiles < g_pair_clusters[dev] ? tiles : g_pair_clusters[dev];
+    cfg.gridDim = dim3(2 * pairs);
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, ConvGeom{0, 0, 0, 0, 0});
+    return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
 }
 
 template <int BN>
@@ -607,7 +733,7 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 15))
         return K_EARG;
     const int BN = N <= 128 ? 128 : 256;
-    CUtensorMap ta, tb, tc;
+    CUtensorMap ta, tb, tc, tb_half;
     if (!make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM) ||
         !make_tmap_bf16(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)BN))
         return K_ETMAP;
@@ -638,6 +764,21 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
     if (BN == 128)
         return launch_bn<128>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
+    // CTA pairs (256 x 256 tiles) when there are enough tiles to give every
+    // pair of SMs at least one, with TMA stores, and the main loop carries
+    // the tile: bf16 output, or K above 1024 (an fp32-output GEMM with short
+    // K, like the attention projection, is bound by its epilogue's HBM
+    // traffic and measured 1 % slower in pairs).
+    const long pair_tiles = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+    if (tma && pair_tiles >= num_sms / 2 && (c_bf16 || K > 1024) &&
+        make_tmap_bf16(&tb_half, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128)) {
+        const bool rope64 = p.rope.mode && p.rope.hd == 64;
+        const int rc = c_bf16 ? (rope64 ? launch_pair<true, true>(ta, tb_half, tc, p, num_sms, st)
+                                        : launch_pair<true, false>(ta, tb_half, tc, p, num_sms, st))
+                              : launch_pair<false, false>(ta, tb_half, tc, p, num_sms, st);
+        if (rc != 1)
+            return rc;
+    }
     return launch_bn<256>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
 }
 

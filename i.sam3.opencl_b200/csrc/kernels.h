@@ -147,14 +147,11 @@ int k_dec_up2_logits(const float *G, const float *bias, const float *feat,
 
 /* SimpleFPN neck (neck.cu). convt_scatter_bf16: G fp32 [n*H*W, 4C] with
  * sub-pixel-major columns (d*C + co) -> out bf16 [n, 2H, 2W, C] =
- * act(G + bias). im2col3x3_bf16: rows [t0, t0 + rows) of a bf16 H x W x C
- * map -> out bf16 [rows, 9C], columns (ky*3 + kx)*C + c, zero padding.
- * permute_conv3x3_bf16: fp32 [cout, cin, 3, 3] -> bf16 [cout, 9 cin] in
- * that column order. C % 8 == 0, 16-byte aligned buffers. */
+ * act(G + bias). permute_conv3x3_bf16: fp32 [cout, cin, 3, 3] -> bf16
+ * [cout, 9 cin], columns (ky*3 + kx)*cin + c (k_conv3x3_bf16_tc's K order).
+ * C % 8 == 0, 16-byte aligned buffers. */
 int k_convt_scatter_bf16(const float *G, const float *bias, int n, int H,
                          int W, int C, int act, void *out, k_stream s);
-int k_im2col3x3_bf16(const void *X, int H, int W, int C, long t0, long rows,
-                     void *out, k_stream s);
 int k_permute_conv3x3_bf16(const float *src, int cout, int cin, void *dst,
                            k_stream s);
 

@@ -1,10 +1,10 @@
 // SPDX-License-Identifier: Unlicense
 // Data-movement kernels of the SimpleFPN neck (sam3_model.c neck_level
 // :1071-1095, conv3x3 :1032-1054, convt2x2 :1058-1065): the 2x2 / stride-2
-// ConvTranspose scatter from its GEMM form, and the 3x3 / pad-1 im2col that
-// turns the convolution into a GEMM. The matrix work itself runs on the
-// tcgen05 GEMM (gemm_tc.cu). Both kernels move 16-byte chunks of channels:
-// every load and store is coalesced.
+// ConvTranspose scatter from its GEMM form and the 3x3 weight permutation.
+// The matrix work itself, the 3x3 convolutions included, runs on the tcgen05
+// GEMM (gemm_tc.cu). The scatter moves 16-byte chunks of channels: every
+// load and store is coalesced.
 #include "kernels.h"
 
 #include <cuda_bf16.h>
@@ -70,31 +70,6 @@ __global__ void __launch_bounds__(256) convt_scatter_bf16_kernel(const float4 *_
     }
 }
 
-// 3x3 / pad-1 im2col (im2col3x3, sam3_kernels.cl:746-760) of rows
-// [t0, t0 + rows) of an H x W x C bf16 map, with the columns in tap-major
-// order (ky * 3 + kx) * C + c (the convolution weight is stored in the same
-// order), so each tap is a contiguous copy of the neighbour's channels;
-// zero outside the map. One thread per 8 channels of one tap.
-__global__ void __launch_bounds__(256) im2col3x3_bf16_kernel(const uint4 *__restrict__ X, int H,
-                                                             int W, int C, long t0, long total,
-                                                             uint4 *__restrict__ out)
-{
-    const int c8 = C >> 3;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long)gridDim.x * blockDim.x) {
-        const int j = (int)(i % c8);
-        const long q = i / c8;
-        const int tap = (int)(q % 9);
-        const long r = q / 9;  // row of the band
-        const long t = t0 + r;
-        const int y = (int)(t / W) + tap / 3 - 1, x = (int)(t % W) + tap % 3 - 1;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (y >= 0 && y < H && x >= 0 && x < W)
-            v = X[((long)y * W + x) * c8 + j];
-        out[i] = v;
-    }
-}
-
 }  // namespace
 }  // namespace sam3
 
@@ -116,22 +91,9 @@ extern "C" int k_convt_scatter_bf16(const float *G, const float *bias, int n, in
     return (int)cudaGetLastError();
 }
 
-extern "C" int k_im2col3x3_bf16(const void *X, int H, int W, int C, long t0, long rows, void *out,
-                                k_stream s)
-{
-    if (H <= 0 || W <= 0 || C <= 0 || (C & 7) || t0 < 0 || rows <= 0 ||
-        t0 + rows > (long)H * W || (reinterpret_cast<uintptr_t>(X) & 15) ||
-        (reinterpret_cast<uintptr_t>(out) & 15))
-        return K_EARG;
-    const long total = rows * 9 * (C >> 3);
-    const int grid = grid_for(total, 256);
-    im2col3x3_bf16_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(
-        reinterpret_cast<const uint4 *>(X), H, W, C, t0, total, reinterpret_cast<uint4 *>(out));
-    return (int)cudaGetLastError();
-}
-
 // Conv2d weight [cout, cin, 3, 3] (fp32) -> bf16 [cout, 9 * cin] with
-// columns tap-major ((ky * 3 + kx) * cin + c), the im2col order above.
+// columns tap-major ((ky * 3 + kx) * cin + c), the K order of the
+// implicit-GEMM 3x3 convolution (k_conv3x3_bf16_tc).
 __global__ void permute_conv3x3_kernel(const float *__restrict__ src, int cout, int cin,
                                        __nv_bfloat16 *__restrict__ dst)
 {

@@ -114,6 +114,79 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     }
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on the two SMs of one TPC: rank 0 issues the
+// pair's tcgen05.mma (cta_group::2) over both CTAs' shared memory and
+// tensor memory.
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of the variable at shared::cta address
+// `addr` in the CTA of the cluster with rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// All threads of both CTAs: every shared-memory write before it (barrier
+// initialisation included) is visible to the cluster after it.
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrival on an mbarrier of any CTA of the cluster (shared::cluster
+// address), releasing this thread's prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for a barrier that CTAs of the cluster other than this one
+// also signal (acquire at cluster scope); bounded in the same way.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int *err,
+                                                  volatile int *abort_flag)
+{
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait_cluster(a, parity))
+        return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try_wait_cluster(a, parity))
+            return true;
+        if ((it & 63) == 0) {
+            if (*abort_flag)
+                return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                atomicCAS(err, kErrNone, kErrWaitTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t x, int32_t y)
@@ -158,6 +231,18 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
         "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
             reinterpret_cast<uint64_t>(map)),
         "r"(x), "r"(y), "r"(smem_addr(smem_src))
+        : "memory");
+}
+
+// 2-D tile load by either CTA of a pair, completing on the mbarrier at
+// shared::cluster address `bar` (rank 0's, which counts both CTAs' bytes).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorMap *map,
+                                                 uint32_t bar, int32_t x, int32_t y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
 
@@ -212,6 +297,27 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
                  : "memory");
 }
 
+// Pair forms, issued by the same warp in both CTAs: the allocation is
+// made at the same address in both CTAs' tensor memory.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before()
 {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -245,6 +351,32 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Pair MMA (issued by rank 0 only): D rows 0..M/2-1 in rank 0's tensor
+// memory, M/2..M-1 in rank 1's; A rows split the same way between the two
+// CTAs' shared memory, B rows (the N dimension) half in each; the
+// descriptors name the same shared-memory offsets in both CTAs.
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One arrival on the mbarrier at the same shared-memory offset in each CTA
+// of `cta_mask` once the pair MMAs issued so far by this thread complete.
+__device__ __forceinline__ void tc_commit_pair(uint64_t *bar, uint16_t cta_mask)
+{
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_addr(bar)),
+        "h"(cta_mask)
         : "memory");
 }
 

@@ -60,8 +60,12 @@ def test_read_write_roundtrip(cb, sb):
 
 
 # ------------------------------------------------------------------ GEMM
+# (9000, 1000, 2048) and, with bf16 output, (10317, 576, 200) (ragged rows,
+# columns and K) and (5184, 1024, 1024) run on the CTA-pair kernel (enough
+# 256 x 256 tiles, a main loop worth pairing); the others on single CTAs.
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 200, 136), (5184, 1024, 1024),
-                                   (129, 3072, 1024), (77, 64, 40)])
+                                   (129, 3072, 1024), (77, 64, 40), (10317, 576, 200),
+                                   (9000, 1000, 2048)])
 @pytest.mark.parametrize("out_bf16", [False, True])
 def test_gemm_tc_vs_fp32_product(cb, sb, M, N, K, out_bf16):
     g = torch.Generator().manual_seed(M * 7 + N + K)
