@@ -35,10 +35,6 @@ constexpr int BK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStageTile = 32 * 128;  // one warp's 32 rows x 128 bytes
-// Staging tiles per epilogue warp. One: the shared memory goes to a fourth
-// A/B stage instead, which the main loop gains more from than the epilogue
-// loses by waiting for its previous TMA store to be read.
-constexpr int kEpiBufs = 1;
 
 struct GemmEpi {
     int M, N, K;
@@ -60,16 +56,20 @@ struct ConvGeom {
     int cH, cW, cimg, cyb, cxb;
 };
 
-// PAIR: each CTA of a pair holds half of the B tile (BN / 2 rows), so a
-// stage is 32 KB and six fit.
+// EPI_BUFS: staging tiles per epilogue warp. Single CTAs: one; the shared
+// memory goes to a fourth A/B stage instead, which the main loop gains more
+// from than the epilogue loses by waiting for its previous TMA store to be
+// read. PAIR: each CTA of a pair holds half of the B tile (BN / 2 rows), so
+// a stage is 32 KB.
 template <int BN, bool PAIR = false>
 struct GemmSmem {
     static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int EPI_BUFS = PAIR ? 1 : 1;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kEpiBufs * kStageTile;
+    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * EPI_BUFS * kStageTile;
     // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort
     static constexpr int BYTES = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
     static_assert(BYTES <= 232448, "GEMM shared memory");
@@ -79,28 +79,31 @@ struct GemmSmem {
 // values, with erf from Abramowitz & Stegun 7.1.26 (Hastings):
 //   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-z^2),
 //   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
-// so GELU(x) = x (1 - h) for x >= 0 and x h for x < 0, with
-// h = erfc(|x| / sqrt 2) / 2 = t (...) 2^(-x^2 log2(e) / 2 - 1). Two MUFU
-// operations per value (reciprocal, 2^x) and the polynomial in packed fp32;
-// the result differs from the erf form by at most 4.2e-7 |x|-relative, far
-// below the bf16 rounding of the output it feeds.
+// so with h = erfc(|x| / sqrt 2) / 2 = t (...) 2^(-x^2 log2(e) / 2 - 1),
+// GELU(x) = x (1 - h) for x >= 0 and x h for x < 0, i.e. max(x, 0) - |x| h
+// for every x. Two MUFU operations per value (reciprocal, 2^x); the
+// polynomial and products run in packed fp32. The result differs from the
+// erf form by at most 4.2e-7 |x|-relative, far below the bf16 rounding of
+// the output it feeds.
 __device__ __forceinline__ void gelu_pair(float &x0, float &x1)
 {
-    const float kP = 0.3275911f;
-    const float t0 = rcp_approx(fmaf(kP * 0.70710678118654752f, fabsf(x0), 1.0f));
-    const float t1 = rcp_approx(fmaf(kP * 0.70710678118654752f, fabsf(x1), 1.0f));
+    const float kP = 0.3275911f * 0.70710678118654752f;
+    const float kE = -0.72134752044448170f;  // -log2(e) / 2
+    const float t0 = rcp_approx(fmaf(kP, fabsf(x0), 1.0f));
+    const float t1 = rcp_approx(fmaf(kP, fabsf(x1), 1.0f));
+    const uint64_t x = f2_make(x0, x1);
     const uint64_t t = f2_make(t0, t1);
     uint64_t q = fma2(f2_make(1.061405429f, 1.061405429f), t, f2_make(-1.453152027f, -1.453152027f));
     q = fma2(q, t, f2_make(1.421413741f, 1.421413741f));
     q = fma2(q, t, f2_make(-0.284496736f, -0.284496736f));
     q = fma2(q, t, f2_make(0.254829592f, 0.254829592f));
-    const float e0 = ex2_approx(fmaf(x0 * x0, -0.72134752044448170f, -1.0f));
-    const float e1 = ex2_approx(fmaf(x1 * x1, -0.72134752044448170f, -1.0f));
-    q = mul2(mul2(q, t), f2_make(e0, e1));
+    float g0, g1;
+    f2_split(fma2(mul2(x, f2_make(kE, kE)), x, f2_make(-1.0f, -1.0f)), g0, g1);
+    q = mul2(mul2(q, t), f2_make(ex2_approx(g0), ex2_approx(g1)));
     float h0, h1;
     f2_split(q, h0, h1);
-    x0 *= x0 >= 0.0f ? 1.0f - h0 : h0;
-    x1 *= x1 >= 0.0f ? 1.0f - h1 : h1;
+    x0 = fmaf(-fabsf(x0), h0, fmaxf(x0, 0.0f));
+    x1 = fmaf(-fabsf(x1), h1, fmaxf(x1, 0.0f));
 }
 
 // Table row of the RoPE rotation for output row m.
@@ -117,8 +120,9 @@ __device__ __forceinline__ int rope_row(const k_rope &r, int m)
 // Epilogue math on CW consecutive columns of row m starting at column n:
 // alpha, bias, activation, residual, RoPE (the reference's order). rv / rot,
 // when given, hold the chunk's residual values / (cos, sin) pairs already
-// loaded into registers; otherwise they are read here.
-template <int CW>
+// loaded into registers; otherwise they are read here. ACT false: the
+// activation is known to be none (not compiled in).
+template <int CW, bool ACT = true>
 __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, float (&v)[CW],
                                               int rrow, const float4 *rv, const float2 *rot)
 {
@@ -144,12 +148,12 @@ __device__ __forceinline__ void epilogue_math(const GemmEpi &p, int m, int n, fl
                     v[j] += __ldg(p.bias + n + j);
         }
     }
-    if (p.act == K_ACT_GELU) {
+    if (ACT && p.act == K_ACT_GELU) {
 #pragma unroll
         for (int j = 0; j < CW; j += 2)
             gelu_pair(v[j], v[j + 1]);
     }
-    else if (p.act == K_ACT_RELU) {
+    else if (ACT && p.act == K_ACT_RELU) {
 #pragma unroll
         for (int j = 0; j < CW; j++)
             v[j] = fmaxf(v[j], 0.0f);
@@ -233,8 +237,8 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 }
 
 // ROPE_PF: bf16 output whose tiles may need RoPE, with the row's (cos, sin)
-// pairs held in registers (a separate instantiation: the register budget of
-// the other epilogues does not carry them).
+// pairs held in registers and no activation (a separate instantiation: the
+// register budget of the other epilogues does not carry them).
 // CONV3: the A operand is a 3x3 / pad-1 convolution's implicit im2col: K =
 // 9 taps x C channels in tap-major order (ky * 3 + kx, then c), each K block
 // of 64 one 4-D TMA load of the input map (C, W, H, image) at the tap's
@@ -453,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ew = warp - 2;          // 0..7
         const int quarter = warp & 3;     // TMEM lane quarter this warp may read
         const int half = ew >> 2;         // which chunks of the tile (c % 2)
+        constexpr int kEpiBufs = L::EPI_BUFS;
         const uint32_t stage0 = smem_addr(smem + L::EPI_OFF + ew * kEpiBufs * kStageTile);
         int buf = 0;
         int acc = 0;
@@ -551,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int j = 0; j < 32; j++)
                                 v[j] = __uint_as_float(r[j]);
                         }
-                        epilogue_math<32>(p, m, n + h * 32, v, rrow, nullptr,
+                        epilogue_math<32, false>(p, m, n + h * 32, v, rrow, nullptr,
                                           rope_tile && n < 2 * p.rope.E ? rc + h * 16 : nullptr);
 #pragma unroll
                         for (int j = 0; j < 16; j++)
@@ -709,7 +714,7 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &t
               bool bf16, const GemmEpi &p, int num_sms, cudaStream_t s)
 {
     if (bf16)
-        return tma ? (p.rope.mode && p.rope.hd == 64
+        return tma ? (p.rope.mode && p.rope.hd == 64 && p.act == K_ACT_NONE
                           ? launch<BN, true, true, true>(ta, tb, tc, p, num_sms, s)
                           : launch<BN, true, true>(ta, tb, tc, p, num_sms, s))
                    : launch<BN, true, false>(ta, tb, tc, p, num_sms, s);
@@ -772,7 +777,7 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     const long pair_tiles = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
     if (tma && pair_tiles >= num_sms / 2 && (c_bf16 || K > 1024) &&
         make_tmap_bf16(&tb_half, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128)) {
-        const bool rope64 = p.rope.mode && p.rope.hd == 64;
+        const bool rope64 = p.rope.mode && p.rope.hd == 64 && p.act == K_ACT_NONE;
         const int rc = c_bf16 ? (rope64 ? launch_pair<true, true>(ta, tb_half, tc, p, num_sms, st)
                                         : launch_pair<true, false>(ta, tb_half, tc, p, num_sms, st))
                               : launch_pair<false, false>(ta, tb_half, tc, p, num_sms, st);
