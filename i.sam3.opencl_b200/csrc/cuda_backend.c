@@ -504,9 +504,27 @@ int cb_profile_entry(cb_backend *b, int i, const char **name, long *calls,
 
 int cb_set_stream(cb_backend *b, void *stream)
 {
+    cudaStream_t next;
+
     if (!b)
         return CB_EARG;
-    b->stream = stream ? (cudaStream_t)stream : b->own_stream;
+    next = stream ? (cudaStream_t)stream : b->own_stream;
+    if (next != b->stream) {
+        /* the backend's scratch buffer is reused by every launch: work on
+         * the new stream starts after the old stream's */
+        cudaEvent_t ev;
+
+        CB_TRY(cbi_enter(b));
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess)
+            return cbi_fail(b, CB_ECUDA, "set_stream: event");
+        if (cudaEventRecord(ev, b->stream) != cudaSuccess ||
+            cudaStreamWaitEvent(next, ev, 0) != cudaSuccess) {
+            cudaEventDestroy(ev);
+            return cbi_fail(b, CB_ECUDA, "set_stream: order");
+        }
+        cudaEventDestroy(ev);
+    }
+    b->stream = next;
     return CB_OK;
 }
 

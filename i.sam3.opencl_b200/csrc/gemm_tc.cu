@@ -48,6 +48,7 @@ struct GemmEpi {
     int act;
     k_rope rope;
     int *err;
+    int red;  // fp32 C updated in place: C += epilogue result by TMA reduce-add
 };
 
 // CONV3 geometry: 3x3 / pad-1 convolution of cimg maps cH x cW x (K / 9)
@@ -601,6 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                           buf * kStageTile;
                         if constexpr (CONV3)
                             tma_store_4d(&tmC, src, n, cx0, cy, cimg);
+                        else if (!OUT_BF16 && p.red)
+                            tma_reduce_add_2d(&tmC, src, n, r0);
                         else
                             tma_store_2d(&tmC, src, n, r0);
                         bulk_commit();
@@ -766,6 +769,16 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     else
         p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
     p.err = err;
+    // In-place residual (C = R, the residual stream x += f(x)): the epilogue
+    // leaves the residual read to L2 and reduce-adds its result into C, so
+    // no epilogue warp waits on residual loads. Same arithmetic: the fp32
+    // sum of the epilogue value and C's element, one rounding.
+    p.red = 0;
+    if (!c_bf16 && tma && R && reinterpret_cast<const void *>(R) == C && ldr == ldc &&
+        rmod == 0) {
+        p.R = nullptr;
+        p.red = 1;
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
     if (BN == 128)
         return launch_bn<128>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
@@ -821,6 +834,7 @@ extern "C" int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C, c
     p.act = K_ACT_NONE;
     p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
     p.err = err;
+    p.red = 0;
     ConvGeom cg;
     cg.cH = H;
     cg.cW = W;

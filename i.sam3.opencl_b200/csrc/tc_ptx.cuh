@@ -246,6 +246,19 @@ __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorM
         : "memory");
 }
 
+// Tile reduce-add shared -> global through a tensor map: every element of
+// the box is added (fp32, one rounding) to the global element in L2;
+// out-of-range rows and columns are skipped. Tracked like tma_store_2d.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *smem_src,
+                                                  int32_t x, int32_t y)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::
+            "l"(reinterpret_cast<uint64_t>(map)),
+        "r"(x), "r"(y), "r"(smem_addr(smem_src))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit()
 {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");

@@ -91,6 +91,32 @@ def test_gemm_tc_vs_fp32_product(cb, sb, M, N, K, out_bf16):
     assert err <= tol, (err, tol)
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 200, 136), (5184, 1024, 1024), (9000, 1000, 2048)])
+def test_gemm_tc_in_place_residual_equals_separate(cb, sb, M, N, K):
+    """C = A B^T + bias + C with C passed as its own residual (the encoder's
+    x += proj(...) and x += fc2(...)): the in-place path, which reduce-adds
+    the epilogue result into C through TMA, is bit-identical to reading a
+    separate residual buffer (single CTAs for the first two shapes, CTA
+    pairs for the third)."""
+    g = torch.Generator().manual_seed(M + 3 * N + 5 * K)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    B = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+    bias = torch.randn(N, generator=g).cuda()
+    R = torch.randn(M, N, generator=g).cuda()
+    C_sep = torch.empty(M, N, device="cuda")
+    C_in = R.clone()
+    torch.cuda.synchronize()
+    mA, mB, mb = cb.wrap(A), cb.wrap(B), cb.wrap(bias)
+    cb.gemm(M, N, K, (mA, 0, K), (mB, 0, K), 1, (cb.wrap(C_sep), 0, N), bias=mb,
+            R=cb.wrap(R))
+    m_in = cb.wrap(C_in)
+    cb.gemm(M, N, K, (mA, 0, K), (mB, 0, K), 1, (m_in, 0, N), bias=mb, R=m_in)
+    cb.sync()
+    assert torch.equal(C_sep, C_in)
+    ref = A.float() @ B.float().T + bias + R
+    assert (C_in - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
 def test_gemm_tc_gelu_epilogue_accuracy(cb, sb):
     """The tensor-core epilogue's GELU (erf from Abramowitz & Stegun 7.1.26)
     against the exact erf form: C = GELU(A I) with an identity B, so the
