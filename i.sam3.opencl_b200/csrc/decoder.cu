@@ -250,53 +250,6 @@ __global__ void __launch_bounds__(256) up1_kernel(const float4 *__restrict__ G,
     }
 }
 
-// Second output-upscaling stage fused with the mask logits
-// (sam3_model.c:1361-1366, 1387-1399). g2 [P*H*W, 128] holds the
-// ConvTranspose 64 -> 32 GEMM in sub-pixel-major columns d * 32 + co (the
-// weight rows are stored in that order), so the 32 channels of output
-// pixel (2y + dy, 2x + dx), d = 2 dy + dx, are one 128-byte run. One thread
-// per output pixel: GELU((g2 + bias) + feat_s0) of its 32 channels, dotted
-// with the prompt's three hypernetwork vectors; the [P, 288, 288, 32] map
-// of the reference is never stored. GELU uses the Abramowitz-Stegun erf
-// (gelu_as); four consecutive threads share one input pixel.
-__global__ void __launch_bounds__(256) up2_logits_kernel(const float4 *__restrict__ G,
-                                                         const float *__restrict__ bias,
-                                                         const float *__restrict__ feat,
-                                                         const float *__restrict__ hyper, int H,
-                                                         int W, long nsub,
-                                                         float *__restrict__ out)
-{
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nsub;
-         i += (long)gridDim.x * blockDim.x) {
-        const long ip = i >> 2;
-        const int d = (int)(i & 3);
-        const int x = (int)(ip % W);
-        const long py = ip / W;
-        const int y = (int)(py % H);
-        const long p = py / H;
-        const long opix = (long)(2 * y + (d >> 1)) * 2 * W + 2 * x + (d & 1);
-        const float4 *g = G + ip * 32 + d * 8;
-        const float4 *f = reinterpret_cast<const float4 *>(feat + opix * 32);
-        const float4 *bq = reinterpret_cast<const float4 *>(bias);
-        const float4 *h = reinterpret_cast<const float4 *>(hyper + p * 96);
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float4 gv = g[j], fv = __ldg(f + j), bv = __ldg(bq + j);
-            const float4 h0 = __ldg(h + j), h1 = __ldg(h + 8 + j), h2 = __ldg(h + 16 + j);
-            const float u0 = gelu_as((gv.x + bv.x) + fv.x), u1 = gelu_as((gv.y + bv.y) + fv.y);
-            const float u2 = gelu_as((gv.z + bv.z) + fv.z), u3 = gelu_as((gv.w + bv.w) + fv.w);
-            a0 = fmaf(u3, h0.w, fmaf(u2, h0.z, fmaf(u1, h0.y, fmaf(u0, h0.x, a0))));
-            a1 = fmaf(u3, h1.w, fmaf(u2, h1.z, fmaf(u1, h1.y, fmaf(u0, h1.x, a1))));
-            a2 = fmaf(u3, h2.w, fmaf(u2, h2.z, fmaf(u1, h2.y, fmaf(u0, h2.x, a2))));
-        }
-        const long onpix = 4L * H * W;
-        out[(p * 3 + 0) * onpix + opix] = a0;
-        out[(p * 3 + 1) * onpix + opix] = a1;
-        out[(p * 3 + 2) * onpix + opix] = a2;
-    }
-}
-
 // src [rows, cols] fp32 -> dst [cols, rows] bf16 (round to nearest even),
 // through 32 x 32 shared-memory tiles. With dmajor, source column
 // c = co * 4 + d becomes destination row d * (cols / 4) + co.
@@ -395,16 +348,3 @@ extern "C" int k_dec_up1(const float *G, const float *bias, const float *feat, c
     return (int)cudaGetLastError();
 }
 
-extern "C" int k_dec_up2_logits(const float *G, const float *bias, const float *feat,
-                                const float *hyper, int P, int H, int W, float *out, k_stream s)
-{
-    if (P <= 0 || H <= 0 || W <= 0 || (reinterpret_cast<uintptr_t>(G) & 15) ||
-        (reinterpret_cast<uintptr_t>(feat) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15) ||
-        (reinterpret_cast<uintptr_t>(hyper) & 15))
-        return K_EARG;
-    const long nsub = 4L * P * H * W;
-    const int grid = grid_for(nsub, 256);
-    up2_logits_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(
-        reinterpret_cast<const float4 *>(G), bias, feat, hyper, H, W, nsub, out);
-    return (int)cudaGetLastError();
-}

@@ -53,8 +53,11 @@ struct GemmEpi {
 
 // CONV3 geometry: 3x3 / pad-1 convolution of cimg maps cH x cW x (K / 9)
 // channels (implicit GEMM); M tiles are 8 x 16 pixel blocks, cyb x cxb per map.
+// LOGITS: cH x cW input maps; hyper = the prompts' hypernetwork vectors
+// [P][3][32].
 struct ConvGeom {
     int cH, cW, cimg, cyb, cxb;
+    const float *hyper;
 };
 
 // EPI_BUFS: staging tiles per epilogue warp. Single CTAs: one; the shared
@@ -237,6 +240,51 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
                      pk[4 * q + 3]);
 }
 
+// LOGITS epilogue: the last output-upscaling stage of the mask decoder fused
+// with the mask logits (sam3_model.c:1361-1366, 1387-1399). Row m of the
+// GEMM is input pixel (prompt, y, x) of an H x W map, its 128 columns the
+// ConvTranspose 2x2 (64 -> 32) outputs in sub-pixel-major order, so chunk c
+// (32 columns) is sub-pixel d = c = 2 dy + dx of output pixel (2y + dy,
+// 2x + dx). Per chunk: u = GELU(acc + bias + feat_s0[pixel]) over the 32
+// channels, dotted with the prompt's three hypernetwork vectors, written as
+// the three logits of that pixel: the [P, 2H, 2W, 32] map is never stored.
+// Output pixel of sub-pixel d of input row m.
+__device__ __forceinline__ long logits_pixel(const ConvGeom &cg, int m, int d)
+{
+    const int x = m % cg.cW, y = (m / cg.cW) % cg.cH;
+    return (2L * y + (d >> 1)) * (2L * cg.cW) + 2 * x + (d & 1);
+}
+
+__device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
+                                             const float (&v)[32])
+{
+    if (m >= p.M)
+        return;
+    const int pr = m / (cg.cW * cg.cH);
+    const long opix = logits_pixel(cg, m, d);
+    const float4 *f = reinterpret_cast<const float4 *>(p.R + opix * 32);
+    const float4 *bq = reinterpret_cast<const float4 *>(p.bias);
+    const float4 *h = reinterpret_cast<const float4 *>(cg.hyper + (long)pr * 96);
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float4 fv = __ldg(f + j), bv = __ldg(bq + j);
+        float u0 = (v[4 * j] + bv.x) + fv.x, u1 = (v[4 * j + 1] + bv.y) + fv.y;
+        float u2 = (v[4 * j + 2] + bv.z) + fv.z, u3 = (v[4 * j + 3] + bv.w) + fv.w;
+        gelu_pair(u0, u1);
+        gelu_pair(u2, u3);
+        const float4 h0 = __ldg(h + j), h1 = __ldg(h + 8 + j), h2 = __ldg(h + 16 + j);
+        a0 = fmaf(u3, h0.w, fmaf(u2, h0.z, fmaf(u1, h0.y, fmaf(u0, h0.x, a0))));
+        a1 = fmaf(u3, h1.w, fmaf(u2, h1.z, fmaf(u1, h1.y, fmaf(u0, h1.x, a1))));
+        a2 = fmaf(u3, h2.w, fmaf(u2, h2.z, fmaf(u1, h2.y, fmaf(u0, h2.x, a2))));
+    }
+    float *o = reinterpret_cast<float *>(p.C);
+    const long onpix = 4L * cg.cH * cg.cW;
+    o[((long)pr * 3 + 0) * onpix + opix] = a0;
+    o[((long)pr * 3 + 1) * onpix + opix] = a1;
+    o[((long)pr * 3 + 2) * onpix + opix] = a2;
+}
+
 // ROPE_PF: bf16 output whose tiles may need RoPE, with the row's (cos, sin)
 // pairs held in registers and no activation (a separate instantiation: the
 // register budget of the other epilogues does not carry them).
@@ -256,7 +304,7 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 // releases the accumulator on rank 0's barrier. Per SM this halves the B
 // tile traffic from L2 into shared memory.
 template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false,
-          bool PAIR = false>
+          bool PAIR = false, bool LOGITS = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -264,6 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const ConvGeom cg)
 {
     static_assert(!(PAIR && CONV3), "pair tiles are row blocks");
+    static_assert(!LOGITS || (BN == 128 && !OUT_BF16 && !TMA_STORE && !PAIR && !CONV3),
+                  "the logits epilogue: one 128-column fp32 tile per row block");
     using L = GemmSmem<BN, PAIR>;
     constexpr int STAGES = L::STAGES;
     constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
@@ -499,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     rc[2 * j + 1] = make_float2(q.z, q.w);
                 }
             }
-            const bool rfast = !OUT_BF16 && p.R && m < p.M && n0 + BN <= p.N &&
+            const bool rfast = !OUT_BF16 && !LOGITS && p.R && m < p.M && n0 + BN <= p.N &&
                                (p.ldr & 3) == 0 &&
                                (reinterpret_cast<uintptr_t>(p.R) & 15) == 0;
             const float *rrowp =
@@ -517,113 +567,138 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-            for (int c = half; c < NCHUNK; c += 2) {
-                const int n = n0 + c * CW;
-                if (n >= p.N)
-                    continue;  // warp-uniform: a chunk entirely beyond C
-                uint32_t pk[32];  // the chunk's 128-byte output row
-                float v32[OUT_BF16 ? 1 : 32];
-                if constexpr (OUT_BF16 && !ROPE_PF) {
-                    // 64 columns in one TMEM round trip.
-                    float v[64];
-                    {
-                        uint32_t r[32], r2[32];
-                        tmem_ld32(tbase + c * CW, r);
-                        tmem_ld32(tbase + c * CW + 32, r2);
-                        tmem_wait_ld();
+            if constexpr (LOGITS) {
+                // both chunks' accumulators first, then the tile is released
+                float va[2][32];
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            v[j] = __uint_as_float(r[j]);
-                            v[32 + j] = __uint_as_float(r2[j]);
-                        }
-                    }
-                    epilogue_math<64>(p, m, n, v, rrow, nullptr, nullptr);
+                for (int cc = 0; cc < 2; cc++) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + (half + 2 * cc) * CW, r);
+                    tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; j++)
-                        pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                        va[cc][j] = __uint_as_float(r[j]);
                 }
-                else if constexpr (OUT_BF16) {
-                    // With the row's RoPE pairs held in registers: 64 columns
-                    // in two halves of 32 (fewer live registers).
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&tempty[acc]);
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        float v[32];
+                for (int cc = 0; cc < 2; cc++)
+                    logits_chunk(p, cg, m, half + 2 * cc, va[cc]);
+                acc ^= 1;
+                if (acc == 0)
+                    acc_phase ^= 1;
+            }
+            else {
+#pragma unroll 1
+                for (int c = half; c < NCHUNK; c += 2) {
+                    const int n = n0 + c * CW;
+                    if (n >= p.N)
+                        continue;  // warp-uniform: a chunk entirely beyond C
+                    uint32_t pk[32];  // the chunk's 128-byte output row
+                    float v32[OUT_BF16 ? 1 : 32];
+                    if constexpr (OUT_BF16 && !ROPE_PF) {
+                        // 64 columns in one TMEM round trip.
+                        float v[64];
+                        {
+                            uint32_t r[32], r2[32];
+                            tmem_ld32(tbase + c * CW, r);
+                            tmem_ld32(tbase + c * CW + 32, r2);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                v[j] = __uint_as_float(r[j]);
+                                v[32 + j] = __uint_as_float(r2[j]);
+                            }
+                        }
+                        epilogue_math<64>(p, m, n, v, rrow, nullptr, nullptr);
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                    }
+                    else if constexpr (OUT_BF16) {
+                        // With the row's RoPE pairs held in registers: 64 columns
+                        // in two halves of 32 (fewer live registers).
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            float v[32];
+                            {
+                                uint32_t r[32];
+                                tmem_ld32(tbase + c * CW + h * 32, r);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 32; j++)
+                                    v[j] = __uint_as_float(r[j]);
+                            }
+                            epilogue_math<32, false>(p, m, n + h * 32, v, rrow, nullptr,
+                                              rope_tile && n < 2 * p.rope.E ? rc + h * 16 : nullptr);
+#pragma unroll
+                            for (int j = 0; j < 16; j++)
+                                pk[h * 16 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                        }
+                    }
+                    else {
+                        float4 rcur[CW / 4];
+#pragma unroll
+                        for (int j = 0; j < CW / 4; j++)
+                            rcur[j] = rnext[j];
+                        if (rfast && c + 2 < NCHUNK) {
+#pragma unroll
+                            for (int j = 0; j < CW / 4; j++)
+                                rnext[j] = *reinterpret_cast<const float4 *>(rrowp + (c + 2) * CW +
+                                                                             4 * j);
+                        }
                         {
                             uint32_t r[32];
-                            tmem_ld32(tbase + c * CW + h * 32, r);
+                            tmem_ld32(tbase + c * CW, r);
                             tmem_wait_ld();
 #pragma unroll
                             for (int j = 0; j < 32; j++)
-                                v[j] = __uint_as_float(r[j]);
+                                v32[j] = __uint_as_float(r[j]);
                         }
-                        epilogue_math<32, false>(p, m, n + h * 32, v, rrow, nullptr,
-                                          rope_tile && n < 2 * p.rope.E ? rc + h * 16 : nullptr);
-#pragma unroll
-                        for (int j = 0; j < 16; j++)
-                            pk[h * 16 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-                    }
-                }
-                else {
-                    float4 rcur[CW / 4];
-#pragma unroll
-                    for (int j = 0; j < CW / 4; j++)
-                        rcur[j] = rnext[j];
-                    if (rfast && c + 2 < NCHUNK) {
-#pragma unroll
-                        for (int j = 0; j < CW / 4; j++)
-                            rnext[j] = *reinterpret_cast<const float4 *>(rrowp + (c + 2) * CW +
-                                                                         4 * j);
-                    }
-                    {
-                        uint32_t r[32];
-                        tmem_ld32(tbase + c * CW, r);
-                        tmem_wait_ld();
+                        epilogue_math<32>(p, m, n, v32, rrow, rfast ? rcur : nullptr, nullptr);
 #pragma unroll
                         for (int j = 0; j < 32; j++)
-                            v32[j] = __uint_as_float(r[j]);
+                            pk[j] = __float_as_uint(v32[j]);
                     }
-                    epilogue_math<32>(p, m, n, v32, rrow, rfast ? rcur : nullptr, nullptr);
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        pk[j] = __float_as_uint(v32[j]);
-                }
-                if (TMA_STORE) {
-                    // The store issued kEpiBufs chunks ago used this buffer.
-                    if (lane == 0)
-                        bulk_wait_read<kEpiBufs - 1>();
-                    __syncwarp();
-                    const uint32_t tile = stage0 + buf * kStageTile;
-                    stage_row(tile, lane, pk);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0 && r0 < p.M) {
-                        const void *src = smem + L::EPI_OFF + ew * kEpiBufs * kStageTile +
-                                          buf * kStageTile;
-                        if constexpr (CONV3)
-                            tma_store_4d(&tmC, src, n, cx0, cy, cimg);
-                        else if (!OUT_BF16 && p.red)
-                            tma_reduce_add_2d(&tmC, src, n, r0);
-                        else
-                            tma_store_2d(&tmC, src, n, r0);
-                        bulk_commit();
+                    if (TMA_STORE) {
+                        // The store issued kEpiBufs chunks ago used this buffer.
+                        if (lane == 0)
+                            bulk_wait_read<kEpiBufs - 1>();
+                        __syncwarp();
+                        const uint32_t tile = stage0 + buf * kStageTile;
+                        stage_row(tile, lane, pk);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && r0 < p.M) {
+                            const void *src = smem + L::EPI_OFF + ew * kEpiBufs * kStageTile +
+                                              buf * kStageTile;
+                            if constexpr (CONV3)
+                                tma_store_4d(&tmC, src, n, cx0, cy, cimg);
+                            else if (!OUT_BF16 && p.red)
+                                tma_reduce_add_2d(&tmC, src, n, r0);
+                            else
+                                tma_store_2d(&tmC, src, n, r0);
+                            bulk_commit();
+                        }
+                        buf = (buf + 1) % kEpiBufs;
                     }
-                    buf = (buf + 1) % kEpiBufs;
+                    else
+                        store_direct<CW, OUT_BF16>(p, m, n, pk);
                 }
-                else
-                    store_direct<CW, OUT_BF16>(p, m, n, pk);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (PAIR)
+                        mbar_arrive_cluster(mapa_shared(smem_addr(&tempty[acc]), 0));
+                    else
+                        mbar_arrive(&tempty[acc]);
+                }
+                acc ^= 1;
+                if (acc == 0)
+                    acc_phase ^= 1;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if constexpr (PAIR)
-                    mbar_arrive_cluster(mapa_shared(smem_addr(&tempty[acc]), 0));
-                else
-                    mbar_arrive(&tempty[acc]);
-            }
-            acc ^= 1;
-            if (acc == 0)
-                acc_phase ^= 1;
         }
         if (TMA_STORE && lane == 0)
             bulk_wait_all();
@@ -644,13 +719,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false, bool CONV3 = false>
+template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false, bool CONV3 = false,
+          bool LOGITS = false>
 int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
            const GemmEpi &p, int num_sms, cudaStream_t s,
            const ConvGeom &cg = ConvGeom{0, 0, 0, 0, 0})
 {
     using L = GemmSmem<BN>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, LOGITS>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess)
@@ -835,7 +911,7 @@ extern "C" int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C, c
     p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
     p.err = err;
     p.red = 0;
-    ConvGeom cg;
+    ConvGeom cg{};
     cg.cH = H;
     cg.cW = W;
     cg.cimg = nimg;
@@ -847,4 +923,38 @@ extern "C" int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C, c
                         : launch<128, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
     return out_bf16 ? launch<256, true, true, false, true>(ta, tb, tc, p, num_sms, st, cg)
                     : launch<256, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
+}
+
+extern "C" int k_dec_convt_logits(const void *X, int P, int H, int W, const void *Wt,
+                                  const float *bias, const float *feat, const float *hyper,
+                                  float *out, int *err, int num_sms, k_stream s)
+{
+    using namespace sam3;
+    if (P <= 0 || H <= 0 || W <= 0 || (long)P * H * W > 0x7fffffffL ||
+        (reinterpret_cast<uintptr_t>(bias) & 15) || (reinterpret_cast<uintptr_t>(feat) & 15) ||
+        (reinterpret_cast<uintptr_t>(hyper) & 15))
+        return K_EARG;
+    const int M = P * H * W;
+    CUtensorMap ta, tb;
+    if (!make_tmap_bf16(&ta, X, (uint64_t)M, 64, 64, BM) ||
+        !make_tmap_bf16(&tb, Wt, 128, 64, 64, 128))
+        return K_ETMAP;
+    GemmEpi p;
+    p.M = M;
+    p.N = 128;
+    p.K = 64;
+    p.C = out;
+    p.ldc = 0;
+    p.bias = bias;
+    p.R = feat;
+    p.ldr = 32;
+    p.rmod = 0;
+    p.alpha = 1.0f;
+    p.act = K_ACT_NONE;
+    p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
+    p.err = err;
+    p.red = 0;
+    ConvGeom cg{H, W, P, 0, 0, hyper};
+    return launch<128, false, false, false, false, true>(ta, tb, ta, p, num_sms,
+                                                        reinterpret_cast<cudaStream_t>(s), cg);
 }

@@ -141,9 +141,14 @@ int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b,
 int k_dec_up1(const float *G, const float *bias, const float *feat,
               const float *g, const float *b, float eps, int P, int H, int W,
               void *out, k_stream s);
-int k_dec_up2_logits(const float *G, const float *bias, const float *feat,
-                     const float *hyper, int P, int H, int W, float *out,
-                     k_stream s);
+/* Last output-upscaling stage + mask logits on the tensor cores (gemm_tc.cu):
+ * X bf16 [P*H*W, 64] (the first stage's output), Wt bf16 [128, 64] (the
+ * ConvTranspose 64 -> 32 weight in sub-pixel-major rows d*32 + co), bias
+ * [32], feat = feat_s0 fp32 [(2H)*(2W), 32], hyper [P, 3, 32] -> out fp32
+ * [P, 3, 2H, 2W] = sum_c hyper[p][k][c] * GELU(convt + bias + feat). */
+int k_dec_convt_logits(const void *X, int P, int H, int W, const void *Wt,
+                       const float *bias, const float *feat, const float *hyper,
+                       float *out, int *err, int num_sms, k_stream s);
 
 /* SimpleFPN neck (neck.cu). convt_scatter_bf16: G fp32 [n*H*W, 4C] with
  * sub-pixel-major columns (d*C + co) -> out bf16 [n, 2H, 2W, C] =

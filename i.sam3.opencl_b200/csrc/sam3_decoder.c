@@ -78,7 +78,6 @@ struct cb_decoder {
     void *bo_bf16;              /* bf16 [batch * T, 128] */
     float *G;                   /* [batch * T, 256], first ConvT GEMM */
     void *u1_bf16;              /* bf16 [batch * 4T, 64] */
-    float *g2;                  /* [batch * 4T, 128] */
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
     void *mha_ws;
     size_t mha_ws_bytes;
@@ -110,7 +109,7 @@ void cb_decoder_free(cb_decoder *d)
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->qin, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
-                       d->bv, d->bo, d->bo_bf16, d->G, d->u1_bf16, d->g2,
+                       d->bv, d->bo, d->bo_bf16, d->G, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
@@ -178,7 +177,6 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->bo_bf16, B * T * 128 * 2);
     A(d->G, B * T * 256 * 4);
     A(d->u1_bf16, B * 4 * T * 64 * 2);
-    A(d->g2, B * 4 * T * 128 * 4);
     A(d->hyper, B * 96 * 4);
     A(d->iou, B * 3 * 4);
     ws_t2i = k_mha_workspace(batch, DEC_NTOK, DEC_T, 128, b->num_sms);
@@ -645,21 +643,19 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     /* Output upscaling (sam3_model.c:1353-1366) and mask_logits
      * (:1387-1399): ConvT 256 -> 64 as a GEMM on the bf16 keys, then its
      * scatter + feat_s1 + LayerNorm2d + GELU in one pass to bf16; ConvT
-     * 64 -> 32 as a GEMM, then its scatter + feat_s0 + GELU dotted with the
-     * hypernetwork outputs in one pass, straight to the logits. */
+     * 64 -> 32 as a GEMM whose epilogue adds feat_s0, applies GELU and dots
+     * with the hypernetwork outputs, straight to the logits. */
     CB_TRY(lin16(d, "dec_gemm_up", d->keys_bf16, rows, DEC_DIM, 256, SAM3_DT_UP0_W, -1, d->G,
                  NULL, 0, K_ACT_NONE));
     LAUNCH("dec_up1", 0, (double)rows * 256 * 4 + (double)rows * 4 * 64 * 2,
            k_dec_up1(d->G, (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1,
                      (const float *)d->w[SAM3_DT_UP1_W], (const float *)d->w[SAM3_DT_UP1_B],
                      LN2D_EPS, P, DEC_GRID, DEC_GRID, d->u1_bf16, (k_stream)b->stream));
-    CB_TRY(lin16(d, "dec_gemm_up", d->u1_bf16, 4 * rows, 64, 128, SAM3_DT_UP3_W, -1, d->g2,
-                 NULL, 0, K_ACT_NONE));
-    LAUNCH("dec_up2_logits", 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
-           (double)4 * rows * 128 * 4 + (double)P * 3 * DEC_LOWRES * DEC_LOWRES * 4,
-           k_dec_up2_logits(d->g2, (const float *)d->w[SAM3_DT_UP3_B], d->feat_s0, d->hyper, P,
-                            2 * DEC_GRID, 2 * DEC_GRID, (float *)lowres->ptr,
-                            (k_stream)b->stream));
+    LAUNCH("dec_up2_logits", 2.0 * 4 * rows * 64 * 128 + 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
+           (double)4 * rows * 64 * 2 + (double)P * 3 * DEC_LOWRES * DEC_LOWRES * 4,
+           k_dec_convt_logits(d->u1_bf16, P, 2 * DEC_GRID, 2 * DEC_GRID, d->w[SAM3_DT_UP3_W],
+                              (const float *)d->w[SAM3_DT_UP3_B], d->feat_s0, d->hyper,
+                              (float *)lowres->ptr, b->d_err, b->num_sms, (k_stream)b->stream));
     CB_TRY(cbi_kstatus(b,
                        (int)cudaMemcpyAsync(iou, d->iou, (size_t)P * 3 * 4,
                                             cudaMemcpyDeviceToHost, b->stream),

@@ -524,22 +524,6 @@ __device__ __forceinline__ float ex2_approx(float x)
     return y;
 }
 
-// GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun
-// 7.1.26 (Hastings; |error of erf| <= 1.5e-7): for z = |x| / sqrt 2,
-// t = 1 / (1 + p z), h = erfc(z) / 2 = t (a1 + t (a2 + t (a3 + t (a4 + t a5))))
-// 2^(-x^2 log2(e) / 2 - 1); GELU = x (1 - h) for x >= 0, x h otherwise.
-// One reciprocal and one 2^x on the MUFU unit.
-__device__ __forceinline__ float gelu_as(float x)
-{
-    const float t = rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, fabsf(x), 1.0f));
-    float q = fmaf(1.061405429f, t, -1.453152027f);
-    q = fmaf(q, t, 1.421413741f);
-    q = fmaf(q, t, -0.284496736f);
-    q = fmaf(q, t, 0.254829592f);
-    const float h = q * t * ex2_approx(fmaf(x * x, -0.72134752044448170f, -1.0f));
-    return x * (x >= 0.0f ? 1.0f - h : h);
-}
-
 // ---------------------------------------------------------------- packed fp32
 // Pairs of fp32 in one 64-bit register for the sm_100 .f32x2 arithmetic
 // (one instruction for two lanes of add / mul / fma).
