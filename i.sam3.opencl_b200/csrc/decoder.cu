@@ -206,50 +206,6 @@ __global__ void __launch_bounds__(256) ln_keys_kernel(const float *X, float *Y,
     }
 }
 
-// First output-upscaling stage in one pass (sam3_model.c:1355-1360): the
-// ConvTranspose 256 -> 64 scatter of G [P*72*72, 256] (column co*4 + dy*2 +
-// dx) + bias + feat_s1, LayerNorm2d over the 64 channels of each output
-// pixel (eps 1e-6), GELU, written as bf16 [P, 144, 144, 64] for the next
-// GEMM. One warp per input pixel: lane l holds G columns 8l..8l+7 (channels
-// 2l, 2l+1 of the four sub-pixels), so each output pixel's LayerNorm is a
-// warp reduction. The reference writes the fp32 map and normalises it in a
-// second kernel; the values are the same up to the order of the sums.
-__global__ void __launch_bounds__(256) up1_kernel(const float4 *__restrict__ G,
-                                                  const float *__restrict__ bias,
-                                                  const float *__restrict__ feat,
-                                                  const float *__restrict__ g,
-                                                  const float *__restrict__ b, float eps, int H,
-                                                  int W, long npix, uint32_t *__restrict__ out)
-{
-    const long ip = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (ip >= npix)
-        return;
-    const int x = (int)(ip % W);
-    const long py = ip / W;
-    const int y = (int)(py % H);
-    const long p = py / H;
-    const float4 a0 = G[ip * 64 + 2 * lane], a1 = G[ip * 64 + 2 * lane + 1];
-    const float ga[4] = {a0.x, a0.y, a0.z, a0.w}, gb[4] = {a1.x, a1.y, a1.z, a1.w};
-    const int c0 = 2 * lane;
-    const float b0 = __ldg(bias + c0), b1 = __ldg(bias + c0 + 1);
-    const float g0 = __ldg(g + c0), g1 = __ldg(g + c0 + 1);
-    const float t0 = __ldg(b + c0), t1 = __ldg(b + c0 + 1);
-#pragma unroll
-    for (int d = 0; d < 4; d++) {
-        const int oy = 2 * y + (d >> 1), ox = 2 * x + (d & 1);
-        const long opix = (long)oy * 2 * W + ox;
-        const float2 f = __ldg(reinterpret_cast<const float2 *>(feat + opix * 64) + lane);
-        const float v0 = (ga[d] + b0) + f.x, v1 = (gb[d] + b1) + f.y;
-        const float mean = warp_sum(v0 + v1) / 64.0f;
-        const float e0 = v0 - mean, e1 = v1 - mean;
-        const float inv = rsqrtf(warp_sum(e0 * e0 + e1 * e1) / 64.0f + eps);
-        const float y0 = act_fn(e0 * inv * g0 + t0, K_ACT_GELU);
-        const float y1 = act_fn(e1 * inv * g1 + t1, K_ACT_GELU);
-        out[(p * 4L * H * W + opix) * 32 + lane] = pack2(y0, y1);
-    }
-}
-
 // src [rows, cols] fp32 -> dst [cols, rows] bf16 (round to nearest even),
 // through 32 x 32 shared-memory tiles. With dmajor, source column
 // c = co * 4 + d becomes destination row d * (cols / 4) + co.
@@ -332,19 +288,6 @@ extern "C" int k_dec_ln_keys(const float *X, float *Y, const float *g, const flo
         return K_EARG;
     ln_keys_kernel<<<grid_for(rows, 8), 256, 0, STREAM(s)>>>(
         X, Y, g, b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb), reinterpret_cast<uint2 *>(Yk));
-    return (int)cudaGetLastError();
-}
-
-extern "C" int k_dec_up1(const float *G, const float *bias, const float *feat, const float *g,
-                         const float *b, float eps, int P, int H, int W, void *out, k_stream s)
-{
-    if (P <= 0 || H <= 0 || W <= 0 || (reinterpret_cast<uintptr_t>(G) & 15) ||
-        (reinterpret_cast<uintptr_t>(feat) & 7) || (reinterpret_cast<uintptr_t>(out) & 3))
-        return K_EARG;
-    const long npix = (long)P * H * W;
-    up1_kernel<<<grid_for(npix, 8), 256, 0, STREAM(s)>>>(reinterpret_cast<const float4 *>(G), bias,
-                                                         feat, g, b, eps, H, W, npix,
-                                                         reinterpret_cast<uint32_t *>(out));
     return (int)cudaGetLastError();
 }
 

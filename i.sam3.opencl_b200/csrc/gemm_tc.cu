@@ -53,11 +53,15 @@ struct GemmEpi {
 
 // CONV3 geometry: 3x3 / pad-1 convolution of cimg maps cH x cW x (K / 9)
 // channels (implicit GEMM); M tiles are 8 x 16 pixel blocks, cyb x cxb per map.
-// LOGITS: cH x cW input maps; hyper = the prompts' hypernetwork vectors
-// [P][3][32].
+// Epilogue kinds beyond the generic one (bias, activation, residual, RoPE):
+// the mask decoder's two output-upscaling stages.
+constexpr int kEpiGeneric = 0, kEpiLogits = 1, kEpiLn2d = 2;
+
+// kEpiLogits / kEpiLn2d: cH x cW input maps; hyper = the prompts'
+// hypernetwork vectors [P][3][32]; lnw / lnb = LayerNorm2d weight and bias.
 struct ConvGeom {
     int cH, cW, cimg, cyb, cxb;
-    const float *hyper;
+    const float *hyper, *lnw, *lnb;
 };
 
 // EPI_BUFS: staging tiles per epilogue warp. Single CTAs: one; the shared
@@ -255,6 +259,64 @@ __device__ __forceinline__ long logits_pixel(const ConvGeom &cg, int m, int d)
     return (2L * y + (d >> 1)) * (2L * cg.cW) + 2 * x + (d & 1);
 }
 
+// kEpiLn2d: the first output-upscaling stage of the mask decoder
+// (sam3_model.c:1355-1360) as the epilogue of its ConvTranspose 2x2
+// (256 -> 64) GEMM: row m is input pixel (prompt, y, x), its 256 columns in
+// sub-pixel-major order, so a 64-column chunk is sub-pixel d of output pixel
+// (2y + dy, 2x + dx). Per chunk: v = acc + bias + feat_s1[pixel], LayerNorm
+// over the 64 channels (eps = p.alpha), GELU, written as the pixel's 64 bf16
+// channels of the [P, 2H, 2W, 64] map.
+__device__ __forceinline__ void ln2d_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
+                                           float (&v)[64])
+{
+    if (m >= p.M)
+        return;
+    const int pr = m / (cg.cW * cg.cH);
+    const long fpix = logits_pixel(cg, m, d);
+    const long opix = fpix + (long)pr * 4 * cg.cH * cg.cW;
+    const float4 *f = reinterpret_cast<const float4 *>(p.R + fpix * 64);
+    const float4 *bq = reinterpret_cast<const float4 *>(p.bias);
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const float4 fv = __ldg(f + j), bv = __ldg(bq + j);
+        v[4 * j] = (v[4 * j] + bv.x) + fv.x;
+        v[4 * j + 1] = (v[4 * j + 1] + bv.y) + fv.y;
+        v[4 * j + 2] = (v[4 * j + 2] + bv.z) + fv.z;
+        v[4 * j + 3] = (v[4 * j + 3] + bv.w) + fv.w;
+        sum += (v[4 * j] + v[4 * j + 1]) + (v[4 * j + 2] + v[4 * j + 3]);
+    }
+    const float mean = sum * (1.0f / 64.0f);
+    float sq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 64; j++) {
+        const float e = v[j] - mean;
+        sq = fmaf(e, e, sq);
+    }
+    const float inv = rsqrtf(sq * (1.0f / 64.0f) + p.alpha);
+    const float4 *gq = reinterpret_cast<const float4 *>(cg.lnw);
+    const float4 *tq = reinterpret_cast<const float4 *>(cg.lnb);
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.C) + opix * 64);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        float y[8];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float4 g = __ldg(gq + 2 * j + h), t = __ldg(tq + 2 * j + h);
+            y[4 * h] = fmaf((v[8 * j + 4 * h] - mean) * inv, g.x, t.x);
+            y[4 * h + 1] = fmaf((v[8 * j + 4 * h + 1] - mean) * inv, g.y, t.y);
+            y[4 * h + 2] = fmaf((v[8 * j + 4 * h + 2] - mean) * inv, g.z, t.z);
+            y[4 * h + 3] = fmaf((v[8 * j + 4 * h + 3] - mean) * inv, g.w, t.w);
+        }
+        gelu_pair(y[0], y[1]);
+        gelu_pair(y[2], y[3]);
+        gelu_pair(y[4], y[5]);
+        gelu_pair(y[6], y[7]);
+        dst[j] = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                            pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+    }
+}
+
 __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
                                              const float (&v)[32])
 {
@@ -304,7 +366,7 @@ __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &c
 // releases the accumulator on rank 0's barrier. Per SM this halves the B
 // tile traffic from L2 into shared memory.
 template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false,
-          bool PAIR = false, bool LOGITS = false>
+          bool PAIR = false, int EPI = kEpiGeneric>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -312,8 +374,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const ConvGeom cg)
 {
     static_assert(!(PAIR && CONV3), "pair tiles are row blocks");
+    constexpr bool LOGITS = EPI == kEpiLogits;
     static_assert(!LOGITS || (BN == 128 && !OUT_BF16 && !TMA_STORE && !PAIR && !CONV3),
                   "the logits epilogue: one 128-column fp32 tile per row block");
+    static_assert(EPI != kEpiLn2d || (BN == 256 && OUT_BF16 && !TMA_STORE && !ROPE_PF && !PAIR &&
+                                      !CONV3),
+                  "the LayerNorm2d epilogue: one 256-column tile per row block, bf16");
     using L = GemmSmem<BN, PAIR>;
     constexpr int STAGES = L::STAGES;
     constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
@@ -612,6 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 v[32 + j] = __uint_as_float(r2[j]);
                             }
                         }
+                        if constexpr (EPI == kEpiLn2d) {
+                            ln2d_chunk(p, cg, m, c, v);
+                            continue;
+                        }
                         epilogue_math<64>(p, m, n, v, rrow, nullptr, nullptr);
 #pragma unroll
                         for (int j = 0; j < 32; j++)
@@ -720,13 +790,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF = false, bool CONV3 = false,
-          bool LOGITS = false>
+          int EPI = kEpiGeneric>
 int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
            const GemmEpi &p, int num_sms, cudaStream_t s,
            const ConvGeom &cg = ConvGeom{0, 0, 0, 0, 0})
 {
     using L = GemmSmem<BN>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, LOGITS>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, EPI>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess)
@@ -954,7 +1024,43 @@ extern "C" int k_dec_convt_logits(const void *X, int P, int H, int W, const void
     p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
     p.err = err;
     p.red = 0;
-    ConvGeom cg{H, W, P, 0, 0, hyper};
-    return launch<128, false, false, false, false, true>(ta, tb, ta, p, num_sms,
-                                                        reinterpret_cast<cudaStream_t>(s), cg);
+    ConvGeom cg{H, W, P, 0, 0, hyper, nullptr, nullptr};
+    return launch<128, false, false, false, false, kEpiLogits>(
+        ta, tb, ta, p, num_sms, reinterpret_cast<cudaStream_t>(s), cg);
+}
+
+extern "C" int k_dec_convt_ln2d(const void *X, int P, int H, int W, const void *Wt,
+                                const float *bias, const float *feat, const float *lnw,
+                                const float *lnb, float eps, void *out, int *err, int num_sms,
+                                k_stream s)
+{
+    using namespace sam3;
+    if (P <= 0 || H <= 0 || W <= 0 || (long)P * H * W > 0x7fffffffL ||
+        (reinterpret_cast<uintptr_t>(bias) & 15) || (reinterpret_cast<uintptr_t>(feat) & 15) ||
+        (reinterpret_cast<uintptr_t>(lnw) & 15) || (reinterpret_cast<uintptr_t>(lnb) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
+        return K_EARG;
+    const int M = P * H * W;
+    CUtensorMap ta, tb;
+    if (!make_tmap_bf16(&ta, X, (uint64_t)M, 256, 256, BM) ||
+        !make_tmap_bf16(&tb, Wt, 256, 256, 256, 256))
+        return K_ETMAP;
+    GemmEpi p;
+    p.M = M;
+    p.N = 256;
+    p.K = 256;
+    p.C = out;
+    p.ldc = 0;
+    p.bias = bias;
+    p.R = feat;
+    p.ldr = 64;
+    p.rmod = 0;
+    p.alpha = eps;
+    p.act = K_ACT_NONE;
+    p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
+    p.err = err;
+    p.red = 0;
+    ConvGeom cg{H, W, P, 0, 0, nullptr, lnw, lnb};
+    return launch<256, true, false, false, false, kEpiLn2d>(
+        ta, tb, ta, p, num_sms, reinterpret_cast<cudaStream_t>(s), cg);
 }

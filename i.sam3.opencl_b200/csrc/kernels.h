@@ -138,9 +138,6 @@ int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor,
 int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b,
                   long rows, float eps, const float *pe, int T, void *Yb,
                   void *Yk, k_stream s);
-int k_dec_up1(const float *G, const float *bias, const float *feat,
-              const float *g, const float *b, float eps, int P, int H, int W,
-              void *out, k_stream s);
 /* Last output-upscaling stage + mask logits on the tensor cores (gemm_tc.cu):
  * X bf16 [P*H*W, 64] (the first stage's output), Wt bf16 [128, 64] (the
  * ConvTranspose 64 -> 32 weight in sub-pixel-major rows d*32 + co), bias
@@ -149,6 +146,15 @@ int k_dec_up1(const float *G, const float *bias, const float *feat,
 int k_dec_convt_logits(const void *X, int P, int H, int W, const void *Wt,
                        const float *bias, const float *feat, const float *hyper,
                        float *out, int *err, int num_sms, k_stream s);
+/* First output-upscaling stage on the tensor cores (gemm_tc.cu): X bf16
+ * [P*H*W, 256] (the keys), Wt bf16 [256, 256] (the ConvTranspose 256 -> 64
+ * weight in sub-pixel-major rows d*64 + co), bias [64], feat = feat_s1 fp32
+ * [(2H)*(2W), 64], LayerNorm2d lnw / lnb [64] -> out bf16 [P, 2H, 2W, 64] =
+ * GELU(LN(convt + bias + feat)). */
+int k_dec_convt_ln2d(const void *X, int P, int H, int W, const void *Wt,
+                     const float *bias, const float *feat, const float *lnw,
+                     const float *lnb, float eps, void *out, int *err, int num_sms,
+                     k_stream s);
 
 /* SimpleFPN neck (neck.cu). convt_scatter_bf16: G fp32 [n*H*W, 4C] with
  * sub-pixel-major columns (d*C + co) -> out bf16 [n, 2H, 2W, C] =

@@ -76,7 +76,6 @@ struct cb_decoder {
     void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
     float *bq, *bk, *bv, *bo;   /* [batch * T, 128] */
     void *bo_bf16;              /* bf16 [batch * T, 128] */
-    float *G;                   /* [batch * T, 256], first ConvT GEMM */
     void *u1_bf16;              /* bf16 [batch * 4T, 64] */
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
     void *mha_ws;
@@ -109,7 +108,7 @@ void cb_decoder_free(cb_decoder *d)
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->qin, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
-                       d->bv, d->bo, d->bo_bf16, d->G, d->u1_bf16,
+                       d->bv, d->bo, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
@@ -175,7 +174,6 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->bv, B * T * 128 * 4);
     A(d->bo, B * T * 128 * 4);
     A(d->bo_bf16, B * T * 128 * 2);
-    A(d->G, B * T * 256 * 4);
     A(d->u1_bf16, B * 4 * T * 64 * 2);
     A(d->hyper, B * 96 * 4);
     A(d->iou, B * 3 * 4);
@@ -260,11 +258,11 @@ static int store_tensor(cb_decoder *d, int i, const float *f32)
     int r, c, k;
 
     sam3_dec_tensor(i, &r, &c, &k);
-    /* ConvTranspose weights [cin, cout * 4] -> GEMM operands [cout * 4, cin];
-     * the second one's rows in sub-pixel-major order d * 32 + co, the
-     * column order its fused scatter + logits pass reads. */
+    /* ConvTranspose weights [cin, cout * 4] -> GEMM operands [cout * 4, cin]
+     * with rows in sub-pixel-major order d * cout + co: a sub-pixel's
+     * channels are one column chunk of the GEMM's fused epilogue. */
     if (i == SAM3_DT_UP0_W || i == SAM3_DT_UP3_W)
-        return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, i == SAM3_DT_UP3_W, d->w[i], st),
+        return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, 1, d->w[i], st),
                            "decoder weights");
     if (is_gemm_weight(i))
         return cbi_kstatus(b, k_cast_f32_bf16(f32, d->w[i], (long)r * c, st), "decoder weights");
@@ -641,16 +639,18 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
            k_dec_heads(d->qry, P, &heads, d->hyper, d->iou, (k_stream)b->stream));
 
     /* Output upscaling (sam3_model.c:1353-1366) and mask_logits
-     * (:1387-1399): ConvT 256 -> 64 as a GEMM on the bf16 keys, then its
-     * scatter + feat_s1 + LayerNorm2d + GELU in one pass to bf16; ConvT
-     * 64 -> 32 as a GEMM whose epilogue adds feat_s0, applies GELU and dots
-     * with the hypernetwork outputs, straight to the logits. */
-    CB_TRY(lin16(d, "dec_gemm_up", d->keys_bf16, rows, DEC_DIM, 256, SAM3_DT_UP0_W, -1, d->G,
-                 NULL, 0, K_ACT_NONE));
-    LAUNCH("dec_up1", 0, (double)rows * 256 * 4 + (double)rows * 4 * 64 * 2,
-           k_dec_up1(d->G, (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1,
-                     (const float *)d->w[SAM3_DT_UP1_W], (const float *)d->w[SAM3_DT_UP1_B],
-                     LN2D_EPS, P, DEC_GRID, DEC_GRID, d->u1_bf16, (k_stream)b->stream));
+     * (:1387-1399) as two tcgen05 GEMMs with fused epilogues: ConvT
+     * 256 -> 64 on the bf16 keys + bias + feat_s1 + LayerNorm2d + GELU,
+     * written as the bf16 operand of ConvT 64 -> 32, whose epilogue adds
+     * feat_s0, applies GELU and dots with the hypernetwork outputs,
+     * straight to the logits. */
+    LAUNCH("dec_up1", 2.0 * rows * DEC_DIM * 256,
+           (double)rows * DEC_DIM * 2 + (double)rows * 4 * 64 * 2,
+           k_dec_convt_ln2d(d->keys_bf16, P, DEC_GRID, DEC_GRID, d->w[SAM3_DT_UP0_W],
+                            (const float *)d->w[SAM3_DT_UP0_B], d->feat_s1,
+                            (const float *)d->w[SAM3_DT_UP1_W],
+                            (const float *)d->w[SAM3_DT_UP1_B], LN2D_EPS, d->u1_bf16, b->d_err,
+                            b->num_sms, (k_stream)b->stream));
     LAUNCH("dec_up2_logits", 2.0 * 4 * rows * 64 * 128 + 2.0 * P * 3 * 32 * DEC_LOWRES * DEC_LOWRES,
            (double)4 * rows * 64 * 2 + (double)P * 3 * DEC_LOWRES * DEC_LOWRES * 4,
            k_dec_convt_logits(d->u1_bf16, P, 2 * DEC_GRID, 2 * DEC_GRID, d->w[SAM3_DT_UP3_W],
