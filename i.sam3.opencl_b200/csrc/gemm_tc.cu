@@ -54,14 +54,17 @@ struct GemmEpi {
 // CONV3 geometry: 3x3 / pad-1 convolution of cimg maps cH x cW x (K / 9)
 // channels (implicit GEMM); M tiles are 8 x 16 pixel blocks, cyb x cxb per map.
 // Epilogue kinds beyond the generic one (bias, activation, residual, RoPE):
-// the mask decoder's two output-upscaling stages.
-constexpr int kEpiGeneric = 0, kEpiLogits = 1, kEpiLn2d = 2;
+// the mask decoder's two output-upscaling stages and the scatter of a 2x2 /
+// stride-2 ConvTranspose.
+constexpr int kEpiGeneric = 0, kEpiLogits = 1, kEpiLn2d = 2, kEpiConvT = 3;
 
-// kEpiLogits / kEpiLn2d: cH x cW input maps; hyper = the prompts'
-// hypernetwork vectors [P][3][32]; lnw / lnb = LayerNorm2d weight and bias.
+// kEpiLogits / kEpiLn2d / kEpiConvT: cH x cW input maps; hyper = the
+// prompts' hypernetwork vectors [P][3][32]; lnw / lnb = LayerNorm2d weight
+// and bias; cout = ConvTranspose output channels.
 struct ConvGeom {
     int cH, cW, cimg, cyb, cxb;
     const float *hyper, *lnw, *lnb;
+    int cout;
 };
 
 // EPI_BUFS: staging tiles per epilogue warp. Single CTAs: one; the shared
@@ -317,6 +320,43 @@ __device__ __forceinline__ void ln2d_chunk(const GemmEpi &p, const ConvGeom &cg,
     }
 }
 
+// kEpiConvT: a 2x2 / stride-2 ConvTranspose as the epilogue of its GEMM:
+// row m is input pixel (map, y, x), the columns sub-pixel-major (d * cout +
+// co), so the 64-column chunk at column n is channels co0 .. co0 + 63 of
+// sub-pixel d = n / cout of output pixel (2y + dy, 2x + dx). bias[co] and
+// the activation are applied and the 64 bf16 values stored straight into
+// the [maps, 2H, 2W, cout] map (one 128-byte run).
+__device__ __forceinline__ void convt_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int n,
+                                            float (&v)[64])
+{
+    if (m >= p.M || n >= p.N)
+        return;
+    const int d = n / cg.cout, co0 = n % cg.cout;
+    const int x = m % cg.cW, t = m / cg.cW, y = t % cg.cH, mp = t / cg.cH;
+    const long opix = ((long)mp * 2 * cg.cH + 2 * y + (d >> 1)) * (2L * cg.cW) + 2 * x + (d & 1);
+    const float4 *bq = reinterpret_cast<const float4 *>(p.bias + co0);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const float4 bv = __ldg(bq + j);
+        v[4 * j] += bv.x;
+        v[4 * j + 1] += bv.y;
+        v[4 * j + 2] += bv.z;
+        v[4 * j + 3] += bv.w;
+    }
+    if (p.act == K_ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 64; j += 2)
+            gelu_pair(v[j], v[j + 1]);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.C) +
+                                           opix * cg.cout + co0);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        dst[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                            pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
 __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
                                              const float (&v)[32])
 {
@@ -380,6 +420,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(EPI != kEpiLn2d || (BN == 256 && OUT_BF16 && !TMA_STORE && !ROPE_PF && !PAIR &&
                                       !CONV3),
                   "the LayerNorm2d epilogue: one 256-column tile per row block, bf16");
+    static_assert(EPI != kEpiConvT || (BN == 256 && OUT_BF16 && !TMA_STORE && !ROPE_PF && !PAIR &&
+                                       !CONV3),
+                  "the ConvTranspose epilogue: bf16 out, direct stores");
     using L = GemmSmem<BN, PAIR>;
     constexpr int STAGES = L::STAGES;
     constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
@@ -680,6 +723,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         if constexpr (EPI == kEpiLn2d) {
                             ln2d_chunk(p, cg, m, c, v);
+                            continue;
+                        }
+                        if constexpr (EPI == kEpiConvT) {
+                            convt_chunk(p, cg, m, n, v);
                             continue;
                         }
                         epilogue_math<64>(p, m, n, v, rrow, nullptr, nullptr);
@@ -1062,5 +1109,39 @@ extern "C" int k_dec_convt_ln2d(const void *X, int P, int H, int W, const void *
     p.red = 0;
     ConvGeom cg{H, W, P, 0, 0, nullptr, lnw, lnb};
     return launch<256, true, false, false, false, kEpiLn2d>(
+        ta, tb, ta, p, num_sms, reinterpret_cast<cudaStream_t>(s), cg);
+}
+
+extern "C" int k_convt2x2_bf16_tc(const void *X, int nimg, int H, int W, int cin, const void *Wt,
+                                  int cout, const float *bias, int act, void *out, int *err,
+                                  int num_sms, k_stream s)
+{
+    using namespace sam3;
+    if (nimg <= 0 || H <= 0 || W <= 0 || cin <= 0 || cin % 8 || cout <= 0 || cout % 64 ||
+        (long)nimg * H * W > 0x7fffffffL || (reinterpret_cast<uintptr_t>(bias) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
+        return K_EARG;
+    const int M = nimg * H * W, N = 4 * cout;
+    CUtensorMap ta, tb;
+    if (!make_tmap_bf16(&ta, X, (uint64_t)M, (uint64_t)cin, (uint64_t)cin, BM) ||
+        !make_tmap_bf16(&tb, Wt, (uint64_t)N, (uint64_t)cin, (uint64_t)cin, 256))
+        return K_ETMAP;
+    GemmEpi p;
+    p.M = M;
+    p.N = N;
+    p.K = cin;
+    p.C = out;
+    p.ldc = 0;
+    p.bias = bias;
+    p.R = nullptr;
+    p.ldr = 0;
+    p.rmod = 0;
+    p.alpha = 1.0f;
+    p.act = act;
+    p.rope = k_rope{nullptr, 0, 0, 0, 0, 0, 0, 0};
+    p.err = err;
+    p.red = 0;
+    ConvGeom cg{H, W, nimg, 0, 0, nullptr, nullptr, nullptr, cout};
+    return launch<256, true, false, false, false, kEpiConvT>(
         ta, tb, ta, p, num_sms, reinterpret_cast<cudaStream_t>(s), cg);
 }

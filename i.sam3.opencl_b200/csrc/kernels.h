@@ -45,6 +45,14 @@ int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const void *B,
                    const struct k_rope *rope, int *err, int num_sms,
                    k_stream s);
 
+/* 2x2 / stride-2 ConvTranspose as a tcgen05 GEMM with the scatter in its
+ * epilogue: X bf16 [nimg, H, W, cin], Wt bf16 [4 * cout, cin] in
+ * sub-pixel-major rows (d * cout + co), out bf16 [nimg, 2H, 2W, cout] =
+ * act(convt + bias[co]). cin % 8 == 0, cout % 64 == 0. */
+int k_convt2x2_bf16_tc(const void *X, int nimg, int H, int W, int cin,
+                       const void *Wt, int cout, const float *bias, int act,
+                       void *out, int *err, int num_sms, k_stream s);
+
 /* 3x3 / pad-1 convolution as an implicit tcgen05 GEMM: X bf16 [nimg, H, W, C]
  * (C % 64 == 0), Wt bf16 [N, 9C] in tap-major column order ((ky*3 + kx)*C +
  * c), out [nimg, H, W, N] fp32 or bf16 (out_bf16) = conv + bias[n]
@@ -156,13 +164,9 @@ int k_dec_convt_ln2d(const void *X, int P, int H, int W, const void *Wt,
                      const float *lnb, float eps, void *out, int *err, int num_sms,
                      k_stream s);
 
-/* SimpleFPN neck (neck.cu). convt_scatter_bf16: G fp32 [n*H*W, 4C] with
- * sub-pixel-major columns (d*C + co) -> out bf16 [n, 2H, 2W, C] =
- * act(G + bias). permute_conv3x3_bf16: fp32 [cout, cin, 3, 3] -> bf16
- * [cout, 9 cin], columns (ky*3 + kx)*cin + c (k_conv3x3_bf16_tc's K order).
- * C % 8 == 0, 16-byte aligned buffers. */
-int k_convt_scatter_bf16(const float *G, const float *bias, int n, int H,
-                         int W, int C, int act, void *out, k_stream s);
+/* SimpleFPN neck (neck.cu). permute_conv3x3_bf16: fp32 [cout, cin, 3, 3]
+ * -> bf16 [cout, 9 cin], columns (ky*3 + kx)*cin + c (k_conv3x3_bf16_tc's
+ * K order). */
 int k_permute_conv3x3_bf16(const float *src, int cout, int cin, void *dst,
                            k_stream s);
 

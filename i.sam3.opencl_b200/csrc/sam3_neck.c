@@ -8,9 +8,9 @@
  * accumulation:
  *   - ConvTranspose 2x2 / stride 2: the GEMM of the map with the weight
  *     stored as [cout * 4, cin] in sub-pixel-major row order (d * cout + co),
- *     so its fp32 output puts each output pixel's channels in one run; one
- *     scatter pass adds the bias, applies the activation and writes the
- *     upsampled map in bf16 (the next GEMM's operand);
+ *     so each 64-column chunk of a row is 64 channels of one output pixel;
+ *     the epilogue adds the bias, applies the activation and writes them
+ *     into the upsampled bf16 map (the next GEMM's operand);
  *   - 1x1: a GEMM with the bias in its epilogue, bf16 out;
  *   - 3x3 / pad 1: an implicit GEMM (k_conv3x3_bf16_tc) against the weight
  *     permuted to tap-major columns ((ky * 3 + kx) * 256 + c): each K block
@@ -33,7 +33,6 @@ struct cb_neck {
     int grid, E, max_tiles, T;
     void *w[SAM3_NT_COUNT]; /* bf16 GEMM weights (layouts above), fp32 vectors */
     void *xb;               /* bf16 [R, E], R = max_tiles * T */
-    float *g;               /* fp32 ConvTranspose GEMM output, up to [4R, E] */
     void *a0;               /* bf16 [4R, E / 2] */
     void *a1;               /* bf16 [16R, E / 4] */
     void *c1;               /* bf16 [16R, 256] */
@@ -68,7 +67,6 @@ void cb_neck_free(cb_neck *n)
     for (i = 0; i < SAM3_NT_COUNT; i++)
         cudaFree(n->w[i]);
     cudaFree(n->xb);
-    cudaFree(n->g);
     cudaFree(n->a0);
     cudaFree(n->a1);
     cudaFree(n->c1);
@@ -107,7 +105,6 @@ int cb_neck_create(cb_backend *b, int grid, int embed, int max_tiles, cb_neck **
         A(n->w[i], (size_t)r * c * (neck_is_matrix(i, embed) ? 2 : 4));
     }
     A(n->xb, R * embed * 2);
-    A(n->g, 4 * R * embed * 4);
     A(n->a0, 4 * R * (embed / 2) * 2);
     A(n->a1, 16 * R * (embed / 4) * 2);
     A(n->c1, 16 * R * NECK_DIM * 2);
@@ -223,18 +220,19 @@ static int ngemm(cb_neck *n, const char *name, const void *A, long rows, int K, 
     return CB_OK;
 }
 
-/* convt2x2 (sam3_model.c:1058-1065) of nt maps H x W x cin (bf16 A): GEMM
- * into g, then scatter + bias + act into out bf16 [nt, 2H, 2W, cout]. */
+/* convt2x2 (sam3_model.c:1058-1065) of nt maps H x W x cin (bf16 A): one
+ * GEMM whose epilogue adds the bias, applies the activation and writes the
+ * upsampled map out bf16 [nt, 2H, 2W, cout]. */
 static int convt(cb_neck *n, const void *A, int nt, int H, int W, int cin, int cout, int wi,
                  int bi, int act, void *out)
 {
     cb_backend *b = n->b;
-    const long rows = (long)nt * H * W;
+    const double rows = (double)nt * H * W;
 
-    CB_TRY(ngemm(n, "neck_gemm_convt", A, rows, cin, 4 * cout, wi, -1, n->g, 0, NULL, 0));
-    LAUNCH("neck_convt_scatter", 0, (double)rows * 4 * cout * 6,
-           k_convt_scatter_bf16(n->g, (const float *)n->w[bi], nt, H, W, cout, act, out,
-                                (k_stream)b->stream));
+    LAUNCH("neck_gemm_convt", 2.0 * rows * cin * 4 * cout,
+           rows * cin * 2 + 4.0 * cout * cin * 2 + rows * 4 * cout * 2,
+           k_convt2x2_bf16_tc(A, nt, H, W, cin, n->w[wi], cout, (const float *)n->w[bi], act, out,
+                              b->d_err, b->num_sms, (k_stream)b->stream));
     return CB_OK;
 }
 
