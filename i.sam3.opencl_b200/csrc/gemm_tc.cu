@@ -5,20 +5,24 @@
 // (bias, GELU/ReLU, residual; sam3_kernels.cl:57-69, 147-153), plus an
 // optional RoPE rotation of the q/k columns (rope_apply,
 // sam3_kernels.cl:679-698) so the QKV output feeds attention directly.
+// The same kernel also runs the implicit-GEMM 3x3 convolution and the 2x2
+// ConvTranspose (scatter in the epilogue) of the neck, and the mask
+// decoder's two output-upscaling stages (LayerNorm2d + GELU, and GELU +
+// mask logits, in the epilogue).
 //
-// One CTA per SM, 10 warps:
+// One CTA per SM (or a CTA pair on the two SMs of a TPC), 10 warps:
 //   warp 0    TMA producer: A/B k-blocks of 64 into a shared-memory ring;
-//   warp 1    tensor-memory owner and MMA issuer (one elected thread):
-//             128 x BN x 16 tcgen05.mma into one of two TMEM accumulators;
+//   warp 1    tensor-memory owner and MMA issuer (one elected thread; in a
+//             pair, rank 0's): 128 x BN x 16 (pair: 256 x BN x 16,
+//             cta_group::2) tcgen05.mma into one of two TMEM accumulators;
 //   warps 2-9 epilogue, two warps per TMEM lane quarter (warp w reads lanes
 //             32*(w%4)...), splitting the tile's 128-byte column chunks:
 //             tcgen05.ld, epilogue math, the chunk written 128B-swizzled
 //             into a per-warp staging tile and stored by TMA (coalesced,
 //             asynchronous, rows/columns beyond C clipped by the tensor
-//             map). Double-buffered staging lets the next chunk's math
-//             overlap the previous chunk's store; the accumulator is
-//             released as soon as it is read, so the MMAs of the next tile
-//             overlap the epilogue of this one.
+//             map; an in-place fp32 residual is a TMA reduce-add). The
+//             accumulator is released as soon as it is read, so the MMAs of
+//             the next tile overlap the epilogue of this one.
 // Tiles are visited m-major (all n-tiles of a row block back to back) so a
 // row block of A is read from HBM once and re-read from L2.
 #include "kernels.h"
