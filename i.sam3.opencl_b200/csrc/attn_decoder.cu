@@ -28,6 +28,7 @@
 // bank groups: rows padded to c + 4 floats per head (few keys) or 16-byte
 // chunks rotated per head (many keys, rows stay 512 bytes for cp.async).
 #include "kernels.h"
+#include "tmap.cuh"
 
 #include <cuda_runtime.h>
 #include <math.h>
@@ -463,7 +464,7 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
 {
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = smem_limit_once<mha_few_kernel<C>>(smem);
     if (e != cudaSuccess)
         return (int)e;
     int per_sm = 1;
@@ -507,9 +508,7 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         const int nsplit = many_splits(P, Nk, num_sms);
         if (!ws || ws_bytes < k_mha_workspace(P, Nq, Nk, dint, num_sms))
             return K_EARG;
-        cudaError_t e = cudaFuncSetAttribute(mha_many_split_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kManySmem);
+        cudaError_t e = smem_limit_once<mha_many_split_kernel>(kManySmem);
         if (e != cudaSuccess)
             return (int)e;
         const int per = ((Nk + nsplit - 1) / nsplit + kChunk - 1) / kChunk * kChunk;

@@ -433,7 +433,7 @@ template <bool OUT_BF16>
 int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int grid, cudaStream_t s)
 {
     auto kern = attn_tc_kernel<OUT_BF16>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = smem_limit_once<attn_tc_kernel<OUT_BF16>>(SMEM_BYTES);
     if (e != cudaSuccess)
         return (int)e;
     kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tkv, a);
@@ -454,9 +454,7 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     if (!make_tmap_bf16(&tq, qkv, rows, 3ull * E, 3ull * E, BQ) ||
         !make_tmap_bf16(&tkv, qkv, rows, 3ull * E, 3ull * E, BKV))
         return K_ETMAP;
-    int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sms();
     AttnArgs a;
     a.nseq = nseq;
     a.N = N;

@@ -849,7 +849,8 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
     using L = GemmSmem<BN>;
     auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, EPI>;
     cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+        smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, EPI>>(
+            L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
     const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM) *
@@ -877,7 +878,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return 1;
     cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+        smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, false, true>>(L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
     cudaLaunchAttribute attr[1];

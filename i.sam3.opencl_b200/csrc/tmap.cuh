@@ -92,4 +92,36 @@ inline bool make_tmap_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t
            CUDA_SUCCESS;
 }
 
+// Raises kernel Kern's dynamic shared-memory limit to `bytes` once per
+// device (the attribute persists; setting it before every launch costs host
+// time in front of short kernels).
+template <auto Kern>
+inline cudaError_t smem_limit_once(int bytes)
+{
+    static int set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (set[dev] >= bytes)
+        return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess)
+        set[dev] = bytes;
+    return e;
+}
+
+// Multiprocessor count of the current device, queried once per device.
+inline int device_sms()
+{
+    static int sms[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return 148;
+    if (!sms[dev] &&
+        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return sms[dev];
+}
+
 }  // namespace sam3
