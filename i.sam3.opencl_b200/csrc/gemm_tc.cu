@@ -399,8 +399,9 @@ __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &c
 // of 64 one 4-D TMA load of the input map (C, W, H, image) at the tap's
 // shifted pixel block -- rows and columns outside the map read as zero, so
 // the padding costs nothing and no im2col is ever written. An M tile is an
-// 8 x 16 pixel block (row r = y * 16 + x), and each epilogue warp's 32 rows
-// (two pixel rows) leave as one 4-D TMA store into the NHWC output.
+// 8 x 16 pixel block (row r = y * 16 + x; a CTA pair's tile is 16 x 16, rank
+// r taking pixel rows 8r .. 8r + 7), and each epilogue warp's 32 rows (two
+// pixel rows) leave as one 4-D TMA store into the NHWC output.
 // PAIR: a cluster of two CTAs (the two SMs of a TPC) computes 256 x BN
 // tiles with cta_group::2 MMAs: each CTA loads its 128 rows of A and half of
 // the B tile into its own shared memory, both signalling rank 0's full
@@ -417,7 +418,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmC, const GemmEpi p,
                         const ConvGeom cg)
 {
-    static_assert(!(PAIR && CONV3), "pair tiles are row blocks");
+    // CONV3 pixel blocks: 8 x 16 per CTA; a pair's tile is 16 x 16, rank r
+    // taking pixel rows 8r .. 8r + 7 of it.
+    constexpr int CBH = PAIR ? 16 : 8;
     constexpr bool LOGITS = EPI == kEpiLogits;
     static_assert(!LOGITS || (BN == 128 && !OUT_BF16 && !TMA_STORE && !PAIR && !CONV3),
                   "the logits epilogue: one 128-column fp32 tile per row block");
@@ -498,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (CONV3) {
                     const int mt = t / num_n;
                     img = mt / (cg.cyb * cg.cxb);
-                    py0 = ((mt / cg.cxb) % cg.cyb) * 8;
+                    py0 = ((mt / cg.cxb) % cg.cyb) * CBH + (int)rank * 8;
                     px0 = (mt % cg.cxb) * 16;
                 }
                 for (int kb = 0; kb < kblocks; kb++) {
@@ -512,7 +515,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (rank == 0)
                             mbar_arrive_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
                         const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
-                        tma_load_2d_pair(sa, &tmA, fb, kb * BK, m0);
+                        if constexpr (CONV3) {
+                            const int cblocks = p.K / (9 * BK), tap = kb / cblocks;
+                            tma_load_4d_pair(sa, &tmA, fb, (kb % cblocks) * BK,
+                                             px0 + tap % 3 - 1, py0 + tap / 3 - 1, img);
+                        }
+                        else
+                            tma_load_2d_pair(sa, &tmA, fb, kb * BK, m0);
                         tma_load_2d_pair(sa + L::A_BYTES, &tmB, fb, kb * BK,
                                          n0 + (int)rank * (BN / 2));
                         issued_mask |= 1u << stage;
@@ -639,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // (p.M when outside the map)
                 const int mt = t / num_n;
                 cimg = mt / (cg.cyb * cg.cxb);
-                cy = ((mt / cg.cxb) % cg.cyb) * 8 + 2 * quarter;
+                cy = ((mt / cg.cxb) % cg.cyb) * CBH + (int)rank * 8 + 2 * quarter;
                 cx0 = (mt % cg.cxb) * 16;
                 const int py = cy + lane / 16, px = cx0 + lane % 16;
                 m = (py < cg.cH && px < cg.cW) ? (cimg * cg.cH + py) * cg.cW + px : p.M;
@@ -867,18 +876,19 @@ static int g_pair_clusters[64];
 // The pair kernel over 256 x 256 tiles: a persistent grid of as many CTA
 // pairs as can be resident at once (each cluster on the two SMs of a TPC).
 // Returns 1 when pairs cannot be launched here (the caller uses single CTAs).
-template <bool OUT_BF16, bool ROPE_PF>
+template <bool OUT_BF16, bool ROPE_PF, bool CONV3 = false>
 int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
-                const GemmEpi &p, int num_sms, cudaStream_t s)
+                const GemmEpi &p, int num_sms, cudaStream_t s,
+                const ConvGeom &cg = ConvGeom{0, 0, 0, 0, 0})
 {
     constexpr int BN = 256;
     using L = GemmSmem<BN, true>;
-    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, false, true>;
+    auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, CONV3, true>;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return 1;
     cudaError_t e =
-        smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, false, true>>(L::BYTES);
+        smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, CONV3, true>>(L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
     cudaLaunchAttribute attr[1];
@@ -903,10 +913,11 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
     }
     if (g_pair_clusters[dev] < 0)
         return 1;
-    const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
+    const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + 2 * BM - 1) / (2 * BM)) *
+                      ((p.N + BN - 1) / BN);
     const int pairs = tiles < g_pair_clusters[dev] ? tiles : g_pair_clusters[dev];
     cfg.gridDim = dim3(2 * pairs);
-    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, ConvGeom{0, 0, 0, 0, 0});
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, cg);
     return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
 }
 
@@ -1043,6 +1054,20 @@ extern "C" int k_conv3x3_bf16_tc(const void *X, int nimg, int H, int W, int C, c
     if (BN == 128)
         return out_bf16 ? launch<128, true, true, false, true>(ta, tb, tc, p, num_sms, st, cg)
                         : launch<128, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
+    // CTA pairs over 16 x 16 pixel blocks (K = 9C is long, so the halved B
+    // traffic pays, as for fc2) when one map alone gives every pair of SMs a
+    // tile: decided per map size, not per batch, so a map's result does not
+    // depend on how many maps are convolved with it.
+    ConvGeom cgp = cg;
+    cgp.cyb = (H + 15) / 16;
+    CUtensorMap tb_half;
+    if (N == 256 && (long)cgp.cyb * cgp.cxb >= num_sms / 2 &&
+        make_tmap_bf16(&tb_half, Wt, (uint64_t)N, (uint64_t)K, (uint64_t)K, 128)) {
+        const int rc = out_bf16 ? launch_pair<true, false, true>(ta, tb_half, tc, p, num_sms, st, cgp)
+                                : launch_pair<false, false, true>(ta, tb_half, tc, p, num_sms, st, cgp);
+        if (rc != 1)
+            return rc;
+    }
     return out_bf16 ? launch<256, true, true, false, true>(ta, tb, tc, p, num_sms, st, cg)
                     : launch<256, false, true, false, true>(ta, tb, tc, p, num_sms, st, cg);
 }

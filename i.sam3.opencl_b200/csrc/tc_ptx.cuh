@@ -259,6 +259,18 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const 
         : "memory");
 }
 
+// 4-D tile load by either CTA of a pair (see tma_load_2d_pair).
+__device__ __forceinline__ void tma_load_4d_pair(void *smem_dst, const CUtensorMap *map,
+                                                 uint32_t bar, int32_t c0, int32_t c1, int32_t c2,
+                                                 int32_t c3)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit()
 {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");

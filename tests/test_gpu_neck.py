@@ -52,14 +52,16 @@ def test_neck_vs_oracle(cb, sb, ob, grid):
     neck.close()
 
 
-def test_neck_batch_equals_single_tiles(cb, sb, ob):
-    """Tiles batched into one call give, bit for bit, the per-tile results."""
-    seed, grid = 52, 24
-    neck = sb.Neck(cb, grid=grid, embed=1024, max_tiles=2)
+@pytest.mark.parametrize("grid,ntile", [(24, 2), (72, 3)])
+def test_neck_batch_equals_single_tiles(cb, sb, ob, grid, ntile):
+    """Tiles batched into one call give, bit for bit, the per-tile results
+    (at grid 72 the 3x3 convolutions of levels 0 and 1 run on CTA pairs)."""
+    seed = 52
+    neck = sb.Neck(cb, grid=grid, embed=1024, max_tiles=ntile)
     neck.init_random(seed, 0.02)
-    xs = ob.normal(seed, 9301, (2, grid * grid, 1024))
-    both = _run(cb, sb, neck, cb.upload(xs, sb.F32), 2, grid)
-    for t in range(2):
+    xs = ob.normal(seed, 9301, (ntile, grid * grid, 1024))
+    both = _run(cb, sb, neck, cb.upload(xs, sb.F32), ntile, grid)
+    for t in range(ntile):
         one = _run(cb, sb, neck, cb.upload(xs[t], sb.F32), 1, grid)
         for a, b in zip(one, both):
             assert np.array_equal(a[0], b[t])
