@@ -219,6 +219,139 @@ __global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const flo
     }
 }
 
+// Image -> token attention (at most kFewSmall keys, 16 channels per head):
+// the kernel above is bound by shared-memory bandwidth (every (query, head)
+// thread reads its head's K and V rows for each key). Here a thread takes
+// two queries of one head, so each K / V read from shared memory serves
+// both: units of 64 queries, thread (head h, slot qt) computing queries
+// qt and qt + 32 of the unit, the next unit's two queries in flight while
+// this one computes. Same arithmetic per query as the small path above.
+__global__ void __launch_bounds__(256, 2) mha_few2_kernel(const float *__restrict__ Q, long sq,
+                                                         const float *__restrict__ K, long sk,
+                                                         const float *__restrict__ V, long sv,
+                                                         float *__restrict__ O, int P, int Nq,
+                                                         int Nk, float scale)
+{
+    constexpr int C = 16, D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
+    extern __shared__ float kv[];  // K rows then V rows, [Nk][8][CP] each
+    float *ks = kv;
+    float *vs = kv + Nk * ROW;
+    const int h = threadIdx.x & 7, qt = threadIdx.x >> 3;
+    const int nqb = (Nq + 63) / 64;
+    const long U = (long)P * nqb;
+    const long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    float q[2][C];
+    auto load2 = [&](long u, float (&dst)[2][C]) {
+        const long pu = u / nqb;
+        const int qb = (int)(u - pu * nqb) * 64 + qt;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int qi = qb + 32 * i;
+            if (qi < Nq)
+                load_q<C>(Q + pu * sq + (long)qi * D + h * C, dst[i], scale);
+        }
+    };
+    if (u0 < u1)
+        load2(u0, q);
+    long staged = -1;
+#pragma unroll 1
+    for (long u = u0; u < u1; u++) {
+        const long p = u / nqb;
+        const int qb = (int)(u - p * nqb) * 64 + qt;
+        if (p != staged) {  // CTA-uniform: stage this prompt's K and V
+            __syncthreads();
+            const float *kb = K + p * sk, *vb = V + p * sv;
+            for (int i = threadIdx.x; i < Nk * (D / 4); i += blockDim.x) {
+                const int j = i / (D / 4), col = (i - j * (D / 4)) * 4;
+                const int dst = j * ROW + (col / C) * CP + col % C;
+                *reinterpret_cast<float4 *>(ks + dst) =
+                    __ldg(reinterpret_cast<const float4 *>(kb + (long)j * D + col));
+                *reinterpret_cast<float4 *>(vs + dst) =
+                    __ldg(reinterpret_cast<const float4 *>(vb + (long)j * D + col));
+            }
+            __syncthreads();
+            staged = p;
+        }
+        float qn[2][C];
+        const bool more = u + 1 < u1;
+        if (more)
+            load2(u + 1, qn);
+        if (qb < Nq) {
+            float sc[2][kFewSmall], m[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int j = 0; j < kFewSmall; j++) {
+                sc[0][j] = sc[1][j] = -INFINITY;
+                if (j < Nk) {
+                    const float4 *kr = reinterpret_cast<const float4 *>(ks + j * ROW + h * CP);
+                    float d[2][4] = {};
+#pragma unroll
+                    for (int c = 0; c < C / 4; c++) {
+                        const float4 k4 = kr[c];
+#pragma unroll
+                        for (int i = 0; i < 2; i++) {
+                            d[i][0] = fmaf(q[i][4 * c], k4.x, d[i][0]);
+                            d[i][1] = fmaf(q[i][4 * c + 1], k4.y, d[i][1]);
+                            d[i][2] = fmaf(q[i][4 * c + 2], k4.z, d[i][2]);
+                            d[i][3] = fmaf(q[i][4 * c + 3], k4.w, d[i][3]);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 2; i++) {
+                        sc[i][j] = (d[i][0] + d[i][1]) + (d[i][2] + d[i][3]);
+                        m[i] = fmaxf(m[i], sc[i][j]);
+                    }
+                }
+            }
+            float o[2][C], l[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int c = 0; c < C; c++)
+                o[0][c] = o[1][c] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kFewSmall; j++) {
+                if (j < Nk) {
+                    float e[2];
+#pragma unroll
+                    for (int i = 0; i < 2; i++) {
+                        e[i] = __expf(sc[i][j] - m[i]);
+                        l[i] += e[i];
+                    }
+                    const float4 *vr = reinterpret_cast<const float4 *>(vs + j * ROW + h * CP);
+#pragma unroll
+                    for (int c = 0; c < C / 4; c++) {
+                        const float4 v4 = vr[c];
+#pragma unroll
+                        for (int i = 0; i < 2; i++) {
+                            o[i][4 * c] = fmaf(e[i], v4.x, o[i][4 * c]);
+                            o[i][4 * c + 1] = fmaf(e[i], v4.y, o[i][4 * c + 1]);
+                            o[i][4 * c + 2] = fmaf(e[i], v4.z, o[i][4 * c + 2]);
+                            o[i][4 * c + 3] = fmaf(e[i], v4.w, o[i][4 * c + 3]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int qi = qb + 32 * i;
+                if (qi < Nq) {
+                    const float inv = 1.0f / l[i];
+                    float4 *op = reinterpret_cast<float4 *>(O + (p * Nq + qi) * D + h * C);
+#pragma unroll
+                    for (int c = 0; c < C / 4; c++)
+                        op[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv,
+                                            o[i][4 * c + 2] * inv, o[i][4 * c + 3] * inv);
+                }
+            }
+        }
+        if (more) {
+#pragma unroll
+            for (int c = 0; c < C; c++) {
+                q[0][c] = qn[0][c];
+                q[1][c] = qn[1][c];
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------ many keys
 constexpr int kManyC = 16;                 // channels per head
 constexpr int kManyD = kManyC * kHeads;    // 128
@@ -458,10 +591,30 @@ int many_splits(int P, int Nk, int num_sms)
     return want < 1 ? 1 : (want > cap ? cap : want);
 }
 
+int launch_few2(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
+                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
+{
+    const int smem = 2 * Nk * kHeads * (16 + 4) * 4;
+    cudaError_t e = smem_limit_once<mha_few2_kernel>(smem);
+    if (e != cudaSuccess)
+        return (int)e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel, 256, smem);
+    if (e != cudaSuccess)
+        return (int)e;
+    const long units = (long)P * ((Nq + 63) / 64);
+    const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
+    mha_few2_kernel<<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
+        qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale);
+    return (int)cudaGetLastError();
+}
+
 template <int C>
 int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
 {
+    if (C == 16 && Nk <= kFewSmall)
+        return launch_few2(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
     cudaError_t e = smem_limit_once<mha_few_kernel<C>>(smem);
