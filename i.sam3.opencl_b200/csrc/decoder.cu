@@ -117,18 +117,33 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
         const int no = l < 2 ? 256 : nout;
         const float *in = (l & 1) ? hs : xs;
         float *o = (l & 1) ? xs : hs;
-        for (int r = warp; r < no; r += 8) {
-            const float *wr = W + (long)r * 256;
-            double acc = 0.0;
+        // Four rows per pass (r0, r0 + 8, r0 + 16, r0 + 24): four independent
+        // accumulation and reduction chains per warp; each row's sum is
+        // formed in the same order as with one row at a time.
+        for (int r0 = warp; r0 < no; r0 += 32) {
+            double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                acc += (double)__ldg(wr + lane + 32 * k) * (double)in[lane + 32 * k];
+            for (int k = 0; k < 8; k++) {
+                const double xv = (double)in[lane + 32 * k];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (r0 + 8 * i < no)
+                        acc[i] += (double)__ldg(W + (long)(r0 + 8 * i) * 256 + lane + 32 * k) * xv;
+            }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
-                acc += __shfl_xor_sync(0xffffffffu, acc, off);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
             if (lane == 0) {
-                acc += (double)__ldg(B + r);
-                o[r] = (l < 2 && acc < 0.0) ? 0.0f : (float)acc;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int r = r0 + 8 * i;
+                    if (r < no) {
+                        const double v = acc[i] + (double)__ldg(B + r);
+                        o[r] = (l < 2 && v < 0.0) ? 0.0f : (float)v;
+                    }
+                }
             }
         }
         __syncthreads();
