@@ -360,6 +360,7 @@ constexpr int kChunk = 32;                 // keys per staged chunk
 constexpr int kStages = 3;                 // staged chunks in flight
 constexpr int kLanes = 8;                  // key lanes per (query, head)
 constexpr int kPart = 2 + kManyC;          // m, l, o[16]
+constexpr float kManyLazy = 8.0f;          // rescale threshold (natural log units)
 constexpr int kManySmem = kStages * 2 * kChunk * kManyRow * 4;  // K and V rings
 
 // Position (in floats) of channels 4c..4c+3 of head h within a staged key
@@ -471,17 +472,23 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
             float e[2][KT];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
-                const float mn = fmaxf(m[u], bm[u]), corr = __expf(m[u] - mn);
-                l[u] *= corr;
+                // The running maximum is raised (and o, l rescaled) only when
+                // the block's maximum exceeds it by more than kManyLazy, so
+                // e <= e^kManyLazy and most blocks skip the rescale; the
+                // final normalisation makes the result independent of it.
+                if (bm[u] > m[u] + kManyLazy) {
+                    const float corr = __expf(m[u] - bm[u]);  // 0 on the first block
+                    l[u] *= corr;
 #pragma unroll
-                for (int cc = 0; cc < kManyC; cc++)
-                    o[u][cc] *= corr;
+                    for (int cc = 0; cc < kManyC; cc++)
+                        o[u][cc] *= corr;
+                    m[u] = bm[u];
+                }
 #pragma unroll
                 for (int t = 0; t < KT; t++) {
-                    e[u][t] = __expf(s[u][t] - mn);  // 0 for keys past the chunk
+                    e[u][t] = __expf(s[u][t] - m[u]);  // 0 for keys past the chunk
                     l[u] += e[u][t];
                 }
-                m[u] = mn;
             }
 #pragma unroll
             for (int t = 0; t < KT; t++) {
