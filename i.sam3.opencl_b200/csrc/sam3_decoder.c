@@ -380,6 +380,15 @@ static int lintok(cb_decoder *d, const float *X, long rows, int in, int out, int
                  residual ? Y : NULL, 0, act);
 }
 
+/* The same on the X that the previous lintok rounded into the token
+ * operand buffer (no second rounding pass). */
+static int lintok_again(cb_decoder *d, long rows, int in, int out, int wi, int bi, float *Y,
+                        int residual, int act)
+{
+    return lin16(d, "dec_gemm_tok", d->tok_bf16, rows, in, out, wi, bi, Y, residual ? Y : NULL, 0,
+                 act);
+}
+
 static int ln(cb_decoder *d, float *X, void *Y, int y_bf16, long rows, int C, int wi, int bi,
               float eps, int act)
 {
@@ -477,13 +486,24 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
     return lintok(d, d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, 1, K_ACT_NONE);
 }
 
-/* token_mlp (sam3_model.c:1231-1237): 256 -> 2048 (ReLU) -> 256, residual. */
+/* token_mlp (sam3_model.c:1231-1237): 256 -> 2048 (ReLU) -> 256, residual.
+ * The hidden layer is written once, in bf16 (into sh's storage), as the
+ * second GEMM's operand. */
 static int token_mlp(cb_decoder *d, int P, int l)
 {
+    cb_backend *b = d->b;
     const long nt = (long)P * DEC_NTOK;
+    const double dr = (double)nt;
 
-    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 2048, LAY(l, M1W), LAY(l, M1B), d->sh, 0, K_ACT_RELU));
-    return lintok(d, d->sh, nt, 2048, DEC_DIM, LAY(l, M2W), LAY(l, M2B), d->qry, 1, K_ACT_NONE);
+    LAUNCH("dec_cast", 0, dr * DEC_DIM * 6,
+           k_cast_f32_bf16(d->qry, d->tok_bf16, nt * DEC_DIM, (k_stream)b->stream));
+    LAUNCH("dec_gemm_tok", 2.0 * dr * DEC_DIM * 2048,
+           dr * DEC_DIM * 2 + (double)DEC_DIM * 2048 * 2 + dr * 2048 * 2,
+           k_gemm_bf16_tc((int)nt, 2048, DEC_DIM, d->tok_bf16, DEC_DIM, d->w[LAY(l, M1W)], DEC_DIM,
+                          d->sh, 2048, 1, (const float *)d->w[LAY(l, M1B)], NULL, 2048, 0, 1.0f,
+                          K_ACT_RELU, NULL, b->d_err, b->num_sms, (k_stream)b->stream));
+    return lin16(d, "dec_gemm_tok", d->sh, nt, 2048, DEC_DIM, LAY(l, M2W), LAY(l, M2B), d->qry,
+                 d->qry, 0, K_ACT_NONE);
 }
 
 /* Self attention of the tokens; layer 0 without positional encoding and
@@ -500,7 +520,7 @@ static int self_attention(cb_decoder *d, int P, int l)
         qk = d->qin;
     }
     CB_TRY(lintok(d, qk, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0, K_ACT_NONE));
-    CB_TRY(lintok(d, qk, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
+    CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
     CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
                   K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_NTOK, DEC_DIM, d->sq, DEC_NTOK * DEC_DIM, d->sk,
