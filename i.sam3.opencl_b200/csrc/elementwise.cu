@@ -213,6 +213,16 @@ __global__ void add_bcast_kernel(float *out, const float *a, const float *b, lon
         out[i] = a[i] + b[i % bmod];
 }
 
+// out = bf16(a + b): the sum rounded once to bf16 (the same value as the
+// fp32 sum followed by a cast), for a sum whose only reader is a GEMM.
+__global__ void add_bf16_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                __nv_bfloat16 *__restrict__ out, long n)
+{
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+        out[i] = __float2bfloat16_rn(a[i] + b[i]);
+}
+
 // window_partition (sam3_kernels.cl:712-724).
 __global__ void window_partition_kernel(const float *X, float *out, int H, int C, int ws, int nwx,
                                         long total)
@@ -438,6 +448,15 @@ extern "C" int k_add_bcast(float *out, const float *a, const float *b, long n, l
     if (bmod <= 0)
         return K_EARG;
     add_bcast_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(out, a, b, n, bmod);
+    LAUNCH_RET();
+}
+
+extern "C" int k_add_bf16(const float *a, const float *b, void *out, long n, k_stream s)
+{
+    if (n <= 0)
+        return K_EARG;
+    add_bf16_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+        a, b, reinterpret_cast<__nv_bfloat16 *>(out), n);
     LAUNCH_RET();
 }
 

@@ -100,6 +100,8 @@ int k_layernorm(const float *X, void *Y, int y_bf16, const float *g,
 int k_softmax_rows(float *S, long rows, int L, k_stream s);
 int k_add_bcast(float *out, const float *a, const float *b, long n, long bmod,
                 k_stream s);
+/* out bf16 [n] = a + b (fp32 sum, one rounding). */
+int k_add_bf16(const float *a, const float *b, void *out, long n, k_stream s);
 int k_window_partition(const float *X, float *out, int H, int C, int ws,
                        int nwx, k_stream s);
 int k_window_unpartition_add(float *X, const float *Wd, int H, int C, int ws,

@@ -69,7 +69,7 @@ struct cb_decoder {
     /* image-side state (sam_encode's decoder caches) */
     float *src, *srcpe, *pe_img, *kp0, *vp0, *qp0, *feat_s0, *feat_s1;
     /* token stream [batch * 8, 256] and its scratch */
-    float *qpe, *qry, *qin, *sq, *sk, *sv, *so, *sh;
+    float *qpe, *qry, *sq, *sk, *sv, *so, *sh;
     void *tok_bf16;             /* bf16 [batch * 8, 2048] GEMM operand */
     /* per-prompt image stream */
     float *keys;                /* [batch * T, 256] */
@@ -106,7 +106,7 @@ void cb_decoder_free(cb_decoder *d)
     }
     {
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
-                       d->feat_s1, d->qpe, d->qry, d->qin, d->sq, d->sk, d->sv, d->so,
+                       d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
                        d->bv, d->bo, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws};
@@ -159,7 +159,6 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->feat_s1, 4 * T * 64 * 4);
     A(d->qpe, nt * DEC_DIM * 4);
     A(d->qry, nt * DEC_DIM * 4);
-    A(d->qin, nt * DEC_DIM * 4);
     A(d->sq, nt * DEC_DIM * 4);
     A(d->sk, nt * DEC_DIM * 4);
     A(d->sv, nt * DEC_DIM * 4);
@@ -409,6 +408,17 @@ static int add(cb_decoder *d, float *out, const float *a, const float *bb, long 
     return CB_OK;
 }
 
+/* tok_bf16 = bf16(qry + qpe): the tokens with their positional encoding,
+ * read only by the Linears that follow (lintok_again). */
+static int add_tok_pe(cb_decoder *d, long nt)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_add", (double)nt * DEC_DIM, (double)nt * DEC_DIM * 10,
+           k_add_bf16(d->qry, d->qpe, d->tok_bf16, nt * DEC_DIM, (k_stream)b->stream));
+    return CB_OK;
+}
+
 static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, long sq,
                const float *k, long sk, const float *v, long sv, float *o)
 {
@@ -474,8 +484,8 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
 {
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
 
-    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
+    CB_TRY(add_tok_pe(d, nt));
+    CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                   K_ACT_NONE));
     CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
                  d->bk, NULL, 0, K_ACT_NONE));
@@ -513,13 +523,15 @@ static int self_attention(cb_decoder *d, int P, int l)
 {
     const long nt = (long)P * DEC_NTOK;
     const int blk = l ? SAM3_DA_L1_SELF : SAM3_DA_L0_SELF;
-    const float *qk = d->qry;
 
     if (l) {
-        CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-        qk = d->qin;
+        CB_TRY(add_tok_pe(d, nt));
+        CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
+                            K_ACT_NONE));
     }
-    CB_TRY(lintok(d, qk, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0, K_ACT_NONE));
+    else
+        CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
+                      K_ACT_NONE));
     CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
     CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
                   K_ACT_NONE));
@@ -542,11 +554,11 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
     const int blk = l ? SAM3_DA_L1_I2T : SAM3_DA_L0_I2T;
 
-    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
+    CB_TRY(add_tok_pe(d, nt));
     if (l)
         CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, QW),
                      ATT(blk, QB), d->bq, NULL, 0, K_ACT_NONE));
-    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
+    CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
                   K_ACT_NONE));
     CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
                   K_ACT_NONE));
@@ -620,8 +632,8 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
      * shared layer-0 projections, MLP, image -> token. */
     CB_TRY(self_attention(d, P, 0));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N1W), LAY(0, N1B), DEC_EPS, K_ACT_NONE));
-    CB_TRY(add(d, d->qin, d->qry, d->qpe, nt * DEC_DIM, nt * DEC_DIM));
-    CB_TRY(lintok(d, d->qin, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
+    CB_TRY(add_tok_pe(d, nt));
+    CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
                   ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->kp0, 0, d->vp0, 0, d->so));
     CB_TRY(lintok(d, d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
