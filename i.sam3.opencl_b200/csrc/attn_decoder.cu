@@ -30,6 +30,7 @@
 #include "kernels.h"
 #include "tmap.cuh"
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -40,6 +41,13 @@ namespace sam3 {
 namespace {
 
 constexpr int kHeads = 8;
+
+// Two floats rounded to nearest-even bf16, packed low / high.
+__device__ __forceinline__ uint32_t bf16_pair(float lo, float hi)
+{
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
 {
@@ -226,10 +234,12 @@ __global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const flo
 // both: units of 64 queries, thread (head h, slot qt) computing queries
 // qt and qt + 32 of the unit, the next unit's two queries in flight while
 // this one computes. Same arithmetic per query as the small path above.
+// OUT_BF16: O is written as bf16 (for a consumer that only feeds a GEMM).
+template <bool OUT_BF16>
 __global__ void __launch_bounds__(256, 2) mha_few2_kernel(const float *__restrict__ Q, long sq,
                                                          const float *__restrict__ K, long sk,
                                                          const float *__restrict__ V, long sv,
-                                                         float *__restrict__ O, int P, int Nq,
+                                                         void *__restrict__ O, int P, int Nq,
                                                          int Nk, float scale)
 {
     constexpr int C = 16, D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
@@ -334,11 +344,25 @@ __global__ void __launch_bounds__(256, 2) mha_few2_kernel(const float *__restric
                 const int qi = qb + 32 * i;
                 if (qi < Nq) {
                     const float inv = 1.0f / l[i];
-                    float4 *op = reinterpret_cast<float4 *>(O + (p * Nq + qi) * D + h * C);
+                    const long off = (p * Nq + qi) * D + h * C;
+                    if (OUT_BF16) {
+                        uint4 *op = reinterpret_cast<uint4 *>(
+                            reinterpret_cast<__nv_bfloat16 *>(O) + off);
 #pragma unroll
-                    for (int c = 0; c < C / 4; c++)
-                        op[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv,
-                                            o[i][4 * c + 2] * inv, o[i][4 * c + 3] * inv);
+                        for (int c = 0; c < C / 8; c++)
+                            op[c] = make_uint4(
+                                bf16_pair(o[i][8 * c] * inv, o[i][8 * c + 1] * inv),
+                                bf16_pair(o[i][8 * c + 2] * inv, o[i][8 * c + 3] * inv),
+                                bf16_pair(o[i][8 * c + 4] * inv, o[i][8 * c + 5] * inv),
+                                bf16_pair(o[i][8 * c + 6] * inv, o[i][8 * c + 7] * inv));
+                    }
+                    else {
+                        float4 *op = reinterpret_cast<float4 *>(reinterpret_cast<float *>(O) + off);
+#pragma unroll
+                        for (int c = 0; c < C / 4; c++)
+                            op[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv,
+                                                o[i][4 * c + 2] * inv, o[i][4 * c + 3] * inv);
+                    }
                 }
             }
         }
@@ -598,20 +622,22 @@ int many_splits(int P, int Nk, int num_sms)
     return want < 1 ? 1 : (want > cap ? cap : want);
 }
 
+template <bool OUT_BF16>
 int launch_few2(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
-                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
+                const float *vp, long sv, void *o, float scale, int num_sms, cudaStream_t st)
 {
     const int smem = 2 * Nk * kHeads * (16 + 4) * 4;
-    cudaError_t e = smem_limit_once<mha_few2_kernel>(smem);
+    cudaError_t e = smem_limit_once<mha_few2_kernel<OUT_BF16>>(smem);
     if (e != cudaSuccess)
         return (int)e;
     int per_sm = 1;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel, 256, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel<OUT_BF16>, 256,
+                                                      smem);
     if (e != cudaSuccess)
         return (int)e;
     const long units = (long)P * ((Nq + 63) / 64);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
-    mha_few2_kernel<<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
+    mha_few2_kernel<OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
         qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale);
     return (int)cudaGetLastError();
 }
@@ -621,7 +647,7 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
 {
     if (C == 16 && Nk <= kFewSmall)
-        return launch_few2(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
+        return launch_few2<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
     cudaError_t e = smem_limit_once<mha_few_kernel<C>>(smem);
@@ -688,4 +714,16 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
     if (c == 32)
         return launch_few<32>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     return K_EARG;
+}
+
+extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
+                              long sk, const float *vp, long sv, void *o, int num_sms, k_stream s)
+{
+    using namespace sam3;
+    if (P <= 0 || Nq <= 0 || Nk <= 0 || Nk > kFewSmall || ((uintptr_t)qp & 15) ||
+        ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
+        (sk & 3) || (sv & 3))
+        return K_EARG;
+    return launch_few2<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f), num_sms,
+                             reinterpret_cast<cudaStream_t>(s));
 }

@@ -74,7 +74,7 @@ struct cb_decoder {
     /* per-prompt image stream */
     float *keys;                /* [batch * T, 256] */
     void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
-    float *bq, *bk, *bv, *bo;   /* [batch * T, 128] */
+    float *bq, *bk, *bv;        /* [batch * T, 128] */
     void *bo_bf16;              /* bf16 [batch * T, 128] */
     void *u1_bf16;              /* bf16 [batch * 4T, 64] */
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
@@ -108,7 +108,7 @@ void cb_decoder_free(cb_decoder *d)
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
-                       d->bv, d->bo, d->bo_bf16, d->u1_bf16,
+                       d->bv, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
@@ -171,7 +171,6 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->bq, B * T * 128 * 4);
     A(d->bk, B * T * 128 * 4);
     A(d->bv, B * T * 128 * 4);
-    A(d->bo, B * T * 128 * 4);
     A(d->bo_bf16, B * T * 128 * 2);
     A(d->u1_bf16, B * 4 * T * 64 * 2);
     A(d->hyper, B * 96 * 4);
@@ -562,10 +561,18 @@ static int i2t_attention(cb_decoder *d, int P, int l)
                   K_ACT_NONE));
     CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
                   K_ACT_NONE));
-    CB_TRY(mha(d, P, DEC_T, DEC_NTOK, 128, l ? d->bq : d->qp0, l ? (long)DEC_T * 128 : 0, d->sk,
-               DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo));
-    CB_TRY(lin32(d, "dec_gemm_img", d->bo, d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW),
-                 ATT(blk, OB), d->keys, l ? d->keys : d->src, l ? 0 : DEC_T, K_ACT_NONE));
+    {
+        cb_backend *b = d->b;
+
+        /* the attention output is read only by the output projection: bf16 */
+        LAUNCH("dec_mha_i2t", 4.0 * P * DEC_T * (double)DEC_NTOK * 128,
+               (double)P * DEC_T * 128 * (4 + 2),
+               k_mha_i2t_bf16(P, DEC_T, DEC_NTOK, l ? d->bq : d->qp0, l ? (long)DEC_T * 128 : 0,
+                              d->sk, DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo_bf16,
+                              b->num_sms, (k_stream)b->stream));
+    }
+    CB_TRY(lin16(d, "dec_gemm_img", d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB),
+                 d->keys, l ? d->keys : d->src, l ? 0 : DEC_T, K_ACT_NONE));
     {
         cb_backend *b = d->b;
 
