@@ -234,9 +234,10 @@ __global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const flo
 // both: units of 64 queries, thread (head h, slot qt) computing queries
 // qt and qt + 32 of the unit, the next unit's two queries in flight while
 // this one computes. Same arithmetic per query as the small path above.
-// OUT_BF16: O is written as bf16 (for a consumer that only feeds a GEMM).
-template <bool OUT_BF16>
-__global__ void __launch_bounds__(256, 2) mha_few2_kernel(const float *__restrict__ Q, long sq,
+// Q_BF16: Q is read as bf16 (written so by its projection); OUT_BF16: O is
+// written as bf16 (for a consumer that only feeds a GEMM).
+template <bool Q_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(256, 2) mha_few2_kernel(const void *__restrict__ Q, long sq,
                                                          const float *__restrict__ K, long sk,
                                                          const float *__restrict__ V, long sv,
                                                          void *__restrict__ O, int P, int Nq,
@@ -257,8 +258,25 @@ __global__ void __launch_bounds__(256, 2) mha_few2_kernel(const float *__restric
 #pragma unroll
         for (int i = 0; i < 2; i++) {
             const int qi = qb + 32 * i;
-            if (qi < Nq)
-                load_q<C>(Q + pu * sq + (long)qi * D + h * C, dst[i], scale);
+            if (qi >= Nq)
+                continue;
+            const long off = pu * sq + (long)qi * D + h * C;
+            if (Q_BF16) {
+                const uint4 *q4 =
+                    reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(Q) + off);
+#pragma unroll
+                for (int c = 0; c < C / 8; c++) {
+                    const uint4 w = __ldg(q4 + c);
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        dst[i][8 * c + 2 * k] = __uint_as_float(ws[k] << 16) * scale;
+                        dst[i][8 * c + 2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u) * scale;
+                    }
+                }
+            }
+            else
+                load_q<C>(reinterpret_cast<const float *>(Q) + off, dst[i], scale);
         }
     };
     if (u0 < u1)
@@ -622,22 +640,22 @@ int many_splits(int P, int Nk, int num_sms)
     return want < 1 ? 1 : (want > cap ? cap : want);
 }
 
-template <bool OUT_BF16>
-int launch_few2(int P, int Nq, int Nk, const float *qp, long sq, const float *kp, long sk,
+template <bool Q_BF16, bool OUT_BF16>
+int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, const float *kp, long sk,
                 const float *vp, long sv, void *o, float scale, int num_sms, cudaStream_t st)
 {
     const int smem = 2 * Nk * kHeads * (16 + 4) * 4;
-    cudaError_t e = smem_limit_once<mha_few2_kernel<OUT_BF16>>(smem);
+    cudaError_t e = smem_limit_once<mha_few2_kernel<Q_BF16, OUT_BF16>>(smem);
     if (e != cudaSuccess)
         return (int)e;
     int per_sm = 1;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel<OUT_BF16>, 256,
-                                                      smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel<Q_BF16, OUT_BF16>,
+                                                      256, smem);
     if (e != cudaSuccess)
         return (int)e;
     const long units = (long)P * ((Nq + 63) / 64);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
-    mha_few2_kernel<OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
+    mha_few2_kernel<Q_BF16, OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
         qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale);
     return (int)cudaGetLastError();
 }
@@ -647,7 +665,7 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
 {
     if (C == 16 && Nk <= kFewSmall)
-        return launch_few2<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
+        return launch_few2<false, false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
     cudaError_t e = smem_limit_once<mha_few_kernel<C>>(smem);
@@ -716,7 +734,7 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
     return K_EARG;
 }
 
-extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
+extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
                               long sk, const float *vp, long sv, void *o, int num_sms, k_stream s)
 {
     using namespace sam3;
@@ -724,6 +742,6 @@ extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const float *qp, long sq, c
         ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
         (sk & 3) || (sv & 3))
         return K_EARG;
-    return launch_few2<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f), num_sms,
+    return launch_few2<true, true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f), num_sms,
                              reinterpret_cast<cudaStream_t>(s));
 }

@@ -119,9 +119,10 @@ int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
           const float *kp, long sk, const float *vp, long sv, float *o,
           void *ws, size_t ws_bytes, int num_sms, k_stream s);
 /* The decoder's image -> token attention (dint 128, at most 8 keys) with its
- * output o written as bf16 [P * Nq, 128] (the operand of the following
- * Linear): the same arithmetic as k_mha, one rounding of each output. */
-int k_mha_i2t_bf16(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
+ * queries qp read as bf16 (rows of 128, row stride sq elements; as the Q
+ * projection writes them) and its output o written as bf16 [P * Nq, 128]
+ * (the operand of the following Linear); otherwise the arithmetic of k_mha. */
+int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
                    long sk, const float *vp, long sv, void *o, int num_sms, k_stream s);
 
 /* Mask decoder (decoder.cu). convt_scatter: G [P*H*W, Co*4] (16-byte

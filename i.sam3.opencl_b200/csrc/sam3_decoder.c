@@ -466,8 +466,15 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_
                  ATT(SAM3_DA_L0_T2I, KW), ATT(SAM3_DA_L0_T2I, KB), d->kp0, NULL, 0, K_ACT_NONE));
     CB_TRY(lin32(d, "dec_gemm_img", d->src, d->kin_bf16, (long)T, DEC_DIM, 128,
                  ATT(SAM3_DA_L0_T2I, VW), ATT(SAM3_DA_L0_T2I, VB), d->vp0, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_img", d->srcpe, d->kin_bf16, (long)T, DEC_DIM, 128,
-                 ATT(SAM3_DA_L0_I2T, QW), ATT(SAM3_DA_L0_I2T, QB), d->qp0, NULL, 0, K_ACT_NONE));
+    /* qp0 is read only by the image -> token attention, as bf16 */
+    LAUNCH("dec_cast", 0, (double)T * DEC_DIM * 6,
+           k_cast_f32_bf16(d->srcpe, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));
+    LAUNCH("dec_gemm_img", 2.0 * T * DEC_DIM * 128,
+           (double)T * DEC_DIM * 2 + DEC_DIM * 128.0 * 2 + (double)T * 128 * 2,
+           k_gemm_bf16_tc(T, 128, DEC_DIM, d->kin_bf16, DEC_DIM, d->w[ATT(SAM3_DA_L0_I2T, QW)],
+                          DEC_DIM, d->qp0, 128, 1, (const float *)d->w[ATT(SAM3_DA_L0_I2T, QB)],
+                          NULL, 128, 0, 1.0f, K_ACT_NONE, NULL, b->d_err, b->num_sms,
+                          (k_stream)b->stream));
     d->have_image = 1;
     return CB_OK;
 }
@@ -554,9 +561,17 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     const int blk = l ? SAM3_DA_L1_I2T : SAM3_DA_L0_I2T;
 
     CB_TRY(add_tok_pe(d, nt));
-    if (l)
-        CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, QW),
-                     ATT(blk, QB), d->bq, NULL, 0, K_ACT_NONE));
+    if (l) {
+        cb_backend *b = d->b;
+
+        /* bq is read only by the image -> token attention, as bf16 */
+        LAUNCH("dec_gemm_img", 2.0 * rows * DEC_DIM * 128,
+               (double)rows * DEC_DIM * 2 + DEC_DIM * 128.0 * 2 + (double)rows * 128 * 2,
+               k_gemm_bf16_tc((int)rows, 128, DEC_DIM, d->kin_bf16, DEC_DIM, d->w[ATT(blk, QW)],
+                              DEC_DIM, d->bq, 128, 1, (const float *)d->w[ATT(blk, QB)], NULL,
+                              128, 0, 1.0f, K_ACT_NONE, NULL, b->d_err, b->num_sms,
+                              (k_stream)b->stream));
+    }
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
                   K_ACT_NONE));
     CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
