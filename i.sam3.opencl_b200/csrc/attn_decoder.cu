@@ -413,14 +413,39 @@ __device__ __forceinline__ int many_pos(int h, int c4)
     return h * kManyC + (((c4 + (h >> 1)) & 3) << 2);
 }
 
+// Byte offset of the 16-byte piece `half` (channels 8 half .. 8 half + 7)
+// of head h within a staged bf16 key row (256 bytes): the halves of heads
+// 4-7 are swapped, so the eight heads' reads of one half hit distinct banks.
+__device__ __forceinline__ int many_pos_bf16(int h, int half)
+{
+    return h * 32 + ((half ^ (h >> 2)) & 1) * 16;
+}
+
+// Eight bf16 values (one 16-byte piece) widened to fp32.
+__device__ __forceinline__ void widen8(const uint4 w, float (&f)[8])
+{
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        f[2 * k] = __uint_as_float(ws[k] << 16);
+        f[2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+    }
+}
+
+// KV_BF16: K and V are bf16 rows (as the decoder's projections write them);
+// staged the same way in half the shared memory and widened on read.
+template <bool KV_BF16>
 __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
-    const float *__restrict__ Q, long sq, const float *__restrict__ K, long sk,
-    const float *__restrict__ V, long sv, float *__restrict__ part, int Nq, int Nk,
+    const float *__restrict__ Q, long sq, const void *__restrict__ Kv, long sk,
+    const void *__restrict__ Vv, long sv, float *__restrict__ part, int Nq, int Nk,
     int keys_per_split, float scale)
 {
     extern __shared__ float sm[];
-    float *ks = sm;                                     // [kStages][kChunk][kManyRow]
-    float *vs = sm + kStages * kChunk * kManyRow;       // [kStages][kChunk][kManyRow]
+    constexpr int ROWF = KV_BF16 ? kManyRow / 2 : kManyRow;  // staged row, in floats
+    float *ks = sm;                                     // [kStages][kChunk][ROWF]
+    float *vs = sm + kStages * kChunk * ROWF;           // [kStages][kChunk][ROWF]
+    const float *K = reinterpret_cast<const float *>(Kv);
+    const float *V = reinterpret_cast<const float *>(Vv);
     const int split = blockIdx.x, nsplit = gridDim.x;
     const long p = blockIdx.y;
     // Thread = (query pair, head, key lane): queries qg and qg + 4 of the
@@ -430,16 +455,25 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
     const int k0 = split * keys_per_split;
     const int k1 = min(Nk, k0 + keys_per_split);
     const int nchunk = k1 > k0 ? (k1 - k0 + kChunk - 1) / kChunk : 0;
-    const float *kb = K + p * sk, *vb = V + p * sv;
+    const char *kb = reinterpret_cast<const char *>(Kv) + p * sk * (KV_BF16 ? 2 : 4);
+    const char *vb = reinterpret_cast<const char *>(Vv) + p * sv * (KV_BF16 ? 2 : 4);
+    (void)K;
+    (void)V;
 
     // Chunk c of this split into buffer b: 16-byte pieces into rotated rows.
     auto stage = [&](int c, int b) {
         const int j0 = k0 + c * kChunk, n = min(kChunk, k1 - j0);
-        for (int i = threadIdx.x; i < n * (kManyD / 4); i += blockDim.x) {
-            const int j = i / (kManyD / 4), col = (i - j * (kManyD / 4)) * 4;
-            const int dst = (b * kChunk + j) * kManyRow + many_pos(col / kManyC, (col % kManyC) / 4);
-            cp_async16(ks + dst, kb + (long)(j0 + j) * kManyD + col);
-            cp_async16(vs + dst, vb + (long)(j0 + j) * kManyD + col);
+        constexpr int PIECES = kManyD * (KV_BF16 ? 2 : 4) / 16;  // per key row
+        for (int i = threadIdx.x; i < n * PIECES; i += blockDim.x) {
+            const int j = i / PIECES, pc = i - j * PIECES;
+            int dst;  // in floats
+            if (KV_BF16)
+                dst = (b * kChunk + j) * ROWF + many_pos_bf16(pc >> 1, pc & 1) / 4;
+            else
+                dst = (b * kChunk + j) * ROWF + many_pos(pc / 4, pc % 4);
+            const long src = ((long)(j0 + j) * PIECES + pc) * 16;  // bytes
+            cp_async16(ks + dst, kb + src);
+            cp_async16(vs + dst, vb + src);
         }
         cp_async_commit();
     };
@@ -490,8 +524,23 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
             const int j = t * kLanes + lane;
             s[0][t] = s[1][t] = -INFINITY;
             if (j < n) {
-                const float *kr = ks + (b * kChunk + j) * kManyRow;
+                const float *kr = ks + (b * kChunk + j) * ROWF;
                 float d[2][4] = {};
+                if (KV_BF16) {
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        float kv[8];
+                        widen8(*reinterpret_cast<const uint4 *>(
+                                   reinterpret_cast<const char *>(kr) + many_pos_bf16(h, hf)),
+                               kv);
+#pragma unroll
+                        for (int t = 0; t < 8; t++)
+#pragma unroll
+                            for (int u = 0; u < 2; u++)
+                                d[u][t & 3] = fmaf(q[u][8 * hf + t], kv[t], d[u][t & 3]);
+                    }
+                }
+                else
 #pragma unroll
                 for (int cc = 0; cc < kManyC / 4; cc++) {
                     const float4 k4 = *reinterpret_cast<const float4 *>(kr + many_pos(h, cc));
@@ -536,7 +585,22 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
             for (int t = 0; t < KT; t++) {
                 const int j = t * kLanes + lane;
                 if (j < n) {
-                    const float *vr = vs + (b * kChunk + j) * kManyRow;
+                    const float *vr = vs + (b * kChunk + j) * ROWF;
+                    if (KV_BF16) {
+#pragma unroll
+                        for (int hf = 0; hf < 2; hf++) {
+                            float vv[8];
+                            widen8(*reinterpret_cast<const uint4 *>(
+                                       reinterpret_cast<const char *>(vr) + many_pos_bf16(h, hf)),
+                                   vv);
+#pragma unroll
+                            for (int ci = 0; ci < 8; ci++)
+#pragma unroll
+                                for (int u = 0; u < 2; u++)
+                                    o[u][8 * hf + ci] = fmaf(e[u][t], vv[ci], o[u][8 * hf + ci]);
+                        }
+                    }
+                    else
 #pragma unroll
                     for (int cc = 0; cc < kManyC / 4; cc++) {
                         const float4 v4 = *reinterpret_cast<const float4 *>(vr + many_pos(h, cc));
@@ -682,6 +746,33 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
     return (int)cudaGetLastError();
 }
 
+template <bool KV_BF16>
+int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp, long sk,
+                const void *vp, long sv, float *o, void *ws, size_t ws_bytes, float scale,
+                int num_sms, cudaStream_t st)
+{
+    const int nsplit = many_splits(P, Nk, num_sms);
+    const size_t need =
+        (size_t)P * nsplit * Nq * kHeads * kPart * sizeof(float);
+    if (!ws || ws_bytes < need)
+        return K_EARG;
+    const int smem = KV_BF16 ? kManySmem / 2 : kManySmem;
+    cudaError_t e = smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
+    if (e != cudaSuccess)
+        return (int)e;
+    const int per = ((Nk + nsplit - 1) / nsplit + kChunk - 1) / kChunk * kChunk;
+    dim3 grid(nsplit, P, (Nq + 7) / 8);
+    mha_many_split_kernel<KV_BF16><<<grid, 256, smem, st>>>(
+        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), Nq, Nk, per, scale);
+    e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return (int)e;
+    const long total = (long)P * Nq * kHeads;
+    mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
+        static_cast<const float *>(ws), o, P, Nq, nsplit);
+    return (int)cudaGetLastError();
+}
+
 }  // namespace
 }  // namespace sam3
 
@@ -709,23 +800,8 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         // The reference rejects the same shape (sam3_model.c:429-430).
         if (c != kManyC)
             return K_EARG;
-        const int nsplit = many_splits(P, Nk, num_sms);
-        if (!ws || ws_bytes < k_mha_workspace(P, Nq, Nk, dint, num_sms))
-            return K_EARG;
-        cudaError_t e = smem_limit_once<mha_many_split_kernel>(kManySmem);
-        if (e != cudaSuccess)
-            return (int)e;
-        const int per = ((Nk + nsplit - 1) / nsplit + kChunk - 1) / kChunk * kChunk;
-        dim3 grid(nsplit, P, (Nq + 7) / 8);
-        mha_many_split_kernel<<<grid, 256, kManySmem, st>>>(
-            qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), Nq, Nk, per, scale);
-        e = cudaGetLastError();
-        if (e != cudaSuccess)
-            return (int)e;
-        const long total = (long)P * Nq * kHeads;
-        mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
-            static_cast<const float *>(ws), o, P, Nq, nsplit);
-        return (int)cudaGetLastError();
+        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes, scale,
+                                  num_sms, st);
     }
     if (c == 16)
         return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
@@ -744,4 +820,17 @@ extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, co
         return K_EARG;
     return launch_few2<true, true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f), num_sms,
                              reinterpret_cast<cudaStream_t>(s));
+}
+
+extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
+                                long sk, const void *vp, long sv, float *o, void *ws,
+                                size_t ws_bytes, int num_sms, k_stream s)
+{
+    using namespace sam3;
+    if (P <= 0 || Nq <= 0 || Nk <= 64 || P > 65535 || ((uintptr_t)qp & 15) ||
+        ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
+        (sk & 7) || (sv & 7))
+        return K_EARG;
+    return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes,
+                             1.0f / sqrtf((float)kManyC), num_sms, STREAM(s));
 }

@@ -357,6 +357,21 @@ static int lin16(cb_decoder *d, const char *name, const void *Xb, long rows, int
     return CB_OK;
 }
 
+/* Y bf16 [rows, out] = X W^T + bias, for outputs read only by an attention
+ * kernel that takes bf16. */
+static int lin16h(cb_decoder *d, const char *name, const void *Xb, long rows, int in, int out,
+                  int wi, int bi, void *Y)
+{
+    cb_backend *b = d->b;
+    const double dr = (double)rows;
+
+    LAUNCH(name, 2.0 * dr * in * out, dr * in * 2 + (double)in * out * 2 + dr * out * 2,
+           k_gemm_bf16_tc((int)rows, out, in, Xb, in, d->w[wi], in, Y, out, 1,
+                          (const float *)d->w[bi], NULL, out, 0, 1.0f, K_ACT_NONE, NULL,
+                          b->d_err, b->num_sms, (k_stream)b->stream));
+    return CB_OK;
+}
+
 /* The same on an fp32 X of the image stream, rounded to bf16 into xs
  * first. */
 static int lin32(cb_decoder *d, const char *name, const float *X, void *xs, long rows, int in,
@@ -431,6 +446,19 @@ static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, l
     return CB_OK;
 }
 
+/* Token -> image attention of the P prompts' queries sq on bf16 keys and
+ * values (row strides in elements; 0: shared by all prompts) into so. */
+static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, long sv)
+{
+    cb_backend *b = d->b;
+
+    LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,
+           4.0 * (double)P * DEC_NTOK * 128 * 2 + 2.0 * (sk ? (double)P : 1.0) * DEC_T * 128 * 2,
+           k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so,
+                            d->mha_ws, d->mha_ws_bytes, b->num_sms, (k_stream)b->stream));
+    return CB_OK;
+}
+
 #define ATT(blk, t) (SAM3_DT_ATTN + 8 * (blk) + (t))
 #define LAY(l, t) (SAM3_DT_LAYER + 12 * (l) + (t))
 enum { QW = 0, QB, KW, KB, VW, VB, OW, OB };
@@ -462,10 +490,15 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_
     CB_TRY(add(d, d->src, (const float *)emb->ptr, (const float *)d->w[SAM3_DT_NO_MASK],
                (long)T * DEC_DIM, DEC_DIM));
     CB_TRY(add(d, d->srcpe, d->src, d->pe_img, (long)T * DEC_DIM, (long)T * DEC_DIM));
-    CB_TRY(lin32(d, "dec_gemm_img", d->srcpe, d->kin_bf16, (long)T, DEC_DIM, 128,
-                 ATT(SAM3_DA_L0_T2I, KW), ATT(SAM3_DA_L0_T2I, KB), d->kp0, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin32(d, "dec_gemm_img", d->src, d->kin_bf16, (long)T, DEC_DIM, 128,
-                 ATT(SAM3_DA_L0_T2I, VW), ATT(SAM3_DA_L0_T2I, VB), d->vp0, NULL, 0, K_ACT_NONE));
+    /* kp0 / vp0 are read only by the token -> image attention, as bf16 */
+    LAUNCH("dec_cast", 0, (double)T * DEC_DIM * 6,
+           k_cast_f32_bf16(d->srcpe, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));
+    CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, (long)T, DEC_DIM, 128,
+                  ATT(SAM3_DA_L0_T2I, KW), ATT(SAM3_DA_L0_T2I, KB), d->kp0));
+    LAUNCH("dec_cast", 0, (double)T * DEC_DIM * 6,
+           k_cast_f32_bf16(d->src, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));
+    CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, (long)T, DEC_DIM, 128,
+                  ATT(SAM3_DA_L0_T2I, VW), ATT(SAM3_DA_L0_T2I, VB), d->vp0));
     /* qp0 is read only by the image -> token attention, as bf16 */
     LAUNCH("dec_cast", 0, (double)T * DEC_DIM * 6,
            k_cast_f32_bf16(d->srcpe, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));
@@ -493,12 +526,11 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
     CB_TRY(add_tok_pe(d, nt));
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                   K_ACT_NONE));
-    CB_TRY(lin16(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
-                 d->bk, NULL, 0, K_ACT_NONE));
-    CB_TRY(lin16(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
-                 ATT(blk, VB), d->bv, NULL, 0, K_ACT_NONE));
-    CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->bk, (long)DEC_T * 128, d->bv,
-               (long)DEC_T * 128, d->so));
+    CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
+                  d->bk));
+    CB_TRY(lin16h(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
+                  ATT(blk, VB), d->bv));
+    CB_TRY(mha_t2i(d, P, d->bk, (long)DEC_T * 128, d->bv, (long)DEC_T * 128));
     return lintok(d, d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, 1, K_ACT_NONE);
 }
 
@@ -657,7 +689,7 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     CB_TRY(add_tok_pe(d, nt));
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
                   ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
-    CB_TRY(mha(d, P, DEC_NTOK, DEC_T, 128, d->sq, DEC_NTOK * 128, d->kp0, 0, d->vp0, 0, d->so));
+    CB_TRY(mha_t2i(d, P, d->kp0, 0, d->vp0, 0));
     CB_TRY(lintok(d, d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
                   ATT(SAM3_DA_L0_T2I, OB), d->qry, 1, K_ACT_NONE));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N2W), LAY(0, N2B), DEC_EPS, K_ACT_NONE));
