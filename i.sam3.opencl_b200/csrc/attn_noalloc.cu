@@ -26,9 +26,18 @@ namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[SAM3_NOALLOC_SCRATCH_BYTES];
 static __device__ __align__(256) int g_noalloc_err;
 
-// Device addresses of the two variables, per device ordinal (0 = not set up).
+// Device addresses of the two variables, per device ordinal (null = not set
+// up). Read and written with atomic loads / stores, so two host threads
+// making their first call on one device at the same time both look the
+// addresses up (the same values) without a data race. Never invalidated: a
+// cudaDeviceReset leaves them stale (documented in sam3_cuda.h).
 static void *g_scratch_addr[SAM3_NOALLOC_MAX_DEVICES];
 static void *g_err_addr[SAM3_NOALLOC_MAX_DEVICES];
+
+void *load_addr(void *const *slot)
+{
+    return __atomic_load_n(slot, __ATOMIC_ACQUIRE);
+}
 
 int status_of(cudaError_t e)
 {
@@ -46,7 +55,7 @@ int status_of_launch(int rc)
 // current device (first call on each device only).
 int setup_current_device(int dev)
 {
-    if (g_scratch_addr[dev] && g_err_addr[dev])
+    if (load_addr(&g_scratch_addr[dev]) && load_addr(&g_err_addr[dev]))
         return CB_OK;
     void *s = nullptr, *e = nullptr;
     cudaError_t rc = cudaGetSymbolAddress(&s, g_noalloc_scratch);
@@ -55,8 +64,8 @@ int setup_current_device(int dev)
     rc = cudaGetSymbolAddress(&e, g_noalloc_err);
     if (rc != cudaSuccess)
         return CB_ECUDA;
-    g_err_addr[dev] = e;
-    g_scratch_addr[dev] = s;
+    __atomic_store_n(&g_err_addr[dev], e, __ATOMIC_RELEASE);
+    __atomic_store_n(&g_scratch_addr[dev], s, __ATOMIC_RELEASE);
     return CB_OK;
 }
 
@@ -84,13 +93,13 @@ extern "C" int cb_attention_noalloc(const float *qkv, int nseq, int N, int E, in
     if (!errp) {
         // The library's own error word keeps the previous call's value:
         // clear it first.
-        errp = static_cast<int *>(g_err_addr[dev]);
+        errp = static_cast<int *>(load_addr(&g_err_addr[dev]));
         int rc = status_of(cudaMemsetAsync(errp, 0, sizeof(int),
                                            reinterpret_cast<cudaStream_t>(stream)));
         if (rc != CB_OK)
             return rc;
     }
-    void *scratch = g_scratch_addr[dev];
+    void *scratch = load_addr(&g_scratch_addr[dev]);
     int rc = cs ? k_rope_cast_bf16(qkv, (long)rows, E, hd, npos, cs, scratch, s)
                 : k_cast_f32_bf16(qkv, scratch, (long)rows * 3 * E, s);
     if (rc != 0)

@@ -193,12 +193,16 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
  * stages it in a fixed 32 MiB array compiled into the library instead, and
  * calls no cudaMalloc, cudaFree or allocating routine.
  *
- * Plain device pointers, no backend: qkv [nseq * N, 3E] fp32, cs (cos, sin)
- * table [npos, 32] fp32 or NULL (no RoPE), out [nseq * N, E] fp32, stream a
- * cudaStream_t (NULL = default stream); runs on the current device and is
- * asynchronous on `stream`. err: a caller-owned device int, zeroed by the
- * caller, that receives CB_ETIMEOUT-style device codes (nonzero = a kernel
- * wait ran out); NULL uses a word inside the library, cleared on each call.
+ * Plain device pointers, no backend: qkv [nseq * N, 3E] fp32, cs the RoPE
+ * table of (cos, sin) pairs, [npos, 32] float2 = npos * 64 fp32, or NULL (no
+ * RoPE), out [nseq * N, E] fp32, stream a cudaStream_t (NULL = default
+ * stream); runs on the current device and is asynchronous on `stream`.
+ * err: a caller-owned device int, zeroed by the caller, that receives
+ * CB_ETIMEOUT-style device codes (nonzero = a kernel wait ran out). With
+ * err == NULL the kernels report into a word inside the library that is
+ * cleared on each call and never read back: a device-side timeout then
+ * cannot be observed (the call still returns CB_OK and out may hold partial
+ * results), so callers that need to see it pass their own err.
  *
  * Limits: hd 64 (E = 64 * heads); nseq * N * 3E * 2 bytes must fit the
  * 32 MiB array (at E = 1024: at most 5461 rows, which covers the 9 x 576
@@ -206,7 +210,9 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
  * CB_EARG before any work is queued.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture. Every call shares the one array, which keeps
+ * before any stream capture. The looked-up address is cached per device
+ * ordinal for the life of the process: after cudaDeviceReset the cache is
+ * stale, so do not call this entry point again on a device that was reset. Every call shares the one array, which keeps
  * the previous call's contents: calls that overlap on the GPU (different
  * streams, or different host threads on one device) race on it. Each GPU
  * that loads the library holds the 32 MiB until the process exits. */

@@ -64,6 +64,32 @@ def test_noalloc_attention_matches_allocating_entry_point(cb, sb):
         assert cos_sim(got, want) >= 0.9999, call
 
 
+def test_noalloc_attention_without_rope_or_error_word(cb, sb):
+    """The other two branches: no RoPE table (plain bf16 cast into the
+    static array) and err == NULL (the library's own error word, cleared by
+    the call itself), two calls in a row."""
+    lib = sb.lib()
+    E, heads, side, nseq = 1024, 16, 24, 2
+    for call, seed in enumerate((303, 404)):
+        N, qkv, _ = _inputs(seed, nseq, side, E)
+        ref_qkv = qkv.clone()
+        out_ref = torch.empty(nseq * N, E, device="cuda")
+        out = torch.full((nseq * N, E), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        cb.attention(cb.wrap(ref_qkv), nseq, N, E, heads, 64, None, N, 0.125,
+                     sb.ATTN_TC, cb.wrap(out_ref))
+        rc = lib.cb_attention_noalloc(C.c_void_p(qkv.data_ptr()), nseq, N, E, heads, None, 0,
+                                      0.125, C.c_void_p(out.data_ptr()), None,
+                                      C.c_void_p(cb.stream))
+        assert rc == 0, lib.cb_errstr(rc)
+        cb.sync()
+        torch.cuda.synchronize()
+        got, want = out.cpu().numpy(), out_ref.cpu().numpy()
+        assert np.isfinite(got).all(), f"call {call}: output not fully written"
+        assert np.abs(got - want).max() <= 1e-2, call
+        assert cos_sim(got, want) >= 0.9999, call
+
+
 def test_noalloc_attention_rejects_oversized_input(cb, sb):
     lib = sb.lib()
     E, heads = 1024, 16
