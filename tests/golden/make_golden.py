@@ -7,7 +7,7 @@ unmodified as host C++ by oracle/Makefile (oracle/_ref/libsam3ref.so), on
 inputs drawn from the seeded generator (include/sam3_synth.h). Only the
 outputs are stored; tests regenerate the inputs from the seeds.
 
-    make -C oracle && python tests/golden/make_golden.py [case names]
+    make -C oracle ref REF=<reference tree> && python tests/golden/make_golden.py [case names]
 
 Launch geometry is the reference host code's: layernorm with 256-item
 work-groups for rows of >= 1024 channels (sam3_model.c:320), softmax_rows
