@@ -34,13 +34,17 @@
 // one thread run in issue order): the scores of the next KV tile are always
 // ready when the softmax finishes one.
 //
-// Softmax per KV tile, one pass: the row's 96 scores in one TMEM round trip;
-// row maximum with three-input max; x = s * scale * log2 e - m in packed
-// fp32; 2^x on the MUFU unit, 1/8 of the values on the FMA pipe
-// (exp2_poly2); row sums in packed fp32; P packed to bf16 pairs. The running
-// maximum is only raised (and O and the sums rescaled by 2^(m_old - m_new))
-// when a tile's maximum exceeds it by more than 8 in log2 units, so P stays
-// <= 2^8 and most tiles skip the rescale; the final division by the row sum
+// Softmax per KV tile, one pass: the row's 96 scores in one TMEM round
+// trip; x = s * scale * log2 e - m in packed fp32; 2^x on the MUFU unit, 2
+// of 8 pairs on the FMA pipe (exp2_poly2); tile sums in packed fp32; P
+// packed to bf16 pairs. The offset m is the row maximum of the item's first
+// KV tile and is kept for the following tiles without taking their maxima
+// (a dependent 48-step chain per tile): P may then exceed 1, which bf16 and
+// the fp32 sums carry without loss. A tile whose row sum reaches 2^13 (a
+// score that far above the offset, or an inf) is taken again: its scores
+// are reloaded from TMEM (P is only written back afterwards), m is raised to
+// the tile maximum and O and the sums are rescaled by 2^(m_old - m_new)
+// once the previous P.V has finished. The final division by the row sum
 // makes the result independent of the offset used.
 #include "kernels.h"
 #include "tc_ptx.cuh"
@@ -62,8 +66,10 @@ constexpr int kCtasPerSm = 2;
 // Of every 8 pairs of scores, this many take the FMA-pipe exponential
 // (exp2_poly2) instead of two MUFU instructions: the MUFU unit runs 16
 // exponentials per clock per SM against 256 MMA flops per score.
-constexpr int kPolyPairsPer16 = 1;
-constexpr float kRescaleThreshold = 8.0f;
+constexpr int kPolyPairsPer8 = 2;
+// A row's tile sum at or above this (some P >= 2^13, or inf / NaN) sends
+// the tile through the maximum pass again with a raised offset.
+constexpr float kOverflowSum = 8192.0f;
 constexpr int Q_BYTES = BQ * HD * 2;
 constexpr int KV_BYTES = BKV * HD * 2;
 constexpr int OFF_Q = 0;                       // [buffer], one query tile each
@@ -304,42 +310,73 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                             if (e >= valid)
                                 s[e] = __float_as_uint(-INFINITY);
                     }
-                    float mx0 = -INFINITY, mx1 = -INFINITY;
+                    // Pass 0 takes the exponentials against the running
+                    // offset m_used, which only the item's first tile sets
+                    // from its maximum. If a value reached 2^13 (tile sum
+                    // check), pass 1 reloads the scores, raises m_used to
+                    // the tile maximum and takes them again.
+                    uint64_t t0, t1;
+#pragma unroll 1
+                    for (int pass = 0;; pass++) {
+                        if (m_used == -INFINITY || pass == 1) {
+                            float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-                    for (int e = 0; e < BKV; e += 4) {
-                        mx0 = max3f(mx0, __uint_as_float(s[e]), __uint_as_float(s[e + 1]));
-                        mx1 = max3f(mx1, __uint_as_float(s[e + 2]), __uint_as_float(s[e + 3]));
-                    }
-                    const float m_tile = fmaxf(mx0, mx1) * sl2;
-                    if (m_used == -INFINITY)
-                        m_used = m_tile;
-                    else if (m_tile > m_used + kRescaleThreshold) {
-                        resc = true;
-                        factor = ex2_approx(m_used - m_tile);
-                        m_used = m_tile;
-                        lsum0 = mul2(lsum0, f2_make(factor, factor));
-                        lsum1 = mul2(lsum1, f2_make(factor, factor));
-                    }
-                    const uint64_t negm = f2_make(-m_used, -m_used);
-#pragma unroll
-                    for (int e = 0; e < BKV; e += 2) {
-                        const uint64_t x2 = fma2(f2_make(__uint_as_float(s[e]),
-                                                         __uint_as_float(s[e + 1])),
-                                                 sl2x2, negm);
-                        float x0, x1, p0, p1;
-                        f2_split(x2, x0, x1);
-                        if (((e >> 1) & 7) >= 8 - kPolyPairsPer16)
-                            exp2_poly2(x0, x1, p0, p1);
-                        else {
-                            p0 = ex2_approx(x0);
-                            p1 = ex2_approx(x1);
+                            for (int e = 0; e < BKV; e += 4) {
+                                mx0 = max3f(mx0, __uint_as_float(s[e]), __uint_as_float(s[e + 1]));
+                                mx1 = max3f(mx1, __uint_as_float(s[e + 2]), __uint_as_float(s[e + 3]));
+                            }
+                            const float m_tile = fmaxf(mx0, mx1) * sl2;
+                            if (m_used == -INFINITY)
+                                m_used = m_tile;
+                            else if (m_tile > m_used) {
+                                resc = true;
+                                factor = ex2_approx(m_used - m_tile);
+                                m_used = m_tile;
+                                lsum0 = mul2(lsum0, f2_make(factor, factor));
+                                lsum1 = mul2(lsum1, f2_make(factor, factor));
+                            }
                         }
-                        if ((e >> 1) & 1)
-                            lsum1 = add2(lsum1, f2_make(p0, p1));
-                        else
-                            lsum0 = add2(lsum0, f2_make(p0, p1));
-                        s[e >> 1] = pack_bf16x2(p0, p1);
+                        const uint64_t negm = f2_make(-m_used, -m_used);
+                        t0 = 0;
+                        t1 = 0;
+#pragma unroll
+                        for (int e = 0; e < BKV; e += 2) {
+                            const uint64_t x2 = fma2(f2_make(__uint_as_float(s[e]),
+                                                             __uint_as_float(s[e + 1])),
+                                                     sl2x2, negm);
+                            float x0, x1, p0, p1;
+                            f2_split(x2, x0, x1);
+                            if (((e >> 1) & 7) >= 8 - kPolyPairsPer8)
+                                exp2_poly2(x0, x1, p0, p1);
+                            else {
+                                p0 = ex2_approx(x0);
+                                p1 = ex2_approx(x1);
+                            }
+                            if ((e >> 1) & 1)
+                                t1 = add2(t1, f2_make(p0, p1));
+                            else
+                                t0 = add2(t0, f2_make(p0, p1));
+                            s[e >> 1] = pack_bf16x2(p0, p1);
+                        }
+                        float u0, u1, u2, u3;
+                        f2_split(t0, u0, u1);
+                        f2_split(t1, u2, u3);
+                        const bool over = !(((u0 + u1) + (u2 + u3)) < kOverflowSum);
+                        if (pass == 1 || !__any_sync(0xffffffffu, over))
+                            break;
+#pragma unroll
+                        for (int c = 0; c < BKV / 32; c++)
+                            tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
+                        tmem_wait_ld();
+                        if (valid < BKV) {
+#pragma unroll
+                            for (int e = 0; e < BKV; e++)
+                                if (e >= valid)
+                                    s[e] = __float_as_uint(-INFINITY);
+                        }
                     }
+                    lsum0 = add2(lsum0, t0);
+                    lsum1 = add2(lsum1, t1);
                     tmem_st32(tS, *reinterpret_cast<const uint32_t(*)[32]>(s));
                     tmem_st16(tS + 32, *reinterpret_cast<const uint32_t(*)[16]>(s + 32));
                 }

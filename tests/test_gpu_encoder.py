@@ -128,3 +128,87 @@ def test_encoder_full_backbone_vs_golden(cb, sb):
     assert c >= 0.999, c
     assert abs(float(got.std()) - float(g["std"])) < 0.01 * float(g["std"])
     enc.close()
+
+
+def _load_checkpoint(enc, w):
+    """Push every tensor of oracle TrunkWeights through cb_encoder_set_weight
+    in the checkpoint's shapes, as a loader following load_encoder
+    (sam3_model.c:473-581) would."""
+    E, p = w.E, w.patch
+    enc.set_weight("PATCH_W", 0, w.pe_w.reshape(E, 3, p, p))
+    enc.set_weight("POS", 0, w.pos)  # [grid^2, E], raster order
+    enc.set_weight("LN_PRE_W", 0, w.lnpw)
+    enc.set_weight("LN_PRE_B", 0, w.lnpb)
+    enc.set_weight("ROPE_WIN", 0, w.rope_win.reshape(w.window * w.window, w.hd // 2, 2))
+    enc.set_weight("ROPE_GLOB", 0, w.rope_glob.reshape(w.grid * w.grid, w.hd // 2, 2))
+    for i, b in enumerate(w.blocks):
+        for name, key in (("N1_W", "n1w"), ("N1_B", "n1b"), ("QKV_W", "qkvw"),
+                          ("QKV_B", "qkvb"), ("PROJ_W", "projw"), ("PROJ_B", "projb"),
+                          ("N2_W", "n2w"), ("N2_B", "n2b"), ("FC1_W", "l1w"),
+                          ("FC1_B", "l1b"), ("FC2_W", "l2w"), ("FC2_B", "l2b")):
+            enc.set_weight(name, i, b[key])
+
+
+def test_encoder_set_weight_equals_init_random(cb, sb, ob):
+    """Loading every tensor from host fp32 data in checkpoint shapes (the
+    loader's path: patch weight padded to the GEMM's K, pos_embed permuted
+    to window-major rows, RoPE tables, every block tensor) gives, bit for
+    bit, the encode of the device-side random init."""
+    seed = 17
+    img = ob.u8(seed, image_stream(0), (1008, 1008, 3))
+    tiles = cb.upload(img, sb.U8)
+    outs = []
+    for loaded in (False, True):
+        enc = sb.Encoder(cb, max_tiles=1, depth=2, global_blocks=(1,))
+        if loaded:
+            _load_checkpoint(enc, ob.TrunkWeights(seed, depth=2, global_blocks=(1,)))
+        else:
+            enc.init_random(seed)
+        out = cb.alloc(5184 * 1024 * 4, sb.F32)
+        enc.encode_tiles(tiles, 1, out)
+        got = np.empty((5184, 1024), np.float32)
+        cb.read(out, got)
+        cb.sync()
+        outs.append(got)
+        enc.close()
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_encoder_pos_embed_tiled_from_pretrain_grid_vs_oracle(cb, sb, ob):
+    """A pos_embed with visible structure: a 24 x 24 pretraining grid (plus
+    the class token that SAM 3 drops) tiled over the 72 x 72 grid as
+    tile_abs_pos does (sam3_model.c:492-498), loaded through set_weight and
+    compared with the oracle, which adds it in raster order. A wrong
+    raster -> window-major permutation of POS fails this test, whereas the
+    init_random comparison above would not see it (both paths permute)."""
+    seed = 18
+    w = ob.TrunkWeights(seed, depth=2, global_blocks=(1,))
+    pt = 24
+    pe = ob.normal(seed, 77, (1 + pt * pt, w.E), 0.0, 0.5)
+    i = np.arange(w.grid * w.grid)
+    y, x = i // w.grid % pt, i % w.grid % pt
+    w.pos = np.ascontiguousarray(pe[1 + y * pt + x])
+    enc = sb.Encoder(cb, max_tiles=1, depth=2, global_blocks=(1,))
+    _load_checkpoint(enc, w)
+    img = ob.u8(seed, image_stream(0), (1008, 1008, 3))
+    tiles = cb.upload(img, sb.U8)
+    out = cb.alloc(5184 * 1024 * 4, sb.F32)
+    enc.encode_tiles(tiles, 1, out)
+    got = np.empty((5184, 1024), np.float32)
+    cb.read(out, got)
+    cb.sync()
+    want = ob.encode_trunk(w, ob.image_input(img))
+    c = cos_sim(got, want)
+    assert c >= 0.999, c
+    assert np.abs(got - want).max() < 0.1 * np.abs(want).max()
+    enc.close()
+
+
+def test_encoder_set_weight_rejects_wrong_shapes(cb, sb):
+    enc = sb.Encoder(cb, max_tiles=1, depth=2, global_blocks=(1,))
+    for which, block, n in (("PATCH_W", 0, 1024 * 588 - 1), ("POS", 0, 5184 * 1024 + 1),
+                            ("ROPE_WIN", 0, 576 * 32), ("QKV_W", 0, 10), ("FC1_B", 1, 1024),
+                            ("N1_W", 2, 1024)):
+        with pytest.raises(sb.CBError):
+            enc.set_weight(which, block, np.zeros(n, np.float32))
+    enc.close()

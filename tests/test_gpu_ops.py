@@ -227,6 +227,36 @@ def test_attention_tc_bf16_qkv_vs_oracle(cb, sb, ob, side, nseq):
     assert cos_sim(got, want) >= 0.9999
 
 
+@pytest.mark.parametrize("side,nseq", [(24, 3), (72, 1), (13, 2)])
+def test_attention_tc_score_jumps_vs_oracle(cb, sb, ob, side, nseq):
+    """Scores that rise far above the offset the kernel takes from a row's
+    first KV tile: the keys after the first third of each sequence are
+    scaled by 5, so later tiles reach P >> 2^13 against that offset and the
+    kernel must retake them with a raised offset and rescale the running
+    output and sums. The softmax is then peaked, the output close to single
+    V rows (|O| up to ~4 instead of ~0.1), and the bf16 rounding of P
+    scales with it: the max-abs bound of the other attention tests is taken
+    relative to the output's magnitude (the kernel without the offset scheme
+    had the same 1.3-1.7e-2 absolute error here); cosine as before."""
+    E = 1024
+    N, qkv, cs, roped = _attn_case(ob, side, nseq, E, stream=24)
+    roped = roped.reshape(nseq, N, 3 * E).copy()
+    roped[:, N // 3:, E:2 * E] *= 5.0
+    roped = roped.reshape(nseq * N, 3 * E)
+    bits = _bf16_bits(roped)
+    exact = (bits.astype(np.uint32) << 16).view(np.float32)  # the inputs the kernel sees
+    want = ob.attention(exact, nseq, N, E, 16, 64, 0.125)
+    mq = cb.upload(bits, sb.BF16)
+    mo = cb.alloc(nseq * N * E * 4, sb.F32)
+    cb.attention(mq, nseq, N, E, 16, 64, None, N, 0.125, sb.ATTN_TC, mo)
+    got = np.empty((nseq * N, E), np.float32)
+    cb.read(mo, got)
+    cb.sync()
+    assert np.isfinite(got).all()
+    assert np.abs(got - want).max() <= 1e-2 * max(1.0, float(np.abs(want).max()))
+    assert cos_sim(got, want) >= 0.9999
+
+
 def test_attention_tc_global_vs_oracle(cb, sb, ob):
     """Config 2: global attention over the 72 x 72 grid, 16 heads."""
     E = 1024
