@@ -574,15 +574,17 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last)
                       "encode_blocks");
 }
 
-/* Chunk of the host-buffer pipeline: about a quarter of a large batch (so
- * that the copies of neighbouring chunks hide behind the compute), at least
- * 8 tiles (GEMM tails stay small), at most max_tiles. */
+/* Chunk of the host-buffer pipeline: about a quarter of the batch, so that
+ * the copies in and out of neighbouring chunks hide behind the compute and
+ * only the first chunk's upload and the last chunk's download stay exposed
+ * (with 8 tiles per GPU, 2-tile chunks), at least 2 tiles (one tile per
+ * GEMM would leave long wave tails), at most max_tiles. */
 static int host_chunk(const cb_encoder *e, int ntile)
 {
     int c = (ntile + 3) / 4;
 
-    if (c < 8)
-        c = ntile < 8 ? ntile : 8;
+    if (c < 2)
+        c = ntile < 2 ? ntile : 2;
     return c > e->cfg.max_tiles ? e->cfg.max_tiles : c;
 }
 
