@@ -715,7 +715,9 @@ def profile_part(part):
     """Small cases of the parts beyond the backbone for ncu captures, each
     run twice (the second run is the one to capture): `decoder` = cb_decode
     of 16 prompts, `neck` = cb_neck_run on 2 tiles, `detector` = the two
-    cb_attend shapes of the bench, `input` = one 2100 x 1500 crop."""
+    cb_attend shapes of the bench, `input` = one 2100 x 1500 crop,
+    `elementwise` = the backbone's element-wise kernels (patch_embed_in,
+    LayerNorm, the RoPE + bf16 cast of the fp32 attention op)."""
     import torch
     sb = load_product()
     cb = sb.Backend(0)
@@ -750,6 +752,29 @@ def profile_part(part):
     elif part == "input":
         for _ in range(2):
             input_bench(sb, cb, torch, iters=1)
+    elif part == "elementwise":
+        # the element-wise kernels on inputs larger than L2: 4 tiles through a
+        # 1-block trunk (patch_embed_in, ln_pre and the two block LayerNorms
+        # on 20736 x 1024 rows), then config 2's fp32 attention op, whose
+        # RoPE + bf16 cast pass (rope_cast) reads the 64 MB fp32 qkv
+        enc = sb.Encoder(cb, max_tiles=4, depth=1, global_blocks=(0,))
+        enc.init_random(SEED)
+        tiles = torch.empty(4, SIDE, SIDE, 3, dtype=torch.uint8)
+        for i in range(4):
+            sb.lib().sam3_synth_u8(SEED, image_stream(i), SIDE * SIDE * 3, tiles[i].data_ptr())
+        dev = tiles.cuda()
+        out = torch.empty(4, T, 1024, device="cuda")
+        qkv = torch.randn(T, 3 * 1024, device="cuda")
+        cs = torch.empty(T * 64, dtype=torch.float32)
+        sb.lib().sam3_synth_rope_axial(72, 64, 10000.0, cs.data_ptr())
+        cs = cs.cuda()
+        o = torch.empty(T, 1024, device="cuda")
+        torch.cuda.synchronize()
+        for _ in range(2):
+            enc.encode_tiles(cb.wrap(dev), 4, cb.wrap(out))
+            cb.attention(cb.wrap(qkv), 1, T, 1024, 16, 64, cb.wrap(cs), T, 0.125, sb.ATTN_TC,
+                         cb.wrap(o))
+        enc.close()
     cb.sync()
     cb.close()
     print(f"profile part done: {part}")
@@ -764,8 +789,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="TILES",
                     help="run the small ncu case on TILES tiles and exit")
-    ap.add_argument("--profile-part", choices=["decoder", "neck", "detector", "input"],
-                    help="run a small case of one part beyond the backbone and exit")
+    ap.add_argument("--profile-part", choices=["decoder", "neck", "detector", "input", "elementwise"],
+                    help="run a small case of one part (beyond the backbone, or its "
+                         "element-wise kernels) and exit")
     args = ap.parse_args()
     if args.profile_part:
         profile_part(args.profile_part)
