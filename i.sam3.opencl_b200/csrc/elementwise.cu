@@ -267,41 +267,67 @@ __global__ void patch_im2col_kernel(const float *img, float *out, int side, int 
 
 // Patch rows straight from uint8 HWC tiles, normalised as
 // image_encoder_input does (image.c:360-366), in window-major token order,
-// bf16, K padded with zeros to kpad. One thread per 8 output columns.
-__global__ void patch_embed_in_kernel(const uint8_t *__restrict__ rgb, int ntile, int side,
-                                      int grid, int ps, int ws, int kpad, __nv_bfloat16 *out)
+// bf16, K padded with zeros to kpad. One CTA per window row of one tile: the
+// ws patches of the row come from ps image rows of ws * ps * 3 contiguous
+// bytes, staged in shared memory with 16-byte loads (byte loads when the
+// rows are not 16-byte aligned); a table maps each patch column (channel,
+// ky, kx) to its byte in the staged rows, and each thread then writes 8
+// output columns of one token with one 16-byte store.
+__global__ void __launch_bounds__(256) patch_embed_in_kernel(const uint8_t *__restrict__ rgb,
+                                                             int side, int grid, int ps, int ws,
+                                                             int kpad, __nv_bfloat16 *out)
 {
-    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const int groups = kpad / 8;
-    const long T = (long)grid * grid;
-    if (gid >= ntile * T * groups)
-        return;
-    const long row = gid / groups;
-    const int g0 = (int)(gid % groups) * 8;
-    const int tile = (int)(row / T), r = (int)(row % T);
-    const int nwx = grid / ws, w2 = ws * ws;
-    const int w = r / w2, i = r % w2;
-    const int ty = (w / nwx) * ws + i / ws, tx = (w % nwx) * ws + i % ws;
+    extern __shared__ uint8_t patch_smem[];
+    const int rowbytes = ws * ps * 3;
     const int K = 3 * ps * ps;
-    const uint8_t *src = rgb + (long)tile * side * side * 3;
-    float v[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-        const int col = g0 + e;
-        float f = 0.0f;
-        if (col < K) {
-            const int c = col / (ps * ps), ky = (col % (ps * ps)) / ps, kx = col % ps;
-            const uint8_t u = src[((long)(ty * ps + ky) * side + tx * ps + kx) * 3 + c];
-            f = ((float)u / 255.0f - 0.5f) / 0.5f;
-        }
-        v[e] = f;
+    int *coloff = reinterpret_cast<int *>(patch_smem);
+    uint8_t *st = patch_smem + (((size_t)K * 4 + 15) & ~(size_t)15);
+    const int nwx = grid / ws, nwin = nwx * nwx;
+    int bid = (int)blockIdx.x;
+    const int iy = bid % ws;
+    bid /= ws;
+    const int w = bid % nwin, tile = bid / nwin;
+    const int ty = (w / nwx) * ws + iy, tx0 = (w % nwx) * ws;
+    const uint8_t *src = rgb + ((long)tile * side * side + (long)ty * ps * side + (long)tx0 * ps) * 3;
+    const long pitch = (long)side * 3;
+    for (int col = threadIdx.x; col < K; col += blockDim.x) {
+        const int c = col / (ps * ps), rem = col - c * ps * ps;
+        const int ky = rem / ps, kx = rem - ky * ps;
+        coloff[col] = ky * rowbytes + kx * 3 + c;
     }
-    uint4 p;
-    p.x = pack_bf16x2(v[0], v[1]);
-    p.y = pack_bf16x2(v[2], v[3]);
-    p.z = pack_bf16x2(v[4], v[5]);
-    p.w = pack_bf16x2(v[6], v[7]);
-    *reinterpret_cast<uint4 *>(out + row * kpad + g0) = p;
+    if (!(((uintptr_t)src | (uintptr_t)pitch | (uintptr_t)rowbytes) & 15)) {
+        const int n16 = rowbytes / 16;
+        for (int i = threadIdx.x; i < ps * n16; i += blockDim.x) {
+            const int r = i / n16, c16 = i - r * n16;
+            reinterpret_cast<uint4 *>(st)[i] =
+                *reinterpret_cast<const uint4 *>(src + (long)r * pitch + 16 * c16);
+        }
+    }
+    else {
+        for (int i = threadIdx.x; i < ps * rowbytes; i += blockDim.x) {
+            const int r = i / rowbytes;
+            st[i] = src[(long)r * pitch + (i - r * rowbytes)];
+        }
+    }
+    __syncthreads();
+    const int groups = kpad / 8;
+    const long row0 = (long)tile * grid * grid + (long)w * ws * ws + (long)iy * ws;
+    for (int i = threadIdx.x; i < ws * groups; i += blockDim.x) {
+        const int j = i / groups, g0 = (i - j * groups) * 8;
+        const uint8_t *pj = st + j * ps * 3;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int col = g0 + e;
+            v[e] = col < K ? ((float)pj[coloff[col]] / 255.0f - 0.5f) / 0.5f : 0.0f;
+        }
+        uint4 p;
+        p.x = pack_bf16x2(v[0], v[1]);
+        p.y = pack_bf16x2(v[2], v[3]);
+        p.z = pack_bf16x2(v[4], v[5]);
+        p.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4 *>(out + (row0 + j) * kpad + g0) = p;
+    }
 }
 
 // Eight values per thread: two 16-byte loads, one 16-byte store.
@@ -488,11 +514,23 @@ extern "C" int k_patch_im2col(const float *img, float *out, int side, int grid, 
 extern "C" int k_patch_embed_in(const uint8_t *rgb, int ntile, int side, int grid, int ps, int ws,
                                 int kpad, void *out, k_stream s)
 {
-    if (kpad % 8 || kpad < 3 * ps * ps || grid % ws || ((uintptr_t)out & 15))
+    if (kpad % 8 || kpad < 3 * ps * ps || grid % ws || ((uintptr_t)out & 15) || ntile <= 0 ||
+        side < grid * ps)
         return K_EARG;
-    const long n = (long)ntile * grid * grid * (kpad / 8);
-    patch_embed_in_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
-        rgb, ntile, side, grid, ps, ws, kpad, reinterpret_cast<__nv_bfloat16 *>(out));
+    const size_t smem = (((size_t)3 * ps * ps * 4 + 15) & ~(size_t)15) + (size_t)ps * ws * ps * 3;
+    if (smem > 227 * 1024)
+        return K_EARG;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(
+            patch_embed_in_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess)
+            return (int)e;
+    }
+    const long blocks = (long)ntile * (grid / ws) * (grid / ws) * ws;
+    if (blocks > 0x7fffffffL)
+        return K_EARG;
+    patch_embed_in_kernel<<<(unsigned)blocks, 256, smem, STREAM(s)>>>(
+        rgb, side, grid, ps, ws, kpad, reinterpret_cast<__nv_bfloat16 *>(out));
     LAUNCH_RET();
 }
 
