@@ -576,15 +576,16 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last)
 
 /* Chunk of the host-buffer pipeline: about a quarter of the batch, so that
  * the copies in and out of neighbouring chunks hide behind the compute and
- * only the first chunk's upload and the last chunk's download stay exposed
- * (with 8 tiles per GPU, 2-tile chunks), at least 2 tiles (one tile per
- * GEMM would leave long wave tails), at most max_tiles. */
+ * only the first chunk's upload and the last chunk's download stay exposed,
+ * but at least 4 tiles: smaller chunks leave the GEMMs and the attention
+ * with wave tails that cost more than the exposed copies save (with 8 tiles
+ * per GPU, two chunks of 4), at most max_tiles. */
 static int host_chunk(const cb_encoder *e, int ntile)
 {
     int c = (ntile + 3) / 4;
 
-    if (c < 2)
-        c = ntile < 2 ? ntile : 2;
+    if (c < 4)
+        c = ntile < 4 ? ntile : 4;
     return c > e->cfg.max_tiles ? e->cfg.max_tiles : c;
 }
 
