@@ -378,14 +378,17 @@ def input_bench(sb, cb, torch, iters=10):
 
 def detector_attention_bench(sb, cb, torch, pk, iters=10):
     """cb_attend on the detector's two image-sized shapes: the fusion
-    encoder's self-attention (5184 tokens, 8 heads of 32; tensor cores) and
-    the decoder's 201 queries over the image with the box relative position
-    bias (fp32 CUDA cores); synthetic N(0, 1) inputs, device-timed."""
+    encoder's self-attention (5184 tokens, 8 heads of 32) and the decoder's
+    201 queries over the image with the box relative position bias, both on
+    the tensor cores (CB_ATTN_TC; the biased one also in the fp32 mode for
+    comparison); synthetic N(0, 1) inputs, device-timed."""
     stream = torch.cuda.ExternalStream(cb.stream)
     g = torch.Generator(device="cuda").manual_seed(SEED + 5)
     heads, hd, T = 8, 32, 5184
     res = {}
-    for name, nq, rpb in (("fusion_self_5184", T, False), ("decoder_image_rpb_201", 201, True)):
+    for name, nq, rpb, mode in (("fusion_self_5184", T, False, 0),
+                                ("decoder_image_rpb_201", 201, True, 0),
+                                ("decoder_image_rpb_201_fp32_mode", 201, True, 1)):
         q = torch.randn(nq, heads * hd, device="cuda", generator=g)
         k = torch.randn(T, heads * hd, device="cuda", generator=g)
         v = torch.randn(T, heads * hd, device="cuda", generator=g)
@@ -401,7 +404,7 @@ def detector_attention_bench(sb, cb, torch, pk, iters=10):
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             cb.attend(nq, T, heads, hd, w[0], heads * hd, w[1], heads * hd, w[2], heads * hd,
-                      w[3], heads * hd, 0, wb[0], wb[1], 72 if rpb else 0, 0)
+                      w[3], heads * hd, 0, wb[0], wb[1], 72 if rpb else 0, mode)
             e1.record(stream)
             e1.synchronize()
             if it >= 3:
@@ -409,7 +412,9 @@ def detector_attention_bench(sb, cb, torch, pk, iters=10):
         t = statistics.median(times)
         flop = 4.0 * nq * T * hd * heads
         res[name] = {"ms": t, "tflops": flop / (t * 1e-3) / 1e12,
-                     "path": "tcgen05 (bf16)" if not rpb else "CUDA cores (fp32)"}
+                     "path": "CUDA cores (fp32)" if mode else (
+                         "tcgen05 (bf16), box bias as a dense term, keys split over CTAs"
+                         if rpb else "tcgen05 (bf16)")}
     return res
 
 

@@ -7,6 +7,11 @@
 //
 // Input: bf16 qkv rows [nseq * N, 3E] (RoPE already applied to q and k by
 // the QKV GEMM epilogue or by k_rope_cast_bf16), head h at column h*64.
+// k_attn_tc_cross runs the same kernel on separate Q, K and V tensors with
+// Nq query and Nk key rows per sequence (the mask decoder's token-to-image
+// attention with keys shared by all prompts, the detector's queries over the
+// image), optionally with an fp32 bias added to every scaled score (SAM 3's
+// box relative position bias, softmax_ext in sam3_kernels.cl:890-921).
 //
 // Work items are (sequence, head, 128-query tile), query tile fastest so
 // that CTAs running at the same time share a head's K/V in L2. Two CTAs run
@@ -88,17 +93,73 @@ constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;
 static_assert(kCtasPerSm * SMEM_BYTES <= 232448, "two CTAs per SM");
 static_assert(TM_O + HD <= TM_COLS && kCtasPerSm * TM_COLS <= 512, "tensor memory");
 
+// nseq sequences of Nq query rows and Nk key / value rows (Q, K and V rows
+// of sequence s start at s * Nq and s * Nk of their tensor maps; head h at
+// column qcol / kcol / vcol + 64 h); out rows s * Nq + q, leading dimension
+// ldo, head h at column 64 h. bias (BIAS instantiation): fp32 added to the
+// scaled scores, [nseq, heads, Nq, Nk] in log2 units.
+// nsplit > 1 (few query tiles): the KV tiles of each (sequence, head,
+// query tile) are split into nsplit equal ranges of nkv tiles, each a work
+// item that writes its unnormalised output and (offset, sum) per row to
+// part ([item][128 rows][64 + 4] fp32: output, offset, sum, 2 unused, so
+// that every row starts 16-byte aligned); combine_kernel merges them.
 struct AttnArgs {
-    int nseq, N, E, heads, nqt, nitems;
+    int nseq, Nq, Nk, heads, nqt, nitems, nsplit, nkv;
+    int qcol, kcol, vcol;
+    long ldo;
     float scale_log2;
     void *out;
+    const float *bias;
+    float *part;
     int *err;
 };
+constexpr int kPartRow = HD + 4;
+static_assert((kPartRow * 4) % 16 == 0, "partial rows 16-byte aligned");
 
-template <bool OUT_BF16>
+// Scores of one KV tile as loaded from TMEM: keys at or beyond `valid`
+// set to -inf; with BIAS, each score becomes s * scale_log2 + b (b: the
+// row's bias for this tile, null for a row beyond the queries, which is only
+// scaled).
+template <bool BIAS>
+__device__ __forceinline__ void prep_scores(uint32_t (&s)[BKV], int valid, const float *b,
+                                            float scale_log2)
+{
+    if (valid < BKV) {
+#pragma unroll
+        for (int e = 0; e < BKV; e++)
+            if (e >= valid)
+                s[e] = __float_as_uint(-INFINITY);
+    }
+    if (!BIAS)
+        return;
+    if (!b) {
+#pragma unroll
+        for (int e = 0; e < BKV; e++)
+            s[e] = __float_as_uint(__uint_as_float(s[e]) * scale_log2);
+    }
+    else if (valid >= BKV && !(reinterpret_cast<uintptr_t>(b) & 15)) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(b);
+#pragma unroll
+        for (int e = 0; e < BKV; e += 4) {
+            const float4 v = __ldg(b4 + e / 4);
+            s[e] = __float_as_uint(fmaf(__uint_as_float(s[e]), scale_log2, v.x));
+            s[e + 1] = __float_as_uint(fmaf(__uint_as_float(s[e + 1]), scale_log2, v.y));
+            s[e + 2] = __float_as_uint(fmaf(__uint_as_float(s[e + 2]), scale_log2, v.z));
+            s[e + 3] = __float_as_uint(fmaf(__uint_as_float(s[e + 3]), scale_log2, v.w));
+        }
+    }
+    else {
+#pragma unroll
+        for (int e = 0; e < BKV; e++)
+            if (e < valid)
+                s[e] = __float_as_uint(fmaf(__uint_as_float(s[e]), scale_log2, __ldg(b + e)));
+    }
+}
+
+template <bool OUT_BF16, bool BIAS, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                 const AttnArgs a)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -112,16 +173,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nkv = (a.N + BKV - 1) / BKV;
+    const int nkv = a.nkv;
     const int nmine = (int)blockIdx.x < a.nitems
                           ? (a.nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1
                           : 0;
     const int total = nmine * nkv;
-    auto coords = [&](int k, int &seq, int &head, int &qt) {
+    // item = ((seq * heads + head) * nqt + qt) * nsplit + split; its KV
+    // tiles start at j0 = split * nkv
+    auto coords = [&](int k, int &seq, int &head, int &qt, int &j0) {
         const int item = (int)blockIdx.x + k * (int)gridDim.x;
-        qt = item % a.nqt;
-        head = (item / a.nqt) % a.heads;
-        seq = item / (a.nqt * a.heads);
+        j0 = SPLIT ? (item % a.nsplit) * nkv : 0;
+        const int u = SPLIT ? item / a.nsplit : item;
+        qt = u % a.nqt;
+        head = (u / a.nqt) % a.heads;
+        seq = u / (a.nqt * a.heads);
     };
 
     if (threadIdx.x == 0) {
@@ -154,35 +219,35 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (warp == kProducerWarp) {
         if (lane < 2) {
             const bool is_k = lane == 0;
-            if (is_k) {
+            const CUtensorMap *tmX = is_k ? &tmK : &tmV;
+            if (is_k)
                 prefetch_tmap(&tmQ);
-                prefetch_tmap(&tmKV);
-            }
+            prefetch_tmap(tmX);
             uint64_t *full = is_k ? k_full : v_full;
             uint64_t *empty = is_k ? k_empty : v_empty;
             uint8_t *ring = smem + (is_k ? OFF_K : OFF_V);
             int lastq = -1, lastg = -1, st = 0, use = 0;
             bool ok = true;
             for (int k = 0; k < nmine && ok; k++) {
-                int seq, head, qt;
-                coords(k, seq, head, qt);
-                const int row0 = seq * a.N;
+                int seq, head, qt, j0;
+                coords(k, seq, head, qt, j0);
+                const int row0 = seq * a.Nk + j0 * BKV;
                 if (is_k) {
                     if (!mbar_wait(&q_empty[k & 1], ((k >> 1) & 1) ^ 1, a.err, abort_flag))
                         break;
                     mbar_arrive_expect_tx(&q_full[k & 1], Q_BYTES);
-                    tma_load_2d(smem + OFF_Q + (k & 1) * Q_BYTES, &tmQ, &q_full[k & 1], head * HD,
-                                row0 + qt * BQ);
+                    tma_load_2d(smem + OFF_Q + (k & 1) * Q_BYTES, &tmQ, &q_full[k & 1],
+                                a.qcol + head * HD, seq * a.Nq + qt * BQ);
                     lastq = k;
                 }
-                const int col = (is_k ? a.E : 2 * a.E) + head * HD;
+                const int col = (is_k ? a.kcol : a.vcol) + head * HD;
                 for (int j = 0; j < nkv; j++) {
                     if (!mbar_wait(&empty[st], (use & 1) ^ 1, a.err, abort_flag)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(&full[st], KV_BYTES);
-                    tma_load_2d(ring + st * KV_BYTES, &tmKV, &full[st], col, row0 + j * BKV);
+                    tma_load_2d(ring + st * KV_BYTES, tmX, &full[st], col, row0 + j * BKV);
                     lastg = k * nkv + j;
                     if (++st == KST) {
                         st = 0;
@@ -278,14 +343,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int r = quarter * 32 + lane;
         const uint32_t tL = tmem_base + ((uint32_t)(quarter * 32) << 16);
         const uint32_t tO = tL + TM_O;
-        const float sl2 = a.scale_log2;
+        // With a bias the scores are scaled and biased when loaded
+        // (prep_scores), so the exponent step uses a unit scale.
+        const float sl2 = BIAS ? 1.0f : a.scale_log2;
         const uint64_t sl2x2 = f2_make(sl2, sl2);
         bool ok = true;
         int g = 0;
         for (int k = 0; k < nmine && ok; k++) {
-            int seq, head, qt;
-            coords(k, seq, head, qt);
-            const bool rows_live = qt * BQ + quarter * 32 < a.N;
+            int seq, head, qt, j0;
+            coords(k, seq, head, qt, j0);
+            const bool rows_live = qt * BQ + quarter * 32 < a.Nq;
+            const int q = qt * BQ + r;
+            const float *brow = BIAS && q < a.Nq
+                                    ? a.bias + ((long)(seq * a.heads + head) * a.Nq + q) * a.Nk
+                                    : nullptr;
             float m_used = -INFINITY;
             uint64_t lsum0 = 0, lsum1 = 0;
             for (int j = 0; j < nkv; j++, g++) {
@@ -303,13 +374,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     for (int c = 0; c < BKV / 32; c++)
                         tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
                     tmem_wait_ld();
-                    const int valid = a.N - j * BKV;
-                    if (valid < BKV) {
-#pragma unroll
-                        for (int e = 0; e < BKV; e++)
-                            if (e >= valid)
-                                s[e] = __float_as_uint(-INFINITY);
-                    }
+                    const int valid = a.Nk - (j0 + j) * BKV;
+                    prep_scores<BIAS>(s, valid, brow ? brow + (j0 + j) * BKV : nullptr,
+                                      a.scale_log2);
                     // Pass 0 takes the exponentials against the running
                     // offset m_used, which only the item's first tile sets
                     // from its maximum. If a value reached 2^13 (tile sum
@@ -368,12 +435,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                         for (int c = 0; c < BKV / 32; c++)
                             tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
                         tmem_wait_ld();
-                        if (valid < BKV) {
-#pragma unroll
-                            for (int e = 0; e < BKV; e++)
-                                if (e >= valid)
-                                    s[e] = __float_as_uint(-INFINITY);
-                        }
+                        prep_scores<BIAS>(s, valid, brow ? brow + (j0 + j) * BKV : nullptr,
+                                          a.scale_log2);
                     }
                     lsum0 = add2(lsum0, t0);
                     lsum1 = add2(lsum1, t1);
@@ -429,10 +492,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 float la, lb, lc, ld;
                 f2_split(lsum0, la, lb);
                 f2_split(lsum1, lc, ld);
-                const float inv = 1.0f / ((la + lb) + (lc + ld));
-                const int q = qt * BQ + r;
-                if (q < a.N) {
-                    const long orow = (long)(seq * a.N + q) * a.E + head * HD;
+                const float lsum = (la + lb) + (lc + ld);
+                if (SPLIT && q < a.Nq) {
+                    const int item = (int)blockIdx.x + k * (int)gridDim.x;
+                    float4 *dst = reinterpret_cast<float4 *>(a.part + ((long)item * BQ + r) * kPartRow);
+#pragma unroll
+                    for (int d = 0; d < HD; d += 4)
+                        dst[d / 4] = make_float4(__uint_as_float(ov[d]), __uint_as_float(ov[d + 1]),
+                                                 __uint_as_float(ov[d + 2]), __uint_as_float(ov[d + 3]));
+                    a.part[((long)item * BQ + r) * kPartRow + HD] = m_used;
+                    a.part[((long)item * BQ + r) * kPartRow + HD + 1] = lsum;
+                }
+                const float inv = 1.0f / lsum;
+                if (!SPLIT && q < a.Nq) {
+                    const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD;
                     if (OUT_BF16) {
                         uint4 *dst = reinterpret_cast<uint4 *>(
                             reinterpret_cast<__nv_bfloat16 *>(a.out) + orow);
@@ -466,15 +539,101 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 }
 
+// Merges the nsplit partial results of each (sequence, head, query row):
+// O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s. One
+// thread per 4 output columns.
 template <bool OUT_BF16>
-int launch(const CUtensorMap &tq, const CUtensorMap &tkv, const AttnArgs &a, int grid, cudaStream_t s)
+__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ part, AttnArgs a)
 {
-    auto kern = attn_tc_kernel<OUT_BF16>;
-    cudaError_t e = smem_limit_once<attn_tc_kernel<OUT_BF16>>(SMEM_BYTES);
+    const long n = (long)a.nseq * a.heads * a.Nq * (HD / 4);
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const int d = (int)(i % (HD / 4)) * 4;
+        const long rq = i / (HD / 4);
+        const int q = (int)(rq % a.Nq);
+        const long sh = rq / a.Nq;  // seq * heads + head
+        const int head = (int)(sh % a.heads), seq = (int)(sh / a.heads);
+        const int qt = q / BQ, r = q % BQ;
+        const float *p0 = part + (((sh * a.nqt + qt) * a.nsplit) * BQ + r) * kPartRow;
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.nsplit; sp++)
+            M = fmaxf(M, p0[(long)sp * BQ * kPartRow + HD]);
+        float L = 0.0f;
+        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int sp = 0; sp < a.nsplit; sp++) {
+            const float *ps = p0 + (long)sp * BQ * kPartRow;
+            const float f = exp2f(ps[HD] - M);
+            L = fmaf(ps[HD + 1], f, L);
+            const float4 v = *reinterpret_cast<const float4 *>(ps + d);
+            o.x = fmaf(v.x, f, o.x);
+            o.y = fmaf(v.y, f, o.y);
+            o.z = fmaf(v.z, f, o.z);
+            o.w = fmaf(v.w, f, o.w);
+        }
+        const float inv = 1.0f / L;
+        const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD + d;
+        if (OUT_BF16) {
+            uint2 w = make_uint2(pack_bf16x2(o.x * inv, o.y * inv), pack_bf16x2(o.z * inv, o.w * inv));
+            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + orow) = w;
+        }
+        else
+            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.out) + orow) =
+                make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+    }
+}
+
+template <bool OUT_BF16, bool BIAS, bool SPLIT>
+int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const AttnArgs &a,
+           int grid, cudaStream_t s)
+{
+    cudaError_t e = smem_limit_once<attn_tc_kernel<OUT_BF16, BIAS, SPLIT>>(SMEM_BYTES);
     if (e != cudaSuccess)
         return (int)e;
-    kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tkv, a);
+    attn_tc_kernel<OUT_BF16, BIAS, SPLIT><<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !SPLIT)
+        return (int)e;
+    const long n = (long)a.nseq * a.heads * a.Nq * (HD / 4);
+    const long blocks = (n + 255) / 256;
+    combine_kernel<OUT_BF16><<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(a.part, a);
     return (int)cudaGetLastError();
+}
+
+// KV split for few query tiles: the largest divisor of the KV tile count
+// that keeps the work items within two per SM (1 when the query tiles
+// already fill the GPU).
+int pick_split(long base_items, int nkv_total, int sms)
+{
+    int best = 1;
+    for (int d = 2; d <= nkv_total; d++)
+        if (nkv_total % d == 0 && base_items * d <= 2L * sms)
+            best = d;
+    return best;
+}
+
+int run(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, AttnArgs &a,
+        bool out_bf16, cudaStream_t st)
+{
+    a.nqt = (a.Nq + BQ - 1) / BQ;
+    a.nkv = (a.Nk + BKV - 1) / BKV / a.nsplit;
+    const long nitems = (long)a.nseq * a.heads * a.nqt * a.nsplit;
+    if (nitems > 0x7fffffffL || (long)a.nseq * a.Nq > 0x7fffffffL ||
+        (long)a.nseq * a.Nk > 0x7fffffffL)
+        return K_EARG;
+    a.nitems = (int)nitems;
+    const int sms = device_sms();
+    const int grid = nitems < kCtasPerSm * sms ? (int)nitems : kCtasPerSm * sms;
+    // self-attention of the backbone: no bias, no split; the cross paths
+    // (fp32 output) with or without either
+    if (!a.bias && a.nsplit == 1)
+        return out_bf16 ? launch<true, false, false>(tq, tk, tv, a, grid, st)
+                        : launch<false, false, false>(tq, tk, tv, a, grid, st);
+    if (out_bf16)
+        return K_EARG;
+    if (a.bias)
+        return a.nsplit > 1 ? launch<false, true, true>(tq, tk, tv, a, grid, st)
+                            : launch<false, true, false>(tq, tk, tv, a, grid, st);
+    return launch<false, false, true>(tq, tk, tv, a, grid, st);
 }
 
 }  // namespace
@@ -491,21 +650,70 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     if (!make_tmap_bf16(&tq, qkv, rows, 3ull * E, 3ull * E, BQ) ||
         !make_tmap_bf16(&tkv, qkv, rows, 3ull * E, 3ull * E, BKV))
         return K_ETMAP;
-    const int sms = device_sms();
     AttnArgs a;
     a.nseq = nseq;
-    a.N = N;
-    a.E = E;
+    a.Nq = N;
+    a.Nk = N;
     a.heads = heads;
-    a.nqt = (N + BQ - 1) / BQ;
+    a.qcol = 0;
+    a.kcol = E;
+    a.vcol = 2 * E;
+    a.ldo = E;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = out;
+    a.bias = nullptr;
+    a.part = nullptr;
+    a.nsplit = 1;
     a.err = err;
-    const long nitems = (long)nseq * heads * a.nqt;
-    if (nitems > 0x7fffffffL)
+    return run(tq, tkv, tkv, a, out_bf16 != 0, reinterpret_cast<cudaStream_t>(s));
+}
+
+extern "C" size_t k_attn_tc_cross_workspace(int nseq, int Nq, int Nk, int heads)
+{
+    using namespace sam3;
+    if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0)
+        return 0;
+    const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
+    const int nsplit = pick_split(base, (Nk + BKV - 1) / BKV, device_sms());
+    return nsplit > 1 ? (size_t)base * nsplit * BQ * kPartRow * sizeof(float) : 0;
+}
+
+extern "C" int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
+                               long ldv, int nseq, int Nq, int Nk, int heads, float scale,
+                               const float *bias, void *out, long ldo, int out_bf16, void *ws,
+                               size_t ws_bytes, int *err, k_stream s)
+{
+    using namespace sam3;
+    const long W = (long)heads * HD;
+    if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0 || ldq < W || ldk < W || ldv < W ||
+        ldo < W || (ldo * (out_bf16 ? 2 : 4)) % 16 || (reinterpret_cast<uintptr_t>(out) & 15))
         return K_EARG;
-    a.nitems = (int)nitems;
-    const int grid = nitems < kCtasPerSm * sms ? (int)nitems : kCtasPerSm * sms;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
-    return out_bf16 ? launch<true>(tq, tkv, a, grid, st) : launch<false>(tq, tkv, a, grid, st);
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_bf16(&tq, Q, (uint64_t)nseq * Nq, (uint64_t)W, (uint64_t)ldq, BQ) ||
+        !make_tmap_bf16(&tk, K, (uint64_t)nseq * Nk, (uint64_t)W, (uint64_t)ldk, BKV) ||
+        !make_tmap_bf16(&tv, V, (uint64_t)nseq * Nk, (uint64_t)W, (uint64_t)ldv, BKV))
+        return K_ETMAP;
+    AttnArgs a;
+    a.nseq = nseq;
+    a.Nq = Nq;
+    a.Nk = Nk;
+    a.heads = heads;
+    a.qcol = 0;
+    a.kcol = 0;
+    a.vcol = 0;
+    a.ldo = ldo;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = out;
+    a.bias = bias;
+    a.err = err;
+    const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
+    a.nsplit = pick_split(base, (Nk + BKV - 1) / BKV, device_sms());
+    a.part = nullptr;
+    if (a.nsplit > 1) {
+        if (!ws || ws_bytes < k_attn_tc_cross_workspace(nseq, Nq, Nk, heads) ||
+            (reinterpret_cast<uintptr_t>(ws) & 15))
+            return K_EARG;
+        a.part = static_cast<float *>(ws);
+    }
+    return run(tq, tk, tv, a, out_bf16 != 0, reinterpret_cast<cudaStream_t>(s));
 }

@@ -65,6 +65,59 @@ __global__ void __launch_bounds__(256) unpack_heads_kernel(const float *__restri
     }
 }
 
+// One operand of a cross-attention, fp32 or bf16 [rows, ld] (head h at
+// column h * hd) -> bf16 [rows, heads * 64] with columns hd..63 of each
+// head zero (the tcgen05 attention's layout). One thread per 4 output
+// columns.
+template <bool SRC_BF16>
+__global__ void __launch_bounds__(256) pad_heads_kernel(const void *__restrict__ src, long ld,
+                                                        long rows, int heads, int hd,
+                                                        uint2 *__restrict__ out)
+{
+    const int q4 = heads * 16;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < rows * q4;
+         i += (long)gridDim.x * blockDim.x) {
+        const long n = i / q4;
+        const int c = (int)(i % q4) * 4, h = c / 64, d = c % 64;
+        uint2 w = make_uint2(0u, 0u);
+        if (d < hd) {
+            if (SRC_BF16)
+                w = *reinterpret_cast<const uint2 *>(
+                    reinterpret_cast<const __nv_bfloat16 *>(src) + n * ld + h * hd + d);
+            else {
+                const float4 x = *reinterpret_cast<const float4 *>(
+                    reinterpret_cast<const float *>(src) + n * ld + h * hd + d);
+                __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y),
+                               hi = __floats2bfloat162_rn(x.z, x.w);
+                w = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+            }
+        }
+        out[i] = w;
+    }
+}
+
+// SAM 3's box relative position bias of softmax_ext (sam3_kernels.cl:
+// 890-921) as a dense [heads, Nq, Nk] term for the tensor-core attention, in
+// log2 units: bias[(h Nq + i) Nk + j] = (dy[(i H + y) nh + h] + dx[(i W +
+// x) nh + h]) log2 e for key j = y W + x.
+__global__ void __launch_bounds__(256) rpb_bias_kernel(const float *__restrict__ dy,
+                                                       const float *__restrict__ dx, int Nq,
+                                                       int Nk, int W, int heads,
+                                                       float *__restrict__ bias)
+{
+    const int H = Nk / W;
+    const long n = (long)heads * Nq * Nk;
+    for (long t = (long)blockIdx.x * blockDim.x + threadIdx.x; t < n;
+         t += (long)gridDim.x * blockDim.x) {
+        const int j = (int)(t % Nk);
+        const long hi = t / Nk;
+        const int i = (int)(hi % Nq), h = (int)(hi / Nq);
+        const int y = j / W, x = j - y * W;
+        bias[t] = (__ldg(dy + ((long)i * H + y) * heads + h) + __ldg(dx + ((long)i * W + x) * heads + h)) *
+                  1.4426950408889634f;
+    }
+}
+
 constexpr int kQB = 32;    // queries per CTA
 constexpr int kLanes = 8;  // key lanes per query
 constexpr int kKC = 32;    // keys per shared-memory chunk
@@ -213,6 +266,35 @@ extern "C" int k_unpack_heads64(const float *in, long N, int heads, int hd, floa
     const int grid = grid_for(N * heads * hd / 4, 256);
     unpack_heads_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(in, N, heads, hd,
                                                                                   O, ldo);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_pad_heads64(const void *src, int src_bf16, long ld, long rows, int heads, int hd,
+                             void *out, k_stream s)
+{
+    if (rows <= 0 || heads <= 0 || hd <= 0 || hd > 64 || (hd & 3) || (ld & 3) ||
+        (reinterpret_cast<uintptr_t>(src) & (src_bf16 ? 7 : 15)) ||
+        (reinterpret_cast<uintptr_t>(out) & 7))
+        return K_EARG;
+    const int grid = grid_for(rows * heads * 16, 256);
+    const int g = grid < 148 * 16 ? grid : 148 * 16;
+    if (src_bf16)
+        pad_heads_kernel<true><<<g, 256, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
+                                                          reinterpret_cast<uint2 *>(out));
+    else
+        pad_heads_kernel<false><<<g, 256, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
+                                                           reinterpret_cast<uint2 *>(out));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_rpb_bias(const float *dy, const float *dx, int Nq, int Nk, int W, int heads,
+                          float *bias, k_stream s)
+{
+    if (Nq <= 0 || Nk <= 0 || W <= 0 || Nk % W || heads <= 0)
+        return K_EARG;
+    const int grid = grid_for((long)heads * Nq * Nk, 256);
+    rpb_bias_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(dy, dx, Nq, Nk, W,
+                                                                             heads, bias);
     return (int)cudaGetLastError();
 }
 

@@ -79,6 +79,21 @@ int k_gemm_simt(int M, int N, int K, const void *A, int adt, long aoff, int lda,
 int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
               void *out, int out_bf16, int *err, k_stream s);
 
+/* The same kernel for cross-attention: nseq sequences of Nq query rows of
+ * Q and Nk key / value rows of K and V (bf16, leading dimensions ldq / ldk /
+ * ldv in elements, head h at column 64 h, 16-byte aligned rows), out rows
+ * seq * Nq + q with leading dimension ldo (head h at column 64 h), fp32
+ * (bf16 only without a bias and without a key split). bias: NULL, or fp32
+ * [nseq, heads, Nq, Nk] added to the scaled scores, in log2 units
+ * (natural-log bias x log2 e). */
+int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
+                    long ldv, int nseq, int Nq, int Nk, int heads, float scale,
+                    const float *bias, void *out, long ldo, int out_bf16, void *ws,
+                    size_t ws_bytes, int *err, k_stream s);
+/* Device workspace k_attn_tc_cross needs (0 when the query tiles fill the
+ * GPU; otherwise the keys are split and the partial results merged). */
+size_t k_attn_tc_cross_workspace(int nseq, int Nq, int Nk, int heads);
+
 /* The same attention in fp32 on CUDA cores (reference mode): qkv fp32. */
 int k_attn_f32(const float *qkv, int nseq, int N, int E, int heads, int hd,
                float scale, float *out, k_stream s);
@@ -213,6 +228,14 @@ int k_pack_qkv_pad64(const float *q, int ldq, const float *k, int ldk,
 int k_unpack_heads64(const float *in, long N, int heads, int hd, float *O,
                      int ldo, k_stream s);
 int k_attend_splits(int Nq, int Nk, int heads, int num_sms);
+/* pad_heads64: one attention operand, fp32 or bf16 (src_bf16) [rows, ld],
+ * head h at column h * hd -> bf16 [rows, heads * 64], columns hd..63 of
+ * each head zero. rpb_bias: the box relative position bias of softmax_ext
+ * as fp32 [heads, Nq, Nk] in log2 units (k_attn_tc_cross's bias). */
+int k_pad_heads64(const void *src, int src_bf16, long ld, long rows, int heads, int hd,
+                  void *out, k_stream s);
+int k_rpb_bias(const float *dy, const float *dx, int Nq, int Nk, int W, int heads,
+               float *bias, k_stream s);
 size_t k_attend_workspace(int Nq, int Nk, int heads, int hd, int num_sms);
 int k_attend_simt(int Nq, int Nk, int heads, int hd, const float *Q, int ldq,
                   const float *K, int ldk, const float *V, int ldv, float *O,

@@ -80,6 +80,14 @@ struct cb_decoder {
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
     void *mha_ws;
     size_t mha_ws_bytes;
+    /* layer 0's token -> image attention on the tensor cores: the shared
+     * keys / values with heads padded to 64 columns (bf16 [T, 512], set
+     * with the image), the queries and output in that layout, and the
+     * key-split workspace */
+    void *k0_pad, *v0_pad, *q_pad;
+    float *o_pad;
+    void *xws;
+    size_t xws_bytes;
     float *h_tok;               /* host [batch * 8, 256] */
 };
 
@@ -109,7 +117,8 @@ void cb_decoder_free(cb_decoder *d)
                        d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
                        d->bv, d->bo_bf16, d->u1_bf16,
-                       d->hyper, d->iou, d->mha_ws};
+                       d->hyper, d->iou, d->mha_ws, d->k0_pad, d->v0_pad, d->q_pad,
+                       d->o_pad, d->xws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
             cudaFree(dev[i]);
@@ -179,6 +188,17 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     ws_i2t = k_mha_workspace(batch, DEC_T, DEC_NTOK, 128, b->num_sms);
     d->mha_ws_bytes = ws_t2i > ws_i2t ? ws_t2i : ws_i2t;
     A(d->mha_ws, d->mha_ws_bytes);
+    A(d->k0_pad, T * 512 * 2);
+    A(d->v0_pad, T * 512 * 2);
+    A(d->q_pad, nt * 512 * 2);
+    A(d->o_pad, nt * 512 * 4);
+    for (i = 1; i <= batch; i++) {  /* fewer prompts split the keys more */
+        const size_t w = k_attn_tc_cross_workspace(1, i * DEC_NTOK, DEC_T, 8);
+
+        if (w > d->xws_bytes)
+            d->xws_bytes = w;
+    }
+    A(d->xws, d->xws_bytes);
 #undef A
     if (rc == CB_OK) {
         d->h_tok = malloc(nt * DEC_DIM * sizeof(float));
@@ -451,7 +471,24 @@ static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, l
 static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, long sv)
 {
     cb_backend *b = d->b;
+    const long nt = (long)P * DEC_NTOK;
 
+    if (!sk && !sv) {
+        /* keys shared by all prompts (layer 0): one cross-attention of the
+         * P * 8 queries over the image on the tensor cores, heads of 16
+         * padded to 64 (the keys once per image, in set_image) */
+        LAUNCH("dec_pad", 0, (double)nt * 128 * 4 + (double)nt * 512 * 2,
+               k_pad_heads64(d->sq, 0, 128, nt, 8, 16, d->q_pad,
+                             (k_stream)b->stream));
+        LAUNCH("dec_mha_t2i", 4.0 * nt * (double)DEC_T * 128,
+               (double)nt * 512 * 2 + 2.0 * DEC_T * 512 * 2 + (double)nt * 512 * 4,
+               k_attn_tc_cross(d->q_pad, 512, d->k0_pad, 512, d->v0_pad, 512, 1, (int)nt, DEC_T,
+                               8, 0.25f, NULL, d->o_pad, 512, 0, d->xws, d->xws_bytes, b->d_err,
+                               (k_stream)b->stream));
+        LAUNCH("dec_pad", 0, (double)nt * 512 * 4 + (double)nt * 128 * 4,
+               k_unpack_heads64(d->o_pad, nt, 8, 16, d->so, 128, (k_stream)b->stream));
+        return CB_OK;
+    }
     LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,
            4.0 * (double)P * DEC_NTOK * 128 * 2 + 2.0 * (sk ? (double)P : 1.0) * DEC_T * 128 * 2,
            k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so,
@@ -499,6 +536,10 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_
            k_cast_f32_bf16(d->src, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));
     CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, (long)T, DEC_DIM, 128,
                   ATT(SAM3_DA_L0_T2I, VW), ATT(SAM3_DA_L0_T2I, VB), d->vp0));
+    LAUNCH("dec_pad", 0, (double)T * 128 * 2 * 2 + (double)T * 512 * 2 * 2,
+           k_pad_heads64(d->kp0, 1, 128, (long)T, 8, 16, d->k0_pad, (k_stream)b->stream));
+    LAUNCH("dec_pad", 0, 0,
+           k_pad_heads64(d->vp0, 1, 128, (long)T, 8, 16, d->v0_pad, (k_stream)b->stream));
     /* qp0 is read only by the image -> token attention, as bf16 */
     LAUNCH("dec_cast", 0, (double)T * DEC_DIM * 6,
            k_cast_f32_bf16(d->srcpe, d->kin_bf16, (long)T * DEC_DIM, (k_stream)b->stream));

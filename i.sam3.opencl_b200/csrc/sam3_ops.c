@@ -370,6 +370,11 @@ int cb_mask_logits(cb_backend *b, cb_mem U, cb_mem hyper, cb_mem out, int P,
                       "mask_logits");
 }
 
+static size_t al256(size_t n)
+{
+    return (n + 255) & ~(size_t)255;
+}
+
 int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ldq,
               cb_mem K, int ldk, cb_mem V, int ldv, cb_mem O, int ldo, int causal,
               cb_mem dy, cb_mem dx, int W, int mode)
@@ -408,6 +413,46 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
         return cbi_kstatus(b,
                            k_unpack_heads64((const float *)(s + packed), Nq, heads, hd,
                                             (float *)O->ptr, ldo, st),
+                           "attend: unpack");
+    }
+    if (mode == CB_ATTN_TC && !causal && Nk >= 1024 && ldq % 4 == 0 && ldk % 4 == 0 &&
+        ldv % 4 == 0 && ldo % 4 == 0 && aligned16(Q->ptr) && aligned16(K->ptr) &&
+        aligned16(V->ptr) && aligned16(O->ptr)) {
+        /* tensor cores for queries over many keys, with or without the box
+         * bias: Q, K, V padded to 64-column heads in bf16, the bias as a
+         * dense [heads, Nq, Nk] term, keys split over CTAs when the query
+         * tiles are few (the detector's 201 queries over the image) */
+        const size_t E64 = (size_t)heads * 64;
+        const size_t szq = al256((size_t)Nq * E64 * 2), szk = al256((size_t)Nk * E64 * 2);
+        const size_t szb = dy ? al256((size_t)heads * Nq * Nk * 4) : 0;
+        const size_t szo = al256((size_t)Nq * E64 * 4);
+        const size_t szw = k_attn_tc_cross_workspace(1, Nq, Nk, heads);
+        char *s = NULL, *qp, *kp, *vp, *bp, *op, *wp;
+
+        CB_TRY(cbi_scratch(b, szq + 2 * szk + szb + szo + szw, (void **)&s));
+        qp = s;
+        kp = qp + szq;
+        vp = kp + szk;
+        bp = vp + szk;
+        op = bp + szb;
+        wp = op + szo;
+        CB_TRY(cbi_kstatus(b, k_pad_heads64(Q->ptr, 0, ldq, Nq, heads, hd, qp, st), "attend: pack"));
+        CB_TRY(cbi_kstatus(b, k_pad_heads64(K->ptr, 0, ldk, Nk, heads, hd, kp, st), "attend: pack"));
+        CB_TRY(cbi_kstatus(b, k_pad_heads64(V->ptr, 0, ldv, Nk, heads, hd, vp, st), "attend: pack"));
+        if (dy)
+            CB_TRY(cbi_kstatus(b,
+                               k_rpb_bias((const float *)dy->ptr, (const float *)dx->ptr, Nq, Nk,
+                                          W, heads, (float *)bp, st),
+                               "attend: bias"));
+        CB_TRY(cbi_kstatus(b,
+                           k_attn_tc_cross(qp, (long)E64, kp, (long)E64, vp, (long)E64, 1, Nq, Nk,
+                                           heads, 1.0f / sqrtf((float)hd),
+                                           dy ? (const float *)bp : NULL, op, (long)E64, 0,
+                                           szw ? wp : NULL, szw, b->d_err, st),
+                           "attend"));
+        return cbi_kstatus(b,
+                           k_unpack_heads64((const float *)op, Nq, heads, hd, (float *)O->ptr,
+                                            ldo, st),
                            "attend: unpack");
     }
     {

@@ -403,12 +403,15 @@ int cb_neck_run(cb_neck *n, cb_mem x, int ntile, cb_mem emb, cb_mem feat_s0,
  * at column h * hd. causal != 0 excludes keys j > query i; dy / dx (F32,
  * both or neither) add SAM 3's box relative position bias dy[(i * (Nk / W)
  * + y) * heads + h] + dx[(i * W + x) * heads + h] for key j = y * W + x
- * (softmax_ext, sam3_kernels.cl:889-921). mode CB_ATTN_TC runs unmasked,
- * unbiased self-attention of at least 1024 tokens (Nq == Nk; the fusion
- * encoder's 5184-token layers) on the tcgen05 flash kernel with bf16
- * operands (heads zero-padded to 64 columns), everything else on the CUDA
- * cores in fp32 (a flash kernel with the keys split over CTAs);
- * CB_ATTN_F32 always uses the fp32 kernel. */
+ * (softmax_ext, sam3_kernels.cl:889-921). mode CB_ATTN_TC runs every
+ * call without the causal mask over at least 1024 keys on the tcgen05 flash
+ * kernel with bf16 operands (heads zero-padded to 64 columns): the fusion
+ * encoder's 5184-token self-attention, and queries over the image with or
+ * without the box bias (the detector decoder's 201 queries; the bias enters
+ * as a dense per-score term, the keys are split over CTAs when the query
+ * tiles are few); everything else runs on the CUDA cores in fp32 (a flash
+ * kernel with the keys split over CTAs). CB_ATTN_F32 always uses the fp32
+ * kernel. */
 int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q,
               int ldq, cb_mem K, int ldk, cb_mem V, int ldv, cb_mem O, int ldo,
               int causal, cb_mem dy, cb_mem dx, int W, int mode);

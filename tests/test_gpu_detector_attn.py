@@ -2,8 +2,10 @@
 sam3_text.c:305-343 with softmax_ext, sam3_kernels.cl:889-921) against the
 oracle's restatement: fp32 CUDA-core path (causal mask, box relative
 position bias, few or many keys) max-abs <= 1e-4 relative to the output
-scale; tensor-core path (fusion-encoder self-attention, bf16 operands,
-heads of 32 zero-padded to 64) cosine >= 0.9999, max-abs <= 1e-2."""
+scale; tensor-core paths (fusion-encoder self-attention; queries over the
+image with or without the box bias; bf16 operands, heads zero-padded to 64)
+cosine >= 0.9999, max-abs <= 1e-2 (relative to the output scale where a
+bias makes rows peaked)."""
 import numpy as np
 import pytest
 
@@ -58,6 +60,35 @@ def test_attend_tensor_core_fusion_encoder_vs_oracle(cb, sb, ob, N):
     a, b = got.astype(np.float64).ravel(), want.astype(np.float64).ravel()
     assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) >= 0.9999
     assert np.abs(got - want).max() <= 1e-2
+
+
+@pytest.mark.parametrize("Nq,Nk,heads,hd,rpb", [
+    (201, 5184, 8, 32, True),    # the detector decoder's queries over the image, box bias
+    (300, 1500, 4, 64, False),   # ragged query and key tiles, no bias
+    (77, 1100, 2, 32, True),     # one query tile, keys split many ways, bias on a 44-wide grid
+])
+def test_attend_tensor_core_cross_vs_oracle(cb, sb, ob, Nq, Nk, heads, hd, rpb):
+    """Queries over many keys on the tcgen05 kernel (k_attn_tc_cross): heads
+    padded to 64 in bf16, the box bias as a dense per-score term, the keys
+    split over CTAs and merged when the query tiles are few. Bound of the
+    other tensor-core attention tests, max-abs relative to the output scale
+    (the bias of std 2 makes some rows peaked)."""
+    E = heads * hd
+    Q = ob.normal(63, 1, (Nq, E))
+    K = ob.normal(63, 2, (Nk, E))
+    V = ob.normal(63, 3, (Nk, E))
+    dy = dx = None
+    W = 0
+    if rpb:
+        W = 72 if Nk == 5184 else 44
+        dy = ob.normal(63, 4, (Nq * (Nk // W) * heads,), 0.0, 2.0)
+        dx = ob.normal(63, 5, (Nq * W * heads,), 0.0, 2.0)
+    got = _run(cb, sb, Q, K, V, heads, hd, 0, dy, dx, W, mode=0)
+    want = ob.attend(Q, K, V, heads, hd, 0, dy, dx, W)
+    a, b = got.astype(np.float64).ravel(), want.astype(np.float64).ravel()
+    assert np.isfinite(got).all()
+    assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) >= 0.9999
+    assert np.abs(got - want).max() <= 1e-2 * max(1.0, float(np.abs(want).max()))
 
 
 def test_attend_rejects_bad_shapes(cb, sb):
