@@ -104,5 +104,6 @@ extern "C" int cb_attention_noalloc(const float *qkv, int nseq, int N, int E, in
                 : k_cast_f32_bf16(qkv, scratch, (long)rows * 3 * E, s);
     if (rc != 0)
         return status_of_launch(rc);
-    return status_of_launch(k_attn_tc(scratch, nseq, N, E, heads, scale, out, 0, errp, s));
+    return status_of_launch(k_attn_tc(scratch, nseq, N, E, heads, scale, out, 0, NULL, 0, errp,
+                                      s));
 }

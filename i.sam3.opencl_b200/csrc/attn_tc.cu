@@ -18,7 +18,12 @@
 // on each SM, each persistent (CTA c takes items c, c + grid, ...) with its
 // own MMA thread and K/V stream: the two pipelines drift apart in phase, so
 // one CTA's softmax runs while the other's tensor-core work or loads do, and
-// a short launch balances at the granularity of one tile. KV tiles hold 96
+// a short launch balances at the granularity of one tile. A launch of few
+// waves given a workspace (the standalone op, the detector, cross-
+// attention) splits the items that do not fill the last wave over their KV
+// range: each part writes its unnormalised rows with (offset, sum), and a
+// merge kernel combines them (the encoder passes none: a tile's result
+// must not depend on the batch it is encoded in). KV tiles hold 96
 // keys (576 = 6 x 96, 5184 = 54 x 96). Rows of a tail tile beyond N (576 =
 // 4.5 x 128) run through the tensor core, but their softmax work is skipped
 // and nothing is stored.
@@ -98,13 +103,14 @@ static_assert(TM_O + HD <= TM_COLS && kCtasPerSm * TM_COLS <= 512, "tensor memor
 // column qcol / kcol / vcol + 64 h); out rows s * Nq + q, leading dimension
 // ldo, head h at column 64 h. bias (BIAS instantiation): fp32 added to the
 // scaled scores, [nseq, heads, Nq, Nk] in log2 units.
-// nsplit > 1 (few query tiles): the KV tiles of each (sequence, head,
-// query tile) are split into nsplit equal ranges of nkv tiles, each a work
-// item that writes its unnormalised output and (offset, sum) per row to
-// part ([item][128 rows][64 + 4] fp32: output, offset, sum, 2 unused, so
-// that every row starts 16-byte aligned); combine_kernel merges them.
+// Work units: the first nfull are whole items (sequence, head, query tile)
+// over all nkv KV tiles; in a SPLIT launch each remaining item (the tail
+// that does not fill a wave of CTAs) is split into tsplit parts of nkv_t
+// KV tiles, each writing its unnormalised output and (offset, sum) per row
+// to part ([part][128 rows][64 + 4] fp32: output, offset, sum, 2 unused,
+// so that every row starts 16-byte aligned); combine_kernel merges them.
 struct AttnArgs {
-    int nseq, Nq, Nk, heads, nqt, nitems, nsplit, nkv;
+    int nseq, Nq, Nk, heads, nqt, nitems, nkv, nfull, tsplit, nkv_t;
     int qcol, kcol, vcol;
     long ldo;
     float scale_log2;
@@ -173,20 +179,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nkv = a.nkv;
     const int nmine = (int)blockIdx.x < a.nitems
                           ? (a.nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1
                           : 0;
-    const int total = nmine * nkv;
-    // item = ((seq * heads + head) * nqt + qt) * nsplit + split; its KV
-    // tiles start at j0 = split * nkv
+    // this CTA's units k < nwhole are whole items, the rest tail parts
+    const int nwhole = !SPLIT ? nmine
+                              : ((int)blockIdx.x < a.nfull
+                                     ? min(nmine, (a.nfull - 1 - (int)blockIdx.x) / (int)gridDim.x + 1)
+                                     : 0);
+    const int total = nwhole * a.nkv + (nmine - nwhole) * a.nkv_t;
+    auto tiles_of = [&](int k) { return k < nwhole ? a.nkv : a.nkv_t; };
+    // item = (seq * heads + head) * nqt + qt; a tail part p of item i is
+    // unit nfull + (i - nfull) * tsplit + p, its KV tiles start at j0
     auto coords = [&](int k, int &seq, int &head, int &qt, int &j0) {
-        const int item = (int)blockIdx.x + k * (int)gridDim.x;
-        j0 = SPLIT ? (item % a.nsplit) * nkv : 0;
-        const int u = SPLIT ? item / a.nsplit : item;
-        qt = u % a.nqt;
-        head = (u / a.nqt) % a.heads;
-        seq = u / (a.nqt * a.heads);
+        const int u = (int)blockIdx.x + k * (int)gridDim.x;
+        int item = u;
+        j0 = 0;
+        if (SPLIT && u >= a.nfull) {
+            const int v = u - a.nfull;
+            item = a.nfull + v / a.tsplit;
+            j0 = (v % a.tsplit) * a.nkv_t;
+        }
+        qt = item % a.nqt;
+        head = (item / a.nqt) % a.heads;
+        seq = item / (a.nqt * a.heads);
     };
 
     if (threadIdx.x == 0) {
@@ -241,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     lastq = k;
                 }
                 const int col = (is_k ? a.kcol : a.vcol) + head * HD;
+                const int nkv = tiles_of(k);
                 for (int j = 0; j < nkv; j++) {
                     if (!mbar_wait(&empty[st], (use & 1) ^ 1, a.err, abort_flag)) {
                         ok = false;
@@ -248,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     }
                     mbar_arrive_expect_tx(&full[st], KV_BYTES);
                     tma_load_2d(ring + st * KV_BYTES, tmX, &full[st], col, row0 + j * BKV);
-                    lastg = k * nkv + j;
+                    lastg++;
                     if (++st == KST) {
                         st = 0;
                         use++;
@@ -281,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     c.kst = 0;
                     c.kph ^= 1;
                 }
-                if (++c.j == nkv) {
+                if (++c.j == tiles_of(c.k)) {
                     c.j = 0;
                     c.k++;
                 }
@@ -300,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     tc_mma(dS, qd + 2 * kq, kd + 2 * kq, idS, kq != 0);
                 tc_commit(&s_full[c.g & 1]);
                 tc_commit(&k_empty[c.kst]);
-                if (c.j == nkv - 1)
+                if (c.j == tiles_of(c.k) - 1)
                     tc_commit(&q_empty[c.k & 1]);
                 return true;
             };
@@ -357,6 +374,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             const float *brow = BIAS && q < a.Nq
                                     ? a.bias + ((long)(seq * a.heads + head) * a.Nq + q) * a.Nk
                                     : nullptr;
+            const bool is_part = SPLIT && k >= nwhole;
+            const int nkv = tiles_of(k);
             float m_used = -INFINITY;
             uint64_t lsum0 = 0, lsum1 = 0;
             for (int j = 0; j < nkv; j++, g++) {
@@ -493,18 +512,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 f2_split(lsum0, la, lb);
                 f2_split(lsum1, lc, ld);
                 const float lsum = (la + lb) + (lc + ld);
-                if (SPLIT && q < a.Nq) {
-                    const int item = (int)blockIdx.x + k * (int)gridDim.x;
-                    float4 *dst = reinterpret_cast<float4 *>(a.part + ((long)item * BQ + r) * kPartRow);
+                if (is_part && q < a.Nq) {
+                    const long v = (long)blockIdx.x + (long)k * gridDim.x - a.nfull;
+                    float *pr = a.part + (v * BQ + r) * kPartRow;
+                    float4 *dst = reinterpret_cast<float4 *>(pr);
 #pragma unroll
                     for (int d = 0; d < HD; d += 4)
                         dst[d / 4] = make_float4(__uint_as_float(ov[d]), __uint_as_float(ov[d + 1]),
                                                  __uint_as_float(ov[d + 2]), __uint_as_float(ov[d + 3]));
-                    a.part[((long)item * BQ + r) * kPartRow + HD] = m_used;
-                    a.part[((long)item * BQ + r) * kPartRow + HD + 1] = lsum;
+                    pr[HD] = m_used;
+                    pr[HD + 1] = lsum;
                 }
                 const float inv = 1.0f / lsum;
-                if (!SPLIT && q < a.Nq) {
+                if (!is_part && q < a.Nq) {
                     const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD;
                     if (OUT_BF16) {
                         uint4 *dst = reinterpret_cast<uint4 *>(
@@ -539,28 +559,32 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 }
 
-// Merges the nsplit partial results of each (sequence, head, query row):
-// O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s. One
-// thread per 4 output columns.
+// Merges the tsplit partial results of each tail item's query rows:
+// O = sum_p O_p 2^(m_p - M) / sum_p l_p 2^(m_p - M), M = max_p m_p. One
+// thread per (tail item, row, 4 output columns).
 template <bool OUT_BF16>
-__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ part, AttnArgs a)
+__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ part, AttnArgs a,
+                                                      int ntail)
 {
-    const long n = (long)a.nseq * a.heads * a.Nq * (HD / 4);
+    const long n = (long)ntail * BQ * (HD / 4);
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long)gridDim.x * blockDim.x) {
         const int d = (int)(i % (HD / 4)) * 4;
-        const long rq = i / (HD / 4);
-        const int q = (int)(rq % a.Nq);
-        const long sh = rq / a.Nq;  // seq * heads + head
-        const int head = (int)(sh % a.heads), seq = (int)(sh / a.heads);
-        const int qt = q / BQ, r = q % BQ;
-        const float *p0 = part + (((sh * a.nqt + qt) * a.nsplit) * BQ + r) * kPartRow;
+        const int r = (int)((i / (HD / 4)) % BQ);
+        const long t = i / ((HD / 4) * BQ);
+        const long item = a.nfull + t;
+        const int qt = (int)(item % a.nqt), head = (int)((item / a.nqt) % a.heads);
+        const int seq = (int)(item / ((long)a.nqt * a.heads));
+        const int q = qt * BQ + r;
+        if (q >= a.Nq)
+            continue;
+        const float *p0 = part + ((t * a.tsplit) * BQ + r) * kPartRow;
         float M = -INFINITY;
-        for (int sp = 0; sp < a.nsplit; sp++)
+        for (int sp = 0; sp < a.tsplit; sp++)
             M = fmaxf(M, p0[(long)sp * BQ * kPartRow + HD]);
         float L = 0.0f;
         float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int sp = 0; sp < a.nsplit; sp++) {
+        for (int sp = 0; sp < a.tsplit; sp++) {
             const float *ps = p0 + (long)sp * BQ * kPartRow;
             const float f = exp2f(ps[HD] - M);
             L = fmaf(ps[HD + 1], f, L);
@@ -593,54 +617,117 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, 
     e = cudaGetLastError();
     if (e != cudaSuccess || !SPLIT)
         return (int)e;
-    const long n = (long)a.nseq * a.heads * a.Nq * (HD / 4);
+    const int ntail = (a.nitems - a.nfull) / a.tsplit;
+    const long n = (long)ntail * BQ * (HD / 4);
     const long blocks = (n + 255) / 256;
-    combine_kernel<OUT_BF16><<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(a.part, a);
+    combine_kernel<OUT_BF16><<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(
+        a.part, a, ntail);
     return (int)cudaGetLastError();
 }
 
-// KV split for few query tiles: the largest divisor of the KV tile count
-// that keeps the work items within two per SM (1 when the query tiles
-// already fill the GPU).
-int pick_split(long base_items, int nkv_total, int sms)
+// Work plan of a launch over `base` items of nkv KV tiles on 2 x sms CTA
+// slots. Launches of many waves run whole items. Otherwise the items that
+// do not fill the last wave (all of them when `all_split`, for few query
+// tiles) are split into parts: the divisor d of nkv that minimises the
+// tail's time in KV-tile times, ceil(tail * d / slots) waves of nkv / d
+// tiles plus kPartCost for a part's start and partial store, plus
+// kMergeCost for the merge launch when d > 1 (measured: a 9-window launch
+// whose 128 tail items split in 2 ran slower, the 16-head global one whose
+// 64 tail items split in 9 faster). Returns the workspace bytes the split
+// needs (0 for none).
+size_t plan(AttnArgs &a, long base, int nkv, int sms, bool all_split)
 {
+    const long slots = 2L * sms;
+    a.nkv = nkv;
+    a.nfull = (int)base;
+    a.tsplit = 1;
+    a.nkv_t = nkv;
+    a.nitems = (int)base;
+    if (!all_split && base >= 8 * slots)
+        return 0;
+    const long nfull = all_split ? 0 : base / slots * slots;
+    const long tail = base - nfull;
+    if (tail == 0)
+        return 0;
+    constexpr long kPartCost = 3, kMergeCost = 4;
     int best = 1;
-    for (int d = 2; d <= nkv_total; d++)
-        if (nkv_total % d == 0 && base_items * d <= 2L * sms)
+    long best_cost = (tail + slots - 1) / slots * (nkv + kPartCost);
+    for (int d = 2; d <= nkv; d++) {
+        if (nkv % d)
+            continue;
+        const long cost = (tail * d + slots - 1) / slots * (nkv / d + kPartCost) + kMergeCost;
+        if (cost < best_cost) {
+            best_cost = cost;
             best = d;
-    return best;
+        }
+    }
+    if (best == 1)
+        return 0;
+    a.nfull = (int)nfull;
+    a.tsplit = best;
+    a.nkv_t = nkv / best;
+    a.nitems = (int)(nfull + tail * best);
+    return (size_t)tail * best * BQ * kPartRow * sizeof(float);
 }
 
+// Plans the launch (splitting only when ws holds the partial results) and
+// runs it.
 int run(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, AttnArgs &a,
-        bool out_bf16, cudaStream_t st)
+        bool out_bf16, bool all_split, void *ws, size_t ws_bytes, cudaStream_t st)
 {
     a.nqt = (a.Nq + BQ - 1) / BQ;
-    a.nkv = (a.Nk + BKV - 1) / BKV / a.nsplit;
-    const long nitems = (long)a.nseq * a.heads * a.nqt * a.nsplit;
-    if (nitems > 0x7fffffffL || (long)a.nseq * a.Nq > 0x7fffffffL ||
+    const long base = (long)a.nseq * a.heads * a.nqt;
+    if (base > 0x3fffffffL || (long)a.nseq * a.Nq > 0x7fffffffL ||
         (long)a.nseq * a.Nk > 0x7fffffffL)
         return K_EARG;
-    a.nitems = (int)nitems;
     const int sms = device_sms();
-    const int grid = nitems < kCtasPerSm * sms ? (int)nitems : kCtasPerSm * sms;
-    // self-attention of the backbone: no bias, no split; the cross paths
-    // (fp32 output) with or without either
-    if (!a.bias && a.nsplit == 1)
+    const int nkv = (a.Nk + BKV - 1) / BKV;
+    size_t need = plan(a, base, nkv, sms, all_split);
+    if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 15)))
+        need = 0;  // no room for the partial results: whole items
+    if (!need) {
+        a.nfull = (int)base;
+        a.tsplit = 1;
+        a.nkv_t = nkv;
+        a.nitems = (int)base;
+    }
+    a.part = need ? static_cast<float *>(ws) : nullptr;
+    if (a.nitems > 0x7fffffff)
+        return K_EARG;
+    const int grid = a.nitems < 2 * sms ? a.nitems : 2 * sms;
+    const bool split = a.nitems != a.nfull;
+    if (!a.bias && !split)
         return out_bf16 ? launch<true, false, false>(tq, tk, tv, a, grid, st)
                         : launch<false, false, false>(tq, tk, tv, a, grid, st);
+    if (!a.bias)
+        return out_bf16 ? launch<true, false, true>(tq, tk, tv, a, grid, st)
+                        : launch<false, false, true>(tq, tk, tv, a, grid, st);
     if (out_bf16)
         return K_EARG;
-    if (a.bias)
-        return a.nsplit > 1 ? launch<false, true, true>(tq, tk, tv, a, grid, st)
-                            : launch<false, true, false>(tq, tk, tv, a, grid, st);
-    return launch<false, false, true>(tq, tk, tv, a, grid, st);
+    return split ? launch<false, true, true>(tq, tk, tv, a, grid, st)
+                 : launch<false, true, false>(tq, tk, tv, a, grid, st);
+}
+
+// Workspace of a launch's plan.
+size_t workspace(int nseq, int Nq, int Nk, int heads, bool all_split)
+{
+    if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0)
+        return 0;
+    AttnArgs a;
+    const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
+    return plan(a, base, (Nk + BKV - 1) / BKV, device_sms(), all_split);
 }
 
 }  // namespace
 }  // namespace sam3
 
+extern "C" size_t k_attn_tc_workspace(int nseq, int N, int heads)
+{
+    return sam3::workspace(nseq, N, N, heads, false);
+}
+
 extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
-                         void *out, int out_bf16, int *err, k_stream s)
+                         void *out, int out_bf16, void *ws, size_t ws_bytes, int *err, k_stream s)
 {
     using namespace sam3;
     if (nseq <= 0 || N <= 0 || heads <= 0 || E != heads * HD || (reinterpret_cast<uintptr_t>(out) & 15))
@@ -662,20 +749,14 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = out;
     a.bias = nullptr;
-    a.part = nullptr;
-    a.nsplit = 1;
     a.err = err;
-    return run(tq, tkv, tkv, a, out_bf16 != 0, reinterpret_cast<cudaStream_t>(s));
+    return run(tq, tkv, tkv, a, out_bf16 != 0, false, ws, ws_bytes,
+               reinterpret_cast<cudaStream_t>(s));
 }
 
 extern "C" size_t k_attn_tc_cross_workspace(int nseq, int Nq, int Nk, int heads)
 {
-    using namespace sam3;
-    if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0)
-        return 0;
-    const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
-    const int nsplit = pick_split(base, (Nk + BKV - 1) / BKV, device_sms());
-    return nsplit > 1 ? (size_t)base * nsplit * BQ * kPartRow * sizeof(float) : 0;
+    return sam3::workspace(nseq, Nq, Nk, heads, true);
 }
 
 extern "C" int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
@@ -706,14 +787,5 @@ extern "C" int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk,
     a.out = out;
     a.bias = bias;
     a.err = err;
-    const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
-    a.nsplit = pick_split(base, (Nk + BKV - 1) / BKV, device_sms());
-    a.part = nullptr;
-    if (a.nsplit > 1) {
-        if (!ws || ws_bytes < k_attn_tc_cross_workspace(nseq, Nq, Nk, heads) ||
-            (reinterpret_cast<uintptr_t>(ws) & 15))
-            return K_EARG;
-        a.part = static_cast<float *>(ws);
-    }
-    return run(tq, tk, tv, a, out_bf16 != 0, reinterpret_cast<cudaStream_t>(s));
+    return run(tq, tk, tv, a, out_bf16 != 0, true, ws, ws_bytes, reinterpret_cast<cudaStream_t>(s));
 }

@@ -77,21 +77,27 @@ int k_gemm_simt(int M, int N, int K, const void *A, int adt, long aoff, int lda,
  * applied), out: [nseq * N, E] fp32 or bf16. scale multiplies the scores
  * (1/sqrt(hd)). hd must be 64; E % 64 == 0. */
 int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
-              void *out, int out_bf16, int *err, k_stream s);
+              void *out, int out_bf16, void *ws, size_t ws_bytes, int *err,
+              k_stream s);
+/* Workspace with which k_attn_tc splits the KV range of the items that do
+ * not fill the last wave of CTAs (0: no split planned; launches of many
+ * waves never split). With a smaller ws, or NULL, the kernel runs whole
+ * items: same results up to rounding, slower tail. */
+size_t k_attn_tc_workspace(int nseq, int N, int heads);
 
 /* The same kernel for cross-attention: nseq sequences of Nq query rows of
  * Q and Nk key / value rows of K and V (bf16, leading dimensions ldq / ldk /
  * ldv in elements, head h at column 64 h, 16-byte aligned rows), out rows
  * seq * Nq + q with leading dimension ldo (head h at column 64 h), fp32
- * (bf16 only without a bias and without a key split). bias: NULL, or fp32
- * [nseq, heads, Nq, Nk] added to the scaled scores, in log2 units
- * (natural-log bias x log2 e). */
+ * (bf16 only without a bias). bias: NULL, or fp32 [nseq, heads, Nq, Nk]
+ * added to the scaled scores, in log2 units (natural-log bias x log2 e). */
 int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
                     long ldv, int nseq, int Nq, int Nk, int heads, float scale,
                     const float *bias, void *out, long ldo, int out_bf16, void *ws,
                     size_t ws_bytes, int *err, k_stream s);
-/* Device workspace k_attn_tc_cross needs (0 when the query tiles fill the
- * GPU; otherwise the keys are split and the partial results merged). */
+/* Device workspace k_attn_tc_cross needs to split the keys of its items
+ * over CTAs and merge the partial results (0: no split planned); with less,
+ * the items run whole. */
 size_t k_attn_tc_cross_workspace(int nseq, int Nq, int Nk, int heads);
 
 /* The same attention in fp32 on CUDA cores (reference mode): qkv fp32. */

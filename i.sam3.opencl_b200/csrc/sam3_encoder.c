@@ -494,7 +494,8 @@ static int run_blocks(cb_encoder *e, int ntile, int first, int last)
                               b->num_sms, st));
         LAUNCH(global ? "attn_global" : "attn_window",
                4.0 * nseq * heads * (double)N * N * e->hd, R * 4 * dE * 2,
-               k_attn_tc(e->qkv, nseq, N, E, heads, scale, e->attn, 1, b->d_err, st));
+               k_attn_tc(e->qkv, nseq, N, E, heads, scale, e->attn, 1, NULL, 0, b->d_err,
+                         st));  /* whole items: a tile's result never depends on its batch */
         LAUNCH("gemm_proj", 2 * R * dE * dE, R * dE * 2 + dE * dE * 2 + R * dE * 8,
                k_gemm_bf16_tc(rows, E, E, e->attn, E, k->projw, E, e->x, E, 0, k->projb,
                               e->x, E, 0, 1.0f, K_ACT_NONE, NULL, b->d_err, b->num_sms,

@@ -274,9 +274,11 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
     if (mode != CB_ATTN_TC || (out->dtype != CB_F32 && out->dtype != CB_BF16))
         return cbi_fail(b, CB_EARG, "attention: mode");
     if (qkv->dtype == CB_F32) {
+        const size_t copy = ((size_t)rows * 3 * E * 2 + 255) & ~(size_t)255;
+        const size_t wsb = k_attn_tc_workspace(nseq, N, heads);
         void *s = NULL;
 
-        CB_TRY(cbi_scratch(b, (size_t)rows * 3 * E * 2, &s));
+        CB_TRY(cbi_scratch(b, copy + wsb, &s));
         if (cs)
             CB_TRY(cbi_kstatus(b,
                               k_rope_cast_bf16((const float *)qkv->ptr,
@@ -292,17 +294,24 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
                               "attention: cast"));
         return cbi_kstatus(b,
                           k_attn_tc(s, nseq, N, E, heads, scale, out->ptr,
-                                    out->dtype == CB_BF16, b->d_err,
-                                    (k_stream)b->stream),
+                                    out->dtype == CB_BF16, (char *)s + copy, wsb,
+                                    b->d_err, (k_stream)b->stream),
                           "attention (tcgen05)");
     }
     if (qkv->dtype != CB_BF16 || cs)
         return cbi_fail(b, CB_EDTYPE, "attention: bf16 qkv must be pre-roped");
-    return cbi_kstatus(b,
-                      k_attn_tc(qkv->ptr, nseq, N, E, heads, scale, out->ptr,
-                                out->dtype == CB_BF16, b->d_err,
-                                (k_stream)b->stream),
-                      "attention (tcgen05)");
+    {
+        const size_t wsb = k_attn_tc_workspace(nseq, N, heads);
+        void *ws = NULL;
+
+        if (wsb)
+            CB_TRY(cbi_scratch(b, wsb, &ws));
+        return cbi_kstatus(b,
+                          k_attn_tc(qkv->ptr, nseq, N, E, heads, scale, out->ptr,
+                                    out->dtype == CB_BF16, ws, wsb, b->d_err,
+                                    (k_stream)b->stream),
+                          "attention (tcgen05)");
+    }
 }
 
 int cb_mha(cb_backend *b, int P, int Nq, int Nk, int dint, cb_mem qp,
@@ -398,9 +407,10 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
         aligned16(Q->ptr) && aligned16(K->ptr) && aligned16(V->ptr) && aligned16(O->ptr)) {
         /* tensor cores: heads zero-padded to 64 columns in bf16 */
         const size_t packed = (size_t)Nq * 3 * heads * 64 * 2, out = (size_t)Nq * heads * 64 * 4;
+        const size_t wsb = k_attn_tc_workspace(1, Nq, heads);
         char *s = NULL;
 
-        CB_TRY(cbi_scratch(b, packed + out, (void **)&s));
+        CB_TRY(cbi_scratch(b, packed + out + wsb, (void **)&s));
         CB_TRY(cbi_kstatus(b,
                            k_pack_qkv_pad64((const float *)Q->ptr, ldq, (const float *)K->ptr,
                                             ldk, (const float *)V->ptr, ldv, Nq, heads, hd, s,
@@ -408,7 +418,8 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
                            "attend: pack"));
         CB_TRY(cbi_kstatus(b,
                            k_attn_tc(s, 1, Nq, heads * 64, heads, 1.0f / sqrtf((float)hd),
-                                     s + packed, 0, b->d_err, st),
+                                     s + packed, 0, wsb ? s + packed + out : NULL, wsb,
+                                     b->d_err, st),
                            "attend"));
         return cbi_kstatus(b,
                            k_unpack_heads64((const float *)(s + packed), Nq, heads, hd,
