@@ -561,48 +561,61 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
 // Merges the tsplit partial results of each tail item's query rows:
 // O = sum_p O_p 2^(m_p - M) / sum_p l_p 2^(m_p - M), M = max_p m_p. One
-// thread per (tail item, row, 4 output columns).
+// warp per (tail item, row): the lanes first take the parts' offsets and
+// sums (lane = part), then two output columns each, reading every part's
+// row as one coalesced 256-byte load with the part's weight shuffled in.
 template <bool OUT_BF16>
 __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ part, AttnArgs a,
                                                       int ntail)
 {
-    const long n = (long)ntail * BQ * (HD / 4);
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (long)gridDim.x * blockDim.x) {
-        const int d = (int)(i % (HD / 4)) * 4;
-        const int r = (int)((i / (HD / 4)) % BQ);
-        const long t = i / ((HD / 4) * BQ);
+    static_assert(HD == 64, "two output columns per lane");
+    const int lane = threadIdx.x & 31;
+    const long nrows = (long)ntail * BQ, pstride = (long)BQ * kPartRow;
+    for (long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < nrows;
+         w += ((long)gridDim.x * blockDim.x) >> 5) {
+        const int r = (int)(w % BQ);
+        const long t = w / BQ;
         const long item = a.nfull + t;
         const int qt = (int)(item % a.nqt), head = (int)((item / a.nqt) % a.heads);
         const int seq = (int)(item / ((long)a.nqt * a.heads));
         const int q = qt * BQ + r;
         if (q >= a.Nq)
-            continue;
+            continue;  // warp-uniform
         const float *p0 = part + ((t * a.tsplit) * BQ + r) * kPartRow;
         float M = -INFINITY;
-        for (int sp = 0; sp < a.tsplit; sp++)
-            M = fmaxf(M, p0[(long)sp * BQ * kPartRow + HD]);
-        float L = 0.0f;
-        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int sp = 0; sp < a.tsplit; sp++) {
-            const float *ps = p0 + (long)sp * BQ * kPartRow;
-            const float f = exp2f(ps[HD] - M);
-            L = fmaf(ps[HD + 1], f, L);
-            const float4 v = *reinterpret_cast<const float4 *>(ps + d);
-            o.x = fmaf(v.x, f, o.x);
-            o.y = fmaf(v.y, f, o.y);
-            o.z = fmaf(v.z, f, o.z);
-            o.w = fmaf(v.w, f, o.w);
+        for (int sp = lane; sp < a.tsplit; sp += 32)
+            M = fmaxf(M, p0[sp * pstride + HD]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f, ox = 0.0f, oy = 0.0f;
+        for (int s0 = 0; s0 < a.tsplit; s0 += 32) {
+            const int sl = s0 + lane;
+            const float2 ml = sl < a.tsplit ? *reinterpret_cast<const float2 *>(p0 + sl * pstride + HD)
+                                            : make_float2(-INFINITY, 0.0f);
+            const float fl = sl < a.tsplit ? exp2f(ml.x - M) : 0.0f;
+            L = fmaf(ml.y, fl, L);
+            const int n = min(32, a.tsplit - s0);
+            const float *pc = p0 + s0 * pstride + 2 * lane;
+#pragma unroll 4
+            for (int j = 0; j < n; j++) {
+                const float f = __shfl_sync(0xffffffffu, fl, j);
+                const float2 v = *reinterpret_cast<const float2 *>(pc + j * pstride);
+                ox = fmaf(v.x, f, ox);
+                oy = fmaf(v.y, f, oy);
+            }
         }
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+            L += __shfl_xor_sync(0xffffffffu, L, o);
         const float inv = 1.0f / L;
-        const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD + d;
-        if (OUT_BF16) {
-            uint2 w = make_uint2(pack_bf16x2(o.x * inv, o.y * inv), pack_bf16x2(o.z * inv, o.w * inv));
-            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + orow) = w;
-        }
+        const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD + 2 * lane;
+        if (OUT_BF16)
+            *reinterpret_cast<uint32_t *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + orow) =
+                pack_bf16x2(ox * inv, oy * inv);
         else
-            *reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.out) + orow) =
-                make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+            *reinterpret_cast<float2 *>(reinterpret_cast<float *>(a.out) + orow) =
+                make_float2(ox * inv, oy * inv);
     }
 }
 
@@ -618,7 +631,7 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, 
     if (e != cudaSuccess || !SPLIT)
         return (int)e;
     const int ntail = (a.nitems - a.nfull) / a.tsplit;
-    const long n = (long)ntail * BQ * (HD / 4);
+    const long n = (long)ntail * BQ * 32;  // a warp per row
     const long blocks = (n + 255) / 256;
     combine_kernel<OUT_BF16><<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(
         a.part, a, ntail);

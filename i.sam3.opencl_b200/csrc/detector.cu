@@ -8,10 +8,16 @@
 //     the tcgen05 flash kernel (attn_tc.cu), then the 32 real columns of each
 //     head are written back in fp32. The padding doubles the tensor-core
 //     work of a kernel whose softmax, not its tensor core, is the bound;
-//   - everything else (the decoder's 201 queries over the image with the
-//     box bias, the prompt cross-attention, the causal text encoder): an
-//     fp32 flash kernel on the CUDA cores with the keys split over CTAs
-//     (online softmax per split, merged by a combine kernel).
+//   - cross-attention over the image (at least 1024 keys, no causal mask:
+//     the decoder's 201 queries with or without the box bias): q, k and v
+//     padded the same way and run through the cross form of the tcgen05
+//     kernel, the box bias expanded by rpb_bias_kernel into a dense fp32
+//     term that the kernel adds to the scaled scores, keys split over CTAs
+//     when the queries alone do not fill the GPU;
+//   - everything else (the prompt cross-attention, the causal text
+//     encoder, the fp32 mode): an fp32 flash kernel on the CUDA cores with
+//     the keys split over CTAs (online softmax per split, merged by a
+//     combine kernel).
 #include "kernels.h"
 
 #include <cuda_bf16.h>
@@ -99,22 +105,37 @@ __global__ void __launch_bounds__(256) pad_heads_kernel(const void *__restrict__
 // SAM 3's box relative position bias of softmax_ext (sam3_kernels.cl:
 // 890-921) as a dense [heads, Nq, Nk] term for the tensor-core attention, in
 // log2 units: bias[(h Nq + i) Nk + j] = (dy[(i H + y) nh + h] + dx[(i W +
-// x) nh + h]) log2 e for key j = y W + x.
+// x) nh + h]) log2 e for key j = y W + x. One CTA per (head, query) row:
+// the row's H + W terms (strided by nh in dy / dx) are gathered into
+// shared memory once, then the Nk outputs are written 4 at a time (W a
+// multiple of 4 keeps the 4 keys of a store in one y) - a write-bound pass.
 __global__ void __launch_bounds__(256) rpb_bias_kernel(const float *__restrict__ dy,
                                                        const float *__restrict__ dx, int Nq,
                                                        int Nk, int W, int heads,
                                                        float *__restrict__ bias)
 {
+    extern __shared__ float rpb_s[];  // [H] dy terms, then [W] dx terms
     const int H = Nk / W;
-    const long n = (long)heads * Nq * Nk;
-    for (long t = (long)blockIdx.x * blockDim.x + threadIdx.x; t < n;
-         t += (long)gridDim.x * blockDim.x) {
-        const int j = (int)(t % Nk);
-        const long hi = t / Nk;
-        const int i = (int)(hi % Nq), h = (int)(hi / Nq);
-        const int y = j / W, x = j - y * W;
-        bias[t] = (__ldg(dy + ((long)i * H + y) * heads + h) + __ldg(dx + ((long)i * W + x) * heads + h)) *
-                  1.4426950408889634f;
+    const int h = blockIdx.x / Nq, i = blockIdx.x - h * Nq;
+    float *dys = rpb_s, *dxs = rpb_s + H;
+    for (int t = threadIdx.x; t < H + W; t += blockDim.x)
+        rpb_s[t] = t < H ? __ldg(dy + ((long)i * H + t) * heads + h) * 1.4426950408889634f
+                         : __ldg(dx + ((long)i * W + (t - H)) * heads + h) * 1.4426950408889634f;
+    __syncthreads();
+    float *row = bias + (long)blockIdx.x * Nk;
+    if (!(W & 3) && !(reinterpret_cast<uintptr_t>(row) & 15)) {
+        float4 *row4 = reinterpret_cast<float4 *>(row);
+        for (int j4 = threadIdx.x; j4 < Nk / 4; j4 += blockDim.x) {
+            const int y = (4 * j4) / W, x = 4 * j4 - y * W;
+            const float b = dys[y];
+            row4[j4] = make_float4(b + dxs[x], b + dxs[x + 1], b + dxs[x + 2], b + dxs[x + 3]);
+        }
+    }
+    else {
+        for (int j = threadIdx.x; j < Nk; j += blockDim.x) {
+            const int y = j / W;
+            row[j] = dys[y] + dxs[j - y * W];
+        }
     }
 }
 
@@ -292,9 +313,11 @@ extern "C" int k_rpb_bias(const float *dy, const float *dx, int Nq, int Nk, int 
 {
     if (Nq <= 0 || Nk <= 0 || W <= 0 || Nk % W || heads <= 0)
         return K_EARG;
-    const int grid = grid_for((long)heads * Nq * Nk, 256);
-    rpb_bias_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(dy, dx, Nq, Nk, W,
-                                                                             heads, bias);
+    const long rows = (long)heads * Nq;
+    const size_t smem = (size_t)(Nk / W + W) * sizeof(float);
+    if (rows > 0x7fffffffL || smem > 48 * 1024)
+        return K_EARG;
+    rpb_bias_kernel<<<(int)rows, 256, smem, STREAM(s)>>>(dy, dx, Nq, Nk, W, heads, bias);
     return (int)cudaGetLastError();
 }
 

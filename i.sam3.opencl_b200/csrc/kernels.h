@@ -237,7 +237,8 @@ int k_attend_splits(int Nq, int Nk, int heads, int num_sms);
 /* pad_heads64: one attention operand, fp32 or bf16 (src_bf16) [rows, ld],
  * head h at column h * hd -> bf16 [rows, heads * 64], columns hd..63 of
  * each head zero. rpb_bias: the box relative position bias of softmax_ext
- * as fp32 [heads, Nq, Nk] in log2 units (k_attn_tc_cross's bias). */
+ * as fp32 [heads, Nq, Nk] in log2 units (k_attn_tc_cross's bias);
+ * K_EARG unless W divides Nk and Nk / W + W <= 12288. */
 int k_pad_heads64(const void *src, int src_bf16, long ld, long rows, int heads, int hd,
                   void *out, k_stream s);
 int k_rpb_bias(const float *dy, const float *dx, int Nq, int Nk, int W, int heads,

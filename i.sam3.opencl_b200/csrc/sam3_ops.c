@@ -426,9 +426,11 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
                                             (float *)O->ptr, ldo, st),
                            "attend: unpack");
     }
+    /* (k_rpb_bias stages a row's Nk / W + W bias terms in 48 KB of shared
+     * memory) */
     if (mode == CB_ATTN_TC && !causal && Nk >= 1024 && ldq % 4 == 0 && ldk % 4 == 0 &&
         ldv % 4 == 0 && ldo % 4 == 0 && aligned16(Q->ptr) && aligned16(K->ptr) &&
-        aligned16(V->ptr) && aligned16(O->ptr)) {
+        aligned16(V->ptr) && aligned16(O->ptr) && (!dy || Nk / W + W <= 12288)) {
         /* tensor cores for queries over many keys, with or without the box
          * bias: Q, K, V padded to 64-column heads in bf16, the bias as a
          * dense [heads, Nq, Nk] term, keys split over CTAs when the query
