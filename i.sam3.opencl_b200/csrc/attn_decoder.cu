@@ -15,19 +15,21 @@
 //   (two passes for up to 8 keys, online beyond);
 //
 //   many keys (Nk > 64, c = 16: token-to-image; attn_manykeys,
-//   sam3_kernels.cl:577-633): the keys are split over `nsplit` CTAs per
-//   prompt so that every SM streams K/V (a prompt's K/V is 2.6 MB); a CTA
-//   (one split of one prompt, for 8 of its queries) pulls 32-key chunks of K
-//   and V with cp.async through a 3-stage ring while its 256 threads (32
-//   (query pair, head) items x 8 key lanes, each K/V read serving two
-//   queries) run a blocked online softmax over the oldest chunk, merges its
-//   key lanes and writes one (m, l, o) partial per (query, head); a second
-//   kernel combines the splits.
+//   sam3_kernels.cl:577-633): the prompts' 32-key chunks form one sequence
+//   cut into equal ranges, one per CTA slot (two per SM), so that every SM
+//   streams K/V (a prompt's K/V is 2.6 MB in fp32); a CTA (one range, for 8
+//   queries) pulls the chunks of K and V with cp.async through a 3-stage
+//   ring while its 256 threads (32 (query pair, head) items x 8 key lanes,
+//   each K/V read serving two queries) run a blocked online softmax over the
+//   oldest chunk with packed f32x2 arithmetic; at the end of each prompt in
+//   its range it merges its key lanes and writes one (m, l, o) partial per
+//   (query, head); a second kernel combines the partials of each prompt.
 //
 // The 8 different heads a warp reads at once fall on distinct shared-memory
 // bank groups: rows padded to c + 4 floats per head (few keys) or 16-byte
 // chunks rotated per head (many keys, rows stay 512 bytes for cp.async).
 #include "kernels.h"
+#include "tc_ptx.cuh"
 #include "tmap.cuh"
 
 #include <cuda_bf16.h>
@@ -421,56 +423,65 @@ __device__ __forceinline__ int many_pos_bf16(int h, int half)
     return h * 32 + ((half ^ (h >> 2)) & 1) * 16;
 }
 
-// Eight bf16 values (one 16-byte piece) widened to fp32.
-__device__ __forceinline__ void widen8(const uint4 w, float (&f)[8])
+// Eight bf16 values (one 16-byte piece) widened to fp32 as four pairs
+// (channels 2k, 2k + 1 in pair k) for the packed arithmetic.
+__device__ __forceinline__ void widen8x2(const uint4 w, uint64_t (&f)[4])
 {
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        f[2 * k] = __uint_as_float(ws[k] << 16);
-        f[2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
-    }
+    for (int k = 0; k < 4; k++)
+        f[k] = f2_make(__uint_as_float(ws[k] << 16), __uint_as_float(ws[k] & 0xffff0000u));
+}
+
+// Work of the many-keys kernel: the P prompts' 32-key chunks taken as one
+// sequence of T = P * nch chunks, CTA g of G doing chunks [g T / G,
+// (g + 1) T / G) (whole prompts' shares differ by at most one chunk, and
+// every SM slot gets one CTA). A CTA's range crosses at most `segs` prompts;
+// it writes one partial per (prompt segment, query, head).
+__host__ __device__ __forceinline__ long many_chunk0(long g, long T, long G)
+{
+    return g * T / G;
 }
 
 // KV_BF16: K and V are bf16 rows (as the decoder's projections write them);
-// staged the same way in half the shared memory and widened on read.
+// staged the same way in half the shared memory and widened on read. The
+// dot products and P.V updates use the packed f32x2 instructions on channel
+// pairs, with the same four partial sums per score and the same
+// accumulation order as the scalar form.
 template <bool KV_BF16>
 __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
     const float *__restrict__ Q, long sq, const void *__restrict__ Kv, long sk,
-    const void *__restrict__ Vv, long sv, float *__restrict__ part, int Nq, int Nk,
-    int keys_per_split, float scale)
+    const void *__restrict__ Vv, long sv, float *__restrict__ part, int P, int Nq, int Nk,
+    int segs, float scale)
 {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     constexpr int ROWF = KV_BF16 ? kManyRow / 2 : kManyRow;  // staged row, in floats
-    float *ks = sm;                                     // [kStages][kChunk][ROWF]
-    float *vs = sm + kStages * kChunk * ROWF;           // [kStages][kChunk][ROWF]
-    const float *K = reinterpret_cast<const float *>(Kv);
-    const float *V = reinterpret_cast<const float *>(Vv);
-    const int split = blockIdx.x, nsplit = gridDim.x;
-    const long p = blockIdx.y;
+    constexpr int BUF = 2 * kChunk * ROWF;                   // one stage: K rows, then V rows
+    const int nch = (Nk + kChunk - 1) / kChunk;
+    const long T = (long)P * nch, G = gridDim.x;
+    const long c0 = many_chunk0(blockIdx.x, T, G), c1 = many_chunk0(blockIdx.x + 1, T, G);
+    const int nloc = (int)(c1 - c0);
+    const long p_first = c0 / nch;
     // Thread = (query pair, head, key lane): queries qg and qg + 4 of the
     // CTA's 8 share every K/V read from shared memory; a warp is one key lane.
     const int h = threadIdx.x & 7, qg = (threadIdx.x >> 3) & 3, lane = threadIdx.x >> 5;
     const int qa = blockIdx.z * 8 + qg, qb = qa + 4;
-    const int k0 = split * keys_per_split;
-    const int k1 = min(Nk, k0 + keys_per_split);
-    const int nchunk = k1 > k0 ? (k1 - k0 + kChunk - 1) / kChunk : 0;
-    const char *kb = reinterpret_cast<const char *>(Kv) + p * sk * (KV_BF16 ? 2 : 4);
-    const char *vb = reinterpret_cast<const char *>(Vv) + p * sv * (KV_BF16 ? 2 : 4);
-    (void)K;
-    (void)V;
 
-    // Chunk c of this split into buffer b: 16-byte pieces into rotated rows.
-    auto stage = [&](int c, int b) {
-        const int j0 = k0 + c * kChunk, n = min(kChunk, k1 - j0);
+    // Chunk i of this CTA's range into stage b: 16-byte pieces into rotated rows.
+    auto stage = [&](int i, int b) {
+        const long idx = c0 + i, p = idx / nch;
+        const int j0 = (int)(idx - p * nch) * kChunk, n = min(kChunk, Nk - j0);
+        const char *kb = reinterpret_cast<const char *>(Kv) + p * sk * (KV_BF16 ? 2 : 4);
+        const char *vb = reinterpret_cast<const char *>(Vv) + p * sv * (KV_BF16 ? 2 : 4);
+        float *ks = sm + b * BUF, *vs = ks + kChunk * ROWF;
         constexpr int PIECES = kManyD * (KV_BF16 ? 2 : 4) / 16;  // per key row
-        for (int i = threadIdx.x; i < n * PIECES; i += blockDim.x) {
-            const int j = i / PIECES, pc = i - j * PIECES;
+        for (int t = threadIdx.x; t < n * PIECES; t += blockDim.x) {
+            const int j = t / PIECES, pc = t - j * PIECES;
             int dst;  // in floats
             if (KV_BF16)
-                dst = (b * kChunk + j) * ROWF + many_pos_bf16(pc >> 1, pc & 1) / 4;
+                dst = j * ROWF + many_pos_bf16(pc >> 1, pc & 1) / 4;
             else
-                dst = (b * kChunk + j) * ROWF + many_pos(pc / 4, pc % 4);
+                dst = j * ROWF + many_pos(pc / 4, pc % 4);
             const long src = ((long)(j0 + j) * PIECES + pc) * 16;  // bytes
             cp_async16(ks + dst, kb + src);
             cp_async16(vs + dst, vb + src);
@@ -478,42 +489,102 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
         cp_async_commit();
     };
 
-    float q[2][kManyC];
+    uint64_t q2[2][kManyC / 2], o2[2][kManyC / 2];
+    float m[2], l[2];
+    auto start_segment = [&](long p) {
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const int qq = (u ? qb : qa) < Nq ? (u ? qb : qa) : 0;
-        const float4 *qp =
-            reinterpret_cast<const float4 *>(Q + p * sq + (long)qq * kManyD + h * kManyC);
+        for (int u = 0; u < 2; u++) {
+            const int qq = (u ? qb : qa) < Nq ? (u ? qb : qa) : 0;
+            const float4 *qp =
+                reinterpret_cast<const float4 *>(Q + p * sq + (long)qq * kManyD + h * kManyC);
 #pragma unroll
-        for (int c = 0; c < kManyC / 4; c++) {
-            const float4 v = __ldg(qp + c);
-            q[u][4 * c] = v.x * scale;
-            q[u][4 * c + 1] = v.y * scale;
-            q[u][4 * c + 2] = v.z * scale;
-            q[u][4 * c + 3] = v.w * scale;
+            for (int c = 0; c < kManyC / 4; c++) {
+                const float4 v = __ldg(qp + c);
+                q2[u][2 * c] = f2_make(v.x * scale, v.y * scale);
+                q2[u][2 * c + 1] = f2_make(v.z * scale, v.w * scale);
+            }
+            m[u] = -INFINITY;
+            l[u] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kManyC / 2; c++)
+                o2[u][c] = 0;
         }
-    }
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, o[2][kManyC];
+    };
+    // Merges the 8 key lanes of each (query, head) through stage b (free
+    // when this runs: its chunk is consumed and the next one is not yet
+    // requested) and writes segment k's partials; one query half per pass.
+    auto flush = [&](int b, long k) {
+        float *mer = sm + b * BUF;  // [7 lanes][32 (query, head)][kPart]
+        static_assert(7 * 32 * kPart <= (KV_BF16 ? 2 * kChunk * kManyRow / 2 : 2 * kChunk * kManyRow),
+                      "lane records fit in one stage");
 #pragma unroll
-    for (int c = 0; c < kManyC; c++)
-        o[0][c] = o[1][c] = 0.0f;
-    // Ring of kStages chunks: chunks c+1 and c+2 load while c computes (an
+        for (int u = 0; u < 2; u++) {  // unrolled: o2, m, l stay in registers
+            const int slot = qg * kHeads + h;
+            if (lane > 0) {
+                float *mine = mer + ((lane - 1) * 32 + slot) * kPart;
+                mine[0] = m[u];
+                mine[1] = l[u];
+#pragma unroll
+                for (int c = 0; c < kManyC / 2; c++)
+                    f2_split(o2[u][c], mine[2 + 2 * c], mine[3 + 2 * c]);
+            }
+            __syncthreads();
+            const int qi = u ? qb : qa;
+            if (lane == 0 && qi < Nq) {
+                float M = m[u];
+                for (int t = 0; t < kLanes - 1; t++)
+                    M = fmaxf(M, mer[(t * 32 + slot) * kPart]);
+                float acc[kManyC];
+                const float f0 = m[u] == -INFINITY ? 0.0f : __expf(m[u] - M);
+                float L = l[u] * f0;
+#pragma unroll
+                for (int c = 0; c < kManyC / 2; c++) {
+                    float a0, a1;
+                    f2_split(o2[u][c], a0, a1);
+                    acc[2 * c] = a0 * f0;
+                    acc[2 * c + 1] = a1 * f0;
+                }
+                for (int t = 0; t < kLanes - 1; t++) {
+                    const float *pt = mer + (t * 32 + slot) * kPart;
+                    const float f = pt[0] == -INFINITY ? 0.0f : __expf(pt[0] - M);
+                    L += pt[1] * f;
+#pragma unroll
+                    for (int cc = 0; cc < kManyC; cc++)
+                        acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
+                }
+                float *dst = part + (((blockIdx.x * (long)segs + k) * Nq + qi) * kHeads + h) * kPart;
+                dst[0] = M;
+                dst[1] = L;
+#pragma unroll
+                for (int cc = 0; cc < kManyC; cc++)
+                    dst[2 + cc] = acc[cc];
+            }
+            __syncthreads();
+        }
+    };
+
+    // Ring of kStages chunks: chunks i+1 and i+2 load while i computes (an
     // empty commit group keeps the wait count uniform at the tail).
-    for (int c = 0; c < kStages - 1; c++) {
-        if (c < nchunk)
-            stage(c, c);
+    for (int i = 0; i < kStages - 1; i++) {
+        if (i < nloc)
+            stage(i, i);
         else
             cp_async_commit();
     }
-    for (int c = 0; c < nchunk; c++) {
-        const int b = c % kStages;
-        if (c + kStages - 1 < nchunk)  // its buffer was released by the barrier below
-            stage(c + kStages - 1, (c + kStages - 1) % kStages);
+    for (int i = 0; i < nloc; i++) {
+        const int b = i % kStages;
+        const long idx = c0 + i, p = idx / nch;
+        const int ci = (int)(idx - p * nch);
+        if (i == 0 || ci == 0)
+            start_segment(p);
+        if (i + kStages - 1 < nloc)  // its stage was released by the barrier below
+            stage(i + kStages - 1, (i + kStages - 1) % kStages);
         else
             cp_async_commit();
         cp_async_wait<kStages - 1>();
         __syncthreads();
-        const int n = min(kChunk, k1 - (k0 + c * kChunk));
+        const float *ks = sm + b * BUF, *vs = ks + kChunk * ROWF;
+        const int n = min(kChunk, Nk - ci * kChunk);
         // This lane's keys of the chunk as one block per query: scores, block
         // maximum, one correction, then P.V.
         constexpr int KT = kChunk / kLanes;
@@ -524,43 +595,46 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
             const int j = t * kLanes + lane;
             s[0][t] = s[1][t] = -INFINITY;
             if (j < n) {
-                const float *kr = ks + (b * kChunk + j) * ROWF;
-                float d[2][4] = {};
+                const float *kr = ks + j * ROWF;
+                uint64_t dA[2] = {0, 0}, dB[2] = {0, 0};  // channel pairs (4c, 4c+1), (4c+2, 4c+3)
                 if (KV_BF16) {
 #pragma unroll
                     for (int hf = 0; hf < 2; hf++) {
-                        float kv[8];
-                        widen8(*reinterpret_cast<const uint4 *>(
-                                   reinterpret_cast<const char *>(kr) + many_pos_bf16(h, hf)),
-                               kv);
+                        uint64_t kv[4];
+                        widen8x2(*reinterpret_cast<const uint4 *>(
+                                     reinterpret_cast<const char *>(kr) + many_pos_bf16(h, hf)),
+                                 kv);
 #pragma unroll
-                        for (int t = 0; t < 8; t++)
-#pragma unroll
-                            for (int u = 0; u < 2; u++)
-                                d[u][t & 3] = fmaf(q[u][8 * hf + t], kv[t], d[u][t & 3]);
+                        for (int u = 0; u < 2; u++) {
+                            dA[u] = fma2(q2[u][4 * hf], kv[0], dA[u]);
+                            dB[u] = fma2(q2[u][4 * hf + 1], kv[1], dB[u]);
+                            dA[u] = fma2(q2[u][4 * hf + 2], kv[2], dA[u]);
+                            dB[u] = fma2(q2[u][4 * hf + 3], kv[3], dB[u]);
+                        }
                     }
                 }
                 else
 #pragma unroll
                 for (int cc = 0; cc < kManyC / 4; cc++) {
-                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + many_pos(h, cc));
+                    const ulonglong2 k2 = *reinterpret_cast<const ulonglong2 *>(kr + many_pos(h, cc));
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
-                        d[u][0] = fmaf(q[u][4 * cc], k4.x, d[u][0]);
-                        d[u][1] = fmaf(q[u][4 * cc + 1], k4.y, d[u][1]);
-                        d[u][2] = fmaf(q[u][4 * cc + 2], k4.z, d[u][2]);
-                        d[u][3] = fmaf(q[u][4 * cc + 3], k4.w, d[u][3]);
+                        dA[u] = fma2(q2[u][2 * cc], k2.x, dA[u]);
+                        dB[u] = fma2(q2[u][2 * cc + 1], k2.y, dB[u]);
                     }
                 }
 #pragma unroll
                 for (int u = 0; u < 2; u++) {
-                    s[u][t] = (d[u][0] + d[u][1]) + (d[u][2] + d[u][3]);
+                    float d0, d1, d2, d3;
+                    f2_split(dA[u], d0, d1);
+                    f2_split(dB[u], d2, d3);
+                    s[u][t] = (d0 + d1) + (d2 + d3);
                     bm[u] = fmaxf(bm[u], s[u][t]);
                 }
             }
         }
         if (bm[0] > -INFINITY) {  // the key count is the same for both queries
-            float e[2][KT];
+            uint64_t e2[2][KT];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 // The running maximum is raised (and o, l rescaled) only when
@@ -570,101 +644,62 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
                 if (bm[u] > m[u] + kManyLazy) {
                     const float corr = __expf(m[u] - bm[u]);  // 0 on the first block
                     l[u] *= corr;
+                    const uint64_t c2 = f2_make(corr, corr);
 #pragma unroll
-                    for (int cc = 0; cc < kManyC; cc++)
-                        o[u][cc] *= corr;
+                    for (int cc = 0; cc < kManyC / 2; cc++)
+                        o2[u][cc] = mul2(o2[u][cc], c2);
                     m[u] = bm[u];
                 }
 #pragma unroll
                 for (int t = 0; t < KT; t++) {
-                    e[u][t] = __expf(s[u][t] - m[u]);  // 0 for keys past the chunk
-                    l[u] += e[u][t];
+                    const float e = __expf(s[u][t] - m[u]);  // 0 for keys past the chunk
+                    l[u] += e;
+                    e2[u][t] = f2_make(e, e);
                 }
             }
 #pragma unroll
             for (int t = 0; t < KT; t++) {
                 const int j = t * kLanes + lane;
                 if (j < n) {
-                    const float *vr = vs + (b * kChunk + j) * ROWF;
+                    const float *vr = vs + j * ROWF;
                     if (KV_BF16) {
 #pragma unroll
                         for (int hf = 0; hf < 2; hf++) {
-                            float vv[8];
-                            widen8(*reinterpret_cast<const uint4 *>(
-                                       reinterpret_cast<const char *>(vr) + many_pos_bf16(h, hf)),
-                                   vv);
+                            uint64_t vv[4];
+                            widen8x2(*reinterpret_cast<const uint4 *>(
+                                         reinterpret_cast<const char *>(vr) + many_pos_bf16(h, hf)),
+                                     vv);
 #pragma unroll
-                            for (int ci = 0; ci < 8; ci++)
+                            for (int ci2 = 0; ci2 < 4; ci2++)
 #pragma unroll
                                 for (int u = 0; u < 2; u++)
-                                    o[u][8 * hf + ci] = fmaf(e[u][t], vv[ci], o[u][8 * hf + ci]);
+                                    o2[u][4 * hf + ci2] = fma2(e2[u][t], vv[ci2], o2[u][4 * hf + ci2]);
                         }
                     }
                     else
 #pragma unroll
                     for (int cc = 0; cc < kManyC / 4; cc++) {
-                        const float4 v4 = *reinterpret_cast<const float4 *>(vr + many_pos(h, cc));
+                        const ulonglong2 v2 = *reinterpret_cast<const ulonglong2 *>(vr + many_pos(h, cc));
 #pragma unroll
                         for (int u = 0; u < 2; u++) {
-                            o[u][4 * cc] = fmaf(e[u][t], v4.x, o[u][4 * cc]);
-                            o[u][4 * cc + 1] = fmaf(e[u][t], v4.y, o[u][4 * cc + 1]);
-                            o[u][4 * cc + 2] = fmaf(e[u][t], v4.z, o[u][4 * cc + 2]);
-                            o[u][4 * cc + 3] = fmaf(e[u][t], v4.w, o[u][4 * cc + 3]);
+                            o2[u][2 * cc] = fma2(e2[u][t], v2.x, o2[u][2 * cc]);
+                            o2[u][2 * cc + 1] = fma2(e2[u][t], v2.y, o2[u][2 * cc + 1]);
                         }
                     }
                 }
             }
         }
-        __syncthreads();  // buffer b may be refilled from the next iteration on
-    }
-    // Merge the key lanes of each (query, head) (shared memory reused), then
-    // one partial per (query, head) of this split.
-    float *mer = sm;  // [kLanes][8 queries][8 heads][kPart]
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-        float *mine = mer + ((lane * 8 + qg + 4 * u) * kHeads + h) * kPart;
-        mine[0] = m[u];
-        mine[1] = l[u];
-#pragma unroll
-        for (int cc = 0; cc < kManyC; cc++)
-            mine[2 + cc] = o[u][cc];
-    }
-    __syncthreads();
-    if (lane == 0) {
-#pragma unroll 1
-        for (int u = 0; u < 2; u++) {
-            const int qi = u ? qb : qa;
-            if (qi >= Nq)
-                continue;
-            const int slot = (qg + 4 * u) * kHeads + h;
-            float M = -INFINITY;
-            for (int t = 0; t < kLanes; t++)
-                M = fmaxf(M, mer[(t * 64 + slot) * kPart]);
-            float L = 0.0f, acc[kManyC];
-#pragma unroll
-            for (int cc = 0; cc < kManyC; cc++)
-                acc[cc] = 0.0f;
-            for (int t = 0; t < kLanes; t++) {
-                const float *pt = mer + (t * 64 + slot) * kPart;
-                const float f = pt[0] == -INFINITY ? 0.0f : __expf(pt[0] - M);
-                L += pt[1] * f;
-#pragma unroll
-                for (int cc = 0; cc < kManyC; cc++)
-                    acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
-            }
-            float *dst = part + (((p * nsplit + split) * Nq + qi) * kHeads + h) * kPart;
-            dst[0] = M;
-            dst[1] = L;
-#pragma unroll
-            for (int cc = 0; cc < kManyC; cc++)
-                dst[2 + cc] = acc[cc];
-        }
+        __syncthreads();  // stage b may be refilled from the next iteration on
+        if (ci == nch - 1 || i == nloc - 1)
+            flush(b, p - p_first);
     }
 }
 
-// Combines the nsplit partials of each (prompt, query, head) into O.
+// Combines the partials of each (prompt, query, head): those of the CTAs
+// whose chunk ranges meet the prompt's chunks [p nch, (p + 1) nch), at
+// segment p - (first prompt of the CTA).
 __global__ void mha_many_combine_kernel(const float *__restrict__ part, float *__restrict__ O,
-                                        int P, int Nq, int nsplit)
+                                        int P, int Nq, int nch, int G, int segs)
 {
     const long g = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (p, qi, h)
     if (g >= (long)P * Nq * kHeads)
@@ -672,15 +707,24 @@ __global__ void mha_many_combine_kernel(const float *__restrict__ part, float *_
     const int h = (int)(g % kHeads);
     const int qi = (int)((g / kHeads) % Nq);
     const long p = g / ((long)kHeads * Nq);
+    const long T = (long)P * nch;
+    // CTA holding chunk c: the largest x with x T / G <= c, i.e.
+    // ceil((c + 1) G / T) - 1.
+    const long x0 = ((p * nch + 1) * G + T - 1) / T - 1;
+    const long x1 = (((p + 1) * nch) * G + T - 1) / T - 1;
+    auto rec = [&](long x) {
+        const long k = p - many_chunk0(x, T, G) / nch;
+        return part + (((x * segs + k) * Nq + qi) * kHeads + h) * kPart;
+    };
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++)
-        M = fmaxf(M, part[(((p * nsplit + s) * Nq + qi) * kHeads + h) * kPart]);
+    for (long x = x0; x <= x1; x++)
+        M = fmaxf(M, rec(x)[0]);
     float L = 0.0f, acc[kManyC];
 #pragma unroll
     for (int cc = 0; cc < kManyC; cc++)
         acc[cc] = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-        const float *pt = part + (((p * nsplit + s) * Nq + qi) * kHeads + h) * kPart;
+    for (long x = x0; x <= x1; x++) {
+        const float *pt = rec(x);
         const float f = pt[0] == -INFINITY ? 0.0f : expf(pt[0] - M);
         L += pt[1] * f;
 #pragma unroll
@@ -695,13 +739,30 @@ __global__ void mha_many_combine_kernel(const float *__restrict__ part, float *_
                              acc[4 * cc + 3] * inv);
 }
 
-// Splits per prompt: as many CTAs as fit two per SM in one wave (rounding
-// up would start a second, mostly empty wave), at most one per 32 keys.
-int many_splits(int P, int Nk, int num_sms)
+// Plan of the many-keys kernel: G CTAs per query group of 8 (two per SM
+// over all groups, at most one per chunk) and the most prompt segments a
+// CTA's chunk range can cross.
+struct ManyPlan {
+    int G, segs;
+};
+
+ManyPlan many_plan(int P, int Nq, int Nk, int num_sms)
 {
-    const int want = 2 * num_sms / P;
-    const int cap = (Nk + kChunk - 1) / kChunk;
-    return want < 1 ? 1 : (want > cap ? cap : want);
+    const long nch = (Nk + kChunk - 1) / kChunk, T = (long)P * nch;
+    const long nz = (Nq + 7) / 8;
+    long G = 2L * num_sms / nz;
+    if (G < 1)
+        G = 1;
+    if (G > T)
+        G = T;
+    const long per = (T + G - 1) / G;  // chunks of the longest range
+    return {(int)G, (int)((per - 1) / nch + 2)};
+}
+
+size_t many_workspace(int P, int Nq, int Nk, int num_sms)
+{
+    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
+    return (size_t)pl.G * pl.segs * Nq * kHeads * kPart * sizeof(float);
 }
 
 template <bool Q_BF16, bool OUT_BF16>
@@ -751,25 +812,22 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                 const void *vp, long sv, float *o, void *ws, size_t ws_bytes, float scale,
                 int num_sms, cudaStream_t st)
 {
-    const int nsplit = many_splits(P, Nk, num_sms);
-    const size_t need =
-        (size_t)P * nsplit * Nq * kHeads * kPart * sizeof(float);
-    if (!ws || ws_bytes < need)
+    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
+    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms))
         return K_EARG;
     const int smem = KV_BF16 ? kManySmem / 2 : kManySmem;
     cudaError_t e = smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
     if (e != cudaSuccess)
         return (int)e;
-    const int per = ((Nk + nsplit - 1) / nsplit + kChunk - 1) / kChunk * kChunk;
-    dim3 grid(nsplit, P, (Nq + 7) / 8);
+    dim3 grid(pl.G, 1, (Nq + 7) / 8);
     mha_many_split_kernel<KV_BF16><<<grid, 256, smem, st>>>(
-        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), Nq, Nk, per, scale);
+        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), P, Nq, Nk, pl.segs, scale);
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return (int)e;
     const long total = (long)P * Nq * kHeads;
     mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
-        static_cast<const float *>(ws), o, P, Nq, nsplit);
+        static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk, pl.G, pl.segs);
     return (int)cudaGetLastError();
 }
 
@@ -780,8 +838,7 @@ extern "C" size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms)
 {
     if (Nk <= 64 || dint != sam3::kManyD || P <= 0 || Nq <= 0)
         return 0;
-    return (size_t)P * sam3::many_splits(P, Nk, num_sms) * Nq * sam3::kHeads * sam3::kPart *
-           sizeof(float);
+    return sam3::many_workspace(P, Nq, Nk, num_sms);
 }
 
 extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,

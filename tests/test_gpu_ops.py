@@ -387,6 +387,8 @@ def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
     ("i2t", 16, 5184, 8, 128, False),
     ("self7", 64, 7, 7, 256, False),
     ("t2i_odd", 3, 11, 1000, 128, False),   # 2 query groups, ragged key splits
+    ("t2i_5", 5, 8, 5184, 128, False),      # CTA chunk ranges end inside prompts
+    ("t2i_short", 1000, 8, 100, 128, False),  # ranges crossing up to 5 prompts
     ("i2t_64keys", 2, 300, 64, 128, False),  # the few-keys limit, ragged query blocks
 ])
 def test_mha_vs_oracle(cb, sb, ob, name, P, Nq, Nk, dint, shared):
