@@ -19,15 +19,16 @@
 //   cut into equal ranges, one per CTA slot (two per SM), so that every SM
 //   streams K/V (a prompt's K/V is 2.6 MB in fp32); a CTA (one range, for 8
 //   queries) pulls the chunks of K and V with cp.async through a 3-stage
-//   ring while its 256 threads (32 (query pair, head) items x 8 key lanes,
-//   each K/V read serving two queries) run a blocked online softmax over the
-//   oldest chunk with packed f32x2 arithmetic; at the end of each prompt in
-//   its range it merges its key lanes and writes one (m, l, o) partial per
-//   (query, head); a second kernel combines the partials of each prompt.
+//   ring, each warp (one head) takes Q.K^T and P.V of every chunk on the
+//   tensor cores (mma.sync, bf16 operand pairs hi + lo for fp32 accuracy)
+//   with an online softmax on the accumulators; at the end of each prompt
+//   in its range it writes one (m, l, o) partial per (query, head); a
+//   second kernel combines the partials of each prompt.
 //
-// The 8 different heads a warp reads at once fall on distinct shared-memory
-// bank groups: rows padded to c + 4 floats per head (few keys) or 16-byte
-// chunks rotated per head (many keys, rows stay 512 bytes for cp.async).
+// Shared-memory layouts keep a warp's reads on distinct bank groups: rows
+// padded to c + 4 floats per head (few keys: the 8 heads a warp reads), or
+// per-head key tiles with XOR-swizzled 16-byte pieces (many keys: the 8
+// key rows of a fragment).
 #include "kernels.h"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -49,12 +50,6 @@ __device__ __forceinline__ uint32_t bf16_pair(float lo, float hi)
 {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
-}
-
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
-{
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit()
@@ -399,38 +394,78 @@ __global__ void __launch_bounds__(256, 2) mha_few2_kernel(const void *__restrict
 // ------------------------------------------------------------ many keys
 constexpr int kManyC = 16;                 // channels per head
 constexpr int kManyD = kManyC * kHeads;    // 128
-constexpr int kManyRow = kManyD;           // 128 floats per staged key
 constexpr int kChunk = 32;                 // keys per staged chunk
 constexpr int kStages = 3;                 // staged chunks in flight
-constexpr int kLanes = 8;                  // key lanes per (query, head)
-constexpr int kPart = 2 + kManyC;          // m, l, o[16]
-constexpr float kManyLazy = 8.0f;          // rescale threshold (natural log units)
-constexpr int kManySmem = kStages * 2 * kChunk * kManyRow * 4;  // K and V rings
+constexpr int kPart = 4 + kManyC;          // m, l, 2 unused, o[16] (16-byte aligned)
+constexpr float kManyLazy = 8.0f;          // rescale threshold (log2 units)
+// One stage: K then V, each [8 heads][32 keys][16 channels].
+constexpr int kManyStage = 2 * kHeads * kChunk * kManyC;  // elements
+constexpr int kManySmem = kStages * kManyStage * 4;       // bytes, fp32 K/V
 
-// Position (in floats) of channels 4c..4c+3 of head h within a staged key
-// row: the 16-byte chunks of a head are rotated by h / 2, so the 8 heads a
-// warp reads at one c fall on 8 different 16-byte bank groups.
-__device__ __forceinline__ int many_pos(int h, int c4)
+// The bf16 tensor-core step: D += A (16 x 16, row-major) . B (16 x 8).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1)
 {
-    return h * kManyC + (((c4 + (h >> 1)) & 3) << 2);
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Byte offset of the 16-byte piece `half` (channels 8 half .. 8 half + 7)
-// of head h within a staged bf16 key row (256 bytes): the halves of heads
-// 4-7 are swapped, so the eight heads' reads of one half hit distinct banks.
-__device__ __forceinline__ int many_pos_bf16(int h, int half)
+// Two fp32 values as bf16 pairs hi + lo (lo = the rounding residual of hi,
+// itself rounded): hi + lo carries about 16 significant bits, so products
+// of such pairs summed as hi.hi + hi.lo + lo.hi keep fp32-level accuracy
+// for these 16-term dot products. Lower half = x0.
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi, uint32_t &lo)
 {
-    return h * 32 + ((half ^ (h >> 2)) & 1) * 16;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+    const float r0 = x0 - __uint_as_float(hi << 16);
+    const float r1 = x1 - __uint_as_float(hi & 0xffff0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r1), "f"(r0));
 }
 
-// Eight bf16 values (one 16-byte piece) widened to fp32 as four pairs
-// (channels 2k, 2k + 1 in pair k) for the packed arithmetic.
-__device__ __forceinline__ void widen8x2(const uint4 w, uint64_t (&f)[4])
+// Transpose of an 8 x 8 bf16 tile held one row pair per thread (the
+// accumulator layout) into the column-pair layout of an MMA B operand.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x)
 {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int k = 0; k < 4; k++)
-        f[k] = f2_make(__uint_as_float(ws[k] << 16), __uint_as_float(ws[k] & 0xffff0000u));
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p, bool trans)
+{
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    if (trans)
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+    else
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+// 16 bytes global -> shared, zero-filled when `bytes` is 0.
+__device__ __forceinline__ void cp_async16z(void *smem, const void *gmem, int bytes)
+{
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(bytes)
+                 : "memory");
+}
+
+// Staged key row layout, per (K or V, head): 32 rows of the head's 16
+// channels. fp32 rows are 64 bytes whose 16-byte pieces are XOR-swizzled by
+// 2 ((row >> 1) & 1), bf16 rows 32 bytes whose two pieces are swizzled by
+// (row >> 2) & 1, so that the fragment loads of one warp (8 rows x a few
+// channels) hit every bank group equally.
+__device__ __forceinline__ int many_sw32(int row, int piece)  // fp32: float offset in row
+{
+    return (piece ^ (2 * ((row >> 1) & 1))) * 4;
+}
+
+__device__ __forceinline__ int many_sw16(int row, int piece)  // bf16: element offset in row
+{
+    return (piece ^ ((row >> 2) & 1)) * 8;
 }
 
 // Work of the many-keys kernel: the P prompts' 32-key chunks taken as one
@@ -443,267 +478,255 @@ __host__ __device__ __forceinline__ long many_chunk0(long g, long T, long G)
     return g * T / G;
 }
 
-// KV_BF16: K and V are bf16 rows (as the decoder's projections write them);
-// staged the same way in half the shared memory and widened on read. The
-// dot products and P.V updates use the packed f32x2 instructions on channel
-// pairs, with the same four partial sums per score and the same
-// accumulation order as the scalar form.
+// Token -> image attention on the tensor cores: warp w of the CTA is head
+// w, for 8 queries of a prompt, over each staged chunk of 32 keys as two
+// blocks of 16. Per block, S^T (16 keys x 8 queries) = K . Q^T and O^T (16
+// channels x 8 queries) += V^T . P^T by mma.sync m16n8k16 in bf16 with
+// fp32 accumulation, every fp32 operand split into a bf16 pair hi + lo
+// and each product taken as hi.hi + lo.hi + hi.lo (K/V given in bf16 are
+// exact: one term fewer). Q carries scale * log2 e, so S is in log2 units.
+// Softmax per query over the chunk: maximum across the warp's 8 key
+// groups by shuffles, the running maximum raised (O, l rescaled) only when
+// the chunk's exceeds it by kManyLazy; P transposed into B fragments by
+// movmatrix. At the end of each prompt in the CTA's range one (m, l, o)
+// partial per (query, head).
 template <bool KV_BF16>
 __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
     const float *__restrict__ Q, long sq, const void *__restrict__ Kv, long sk,
     const void *__restrict__ Vv, long sv, float *__restrict__ part, int P, int Nq, int Nk,
-    int segs, float scale)
+    int segs, float qscale)
 {
     extern __shared__ __align__(16) float sm[];
-    constexpr int ROWF = KV_BF16 ? kManyRow / 2 : kManyRow;  // staged row, in floats
-    constexpr int BUF = 2 * kChunk * ROWF;                   // one stage: K rows, then V rows
+    constexpr int ESZ = KV_BF16 ? 2 : 4;
+    constexpr int STAGE_B = kManyStage * ESZ;             // bytes per stage
+    constexpr int TILE_B = kChunk * kManyC * ESZ;          // bytes per (K or V, head)
+    char *smb = reinterpret_cast<char *>(sm);
     const int nch = (Nk + kChunk - 1) / kChunk;
     const long T = (long)P * nch, G = gridDim.x;
     const long c0 = many_chunk0(blockIdx.x, T, G), c1 = many_chunk0(blockIdx.x + 1, T, G);
     const int nloc = (int)(c1 - c0);
     const long p_first = c0 / nch;
-    // Thread = (query pair, head, key lane): queries qg and qg + 4 of the
-    // CTA's 8 share every K/V read from shared memory; a warp is one key lane.
-    const int h = threadIdx.x & 7, qg = (threadIdx.x >> 3) & 3, lane = threadIdx.x >> 5;
-    const int qa = blockIdx.z * 8 + qg, qb = qa + 4;
+    const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int qz = blockIdx.z * 8;
 
-    // Chunk i of this CTA's range into stage b: 16-byte pieces into rotated rows.
-    auto stage = [&](int i, int b) {
-        const long idx = c0 + i, p = idx / nch;
-        const int j0 = (int)(idx - p * nch) * kChunk, n = min(kChunk, Nk - j0);
-        const char *kb = reinterpret_cast<const char *>(Kv) + p * sk * (KV_BF16 ? 2 : 4);
-        const char *vb = reinterpret_cast<const char *>(Vv) + p * sv * (KV_BF16 ? 2 : 4);
-        float *ks = sm + b * BUF, *vs = ks + kChunk * ROWF;
-        constexpr int PIECES = kManyD * (KV_BF16 ? 2 : 4) / 16;  // per key row
-        for (int t = threadIdx.x; t < n * PIECES; t += blockDim.x) {
-            const int j = t / PIECES, pc = t - j * PIECES;
-            int dst;  // in floats
-            if (KV_BF16)
-                dst = j * ROWF + many_pos_bf16(pc >> 1, pc & 1) / 4;
-            else
-                dst = j * ROWF + many_pos(pc / 4, pc % 4);
-            const long src = ((long)(j0 + j) * PIECES + pc) * 16;  // bytes
-            cp_async16(ks + dst, kb + src);
-            cp_async16(vs + dst, vb + src);
+    // Staging: thread -> (head, piece) and rows r0 + R k of the chunk.
+    constexpr int PIECES = kManyC * ESZ / 16;              // 16-byte pieces per head row
+    constexpr int TPR = kHeads * PIECES;                   // threads per key row
+    constexpr int R = 256 / TPR;                           // row step
+    const int sh = (threadIdx.x % TPR) / PIECES, spc = threadIdx.x % PIECES;
+    const int r0 = threadIdx.x / TPR;
+    const int soff = KV_BF16 ? many_sw16(r0, spc) * 2 : many_sw32(r0, spc) * 4;  // bytes
+    // Chunk cursors (prompt, chunk of the prompt), advanced without division.
+    struct Cur {
+        long p;
+        int ci;
+    };
+    auto advance = [&](Cur &c) {
+        if (++c.ci == nch) {
+            c.ci = 0;
+            c.p++;
+        }
+    };
+    const long src0 = ((long)r0 * kManyD + sh * kManyC) * ESZ + spc * 16;  // bytes
+    auto stage = [&](const Cur &c, int b) {
+        const int j0 = c.ci * kChunk, n = min(kChunk, Nk - j0);
+        const char *kb = reinterpret_cast<const char *>(Kv) + (c.p * sk + (long)j0 * kManyD) * ESZ;
+        const char *vb = reinterpret_cast<const char *>(Vv) + (c.p * sv + (long)j0 * kManyD) * ESZ;
+        char *dk = smb + b * STAGE_B + sh * TILE_B + soff;
+        char *dv = dk + kHeads * TILE_B;
+#pragma unroll
+        for (int k = 0; k < kChunk / R; k++) {
+            const int r = r0 + k * R;
+            const int ok = r < n ? 16 : 0;  // rows past the keys: zero-filled
+            const long src = ok ? src0 + (long)k * R * kManyD * ESZ : 0;
+            cp_async16z(dk + r * kManyC * ESZ, kb + src, ok);
+            cp_async16z(dv + r * kManyC * ESZ, vb + src, ok);
         }
         cp_async_commit();
     };
 
-    uint64_t q2[2][kManyC / 2], o2[2][kManyC / 2];
-    float m[2], l[2];
+    uint32_t qh[2], ql[2];  // B fragments of Q^T (hi, lo)
+    float o[2][4], m[2], l[2];  // O^T per key block (two independent MMA chains)
     auto start_segment = [&](long p) {
+        const int qi = qz + g;
+        float2 x0 = make_float2(0.0f, 0.0f), x1 = x0;
+        if (qi < Nq) {
+            const float *qp = Q + p * sq + (long)qi * kManyD + h * kManyC + 2 * t;
+            x0 = *reinterpret_cast<const float2 *>(qp);
+            x1 = *reinterpret_cast<const float2 *>(qp + 8);
+        }
+        split_bf16x2(x0.x * qscale, x0.y * qscale, qh[0], ql[0]);
+        split_bf16x2(x1.x * qscale, x1.y * qscale, qh[1], ql[1]);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            o[0][k] = o[1][k] = 0.0f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.0f;
+    };
+    // Segment k's partials: l summed over the 8 key groups; the lane of
+    // key group g writes channels g and g + 8 of queries 2t, 2t + 1.
+    auto flush = [&](long k) {
 #pragma unroll
         for (int u = 0; u < 2; u++) {
-            const int qq = (u ? qb : qa) < Nq ? (u ? qb : qa) : 0;
-            const float4 *qp =
-                reinterpret_cast<const float4 *>(Q + p * sq + (long)qq * kManyD + h * kManyC);
-#pragma unroll
-            for (int c = 0; c < kManyC / 4; c++) {
-                const float4 v = __ldg(qp + c);
-                q2[u][2 * c] = f2_make(v.x * scale, v.y * scale);
-                q2[u][2 * c + 1] = f2_make(v.z * scale, v.w * scale);
-            }
-            m[u] = -INFINITY;
-            l[u] = 0.0f;
-#pragma unroll
-            for (int c = 0; c < kManyC / 2; c++)
-                o2[u][c] = 0;
-        }
-    };
-    // Merges the 8 key lanes of each (query, head) through stage b (free
-    // when this runs: its chunk is consumed and the next one is not yet
-    // requested) and writes segment k's partials; one query half per pass.
-    auto flush = [&](int b, long k) {
-        float *mer = sm + b * BUF;  // [7 lanes][32 (query, head)][kPart]
-        static_assert(7 * 32 * kPart <= (KV_BF16 ? 2 * kChunk * kManyRow / 2 : 2 * kChunk * kManyRow),
-                      "lane records fit in one stage");
-#pragma unroll
-        for (int u = 0; u < 2; u++) {  // unrolled: o2, m, l stay in registers
-            const int slot = qg * kHeads + h;
-            if (lane > 0) {
-                float *mine = mer + ((lane - 1) * 32 + slot) * kPart;
-                mine[0] = m[u];
-                mine[1] = l[u];
-#pragma unroll
-                for (int c = 0; c < kManyC / 2; c++)
-                    f2_split(o2[u][c], mine[2 + 2 * c], mine[3 + 2 * c]);
-            }
-            __syncthreads();
-            const int qi = u ? qb : qa;
-            if (lane == 0 && qi < Nq) {
-                float M = m[u];
-                for (int t = 0; t < kLanes - 1; t++)
-                    M = fmaxf(M, mer[(t * 32 + slot) * kPart]);
-                float acc[kManyC];
-                const float f0 = m[u] == -INFINITY ? 0.0f : __expf(m[u] - M);
-                float L = l[u] * f0;
-#pragma unroll
-                for (int c = 0; c < kManyC / 2; c++) {
-                    float a0, a1;
-                    f2_split(o2[u][c], a0, a1);
-                    acc[2 * c] = a0 * f0;
-                    acc[2 * c + 1] = a1 * f0;
+            float L = l[u];
+            L += __shfl_xor_sync(0xffffffffu, L, 4);
+            L += __shfl_xor_sync(0xffffffffu, L, 8);
+            L += __shfl_xor_sync(0xffffffffu, L, 16);
+            const int qi = qz + 2 * t + u;
+            if (qi < Nq) {
+                float *dst =
+                    part + (((blockIdx.x * (long)segs + k) * Nq + qi) * kHeads + h) * kPart;
+                if (g == 0) {
+                    dst[0] = m[u];
+                    dst[1] = L;
                 }
-                for (int t = 0; t < kLanes - 1; t++) {
-                    const float *pt = mer + (t * 32 + slot) * kPart;
-                    const float f = pt[0] == -INFINITY ? 0.0f : __expf(pt[0] - M);
-                    L += pt[1] * f;
-#pragma unroll
-                    for (int cc = 0; cc < kManyC; cc++)
-                        acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
-                }
-                float *dst = part + (((blockIdx.x * (long)segs + k) * Nq + qi) * kHeads + h) * kPart;
-                dst[0] = M;
-                dst[1] = L;
-#pragma unroll
-                for (int cc = 0; cc < kManyC; cc++)
-                    dst[2 + cc] = acc[cc];
+                dst[4 + g] = o[0][u] + o[1][u];
+                dst[4 + g + 8] = o[0][2 + u] + o[1][2 + u];
             }
-            __syncthreads();
         }
     };
 
-    // Ring of kStages chunks: chunks i+1 and i+2 load while i computes (an
-    // empty commit group keeps the wait count uniform at the tail).
+    Cur cur = {p_first, (int)(c0 - p_first * nch)}, ahead = cur;
     for (int i = 0; i < kStages - 1; i++) {
-        if (i < nloc)
-            stage(i, i);
+        if (i < nloc) {
+            stage(ahead, i);
+            advance(ahead);
+        }
         else
             cp_async_commit();
     }
-    for (int i = 0; i < nloc; i++) {
+    for (int i = 0; i < nloc; i++, advance(cur)) {
         const int b = i % kStages;
-        const long idx = c0 + i, p = idx / nch;
-        const int ci = (int)(idx - p * nch);
+        const long p = cur.p;
+        const int ci = cur.ci;
         if (i == 0 || ci == 0)
             start_segment(p);
-        if (i + kStages - 1 < nloc)  // its stage was released by the barrier below
-            stage(i + kStages - 1, (i + kStages - 1) % kStages);
+        if (i + kStages - 1 < nloc) {  // its stage was released by the barrier below
+            stage(ahead, (i + kStages - 1) % kStages);
+            advance(ahead);
+        }
         else
             cp_async_commit();
         cp_async_wait<kStages - 1>();
         __syncthreads();
-        const float *ks = sm + b * BUF, *vs = ks + kChunk * ROWF;
         const int n = min(kChunk, Nk - ci * kChunk);
-        // This lane's keys of the chunk as one block per query: scores, block
-        // maximum, one correction, then P.V.
-        constexpr int KT = kChunk / kLanes;
-        float s[2][KT];
-        float bm[2] = {-INFINITY, -INFINITY};
+        const char *tk = smb + b * STAGE_B + h * TILE_B;
+        const char *tv = tk + kHeads * TILE_B;
+        // S^T of the two key blocks: s[blk][0..3] = keys (g, g, g+8, g+8) of
+        // the block x queries (2t, 2t+1, 2t, 2t+1).
+        float s[2][4];
 #pragma unroll
-        for (int t = 0; t < KT; t++) {
-            const int j = t * kLanes + lane;
-            s[0][t] = s[1][t] = -INFINITY;
-            if (j < n) {
-                const float *kr = ks + j * ROWF;
-                uint64_t dA[2] = {0, 0}, dB[2] = {0, 0};  // channel pairs (4c, 4c+1), (4c+2, 4c+3)
-                if (KV_BF16) {
+        for (int blk = 0; blk < 2; blk++) {
+            float (&d)[4] = s[blk];
+            d[0] = d[1] = d[2] = d[3] = 0.0f;
+            const int j = blk * 16 + g;
+            if (KV_BF16) {
+                // rows of matrices 0..3: keys 0-7 / 8-15 x channels 0-7 / 8-15
+                const int mi = lane >> 3, rr = blk * 16 + (lane & 7) + (mi & 1) * 8;
+                uint32_t a[4];
+                ldmatrix_x4(a, tk + (rr * kManyC + many_sw16(rr, mi >> 1)) * 2, false);
+                mma_bf16(d, a, qh[0], qh[1]);
+                mma_bf16(d, a, ql[0], ql[1]);
+            }
+            else {
+                const float *kr = reinterpret_cast<const float *>(tk);
+                const float2 x0 = *reinterpret_cast<const float2 *>(kr + j * kManyC + many_sw32(j, t >> 1) + 2 * (t & 1));
+                const float2 x1 = *reinterpret_cast<const float2 *>(kr + (j + 8) * kManyC + many_sw32(j + 8, t >> 1) + 2 * (t & 1));
+                const float2 x2 = *reinterpret_cast<const float2 *>(kr + j * kManyC + many_sw32(j, 2 + (t >> 1)) + 2 * (t & 1));
+                const float2 x3 = *reinterpret_cast<const float2 *>(kr + (j + 8) * kManyC + many_sw32(j + 8, 2 + (t >> 1)) + 2 * (t & 1));
+                uint32_t ah[4], al[4];
+                split_bf16x2(x0.x, x0.y, ah[0], al[0]);
+                split_bf16x2(x1.x, x1.y, ah[1], al[1]);
+                split_bf16x2(x2.x, x2.y, ah[2], al[2]);
+                split_bf16x2(x3.x, x3.y, ah[3], al[3]);
+                mma_bf16(d, ah, qh[0], qh[1]);
+                mma_bf16(d, al, qh[0], qh[1]);
+                mma_bf16(d, ah, ql[0], ql[1]);
+            }
+            if (j >= n)
+                d[0] = d[1] = -INFINITY;
+            if (j + 8 >= n)
+                d[2] = d[3] = -INFINITY;
+        }
+        float bm[2];
 #pragma unroll
-                    for (int hf = 0; hf < 2; hf++) {
-                        uint64_t kv[4];
-                        widen8x2(*reinterpret_cast<const uint4 *>(
-                                     reinterpret_cast<const char *>(kr) + many_pos_bf16(h, hf)),
-                                 kv);
-#pragma unroll
-                        for (int u = 0; u < 2; u++) {
-                            dA[u] = fma2(q2[u][4 * hf], kv[0], dA[u]);
-                            dB[u] = fma2(q2[u][4 * hf + 1], kv[1], dB[u]);
-                            dA[u] = fma2(q2[u][4 * hf + 2], kv[2], dA[u]);
-                            dB[u] = fma2(q2[u][4 * hf + 3], kv[3], dB[u]);
-                        }
-                    }
-                }
-                else
-#pragma unroll
-                for (int cc = 0; cc < kManyC / 4; cc++) {
-                    const ulonglong2 k2 = *reinterpret_cast<const ulonglong2 *>(kr + many_pos(h, cc));
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        dA[u] = fma2(q2[u][2 * cc], k2.x, dA[u]);
-                        dB[u] = fma2(q2[u][2 * cc + 1], k2.y, dB[u]);
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    float d0, d1, d2, d3;
-                    f2_split(dA[u], d0, d1);
-                    f2_split(dB[u], d2, d3);
-                    s[u][t] = (d0 + d1) + (d2 + d3);
-                    bm[u] = fmaxf(bm[u], s[u][t]);
-                }
+        for (int u = 0; u < 2; u++) {
+            float x = fmaxf(fmaxf(s[0][u], s[0][2 + u]), fmaxf(s[1][u], s[1][2 + u]));
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
+            bm[u] = x;
+            if (bm[u] > m[u] + kManyLazy) {  // uniform over the lanes of query 2t + u
+                const float corr = exp2f(m[u] - bm[u]);  // 0 on the first chunk
+                l[u] *= corr;
+                o[0][u] *= corr;
+                o[0][2 + u] *= corr;
+                o[1][u] *= corr;
+                o[1][2 + u] *= corr;
+                m[u] = bm[u];
             }
         }
-        if (bm[0] > -INFINITY) {  // the key count is the same for both queries
-            uint64_t e2[2][KT];
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                // The running maximum is raised (and o, l rescaled) only when
-                // the block's maximum exceeds it by more than kManyLazy, so
-                // e <= e^kManyLazy and most blocks skip the rescale; the
-                // final normalisation makes the result independent of it.
-                if (bm[u] > m[u] + kManyLazy) {
-                    const float corr = __expf(m[u] - bm[u]);  // 0 on the first block
-                    l[u] *= corr;
-                    const uint64_t c2 = f2_make(corr, corr);
+        for (int blk = 0; blk < 2; blk++) {
+            float pe[4];
 #pragma unroll
-                    for (int cc = 0; cc < kManyC / 2; cc++)
-                        o2[u][cc] = mul2(o2[u][cc], c2);
-                    m[u] = bm[u];
-                }
-#pragma unroll
-                for (int t = 0; t < KT; t++) {
-                    const float e = __expf(s[u][t] - m[u]);  // 0 for keys past the chunk
-                    l[u] += e;
-                    e2[u][t] = f2_make(e, e);
-                }
+            for (int k = 0; k < 4; k++) {
+                pe[k] = ex2_approx(s[blk][k] - m[k & 1]);  // 0 for masked keys
+                l[k & 1] += pe[k];
             }
-#pragma unroll
-            for (int t = 0; t < KT; t++) {
-                const int j = t * kLanes + lane;
-                if (j < n) {
-                    const float *vr = vs + j * ROWF;
-                    if (KV_BF16) {
-#pragma unroll
-                        for (int hf = 0; hf < 2; hf++) {
-                            uint64_t vv[4];
-                            widen8x2(*reinterpret_cast<const uint4 *>(
-                                         reinterpret_cast<const char *>(vr) + many_pos_bf16(h, hf)),
-                                     vv);
-#pragma unroll
-                            for (int ci2 = 0; ci2 < 4; ci2++)
-#pragma unroll
-                                for (int u = 0; u < 2; u++)
-                                    o2[u][4 * hf + ci2] = fma2(e2[u][t], vv[ci2], o2[u][4 * hf + ci2]);
-                        }
-                    }
-                    else
-#pragma unroll
-                    for (int cc = 0; cc < kManyC / 4; cc++) {
-                        const ulonglong2 v2 = *reinterpret_cast<const ulonglong2 *>(vr + many_pos(h, cc));
-#pragma unroll
-                        for (int u = 0; u < 2; u++) {
-                            o2[u][2 * cc] = fma2(e2[u][t], v2.x, o2[u][2 * cc]);
-                            o2[u][2 * cc + 1] = fma2(e2[u][t], v2.y, o2[u][2 * cc + 1]);
-                        }
-                    }
-                }
+            // P^T tiles (keys 0-7 / 8-15 x 8 queries) -> B fragments
+            uint32_t ph0, pl0, ph1, pl1;
+            split_bf16x2(pe[0], pe[1], ph0, pl0);
+            split_bf16x2(pe[2], pe[3], ph1, pl1);
+            ph0 = movmatrix_t(ph0);
+            ph1 = movmatrix_t(ph1);
+            pl0 = movmatrix_t(pl0);
+            pl1 = movmatrix_t(pl1);
+            if (KV_BF16) {
+                // V^T fragments: matrices (keys 0-7 / 8-15) x (channels 0-7 / 8-15), transposed
+                const int mi = lane >> 3;
+                const int rr = blk * 16 + (lane & 7) + (mi >> 1) * 8;
+                uint32_t a[4];
+                ldmatrix_x4(a, tv + (rr * kManyC + many_sw16(rr, mi & 1)) * 2, true);
+                mma_bf16(o[blk], a, ph0, ph1);
+                mma_bf16(o[blk], a, pl0, pl1);
+            }
+            else {
+                const float *vr = reinterpret_cast<const float *>(tv);
+                const int k0 = blk * 16 + 2 * t;
+                auto ld = [&](int key, int ch) {
+                    return vr[key * kManyC + many_sw32(key, ch >> 2) + (ch & 3)];
+                };
+                uint32_t ah[4], al[4];
+                split_bf16x2(ld(k0, g), ld(k0 + 1, g), ah[0], al[0]);
+                split_bf16x2(ld(k0, g + 8), ld(k0 + 1, g + 8), ah[1], al[1]);
+                split_bf16x2(ld(k0 + 8, g), ld(k0 + 9, g), ah[2], al[2]);
+                split_bf16x2(ld(k0 + 8, g + 8), ld(k0 + 9, g + 8), ah[3], al[3]);
+                mma_bf16(o[blk], ah, ph0, ph1);
+                mma_bf16(o[blk], al, ph0, ph1);
+                mma_bf16(o[blk], ah, pl0, pl1);
             }
         }
         __syncthreads();  // stage b may be refilled from the next iteration on
         if (ci == nch - 1 || i == nloc - 1)
-            flush(b, p - p_first);
+            flush(p - p_first);
     }
 }
 
 // Combines the partials of each (prompt, query, head): those of the CTAs
 // whose chunk ranges meet the prompt's chunks [p nch, (p + 1) nch), at
-// segment p - (first prompt of the CTA).
-__global__ void mha_many_combine_kernel(const float *__restrict__ part, float *__restrict__ O,
-                                        int P, int Nq, int nch, int G, int segs)
+// segment p - (first prompt of the CTA); offsets in log2 units. One thread
+// per 4 output channels.
+__global__ void __launch_bounds__(128) mha_many_combine_kernel(const float *__restrict__ part,
+                                                               float *__restrict__ O, int P,
+                                                               int Nq, int nch, int G, int segs)
 {
-    const long g = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (p, qi, h)
-    if (g >= (long)P * Nq * kHeads)
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (p, qi, h, quad)
+    if (i >= (long)P * Nq * kHeads * 4)
         return;
+    const int quad = (int)(i & 3);
+    const long g = i >> 2;
     const int h = (int)(g % kHeads);
     const int qi = (int)((g / kHeads) % Nq);
     const long p = g / ((long)kHeads * Nq);
@@ -718,25 +741,23 @@ __global__ void mha_many_combine_kernel(const float *__restrict__ part, float *_
     };
     float M = -INFINITY;
     for (long x = x0; x <= x1; x++)
-        M = fmaxf(M, rec(x)[0]);
-    float L = 0.0f, acc[kManyC];
-#pragma unroll
-    for (int cc = 0; cc < kManyC; cc++)
-        acc[cc] = 0.0f;
+        M = fmaxf(M, __ldg(rec(x)));
+    float L = 0.0f;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (long x = x0; x <= x1; x++) {
         const float *pt = rec(x);
-        const float f = pt[0] == -INFINITY ? 0.0f : expf(pt[0] - M);
-        L += pt[1] * f;
-#pragma unroll
-        for (int cc = 0; cc < kManyC; cc++)
-            acc[cc] = fmaf(pt[2 + cc], f, acc[cc]);
+        const float2 ml = __ldg(reinterpret_cast<const float2 *>(pt));
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(pt + 4) + quad);
+        const float f = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);
+        L = fmaf(ml.y, f, L);
+        acc.x = fmaf(v.x, f, acc.x);
+        acc.y = fmaf(v.y, f, acc.y);
+        acc.z = fmaf(v.z, f, acc.z);
+        acc.w = fmaf(v.w, f, acc.w);
     }
     const float inv = 1.0f / L;
-    float4 *op = reinterpret_cast<float4 *>(O + (p * Nq + qi) * kManyD + h * kManyC);
-#pragma unroll
-    for (int cc = 0; cc < kManyC / 4; cc++)
-        op[cc] = make_float4(acc[4 * cc] * inv, acc[4 * cc + 1] * inv, acc[4 * cc + 2] * inv,
-                             acc[4 * cc + 3] * inv);
+    reinterpret_cast<float4 *>(O + (p * Nq + qi) * kManyD + h * kManyC)[quad] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 // Plan of the many-keys kernel: G CTAs per query group of 8 (two per SM
@@ -813,7 +834,7 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                 int num_sms, cudaStream_t st)
 {
     const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
-    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms))
+    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15))
         return K_EARG;
     const int smem = KV_BF16 ? kManySmem / 2 : kManySmem;
     cudaError_t e = smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
@@ -821,11 +842,12 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
         return (int)e;
     dim3 grid(pl.G, 1, (Nq + 7) / 8);
     mha_many_split_kernel<KV_BF16><<<grid, 256, smem, st>>>(
-        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), P, Nq, Nk, pl.segs, scale);
+        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
+        scale * 1.4426950408889634f);
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return (int)e;
-    const long total = (long)P * Nq * kHeads;
+    const long total = (long)P * Nq * kHeads * 4;
     mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
         static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk, pl.G, pl.segs);
     return (int)cudaGetLastError();
