@@ -38,6 +38,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #define STREAM(s) reinterpret_cast<cudaStream_t>(s)
 
 namespace sam3 {
@@ -224,173 +226,6 @@ __global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const flo
     }
 }
 
-// Image -> token attention (at most kFewSmall keys, 16 channels per head):
-// the kernel above is bound by shared-memory bandwidth (every (query, head)
-// thread reads its head's K and V rows for each key). Here a thread takes
-// two queries of one head, so each K / V read from shared memory serves
-// both: units of 64 queries, thread (head h, slot qt) computing queries
-// qt and qt + 32 of the unit, the next unit's two queries in flight while
-// this one computes. Same arithmetic per query as the small path above.
-// Q_BF16: Q is read as bf16 (written so by its projection); OUT_BF16: O is
-// written as bf16 (for a consumer that only feeds a GEMM).
-template <bool Q_BF16, bool OUT_BF16>
-__global__ void __launch_bounds__(256, 2) mha_few2_kernel(const void *__restrict__ Q, long sq,
-                                                         const float *__restrict__ K, long sk,
-                                                         const float *__restrict__ V, long sv,
-                                                         void *__restrict__ O, int P, int Nq,
-                                                         int Nk, float scale)
-{
-    constexpr int C = 16, D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
-    extern __shared__ float kv[];  // K rows then V rows, [Nk][8][CP] each
-    float *ks = kv;
-    float *vs = kv + Nk * ROW;
-    const int h = threadIdx.x & 7, qt = threadIdx.x >> 3;
-    const int nqb = (Nq + 63) / 64;
-    const long U = (long)P * nqb;
-    const long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
-    float q[2][C];
-    auto load2 = [&](long u, float (&dst)[2][C]) {
-        const long pu = u / nqb;
-        const int qb = (int)(u - pu * nqb) * 64 + qt;
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const int qi = qb + 32 * i;
-            if (qi >= Nq)
-                continue;
-            const long off = pu * sq + (long)qi * D + h * C;
-            if (Q_BF16) {
-                const uint4 *q4 =
-                    reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(Q) + off);
-#pragma unroll
-                for (int c = 0; c < C / 8; c++) {
-                    const uint4 w = __ldg(q4 + c);
-                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        dst[i][8 * c + 2 * k] = __uint_as_float(ws[k] << 16) * scale;
-                        dst[i][8 * c + 2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u) * scale;
-                    }
-                }
-            }
-            else
-                load_q<C>(reinterpret_cast<const float *>(Q) + off, dst[i], scale);
-        }
-    };
-    if (u0 < u1)
-        load2(u0, q);
-    long staged = -1;
-#pragma unroll 1
-    for (long u = u0; u < u1; u++) {
-        const long p = u / nqb;
-        const int qb = (int)(u - p * nqb) * 64 + qt;
-        if (p != staged) {  // CTA-uniform: stage this prompt's K and V
-            __syncthreads();
-            const float *kb = K + p * sk, *vb = V + p * sv;
-            for (int i = threadIdx.x; i < Nk * (D / 4); i += blockDim.x) {
-                const int j = i / (D / 4), col = (i - j * (D / 4)) * 4;
-                const int dst = j * ROW + (col / C) * CP + col % C;
-                *reinterpret_cast<float4 *>(ks + dst) =
-                    __ldg(reinterpret_cast<const float4 *>(kb + (long)j * D + col));
-                *reinterpret_cast<float4 *>(vs + dst) =
-                    __ldg(reinterpret_cast<const float4 *>(vb + (long)j * D + col));
-            }
-            __syncthreads();
-            staged = p;
-        }
-        float qn[2][C];
-        const bool more = u + 1 < u1;
-        if (more)
-            load2(u + 1, qn);
-        if (qb < Nq) {
-            float sc[2][kFewSmall], m[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-            for (int j = 0; j < kFewSmall; j++) {
-                sc[0][j] = sc[1][j] = -INFINITY;
-                if (j < Nk) {
-                    const float4 *kr = reinterpret_cast<const float4 *>(ks + j * ROW + h * CP);
-                    float d[2][4] = {};
-#pragma unroll
-                    for (int c = 0; c < C / 4; c++) {
-                        const float4 k4 = kr[c];
-#pragma unroll
-                        for (int i = 0; i < 2; i++) {
-                            d[i][0] = fmaf(q[i][4 * c], k4.x, d[i][0]);
-                            d[i][1] = fmaf(q[i][4 * c + 1], k4.y, d[i][1]);
-                            d[i][2] = fmaf(q[i][4 * c + 2], k4.z, d[i][2]);
-                            d[i][3] = fmaf(q[i][4 * c + 3], k4.w, d[i][3]);
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < 2; i++) {
-                        sc[i][j] = (d[i][0] + d[i][1]) + (d[i][2] + d[i][3]);
-                        m[i] = fmaxf(m[i], sc[i][j]);
-                    }
-                }
-            }
-            float o[2][C], l[2] = {0.0f, 0.0f};
-#pragma unroll
-            for (int c = 0; c < C; c++)
-                o[0][c] = o[1][c] = 0.0f;
-#pragma unroll
-            for (int j = 0; j < kFewSmall; j++) {
-                if (j < Nk) {
-                    float e[2];
-#pragma unroll
-                    for (int i = 0; i < 2; i++) {
-                        e[i] = __expf(sc[i][j] - m[i]);
-                        l[i] += e[i];
-                    }
-                    const float4 *vr = reinterpret_cast<const float4 *>(vs + j * ROW + h * CP);
-#pragma unroll
-                    for (int c = 0; c < C / 4; c++) {
-                        const float4 v4 = vr[c];
-#pragma unroll
-                        for (int i = 0; i < 2; i++) {
-                            o[i][4 * c] = fmaf(e[i], v4.x, o[i][4 * c]);
-                            o[i][4 * c + 1] = fmaf(e[i], v4.y, o[i][4 * c + 1]);
-                            o[i][4 * c + 2] = fmaf(e[i], v4.z, o[i][4 * c + 2]);
-                            o[i][4 * c + 3] = fmaf(e[i], v4.w, o[i][4 * c + 3]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const int qi = qb + 32 * i;
-                if (qi < Nq) {
-                    const float inv = 1.0f / l[i];
-                    const long off = (p * Nq + qi) * D + h * C;
-                    if (OUT_BF16) {
-                        uint4 *op = reinterpret_cast<uint4 *>(
-                            reinterpret_cast<__nv_bfloat16 *>(O) + off);
-#pragma unroll
-                        for (int c = 0; c < C / 8; c++)
-                            op[c] = make_uint4(
-                                bf16_pair(o[i][8 * c] * inv, o[i][8 * c + 1] * inv),
-                                bf16_pair(o[i][8 * c + 2] * inv, o[i][8 * c + 3] * inv),
-                                bf16_pair(o[i][8 * c + 4] * inv, o[i][8 * c + 5] * inv),
-                                bf16_pair(o[i][8 * c + 6] * inv, o[i][8 * c + 7] * inv));
-                    }
-                    else {
-                        float4 *op = reinterpret_cast<float4 *>(reinterpret_cast<float *>(O) + off);
-#pragma unroll
-                        for (int c = 0; c < C / 4; c++)
-                            op[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv,
-                                                o[i][4 * c + 2] * inv, o[i][4 * c + 3] * inv);
-                    }
-                }
-            }
-        }
-        if (more) {
-#pragma unroll
-            for (int c = 0; c < C; c++) {
-                q[0][c] = qn[0][c];
-                q[1][c] = qn[1][c];
-            }
-        }
-    }
-}
-
 // ------------------------------------------------------------ many keys
 constexpr int kManyC = 16;                 // channels per head
 constexpr int kManyD = kManyC * kHeads;    // 128
@@ -466,6 +301,176 @@ __device__ __forceinline__ int many_sw32(int row, int piece)  // fp32: float off
 __device__ __forceinline__ int many_sw16(int row, int piece)  // bf16: element offset in row
 {
     return (piece ^ ((row >> 2) & 1)) * 8;
+}
+
+// The bf16 tensor-core step with K = 8: D += A (16 x 8) . B (8 x 8).
+__device__ __forceinline__ void mma_bf16_k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// Image -> token attention (at most 8 keys, 16 channels per head) on the
+// tensor cores: a CTA takes a contiguous range of 16-query units (mostly of
+// one prompt, whose K and V fragments it loads once), warp w = head w. Per
+// unit, S (16 queries x 8 keys) = Q . K^T by mma.sync m16n8k16 and O
+// (16 queries x 16 channels) = P . V by two m16n8k8 in bf16 with fp32
+// accumulation, fp32 operands split into bf16 pairs hi + lo and each
+// product taken as hi.hi + lo.hi + hi.lo (a bf16 Q is exact: one term
+// fewer); K carries scale * log2 e, so S is in log2 units. A query row's 8
+// scores sit in the 4 lanes of a quad: its maximum and sum are two
+// shuffles each, and P stays in the accumulator layout, which is the A
+// layout of the P . V step. The next unit's Q fragment loads while this
+// one computes. Q_BF16: Q is read as bf16 (written so by its projection);
+// OUT_BF16: O is written as bf16 (for a consumer that only feeds a GEMM).
+template <bool Q_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(256) mha_few2_kernel(const void *__restrict__ Q, long sq,
+                                                      const float *__restrict__ K, long sk,
+                                                      const float *__restrict__ V, long sv,
+                                                      void *__restrict__ O, int P, int Nq, int Nk,
+                                                      float kscale)
+{
+    constexpr int D = kManyD;
+    const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int nqb = (Nq + 15) / 16;
+    const long U = (long)P * nqb;
+    const long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    if (u0 >= u1)
+        return;
+    // Q fragment of a unit: (row g | g + 8) x channels (2t, 2t+1 | 2t+8, 2t+9),
+    // in the order a0 (g, lo), a1 (g+8, lo), a2 (g, hi), a3 (g+8, hi).
+    using QRaw = typename std::conditional<Q_BF16, uint32_t, float2>::type;
+    auto load_q = [&](long p, int q0, QRaw (&r)[4]) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int q = q0 + g + (k & 1) * 8;
+            const long off = p * sq + (long)q * D + h * kManyC + 2 * t + (k >> 1) * 8;
+            if (q < Nq) {
+                if (Q_BF16)
+                    reinterpret_cast<uint32_t &>(r[k]) =
+                        __ldg(reinterpret_cast<const uint32_t *>(
+                            reinterpret_cast<const __nv_bfloat16 *>(Q) + off));
+                else
+                    reinterpret_cast<float2 &>(r[k]) =
+                        __ldg(reinterpret_cast<const float2 *>(reinterpret_cast<const float *>(Q) + off));
+            }
+            else {
+                if (Q_BF16)
+                    reinterpret_cast<uint32_t &>(r[k]) = 0u;
+                else
+                    reinterpret_cast<float2 &>(r[k]) = make_float2(0.0f, 0.0f);
+            }
+        }
+    };
+    // Unit cursors (prompt, first query), advanced without division.
+    long pc = u0 / nqb, pn;
+    int qc = (int)(u0 - pc * nqb) * 16, qn;
+    pn = pc;
+    qn = qc;
+    auto advance = [&](long &p, int &q) {
+        q += 16;
+        if (q >= nqb * 16) {
+            q = 0;
+            p++;
+        }
+    };
+    QRaw qr[4], qx[4];
+    load_q(pc, qc, qr);
+    advance(pn, qn);
+    long staged = -1;
+    uint32_t kh[2], kl[2], vh[2], vl[2];
+#pragma unroll 1
+    for (long u = u0; u < u1; u++) {
+        if (pc != staged) {  // this prompt's K^T and V fragments
+            float kv[4];
+            const float *kb = K + pc * sk, *vb = V + pc * sv;
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const float *kr = kb + (long)g * D + h * kManyC + 2 * t + k * 8;
+                kv[0] = g < Nk ? __ldg(kr) * kscale : 0.0f;
+                kv[1] = g < Nk ? __ldg(kr + 1) * kscale : 0.0f;
+                split_bf16x2(kv[0], kv[1], kh[k], kl[k]);
+                const float *vr = vb + (long)(2 * t) * D + h * kManyC + k * 8 + g;
+                kv[2] = 2 * t < Nk ? __ldg(vr) : 0.0f;
+                kv[3] = 2 * t + 1 < Nk ? __ldg(vr + D) : 0.0f;
+                split_bf16x2(kv[2], kv[3], vh[k], vl[k]);
+            }
+            staged = pc;
+        }
+        const bool more = u + 1 < u1;
+        if (more)
+            load_q(pn, qn, qx);
+        uint32_t ah[4], al[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if (Q_BF16)
+                ah[k] = reinterpret_cast<const uint32_t &>(qr[k]);
+            else {
+                const float2 x = reinterpret_cast<const float2 &>(qr[k]);
+                split_bf16x2(x.x, x.y, ah[k], al[k]);
+            }
+        }
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // rows (g, g, g+8, g+8) x keys (2t, 2t+1)
+        mma_bf16(sc, ah, kh[0], kh[1]);
+        if (!Q_BF16)
+            mma_bf16(sc, al, kh[0], kh[1]);
+        mma_bf16(sc, ah, kl[0], kl[1]);
+        if (2 * t >= Nk)
+            sc[0] = sc[2] = -INFINITY;
+        if (2 * t + 1 >= Nk)
+            sc[1] = sc[3] = -INFINITY;
+        float m0 = fmaxf(sc[0], sc[1]), m1 = fmaxf(sc[2], sc[3]);
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+        const float p0 = ex2_approx(sc[0] - m0), p1 = ex2_approx(sc[1] - m0);
+        const float p2 = ex2_approx(sc[2] - m1), p3 = ex2_approx(sc[3] - m1);
+        float l0 = p0 + p1, l1 = p2 + p3;
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        uint32_t ph0, pl0, ph1, pl1;
+        split_bf16x2(p0, p1, ph0, pl0);
+        split_bf16x2(p2, p3, ph1, pl1);
+        const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+        const int qa = qc + g, qb = qa + 8;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            mma_bf16_k8(o, ph0, ph1, vh[nt]);
+            mma_bf16_k8(o, pl0, pl1, vh[nt]);
+            mma_bf16_k8(o, ph0, ph1, vl[nt]);
+            const long col = h * kManyC + nt * 8 + 2 * t;
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int q = r ? qb : qa;
+                if (q >= Nq)
+                    continue;
+                const float inv = r ? i1 : i0;
+                const long off = (pc * Nq + q) * D + col;
+                if (OUT_BF16)
+                    *reinterpret_cast<uint32_t *>(reinterpret_cast<__nv_bfloat16 *>(O) + off) =
+                        bf16_pair(o[2 * r] * inv, o[2 * r + 1] * inv);
+                else
+                    *reinterpret_cast<float2 *>(reinterpret_cast<float *>(O) + off) =
+                        make_float2(o[2 * r] * inv, o[2 * r + 1] * inv);
+            }
+        }
+        if (more) {
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                qr[k] = qx[k];
+            pc = pn;
+            qc = qn;
+            advance(pn, qn);
+        }
+    }
 }
 
 // Work of the many-keys kernel: the P prompts' 32-key chunks taken as one
@@ -790,19 +795,15 @@ template <bool Q_BF16, bool OUT_BF16>
 int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, const float *kp, long sk,
                 const float *vp, long sv, void *o, float scale, int num_sms, cudaStream_t st)
 {
-    const int smem = 2 * Nk * kHeads * (16 + 4) * 4;
-    cudaError_t e = smem_limit_once<mha_few2_kernel<Q_BF16, OUT_BF16>>(smem);
-    if (e != cudaSuccess)
-        return (int)e;
     int per_sm = 1;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mha_few2_kernel<Q_BF16, OUT_BF16>,
-                                                      256, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, mha_few2_kernel<Q_BF16, OUT_BF16>, 256, 0);
     if (e != cudaSuccess)
         return (int)e;
-    const long units = (long)P * ((Nq + 63) / 64);
+    const long units = (long)P * ((Nq + 15) / 16);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
-    mha_few2_kernel<Q_BF16, OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(
-        qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale);
+    mha_few2_kernel<Q_BF16, OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, 0, st>>>(
+        qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale * 1.4426950408889634f);
     return (int)cudaGetLastError();
 }
 

@@ -385,6 +385,7 @@ def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
     ("t2i", 64, 8, 5184, 128, False),
     ("t2i_shared", 64, 7, 5184, 128, True),
     ("i2t", 16, 5184, 8, 128, False),
+    ("i2t_7_ragged", 5, 1001, 7, 128, False),  # 7 keys, query units ending inside prompts
     ("self7", 64, 7, 7, 256, False),
     ("t2i_odd", 3, 11, 1000, 128, False),   # 2 query groups, ragged key splits
     ("t2i_5", 5, 8, 5184, 128, False),      # CTA chunk ranges end inside prompts
