@@ -721,48 +721,62 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
 
 // Combines the partials of each (prompt, query, head): those of the CTAs
 // whose chunk ranges meet the prompt's chunks [p nch, (p + 1) nch), at
-// segment p - (first prompt of the CTA); offsets in log2 units. One thread
-// per 4 output channels.
-__global__ void __launch_bounds__(128) mha_many_combine_kernel(const float *__restrict__ part,
+// segment p - (first prompt of the CTA); offsets in log2 units. One warp
+// per (prompt, query, head): the lanes take the records' offsets and sums
+// (lane = record) for the maximum and the weights, then half-warps take
+// alternate records, a lane one output channel, and the halves are added.
+__global__ void __launch_bounds__(256) mha_many_combine_kernel(const float *__restrict__ part,
                                                                float *__restrict__ O, int P,
                                                                int Nq, int nch, int G, int segs)
 {
-    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (p, qi, h, quad)
-    if (i >= (long)P * Nq * kHeads * 4)
-        return;
-    const int quad = (int)(i & 3);
-    const long g = i >> 2;
-    const int h = (int)(g % kHeads);
-    const int qi = (int)((g / kHeads) % Nq);
-    const long p = g / ((long)kHeads * Nq);
+    const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // (p, qi, h)
+    const int lane = threadIdx.x & 31;
+    if (w >= (long)P * Nq * kHeads)
+        return;  // warp-uniform
+    const int h = (int)(w % kHeads);
+    const int qi = (int)((w / kHeads) % Nq);
+    const long p = w / ((long)kHeads * Nq);
     const long T = (long)P * nch;
     // CTA holding chunk c: the largest x with x T / G <= c, i.e.
     // ceil((c + 1) G / T) - 1.
     const long x0 = ((p * nch + 1) * G + T - 1) / T - 1;
     const long x1 = (((p + 1) * nch) * G + T - 1) / T - 1;
-    auto rec = [&](long x) {
+    const int nr = (int)(x1 - x0 + 1);
+    auto rec = [&](int r) {
+        const long x = x0 + r;
         const long k = p - many_chunk0(x, T, G) / nch;
         return part + (((x * segs + k) * Nq + qi) * kHeads + h) * kPart;
     };
     float M = -INFINITY;
-    for (long x = x0; x <= x1; x++)
-        M = fmaxf(M, __ldg(rec(x)));
-    float L = 0.0f;
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (long x = x0; x <= x1; x++) {
-        const float *pt = rec(x);
-        const float2 ml = __ldg(reinterpret_cast<const float2 *>(pt));
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(pt + 4) + quad);
-        const float f = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);
-        L = fmaf(ml.y, f, L);
-        acc.x = fmaf(v.x, f, acc.x);
-        acc.y = fmaf(v.y, f, acc.y);
-        acc.z = fmaf(v.z, f, acc.z);
-        acc.w = fmaf(v.w, f, acc.w);
+    for (int r = lane; r < nr; r += 32)
+        M = fmaxf(M, __ldg(rec(r)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.0f, acc = 0.0f;
+    const int half = lane >> 4, c = lane & 15;
+    for (int r0 = 0; r0 < nr; r0 += 32) {
+        float f = 0.0f;
+        if (r0 + lane < nr) {
+            const float2 ml = __ldg(reinterpret_cast<const float2 *>(rec(r0 + lane)));
+            f = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);
+            L = fmaf(ml.y, f, L);
+        }
+        const int n = min(32, nr - r0);
+#pragma unroll 4
+        for (int jj = 0; jj < n; jj += 2) {  // same trip count in both halves
+            const int j = jj + half;
+            const float fj = __shfl_sync(0xffffffffu, f, j & 31);
+            if (j < n)
+                acc = fmaf(__ldg(rec(r0 + j) + 4 + c), fj, acc);
+        }
     }
-    const float inv = 1.0f / L;
-    reinterpret_cast<float4 *>(O + (p * Nq + qi) * kManyD + h * kManyC)[quad] =
-        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+        L += __shfl_xor_sync(0xffffffffu, L, o);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+    if (half == 0)
+        O[(p * Nq + qi) * kManyD + h * kManyC + c] = acc / L;
 }
 
 // Plan of the many-keys kernel: G CTAs per query group of 8 (two per SM
@@ -848,8 +862,8 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return (int)e;
-    const long total = (long)P * Nq * kHeads * 4;
-    mha_many_combine_kernel<<<(unsigned)((total + 127) / 128), 128, 0, st>>>(
+    const long total = (long)P * Nq * kHeads * 32;  // a warp per (prompt, query, head)
+    mha_many_combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
         static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk, pl.G, pl.segs);
     return (int)cudaGetLastError();
 }
