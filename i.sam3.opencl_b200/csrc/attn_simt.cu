@@ -5,6 +5,7 @@
 // does not take (sam3_kernels.cl:57-156). The mask decoder's attention is in
 // attn_decoder.cu.
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -14,7 +15,9 @@ namespace {
 
 // ------------------------------------------------------ fp32 attention
 // One thread per query row (128 per CTA), K/V tiles of 32 keys staged in
-// shared memory, online softmax per tile with expf. hd = 64.
+// shared memory, online softmax per tile with expf. hd = 64. Q, O and the
+// dot products are held as fp32 pairs for the packed f32x2 instructions
+// (each lane an IEEE fp32 fma; a score is four interleaved partial sums).
 constexpr int F_HD = 64;
 constexpr int F_BQ = 128;
 constexpr int F_BK = 32;
@@ -23,8 +26,8 @@ __global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict_
                                                        int N, int E, int heads, float scale,
                                                        float *__restrict__ out)
 {
-    __shared__ float ks[F_BK][F_HD];
-    __shared__ float vs[F_BK][F_HD];
+    __shared__ __align__(16) float ks[F_BK][F_HD];
+    __shared__ __align__(16) float vs[F_BK][F_HD];
     const int nqt = (N + F_BQ - 1) / F_BQ;
     const int qt = blockIdx.x % nqt;
     const int h = (blockIdx.x / nqt) % heads;
@@ -33,16 +36,14 @@ __global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict_
     const long base = (long)seq * N * ld;
     const int qi = qt * F_BQ + threadIdx.x;
     const bool valid = qi < N;
-    float q[F_HD], o[F_HD];
+    uint64_t q2[F_HD / 2], o2[F_HD / 2];
     const float *qp = qkv + base + (long)(valid ? qi : 0) * ld + h * F_HD;
 #pragma unroll
     for (int d = 0; d < F_HD; d += 4) {
         const float4 v = *reinterpret_cast<const float4 *>(qp + d);
-        q[d] = v.x * scale;
-        q[d + 1] = v.y * scale;
-        q[d + 2] = v.z * scale;
-        q[d + 3] = v.w * scale;
-        o[d] = o[d + 1] = o[d + 2] = o[d + 3] = 0.0f;
+        q2[d / 2] = f2_make(v.x * scale, v.y * scale);
+        q2[d / 2 + 1] = f2_make(v.z * scale, v.w * scale);
+        o2[d / 2] = o2[d / 2 + 1] = 0;
     }
     float m = -INFINITY, l = 0.0f;
     for (int k0 = 0; k0 < N; k0 += F_BK) {
@@ -64,25 +65,37 @@ __global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict_
         float mx = m;
 #pragma unroll
         for (int j = 0; j < F_BK; j++) {
-            float acc = 0.0f;
+            uint64_t a0 = 0, a1 = 0;
 #pragma unroll
-            for (int d = 0; d < F_HD; d++)
-                acc = fmaf(q[d], ks[j][d], acc);
+            for (int d = 0; d < F_HD; d += 4) {
+                const ulonglong2 k2 = *reinterpret_cast<const ulonglong2 *>(&ks[j][d]);
+                a0 = fma2(q2[d / 2], k2.x, a0);
+                a1 = fma2(q2[d / 2 + 1], k2.y, a1);
+            }
+            float x0, x1, x2, x3;
+            f2_split(a0, x0, x1);
+            f2_split(a1, x2, x3);
+            const float acc = (x0 + x1) + (x2 + x3);
             s[j] = j < nk ? acc : -INFINITY;
             mx = fmaxf(mx, s[j]);
         }
         const float corr = expf(m - mx);
         l *= corr;
+        const uint64_t c2 = f2_make(corr, corr);
 #pragma unroll
-        for (int d = 0; d < F_HD; d++)
-            o[d] *= corr;
+        for (int d = 0; d < F_HD / 2; d++)
+            o2[d] = mul2(o2[d], c2);
 #pragma unroll
         for (int j = 0; j < F_BK; j++) {
             const float p = expf(s[j] - mx);
             l += p;
+            const uint64_t p2 = f2_make(p, p);
 #pragma unroll
-            for (int d = 0; d < F_HD; d++)
-                o[d] = fmaf(p, vs[j][d], o[d]);
+            for (int d = 0; d < F_HD; d += 4) {
+                const ulonglong2 v2 = *reinterpret_cast<const ulonglong2 *>(&vs[j][d]);
+                o2[d / 2] = fma2(p2, v2.x, o2[d / 2]);
+                o2[d / 2 + 1] = fma2(p2, v2.y, o2[d / 2 + 1]);
+            }
         }
         m = mx;
     }
@@ -90,9 +103,12 @@ __global__ void __launch_bounds__(F_BQ) attn_f32_kernel(const float *__restrict_
         const float inv = 1.0f / l;
         float *op = out + ((long)seq * N + qi) * E + h * F_HD;
 #pragma unroll
-        for (int d = 0; d < F_HD; d += 4)
-            *reinterpret_cast<float4 *>(op + d) =
-                make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+        for (int d = 0; d < F_HD; d += 4) {
+            float a, b, c, e;
+            f2_split(o2[d / 2], a, b);
+            f2_split(o2[d / 2 + 1], c, e);
+            *reinterpret_cast<float4 *>(op + d) = make_float4(a * inv, b * inv, c * inv, e * inv);
+        }
     }
 }
 
