@@ -742,11 +742,12 @@ __global__ void __launch_bounds__(256) mha_many_combine_kernel(const float *__re
     const long x0 = ((p * nch + 1) * G + T - 1) / T - 1;
     const long x1 = (((p + 1) * nch) * G + T - 1) / T - 1;
     const int nr = (int)(x1 - x0 + 1);
-    auto rec = [&](int r) {
-        const long x = x0 + r;
-        const long k = p - many_chunk0(x, T, G) / nch;
-        return part + (((x * segs + k) * Nq + qi) * kHeads + h) * kPart;
-    };
+    // Only CTA x0 can start before the prompt (segment k0 > 0 of its
+    // range); every later one starts inside it (segment 0).
+    const long k0 = p - many_chunk0(x0, T, G) / nch;
+    const float *base = part + ((x0 * segs * Nq + qi) * kHeads + h) * kPart;
+    const long xstride = (long)segs * Nq * kHeads * kPart, kstride = (long)Nq * kHeads * kPart;
+    auto rec = [&](int r) { return base + r * xstride + (r == 0 ? k0 * kstride : 0); };
     float M = -INFINITY;
     for (int r = lane; r < nr; r += 32)
         M = fmaxf(M, __ldg(rec(r)));

@@ -113,6 +113,7 @@ struct AttnArgs {
     int nseq, Nq, Nk, heads, nqt, nitems, nkv, nfull, tsplit, nkv_t;
     int qcol, kcol, vcol;
     long ldo;
+    int ohd;  // output columns per head (16, 32 or 64): head h at column h * ohd
     float scale_log2;
     void *out;
     const float *bias;
@@ -525,12 +526,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 }
                 const float inv = 1.0f / lsum;
                 if (!is_part && q < a.Nq) {
-                    const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD;
+                    const long orow = (long)(seq * a.Nq + q) * a.ldo + head * a.ohd;
                     if (OUT_BF16) {
                         uint4 *dst = reinterpret_cast<uint4 *>(
                             reinterpret_cast<__nv_bfloat16 *>(a.out) + orow);
 #pragma unroll
                         for (int d = 0; d < HD; d += 8) {
+                            if (d >= a.ohd)
+                                break;
                             uint4 w;
                             w.x = pack_bf16x2(__uint_as_float(ov[d]) * inv, __uint_as_float(ov[d + 1]) * inv);
                             w.y = pack_bf16x2(__uint_as_float(ov[d + 2]) * inv, __uint_as_float(ov[d + 3]) * inv);
@@ -543,8 +546,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                         float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.out) + orow);
 #pragma unroll
                         for (int d = 0; d < HD; d += 4)
-                            dst[d / 4] = make_float4(__uint_as_float(ov[d]) * inv, __uint_as_float(ov[d + 1]) * inv,
-                                                     __uint_as_float(ov[d + 2]) * inv, __uint_as_float(ov[d + 3]) * inv);
+                            if (d < a.ohd)
+                                dst[d / 4] = make_float4(__uint_as_float(ov[d]) * inv, __uint_as_float(ov[d + 1]) * inv,
+                                                         __uint_as_float(ov[d + 2]) * inv, __uint_as_float(ov[d + 3]) * inv);
                     }
                 }
                 tc_fence_before();
@@ -608,8 +612,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
 #pragma unroll
         for (int o = 16; o; o >>= 1)
             L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (2 * lane >= a.ohd)
+            continue;  // beyond the head's output columns
         const float inv = 1.0f / L;
-        const long orow = (long)(seq * a.Nq + q) * a.ldo + head * HD + 2 * lane;
+        const long orow = (long)(seq * a.Nq + q) * a.ldo + head * a.ohd + 2 * lane;
         if (OUT_BF16)
             *reinterpret_cast<uint32_t *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + orow) =
                 pack_bf16x2(ox * inv, oy * inv);
@@ -640,15 +646,15 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, 
 
 // Work plan of a launch over `base` items of nkv KV tiles on 2 x sms CTA
 // slots. Launches of many waves run whole items. Otherwise the items that
-// do not fill the last wave (all of them when `all_split`, for few query
-// tiles) are split into parts: the divisor d of nkv that minimises the
+// do not fill the last wave (all of them when there are fewer items than
+// slots, as for few query tiles over many keys) are split into parts: the divisor d of nkv that minimises the
 // tail's time in KV-tile times, ceil(tail * d / slots) waves of nkv / d
 // tiles plus kPartCost for a part's start and partial store, plus
 // kMergeCost for the merge launch when d > 1 (measured: a 9-window launch
 // whose 128 tail items split in 2 ran slower, the 16-head global one whose
 // 64 tail items split in 9 faster). Returns the workspace bytes the split
 // needs (0 for none).
-size_t plan(AttnArgs &a, long base, int nkv, int sms, bool all_split)
+size_t plan(AttnArgs &a, long base, int nkv, int sms)
 {
     const long slots = 2L * sms;
     a.nkv = nkv;
@@ -656,9 +662,9 @@ size_t plan(AttnArgs &a, long base, int nkv, int sms, bool all_split)
     a.tsplit = 1;
     a.nkv_t = nkv;
     a.nitems = (int)base;
-    if (!all_split && base >= 8 * slots)
+    if (base >= 8 * slots)
         return 0;
-    const long nfull = all_split ? 0 : base / slots * slots;
+    const long nfull = base / slots * slots;
     const long tail = base - nfull;
     if (tail == 0)
         return 0;
@@ -686,7 +692,7 @@ size_t plan(AttnArgs &a, long base, int nkv, int sms, bool all_split)
 // Plans the launch (splitting only when ws holds the partial results) and
 // runs it.
 int run(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, AttnArgs &a,
-        bool out_bf16, bool all_split, void *ws, size_t ws_bytes, cudaStream_t st)
+        bool out_bf16, void *ws, size_t ws_bytes, cudaStream_t st)
 {
     a.nqt = (a.Nq + BQ - 1) / BQ;
     const long base = (long)a.nseq * a.heads * a.nqt;
@@ -695,7 +701,7 @@ int run(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, Att
         return K_EARG;
     const int sms = device_sms();
     const int nkv = (a.Nk + BKV - 1) / BKV;
-    size_t need = plan(a, base, nkv, sms, all_split);
+    size_t need = plan(a, base, nkv, sms);
     if (need && (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 15)))
         need = 0;  // no room for the partial results: whole items
     if (!need) {
@@ -722,13 +728,13 @@ int run(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, Att
 }
 
 // Workspace of a launch's plan.
-size_t workspace(int nseq, int Nq, int Nk, int heads, bool all_split)
+size_t workspace(int nseq, int Nq, int Nk, int heads)
 {
     if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0)
         return 0;
     AttnArgs a;
     const long base = (long)nseq * heads * ((Nq + BQ - 1) / BQ);
-    return plan(a, base, (Nk + BKV - 1) / BKV, device_sms(), all_split);
+    return plan(a, base, (Nk + BKV - 1) / BKV, device_sms());
 }
 
 }  // namespace
@@ -736,7 +742,7 @@ size_t workspace(int nseq, int Nq, int Nk, int heads, bool all_split)
 
 extern "C" size_t k_attn_tc_workspace(int nseq, int N, int heads)
 {
-    return sam3::workspace(nseq, N, N, heads, false);
+    return sam3::workspace(nseq, N, N, heads);
 }
 
 extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, float scale,
@@ -759,28 +765,30 @@ extern "C" int k_attn_tc(const void *qkv, int nseq, int N, int E, int heads, flo
     a.kcol = E;
     a.vcol = 2 * E;
     a.ldo = E;
+    a.ohd = HD;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = out;
     a.bias = nullptr;
     a.err = err;
-    return run(tq, tkv, tkv, a, out_bf16 != 0, false, ws, ws_bytes,
+    return run(tq, tkv, tkv, a, out_bf16 != 0, ws, ws_bytes,
                reinterpret_cast<cudaStream_t>(s));
 }
 
 extern "C" size_t k_attn_tc_cross_workspace(int nseq, int Nq, int Nk, int heads)
 {
-    return sam3::workspace(nseq, Nq, Nk, heads, true);
+    return sam3::workspace(nseq, Nq, Nk, heads);
 }
 
 extern "C" int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
                                long ldv, int nseq, int Nq, int Nk, int heads, float scale,
-                               const float *bias, void *out, long ldo, int out_bf16, void *ws,
-                               size_t ws_bytes, int *err, k_stream s)
+                               const float *bias, void *out, long ldo, int ohd, int out_bf16,
+                               void *ws, size_t ws_bytes, int *err, k_stream s)
 {
     using namespace sam3;
     const long W = (long)heads * HD;
     if (nseq <= 0 || Nq <= 0 || Nk <= 0 || heads <= 0 || ldq < W || ldk < W || ldv < W ||
-        ldo < W || (ldo * (out_bf16 ? 2 : 4)) % 16 || (reinterpret_cast<uintptr_t>(out) & 15))
+        (ohd != 16 && ohd != 32 && ohd != HD) || ldo < (long)heads * ohd ||
+        (ldo * (out_bf16 ? 2 : 4)) % 16 || (reinterpret_cast<uintptr_t>(out) & 15))
         return K_EARG;
     CUtensorMap tq, tk, tv;
     if (!make_tmap_bf16(&tq, Q, (uint64_t)nseq * Nq, (uint64_t)W, (uint64_t)ldq, BQ) ||
@@ -796,9 +804,10 @@ extern "C" int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk,
     a.kcol = 0;
     a.vcol = 0;
     a.ldo = ldo;
+    a.ohd = ohd;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = out;
     a.bias = bias;
     a.err = err;
-    return run(tq, tk, tv, a, out_bf16 != 0, true, ws, ws_bytes, reinterpret_cast<cudaStream_t>(s));
+    return run(tq, tk, tv, a, out_bf16 != 0, ws, ws_bytes, reinterpret_cast<cudaStream_t>(s));
 }

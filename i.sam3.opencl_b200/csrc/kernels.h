@@ -88,12 +88,15 @@ size_t k_attn_tc_workspace(int nseq, int N, int heads);
 /* The same kernel for cross-attention: nseq sequences of Nq query rows of
  * Q and Nk key / value rows of K and V (bf16, leading dimensions ldq / ldk /
  * ldv in elements, head h at column 64 h, 16-byte aligned rows), out rows
- * seq * Nq + q with leading dimension ldo (head h at column 64 h), fp32
- * (bf16 only without a bias). bias: NULL, or fp32 [nseq, heads, Nq, Nk]
- * added to the scaled scores, in log2 units (natural-log bias x log2 e). */
+ * seq * Nq + q with leading dimension ldo, the first ohd (16, 32 or 64)
+ * columns of head h at column ohd h (heads narrower than 64 given
+ * zero-padded: their real columns written straight to the caller's
+ * layout), fp32 (bf16 only without a bias). bias: NULL, or fp32 [nseq,
+ * heads, Nq, Nk] added to the scaled scores, in log2 units (natural-log
+ * bias x log2 e). */
 int k_attn_tc_cross(const void *Q, long ldq, const void *K, long ldk, const void *V,
                     long ldv, int nseq, int Nq, int Nk, int heads, float scale,
-                    const float *bias, void *out, long ldo, int out_bf16, void *ws,
+                    const float *bias, void *out, long ldo, int ohd, int out_bf16, void *ws,
                     size_t ws_bytes, int *err, k_stream s);
 /* Device workspace k_attn_tc_cross needs to split the keys of its items
  * over CTAs and merge the partial results (0: no split planned); with less,

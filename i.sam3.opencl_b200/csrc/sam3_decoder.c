@@ -82,10 +82,9 @@ struct cb_decoder {
     size_t mha_ws_bytes;
     /* layer 0's token -> image attention on the tensor cores: the shared
      * keys / values with heads padded to 64 columns (bf16 [T, 512], set
-     * with the image), the queries and output in that layout, and the
-     * key-split workspace */
+     * with the image), the queries in that layout, and the key-split
+     * workspace (the kernel writes the 16 real columns of each head) */
     void *k0_pad, *v0_pad, *q_pad;
-    float *o_pad;
     void *xws;
     size_t xws_bytes;
     float *h_tok;               /* host [batch * 8, 256] */
@@ -118,7 +117,7 @@ void cb_decoder_free(cb_decoder *d)
                        d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
                        d->bv, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws, d->k0_pad, d->v0_pad, d->q_pad,
-                       d->o_pad, d->xws};
+                       d->xws};
 
         for (i = 0; i < (int)(sizeof(dev) / sizeof(dev[0])); i++)
             cudaFree(dev[i]);
@@ -191,7 +190,6 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->k0_pad, T * 512 * 2);
     A(d->v0_pad, T * 512 * 2);
     A(d->q_pad, nt * 512 * 2);
-    A(d->o_pad, nt * 512 * 4);
     for (i = 1; i <= batch; i++) {  /* fewer prompts split the keys more */
         const size_t w = k_attn_tc_cross_workspace(1, i * DEC_NTOK, DEC_T, 8);
 
@@ -481,12 +479,10 @@ static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, 
                k_pad_heads64(d->sq, 0, 128, nt, 8, 16, d->q_pad,
                              (k_stream)b->stream));
         LAUNCH("dec_mha_t2i", 4.0 * nt * (double)DEC_T * 128,
-               (double)nt * 512 * 2 + 2.0 * DEC_T * 512 * 2 + (double)nt * 512 * 4,
+               (double)nt * 512 * 2 + 2.0 * DEC_T * 512 * 2 + (double)nt * 128 * 4,
                k_attn_tc_cross(d->q_pad, 512, d->k0_pad, 512, d->v0_pad, 512, 1, (int)nt, DEC_T,
-                               8, 0.25f, NULL, d->o_pad, 512, 0, d->xws, d->xws_bytes, b->d_err,
+                               8, 0.25f, NULL, d->so, 128, 16, 0, d->xws, d->xws_bytes, b->d_err,
                                (k_stream)b->stream));
-        LAUNCH("dec_pad", 0, (double)nt * 512 * 4 + (double)nt * 128 * 4,
-               k_unpack_heads64(d->o_pad, nt, 8, 16, d->so, 128, (k_stream)b->stream));
         return CB_OK;
     }
     LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,

@@ -405,26 +405,25 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
     if (mode == CB_ATTN_TC && !causal && !dy && Nq == Nk && Nq >= 1024 &&
         ldq % 4 == 0 && ldk % 4 == 0 && ldv % 4 == 0 && ldo % 4 == 0 &&
         aligned16(Q->ptr) && aligned16(K->ptr) && aligned16(V->ptr) && aligned16(O->ptr)) {
-        /* tensor cores: heads zero-padded to 64 columns in bf16 */
-        const size_t packed = (size_t)Nq * 3 * heads * 64 * 2, out = (size_t)Nq * heads * 64 * 4;
-        const size_t wsb = k_attn_tc_workspace(1, Nq, heads);
+        /* tensor cores: heads zero-padded to 64 columns in bf16; the kernel
+         * writes each head's hd real columns into O */
+        const size_t E64 = (size_t)heads * 64;
+        const size_t packed = al256((size_t)Nq * 3 * E64 * 2);
+        const size_t wsb = k_attn_tc_cross_workspace(1, Nq, Nq, heads);
         char *s = NULL;
 
-        CB_TRY(cbi_scratch(b, packed + out + wsb, (void **)&s));
+        CB_TRY(cbi_scratch(b, packed + wsb, (void **)&s));
         CB_TRY(cbi_kstatus(b,
                            k_pack_qkv_pad64((const float *)Q->ptr, ldq, (const float *)K->ptr,
                                             ldk, (const float *)V->ptr, ldv, Nq, heads, hd, s,
                                             st),
                            "attend: pack"));
-        CB_TRY(cbi_kstatus(b,
-                           k_attn_tc(s, 1, Nq, heads * 64, heads, 1.0f / sqrtf((float)hd),
-                                     s + packed, 0, wsb ? s + packed + out : NULL, wsb,
-                                     b->d_err, st),
-                           "attend"));
         return cbi_kstatus(b,
-                           k_unpack_heads64((const float *)(s + packed), Nq, heads, hd,
-                                            (float *)O->ptr, ldo, st),
-                           "attend: unpack");
+                           k_attn_tc_cross(s, (long)(3 * E64), s + E64 * 2, (long)(3 * E64),
+                                           s + 2 * E64 * 2, (long)(3 * E64), 1, Nq, Nq, heads,
+                                           1.0f / sqrtf((float)hd), NULL, O->ptr, (long)ldo, hd,
+                                           0, wsb ? s + packed : NULL, wsb, b->d_err, st),
+                           "attend");
     }
     /* (k_rpb_bias stages a row's Nk / W + W bias terms in 48 KB of shared
      * memory) */
@@ -438,17 +437,15 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
         const size_t E64 = (size_t)heads * 64;
         const size_t szq = al256((size_t)Nq * E64 * 2), szk = al256((size_t)Nk * E64 * 2);
         const size_t szb = dy ? al256((size_t)heads * Nq * Nk * 4) : 0;
-        const size_t szo = al256((size_t)Nq * E64 * 4);
         const size_t szw = k_attn_tc_cross_workspace(1, Nq, Nk, heads);
-        char *s = NULL, *qp, *kp, *vp, *bp, *op, *wp;
+        char *s = NULL, *qp, *kp, *vp, *bp, *wp;
 
-        CB_TRY(cbi_scratch(b, szq + 2 * szk + szb + szo + szw, (void **)&s));
+        CB_TRY(cbi_scratch(b, szq + 2 * szk + szb + szw, (void **)&s));
         qp = s;
         kp = qp + szq;
         vp = kp + szk;
         bp = vp + szk;
-        op = bp + szb;
-        wp = op + szo;
+        wp = bp + szb;
         CB_TRY(cbi_kstatus(b, k_pad_heads64(Q->ptr, 0, ldq, Nq, heads, hd, qp, st), "attend: pack"));
         CB_TRY(cbi_kstatus(b, k_pad_heads64(K->ptr, 0, ldk, Nk, heads, hd, kp, st), "attend: pack"));
         CB_TRY(cbi_kstatus(b, k_pad_heads64(V->ptr, 0, ldv, Nk, heads, hd, vp, st), "attend: pack"));
@@ -457,16 +454,12 @@ int cb_attend(cb_backend *b, int Nq, int Nk, int heads, int hd, cb_mem Q, int ld
                                k_rpb_bias((const float *)dy->ptr, (const float *)dx->ptr, Nq, Nk,
                                           W, heads, (float *)bp, st),
                                "attend: bias"));
-        CB_TRY(cbi_kstatus(b,
+        return cbi_kstatus(b,
                            k_attn_tc_cross(qp, (long)E64, kp, (long)E64, vp, (long)E64, 1, Nq, Nk,
                                            heads, 1.0f / sqrtf((float)hd),
-                                           dy ? (const float *)bp : NULL, op, (long)E64, 0,
-                                           szw ? wp : NULL, szw, b->d_err, st),
-                           "attend"));
-        return cbi_kstatus(b,
-                           k_unpack_heads64((const float *)op, Nq, heads, hd, (float *)O->ptr,
-                                            ldo, st),
-                           "attend: unpack");
+                                           dy ? (const float *)bp : NULL, O->ptr, (long)ldo, hd,
+                                           0, szw ? wp : NULL, szw, b->d_err, st),
+                           "attend");
     }
     {
         const size_t wsb = k_attend_workspace(Nq, Nk, heads, hd, b->num_sms);
