@@ -34,25 +34,32 @@ inline int grid_for(long n, int block)
 
 // q, k, v fp32 [N, ld*] (head h at column h * hd) -> bf16 [N, 3 * heads * 64]
 // (q | k | v blocks, head h at column h * 64), columns hd..63 of each head
-// zero. One thread per 4 output columns.
-__global__ void __launch_bounds__(256) pack_qkv_kernel(const float *__restrict__ q, int ldq,
+// zero. A CTA per kPackRows rows, a thread per 4 output columns.
+constexpr int kPackRows = 4;
+__global__ void __launch_bounds__(128) pack_qkv_kernel(const float *__restrict__ q, int ldq,
                                                        const float *__restrict__ k, int ldk,
                                                        const float *__restrict__ v, int ldv,
                                                        long N, int heads, int hd,
                                                        uint2 *__restrict__ out)
 {
-    const int E = heads * 64, q4 = 3 * E / 4;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < N * q4;
-         i += (long)gridDim.x * blockDim.x) {
-        const long n = i / q4;
-        const int c = (int)(i % q4) * 4, blk = c / E, hc = c % E, h = hc / 64, d = hc % 64;
-        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (d < hd) {
+    const int e4 = heads * 16;  // 4-column groups per block of q, k or v
+    for (int r = 0; r < kPackRows; r++) {
+        const long n = (long)blockIdx.x * kPackRows + r;
+        if (n >= N)
+            return;
+#pragma unroll
+        for (int blk = 0; blk < 3; blk++) {
             const float *src = blk == 0 ? q + n * ldq : (blk == 1 ? k + n * ldk : v + n * ldv);
-            x = *reinterpret_cast<const float4 *>(src + h * hd + d);
+            uint2 *dst = out + (n * 3 + blk) * e4;
+            for (int c4 = threadIdx.x; c4 < e4; c4 += blockDim.x) {
+                const int h = c4 >> 4, d = (c4 & 15) * 4;
+                float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (d < hd)
+                    x = __ldg(reinterpret_cast<const float4 *>(src + h * hd + d));
+                __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y), hi = __floats2bfloat162_rn(x.z, x.w);
+                dst[c4] = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+            }
         }
-        __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y), hi = __floats2bfloat162_rn(x.z, x.w);
-        out[i] = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
     }
 }
 
@@ -73,32 +80,35 @@ __global__ void __launch_bounds__(256) unpack_heads_kernel(const float *__restri
 
 // One operand of a cross-attention, fp32 or bf16 [rows, ld] (head h at
 // column h * hd) -> bf16 [rows, heads * 64] with columns hd..63 of each
-// head zero (the tcgen05 attention's layout). One thread per 4 output
-// columns.
+// head zero (the tcgen05 attention's layout). A CTA per kPackRows rows, a
+// thread per 4 output columns.
 template <bool SRC_BF16>
-__global__ void __launch_bounds__(256) pad_heads_kernel(const void *__restrict__ src, long ld,
+__global__ void __launch_bounds__(128) pad_heads_kernel(const void *__restrict__ src, long ld,
                                                         long rows, int heads, int hd,
                                                         uint2 *__restrict__ out)
 {
-    const int q4 = heads * 16;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < rows * q4;
-         i += (long)gridDim.x * blockDim.x) {
-        const long n = i / q4;
-        const int c = (int)(i % q4) * 4, h = c / 64, d = c % 64;
-        uint2 w = make_uint2(0u, 0u);
-        if (d < hd) {
-            if (SRC_BF16)
-                w = *reinterpret_cast<const uint2 *>(
-                    reinterpret_cast<const __nv_bfloat16 *>(src) + n * ld + h * hd + d);
-            else {
-                const float4 x = *reinterpret_cast<const float4 *>(
-                    reinterpret_cast<const float *>(src) + n * ld + h * hd + d);
-                __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y),
-                               hi = __floats2bfloat162_rn(x.z, x.w);
-                w = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+    const int e4 = heads * 16;
+    for (int r = 0; r < kPackRows; r++) {
+        const long n = (long)blockIdx.x * kPackRows + r;
+        if (n >= rows)
+            return;
+        for (int c4 = threadIdx.x; c4 < e4; c4 += blockDim.x) {
+            const int h = c4 >> 4, d = (c4 & 15) * 4;
+            uint2 w = make_uint2(0u, 0u);
+            if (d < hd) {
+                if (SRC_BF16)
+                    w = __ldg(reinterpret_cast<const uint2 *>(
+                        reinterpret_cast<const __nv_bfloat16 *>(src) + n * ld + h * hd + d));
+                else {
+                    const float4 x = __ldg(reinterpret_cast<const float4 *>(
+                        reinterpret_cast<const float *>(src) + n * ld + h * hd + d));
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y),
+                                   hi = __floats2bfloat162_rn(x.z, x.w);
+                    w = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+                }
             }
+            out[n * e4 + c4] = w;
         }
-        out[i] = w;
     }
 }
 
@@ -272,8 +282,7 @@ extern "C" int k_pack_qkv_pad64(const float *q, int ldq, const float *k, int ldk
         (ldv & 3) || (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k) & 15) ||
         (reinterpret_cast<uintptr_t>(v) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
         return K_EARG;
-    const int grid = grid_for(N * 3 * heads * 16, 256);
-    pack_qkv_kernel<<<grid < 148 * 16 ? grid : 148 * 16, 256, 0, STREAM(s)>>>(
+    pack_qkv_kernel<<<grid_for(N, kPackRows), 128, 0, STREAM(s)>>>(
         q, ldq, k, ldk, v, ldv, N, heads, hd, reinterpret_cast<uint2 *>(out));
     return (int)cudaGetLastError();
 }
@@ -297,13 +306,12 @@ extern "C" int k_pad_heads64(const void *src, int src_bf16, long ld, long rows, 
         (reinterpret_cast<uintptr_t>(src) & (src_bf16 ? 7 : 15)) ||
         (reinterpret_cast<uintptr_t>(out) & 7))
         return K_EARG;
-    const int grid = grid_for(rows * heads * 16, 256);
-    const int g = grid < 148 * 16 ? grid : 148 * 16;
+    const int g = grid_for(rows, kPackRows);
     if (src_bf16)
-        pad_heads_kernel<true><<<g, 256, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
+        pad_heads_kernel<true><<<g, 128, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
                                                           reinterpret_cast<uint2 *>(out));
     else
-        pad_heads_kernel<false><<<g, 256, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
+        pad_heads_kernel<false><<<g, 128, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
                                                            reinterpret_cast<uint2 *>(out));
     return (int)cudaGetLastError();
 }
