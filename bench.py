@@ -67,14 +67,20 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling during the timed region (one sampler, on rank 0,
+    for all the job's GPUs). Entering waits for the first sample, so that
+    a short timed region (8 GPUs: a few hundred ms) still has samples
+    inside it."""
 
-    def __init__(self, gpus):
+    def __init__(self, gpus, active=True):
         self.gpus = gpus
+        self.active = active
         self.proc = None
         self.path = f"/tmp/sam3_bench_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
+        if not self.active:
+            return self
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -82,10 +88,18 @@ class Clocks:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", ",".join(str(g) for g in self.gpus),
-                 f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200"],
+                 f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        t0 = time.time()
+        while self.proc and self.proc.poll() is None and time.time() - t0 < 5.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *a):
@@ -95,6 +109,8 @@ class Clocks:
             self.f.close()
 
     def summary(self):
+        if not self.active:
+            return None
         try:
             rows = [r.split(",") for r in open(self.path).read().strip().splitlines()]
         except Exception:
@@ -114,6 +130,19 @@ class Clocks:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_indices(devs):
+    """nvidia-smi indices of CUDA devices (through CUDA_VISIBLE_DEVICES when
+    it lists plain indices)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    try:
+        phys = [int(x) for x in vis.split(",")] if vis else None
+    except ValueError:
+        phys = None
+    if phys is None:
+        return devs
+    return [phys[d] for d in devs if d < len(phys)]
 
 
 def dist_setup(args):
@@ -610,7 +639,8 @@ def our_arm(args, world, rank, local, pg):
         enc.encode_tiles(m_tiles, n, m_out)
     barrier()
     # `value`: the timed steps with the backend's per-launch profiler off
-    with Clocks([local] if world == 1 else list(range(world))) as clk:
+    with Clocks(smi_indices([local] if world == 1 else list(range(world))),
+                active=rank == 0) as clk:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
