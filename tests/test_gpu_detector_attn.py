@@ -91,6 +91,29 @@ def test_attend_tensor_core_cross_vs_oracle(cb, sb, ob, Nq, Nk, heads, hd, rpb):
     assert np.abs(got - want).max() <= 1e-2 * max(1.0, float(np.abs(want).max()))
 
 
+@pytest.mark.parametrize("Nq,Nk,hd", [(1500, 1500, 32), (300, 1500, 32), (150, 2000, 64)])
+def test_attend_tensor_core_strided_output_vs_oracle(cb, sb, ob, Nq, Nk, hd):
+    """Row strides wider than the heads (inputs and output): the tensor-core
+    kernel writes each head's hd real columns straight into the caller's
+    rows and leaves the columns past the heads untouched."""
+    heads = 4
+    E = heads * hd
+    lq, lk, lo = E + 4, E + 8, E + 12
+    Q = ob.normal(64, 1, (Nq, lq))
+    K = ob.normal(64, 2, (Nk, lk))
+    V = ob.normal(64, 3, (Nk, lk))
+    up = lambda a: cb.upload(np.ascontiguousarray(a, np.float32), sb.F32)  # noqa: E731
+    O = up(np.full((Nq, lo), 7.0, np.float32))
+    cb.attend(Nq, Nk, heads, hd, up(Q), lq, up(K), lk, up(V), lk, O, lo, 0, None, None, 0, 0)
+    got = np.empty((Nq, lo), np.float32)
+    cb.read(O, got)
+    want = ob.attend(Q[:, :E], K[:, :E], V[:, :E], heads, hd)
+    assert (got[:, E:] == 7.0).all()
+    a, b = got[:, :E].astype(np.float64).ravel(), want.astype(np.float64).ravel()
+    assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) >= 0.9999
+    assert np.abs(got[:, :E] - want).max() <= 1e-2
+
+
 def test_attend_rejects_bad_shapes(cb, sb):
     m = cb.alloc(64 * 64 * 4, sb.F32)
     with pytest.raises(sb.CBError):
