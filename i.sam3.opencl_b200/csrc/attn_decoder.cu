@@ -54,16 +54,6 @@ __device__ __forceinline__ uint32_t bf16_pair(float lo, float hi)
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-__device__ __forceinline__ void cp_async_commit()
-{
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait()
-{
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // ------------------------------------------------------------ few keys
 constexpr int kFewSmall = 8;              // key counts up to this take two passes
@@ -235,7 +225,7 @@ constexpr int kPart = 4 + kManyC;          // m, l, 2 unused, o[16] (16-byte ali
 constexpr float kManyLazy = 8.0f;          // rescale threshold (log2 units)
 // One stage: K then V, each [8 heads][32 keys][16 channels].
 constexpr int kManyStage = 2 * kHeads * kChunk * kManyC;  // elements
-constexpr int kManySmem = kStages * kManyStage * 4;       // bytes, fp32 K/V
+constexpr int kManySmem = kStages * kManyStage * 4;       // bytes, fp32 K/V ring
 
 // The bf16 tensor-core step: D += A (16 x 16, row-major) . B (16 x 8).
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -280,22 +270,16 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p, boo
                      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
 }
 
-// 16 bytes global -> shared, zero-filled when `bytes` is 0.
-__device__ __forceinline__ void cp_async16z(void *smem, const void *gmem, int bytes)
-{
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(bytes)
-                 : "memory");
-}
-
-// Staged key row layout, per (K or V, head): 32 rows of the head's 16
-// channels. fp32 rows are 64 bytes whose 16-byte pieces are XOR-swizzled by
-// 2 ((row >> 1) & 1), bf16 rows 32 bytes whose two pieces are swizzled by
-// (row >> 2) & 1, so that the fragment loads of one warp (8 rows x a few
-// channels) hit every bank group equally.
+// Staged key tile layout, per (K or V, head): 32 rows of the head's 16
+// channels, written by one TMA box load with the hardware swizzle that
+// matches the row size: fp32 rows are 64 bytes whose 16-byte pieces are
+// XOR-ed with (row >> 1) & 3 (64-byte swizzle), bf16 rows 32 bytes whose
+// two pieces are XOR-ed with (row >> 2) & 1 (32-byte swizzle); tiles start
+// 1024-byte aligned. The fragment loads of one warp (8 rows x a few
+// channels) then hit every bank group equally.
 __device__ __forceinline__ int many_sw32(int row, int piece)  // fp32: float offset in row
 {
-    return (piece ^ (2 * ((row >> 1) & 1))) * 4;
+    return (piece ^ ((row >> 1) & 3)) * 4;
 }
 
 __device__ __forceinline__ int many_sw16(int row, int piece)  // bf16: element offset in row
@@ -495,17 +479,23 @@ __host__ __device__ __forceinline__ long many_chunk0(long g, long T, long G)
 // the chunk's exceeds it by kManyLazy; P transposed into B fragments by
 // movmatrix. At the end of each prompt in the CTA's range one (m, l, o)
 // partial per (query, head).
+constexpr int kManyThreads = 32 * (kHeads + 1);  // 8 head warps + the producer warp
+
 template <bool KV_BF16>
-__global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
-    const float *__restrict__ Q, long sq, const void *__restrict__ Kv, long sk,
-    const void *__restrict__ Vv, long sv, float *__restrict__ part, int P, int Nq, int Nk,
-    int segs, float qscale)
+__global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    const float *__restrict__ Q, long sq, int k_per_prompt, int v_per_prompt,
+    float *__restrict__ part, int P, int Nq, int Nk, int segs, float qscale, int *err)
 {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(16) float sm_raw[];
     constexpr int ESZ = KV_BF16 ? 2 : 4;
     constexpr int STAGE_B = kManyStage * ESZ;             // bytes per stage
     constexpr int TILE_B = kChunk * kManyC * ESZ;          // bytes per (K or V, head)
-    char *smb = reinterpret_cast<char *>(sm);
+    char *smb = reinterpret_cast<char *>(
+        (reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smb + kStages * STAGE_B);
+    uint64_t *empty = full + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
     const int nch = (Nk + kChunk - 1) / kChunk;
     const long T = (long)P * nch, G = gridDim.x;
     const long c0 = many_chunk0(blockIdx.x, T, G), c1 = many_chunk0(blockIdx.x + 1, T, G);
@@ -514,14 +504,6 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
     const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int qz = blockIdx.z * 8;
-
-    // Staging: thread -> (head, piece) and rows r0 + R k of the chunk.
-    constexpr int PIECES = kManyC * ESZ / 16;              // 16-byte pieces per head row
-    constexpr int TPR = kHeads * PIECES;                   // threads per key row
-    constexpr int R = 256 / TPR;                           // row step
-    const int sh = (threadIdx.x % TPR) / PIECES, spc = threadIdx.x % PIECES;
-    const int r0 = threadIdx.x / TPR;
-    const int soff = KV_BF16 ? many_sw16(r0, spc) * 2 : many_sw32(r0, spc) * 4;  // bytes
     // Chunk cursors (prompt, chunk of the prompt), advanced without division.
     struct Cur {
         long p;
@@ -533,23 +515,45 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
             c.p++;
         }
     };
-    const long src0 = ((long)r0 * kManyD + sh * kManyC) * ESZ + spc * 16;  // bytes
-    auto stage = [&](const Cur &c, int b) {
-        const int j0 = c.ci * kChunk, n = min(kChunk, Nk - j0);
-        const char *kb = reinterpret_cast<const char *>(Kv) + (c.p * sk + (long)j0 * kManyD) * ESZ;
-        const char *vb = reinterpret_cast<const char *>(Vv) + (c.p * sv + (long)j0 * kManyD) * ESZ;
-        char *dk = smb + b * STAGE_B + sh * TILE_B + soff;
-        char *dv = dk + kHeads * TILE_B;
-#pragma unroll
-        for (int k = 0; k < kChunk / R; k++) {
-            const int r = r0 + k * R;
-            const int ok = r < n ? 16 : 0;  // rows past the keys: zero-filled
-            const long src = ok ? src0 + (long)k * R * kManyD * ESZ : 0;
-            cp_async16z(dk + r * kManyC * ESZ, kb + src, ok);
-            cp_async16z(dv + r * kManyC * ESZ, vb + src, ok);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kHeads);
         }
-        cp_async_commit();
-    };
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (h == kHeads) {  // producer warp: one thread issues the ring's TMA box loads
+        if (lane == 0 && nloc > 0) {
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            Cur c = {p_first, (int)(c0 - p_first * nch)};
+            int issued = 0;
+            for (int i = 0; i < nloc; i++, advance(c)) {
+                const int b = i % kStages;
+                if (i >= kStages && !mbar_wait(&empty[b], ((i / kStages) - 1) & 1, err, abort_flag))
+                    break;
+                mbar_arrive_expect_tx(&full[b], 2 * kHeads * TILE_B);
+                char *dst = smb + b * STAGE_B;
+                const int j0 = c.ci * kChunk;
+                const int zk = k_per_prompt ? (int)c.p : 0, zv = v_per_prompt ? (int)c.p : 0;
+#pragma unroll
+                for (int hh = 0; hh < kHeads; hh++) {
+                    tma_load_3d(dst + hh * TILE_B, &tmK, &full[b], hh * kManyC, j0, zk);
+                    tma_load_3d(dst + (kHeads + hh) * TILE_B, &tmV, &full[b], hh * kManyC, j0, zv);
+                }
+                issued = i + 1;
+            }
+            // copies in flight land before the CTA exits (bounded wait)
+            volatile int no_abort = 0;
+            for (int i = issued - kStages; i < issued; i++)
+                if (i >= 0)
+                    mbar_wait(&full[i % kStages], (i / kStages) & 1, err, &no_abort);
+        }
+        return;
+    }
 
     uint32_t qh[2], ql[2];  // B fragments of Q^T (hi, lo)
     float o[2][4], m[2], l[2];  // O^T per key block (two independent MMA chains)
@@ -592,29 +596,17 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
         }
     };
 
-    Cur cur = {p_first, (int)(c0 - p_first * nch)}, ahead = cur;
-    for (int i = 0; i < kStages - 1; i++) {
-        if (i < nloc) {
-            stage(ahead, i);
-            advance(ahead);
-        }
-        else
-            cp_async_commit();
-    }
+    // Head warps: each waits for a stage, computes its head, releases the
+    // stage (one arrival per warp); no CTA-wide barrier in the loop.
+    Cur cur = {p_first, (int)(c0 - p_first * nch)};
     for (int i = 0; i < nloc; i++, advance(cur)) {
         const int b = i % kStages;
         const long p = cur.p;
         const int ci = cur.ci;
         if (i == 0 || ci == 0)
             start_segment(p);
-        if (i + kStages - 1 < nloc) {  // its stage was released by the barrier below
-            stage(ahead, (i + kStages - 1) % kStages);
-            advance(ahead);
-        }
-        else
-            cp_async_commit();
-        cp_async_wait<kStages - 1>();
-        __syncthreads();
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[b], (i / kStages) & 1, err, abort_flag)))
+            break;
         const int n = min(kChunk, Nk - ci * kChunk);
         const char *tk = smb + b * STAGE_B + h * TILE_B;
         const char *tv = tk + kHeads * TILE_B;
@@ -713,7 +705,9 @@ __global__ void __launch_bounds__(256, 2) mha_many_split_kernel(
                 mma_bf16(o[blk], ah, pl0, pl1);
             }
         }
-        __syncthreads();  // stage b may be refilled from the next iteration on
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[b]);  // this warp is done with stage b
         if (ci == nch - 1 || i == nloc - 1)
             flush(p - p_first);
     }
@@ -847,19 +841,32 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
 template <bool KV_BF16>
 int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp, long sk,
                 const void *vp, long sv, float *o, void *ws, size_t ws_bytes, float scale,
-                int num_sms, cudaStream_t st)
+                int *err, int num_sms, cudaStream_t st)
 {
     const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
-    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15))
+    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15) ||
+        !err || (long)P > 0x7fffffffL)
         return K_EARG;
-    const int smem = KV_BF16 ? kManySmem / 2 : kManySmem;
+    // K and V as [P][Nk][128] boxes of 32 keys x one head's 16 channels
+    // (prompt pitch sk / sv elements; 0: one block shared by all prompts)
+    const CUtensorMapDataType dt =
+        KV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const CUtensorMapSwizzle swz = KV_BF16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const uint32_t es = KV_BF16 ? 2 : 4;
+    CUtensorMap tk, tv;
+    if (!make_tmap_3d(&tk, dt, es, kp, (uint64_t)P, (uint64_t)Nk, kManyD, kManyD, (uint64_t)sk,
+                      kManyC, kChunk, swz) ||
+        !make_tmap_3d(&tv, dt, es, vp, (uint64_t)P, (uint64_t)Nk, kManyD, kManyD, (uint64_t)sv,
+                      kManyC, kChunk, swz))
+        return K_ETMAP;
+    const int smem = (KV_BF16 ? kManySmem / 2 : kManySmem) + 1024 + 64;  // ring, alignment, barriers
     cudaError_t e = smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
     if (e != cudaSuccess)
         return (int)e;
     dim3 grid(pl.G, 1, (Nq + 7) / 8);
-    mha_many_split_kernel<KV_BF16><<<grid, 256, smem, st>>>(
-        qp, sq, kp, sk, vp, sv, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
-        scale * 1.4426950408889634f);
+    mha_many_split_kernel<KV_BF16><<<grid, kManyThreads, smem, st>>>(
+        tk, tv, qp, sq, sk != 0, sv != 0, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
+        scale * 1.4426950408889634f, err);
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return (int)e;
@@ -881,7 +888,7 @@ extern "C" size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms)
 
 extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,
                      long sk, const float *vp, long sv, float *o, void *ws, size_t ws_bytes,
-                     int num_sms, k_stream s)
+                     int *err, int num_sms, k_stream s)
 {
     using namespace sam3;
     const int c = dint / kHeads;
@@ -895,7 +902,7 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         // The reference rejects the same shape (sam3_model.c:429-430).
         if (c != kManyC)
             return K_EARG;
-        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes, scale,
+        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes, scale, err,
                                   num_sms, st);
     }
     if (c == 16)
@@ -919,7 +926,7 @@ extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, co
 
 extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                                 long sk, const void *vp, long sv, float *o, void *ws,
-                                size_t ws_bytes, int num_sms, k_stream s)
+                                size_t ws_bytes, int *err, int num_sms, k_stream s)
 {
     using namespace sam3;
     if (P <= 0 || Nq <= 0 || Nk <= 64 || P > 65535 || ((uintptr_t)qp & 15) ||
@@ -927,5 +934,5 @@ extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq,
         (sk & 7) || (sv & 7))
         return K_EARG;
     return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes,
-                             1.0f / sqrtf((float)kManyC), num_sms, STREAM(s));
+                             1.0f / sqrtf((float)kManyC), err, num_sms, STREAM(s));
 }

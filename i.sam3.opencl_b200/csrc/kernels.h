@@ -137,11 +137,13 @@ int k_cast_bf16_f32(const void *x, float *y, long n, k_stream s);
 
 /* Decoder attention (sam3_kernels.cl:527-633): 8 heads, scale 1/sqrt(c).
  * Nk > 64 (c = 16 only) splits the keys over CTAs and needs a device
- * workspace of k_mha_workspace(...) bytes (0 otherwise). */
+ * workspace of k_mha_workspace(...) bytes (0 otherwise) and the device
+ * error word err (a pipeline wait that times out records kErrWaitTimeout
+ * there instead of hanging). */
 size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms);
 int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
           const float *kp, long sk, const float *vp, long sv, float *o,
-          void *ws, size_t ws_bytes, int num_sms, k_stream s);
+          void *ws, size_t ws_bytes, int *err, int num_sms, k_stream s);
 /* The decoder's image -> token attention (dint 128, at most 8 keys) with its
  * queries qp read as bf16 (rows of 128, row stride sq elements; as the Q
  * projection writes them) and its output o written as bf16 [P * Nq, 128]
@@ -153,7 +155,7 @@ int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *
  * them; row strides in elements); otherwise k_mha (same workspace). */
 int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                      long sk, const void *vp, long sv, float *o, void *ws,
-                     size_t ws_bytes, int num_sms, k_stream s);
+                     size_t ws_bytes, int *err, int num_sms, k_stream s);
 
 /* Mask decoder (decoder.cu). convt_scatter: G [P*H*W, Co*4] (16-byte
  * aligned) -> out [P, 2H, 2W, Co], + bias, + add (shared, may be NULL),

@@ -460,7 +460,7 @@ static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, l
            4.0 * P * Nq * (double)Nk * dint,
            4.0 * ((double)P * Nq * dint * 2 + (sk ? (double)P : 1.0) * Nk * dint * 2),
            k_mha(P, Nq, Nk, dint, q, sq, k, sk, v, sv, o, d->mha_ws, d->mha_ws_bytes,
-                 b->num_sms, (k_stream)b->stream));
+                 b->d_err, b->num_sms, (k_stream)b->stream));
     return CB_OK;
 }
 
@@ -488,7 +488,8 @@ static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, 
     LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,
            4.0 * (double)P * DEC_NTOK * 128 * 2 + 2.0 * (sk ? (double)P : 1.0) * DEC_T * 128 * 2,
            k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so,
-                            d->mha_ws, d->mha_ws_bytes, b->num_sms, (k_stream)b->stream));
+                            d->mha_ws, d->mha_ws_bytes, b->d_err, b->num_sms,
+                            (k_stream)b->stream));
     return CB_OK;
 }
 

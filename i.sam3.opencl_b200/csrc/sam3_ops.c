@@ -338,7 +338,7 @@ int cb_mha(cb_backend *b, int P, int Nq, int Nk, int dint, cb_mem qp,
                           k_mha(P, Nq, Nk, dint, (const float *)qp->ptr, (long)sq,
                                 (const float *)kp->ptr, (long)sk,
                                 (const float *)vp->ptr, (long)sv, (float *)o->ptr, ws,
-                                wsb, b->num_sms, (k_stream)b->stream),
+                                wsb, b->d_err, b->num_sms, (k_stream)b->stream),
                           "mha");
     }
 }

@@ -71,6 +71,30 @@ inline bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t e
            CUDA_SUCCESS;
 }
 
+// 3-D map over n blocks of rows x cols elements (row pitch ld, block pitch
+// bld elements; bld 0: one block), box box_cols x box_rows x 1 with the
+// given swizzle (box_cols * esize must not exceed the swizzle span).
+// Out-of-range elements read as zero.
+inline bool make_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t esize,
+                         const void *base, uint64_t n, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint64_t bld, uint32_t box_cols, uint32_t box_rows,
+                         CUtensorMapSwizzle swz)
+{
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esize) & 15) ||
+        ((bld * esize) & 15) || box_rows > 256 || rows == 0 || cols == 0 || n == 0)
+        return false;
+    if (bld == 0)
+        n = 1;
+    cuuint64_t dims[3] = {cols, rows, n};
+    cuuint64_t strides[2] = {ld * esize, (bld ? bld : rows * ld) * esize};
+    cuuint32_t box[3] = {box_cols, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 4-D map over n images of h x w pixels of c channels (channels innermost,
 // packed), box box_c x box_w x box_h x 1 with 128-byte swizzle (box_c *
 // esize = 128 or less). Out-of-range elements read as zero; stores clip.
