@@ -604,8 +604,34 @@ __global__ void diag_exp2_kernel(const float *x, float *y_poly, float *y_mufu, i
         y_mufu[i + 1] = ex2_approx(x[i + 1]);
     }
 }
+// One thread waits on an mbarrier that nothing arrives on, with the given
+// limit: the bounded wait must give up, record kErrWaitTimeout in *err and
+// leave the context usable. status[0] = the wait's result (0: timed out),
+// status[1] = the abort flag it raised.
+__global__ void diag_wait_timeout_kernel(int *err, int *status, uint64_t limit_ns)
+{
+    __shared__ uint64_t bar;
+    __shared__ volatile int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+        const bool ok = mbar_wait(&bar, 0, err, &abort_flag, limit_ns);
+        status[0] = ok ? 1 : 0;
+        status[1] = abort_flag;
+    }
+}
 }  // namespace
 }  // namespace sam3
+
+extern "C" int cb_diag_wait_timeout(int *err, int *status, int limit_us, void *stream)
+{
+    if (!err || !status || limit_us <= 0 || limit_us > 1000000)
+        return 3;  // CB_EARG
+    sam3::diag_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        err, status, (uint64_t)limit_us * 1000);
+    return cudaGetLastError() == cudaSuccess ? 0 : 4;  // CB_OK / CB_ECUDA
+}
 
 extern "C" int cb_diag_exp2(const float *x, float *y_poly, float *y_mufu, int n, void *stream)
 {

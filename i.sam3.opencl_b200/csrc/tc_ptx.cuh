@@ -89,11 +89,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 }
 
 // Waits for the phase with the given parity to complete. Bounded: after
-// kWaitLimitNs it records kErrWaitTimeout in *err, raises the CTA's abort
-// flag and returns false. Also returns false at once when another thread of
-// the CTA has raised the abort flag, so every role unwinds.
+// limit_ns (default kWaitLimitNs) it records kErrWaitTimeout in *err,
+// raises the CTA's abort flag and returns false. Also returns false at
+// once when another thread of the CTA has raised the abort flag, so every
+// role unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
-                                          volatile int *abort_flag)
+                                          volatile int *abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs)
 {
     const uint32_t a = smem_addr(bar);
     if (mbar_try_wait(a, parity))
@@ -105,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
         if ((it & 63) == 0) {
             if (*abort_flag)
                 return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 atomicCAS(err, kErrNone, kErrWaitTimeout);
                 *abort_flag = 1;
                 return false;

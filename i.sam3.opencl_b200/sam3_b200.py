@@ -34,7 +34,7 @@ EXPORTS = [
     "cb_encoder_default_config",
     "cb_encoder_create", "cb_encoder_free", "cb_encoder_init_random",
     "cb_encoder_set_weight", "cb_encode_tiles", "cb_encode_blocks",
-    "cb_encode_tiles_host", "cb_synth_normal", "cb_diag_exp2",
+    "cb_encode_tiles_host", "cb_synth_normal", "cb_diag_exp2", "cb_diag_wait_timeout",
     "cb_convt_scatter", "cb_mask_logits", "cb_decoder_create", "cb_decoder_free",
     "cb_decoder_init_random", "cb_decoder_set_weight", "cb_decoder_set_image",
     "cb_decode", "cb_neck_create", "cb_neck_free", "cb_neck_init_random",
@@ -157,6 +157,7 @@ def lib():
         "cb_encode_tiles_host": (i32, [vp, vp, i32, vp]),
         "cb_synth_normal": (i32, [vp, C.c_uint64, C.c_uint64, f32, f32, vp, sz]),
         "cb_diag_exp2": (i32, [vp, vp, vp, i32, vp]),
+        "cb_diag_wait_timeout": (i32, [vp, vp, i32, vp]),
         "cb_convt_scatter": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32]),
         "cb_mask_logits": (i32, [vp, vp, vp, vp, i32, i32]),
         "cb_decoder_create": (i32, [vp, i32, C.POINTER(vp)]),

@@ -438,6 +438,14 @@ int cb_image_encoder_input(cb_backend *b, cb_mem img, int cols, int rows,
 int cb_diag_exp2(const float *x, float *y_poly, float *y_mufu, int n,
                  void *stream);
 
+/* Diagnostics: the kernels' bounded pipeline wait on an mbarrier that
+ * nothing arrives on, limited to limit_us (1 .. 1e6) microseconds. On the
+ * device: *err (int, device memory) receives the wait-timeout code 1 unless
+ * it already holds a code; status (2 device ints) = {wait returned
+ * success, abort flag raised}. Tests that a wait gives up with a status
+ * instead of hanging the GPU. */
+int cb_diag_wait_timeout(int *err, int *status, int limit_us, void *stream);
+
 /* Generator: fill a device buffer with normal(seed, stream, i) values
  * (include/sam3_synth.h) as F32 or BF16 (the buffer's dtype). */
 int cb_synth_normal(cb_backend *b, uint64_t seed, uint64_t stream, float mean,

@@ -432,6 +432,30 @@ def test_softmax_exp2_paths_vs_cuda_exp2(cb, sb):
     assert (yp[~normal].abs() <= 2.0 ** -124).all()
 
 
+def test_bounded_wait_gives_up_with_status(cb, sb):
+    """The kernels' pipeline waits are bounded: a wait on an mbarrier that
+    nothing arrives on returns after its limit with the timeout code in the
+    error word and the abort flag raised, and the context stays usable (a
+    kernel launched afterwards runs and is correct)."""
+    import ctypes as C
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.full((2,), -1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    rc = sb.lib().cb_diag_wait_timeout(C.c_void_p(err.data_ptr()), C.c_void_p(status.data_ptr()),
+                                       20000, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert err.item() == 1
+    assert status.tolist() == [0, 1]
+    x = -torch.rand(1 << 12, device="cuda") * 10.0
+    yp, ym = torch.empty_like(x), torch.empty_like(x)
+    torch.cuda.synchronize()
+    assert sb.lib().cb_diag_exp2(C.c_void_p(x.data_ptr()), C.c_void_p(yp.data_ptr()),
+                                 C.c_void_p(ym.data_ptr()), x.numel(), None) == 0
+    torch.cuda.synchronize()
+    assert torch.allclose(ym, torch.exp2(x), rtol=1e-5, atol=0)
+
+
 def test_mha_rejects_unsupported_shape(cb, sb):
     m = cb.alloc(8 * 100 * 256 * 4, sb.F32)
     with pytest.raises(sb.CBError) as e:
