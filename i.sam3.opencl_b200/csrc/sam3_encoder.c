@@ -632,7 +632,7 @@ int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
 {
     size_t side, tile_in, tile_out;
     cb_backend *b;
-    int chunk, t0, c;
+    int chunk, t0, c, n, tail, lim, nfull;
 
     if (!e || !tiles || !out || ntile <= 0)
         return cbi_fail(e ? e->b : NULL, CB_EARG, "encode_tiles_host");
@@ -643,9 +643,17 @@ int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
     CB_TRY(cbi_enter(b));
     chunk = host_chunk(e, ntile);
     CB_TRY(host_pipeline_setup(e, chunk));
-    for (t0 = 0, c = 0; t0 < ntile; t0 += chunk, c++) {
-        const int n = ntile - t0 < chunk ? ntile - t0 : chunk;
+    /* The last chunk's read-back is the copy nothing overlaps: when the
+     * batch spans more than two chunks plus a small one, it ends with a
+     * chunk of 4 tiles and the rest is cut into near-equal chunks of at
+     * most `chunk` (64 tiles: 15 + 15 + 15 + 15 + 4). */
+    tail = ntile >= 2 * chunk + 4 && chunk > 4 ? 4 : 0;
+    lim = ntile - tail;
+    nfull = (lim + chunk - 1) / chunk;
+    for (t0 = 0, c = 0; t0 < ntile; t0 += n, c++) {
         const int i = c & 1;
+
+        n = c < nfull ? lim / nfull + (c < lim % nfull) : tail;
 
         if (c >= 2)  /* chunk c - 2's encode has read tiles[i] */
             CB_TRY(cbi_kstatus(b, (int)cudaStreamWaitEvent(e->h2d, e->ev_done[i], 0),

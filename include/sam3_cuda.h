@@ -303,9 +303,11 @@ int cb_encode_blocks(cb_encoder *e, cb_mem x, int ntile, int first, int last);
 
 /* Host-to-host convenience: tiles from host memory, tokens back to host
  * memory out [ntile, grid^2, E]. Blocking. Runs as a pipeline over chunks
- * (about ntile / 4 tiles, at least 4, at most max_tiles): the copy of the
- * next chunk in and of the previous chunk out overlap the encode of the
- * current one (page-locked host buffers let the copies run asynchronously). */
+ * (about ntile / 4 tiles, at least 4, at most max_tiles; a batch of more
+ * than two chunks plus 4 tiles ends with a chunk of 4, whose read-back is
+ * the copy nothing overlaps): the copy of the next chunk in and of the
+ * previous chunk out overlap the encode of the current one (page-locked
+ * host buffers let the copies run asynchronously). */
 int cb_encode_tiles_host(cb_encoder *e, const uint8_t *tiles, int ntile,
                          float *out);
 

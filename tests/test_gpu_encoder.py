@@ -63,12 +63,12 @@ def test_encoder_batch_equals_single_tiles(cb, sb, ob):
     enc.close()
 
 
-@pytest.mark.parametrize("ntile", [3, 8, 11, 16])
+@pytest.mark.parametrize("ntile", [3, 8, 11, 16, 21])
 def test_encode_tiles_host_pipeline_equals_device_path(cb, sb, ob, ntile):
     """The host-buffer entry point (chunks of about a quarter of the tiles,
     at least 4, with copies in and out overlapping the encode: 3 tiles = one
-    chunk, 8 = 2 x 4 as one GPU of eight gets, 11 = 4 + 4 + 3, 16 = 4 x 4)
-    returns,
+    chunk, 8 = 2 x 4 as one GPU of eight gets, 11 = 4 + 4 + 3, 16 = 4 x 4,
+    21 = 6 + 6 + 5 + a final 4) returns,
     bit for bit, what the device-buffer path returns for the same tiles, and
     a second call reuses its staging buffers."""
     seed = 8
