@@ -992,12 +992,13 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
     if (BN == 128)
         return launch_bn<128>(ta, tb, tc, tma, c_bf16 != 0, p, num_sms, st);
     // CTA pairs (256 x 256 tiles) when there are enough tiles to give every
-    // pair of SMs at least one, with TMA stores, and the main loop carries
-    // the tile: bf16 output, or K above 1024 (an fp32-output GEMM with short
-    // K, like the attention projection, is bound by its epilogue's HBM
-    // traffic and measured 1 % slower in pairs).
+    // pair of SMs at least one, with TMA stores, and the main loop or the
+    // in-place reduce-add carries the tile: bf16 output, K above 1024, or an
+    // fp32 residual updated in place (the attention projection, K = 1024:
+    // 830 -> 935 TFLOP/s in pairs once its epilogue stopped reading the
+    // residual; other fp32-output GEMMs with short K stay on single CTAs).
     const long pair_tiles = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
-    if (tma && pair_tiles >= num_sms / 2 && (c_bf16 || K > 1024) &&
+    if (tma && pair_tiles >= num_sms / 2 && (c_bf16 || K > 1024 || p.red) &&
         make_tmap_bf16(&tb_half, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128)) {
         const bool rope64 = p.rope.mode && p.rope.hd == 64 && p.act == K_ACT_NONE;
         const int rc = c_bf16 ? (rope64 ? launch_pair<true, true>(ta, tb_half, tc, p, num_sms, st)
