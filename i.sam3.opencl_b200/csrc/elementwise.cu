@@ -179,29 +179,36 @@ __global__ void rope_apply_kernel(float *qkv, long rows, int E, int hd, int npos
     *x = make_float2(v.x * rot.x - v.y * rot.y, v.x * rot.y + v.y * rot.x);
 }
 
-// fp32 qkv -> bf16 qkv, RoPE on q and k, plain cast of v. One thread per
-// 4 columns (two pairs).
-__global__ void rope_cast_kernel(const float *__restrict__ qkv, long rows, int E, int hd,
-                                 int npos, const float2 *__restrict__ cs, __nv_bfloat16 *out)
+// fp32 qkv -> bf16 qkv, RoPE on q and k, plain cast of v. A CTA per
+// kRopeRows rows, a thread per 4 columns (two pairs) of a row, 32-bit index
+// math (the table row r % npos once per row).
+constexpr int kRopeRows = 2;
+__global__ void __launch_bounds__(256) rope_cast_kernel(const float *__restrict__ qkv, long rows,
+                                                        int E, int hd, int npos,
+                                                        const float2 *__restrict__ cs,
+                                                        __nv_bfloat16 *__restrict__ out)
 {
-    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const int per_row = 3 * E / 4;
-    if (gid >= rows * per_row)
-        return;
-    const long r = gid / per_row;
-    const int c = (int)(gid % per_row) * 4;
-    float4 v = *reinterpret_cast<const float4 *>(qkv + r * 3 * E + c);
-    if (c < 2 * E) {
-        const int j = (c % hd) / 2, nf = hd / 2;
-        const float2 *t = cs + (r % npos) * nf + j;
-        const float2 r0 = __ldg(t), r1 = __ldg(t + 1);
-        v = make_float4(v.x * r0.x - v.y * r0.y, v.x * r0.y + v.y * r0.x,
-                        v.z * r1.x - v.w * r1.y, v.z * r1.y + v.w * r1.x);
+    const int per_row = 3 * E / 4, nf = hd / 2;
+#pragma unroll
+    for (int rr = 0; rr < kRopeRows; rr++) {
+        const long r = (long)blockIdx.x * kRopeRows + rr;
+        if (r >= rows)
+            return;
+        const float4 *src = reinterpret_cast<const float4 *>(qkv + r * 3 * E);
+        uint2 *dst = reinterpret_cast<uint2 *>(out + r * 3 * E);
+        const float2 *trow = cs + (long)(int)(r % npos) * nf;
+        for (int k = threadIdx.x; k < per_row; k += blockDim.x) {
+            const int c = 4 * k;
+            float4 v = __ldg(src + k);
+            if (c < 2 * E) {
+                const int j = (c % hd) / 2;
+                const float2 r0 = __ldg(trow + j), r1 = __ldg(trow + j + 1);
+                v = make_float4(v.x * r0.x - v.y * r0.y, v.x * r0.y + v.y * r0.x,
+                                v.z * r1.x - v.w * r1.y, v.z * r1.y + v.w * r1.x);
+            }
+            dst[k] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        }
     }
-    uint2 p;
-    p.x = pack_bf16x2(v.x, v.y);
-    p.y = pack_bf16x2(v.z, v.w);
-    *reinterpret_cast<uint2 *>(out + r * 3 * E + c) = p;
 }
 
 // ---------------------------------------------------------------- misc
@@ -223,32 +230,58 @@ __global__ void add_bf16_kernel(const float *__restrict__ a, const float *__rest
         out[i] = __float2bfloat16_rn(a[i] + b[i]);
 }
 
-// window_partition (sam3_kernels.cl:712-724).
-__global__ void window_partition_kernel(const float *X, float *out, int H, int C, int ws, int nwx,
-                                        long total)
+// window_partition (sam3_kernels.cl:712-724): window-major row r = (window
+// w, in-window position i) <- token (y, x), zero past the image. A CTA per
+// row; V4: 16-byte copies (C % 4 == 0, 16-byte aligned buffers).
+template <bool V4>
+__global__ void __launch_bounds__(256) window_partition_kernel(const float *__restrict__ X,
+                                                               float *__restrict__ out, int H,
+                                                               int C, int ws, int nwx)
 {
-    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= total)
-        return;
-    const long r = gid / C;
-    const int c = (int)(gid % C);
-    const int w = (int)(r / (ws * ws)), i = (int)(r % (ws * ws));
+    const int r = blockIdx.x;
+    const int w = r / (ws * ws), i = r - w * (ws * ws);
     const int y = (w / nwx) * ws + i / ws, x = (w % nwx) * ws + i % ws;
-    out[gid] = (y < H && x < H) ? X[((long)y * H + x) * C + c] : 0.0f;
+    const bool in = y < H && x < H;
+    const float *src = X + ((long)y * H + x) * C;
+    float *dst = out + (long)r * C;
+    if (V4) {
+        for (int c = threadIdx.x; c < C / 4; c += blockDim.x)
+            reinterpret_cast<float4 *>(dst)[c] =
+                in ? __ldg(reinterpret_cast<const float4 *>(src) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    else {
+        for (int c = threadIdx.x; c < C; c += blockDim.x)
+            dst[c] = in ? src[c] : 0.0f;
+    }
 }
 
-// window_unpartition_add (sam3_kernels.cl:728-741).
-__global__ void window_unpartition_add_kernel(float *X, const float *Wd, int H, int C, int ws,
-                                              int nwx)
+// window_unpartition_add (sam3_kernels.cl:728-741): token (y, x) += its
+// window-major row. A CTA per token.
+template <bool V4>
+__global__ void __launch_bounds__(256) window_unpartition_add_kernel(float *__restrict__ X,
+                                                                     const float *__restrict__ Wd,
+                                                                     int H, int C, int ws, int nwx)
 {
-    const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long t = gid / C;
-    if (t >= (long)H * H)
-        return;
-    const int c = (int)(gid % C);
-    const int y = (int)(t / H), x = (int)(t % H);
+    const int t = blockIdx.x;
+    const int y = t / H, x = t - y * H;
     const int w = (y / ws) * nwx + x / ws, i = (y % ws) * ws + x % ws;
-    X[gid] += Wd[((long)w * ws * ws + i) * C + c];
+    float *dst = X + (long)t * C;
+    const float *src = Wd + ((long)w * ws * ws + i) * C;
+    if (V4) {
+        for (int c = threadIdx.x; c < C / 4; c += blockDim.x) {
+            float4 a = reinterpret_cast<float4 *>(dst)[c];
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(src) + c);
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+            reinterpret_cast<float4 *>(dst)[c] = a;
+        }
+    }
+    else {
+        for (int c = threadIdx.x; c < C; c += blockDim.x)
+            dst[c] += src[c];
+    }
 }
 
 // patch_im2col (sam3_kernels.cl:661-672).
@@ -459,8 +492,7 @@ extern "C" int k_rope_cast_bf16(const float *qkv, long rows, int E, int hd, int 
 {
     if (hd % 4 || E % hd || npos <= 0 || ((uintptr_t)qkv & 15) || ((uintptr_t)out & 7))
         return K_EARG;
-    const long n = rows * (3L * E / 4);
-    rope_cast_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
+    rope_cast_kernel<<<grid_for(rows, kRopeRows), 256, 0, STREAM(s)>>>(
         qkv, rows, E, hd, npos, reinterpret_cast<const float2 *>(cs),
         reinterpret_cast<__nv_bfloat16 *>(out));
     LAUNCH_RET();
@@ -489,17 +521,34 @@ extern "C" int k_add_bf16(const float *a, const float *b, void *out, long n, k_s
 extern "C" int k_window_partition(const float *X, float *out, int H, int C, int ws, int nwx,
                                   k_stream s)
 {
-    const long total = (long)nwx * nwx * ws * ws * C;
-    window_partition_kernel<<<grid_for(total, 256), 256, 0, STREAM(s)>>>(X, out, H, C, ws, nwx,
-                                                                          total);
+    const long rows = (long)nwx * nwx * ws * ws;
+    if (rows <= 0 || C <= 0)
+        return rows == 0 ? 0 : K_EARG;
+    if (rows > 0x7fffffffL)
+        return K_EARG;
+    const bool v4 = !(C & 3) && !((uintptr_t)X & 15) && !((uintptr_t)out & 15);
+    if (v4)
+        window_partition_kernel<true><<<(unsigned)rows, 256, 0, STREAM(s)>>>(X, out, H, C, ws, nwx);
+    else
+        window_partition_kernel<false><<<(unsigned)rows, 256, 0, STREAM(s)>>>(X, out, H, C, ws, nwx);
     LAUNCH_RET();
 }
 
 extern "C" int k_window_unpartition_add(float *X, const float *Wd, int H, int C, int ws, int nwx,
                                         k_stream s)
 {
-    const long n = (long)H * H * C;
-    window_unpartition_add_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(X, Wd, H, C, ws, nwx);
+    const long rows = (long)H * H;
+    if (rows <= 0 || C <= 0)
+        return rows == 0 ? 0 : K_EARG;
+    if (rows > 0x7fffffffL)
+        return K_EARG;
+    const bool v4 = !(C & 3) && !((uintptr_t)X & 15) && !((uintptr_t)Wd & 15);
+    if (v4)
+        window_unpartition_add_kernel<true><<<(unsigned)rows, 256, 0, STREAM(s)>>>(X, Wd, H, C, ws,
+                                                                                   nwx);
+    else
+        window_unpartition_add_kernel<false><<<(unsigned)rows, 256, 0, STREAM(s)>>>(X, Wd, H, C, ws,
+                                                                                    nwx);
     LAUNCH_RET();
 }
 
