@@ -486,6 +486,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_n = (p.N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int kblocks = (p.K + BK - 1) / BK;
+    // Tile sequence of this CTA (or pair): every step-th tile; with RoPE a
+    // contiguous range of the m-major order instead (same count +-1), so
+    // that consecutive tiles share their rows and the epilogue keeps the
+    // rows' (cos, sin) pairs in registers across them.
+    int t_begin = first, t_end = num_tiles, t_step = step;
+    if (ROPE_PF && p.rope.mode) {
+        t_begin = (int)((long)first * num_tiles / step);
+        t_end = (int)((long)(first + 1) * num_tiles / step);
+        t_step = 1;
+    }
 
     if (warp == 0) {
         if (elect_one()) {
@@ -495,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, last_parity = 0;
             bool ok = true;
-            for (int t = first; t < num_tiles && ok; t += step) {
+            for (int t = t_begin; t < t_end && ok; t += t_step) {
                 const int m0 = (t / num_n) * TM + (int)rank * BM, n0 = (t % num_n) * BN;
                 int img = 0, py0 = 0, px0 = 0;
                 if constexpr (CONV3) {
@@ -568,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int acc = 0;
                 uint32_t acc_phase = 0;
                 bool ok = true;
-                for (int t = first; t < num_tiles && ok; t += step) {
+                for (int t = t_begin; t < t_end && ok; t += t_step) {
                     if (!(PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.err, abort_flag)
                                : mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, abort_flag)))
                         break;
@@ -637,7 +647,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         if (TMA_STORE && lane == 0)
             prefetch_tmap(&tmC);
-        for (int t = first; t < num_tiles; t += step) {
+        float2 rc[ROPE_PF ? 32 : 1];  // this row's RoPE (cos, sin) pairs
+        int rc_row = -1;               // the table row they are of
+        for (int t = t_begin; t < t_end; t += t_step) {
             const int m0 = (t / num_n) * TM + (int)rank * BM, n0 = (t % num_n) * BN;
             int r0 = m0 + quarter * 32;
             int m = r0 + lane;
@@ -657,12 +669,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rrow = p.rope.mode ? rope_row(p.rope, m < p.M ? m : 0) : 0;
             // Global reads issued before the accumulator wait, so that their
             // latency hides behind the tile's main loop: with bf16 output the
-            // row's 32 RoPE (cos, sin) pairs (every 64-column chunk is one
-            // head and uses all of them); with fp32 output the residual of
-            // this warp's first chunk (later chunks are fetched one ahead).
-            float2 rc[ROPE_PF ? 32 : 1];
+            // row's 32 RoPE (cos, sin) pairs when the row changed (every
+            // 64-column chunk is one head and uses all of them); with fp32
+            // output the residual of this warp's first chunk (later chunks
+            // are fetched one ahead).
             const bool rope_tile = ROPE_PF && p.rope.mode && p.rope.hd == 64 && n0 < 2 * p.rope.E;
-            if (ROPE_PF && rope_tile) {
+            if (ROPE_PF && rope_tile && rrow != rc_row) {
+                rc_row = rrow;
                 const float4 *cs = reinterpret_cast<const float4 *>(p.rope.cs) + (long)rrow * 16;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
