@@ -7,23 +7,26 @@
 //
 //   few keys (Nk <= 64: image-to-token, token self-attention;
 //   attn_fewkeys, sam3_kernels.cl:527-569): persistent CTAs, each taking a
-//   contiguous range of 32-query units (so a prompt's K and V, a few KB, are
-//   staged in shared memory once per CTA and prompt), one thread per
-//   (query, head), the next unit's query loaded while the current one
-//   computes; the 8 heads of a query sit in 8 adjacent threads (whole
-//   512-byte rows per 8 threads); softmax over the keys from shared memory
-//   (two passes for up to 8 keys, online beyond);
+//   contiguous range of query units (so a prompt's K and V, a few KB, are
+//   loaded once per CTA and prompt). Up to 8 keys with c = 16 (the
+//   decoder's image-to-token attention): warp = head, 16-query units on
+//   mma.sync tensor tiles (bf16 hi / lo operand pairs), the softmax over a
+//   query's 8 keys across the 4 lanes of a quad. Otherwise one thread per
+//   (query, head) on the CUDA cores, the 8 heads of a query in 8 adjacent
+//   threads (whole 512-byte rows per 8 threads), K and V staged in shared
+//   memory, softmax in two passes for up to 8 keys, online beyond;
 //
 //   many keys (Nk > 64, c = 16: token-to-image; attn_manykeys,
 //   sam3_kernels.cl:577-633): the prompts' 32-key chunks form one sequence
 //   cut into equal ranges, one per CTA slot (two per SM), so that every SM
-//   streams K/V (a prompt's K/V is 2.6 MB in fp32); a CTA (one range, for 8
-//   queries) pulls the chunks of K and V with cp.async through a 3-stage
-//   ring, each warp (one head) takes Q.K^T and P.V of every chunk on the
-//   tensor cores (mma.sync, bf16 operand pairs hi + lo for fp32 accuracy)
-//   with an online softmax on the accumulators; at the end of each prompt
-//   in its range it writes one (m, l, o) partial per (query, head); a
-//   second kernel combines the partials of each prompt.
+//   streams K/V (a prompt's K/V is 2.6 MB in fp32); in a CTA (one range,
+//   for 8 queries) a producer warp loads the chunks of K and V by TMA into
+//   a 3-stage ring (full / empty mbarriers), each head warp takes Q.K^T and
+//   P.V of every chunk on the tensor cores (mma.sync, bf16 operand pairs
+//   hi + lo for fp32 accuracy) with an online softmax on the accumulators;
+//   at the end of each prompt in its range it writes one (m, l, o) partial
+//   per (query, head); a second kernel combines the partials of each
+//   prompt.
 //
 // Shared-memory layouts keep a warp's reads on distinct bank groups: rows
 // padded to c + 4 floats per head (few keys: the 8 heads a warp reads), or
