@@ -386,6 +386,9 @@ def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
     ("t2i_shared", 64, 7, 5184, 128, True),
     ("i2t", 16, 5184, 8, 128, False),
     ("i2t_7_ragged", 5, 1001, 7, 128, False),  # 7 keys, query units ending inside prompts
+    ("i2t_3keys", 3, 200, 3, 128, False),      # few keys: masked key columns of the tile
+    ("t2i_65", 4, 8, 65, 128, False),          # last 32-key chunk holds one key (TMA zero fill)
+    ("t2i_65_shared", 4, 9, 65, 128, True),    # keys shared, two query groups
     ("self7", 64, 7, 7, 256, False),
     ("t2i_odd", 3, 11, 1000, 128, False),   # 2 query groups, ragged key splits
     ("t2i_5", 5, 8, 5184, 128, False),      # CTA chunk ranges end inside prompts
