@@ -470,9 +470,12 @@ __host__ __device__ __forceinline__ long many_chunk0(long g, long T, long G)
     return g * T / G;
 }
 
-// Token -> image attention on the tensor cores: warp w of the CTA is head
-// w, for 8 queries of a prompt, over each staged chunk of 32 keys as two
-// blocks of 16. Per block, S^T (16 keys x 8 queries) = K . Q^T and O^T (16
+// Token -> image attention on the tensor cores: warp w < 8 of the CTA is
+// head w, for 8 queries of a prompt, over each staged chunk of 32 keys as
+// two blocks of 16; warp 8 stages the chunks (TMA boxes of 32 keys x one
+// head's 16 channels, K and V of every head, into a 3-stage ring guarded
+// by full / empty mbarriers with bounded waits). KV_BF16: K and V given in
+// bf16 (as the decoder's projections write them). Per block, S^T (16 keys x 8 queries) = K . Q^T and O^T (16
 // channels x 8 queries) += V^T . P^T by mma.sync m16n8k16 in bf16 with
 // fp32 accumulation, every fp32 operand split into a bf16 pair hi + lo
 // and each product taken as hi.hi + lo.hi + hi.lo (K/V given in bf16 are
