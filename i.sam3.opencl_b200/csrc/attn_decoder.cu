@@ -851,7 +851,7 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
 {
     const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
     if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15) ||
-        !err || (long)P > 0x7fffffffL)
+        !err)
         return K_EARG;
     // K and V as [P][Nk][128] boxes of 32 keys x one head's 16 channels
     // (prompt pitch sk / sv elements; 0: one block shared by all prompts)
