@@ -768,7 +768,8 @@ def profile_part(part):
     of 16 prompts, `neck` = cb_neck_run on 2 tiles, `detector` = the two
     cb_attend shapes of the bench, `input` = one 2100 x 1500 crop,
     `elementwise` = the backbone's element-wise kernels (patch_embed_in,
-    LayerNorm, the RoPE + bf16 cast of the fp32 attention op)."""
+    LayerNorm, the RoPE + bf16 cast of the fp32 attention op),
+    `decoder_attention` = config 3's two cb_mha forms at 64 prompts."""
     import torch
     sb = load_product()
     cb = sb.Backend(0)
@@ -800,6 +801,21 @@ def profile_part(part):
     elif part == "detector":
         for _ in range(2):
             detector_attention_bench(sb, cb, torch, None, iters=1)
+    elif part == "decoder_attention":
+        # config 3's cb_mha forms at 64 prompts, two calls each: token ->
+        # image over per-prompt K/V (split + merge), then image -> token
+        P, N, D = DEC_P, DEC_NK, DEC_D
+        g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+        for nq, nk, qrows, kvrows in ((8, N, P * 8, P * N), (N, 8, P * N, P * 8)):
+            q = torch.randn(qrows, D, device="cuda", generator=g)
+            k = torch.randn(kvrows, D, device="cuda", generator=g)
+            v = torch.randn(kvrows, D, device="cuda", generator=g)
+            o = torch.empty(qrows, D, device="cuda")
+            torch.cuda.synchronize()
+            mq, mk, mv, mo = cb.wrap(q), cb.wrap(k), cb.wrap(v), cb.wrap(o)
+            for _ in range(2):
+                cb.mha(P, nq, nk, D, mq, nq * D, mk, nk * D, mv, nk * D, mo)
+            cb.sync()
     elif part == "input":
         for _ in range(2):
             input_bench(sb, cb, torch, iters=1)
@@ -840,7 +856,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="TILES",
                     help="run the small ncu case on TILES tiles and exit")
-    ap.add_argument("--profile-part", choices=["decoder", "neck", "detector", "input", "elementwise"],
+    ap.add_argument("--profile-part", choices=["decoder", "neck", "detector", "input", "elementwise",
+                                               "decoder_attention"],
                     help="run a small case of one part (beyond the backbone, or its "
                          "element-wise kernels) and exit")
     args = ap.parse_args()
