@@ -173,12 +173,15 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi)
 
 // LayerNorm of the decoder's image stream (256 channels, norm4 of the
 // image -> token attention, sam3_model.c:1309/1348) with the outputs its
-// consumers need written in the same pass: Y (fp32, may alias X; NULL =
-// not written), Yb = bf16(Y) (operand of the value projection and of the
+// consumers need written in the same pass. R (optional) is the residual
+// shared by every prompt, row % T, added to X before the statistics (layer
+// 0's input: the image embedding), so the output projection before this
+// kernel stores plainly. Y (fp32, may alias X; NULL = not written), Yb = bf16(Y) (operand of the value projection and of the
 // first upscaling GEMM) and Yk = bf16(Y + pe[row % T]) (keys + dense
 // positional encoding, operand of the key / query projections). One warp
 // per row, 8 values per lane; two-pass mean / variance as the reference.
-__global__ void __launch_bounds__(256) ln_keys_kernel(const float *X, float *Y,
+__global__ void __launch_bounds__(256) ln_keys_kernel(const float *X,
+                                                      const float *__restrict__ R, float *Y,
                                                       const float *__restrict__ g,
                                                       const float *__restrict__ b, long rows,
                                                       float eps, const float *__restrict__ pe,
@@ -191,6 +194,17 @@ __global__ void __launch_bounds__(256) ln_keys_kernel(const float *X, float *Y,
         return;
     const float4 *x = reinterpret_cast<const float4 *>(X + row * 256);
     float4 v[2] = {x[lane], x[32 + lane]};
+    if (R) {  // the residual shared by all prompts, added as the GEMM epilogue would
+        const float4 *rr = reinterpret_cast<const float4 *>(R + (row % T) * 256);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float4 a = __ldg(rr + i * 32 + lane);
+            v[i].x += a.x;
+            v[i].y += a.y;
+            v[i].z += a.z;
+            v[i].w += a.w;
+        }
+    }
     const float mean =
         warp_sum((v[0].x + v[0].y) + (v[0].z + v[0].w) + (v[1].x + v[1].y) + (v[1].z + v[1].w)) /
         256.0f;
@@ -294,15 +308,17 @@ extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, int d
     return (int)cudaGetLastError();
 }
 
-extern "C" int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b, long rows,
-                             float eps, const float *pe, int T, void *Yb, void *Yk, k_stream s)
+extern "C" int k_dec_ln_keys(const float *X, const float *R, float *Y, const float *g,
+                             const float *b, long rows, float eps, const float *pe, int T, void *Yb,
+                             void *Yk, k_stream s)
 {
     if (rows <= 0 || T <= 0 || !Yb || !Yk || (reinterpret_cast<uintptr_t>(X) & 15) ||
+        (reinterpret_cast<uintptr_t>(R) & 15) ||
         (reinterpret_cast<uintptr_t>(Y) & 15) || (reinterpret_cast<uintptr_t>(pe) & 15) ||
         (reinterpret_cast<uintptr_t>(Yb) & 7) || (reinterpret_cast<uintptr_t>(Yk) & 7))
         return K_EARG;
     ln_keys_kernel<<<grid_for(rows, 8), 256, 0, STREAM(s)>>>(
-        X, Y, g, b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb), reinterpret_cast<uint2 *>(Yk));
+        X, R, Y, g, b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb), reinterpret_cast<uint2 *>(Yk));
     return (int)cudaGetLastError();
 }
 

@@ -175,17 +175,18 @@ int k_dec_heads(const float *tok, int P, const struct k_dec_heads_w *hw,
                 float *hyper, float *iou, k_stream s);
 int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor,
                           void *dst, k_stream s);
-/* Decoder fusions. ln_keys: LayerNorm of 256-wide rows, Y fp32 (may alias
- * X, NULL = skipped), Yb = bf16(Y), Yk = bf16(Y + pe[row % T]). up1:
+/* Decoder fusions. ln_keys: LayerNorm of 256-wide rows X (+ R[row % T]
+ * first when R is given), Y fp32 (may alias X, NULL = skipped), Yb =
+ * bf16(Y), Yk = bf16(Y + pe[row % T]). up1:
  * ConvT 256 -> 64 scatter of G [P*H*W, 256] + bias + feat [4HW, 64],
  * LayerNorm2d (g, b, eps), GELU -> bf16 [P, 2H, 2W, 64]. up2_logits: ConvT
  * 64 -> 32 scatter of G [P*H*W, 128] (sub-pixel-major columns d*32 + co)
  * + bias + feat [4HW, 32], GELU, dotted with hyper [P, 96] -> out
  * [P, 3, 2H * 2W]. transpose_cast with dmajor: source column co*4 + d
  * becomes row d * cols/4 + co. */
-int k_dec_ln_keys(const float *X, float *Y, const float *g, const float *b,
-                  long rows, float eps, const float *pe, int T, void *Yb,
-                  void *Yk, k_stream s);
+int k_dec_ln_keys(const float *X, const float *R, float *Y, const float *g,
+                  const float *b, long rows, float eps, const float *pe, int T,
+                  void *Yb, void *Yk, k_stream s);
 /* Last output-upscaling stage + mask logits on the tensor cores (gemm_tc.cu):
  * X bf16 [P*H*W, 64] (the first stage's output), Wt bf16 [128, 64] (the
  * ConvTranspose 64 -> 32 weight in sub-pixel-major rows d*32 + co), bias

@@ -657,12 +657,13 @@ static int i2t_attention(cb_decoder *d, int P, int l)
                               b->num_sms, (k_stream)b->stream));
     }
     CB_TRY(lin16(d, "dec_gemm_img", d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB),
-                 d->keys, l ? d->keys : d->src, l ? 0 : DEC_T, K_ACT_NONE));
+                 d->keys, l ? d->keys : NULL, 0, K_ACT_NONE));
     {
         cb_backend *b = d->b;
 
         LAUNCH("dec_ln_keys", 8.0 * rows * DEC_DIM, (double)rows * DEC_DIM * (l ? 8 : 12),
-               k_dec_ln_keys(d->keys, l ? NULL : d->keys, (const float *)d->w[LAY(l, N4W)],
+               k_dec_ln_keys(d->keys, l ? NULL : d->src, l ? NULL : d->keys,
+                             (const float *)d->w[LAY(l, N4W)],
                              (const float *)d->w[LAY(l, N4B)], rows, DEC_EPS, d->pe_img, DEC_T,
                              d->keys_bf16, d->kin_bf16, (k_stream)b->stream));
     }
