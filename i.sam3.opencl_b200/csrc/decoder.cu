@@ -257,6 +257,36 @@ __global__ void transpose_cast_kernel(const float *__restrict__ src, int rows, i
     }
 }
 
+// The upscaling epilogues' per-pixel residual in the layout they read:
+// feat [(2H) * (2W), C] (NHWC of one image) -> out [4][C][H * W] with
+// out[(d * C + c) * H * W + y * W + x] = feat[(2y + d / 2, 2x + d % 2)][c],
+// i.e. for ConvTranspose input pixel (y, x), sub-pixel d, channel c. An
+// epilogue thread owns one input pixel (GEMM row), so the 32 threads of a
+// warp read one channel of 32 consecutive pixels as one 128-byte line
+// instead of 32 lines. Through 32 x 32 shared-memory tiles, both sides
+// coalesced.
+__global__ void feat_subpix_kernel(const float *__restrict__ feat, int H, int W, int C,
+                                   float *__restrict__ out)
+{
+    __shared__ float tile[32][33];
+    const int HW = H * W, d = blockIdx.z;
+    const int i0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const int i = i0 + j;
+        if (i < HW) {
+            const int y = i / W, x = i - y * W;
+            const long pix = (long)(2 * y + (d >> 1)) * (2 * W) + 2 * x + (d & 1);
+            tile[j][threadIdx.x] = feat[pix * C + c0 + threadIdx.x];
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const int i = i0 + threadIdx.x;
+        if (i < HW)
+            out[(long)(d * C + c0 + j) * HW + i] = tile[threadIdx.x][j];
+    }
+}
+
 }  // namespace
 }  // namespace sam3
 
@@ -305,6 +335,15 @@ extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, int d
         return K_EARG;
     transpose_cast_kernel<<<dim3((cols + 31) / 32, (rows + 31) / 32), dim3(32, 8), 0, STREAM(s)>>>(
         src, rows, cols, dmajor, reinterpret_cast<__nv_bfloat16 *>(dst));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int k_dec_feat_subpix(const float *feat, int H, int W, int C, float *out, k_stream s)
+{
+    if (!feat || !out || H <= 0 || W <= 0 || C <= 0 || C % 32 || (long)H * W > 0x7fffffffL / C)
+        return K_EARG;
+    feat_subpix_kernel<<<dim3((H * W + 31) / 32, C / 32, 4), dim3(32, 8), 0, STREAM(s)>>>(
+        feat, H, W, C, out);
     return (int)cudaGetLastError();
 }
 

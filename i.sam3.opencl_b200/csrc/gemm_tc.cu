@@ -36,8 +36,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarps = 8;  // epilogue warps: two per TMEM lane quarter
 constexpr int kStageTile = 32 * 128;  // one warp's 32 rows x 128 bytes
 
 struct GemmEpi {
@@ -62,6 +61,12 @@ struct GemmEpi {
 // stride-2 ConvTranspose.
 constexpr int kEpiGeneric = 0, kEpiLogits = 1, kEpiLn2d = 2, kEpiConvT = 3;
 
+// Epilogue warps per CTA: four per TMEM lane quarter (one 32-column chunk
+// each) for the mask logits, whose GELU chains are latency-bound with two;
+// threads = a producer warp, an MMA warp and the epilogue warps.
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == kEpiLogits ? 16 : kEpiWarps; }
+__host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
+
 // kEpiLogits / kEpiLn2d / kEpiConvT: cH x cW input maps; hyper = the
 // prompts' hypernetwork vectors [P][3][32]; lnw / lnb = LayerNorm2d weight
 // and bias; cout = ConvTranspose output channels.
@@ -75,8 +80,9 @@ struct ConvGeom {
 // memory goes to a fourth A/B stage instead, which the main loop gains more
 // from than the epilogue loses by waiting for its previous TMA store to be
 // read. PAIR: each CTA of a pair holds half of the B tile (BN / 2 rows), so
-// a stage is 32 KB.
-template <int BN, bool PAIR = false>
+// a stage is 32 KB. EW: epilogue warps with a staging tile (0 for the
+// epilogues that store directly).
+template <int BN, bool PAIR = false, int EW = kEpiWarps>
 struct GemmSmem {
     static constexpr int STAGES = PAIR ? 6 : 4;
     static constexpr int EPI_BUFS = PAIR ? 1 : 1;
@@ -84,7 +90,7 @@ struct GemmSmem {
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-    static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * EPI_BUFS * kStageTile;
+    static constexpr int BAR_OFF = EPI_OFF + EW * EPI_BUFS * kStageTile;
     // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort
     static constexpr int BYTES = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
     static_assert(BYTES <= 232448, "GEMM shared memory");
@@ -257,7 +263,7 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 // ConvTranspose 2x2 (64 -> 32) outputs in sub-pixel-major order, so chunk c
 // (32 columns) is sub-pixel d = c = 2 dy + dx of output pixel (2y + dy,
 // 2x + dx). Per chunk: u = GELU(acc + bias + feat_s0[pixel]) over the 32
-// channels, dotted with the prompt's three hypernetwork vectors, written as
+// channels (feat_s0 as k_dec_feat_subpix lays it out), dotted with the prompt's three hypernetwork vectors, written as
 // the three logits of that pixel: the [P, 2H, 2W, 32] map is never stored.
 // Output pixel of sub-pixel d of input row m.
 __device__ __forceinline__ long logits_pixel(const ConvGeom &cg, int m, int d)
@@ -266,11 +272,29 @@ __device__ __forceinline__ long logits_pixel(const ConvGeom &cg, int m, int d)
     return (2L * y + (d >> 1)) * (2L * cg.cW) + 2 * x + (d & 1);
 }
 
+// feat of sub-pixel d for row m (k_dec_feat_subpix layout [4][C][H*W]):
+// channel c of the warp's 32 consecutive pixels is one 128-byte line. Read
+// before the accumulator is waited for, so the L2 latency hides behind the
+// tile's main loop.
+template <int C>
+__device__ __forceinline__ void feat_load(const GemmEpi &p, const ConvGeom &cg, int m, int d,
+                                          float (&f)[C])
+{
+    if (m >= p.M)
+        return;
+    const int hw = cg.cW * cg.cH;
+    const float *src = p.R + (long)d * C * hw + (m % hw);
+#pragma unroll
+    for (int c = 0; c < C; c++)
+        f[c] = __ldg(src + c * hw);
+}
+
 // kEpiLn2d: the first output-upscaling stage of the mask decoder
 // (sam3_model.c:1355-1360) as the epilogue of its ConvTranspose 2x2
 // (256 -> 64) GEMM: row m is input pixel (prompt, y, x), its 256 columns in
 // sub-pixel-major order, so a 64-column chunk is sub-pixel d of output pixel
-// (2y + dy, 2x + dx). Per chunk: v = acc + bias + feat_s1[pixel], LayerNorm
+// (2y + dy, 2x + dx). Per chunk: v = acc + bias + feat_s1[pixel] (as
+// k_dec_feat_subpix lays it out), LayerNorm
 // over the 64 channels (eps = p.alpha), GELU, written as the pixel's 64 bf16
 // channels of the [P, 2H, 2W, 64] map.
 __device__ __forceinline__ void ln2d_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
@@ -278,19 +302,18 @@ __device__ __forceinline__ void ln2d_chunk(const GemmEpi &p, const ConvGeom &cg,
 {
     if (m >= p.M)
         return;
-    const int pr = m / (cg.cW * cg.cH);
-    const long fpix = logits_pixel(cg, m, d);
-    const long opix = fpix + (long)pr * 4 * cg.cH * cg.cW;
-    const float4 *f = reinterpret_cast<const float4 *>(p.R + fpix * 64);
+    const int hw = cg.cW * cg.cH, pr = m / hw;
+    const long opix = logits_pixel(cg, m, d) + (long)pr * 4 * hw;
+    const float *f = p.R + (long)d * 64 * hw + (m - pr * hw);
     const float4 *bq = reinterpret_cast<const float4 *>(p.bias);
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < 16; j++) {
-        const float4 fv = __ldg(f + j), bv = __ldg(bq + j);
-        v[4 * j] = (v[4 * j] + bv.x) + fv.x;
-        v[4 * j + 1] = (v[4 * j + 1] + bv.y) + fv.y;
-        v[4 * j + 2] = (v[4 * j + 2] + bv.z) + fv.z;
-        v[4 * j + 3] = (v[4 * j + 3] + bv.w) + fv.w;
+        const float4 bv = __ldg(bq + j);
+        v[4 * j] = (v[4 * j] + bv.x) + __ldg(f + (4 * j) * hw);
+        v[4 * j + 1] = (v[4 * j + 1] + bv.y) + __ldg(f + (4 * j + 1) * hw);
+        v[4 * j + 2] = (v[4 * j + 2] + bv.z) + __ldg(f + (4 * j + 2) * hw);
+        v[4 * j + 3] = (v[4 * j + 3] + bv.w) + __ldg(f + (4 * j + 3) * hw);
         sum += (v[4 * j] + v[4 * j + 1]) + (v[4 * j + 2] + v[4 * j + 3]);
     }
     const float mean = sum * (1.0f / 64.0f);
@@ -362,21 +385,20 @@ __device__ __forceinline__ void convt_chunk(const GemmEpi &p, const ConvGeom &cg
 }
 
 __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &cg, int m, int d,
-                                             const float (&v)[32])
+                                             const float (&v)[32], const float (&f)[32])
 {
     if (m >= p.M)
         return;
     const int pr = m / (cg.cW * cg.cH);
     const long opix = logits_pixel(cg, m, d);
-    const float4 *f = reinterpret_cast<const float4 *>(p.R + opix * 32);
     const float4 *bq = reinterpret_cast<const float4 *>(p.bias);
     const float4 *h = reinterpret_cast<const float4 *>(cg.hyper + (long)pr * 96);
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        const float4 fv = __ldg(f + j), bv = __ldg(bq + j);
-        float u0 = (v[4 * j] + bv.x) + fv.x, u1 = (v[4 * j + 1] + bv.y) + fv.y;
-        float u2 = (v[4 * j + 2] + bv.z) + fv.z, u3 = (v[4 * j + 3] + bv.w) + fv.w;
+        const float4 bv = __ldg(bq + j);
+        float u0 = (v[4 * j] + bv.x) + f[4 * j], u1 = (v[4 * j + 1] + bv.y) + f[4 * j + 1];
+        float u2 = (v[4 * j + 2] + bv.z) + f[4 * j + 2], u3 = (v[4 * j + 3] + bv.w) + f[4 * j + 3];
         gelu_pair(u0, u1);
         gelu_pair(u2, u3);
         const float4 h0 = __ldg(h + j), h1 = __ldg(h + 8 + j), h2 = __ldg(h + 16 + j);
@@ -412,7 +434,7 @@ __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &c
 // tile traffic from L2 into shared memory.
 template <int BN, bool OUT_BF16, bool TMA_STORE, bool ROPE_PF, bool CONV3 = false,
           bool PAIR = false, int EPI = kEpiGeneric>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmEpi p,
@@ -430,7 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(EPI != kEpiConvT || (BN == 256 && OUT_BF16 && !TMA_STORE && !ROPE_PF && !PAIR &&
                                        !CONV3),
                   "the ConvTranspose epilogue: bf16 out, direct stores");
-    using L = GemmSmem<BN, PAIR>;
+    constexpr int EW = epi_warps(EPI);
+    constexpr int CSTEP = EW / 4;  // chunk stride of an epilogue warp
+    using L = GemmSmem<BN, PAIR, TMA_STORE ? EW : 0>;  // staging tiles for TMA stores only
     constexpr int STAGES = L::STAGES;
     constexpr int CW = OUT_BF16 ? 64 : 32;  // columns per 128-byte chunk
     constexpr int NCHUNK = BN / CW;
@@ -456,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);
+            mbar_init(&tempty[i], PAIR ? 2 * EW : EW);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -637,9 +661,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     else {
-        const int ew = warp - 2;          // 0..7
+        const int ew = warp - 2;          // 0 .. EW - 1
         const int quarter = warp & 3;     // TMEM lane quarter this warp may read
-        const int half = ew >> 2;         // which chunks of the tile (c % 2)
+        const int half = ew >> 2;         // which chunks of the tile (c % CSTEP)
         constexpr int kEpiBufs = L::EPI_BUFS;
         const uint32_t stage0 = smem_addr(smem + L::EPI_OFF + ew * kEpiBufs * kStageTile);
         int buf = 0;
@@ -695,6 +719,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < CW / 4; j++)
                     rnext[j] = *reinterpret_cast<const float4 *>(rrowp + half * CW + 4 * j);
             }
+            // mask logits: the feat values of the warp's chunks, read ahead
+            // as well
+            constexpr int LCH = LOGITS ? NCHUNK / CSTEP : 1;
+            float fpre[LCH][LOGITS ? 32 : 1];
+            if constexpr (LOGITS) {
+#pragma unroll
+                for (int cc = 0; cc < LCH; cc++)
+                    feat_load<32>(p, cg, m, half + CSTEP * cc, fpre[cc]);
+            }
             const bool ok = PAIR ? mbar_wait_cluster(&tfull[acc], acc_phase, p.err, abort_flag)
                                  : mbar_wait(&tfull[acc], acc_phase, p.err, abort_flag);
             if (!__all_sync(0xffffffffu, ok))
@@ -703,12 +736,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
             if constexpr (LOGITS) {
-                // both chunks' accumulators first, then the tile is released
-                float va[2][32];
+                // the warp's chunks' accumulators first, then the tile is
+                // released
+                float va[LCH][32];
 #pragma unroll
-                for (int cc = 0; cc < 2; cc++) {
+                for (int cc = 0; cc < LCH; cc++) {
                     uint32_t r[32];
-                    tmem_ld32(tbase + (half + 2 * cc) * CW, r);
+                    tmem_ld32(tbase + (half + CSTEP * cc) * CW, r);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; j++)
@@ -719,15 +753,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0)
                     mbar_arrive(&tempty[acc]);
 #pragma unroll
-                for (int cc = 0; cc < 2; cc++)
-                    logits_chunk(p, cg, m, half + 2 * cc, va[cc]);
+                for (int cc = 0; cc < LCH; cc++)
+                    logits_chunk(p, cg, m, half + CSTEP * cc, va[cc], fpre[cc]);
+                acc ^= 1;
+                if (acc == 0)
+                    acc_phase ^= 1;
+            }
+            else if constexpr (EPI == kEpiLn2d) {
+                // chunks half and half + CSTEP (sub-pixels); the tile is
+                // released once the second chunk's accumulator is loaded
+                static_assert(NCHUNK == 2 * CSTEP, "two chunks per epilogue warp");
+                float v[64];
+#pragma unroll 1
+                for (int cc = 0; cc < 2; cc++) {
+                    {
+                        uint32_t r[32], r2[32];
+                        tmem_ld32(tbase + (half + CSTEP * cc) * CW, r);
+                        tmem_ld32(tbase + (half + CSTEP * cc) * CW + 32, r2);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            v[j] = __uint_as_float(r[j]);
+                            v[32 + j] = __uint_as_float(r2[j]);
+                        }
+                    }
+                    if (cc == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive(&tempty[acc]);
+                    }
+                    ln2d_chunk(p, cg, m, half + CSTEP * cc, v);
+                }
                 acc ^= 1;
                 if (acc == 0)
                     acc_phase ^= 1;
             }
             else {
 #pragma unroll 1
-                for (int c = half; c < NCHUNK; c += 2) {
+                for (int c = half; c < NCHUNK; c += CSTEP) {
                     const int n = n0 + c * CW;
                     if (n >= p.N)
                         continue;  // warp-uniform: a chunk entirely beyond C
@@ -746,10 +810,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 v[j] = __uint_as_float(r[j]);
                                 v[32 + j] = __uint_as_float(r2[j]);
                             }
-                        }
-                        if constexpr (EPI == kEpiLn2d) {
-                            ln2d_chunk(p, cg, m, c, v);
-                            continue;
                         }
                         if constexpr (EPI == kEpiConvT) {
                             convt_chunk(p, cg, m, n, v);
@@ -786,10 +846,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < CW / 4; j++)
                             rcur[j] = rnext[j];
-                        if (rfast && c + 2 < NCHUNK) {
+                        if (rfast && c + CSTEP < NCHUNK) {
 #pragma unroll
                             for (int j = 0; j < CW / 4; j++)
-                                rnext[j] = *reinterpret_cast<const float4 *>(rrowp + (c + 2) * CW +
+                                rnext[j] = *reinterpret_cast<const float4 *>(rrowp + (c + CSTEP) * CW +
                                                                              4 * j);
                         }
                         {
@@ -868,7 +928,7 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
            const GemmEpi &p, int num_sms, cudaStream_t s,
            const ConvGeom &cg = ConvGeom{0, 0, 0, 0, 0})
 {
-    using L = GemmSmem<BN>;
+    using L = GemmSmem<BN, false, TMA_STORE ? epi_warps(EPI) : 0>;
     auto kern = gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, EPI>;
     cudaError_t e =
         smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, TMA_STORE, ROPE_PF, CONV3, false, EPI>>(
@@ -878,7 +938,7 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
     const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM) *
                       ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, kThreads, L::BYTES, s>>>(ta, tb, tc, p, cg);
+    kern<<<grid, gemm_threads(EPI), L::BYTES, s>>>(ta, tb, tc, p, cg);
     return (int)cudaGetLastError();
 }
 
@@ -911,7 +971,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms / 2 > 0 ? num_sms / 2 : 1));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(gemm_threads(kEpiGeneric));
     cfg.dynamicSmemBytes = L::BYTES;
     cfg.stream = s;
     cfg.attrs = attr;

@@ -187,18 +187,26 @@ int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor,
 int k_dec_ln_keys(const float *X, const float *R, float *Y, const float *g,
                   const float *b, long rows, float eps, const float *pe, int T,
                   void *Yb, void *Yk, k_stream s);
+/* feat_subpix: an upscaling stage's residual feat fp32 [(2H)*(2W), C] (one
+ * image, NHWC) -> out fp32 [4][C][H*W], out[(d*C + c)*H*W + y*W + x] =
+ * feat[pixel (2y + d/2, 2x + d%2)][c] (ConvTranspose input pixel (y, x),
+ * sub-pixel d); C a multiple of 32. The layout the two epilogues below
+ * read. */
+int k_dec_feat_subpix(const float *feat, int H, int W, int C, float *out, k_stream s);
 /* Last output-upscaling stage + mask logits on the tensor cores (gemm_tc.cu):
  * X bf16 [P*H*W, 64] (the first stage's output), Wt bf16 [128, 64] (the
  * ConvTranspose 64 -> 32 weight in sub-pixel-major rows d*32 + co), bias
- * [32], feat = feat_s0 fp32 [(2H)*(2W), 32], hyper [P, 3, 32] -> out fp32
- * [P, 3, 2H, 2W] = sum_c hyper[p][k][c] * GELU(convt + bias + feat). */
+ * [32], feat = feat_s0 [(2H)*(2W), 32] through k_dec_feat_subpix (fp32
+ * [4][32][H*W]), hyper [P, 3, 32] -> out fp32 [P, 3, 2H, 2W] =
+ * sum_c hyper[p][k][c] * GELU(convt + bias + feat). */
 int k_dec_convt_logits(const void *X, int P, int H, int W, const void *Wt,
                        const float *bias, const float *feat, const float *hyper,
                        float *out, int *err, int num_sms, k_stream s);
 /* First output-upscaling stage on the tensor cores (gemm_tc.cu): X bf16
  * [P*H*W, 256] (the keys), Wt bf16 [256, 256] (the ConvTranspose 256 -> 64
- * weight in sub-pixel-major rows d*64 + co), bias [64], feat = feat_s1 fp32
- * [(2H)*(2W), 64], LayerNorm2d lnw / lnb [64] -> out bf16 [P, 2H, 2W, 64] =
+ * weight in sub-pixel-major rows d*64 + co), bias [64], feat = feat_s1
+ * [(2H)*(2W), 64] through k_dec_feat_subpix (fp32 [4][64][H*W]),
+ * LayerNorm2d lnw / lnb [64] -> out bf16 [P, 2H, 2W, 64] =
  * GELU(LN(convt + bias + feat)). */
 int k_dec_convt_ln2d(const void *X, int P, int H, int W, const void *Wt,
                      const float *bias, const float *feat, const float *lnw,

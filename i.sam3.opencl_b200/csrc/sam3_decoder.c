@@ -511,14 +511,14 @@ int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_
         feat_s1->bytes < 4 * T * 64 * 4)
         return cbi_fail(b, CB_EARG, "decoder set_image");
     CB_TRY(cbi_enter(b));
-    CB_TRY(cbi_kstatus(b,
-                       (int)cudaMemcpyAsync(d->feat_s0, feat_s0->ptr, 16 * T * 32 * 4,
-                                            cudaMemcpyDeviceToDevice, b->stream),
-                       "decoder set_image"));
-    CB_TRY(cbi_kstatus(b,
-                       (int)cudaMemcpyAsync(d->feat_s1, feat_s1->ptr, 4 * T * 64 * 4,
-                                            cudaMemcpyDeviceToDevice, b->stream),
-                       "decoder set_image"));
+    /* the upscaling residuals, sub-pixel-major and channel-major, the
+     * layout the two upscaling epilogues read */
+    LAUNCH("dec_feat", 0, 2.0 * 16 * T * 32 * 4,
+           k_dec_feat_subpix((const float *)feat_s0->ptr, 2 * DEC_GRID, 2 * DEC_GRID, 32,
+                             d->feat_s0, (k_stream)b->stream));
+    LAUNCH("dec_feat", 0, 2.0 * 4 * T * 64 * 4,
+           k_dec_feat_subpix((const float *)feat_s1->ptr, DEC_GRID, DEC_GRID, 64, d->feat_s1,
+                             (k_stream)b->stream));
     /* src = emb + no_mask_embed, srcpe = src + dense PE; the layer-0
      * projections every prompt shares (sam3_model.c:1160-1168) */
     CB_TRY(add(d, d->src, (const float *)emb->ptr, (const float *)d->w[SAM3_DT_NO_MASK],
