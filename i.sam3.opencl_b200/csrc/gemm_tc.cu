@@ -502,6 +502,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         cluster_sync_all();  // both CTAs' barriers exist before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched as a programmatic dependent of the previous kernel: the setup
+    // above used only this CTA's shared and tensor memory (and the tensor
+    // maps, kernel parameters); every global access below waits for that
+    // kernel. All of this grid's CTAs are resident from the start
+    // (persistent grid), so the next kernel may be scheduled right away.
+    griddep_launch();
+    griddep_wait();
 
     constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile
     const int first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
@@ -938,8 +945,17 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
     const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM) *
                       ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, gemm_threads(EPI), L::BYTES, s>>>(ta, tb, tc, p, cg);
-    return (int)cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(gemm_threads(EPI));
+    cfg.dynamicSmemBytes = L::BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, cg);
 }
 
 // Co-resident clusters of two CTAs of the pair kernel, per device (0: not
@@ -964,7 +980,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
         smem_limit_once<gemm_bf16_tc_kernel<BN, OUT_BF16, true, ROPE_PF, CONV3, true>>(L::BYTES);
     if (e != cudaSuccess)
         return (int)e;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
@@ -990,6 +1006,9 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
                       ((p.N + BN - 1) / BN);
     const int pairs = tiles < g_pair_clusters[dev] ? tiles : g_pair_clusters[dev];
     cfg.gridDim = dim3(2 * pairs);
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, cg);
     return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
 }
