@@ -25,7 +25,7 @@ CU = ["gemm_tc.cu", "attn_tc.cu", "attn_simt.cu", "attn_decoder.cu", "elementwis
       "detector.cu"]
 C = ["cuda_backend.c", "sam3_ops.c", "sam3_encoder.c", "sam3_decoder.c", "sam3_neck.c", "sam3_input.c",
      "synth.c"]
-HEADERS = ["tc_ptx.cuh", "tmap.cuh", "kernels.h", "backend_internal.h"]
+HEADERS = ["tc_ptx.cuh", "tmap.cuh", "pdl.cuh", "kernels.h", "backend_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC",

@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(256, C == 16 ? 3 : 1) mha_few_kernel(const flo
                                                       float *__restrict__ O, int P, int Nq,
                                                       int Nk, float scale)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     constexpr int D = C * kHeads, CP = C + 4, ROW = kHeads * CP;
     extern __shared__ float kv[];  // K rows then V rows, [Nk][8][CP] each
     float *ks = kv;
@@ -320,6 +322,8 @@ __global__ void __launch_bounds__(256) mha_few2_kernel(const void *__restrict__ 
                                                       void *__restrict__ O, int P, int Nq, int Nk,
                                                       float kscale)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     constexpr int D = kManyD;
     const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -493,6 +497,8 @@ __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
     const float *__restrict__ Q, long sq, int k_per_prompt, int v_per_prompt,
     float *__restrict__ part, int P, int Nq, int Nk, int segs, float qscale, int *err)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     extern __shared__ __align__(16) float sm_raw[];
     constexpr int ESZ = KV_BF16 ? 2 : 4;
     constexpr int STAGE_B = kManyStage * ESZ;             // bytes per stage
@@ -729,6 +735,8 @@ __global__ void __launch_bounds__(256) mha_many_combine_kernel(const float *__re
                                                                float *__restrict__ O, int P,
                                                                int Nq, int nch, int G, int segs)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // (p, qi, h)
     const int lane = threadIdx.x & 31;
     if (w >= (long)P * Nq * kHeads)
@@ -817,9 +825,9 @@ int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
         return (int)e;
     const long units = (long)P * ((Nq + 15) / 16);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
-    mha_few2_kernel<Q_BF16, OUT_BF16><<<(unsigned)(units < cap ? units : cap), 256, 0, st>>>(
-        qp, sq, kp, sk, vp, sv, o, P, Nq, Nk, scale * 1.4426950408889634f);
-    return (int)cudaGetLastError();
+    return launch_pdl(mha_few2_kernel<Q_BF16, OUT_BF16>, dim3((unsigned)(units < cap ? units : cap)),
+                      dim3(256), 0, st, qp, sq, kp, sk, vp, sv, o, P, Nq, Nk,
+                      scale * 1.4426950408889634f);
 }
 
 template <int C>
@@ -839,9 +847,8 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
         return (int)e;
     const long units = (long)P * ((Nq + 31) / 32);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
-    kern<<<(unsigned)(units < cap ? units : cap), 256, smem, st>>>(qp, sq, kp, sk, vp, sv, o, P,
-                                                                    Nq, Nk, scale);
-    return (int)cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)(units < cap ? units : cap)), dim3(256), smem, st, qp, sq,
+                      kp, sk, vp, sv, o, P, Nq, Nk, scale);
 }
 
 template <bool KV_BF16>
@@ -870,16 +877,15 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
     if (e != cudaSuccess)
         return (int)e;
     dim3 grid(pl.G, 1, (Nq + 7) / 8);
-    mha_many_split_kernel<KV_BF16><<<grid, kManyThreads, smem, st>>>(
-        tk, tv, qp, sq, sk != 0, sv != 0, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
-        scale * 1.4426950408889634f, err);
-    e = cudaGetLastError();
-    if (e != cudaSuccess)
-        return (int)e;
+    int rc = launch_pdl(mha_many_split_kernel<KV_BF16>, grid, dim3(kManyThreads), smem, st, tk, tv,
+                        qp, sq, sk != 0, sv != 0, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
+                        scale * 1.4426950408889634f, err);
+    if (rc != 0)
+        return rc;
     const long total = (long)P * Nq * kHeads * 32;  // a warp per (prompt, query, head)
-    mha_many_combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-        static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk, pl.G, pl.segs);
-    return (int)cudaGetLastError();
+    return launch_pdl(mha_many_combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0,
+                      st, static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk,
+                      pl.G, pl.segs);
 }
 
 }  // namespace

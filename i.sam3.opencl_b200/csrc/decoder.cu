@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
                                                         float *__restrict__ hyper,
                                                         float *__restrict__ iou)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     __shared__ float xs[256], hs[256];
     const int p = blockIdx.x, m = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(256) ln_keys_kernel(const float *X,
                                                       int T, uint2 *__restrict__ Yb,
                                                       uint2 *__restrict__ Yk)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows)
@@ -324,8 +328,7 @@ extern "C" int k_dec_heads(const float *tok, int P, const k_dec_heads_w *hw, flo
 {
     if (P <= 0 || P > 65535 || !hw)
         return K_EARG;
-    dec_heads_kernel<<<dim3(P, 4), 256, 0, STREAM(s)>>>(tok, *hw, hyper, iou);
-    return (int)cudaGetLastError();
+    return launch_pdl(dec_heads_kernel, dim3(P, 4), dim3(256), 0, STREAM(s), tok, *hw, hyper, iou);
 }
 
 extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor, void *dst,
@@ -356,8 +359,8 @@ extern "C" int k_dec_ln_keys(const float *X, const float *R, float *Y, const flo
         (reinterpret_cast<uintptr_t>(Y) & 15) || (reinterpret_cast<uintptr_t>(pe) & 15) ||
         (reinterpret_cast<uintptr_t>(Yb) & 7) || (reinterpret_cast<uintptr_t>(Yk) & 7))
         return K_EARG;
-    ln_keys_kernel<<<grid_for(rows, 8), 256, 0, STREAM(s)>>>(
-        X, R, Y, g, b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb), reinterpret_cast<uint2 *>(Yk));
-    return (int)cudaGetLastError();
+    return launch_pdl(ln_keys_kernel, dim3(grid_for(rows, 8)), dim3(256), 0, STREAM(s), X, R, Y, g,
+                      b, rows, eps, pe, T, reinterpret_cast<uint2 *>(Yb),
+                      reinterpret_cast<uint2 *>(Yk));
 }
 

@@ -19,6 +19,7 @@
 //     the keys split over CTAs (online softmax per split, merged by a
 //     combine kernel).
 #include "kernels.h"
+#include "pdl.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -87,6 +88,8 @@ __global__ void __launch_bounds__(128) pad_heads_kernel(const void *__restrict__
                                                         long rows, int heads, int hd,
                                                         uint2 *__restrict__ out)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const int e4 = heads * 16;
     for (int r = 0; r < kPackRows; r++) {
         const long n = (long)blockIdx.x * kPackRows + r;
@@ -308,12 +311,10 @@ extern "C" int k_pad_heads64(const void *src, int src_bf16, long ld, long rows, 
         return K_EARG;
     const int g = grid_for(rows, kPackRows);
     if (src_bf16)
-        pad_heads_kernel<true><<<g, 128, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
-                                                          reinterpret_cast<uint2 *>(out));
-    else
-        pad_heads_kernel<false><<<g, 128, 0, STREAM(s)>>>(src, ld, rows, heads, hd,
-                                                           reinterpret_cast<uint2 *>(out));
-    return (int)cudaGetLastError();
+        return launch_pdl(pad_heads_kernel<true>, dim3(g), dim3(128), 0, STREAM(s), src, ld, rows,
+                          heads, hd, reinterpret_cast<uint2 *>(out));
+    return launch_pdl(pad_heads_kernel<false>, dim3(g), dim3(128), 0, STREAM(s), src, ld, rows,
+                      heads, hd, reinterpret_cast<uint2 *>(out));
 }
 
 extern "C" int k_rpb_bias(const float *dy, const float *dx, int Nq, int Nk, int W, int heads,

@@ -215,6 +215,8 @@ __global__ void __launch_bounds__(256) rope_cast_kernel(const float *__restrict_
 // add_bcast (sam3_kernels.cl:701-708).
 __global__ void add_bcast_kernel(float *out, const float *a, const float *b, long n, long bmod)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n)
         out[i] = a[i] + b[i % bmod];
@@ -225,6 +227,8 @@ __global__ void add_bcast_kernel(float *out, const float *a, const float *b, lon
 __global__ void add_bf16_kernel(const float *__restrict__ a, const float *__restrict__ b,
                                 __nv_bfloat16 *__restrict__ out, long n)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n)
         out[i] = __float2bfloat16_rn(a[i] + b[i]);
@@ -367,6 +371,8 @@ __global__ void __launch_bounds__(256) patch_embed_in_kernel(const uint8_t *__re
 __global__ void cast_f32_bf16_v8_kernel(const float4 *__restrict__ x, uint4 *__restrict__ y,
                                         long n8)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
          i += (long)gridDim.x * blockDim.x) {
         const float4 a = x[2 * i], b = x[2 * i + 1];
@@ -377,6 +383,8 @@ __global__ void cast_f32_bf16_v8_kernel(const float4 *__restrict__ x, uint4 *__r
 
 __global__ void cast_f32_bf16_kernel(const float *x, __nv_bfloat16 *y, long n)
 {
+    griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
+    griddep_launch();
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n)
         y[i] = __float2bfloat16_rn(x[i]);
@@ -505,17 +513,16 @@ extern "C" int k_add_bcast(float *out, const float *a, const float *b, long n, l
         return 0;
     if (bmod <= 0)
         return K_EARG;
-    add_bcast_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(out, a, b, n, bmod);
-    LAUNCH_RET();
+    return launch_pdl(add_bcast_kernel, dim3(grid_for(n, 256)), dim3(256), 0, STREAM(s), out, a, b,
+                      n, bmod);
 }
 
 extern "C" int k_add_bf16(const float *a, const float *b, void *out, long n, k_stream s)
 {
     if (n <= 0)
         return K_EARG;
-    add_bf16_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
-        a, b, reinterpret_cast<__nv_bfloat16 *>(out), n);
-    LAUNCH_RET();
+    return launch_pdl(add_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, STREAM(s), a, b,
+                      reinterpret_cast<__nv_bfloat16 *>(out), n);
 }
 
 extern "C" int k_window_partition(const float *X, float *out, int H, int C, int ws, int nwx,
@@ -589,13 +596,12 @@ extern "C" int k_cast_f32_bf16(const float *x, void *y, long n, k_stream s)
         return 0;
     if (n % 8 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 15)) {
         const int g = grid_for(n / 8, 256);
-        cast_f32_bf16_v8_kernel<<<g < 148 * 16 ? g : 148 * 16, 256, 0, STREAM(s)>>>(
-            reinterpret_cast<const float4 *>(x), reinterpret_cast<uint4 *>(y), n / 8);
-        LAUNCH_RET();
+        return launch_pdl(cast_f32_bf16_v8_kernel, dim3(g < 148 * 16 ? g : 148 * 16), dim3(256), 0,
+                          STREAM(s), reinterpret_cast<const float4 *>(x),
+                          reinterpret_cast<uint4 *>(y), n / 8);
     }
-    cast_f32_bf16_kernel<<<grid_for(n, 256), 256, 0, STREAM(s)>>>(
-        x, reinterpret_cast<__nv_bfloat16 *>(y), n);
-    LAUNCH_RET();
+    return launch_pdl(cast_f32_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, STREAM(s), x,
+                      reinterpret_cast<__nv_bfloat16 *>(y), n);
 }
 
 extern "C" int k_cast_bf16_f32(const void *x, float *y, long n, k_stream s)

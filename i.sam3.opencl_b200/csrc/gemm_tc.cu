@@ -502,11 +502,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         cluster_sync_all();  // both CTAs' barriers exist before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Launched as a programmatic dependent of the previous kernel: the setup
-    // above used only this CTA's shared and tensor memory (and the tensor
-    // maps, kernel parameters); every global access below waits for that
-    // kernel. All of this grid's CTAs are resident from the start
-    // (persistent grid), so the next kernel may be scheduled right away.
+    // Launched as a programmatic dependent of the previous kernel (pdl.cuh):
+    // the setup above used only this CTA's shared and tensor memory (and the
+    // tensor maps, kernel parameters); every global access below waits for
+    // that kernel. The next kernel may be scheduled once every CTA has its
+    // tensor memory.
     griddep_launch();
     griddep_wait();
 
@@ -945,17 +945,7 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
     const int tiles = (CONV3 ? cg.cimg * cg.cyb * cg.cxb : (p.M + BM - 1) / BM) *
                       ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(gemm_threads(EPI));
-    cfg.dynamicSmemBytes = L::BYTES;
-    cfg.stream = s;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p, cg);
+    return launch_pdl(kern, dim3(grid), dim3(gemm_threads(EPI)), L::BYTES, s, ta, tb, tc, p, cg);
 }
 
 // Co-resident clusters of two CTAs of the pair kernel, per device (0: not

@@ -5,6 +5,8 @@
 // tcgen05.mma (PTX ISA "Matrix Descriptors" and "Instruction descriptor").
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -61,24 +63,6 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
 __device__ __forceinline__ void fence_mbar_init()
 {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Programmatic dependent launch. A kernel launched with the programmatic
-// stream-serialization attribute may start while the previous kernel in the
-// stream is still running: griddep_wait() blocks until that kernel has
-// completed and its memory operations are visible (a no-op without the
-// attribute), so nothing before it may touch global memory the previous
-// kernel reads or writes. griddep_launch() lets the next such kernel be
-// scheduled once every CTA of this grid has executed it (or exited); that
-// kernel still waits for this one's completion before its own accesses.
-__device__ __forceinline__ void griddep_wait()
-{
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-__device__ __forceinline__ void griddep_launch()
-{
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
