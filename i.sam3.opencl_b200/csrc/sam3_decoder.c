@@ -620,11 +620,12 @@ static int self_attention(cb_decoder *d, int P, int l)
 /* Image -> token attention of layer l (sam3_model.c:1297-1309, 1334-1348):
  * queries from the image stream (the shared layer-0 projection, or kin of
  * layer 1), keys and values from the tokens; the output projection lands
- * in keys, + src (layer 0: the add_bcast of sam3_model.c:1307 as the GEMM
- * residual with row m % T) or + keys (layer 1), then norm4, which also
- * writes the bf16 operands keys and keys + PE of the next token -> image
- * attention (and of the upscaling). After layer 1 nothing reads the fp32
- * keys again, so that LayerNorm writes only the bf16 copies. */
+ * in keys, + keys as the GEMM residual (layer 1) or + src (layer 0: the
+ * add_bcast of sam3_model.c:1307, row m % T, added by norm4 before its
+ * statistics), then norm4, which also writes the bf16 operands keys and
+ * keys + PE of the next token -> image attention (and of the upscaling).
+ * After layer 1 nothing reads the fp32 keys again, so that LayerNorm writes
+ * only the bf16 copies. */
 static int i2t_attention(cb_decoder *d, int P, int l)
 {
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
