@@ -1031,7 +1031,12 @@ extern "C" int k_gemm_bf16_tc(int M, int N, int K, const void *A, int lda, const
         return K_EARG;
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 15))
         return K_EARG;
-    const int BN = N <= 128 ? 128 : 256;
+    // 128-wide tiles for N <= 128, and where 256-wide ones would leave more
+    // than half of the SMs without a tile (the decoder's token stream: 512
+    // rows, 4 tiles at N = 256): twice the CTAs, half the serial MMA work
+    // per CTA.
+    const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
+    const int BN = N <= 128 || tiles256 < num_sms / 2 ? 128 : 256;
     CUtensorMap ta, tb, tc, tb_half;
     if (!make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM) ||
         !make_tmap_bf16(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)BN))
