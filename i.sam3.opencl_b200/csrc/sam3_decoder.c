@@ -71,6 +71,9 @@ struct cb_decoder {
     /* token stream [batch * 8, 256] and its scratch */
     float *qpe, *qry, *sq, *sk, *sv, *so, *sh;
     void *tok_bf16;             /* bf16 [batch * 8, 2048] GEMM operand */
+    void *qv_bf16;              /* bf16(qry) [batch * 8, 256]: input of the
+                                 * image -> token values, kept for the next
+                                 * layer's self-attention values */
     /* per-prompt image stream */
     float *keys;                /* [batch * T, 256] */
     void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
@@ -114,7 +117,7 @@ void cb_decoder_free(cb_decoder *d)
     {
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
-                       d->sh, d->tok_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
+                       d->sh, d->tok_bf16, d->qv_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
                        d->bv, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws, d->k0_pad, d->v0_pad, d->q_pad,
                        d->xws};
@@ -173,6 +176,7 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->so, nt * DEC_DIM * 4);
     A(d->sh, nt * 2048 * 4);
     A(d->tok_bf16, nt * 2048 * 2);
+    A(d->qv_bf16, nt * DEC_DIM * 2);
     A(d->keys, B * T * DEC_DIM * 4);
     A(d->keys_bf16, B * T * DEC_DIM * 2);
     A(d->kin_bf16, B * T * DEC_DIM * 2);
@@ -609,8 +613,15 @@ static int self_attention(cb_decoder *d, int P, int l)
         CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                       K_ACT_NONE));
     CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
-    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
-                  K_ACT_NONE));
+    /* The values' input bf16(qry) is already rounded: in layer 0 by the
+     * queries' projection above, in layer 1 by the previous image -> token
+     * attention (qry is unchanged since). */
+    if (l)
+        CB_TRY(lin16(d, "dec_gemm_tok", d->qv_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, VW),
+                     ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    else
+        CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
+                            K_ACT_NONE));
     CB_TRY(mha(d, P, DEC_NTOK, DEC_NTOK, DEC_DIM, d->sq, DEC_NTOK * DEC_DIM, d->sk,
                DEC_NTOK * DEC_DIM, d->sv, DEC_NTOK * DEC_DIM, d->so));
     return lintok(d, d->so, nt, DEC_DIM, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, l,
@@ -645,8 +656,9 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     }
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
                   K_ACT_NONE));
-    CB_TRY(lintok(d, d->qry, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB), d->sv, 0,
-                  K_ACT_NONE));
+    /* bf16(qry) into qv_bf16, kept for the next layer's self-attention */
+    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->qv_bf16, nt, DEC_DIM, 128, ATT(blk, VW),
+                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
     {
         cb_backend *b = d->b;
 
