@@ -178,9 +178,11 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi)
 // consumers need written in the same pass. R (optional) is the residual
 // shared by every prompt, row % T, added to X before the statistics (layer
 // 0's input: the image embedding), so the output projection before this
-// kernel stores plainly. Y (fp32, may alias X; NULL = not written), Yb = bf16(Y) (operand of the value projection and of the
-// first upscaling GEMM) and Yk = bf16(Y + pe[row % T]) (keys + dense
-// positional encoding, operand of the key / query projections). One warp
+// kernel stores plainly. Y (fp32, may alias X), Yb = bf16(Y) (operand of
+// the value projection and of the first upscaling GEMM) and Yk = bf16(Y +
+// pe[row % T]) (keys + dense positional encoding, operand of the key /
+// query projections); each NULL = not written. The token stream's norms
+// use it too (T = rows, pe = the tokens' positional encoding). One warp
 // per row, 8 values per lane; two-pass mean / variance as the reference.
 __global__ void __launch_bounds__(256) ln_keys_kernel(const float *X,
                                                       const float *__restrict__ R, float *Y,
@@ -232,10 +234,13 @@ __global__ void __launch_bounds__(256) ln_keys_kernel(const float *X,
         y.w = (v[i].w - mean) * inv * gg.w + bt.w;
         if (Y)
             reinterpret_cast<float4 *>(Y + row * 256)[c4] = y;
-        Yb[row * 64 + c4] = make_uint2(pack2(y.x, y.y), pack2(y.z, y.w));
-        const float4 p4 = __ldg(pr + c4);
-        Yk[row * 64 + c4] =
-            make_uint2(pack2(y.x + p4.x, y.y + p4.y), pack2(y.z + p4.z, y.w + p4.w));
+        if (Yb)
+            Yb[row * 64 + c4] = make_uint2(pack2(y.x, y.y), pack2(y.z, y.w));
+        if (Yk) {
+            const float4 p4 = __ldg(pr + c4);
+            Yk[row * 64 + c4] =
+                make_uint2(pack2(y.x + p4.x, y.y + p4.y), pack2(y.z + p4.z, y.w + p4.w));
+        }
     }
 }
 
@@ -354,7 +359,8 @@ extern "C" int k_dec_ln_keys(const float *X, const float *R, float *Y, const flo
                              const float *b, long rows, float eps, const float *pe, int T, void *Yb,
                              void *Yk, k_stream s)
 {
-    if (rows <= 0 || T <= 0 || !Yb || !Yk || (reinterpret_cast<uintptr_t>(X) & 15) ||
+    if (rows <= 0 || T <= 0 || (!Y && !Yb && !Yk) || (Yk && !pe) ||
+        (reinterpret_cast<uintptr_t>(X) & 15) ||
         (reinterpret_cast<uintptr_t>(R) & 15) ||
         (reinterpret_cast<uintptr_t>(Y) & 15) || (reinterpret_cast<uintptr_t>(pe) & 15) ||
         (reinterpret_cast<uintptr_t>(Yb) & 7) || (reinterpret_cast<uintptr_t>(Yk) & 7))

@@ -176,8 +176,8 @@ int k_dec_heads(const float *tok, int P, const struct k_dec_heads_w *hw,
 int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor,
                           void *dst, k_stream s);
 /* Decoder fusions. ln_keys: LayerNorm of 256-wide rows X (+ R[row % T]
- * first when R is given), Y fp32 (may alias X, NULL = skipped), Yb =
- * bf16(Y), Yk = bf16(Y + pe[row % T]). up1:
+ * first when R is given), Y fp32 (may alias X), Yb = bf16(Y), Yk =
+ * bf16(Y + pe[row % T]); each output NULL = skipped, at least one given. up1:
  * ConvT 256 -> 64 scatter of G [P*H*W, 256] + bias + feat [4HW, 64],
  * LayerNorm2d (g, b, eps), GELU -> bf16 [P, 2H, 2W, 64]. up2_logits: ConvT
  * 64 -> 32 scatter of G [P*H*W, 128] (sub-pixel-major columns d*32 + co)

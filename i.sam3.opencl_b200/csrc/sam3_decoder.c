@@ -71,9 +71,10 @@ struct cb_decoder {
     /* token stream [batch * 8, 256] and its scratch */
     float *qpe, *qry, *sq, *sk, *sv, *so, *sh;
     void *tok_bf16;             /* bf16 [batch * 8, 2048] GEMM operand */
-    void *qv_bf16;              /* bf16(qry) [batch * 8, 256]: input of the
-                                 * image -> token values, kept for the next
-                                 * layer's self-attention values */
+    void *qv_bf16;              /* bf16(qry) [batch * 8, 256] from a layer's
+                                 * last token norm: input of its image ->
+                                 * token values and of the next layer's
+                                 * self-attention values */
     /* per-prompt image stream */
     float *keys;                /* [batch * T, 256] */
     void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
@@ -444,14 +445,22 @@ static int add(cb_decoder *d, float *out, const float *a, const float *bb, long 
     return CB_OK;
 }
 
-/* tok_bf16 = bf16(qry + qpe): the tokens with their positional encoding,
- * read only by the Linears that follow (lintok_again). */
-static int add_tok_pe(cb_decoder *d, long nt)
+/* A norm of the token stream (LayerNorm of qry in place, weights wi / bi)
+ * that also writes the bf16 operands of the Linears after it in the same
+ * pass: yb = bf16(qry) (NULL: none) and, with pe, tok_bf16 = bf16(qry +
+ * qpe), the queries / keys input of the next attention. Each attention
+ * step reads tok_bf16 as the last norm left it (lintok_again): qry does not
+ * change between a norm and the attention projections that follow it (the
+ * image -> token attention updates the image stream only). */
+static int lntok(cb_decoder *d, long nt, int wi, int bi, void *yb, int pe)
 {
     cb_backend *b = d->b;
 
-    LAUNCH("dec_add", (double)nt * DEC_DIM, (double)nt * DEC_DIM * 10,
-           k_add_bf16(d->qry, d->qpe, d->tok_bf16, nt * DEC_DIM, (k_stream)b->stream));
+    LAUNCH("dec_layernorm", 8.0 * nt * DEC_DIM,
+           (double)nt * DEC_DIM * (8 + (yb ? 2 : 0) + (pe ? 6 : 0)),
+           k_dec_ln_keys(d->qry, NULL, d->qry, (const float *)d->w[wi], (const float *)d->w[bi],
+                         nt, DEC_EPS, d->qpe, (int)nt, yb, pe ? d->tok_bf16 : NULL,
+                         (k_stream)b->stream));
     return CB_OK;
 }
 
@@ -565,7 +574,6 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
 {
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
 
-    CB_TRY(add_tok_pe(d, nt));
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                   K_ACT_NONE));
     CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
@@ -585,8 +593,7 @@ static int token_mlp(cb_decoder *d, int P, int l)
     const long nt = (long)P * DEC_NTOK;
     const double dr = (double)nt;
 
-    LAUNCH("dec_cast", 0, dr * DEC_DIM * 6,
-           k_cast_f32_bf16(d->qry, d->tok_bf16, nt * DEC_DIM, (k_stream)b->stream));
+    /* tok_bf16 = bf16(qry), written by the norm before (lntok) */
     LAUNCH("dec_gemm_tok", 2.0 * dr * DEC_DIM * 2048,
            dr * DEC_DIM * 2 + (double)DEC_DIM * 2048 * 2 + dr * 2048 * 2,
            k_gemm_bf16_tc((int)nt, 2048, DEC_DIM, d->tok_bf16, DEC_DIM, d->w[LAY(l, M1W)], DEC_DIM,
@@ -604,18 +611,16 @@ static int self_attention(cb_decoder *d, int P, int l)
     const long nt = (long)P * DEC_NTOK;
     const int blk = l ? SAM3_DA_L1_SELF : SAM3_DA_L0_SELF;
 
-    if (l) {
-        CB_TRY(add_tok_pe(d, nt));
+    if (l)  /* tok_bf16 = bf16(qry + qpe) from layer 0's last token norm */
         CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                             K_ACT_NONE));
-    }
     else
         CB_TRY(lintok(d, d->qry, nt, DEC_DIM, DEC_DIM, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                       K_ACT_NONE));
     CB_TRY(lintok_again(d, nt, DEC_DIM, DEC_DIM, ATT(blk, KW), ATT(blk, KB), d->sk, 0, K_ACT_NONE));
     /* The values' input bf16(qry) is already rounded: in layer 0 by the
-     * queries' projection above, in layer 1 by the previous image -> token
-     * attention (qry is unchanged since). */
+     * queries' projection above, in layer 1 by layer 0's last token norm
+     * (qry is unchanged since). */
     if (l)
         CB_TRY(lin16(d, "dec_gemm_tok", d->qv_bf16, nt, DEC_DIM, DEC_DIM, ATT(blk, VW),
                      ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
@@ -642,7 +647,6 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
     const int blk = l ? SAM3_DA_L1_I2T : SAM3_DA_L0_I2T;
 
-    CB_TRY(add_tok_pe(d, nt));
     if (l) {
         cb_backend *b = d->b;
 
@@ -656,9 +660,10 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     }
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
                   K_ACT_NONE));
-    /* bf16(qry) into qv_bf16, kept for the next layer's self-attention */
-    CB_TRY(lin32(d, "dec_gemm_tok", d->qry, d->qv_bf16, nt, DEC_DIM, 128, ATT(blk, VW),
-                 ATT(blk, VB), d->sv, NULL, 0, K_ACT_NONE));
+    /* keys from tok_bf16, values from qv_bf16: both written by the norm
+     * before (lntok) */
+    CB_TRY(lin16(d, "dec_gemm_tok", d->qv_bf16, nt, DEC_DIM, 128, ATT(blk, VW), ATT(blk, VB),
+                 d->sv, NULL, 0, K_ACT_NONE));
     {
         cb_backend *b = d->b;
 
@@ -737,28 +742,28 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     /* Layer 0: self attention (no PE, no residual), token -> image on the
      * shared layer-0 projections, MLP, image -> token. */
     CB_TRY(self_attention(d, P, 0));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N1W), LAY(0, N1B), DEC_EPS, K_ACT_NONE));
-    CB_TRY(add_tok_pe(d, nt));
+    CB_TRY(lntok(d, nt, LAY(0, N1W), LAY(0, N1B), NULL, 1));
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
                   ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
     CB_TRY(mha_t2i(d, P, d->kp0, 0, d->vp0, 0));
     CB_TRY(lintok(d, d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
                   ATT(SAM3_DA_L0_T2I, OB), d->qry, 1, K_ACT_NONE));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N2W), LAY(0, N2B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(lntok(d, nt, LAY(0, N2W), LAY(0, N2B), d->tok_bf16, 0));
     CB_TRY(token_mlp(d, P, 0));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(0, N3W), LAY(0, N3B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(lntok(d, nt, LAY(0, N3W), LAY(0, N3B), d->qv_bf16, 1));
     CB_TRY(i2t_attention(d, P, 0));
 
     /* Layer 1. */
     CB_TRY(self_attention(d, P, 1));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N1W), LAY(1, N1B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(lntok(d, nt, LAY(1, N1W), LAY(1, N1B), NULL, 1));
     CB_TRY(t2i_attention(d, P, SAM3_DA_L1_T2I));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N2W), LAY(1, N2B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(lntok(d, nt, LAY(1, N2W), LAY(1, N2B), d->tok_bf16, 0));
     CB_TRY(token_mlp(d, P, 1));
-    CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, LAY(1, N3W), LAY(1, N3B), DEC_EPS, K_ACT_NONE));
+    CB_TRY(lntok(d, nt, LAY(1, N3W), LAY(1, N3B), d->qv_bf16, 1));
     CB_TRY(i2t_attention(d, P, 1));
 
-    /* Final token -> image attention. */
+    /* Final token -> image attention (its queries' input tok_bf16 from
+     * layer 1's last token norm). */
     CB_TRY(t2i_attention(d, P, SAM3_DA_FINAL_T2I));
     CB_TRY(ln(d, d->qry, d->qry, 0, nt, DEC_DIM, SAM3_DT_NF_W, SAM3_DT_NF_B, DEC_EPS,
               K_ACT_NONE));
