@@ -731,8 +731,10 @@ __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
 // per (prompt, query, head): the lanes take the records' offsets and sums
 // (lane = record) for the maximum and the weights, then half-warps take
 // alternate records, a lane one output channel, and the halves are added.
+// OUT_BF16: O written as bf16 (the operand of the output projection).
+template <bool OUT_BF16>
 __global__ void __launch_bounds__(256) mha_many_combine_kernel(const float *__restrict__ part,
-                                                               float *__restrict__ O, int P,
+                                                               void *__restrict__ O, int P,
                                                                int Nq, int nch, int G, int segs)
 {
     griddep_wait();  // launched as a programmatic dependent (pdl.cuh)
@@ -784,8 +786,13 @@ __global__ void __launch_bounds__(256) mha_many_combine_kernel(const float *__re
     for (int o = 16; o; o >>= 1)
         L += __shfl_xor_sync(0xffffffffu, L, o);
     acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-    if (half == 0)
-        O[(p * Nq + qi) * kManyD + h * kManyC + c] = acc / L;
+    if (half == 0) {
+        const long i = (p * Nq + qi) * kManyD + h * kManyC + c;
+        if constexpr (OUT_BF16)
+            static_cast<__nv_bfloat16 *>(O)[i] = __float2bfloat16_rn(acc / L);
+        else
+            static_cast<float *>(O)[i] = acc / L;
+    }
 }
 
 // Plan of the many-keys kernel: G CTAs per query group of 8 (two per SM
@@ -853,8 +860,8 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
 
 template <bool KV_BF16>
 int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp, long sk,
-                const void *vp, long sv, float *o, void *ws, size_t ws_bytes, float scale,
-                int *err, int num_sms, cudaStream_t st)
+                const void *vp, long sv, void *o, bool out_bf16, void *ws, size_t ws_bytes,
+                float scale, int *err, int num_sms, cudaStream_t st)
 {
     const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
     if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15) ||
@@ -883,9 +890,13 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
     if (rc != 0)
         return rc;
     const long total = (long)P * Nq * kHeads * 32;  // a warp per (prompt, query, head)
-    return launch_pdl(mha_many_combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0,
-                      st, static_cast<const float *>(ws), o, P, Nq, (Nk + kChunk - 1) / kChunk,
-                      pl.G, pl.segs);
+    const dim3 cgrid((unsigned)((total + 255) / 256));
+    const float *part = static_cast<const float *>(ws);
+    const int nch = (Nk + kChunk - 1) / kChunk;
+    return out_bf16 ? launch_pdl(mha_many_combine_kernel<true>, cgrid, dim3(256), 0, st, part, o,
+                                 P, Nq, nch, pl.G, pl.segs)
+                    : launch_pdl(mha_many_combine_kernel<false>, cgrid, dim3(256), 0, st, part, o,
+                                 P, Nq, nch, pl.G, pl.segs);
 }
 
 }  // namespace
@@ -914,8 +925,8 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         // The reference rejects the same shape (sam3_model.c:429-430).
         if (c != kManyC)
             return K_EARG;
-        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes, scale, err,
-                                  num_sms, st);
+        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, false, ws, ws_bytes, scale,
+                                  err, num_sms, st);
     }
     if (c == 16)
         return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
@@ -937,7 +948,7 @@ extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, co
 }
 
 extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
-                                long sk, const void *vp, long sv, float *o, void *ws,
+                                long sk, const void *vp, long sv, void *o, int out_bf16, void *ws,
                                 size_t ws_bytes, int *err, int num_sms, k_stream s)
 {
     using namespace sam3;
@@ -945,6 +956,6 @@ extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq,
         ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
         (sk & 7) || (sv & 7))
         return K_EARG;
-    return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, ws, ws_bytes,
+    return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, out_bf16 != 0, ws, ws_bytes,
                              1.0f / sqrtf((float)kManyC), err, num_sms, STREAM(s));
 }

@@ -152,9 +152,11 @@ int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *
                    long sk, const float *vp, long sv, void *o, int num_sms, k_stream s);
 /* The decoder's token -> image attention (dint 128, more than 64 keys) with
  * its keys and values kp / vp read as bf16 rows (as their projections write
- * them; row strides in elements); otherwise k_mha (same workspace). */
+ * them; row strides in elements) and o written as bf16 when out_bf16 (the
+ * operand of the output projection), else fp32; otherwise k_mha (same
+ * workspace). */
 int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
-                     long sk, const void *vp, long sv, float *o, void *ws,
+                     long sk, const void *vp, long sv, void *o, int out_bf16, void *ws,
                      size_t ws_bytes, int *err, int num_sms, k_stream s);
 
 /* Mask decoder (decoder.cu). convt_scatter: G [P*H*W, Co*4] (16-byte

@@ -478,7 +478,9 @@ static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, l
 }
 
 /* Token -> image attention of the P prompts' queries sq on bf16 keys and
- * values (row strides in elements; 0: shared by all prompts) into so. */
+ * values (row strides in elements; 0: shared by all prompts) into so's
+ * storage as bf16 [P * 8, 128], the operand of the output projection (no
+ * rounding pass). */
 static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, long sv)
 {
     cb_backend *b = d->b;
@@ -494,13 +496,13 @@ static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, 
         LAUNCH("dec_mha_t2i", 4.0 * nt * (double)DEC_T * 128,
                (double)nt * 512 * 2 + 2.0 * DEC_T * 512 * 2 + (double)nt * 128 * 4,
                k_attn_tc_cross(d->q_pad, 512, d->k0_pad, 512, d->v0_pad, 512, 1, (int)nt, DEC_T,
-                               8, 0.25f, NULL, d->so, 128, 16, 0, d->xws, d->xws_bytes, b->d_err,
+                               8, 0.25f, NULL, d->so, 128, 16, 1, d->xws, d->xws_bytes, b->d_err,
                                (k_stream)b->stream));
         return CB_OK;
     }
     LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,
            4.0 * (double)P * DEC_NTOK * 128 * 2 + 2.0 * (sk ? (double)P : 1.0) * DEC_T * 128 * 2,
-           k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so,
+           k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so, 1,
                             d->mha_ws, d->mha_ws_bytes, b->d_err, b->num_sms,
                             (k_stream)b->stream));
     return CB_OK;
@@ -581,7 +583,8 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
     CB_TRY(lin16h(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
                   ATT(blk, VB), d->bv));
     CB_TRY(mha_t2i(d, P, d->bk, (long)DEC_T * 128, d->bv, (long)DEC_T * 128));
-    return lintok(d, d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry, 1, K_ACT_NONE);
+    return lin16(d, "dec_gemm_tok", d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry,
+                 d->qry, 0, K_ACT_NONE);
 }
 
 /* token_mlp (sam3_model.c:1231-1237): 256 -> 2048 (ReLU) -> 256, residual.
@@ -746,8 +749,8 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
                   ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
     CB_TRY(mha_t2i(d, P, d->kp0, 0, d->vp0, 0));
-    CB_TRY(lintok(d, d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
-                  ATT(SAM3_DA_L0_T2I, OB), d->qry, 1, K_ACT_NONE));
+    CB_TRY(lin16(d, "dec_gemm_tok", d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
+                 ATT(SAM3_DA_L0_T2I, OB), d->qry, d->qry, 0, K_ACT_NONE));
     CB_TRY(lntok(d, nt, LAY(0, N2W), LAY(0, N2B), d->tok_bf16, 0));
     CB_TRY(token_mlp(d, P, 0));
     CB_TRY(lntok(d, nt, LAY(0, N3W), LAY(0, N3B), d->qv_bf16, 1));
