@@ -393,24 +393,36 @@ __device__ __forceinline__ void logits_chunk(const GemmEpi &p, const ConvGeom &c
     const long opix = logits_pixel(cg, m, d);
     const float4 *bq = reinterpret_cast<const float4 *>(p.bias);
     const float4 *h = reinterpret_cast<const float4 *>(cg.hyper + (long)pr * 96);
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
+    // packed fp32 (the epilogue is issue-bound): the adds on channel pairs,
+    // each logit as even / odd channel partial sums added at the end
+    uint64_t a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const float4 bv = __ldg(bq + j);
-        float u0 = (v[4 * j] + bv.x) + f[4 * j], u1 = (v[4 * j + 1] + bv.y) + f[4 * j + 1];
-        float u2 = (v[4 * j + 2] + bv.z) + f[4 * j + 2], u3 = (v[4 * j + 3] + bv.w) + f[4 * j + 3];
+        float u0, u1, u2, u3;
+        f2_split(add2(add2(f2_make(v[4 * j], v[4 * j + 1]), f2_make(bv.x, bv.y)),
+                      f2_make(f[4 * j], f[4 * j + 1])),
+                 u0, u1);
+        f2_split(add2(add2(f2_make(v[4 * j + 2], v[4 * j + 3]), f2_make(bv.z, bv.w)),
+                      f2_make(f[4 * j + 2], f[4 * j + 3])),
+                 u2, u3);
         gelu_pair(u0, u1);
         gelu_pair(u2, u3);
+        const uint64_t g01 = f2_make(u0, u1), g23 = f2_make(u2, u3);
         const float4 h0 = __ldg(h + j), h1 = __ldg(h + 8 + j), h2 = __ldg(h + 16 + j);
-        a0 = fmaf(u3, h0.w, fmaf(u2, h0.z, fmaf(u1, h0.y, fmaf(u0, h0.x, a0))));
-        a1 = fmaf(u3, h1.w, fmaf(u2, h1.z, fmaf(u1, h1.y, fmaf(u0, h1.x, a1))));
-        a2 = fmaf(u3, h2.w, fmaf(u2, h2.z, fmaf(u1, h2.y, fmaf(u0, h2.x, a2))));
+        a0 = fma2(g23, f2_make(h0.z, h0.w), fma2(g01, f2_make(h0.x, h0.y), a0));
+        a1 = fma2(g23, f2_make(h1.z, h1.w), fma2(g01, f2_make(h1.x, h1.y), a1));
+        a2 = fma2(g23, f2_make(h2.z, h2.w), fma2(g01, f2_make(h2.x, h2.y), a2));
     }
+    float e0, o0, e1, o1, e2, o2;
+    f2_split(a0, e0, o0);
+    f2_split(a1, e1, o1);
+    f2_split(a2, e2, o2);
     float *o = reinterpret_cast<float *>(p.C);
     const long onpix = 4L * cg.cH * cg.cW;
-    o[((long)pr * 3 + 0) * onpix + opix] = a0;
-    o[((long)pr * 3 + 1) * onpix + opix] = a1;
-    o[((long)pr * 3 + 2) * onpix + opix] = a2;
+    o[((long)pr * 3 + 0) * onpix + opix] = e0 + o0;
+    o[((long)pr * 3 + 1) * onpix + opix] = e1 + o1;
+    o[((long)pr * 3 + 2) * onpix + opix] = e2 + o2;
 }
 
 // ROPE_PF: bf16 output whose tiles may need RoPE, with the row's (cos, sin)
