@@ -212,10 +212,11 @@ int cb_attention(cb_backend *b, cb_mem qkv, int nseq, int N, int E, int heads,
  * (cudaGetSymbolAddress, with that device current); make that first call
  * before any stream capture. The looked-up address is cached per device
  * ordinal for the life of the process: after cudaDeviceReset the cache is
- * stale, so do not call this entry point again on a device that was reset. Every call shares the one array, which keeps
- * the previous call's contents: calls that overlap on the GPU (different
- * streams, or different host threads on one device) race on it. Each GPU
- * that loads the library holds the 32 MiB until the process exits. */
+ * stale, so do not call this entry point again on a device that was reset.
+ * Every call shares the one array, which keeps the previous call's
+ * contents: calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race on it. Each GPU that loads the library
+ * holds the 32 MiB until the process exits. */
 int cb_attention_noalloc(const float *qkv, int nseq, int N, int E, int heads,
                          const float *cs, int npos, float scale, float *out,
                          int *err, void *stream);
