@@ -118,8 +118,8 @@ void cb_decoder_free(cb_decoder *d)
     {
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
-                       d->sh, d->tok_bf16, d->qv_bf16, d->keys, d->keys_bf16, d->kin_bf16, d->bq, d->bk,
-                       d->bv, d->bo_bf16, d->u1_bf16,
+                       d->sh, d->tok_bf16, d->qv_bf16, d->keys, d->keys_bf16, d->kin_bf16,
+                       d->bq, d->bk, d->bv, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws, d->k0_pad, d->v0_pad, d->q_pad,
                        d->xws};
 
