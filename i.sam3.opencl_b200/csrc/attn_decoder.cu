@@ -488,10 +488,13 @@ __host__ __device__ __forceinline__ long many_chunk0(long g, long T, long G)
 // groups by shuffles, the running maximum raised (O, l rescaled) only when
 // the chunk's exceeds it by kManyLazy; P transposed into B fragments by
 // movmatrix. At the end of each prompt in the CTA's range one (m, l, o)
-// partial per (query, head).
+// partial per (query, head). QG > 1 (keys and values shared by all
+// prompts, whose queries the host flattens into one prompt): a warp takes
+// QG groups of 8 queries, each chunk's K and V fragments loaded and split
+// once for all of them.
 constexpr int kManyThreads = 32 * (kHeads + 1);  // 8 head warps + the producer warp
 
-template <bool KV_BF16>
+template <bool KV_BF16, int QG = 1>
 __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const float *__restrict__ Q, long sq, int k_per_prompt, int v_per_prompt,
@@ -515,7 +518,7 @@ __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
     const long p_first = c0 / nch;
     const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int qz = blockIdx.z * 8;
+    const int qz = blockIdx.z * 8 * QG;
     // Chunk cursors (prompt, chunk of the prompt), advanced without division.
     struct Cur {
         long p;
@@ -567,43 +570,49 @@ __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
         return;
     }
 
-    uint32_t qh[2], ql[2];  // B fragments of Q^T (hi, lo)
-    float o[2][4], m[2], l[2];  // O^T per key block (two independent MMA chains)
+    uint32_t qh[QG][2], ql[QG][2];  // B fragments of Q^T (hi, lo) per query group
+    float o[QG][2][4], m[QG][2], l[QG][2];  // O^T per key block (two MMA chains)
     auto start_segment = [&](long p) {
-        const int qi = qz + g;
-        float2 x0 = make_float2(0.0f, 0.0f), x1 = x0;
-        if (qi < Nq) {
-            const float *qp = Q + p * sq + (long)qi * kManyD + h * kManyC + 2 * t;
-            x0 = *reinterpret_cast<const float2 *>(qp);
-            x1 = *reinterpret_cast<const float2 *>(qp + 8);
-        }
-        split_bf16x2(x0.x * qscale, x0.y * qscale, qh[0], ql[0]);
-        split_bf16x2(x1.x * qscale, x1.y * qscale, qh[1], ql[1]);
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            o[0][k] = o[1][k] = 0.0f;
-        m[0] = m[1] = -INFINITY;
-        l[0] = l[1] = 0.0f;
+        for (int jq = 0; jq < QG; jq++) {
+            const int qi = qz + 8 * jq + g;
+            float2 x0 = make_float2(0.0f, 0.0f), x1 = x0;
+            if (qi < Nq) {
+                const float *qp = Q + p * sq + (long)qi * kManyD + h * kManyC + 2 * t;
+                x0 = *reinterpret_cast<const float2 *>(qp);
+                x1 = *reinterpret_cast<const float2 *>(qp + 8);
+            }
+            split_bf16x2(x0.x * qscale, x0.y * qscale, qh[jq][0], ql[jq][0]);
+            split_bf16x2(x1.x * qscale, x1.y * qscale, qh[jq][1], ql[jq][1]);
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                o[jq][0][k] = o[jq][1][k] = 0.0f;
+            m[jq][0] = m[jq][1] = -INFINITY;
+            l[jq][0] = l[jq][1] = 0.0f;
+        }
     };
     // Segment k's partials: l summed over the 8 key groups; the lane of
     // key group g writes channels g and g + 8 of queries 2t, 2t + 1.
     auto flush = [&](long k) {
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            float L = l[u];
-            L += __shfl_xor_sync(0xffffffffu, L, 4);
-            L += __shfl_xor_sync(0xffffffffu, L, 8);
-            L += __shfl_xor_sync(0xffffffffu, L, 16);
-            const int qi = qz + 2 * t + u;
-            if (qi < Nq) {
-                float *dst =
-                    part + (((blockIdx.x * (long)segs + k) * Nq + qi) * kHeads + h) * kPart;
-                if (g == 0) {
-                    dst[0] = m[u];
-                    dst[1] = L;
+        for (int jq = 0; jq < QG; jq++) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                float L = l[jq][u];
+                L += __shfl_xor_sync(0xffffffffu, L, 4);
+                L += __shfl_xor_sync(0xffffffffu, L, 8);
+                L += __shfl_xor_sync(0xffffffffu, L, 16);
+                const int qi = qz + 8 * jq + 2 * t + u;
+                if (qi < Nq) {
+                    float *dst =
+                        part + (((blockIdx.x * (long)segs + k) * Nq + qi) * kHeads + h) * kPart;
+                    if (g == 0) {
+                        dst[0] = m[jq][u];
+                        dst[1] = L;
+                    }
+                    dst[4 + g] = o[jq][0][u] + o[jq][1][u];
+                    dst[4 + g + 8] = o[jq][0][2 + u] + o[jq][1][2 + u];
                 }
-                dst[4 + g] = o[0][u] + o[1][u];
-                dst[4 + g + 8] = o[0][2 + u] + o[1][2 + u];
             }
         }
     };
@@ -622,99 +631,117 @@ __global__ void __launch_bounds__(kManyThreads, 2) mha_many_split_kernel(
         const int n = min(kChunk, Nk - ci * kChunk);
         const char *tk = smb + b * STAGE_B + h * TILE_B;
         const char *tv = tk + kHeads * TILE_B;
-        // S^T of the two key blocks: s[blk][0..3] = keys (g, g, g+8, g+8) of
-        // the block x queries (2t, 2t+1, 2t, 2t+1).
-        float s[2][4];
+        // K and V^T fragments of the two key blocks (bf16: ka / va; fp32:
+        // hi in ka / va, lo in kb / vb), loaded by the first query group
+        // and kept for the others.
+        uint32_t ka[2][4], kb[2][4], va[2][4], vb[2][4];
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            float (&d)[4] = s[blk];
-            d[0] = d[1] = d[2] = d[3] = 0.0f;
-            const int j = blk * 16 + g;
-            if (KV_BF16) {
-                // rows of matrices 0..3: keys 0-7 / 8-15 x channels 0-7 / 8-15
-                const int mi = lane >> 3, rr = blk * 16 + (lane & 7) + (mi & 1) * 8;
-                uint32_t a[4];
-                ldmatrix_x4(a, tk + (rr * kManyC + many_sw16(rr, mi >> 1)) * 2, false);
-                mma_bf16(d, a, qh[0], qh[1]);
-                mma_bf16(d, a, ql[0], ql[1]);
-            }
-            else {
-                const float *kr = reinterpret_cast<const float *>(tk);
-                const float2 x0 = *reinterpret_cast<const float2 *>(kr + j * kManyC + many_sw32(j, t >> 1) + 2 * (t & 1));
-                const float2 x1 = *reinterpret_cast<const float2 *>(kr + (j + 8) * kManyC + many_sw32(j + 8, t >> 1) + 2 * (t & 1));
-                const float2 x2 = *reinterpret_cast<const float2 *>(kr + j * kManyC + many_sw32(j, 2 + (t >> 1)) + 2 * (t & 1));
-                const float2 x3 = *reinterpret_cast<const float2 *>(kr + (j + 8) * kManyC + many_sw32(j + 8, 2 + (t >> 1)) + 2 * (t & 1));
-                uint32_t ah[4], al[4];
-                split_bf16x2(x0.x, x0.y, ah[0], al[0]);
-                split_bf16x2(x1.x, x1.y, ah[1], al[1]);
-                split_bf16x2(x2.x, x2.y, ah[2], al[2]);
-                split_bf16x2(x3.x, x3.y, ah[3], al[3]);
-                mma_bf16(d, ah, qh[0], qh[1]);
-                mma_bf16(d, al, qh[0], qh[1]);
-                mma_bf16(d, ah, ql[0], ql[1]);
-            }
-            if (j >= n)
-                d[0] = d[1] = -INFINITY;
-            if (j + 8 >= n)
-                d[2] = d[3] = -INFINITY;
-        }
-        float bm[2];
+        for (int jq = 0; jq < QG; jq++) {
+            // S^T of the two key blocks: s[blk][0..3] = keys (g, g, g+8, g+8)
+            // of the block x queries (2t, 2t+1, 2t, 2t+1) of group jq.
+            float s[2][4];
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            float x = fmaxf(fmaxf(s[0][u], s[0][2 + u]), fmaxf(s[1][u], s[1][2 + u]));
-            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
-            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
-            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
-            bm[u] = x;
-            if (bm[u] > m[u] + kManyLazy) {  // uniform over the lanes of query 2t + u
-                const float corr = exp2f(m[u] - bm[u]);  // 0 on the first chunk
-                l[u] *= corr;
-                o[0][u] *= corr;
-                o[0][2 + u] *= corr;
-                o[1][u] *= corr;
-                o[1][2 + u] *= corr;
-                m[u] = bm[u];
+            for (int blk = 0; blk < 2; blk++) {
+                float (&d)[4] = s[blk];
+                d[0] = d[1] = d[2] = d[3] = 0.0f;
+                const int j = blk * 16 + g;
+                if (KV_BF16) {
+                    if (jq == 0) {
+                        // rows of matrices 0..3: keys 0-7 / 8-15 x channels 0-7 / 8-15
+                        const int mi = lane >> 3, rr = blk * 16 + (lane & 7) + (mi & 1) * 8;
+                        ldmatrix_x4(ka[blk], tk + (rr * kManyC + many_sw16(rr, mi >> 1)) * 2,
+                                    false);
+                    }
+                    mma_bf16(d, ka[blk], qh[jq][0], qh[jq][1]);
+                    mma_bf16(d, ka[blk], ql[jq][0], ql[jq][1]);
+                }
+                else {
+                    if (jq == 0) {
+                        const float *kr = reinterpret_cast<const float *>(tk);
+                        const float2 x0 = *reinterpret_cast<const float2 *>(
+                            kr + j * kManyC + many_sw32(j, t >> 1) + 2 * (t & 1));
+                        const float2 x1 = *reinterpret_cast<const float2 *>(
+                            kr + (j + 8) * kManyC + many_sw32(j + 8, t >> 1) + 2 * (t & 1));
+                        const float2 x2 = *reinterpret_cast<const float2 *>(
+                            kr + j * kManyC + many_sw32(j, 2 + (t >> 1)) + 2 * (t & 1));
+                        const float2 x3 = *reinterpret_cast<const float2 *>(
+                            kr + (j + 8) * kManyC + many_sw32(j + 8, 2 + (t >> 1)) + 2 * (t & 1));
+                        split_bf16x2(x0.x, x0.y, ka[blk][0], kb[blk][0]);
+                        split_bf16x2(x1.x, x1.y, ka[blk][1], kb[blk][1]);
+                        split_bf16x2(x2.x, x2.y, ka[blk][2], kb[blk][2]);
+                        split_bf16x2(x3.x, x3.y, ka[blk][3], kb[blk][3]);
+                    }
+                    mma_bf16(d, ka[blk], qh[jq][0], qh[jq][1]);
+                    mma_bf16(d, kb[blk], qh[jq][0], qh[jq][1]);
+                    mma_bf16(d, ka[blk], ql[jq][0], ql[jq][1]);
+                }
+                if (j >= n)
+                    d[0] = d[1] = -INFINITY;
+                if (j + 8 >= n)
+                    d[2] = d[3] = -INFINITY;
             }
-        }
+            float bm[2];
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            float pe[4];
+            for (int u = 0; u < 2; u++) {
+                float x = fmaxf(fmaxf(s[0][u], s[0][2 + u]), fmaxf(s[1][u], s[1][2 + u]));
+                x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+                x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+                x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
+                bm[u] = x;
+                if (bm[u] > m[jq][u] + kManyLazy) {  // uniform over the lanes of query 2t + u
+                    const float corr = exp2f(m[jq][u] - bm[u]);  // 0 on the first chunk
+                    l[jq][u] *= corr;
+                    o[jq][0][u] *= corr;
+                    o[jq][0][2 + u] *= corr;
+                    o[jq][1][u] *= corr;
+                    o[jq][1][2 + u] *= corr;
+                    m[jq][u] = bm[u];
+                }
+            }
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                pe[k] = ex2_approx(s[blk][k] - m[k & 1]);  // 0 for masked keys
-                l[k & 1] += pe[k];
-            }
-            // P^T tiles (keys 0-7 / 8-15 x 8 queries) -> B fragments
-            uint32_t ph0, pl0, ph1, pl1;
-            split_bf16x2(pe[0], pe[1], ph0, pl0);
-            split_bf16x2(pe[2], pe[3], ph1, pl1);
-            ph0 = movmatrix_t(ph0);
-            ph1 = movmatrix_t(ph1);
-            pl0 = movmatrix_t(pl0);
-            pl1 = movmatrix_t(pl1);
-            if (KV_BF16) {
-                // V^T fragments: matrices (keys 0-7 / 8-15) x (channels 0-7 / 8-15), transposed
-                const int mi = lane >> 3;
-                const int rr = blk * 16 + (lane & 7) + (mi >> 1) * 8;
-                uint32_t a[4];
-                ldmatrix_x4(a, tv + (rr * kManyC + many_sw16(rr, mi & 1)) * 2, true);
-                mma_bf16(o[blk], a, ph0, ph1);
-                mma_bf16(o[blk], a, pl0, pl1);
-            }
-            else {
-                const float *vr = reinterpret_cast<const float *>(tv);
-                const int k0 = blk * 16 + 2 * t;
-                auto ld = [&](int key, int ch) {
-                    return vr[key * kManyC + many_sw32(key, ch >> 2) + (ch & 3)];
-                };
-                uint32_t ah[4], al[4];
-                split_bf16x2(ld(k0, g), ld(k0 + 1, g), ah[0], al[0]);
-                split_bf16x2(ld(k0, g + 8), ld(k0 + 1, g + 8), ah[1], al[1]);
-                split_bf16x2(ld(k0 + 8, g), ld(k0 + 9, g), ah[2], al[2]);
-                split_bf16x2(ld(k0 + 8, g + 8), ld(k0 + 9, g + 8), ah[3], al[3]);
-                mma_bf16(o[blk], ah, ph0, ph1);
-                mma_bf16(o[blk], al, ph0, ph1);
-                mma_bf16(o[blk], ah, pl0, pl1);
+            for (int blk = 0; blk < 2; blk++) {
+                float pe[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    pe[k] = ex2_approx(s[blk][k] - m[jq][k & 1]);  // 0 for masked keys
+                    l[jq][k & 1] += pe[k];
+                }
+                // P^T tiles (keys 0-7 / 8-15 x 8 queries) -> B fragments
+                uint32_t ph0, pl0, ph1, pl1;
+                split_bf16x2(pe[0], pe[1], ph0, pl0);
+                split_bf16x2(pe[2], pe[3], ph1, pl1);
+                ph0 = movmatrix_t(ph0);
+                ph1 = movmatrix_t(ph1);
+                pl0 = movmatrix_t(pl0);
+                pl1 = movmatrix_t(pl1);
+                if (KV_BF16) {
+                    if (jq == 0) {
+                        // V^T fragments: matrices (keys 0-7 / 8-15) x (channels 0-7 / 8-15),
+                        // transposed
+                        const int mi = lane >> 3;
+                        const int rr = blk * 16 + (lane & 7) + (mi >> 1) * 8;
+                        ldmatrix_x4(va[blk], tv + (rr * kManyC + many_sw16(rr, mi & 1)) * 2, true);
+                    }
+                    mma_bf16(o[jq][blk], va[blk], ph0, ph1);
+                    mma_bf16(o[jq][blk], va[blk], pl0, pl1);
+                }
+                else {
+                    if (jq == 0) {
+                        const float *vr = reinterpret_cast<const float *>(tv);
+                        const int k0 = blk * 16 + 2 * t;
+                        auto ld = [&](int key, int ch) {
+                            return vr[key * kManyC + many_sw32(key, ch >> 2) + (ch & 3)];
+                        };
+                        split_bf16x2(ld(k0, g), ld(k0 + 1, g), va[blk][0], vb[blk][0]);
+                        split_bf16x2(ld(k0, g + 8), ld(k0 + 1, g + 8), va[blk][1], vb[blk][1]);
+                        split_bf16x2(ld(k0 + 8, g), ld(k0 + 9, g), va[blk][2], vb[blk][2]);
+                        split_bf16x2(ld(k0 + 8, g + 8), ld(k0 + 9, g + 8), va[blk][3],
+                                     vb[blk][3]);
+                    }
+                    mma_bf16(o[jq][blk], va[blk], ph0, ph1);
+                    mma_bf16(o[jq][blk], vb[blk], ph0, ph1);
+                    mma_bf16(o[jq][blk], va[blk], pl0, pl1);
+                }
             }
         }
         __syncwarp();
@@ -802,10 +829,10 @@ struct ManyPlan {
     int G, segs;
 };
 
-ManyPlan many_plan(int P, int Nq, int Nk, int num_sms)
+ManyPlan many_plan(int P, int Nq, int Nk, int num_sms, int qg = 1)
 {
     const long nch = (Nk + kChunk - 1) / kChunk, T = (long)P * nch;
-    const long nz = (Nq + 7) / 8;
+    const long nz = (Nq + 8 * qg - 1) / (8 * qg);
     long G = 2L * num_sms / nz;
     if (G < 1)
         G = 1;
@@ -815,10 +842,22 @@ ManyPlan many_plan(int P, int Nq, int Nk, int num_sms)
     return {(int)G, (int)((per - 1) / nch + 2)};
 }
 
-size_t many_workspace(int P, int Nq, int Nk, int num_sms)
+size_t many_workspace(int P, int Nq, int Nk, int num_sms, int qg = 1)
 {
-    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
+    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms, qg);
     return (size_t)pl.G * pl.segs * Nq * kHeads * kPart * sizeof(float);
+}
+
+// Keys and values shared by all prompts, fp32, and the prompts' queries
+// contiguous: the launch flattens them into one prompt of P * Nq queries in
+// groups of 16 (two per warp), so each chunk's K / V fragments serve two
+// groups. The flattened plan's workspace (k_mha_workspace reports the
+// larger of the two).
+constexpr int kManyFlatQG = 2;
+bool many_flat(int P, int Nq, long sq, long sk, long sv, bool kv_bf16)
+{
+    return !kv_bf16 && sk == 0 && sv == 0 && (P == 1 || sq == (long)Nq * kManyD) &&
+           (long)P * Nq >= 8 * kManyFlatQG && (long)P * Nq <= 0x7fffffffL;
 }
 
 template <bool Q_BF16, bool OUT_BF16>
@@ -863,9 +902,16 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                 const void *vp, long sv, void *o, bool out_bf16, void *ws, size_t ws_bytes,
                 float scale, int *err, int num_sms, cudaStream_t st)
 {
-    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms);
-    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms) || (reinterpret_cast<uintptr_t>(ws) & 15) ||
-        !err)
+    const bool flat = many_flat(P, Nq, sq, sk, sv, KV_BF16);
+    if (flat) {
+        Nq *= P;
+        P = 1;
+        sq = 0;
+    }
+    const int qg = flat ? kManyFlatQG : 1;
+    const ManyPlan pl = many_plan(P, Nq, Nk, num_sms, qg);
+    if (!ws || ws_bytes < many_workspace(P, Nq, Nk, num_sms, qg) ||
+        (reinterpret_cast<uintptr_t>(ws) & 15) || !err)
         return K_EARG;
     // K and V as [P][Nk][128] boxes of 32 keys x one head's 16 channels
     // (prompt pitch sk / sv elements; 0: one block shared by all prompts)
@@ -880,13 +926,18 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
                       kManyC, kChunk, swz))
         return K_ETMAP;
     const int smem = (KV_BF16 ? kManySmem / 2 : kManySmem) + 1024 + 64;  // ring, alignment, barriers
-    cudaError_t e = smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
+    cudaError_t e = flat ? smem_limit_once<mha_many_split_kernel<KV_BF16, kManyFlatQG>>(smem)
+                         : smem_limit_once<mha_many_split_kernel<KV_BF16>>(smem);
     if (e != cudaSuccess)
         return (int)e;
-    dim3 grid(pl.G, 1, (Nq + 7) / 8);
-    int rc = launch_pdl(mha_many_split_kernel<KV_BF16>, grid, dim3(kManyThreads), smem, st, tk, tv,
-                        qp, sq, sk != 0, sv != 0, static_cast<float *>(ws), P, Nq, Nk, pl.segs,
-                        scale * 1.4426950408889634f, err);
+    dim3 grid(pl.G, 1, (Nq + 8 * qg - 1) / (8 * qg));
+    int rc = flat ? launch_pdl(mha_many_split_kernel<KV_BF16, kManyFlatQG>, grid,
+                               dim3(kManyThreads), smem, st, tk, tv, qp, sq, 0, 0,
+                               static_cast<float *>(ws), P, Nq, Nk, pl.segs,
+                               scale * 1.4426950408889634f, err)
+                  : launch_pdl(mha_many_split_kernel<KV_BF16>, grid, dim3(kManyThreads), smem, st,
+                               tk, tv, qp, sq, sk != 0, sv != 0, static_cast<float *>(ws), P, Nq,
+                               Nk, pl.segs, scale * 1.4426950408889634f, err);
     if (rc != 0)
         return rc;
     const long total = (long)P * Nq * kHeads * 32;  // a warp per (prompt, query, head)
@@ -906,7 +957,11 @@ extern "C" size_t k_mha_workspace(int P, int Nq, int Nk, int dint, int num_sms)
 {
     if (Nk <= 64 || dint != sam3::kManyD || P <= 0 || Nq <= 0)
         return 0;
-    return sam3::many_workspace(P, Nq, Nk, num_sms);
+    const size_t a = sam3::many_workspace(P, Nq, Nk, num_sms);
+    const size_t b = (long)P * Nq <= 0x7fffffffL
+                         ? sam3::many_workspace(1, P * Nq, Nk, num_sms, sam3::kManyFlatQG)
+                         : 0;
+    return a > b ? a : b;
 }
 
 extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, const float *kp,

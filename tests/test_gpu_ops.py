@@ -389,6 +389,8 @@ def test_softmax_rope_window_im2col_add_vs_oracle(cb, sb, ob):
     ("i2t_3keys", 3, 200, 3, 128, False),      # few keys: masked key columns of the tile
     ("t2i_65", 4, 8, 65, 128, False),          # last 32-key chunk holds one key (TMA zero fill)
     ("t2i_65_shared", 4, 9, 65, 128, True),    # keys shared, two query groups
+    ("t2i_shared_15", 3, 5, 1000, 128, True),  # keys shared, 15 queries: per-prompt launch
+    ("t2i_shared_136", 17, 8, 300, 128, True),  # keys shared, flattened: 8.5 groups of 16
     ("self7", 64, 7, 7, 256, False),
     ("t2i_odd", 3, 11, 1000, 128, False),   # 2 query groups, ragged key splits
     ("t2i_5", 5, 8, 5184, 128, False),      # CTA chunk ranges end inside prompts
