@@ -97,9 +97,13 @@ __global__ void __launch_bounds__(256) mask_logits_kernel(const float4 *__restri
 // sam3_model.c:1188-1210, 1370-1385): block (p, m) runs MLP m on its token
 // (mask token m for m < 3 -> rows 3..5, the IoU token row 1 for m = 3):
 // 256 -> 256 (ReLU) -> 256 (ReLU) -> nout. A warp per output row, lanes
-// over the inputs, double accumulation as host_linear. Outputs: hyper
+// over the inputs, double accumulation as host_linear; 32 warps, four rows
+// each per pass, so a 256-row layer is two passes (each pass waits for its
+// weight rows from L2: few passes, short latency chain). Outputs: hyper
 // [P, 96] (m * 32 + o), iou [P, 3] = sigmoid(out[1..3]) of the IoU head.
-__global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict__ tok,
+constexpr int kHeadWarps = 32;
+
+__global__ void __launch_bounds__(32 * kHeadWarps) dec_heads_kernel(const float *__restrict__ tok,
                                                         const k_dec_heads_w a,
                                                         float *__restrict__ hyper,
                                                         float *__restrict__ iou)
@@ -111,7 +115,8 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = m < 3 ? 3 + m : 1;
     const float *t = tok + ((long)p * 8 + row) * 256;
-    xs[threadIdx.x] = t[threadIdx.x];
+    if (threadIdx.x < 256)
+        xs[threadIdx.x] = t[threadIdx.x];
     __syncthreads();
     const int nout = m < 3 ? 32 : 4;
     for (int l = 0; l < 3; l++) {
@@ -119,18 +124,20 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
         const int no = l < 2 ? 256 : nout;
         const float *in = (l & 1) ? hs : xs;
         float *o = (l & 1) ? xs : hs;
-        // Four rows per pass (r0, r0 + 8, r0 + 16, r0 + 24): four independent
+        // Four rows per pass (r0 + W i, W = kHeadWarps): four independent
         // accumulation and reduction chains per warp; each row's sum is
         // formed in the same order as with one row at a time.
-        for (int r0 = warp; r0 < no; r0 += 32) {
+        for (int r0 = warp; r0 < no; r0 += 4 * kHeadWarps) {
             double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const double xv = (double)in[lane + 32 * k];
 #pragma unroll
                 for (int i = 0; i < 4; i++)
-                    if (r0 + 8 * i < no)
-                        acc[i] += (double)__ldg(W + (long)(r0 + 8 * i) * 256 + lane + 32 * k) * xv;
+                    if (r0 + kHeadWarps * i < no)
+                        acc[i] += (double)__ldg(W + (long)(r0 + kHeadWarps * i) * 256 + lane +
+                                                32 * k) *
+                                  xv;
             }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
@@ -140,7 +147,7 @@ __global__ void __launch_bounds__(256) dec_heads_kernel(const float *__restrict_
             if (lane == 0) {
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const int r = r0 + 8 * i;
+                    const int r = r0 + kHeadWarps * i;
                     if (r < no) {
                         const double v = acc[i] + (double)__ldg(B + r);
                         o[r] = (l < 2 && v < 0.0) ? 0.0f : (float)v;
@@ -333,7 +340,8 @@ extern "C" int k_dec_heads(const float *tok, int P, const k_dec_heads_w *hw, flo
 {
     if (P <= 0 || P > 65535 || !hw)
         return K_EARG;
-    return launch_pdl(dec_heads_kernel, dim3(P, 4), dim3(256), 0, STREAM(s), tok, *hw, hyper, iou);
+    return launch_pdl(dec_heads_kernel, dim3(P, 4), dim3(32 * kHeadWarps), 0, STREAM(s), tok, *hw,
+                      hyper, iou);
 }
 
 extern "C" int k_transpose_cast_bf16(const float *src, int rows, int cols, int dmajor, void *dst,
