@@ -263,8 +263,9 @@ __device__ __forceinline__ void stage_row(uint32_t tile, int r, const uint32_t (
 // ConvTranspose 2x2 (64 -> 32) outputs in sub-pixel-major order, so chunk c
 // (32 columns) is sub-pixel d = c = 2 dy + dx of output pixel (2y + dy,
 // 2x + dx). Per chunk: u = GELU(acc + bias + feat_s0[pixel]) over the 32
-// channels (feat_s0 as k_dec_feat_subpix lays it out), dotted with the prompt's three hypernetwork vectors, written as
-// the three logits of that pixel: the [P, 2H, 2W, 32] map is never stored.
+// channels (feat_s0 as k_dec_feat_subpix lays it out), dotted with the
+// prompt's three hypernetwork vectors, written as the three logits of that
+// pixel: the [P, 2H, 2W, 32] map is never stored.
 // Output pixel of sub-pixel d of input row m.
 __device__ __forceinline__ long logits_pixel(const ConvGeom &cg, int m, int d)
 {
