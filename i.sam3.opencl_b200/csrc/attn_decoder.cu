@@ -317,7 +317,8 @@ __device__ __forceinline__ void mma_bf16_k8(float (&d)[4], uint32_t a0, uint32_t
 // OUT_BF16: O is written as bf16 (for a consumer that only feeds a GEMM).
 template <bool Q_BF16, bool OUT_BF16>
 __global__ void __launch_bounds__(256) mha_few2_kernel(const void *__restrict__ Q, long sq,
-                                                      const float *__restrict__ K, long sk,
+                                                      long ldq, const float *__restrict__ K,
+                                                      long sk,
                                                       const float *__restrict__ V, long sv,
                                                       void *__restrict__ O, int P, int Nq, int Nk,
                                                       float kscale)
@@ -339,7 +340,7 @@ __global__ void __launch_bounds__(256) mha_few2_kernel(const void *__restrict__ 
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int q = q0 + g + (k & 1) * 8;
-            const long off = p * sq + (long)q * D + h * kManyC + 2 * t + (k >> 1) * 8;
+            const long off = p * sq + (long)q * ldq + h * kManyC + 2 * t + (k >> 1) * 8;
             if (q < Nq) {
                 if (Q_BF16)
                     reinterpret_cast<uint32_t &>(r[k]) =
@@ -861,8 +862,9 @@ bool many_flat(int P, int Nq, long sq, long sk, long sv, bool kv_bf16)
 }
 
 template <bool Q_BF16, bool OUT_BF16>
-int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, const float *kp, long sk,
-                const float *vp, long sv, void *o, float scale, int num_sms, cudaStream_t st)
+int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, long ldq, const float *kp,
+                long sk, const float *vp, long sv, void *o, float scale, int num_sms,
+                cudaStream_t st)
 {
     int per_sm = 1;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
@@ -872,7 +874,7 @@ int launch_few2(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
     const long units = (long)P * ((Nq + 15) / 16);
     const long cap = (long)num_sms * (per_sm > 0 ? per_sm : 1);
     return launch_pdl(mha_few2_kernel<Q_BF16, OUT_BF16>, dim3((unsigned)(units < cap ? units : cap)),
-                      dim3(256), 0, st, qp, sq, kp, sk, vp, sv, o, P, Nq, Nk,
+                      dim3(256), 0, st, qp, sq, ldq, kp, sk, vp, sv, o, P, Nq, Nk,
                       scale * 1.4426950408889634f);
 }
 
@@ -881,7 +883,8 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
                const float *vp, long sv, float *o, float scale, int num_sms, cudaStream_t st)
 {
     if (C == 16 && Nk <= kFewSmall)
-        return launch_few2<false, false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
+        return launch_few2<false, false>(P, Nq, Nk, qp, sq, (long)kManyD, kp, sk, vp, sv, o, scale,
+                                         num_sms, st);
     const int smem = 2 * Nk * kHeads * (C + 4) * 4;
     auto kern = mha_few_kernel<C>;
     cudaError_t e = smem_limit_once<mha_few_kernel<C>>(smem);
@@ -899,8 +902,8 @@ int launch_few(int P, int Nq, int Nk, const float *qp, long sq, const float *kp,
 
 template <bool KV_BF16>
 int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp, long sk,
-                const void *vp, long sv, void *o, bool out_bf16, void *ws, size_t ws_bytes,
-                float scale, int *err, int num_sms, cudaStream_t st)
+                long kld, const void *vp, long sv, long vld, void *o, bool out_bf16, void *ws,
+                size_t ws_bytes, float scale, int *err, int num_sms, cudaStream_t st)
 {
     const bool flat = many_flat(P, Nq, sq, sk, sv, KV_BF16);
     if (flat) {
@@ -920,10 +923,10 @@ int launch_many(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
     const CUtensorMapSwizzle swz = KV_BF16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
     const uint32_t es = KV_BF16 ? 2 : 4;
     CUtensorMap tk, tv;
-    if (!make_tmap_3d(&tk, dt, es, kp, (uint64_t)P, (uint64_t)Nk, kManyD, kManyD, (uint64_t)sk,
-                      kManyC, kChunk, swz) ||
-        !make_tmap_3d(&tv, dt, es, vp, (uint64_t)P, (uint64_t)Nk, kManyD, kManyD, (uint64_t)sv,
-                      kManyC, kChunk, swz))
+    if (!make_tmap_3d(&tk, dt, es, kp, (uint64_t)P, (uint64_t)Nk, kManyD, (uint64_t)kld,
+                      (uint64_t)sk, kManyC, kChunk, swz) ||
+        !make_tmap_3d(&tv, dt, es, vp, (uint64_t)P, (uint64_t)Nk, kManyD, (uint64_t)vld,
+                      (uint64_t)sv, kManyC, kChunk, swz))
         return K_ETMAP;
     const int smem = (KV_BF16 ? kManySmem / 2 : kManySmem) + 1024 + 64;  // ring, alignment, barriers
     cudaError_t e = flat ? smem_limit_once<mha_many_split_kernel<KV_BF16, kManyFlatQG>>(smem)
@@ -980,8 +983,8 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
         // The reference rejects the same shape (sam3_model.c:429-430).
         if (c != kManyC)
             return K_EARG;
-        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, false, ws, ws_bytes, scale,
-                                  err, num_sms, st);
+        return launch_many<false>(P, Nq, Nk, qp, sq, kp, sk, (long)kManyD, vp, sv, (long)kManyD, o,
+                                  false, ws, ws_bytes, scale, err, num_sms, st);
     }
     if (c == 16)
         return launch_few<16>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, scale, num_sms, st);
@@ -990,27 +993,29 @@ extern "C" int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq, 
     return K_EARG;
 }
 
-extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
-                              long sk, const float *vp, long sv, void *o, int num_sms, k_stream s)
+extern "C" int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, long ldq,
+                              const float *kp, long sk, const float *vp, long sv, void *o,
+                              int num_sms, k_stream s)
 {
     using namespace sam3;
     if (P <= 0 || Nq <= 0 || Nk <= 0 || Nk > kFewSmall || ((uintptr_t)qp & 15) ||
         ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
-        (sk & 3) || (sv & 3))
+        ldq < kManyD || (ldq & 3) || (sk & 3) || (sv & 3))
         return K_EARG;
-    return launch_few2<true, true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f), num_sms,
-                             reinterpret_cast<cudaStream_t>(s));
+    return launch_few2<true, true>(P, Nq, Nk, qp, sq, ldq, kp, sk, vp, sv, o, 1.0f / sqrtf(16.0f),
+                                   num_sms, reinterpret_cast<cudaStream_t>(s));
 }
 
 extern "C" int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
-                                long sk, const void *vp, long sv, void *o, int out_bf16, void *ws,
-                                size_t ws_bytes, int *err, int num_sms, k_stream s)
+                                long sk, long kld, const void *vp, long sv, long vld, void *o,
+                                int out_bf16, void *ws, size_t ws_bytes, int *err, int num_sms,
+                                k_stream s)
 {
     using namespace sam3;
     if (P <= 0 || Nq <= 0 || Nk <= 64 || P > 65535 || ((uintptr_t)qp & 15) ||
         ((uintptr_t)kp & 15) || ((uintptr_t)vp & 15) || ((uintptr_t)o & 15) || (sq & 3) ||
-        (sk & 7) || (sv & 7))
+        (sk & 7) || (sv & 7) || kld < kManyD || vld < kManyD || (kld & 7) || (vld & 7))
         return K_EARG;
-    return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, vp, sv, o, out_bf16 != 0, ws, ws_bytes,
-                             1.0f / sqrtf((float)kManyC), err, num_sms, STREAM(s));
+    return launch_many<true>(P, Nq, Nk, qp, sq, kp, sk, kld, vp, sv, vld, o, out_bf16 != 0, ws,
+                             ws_bytes, 1.0f / sqrtf((float)kManyC), err, num_sms, STREAM(s));
 }

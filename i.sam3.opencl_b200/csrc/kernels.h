@@ -145,19 +145,22 @@ int k_mha(int P, int Nq, int Nk, int dint, const float *qp, long sq,
           const float *kp, long sk, const float *vp, long sv, float *o,
           void *ws, size_t ws_bytes, int *err, int num_sms, k_stream s);
 /* The decoder's image -> token attention (dint 128, at most 8 keys) with its
- * queries qp read as bf16 (rows of 128, row stride sq elements; as the Q
- * projection writes them) and its output o written as bf16 [P * Nq, 128]
- * (the operand of the following Linear); otherwise the arithmetic of k_mha. */
-int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, const float *kp,
-                   long sk, const float *vp, long sv, void *o, int num_sms, k_stream s);
+ * queries qp read as bf16 (rows of 128 channels, prompt stride sq and row
+ * stride ldq in elements; as the Q projection writes them) and its output o
+ * written as bf16 [P * Nq, 128] (the operand of the following Linear);
+ * otherwise the arithmetic of k_mha. */
+int k_mha_i2t_bf16(int P, int Nq, int Nk, const void *qp, long sq, long ldq,
+                   const float *kp, long sk, const float *vp, long sv, void *o, int num_sms,
+                   k_stream s);
 /* The decoder's token -> image attention (dint 128, more than 64 keys) with
- * its keys and values kp / vp read as bf16 rows (as their projections write
- * them; row strides in elements) and o written as bf16 when out_bf16 (the
- * operand of the output projection), else fp32; otherwise k_mha (same
- * workspace). */
+ * its keys and values kp / vp read as bf16 rows of 128 channels (as their
+ * projections write them; prompt strides sk / sv and row strides kld / vld
+ * in elements) and o written as bf16 when out_bf16 (the operand of the
+ * output projection), else fp32; otherwise k_mha (same workspace). */
 int k_mha_t2i_bf16kv(int P, int Nq, int Nk, const float *qp, long sq, const void *kp,
-                     long sk, const void *vp, long sv, void *o, int out_bf16, void *ws,
-                     size_t ws_bytes, int *err, int num_sms, k_stream s);
+                     long sk, long kld, const void *vp, long sv, long vld, void *o,
+                     int out_bf16, void *ws, size_t ws_bytes, int *err, int num_sms,
+                     k_stream s);
 
 /* Mask decoder (decoder.cu). convt_scatter: G [P*H*W, Co*4] (16-byte
  * aligned) -> out [P, 2H, 2W, Co], + bias, + add (shared, may be NULL),

@@ -71,6 +71,11 @@ struct cb_decoder {
     /* token stream [batch * 8, 256] and its scratch */
     float *qpe, *qry, *sq, *sk, *sv, *so, *sh;
     void *tok_bf16;             /* bf16 [batch * 8, 2048] GEMM operand */
+    /* layer 1's token -> image key projection and image -> token query
+     * projection stacked ([256, 256] bf16 weight, [256] bias): both read
+     * kin, so one GEMM writes [keys | queries] rows of 256 */
+    void *w_kq1;
+    float *b_kq1;
     void *qv_bf16;              /* bf16(qry) [batch * 8, 256] from a layer's
                                  * last token norm: input of its image ->
                                  * token values and of the next layer's
@@ -78,7 +83,10 @@ struct cb_decoder {
     /* per-prompt image stream */
     float *keys;                /* [batch * T, 256] */
     void *keys_bf16, *kin_bf16; /* bf16 [batch * T, 256] */
-    float *bq, *bk, *bv;        /* [batch * T, 128] */
+    float *bk, *bv;             /* [batch * T, 128] fp32-sized: bf16 keys /
+                                 * values of the token -> image attention
+                                 * (layer 1: bk holds [keys | queries] rows
+                                 * of 256 bf16) */
     void *bo_bf16;              /* bf16 [batch * T, 128] */
     void *u1_bf16;              /* bf16 [batch * 4T, 64] */
     float *hyper, *iou;         /* [batch, 96], [batch, 3] */
@@ -118,8 +126,9 @@ void cb_decoder_free(cb_decoder *d)
     {
         void *dev[] = {d->src, d->srcpe, d->pe_img, d->kp0, d->vp0, d->qp0, d->feat_s0,
                        d->feat_s1, d->qpe, d->qry, d->sq, d->sk, d->sv, d->so,
-                       d->sh, d->tok_bf16, d->qv_bf16, d->keys, d->keys_bf16, d->kin_bf16,
-                       d->bq, d->bk, d->bv, d->bo_bf16, d->u1_bf16,
+                       d->sh, d->tok_bf16, d->qv_bf16, d->w_kq1, d->b_kq1, d->keys,
+                       d->keys_bf16, d->kin_bf16,
+                       d->bk, d->bv, d->bo_bf16, d->u1_bf16,
                        d->hyper, d->iou, d->mha_ws, d->k0_pad, d->v0_pad, d->q_pad,
                        d->xws};
 
@@ -178,10 +187,11 @@ int cb_decoder_create(cb_backend *b, int batch, cb_decoder **out)
     A(d->sh, nt * 2048 * 4);
     A(d->tok_bf16, nt * 2048 * 2);
     A(d->qv_bf16, nt * DEC_DIM * 2);
+    A(d->w_kq1, (size_t)256 * DEC_DIM * 2);
+    A(d->b_kq1, (size_t)256 * 4);
     A(d->keys, B * T * DEC_DIM * 4);
     A(d->keys_bf16, B * T * DEC_DIM * 2);
     A(d->kin_bf16, B * T * DEC_DIM * 2);
-    A(d->bq, B * T * 128 * 4);
     A(d->bk, B * T * 128 * 4);
     A(d->bv, B * T * 128 * 4);
     A(d->bo_bf16, B * T * 128 * 2);
@@ -269,6 +279,13 @@ static int compute_pe_img(cb_decoder *d)
     return rc;
 }
 
+/* Decoder tensor indices: attention block blk's tensor t, layer l's
+ * tensor t. */
+#define ATT(blk, t) (SAM3_DT_ATTN + 8 * (blk) + (t))
+#define LAY(l, t) (SAM3_DT_LAYER + 12 * (l) + (t))
+enum { QW = 0, QB, KW, KB, VW, VB, OW, OB };
+enum { N1W = 0, N1B, N2W, N2B, N3W, N3B, N4W, N4B, M1W, M1B, M2W, M2B };
+
 /* Device copy of tensor i from fp32 values already on the device (rows x
  * cols in the checkpoint layout): bf16 for GEMM weights (the ConvTranspose
  * ones transposed to [cout * 4, cin]), fp32 otherwise. */
@@ -286,11 +303,30 @@ static int store_tensor(cb_decoder *d, int i, const float *f32)
         return cbi_kstatus(b, k_transpose_cast_bf16(f32, r, c, 1, d->w[i], st),
                            "decoder weights");
     if (is_gemm_weight(i))
-        return cbi_kstatus(b, k_cast_f32_bf16(f32, d->w[i], (long)r * c, st), "decoder weights");
-    return cbi_kstatus(b,
-                       (int)cudaMemcpyAsync(d->w[i], f32, (size_t)r * c * 4,
-                                            cudaMemcpyDeviceToDevice, b->stream),
-                       "decoder weights");
+        CB_TRY(cbi_kstatus(b, k_cast_f32_bf16(f32, d->w[i], (long)r * c, st),
+                           "decoder weights"));
+    else
+        CB_TRY(cbi_kstatus(b,
+                           (int)cudaMemcpyAsync(d->w[i], f32, (size_t)r * c * 4,
+                                                cudaMemcpyDeviceToDevice, b->stream),
+                           "decoder weights"));
+    /* the stacked copy of layer 1's key (rows 0-127) and query (128-255)
+     * projections */
+    {
+        const int kq = i == ATT(SAM3_DA_L1_T2I, KW) || i == ATT(SAM3_DA_L1_T2I, KB) ? 0
+                       : i == ATT(SAM3_DA_L1_I2T, QW) || i == ATT(SAM3_DA_L1_I2T, QB) ? 1
+                                                                                       : -1;
+        if (kq >= 0) {
+            const int w = i == ATT(SAM3_DA_L1_T2I, KW) || i == ATT(SAM3_DA_L1_I2T, QW);
+            const size_t bytes = w ? (size_t)128 * DEC_DIM * 2 : (size_t)128 * 4;
+            char *dst = w ? (char *)d->w_kq1 : (char *)d->b_kq1;
+            return cbi_kstatus(b,
+                               (int)cudaMemcpyAsync(dst + kq * bytes, d->w[i], bytes,
+                                                    cudaMemcpyDeviceToDevice, b->stream),
+                               "decoder weights");
+        }
+    }
+    return CB_OK;
 }
 
 static void init_params(int kind, float std, float *mean, float *sd)
@@ -478,10 +514,11 @@ static int mha(cb_decoder *d, int P, int Nq, int Nk, int dint, const float *q, l
 }
 
 /* Token -> image attention of the P prompts' queries sq on bf16 keys and
- * values (row strides in elements; 0: shared by all prompts) into so's
- * storage as bf16 [P * 8, 128], the operand of the output projection (no
- * rounding pass). */
-static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, long sv)
+ * values (prompt strides sk / sv in elements, 0: shared by all prompts; key
+ * row stride kld, value rows of 128) into so's storage as bf16 [P * 8, 128],
+ * the operand of the output projection (no rounding pass). */
+static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, long kld, const void *v,
+                   long sv)
 {
     cb_backend *b = d->b;
     const long nt = (long)P * DEC_NTOK;
@@ -502,16 +539,11 @@ static int mha_t2i(cb_decoder *d, int P, const void *k, long sk, const void *v, 
     }
     LAUNCH("dec_mha_t2i", 4.0 * P * DEC_NTOK * (double)DEC_T * 128,
            4.0 * (double)P * DEC_NTOK * 128 * 2 + 2.0 * (sk ? (double)P : 1.0) * DEC_T * 128 * 2,
-           k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, v, sv, d->so, 1,
-                            d->mha_ws, d->mha_ws_bytes, b->d_err, b->num_sms,
+           k_mha_t2i_bf16kv(P, DEC_NTOK, DEC_T, d->sq, DEC_NTOK * 128, k, sk, kld, v, sv, 128,
+                            d->so, 1, d->mha_ws, d->mha_ws_bytes, b->d_err, b->num_sms,
                             (k_stream)b->stream));
     return CB_OK;
 }
-
-#define ATT(blk, t) (SAM3_DT_ATTN + 8 * (blk) + (t))
-#define LAY(l, t) (SAM3_DT_LAYER + 12 * (l) + (t))
-enum { QW = 0, QB, KW, KB, VW, VB, OW, OB };
-enum { N1W = 0, N1B, N2W, N2B, N3W, N3B, N4W, N4B, M1W, M1B, M2W, M2B };
 
 int cb_decoder_set_image(cb_decoder *d, cb_mem emb, cb_mem feat_s0, cb_mem feat_s1)
 {
@@ -578,11 +610,27 @@ static int t2i_attention(cb_decoder *d, int P, int blk)
 
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, QW), ATT(blk, QB), d->sq, 0,
                   K_ACT_NONE));
-    CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB),
-                  d->bk));
+    if (blk == SAM3_DA_L1_T2I) {
+        cb_backend *b = d->b;
+
+        /* keys and layer 1's image -> token queries from kin in one GEMM:
+         * [keys | queries] rows of 256 bf16 in bk's storage */
+        LAUNCH("dec_gemm_img", 2.0 * rows * DEC_DIM * 256,
+               (double)rows * DEC_DIM * 2 + DEC_DIM * 256.0 * 2 + (double)rows * 256 * 2,
+               k_gemm_bf16_tc((int)rows, 256, DEC_DIM, d->kin_bf16, DEC_DIM, d->w_kq1, DEC_DIM,
+                              d->bk, 256, 1, d->b_kq1, NULL, 256, 0, 1.0f, K_ACT_NONE, NULL,
+                              b->d_err, b->num_sms, (k_stream)b->stream));
+    }
+    else
+        CB_TRY(lin16h(d, "dec_gemm_img", d->kin_bf16, rows, DEC_DIM, 128, ATT(blk, KW),
+                      ATT(blk, KB), d->bk));
     CB_TRY(lin16h(d, "dec_gemm_img", d->keys_bf16, rows, DEC_DIM, 128, ATT(blk, VW),
                   ATT(blk, VB), d->bv));
-    CB_TRY(mha_t2i(d, P, d->bk, (long)DEC_T * 128, d->bv, (long)DEC_T * 128));
+    {
+        const long kld = blk == SAM3_DA_L1_T2I ? 256 : 128;
+
+        CB_TRY(mha_t2i(d, P, d->bk, (long)DEC_T * kld, kld, d->bv, (long)DEC_T * 128));
+    }
     return lin16(d, "dec_gemm_tok", d->so, nt, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB), d->qry,
                  d->qry, 0, K_ACT_NONE);
 }
@@ -650,17 +698,9 @@ static int i2t_attention(cb_decoder *d, int P, int l)
     const long nt = (long)P * DEC_NTOK, rows = (long)P * DEC_T;
     const int blk = l ? SAM3_DA_L1_I2T : SAM3_DA_L0_I2T;
 
-    if (l) {
-        cb_backend *b = d->b;
-
-        /* bq is read only by the image -> token attention, as bf16 */
-        LAUNCH("dec_gemm_img", 2.0 * rows * DEC_DIM * 128,
-               (double)rows * DEC_DIM * 2 + DEC_DIM * 128.0 * 2 + (double)rows * 128 * 2,
-               k_gemm_bf16_tc((int)rows, 128, DEC_DIM, d->kin_bf16, DEC_DIM, d->w[ATT(blk, QW)],
-                              DEC_DIM, d->bq, 128, 1, (const float *)d->w[ATT(blk, QB)], NULL,
-                              128, 0, 1.0f, K_ACT_NONE, NULL, b->d_err, b->num_sms,
-                              (k_stream)b->stream));
-    }
+    /* layer 1's queries: columns 128-255 of the [keys | queries] rows that
+     * layer 1's token -> image attention projected from kin (unchanged
+     * since: the token steps in between leave the image stream alone) */
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(blk, KW), ATT(blk, KB), d->sk, 0,
                   K_ACT_NONE));
     /* keys from tok_bf16, values from qv_bf16: both written by the norm
@@ -673,9 +713,11 @@ static int i2t_attention(cb_decoder *d, int P, int l)
         /* the attention output is read only by the output projection: bf16 */
         LAUNCH("dec_mha_i2t", 4.0 * P * DEC_T * (double)DEC_NTOK * 128,
                (double)P * DEC_T * 128 * (4 + 2),
-               k_mha_i2t_bf16(P, DEC_T, DEC_NTOK, l ? d->bq : d->qp0, l ? (long)DEC_T * 128 : 0,
-                              d->sk, DEC_NTOK * 128, d->sv, DEC_NTOK * 128, d->bo_bf16,
-                              b->num_sms, (k_stream)b->stream));
+               k_mha_i2t_bf16(P, DEC_T, DEC_NTOK,
+                              l ? (const void *)((const uint16_t *)d->bk + 128) : d->qp0,
+                              l ? (long)DEC_T * 256 : 0, l ? 256 : 128, d->sk, DEC_NTOK * 128,
+                              d->sv, DEC_NTOK * 128, d->bo_bf16, b->num_sms,
+                              (k_stream)b->stream));
     }
     CB_TRY(lin16(d, "dec_gemm_img", d->bo_bf16, rows, 128, DEC_DIM, ATT(blk, OW), ATT(blk, OB),
                  d->keys, l ? d->keys : NULL, 0, K_ACT_NONE));
@@ -748,7 +790,7 @@ int cb_decode(cb_decoder *d, int P, const float *points, float *iou, cb_mem lowr
     CB_TRY(lntok(d, nt, LAY(0, N1W), LAY(0, N1B), NULL, 1));
     CB_TRY(lintok_again(d, nt, DEC_DIM, 128, ATT(SAM3_DA_L0_T2I, QW),
                   ATT(SAM3_DA_L0_T2I, QB), d->sq, 0, K_ACT_NONE));
-    CB_TRY(mha_t2i(d, P, d->kp0, 0, d->vp0, 0));
+    CB_TRY(mha_t2i(d, P, d->kp0, 0, 128, d->vp0, 0));
     CB_TRY(lin16(d, "dec_gemm_tok", d->so, nt, 128, DEC_DIM, ATT(SAM3_DA_L0_T2I, OW),
                  ATT(SAM3_DA_L0_T2I, OB), d->qry, d->qry, 0, K_ACT_NONE));
     CB_TRY(lntok(d, nt, LAY(0, N2W), LAY(0, N2B), d->tok_bf16, 0));
